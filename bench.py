@@ -1,0 +1,461 @@
+"""Benchmark of the kadan_b200 quantized-weight linear path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (decode): the Llama-3-8B-shaped Q4_K linear stack,
+32 layers x {q, o: 4096x4096; k, v: 1024x4096; gate, up: 14336x4096;
+down: 4096x14336}, one input row (T=1). A step is one token through the whole
+stack: per layer four dependent launches ([q,k,v], [o], [gate,up], [down]),
+captured once in a CUDA graph. The weights (3.93 GB) are far larger than L2,
+so no flush is needed between steps.
+
+metric value = weight+activation bytes streamed per step / device time per
+step, summed over ranks (each rank runs its own replica of the stack: the path
+has no exchange step at this config, so scaling is weak).
+
+`--impl reference` times the reference's own CPU path (kadan::text::CpuMatvec
+over ggml's AVX2 Q4_K dot, compiled from the reference sources into
+oracle/_ref) on a bounded sample of the same stack with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode GB/s (% HBM peak) & MXFP4 MoE tokens/s at 1/2/4/8 B200"
+HIDDEN, KV, FFN, LAYERS = 4096, 1024, 14336, 32
+# (name, out, in) per layer; dependency groups of one decode step.
+GROUPS = [[("q", HIDDEN, HIDDEN), ("k", KV, HIDDEN), ("v", KV, HIDDEN)],
+          [("o", HIDDEN, HIDDEN)],
+          [("gate", FFN, HIDDEN), ("up", FFN, HIDDEN)],
+          [("down", HIDDEN, FFN)]]
+Q4K_BLOCK, Q4K_VALUES = 144, 256
+FALLBACK_HBM_GBS = 6650.0
+
+
+def weight_bytes(out: int, in_: int) -> int:
+    return out * in_ // Q4K_VALUES * Q4K_BLOCK
+
+
+def layer_weight_bytes() -> int:
+    return sum(weight_bytes(o, i) for g in GROUPS for _, o, i in g)
+
+
+def step_bytes() -> tuple[int, int]:
+    """(weight bytes, activation bytes) streamed per step."""
+    w = LAYERS * layer_weight_bytes()
+    act = 0
+    for g in GROUPS:
+        act += g[0][2] * 4  # shared fp32 input of the group
+        act += sum(o * 4 for _, o, _ in g)  # fp32 outputs
+    return w, LAYERS * act
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during timing."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.file.flush()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in Path(self.file.name).read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        finally:
+            os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3] not in ("", "[N/A]"))}
+
+
+# --------------------------------------------------------------------- ours
+def build_stack(torch, kb, device, seed: int = 0):
+    from kadan_b200 import synth
+
+    layers = []
+    for layer in range(LAYERS):
+        mats = {}
+        for g in GROUPS:
+            for i, (name, out, in_) in enumerate(g):
+                mats[name] = synth.device_gguf(kb.Q4_K, out, in_, seed * 1000 + layer * 16 + len(mats), device)
+        layers.append(mats)
+    gen = torch.Generator(device=device).manual_seed(seed + 7)
+    acts = {n: torch.randn(1, k, device=device, generator=gen).half().float()
+            for n, k in (("x", HIDDEN), ("attn", HIDDEN), ("h", HIDDEN), ("g", FFN))}
+    outs = {name: torch.empty(1, out, device=device) for g in GROUPS for name, out, _ in g}
+    return layers, acts, outs
+
+
+def step_jobs(kb, layers, acts, outs):
+    """Per layer, per group: a ctypes job array ready for kb200_gguf_gemv_batch."""
+    inputs = ["x", "attn", "h", "g"]
+    calls = []
+    for mats in layers:
+        for gi, g in enumerate(GROUPS):
+            jobs = [kb.gemv_job(kb.Q4_K, mats[name], acts[inputs[gi]], outs[name], in_=in_, columns=out, rows=1)
+                    for name, out, in_ in g]
+            arr = (kb.GemvJob * len(jobs))(*jobs)
+            calls.append((gi, arr, len(jobs)))
+    return calls
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    import kadan_b200 as kb
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    layers, acts, outs = build_stack(torch, kb, device, seed=rank)
+    calls = step_jobs(kb, layers, acts, outs)
+    stream = torch.cuda.Stream(device)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    gate_up_bytes = 2 * weight_bytes(FFN, HIDDEN)
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]
+
+    def launch_step(record):
+        layer = 0
+        for gi, arr, n in calls:
+            if record and gi == 2:
+                pairs[layer][0].record(stream)
+            kb.check(kb.lib.kb200_gguf_gemv_batch(arr, n, sptr))
+            if record and gi == 2:
+                pairs[layer][1].record(stream)
+            if gi == 3:
+                layer += 1
+
+    # First call per kernel sets attributes/occupancy outside capture.
+    with torch.cuda.stream(stream):
+        launch_step(False)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch_step(True)
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gate_up_ms = []
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    # The events inside the graph hold the last replay's gate/up launches.
+    gate_up_ms = [a.elapsed_time(b) for a, b in pairs]
+    ms = start.elapsed_time(end) / args.steps
+    if dist:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    wbytes, abytes = step_bytes()
+    value = world * (wbytes + abytes) / (ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    achieved = gate_up_bytes / (statistics.mean(gate_up_ms) * 1e-3) / 1e9
+
+    # End to end through the host-span C ABI: host inputs, one upload, the
+    # launches, one download and a sync per dependency group (128 per token).
+    import numpy as np
+
+    ctx = kb.Context(local_rank)
+    host_in = {n: a.cpu().numpy().copy() for n, a in acts.items()}
+    host_out = {n: np.empty((1, o), dtype=np.float32) for g in GROUPS for n, o, _ in g}
+    inputs = ["x", "attn", "h", "g"]
+    host_calls = []
+    for mats in layers:
+        for gi, g in enumerate(GROUPS):
+            jobs = [kb.host_job(kb.Q4_K, mats[n].data_ptr(), host_in[inputs[gi]], host_out[n], in_=i, out=o,
+                                validated=True) for n, o, i in g]
+            host_calls.append((kb.HostJob * len(jobs))(*jobs))
+    result = ctypes.c_int(0)
+
+    def e2e_step():
+        for arr in host_calls:
+            kb.check(kb.lib.kb200_dense_gguf_batch(ctx.handle, arr, len(arr), None, ctypes.byref(result)))
+
+    e2e_step()
+    e2e_steps = max(3, min(args.steps // 20, 50))
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if dist:
+        t = torch.tensor([e2e_s], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    h2d = LAYERS * sum(g[0][2] * 4 for g in GROUPS)
+    d2h = LAYERS * sum(o * 4 for g in GROUPS for _, o, _ in g)
+    e2e = {"value": round(world * (wbytes + abytes) / e2e_s / 1e9, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "calls_per_step": len(host_calls), "ms_per_step": round(e2e_s * 1e3, 4),
+           "timing": "host wall clock around synchronous kb200_dense_gguf_batch calls"}
+    ctx.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(layers, kb, budget_s=args.cpu_seconds)
+
+    clock = clocks.summary()
+    if dist:
+        graph = None
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "q4_k weights, fp32 activations and accumulation",
+        "data": "synthetic (seeded Q4_K blocks and fp16-representable N(0,1) activations on the device)",
+        "config": {"workload": "BASELINE config 2 decode: Llama-3-8B Q4_K linear stack, 32 layers, T=1",
+                   "weight_bytes_per_step": wbytes, "activation_bytes_per_step": abytes,
+                   "l2": "inputs larger than L2 (3.93 GB of weights per step)",
+                   "launch": "one CUDA graph per step, 4 dependent launches per layer",
+                   "parallelism": f"replicas x{world}"},
+        "hbm_frac": round(value / world / peak, 4),
+        "gpu_launches": len(calls) * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "gemv_staged_kernel<Q4K,1> (gate+up launch)",
+                     "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                     "traffic": None,
+                     "algorithmic_bytes_per_launch": gate_up_bytes},
+        "e2e": e2e,
+        "clocks": clock,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(layers, kb, budget_s: float = 15.0):
+    """The reference's CpuMatvec on the same bytes: one layer's seven matrices
+    copied to the host, repeated for about `budget_s` seconds on all cores."""
+    from oracle.pyoracle import REF_LIB, Oracle, Reference
+
+    import numpy as np
+
+    threads = os.cpu_count() or 1
+    mats = {n: t.cpu().numpy() for n, t in layers[0].items()}
+    x = {HIDDEN: np.random.default_rng(0).standard_normal(HIDDEN).astype(np.float16).astype(np.float32),
+         FFN: np.random.default_rng(1).standard_normal(FFN).astype(np.float16).astype(np.float32)}
+    if REF_LIB.exists():
+        ref = Reference()
+        kind = "reference"
+
+        def one_layer():
+            for g in GROUPS:
+                for n, o, i in g:
+                    ref.cpu_matvec(12, mats[n], x[i], i, o, threads=threads)
+    else:
+        orc = Oracle()
+        kind, threads = "port", 1
+
+        def one_layer():
+            for g in GROUPS:
+                for n, o, i in g:
+                    orc.gemv_f64(1, mats[n][: max(1, o // 64)], x[i], i, max(1, o // 64))
+
+    one_layer()
+    t0, n = time.perf_counter(), 0
+    while time.perf_counter() - t0 < budget_s:
+        one_layer()
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    per_layer = layer_weight_bytes() if kind == "reference" else sum(
+        weight_bytes(max(1, o // 64), i) for g in GROUPS for _, o, i in g)
+    return {"value": round(per_layer / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"layer 0 of the stack (7 matrices, {per_layer} weight bytes) x {n} repetitions, "
+                      f"{round(dt * n, 1)} s; kadan::text::CpuMatvec 64-column units, activations quantized "
+                      f"to Q8_K once per input as the reference does"}
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the reference's CPU path on the box's host cores."""
+    if rank != 0:
+        return
+    import numpy as np
+
+    from kadan_b200 import synth
+    from oracle.pyoracle import REF_LIB, Oracle, Reference
+
+    threads = os.cpu_count() or 1
+    rng_x = {HIDDEN: synth.activations(HIDDEN, seed=1), FFN: synth.activations(FFN, seed=2)}
+    # Bounded sample: one layer's matrices (122.7 MB) drawn host-side per step.
+    mats = {}
+    for g in GROUPS:
+        for n, o, i in g:
+            mats[n] = synth.q4_k(o, i, seed=len(mats))
+    if REF_LIB.exists():
+        ref = Reference()
+        kind = "reference"
+
+        def sample():
+            for g in GROUPS:
+                for n, o, i in g:
+                    ref.cpu_matvec(12, mats[n], rng_x[i], i, o, threads=threads)
+        sample_bytes = layer_weight_bytes()
+    else:
+        orc = Oracle()
+        kind, threads = "port", 1
+
+        def sample():
+            for g in GROUPS:
+                for n, o, i in g:
+                    orc.gemv_f64(1, mats[n][:64], rng_x[i], i, 64)
+        sample_bytes = sum(weight_bytes(64, i) for g in GROUPS for _, _, i in g)
+    for _ in range(args.warmup):
+        sample()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        sample()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = sample_bytes / dt / 1e9
+    wbytes, abytes = step_bytes()
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_k weights, Q8_K-quantized activations (reference CPU dot)",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": "BASELINE config 2 decode: Llama-3-8B Q4_K linear stack, 32 layers, T=1",
+                   "sample": "one layer (7 matrices) per step", "full_step_weight_bytes": wbytes},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": "one layer of the stack per step"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_case(args):
+    """Small single-kernel cases for profiling (not the headline number):
+    gemv-q4k: one batched launch of four 14336x4096 Q4_K GEMVs (132 MB of
+    weights, more than L2), T=1, repeated --steps times after --warmup."""
+    import torch
+
+    import kadan_b200 as kb
+    from kadan_b200 import synth
+
+    dev = torch.device("cuda:0")
+    enc = {"gemv-q4k": kb.Q4_K, "gemv-q6k": kb.Q6_K, "gemv-q8": kb.Q8_0}[args.case]
+    mats = [synth.device_gguf(enc, FFN, HIDDEN, 100 + i, dev) for i in range(4)]
+    x = torch.randn(1, HIDDEN, device=dev).half().float()
+    ys = [torch.empty(1, FFN, device=dev) for _ in mats]
+    jobs = [kb.gemv_job(enc, w, x, y, in_=HIDDEN, columns=FFN, rows=1) for w, y in zip(mats, ys)]
+    for _ in range(args.warmup):
+        kb.gguf_gemv_batch(jobs)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        kb.gguf_gemv_batch(jobs)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    nbytes = sum(w.numel() for w in mats)
+    print(json.dumps({"case": args.case, "ms_per_launch": round(ms, 5),
+                      "gbps": round(nbytes / (ms * 1e-3) / 1e9, 1), "weight_bytes": nbytes}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None, help="profiling case instead of the headline workload")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
+        if args.steps > 200:
+            args.steps = 20
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

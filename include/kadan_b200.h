@@ -1,0 +1,184 @@
+/* kadan_b200 — B200 (sm_100a) quantized-weight linear path, C ABI.
+ *
+ * This is the drop-in boundary under the Hikari inference worker's
+ * kadan::DenseCompute operator interface
+ * (services/hikari/inference_worker/include/kadan/dense_compute.hpp:60-342 in
+ * ghalrym/Kadan; "IW/" below abbreviates services/hikari/inference_worker/).
+ * Every entry point takes plain pointers and sizes, returns a kb200_status,
+ * throws nothing, and is asynchronous on the given CUDA stream unless it says
+ * otherwise. Pointers marked "device" must address memory of the current
+ * CUDA device. The C++ adapter kadan::b200::Compute (include/kadan/b200_compute.hpp)
+ * maps these status codes back onto the reference's ProjectionResult /
+ * std::runtime_error conventions.
+ */
+#ifndef KADAN_B200_H
+#define KADAN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KB200_API __attribute__((visibility("default")))
+#else
+#define KB200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The reference throws std::runtime_error with "h3_cuda_*"
+ * messages for the execution failures (IW/src/cuda/h3_compute.cu:34-51);
+ * kb200_status_name() returns the matching message text. */
+typedef enum kb200_status {
+    KB200_OK = 0,
+    KB200_UNSUPPORTED = 1,       /* ProjectionResult::unsupported: nothing read or written */
+    KB200_INVALID = 2,           /* bad shape/pointer/alignment argument */
+    KB200_CUDA = 3,              /* a CUDA runtime call failed ("h3_cuda: ...") */
+    KB200_NONFINITE_WEIGHT = 4,  /* "h3_cuda_nonfinite_weight" */
+    KB200_NONFINITE_INPUT = 5,   /* "h3_cuda_nonfinite_input" */
+    KB200_ALIAS = 6,             /* "h3_cuda_alias": output overlaps an input */
+    KB200_CANCELLED = 7,         /* "h3_cuda_cancelled" */
+    KB200_TIMEOUT = 8,           /* a bounded device-side wait ran out */
+    KB200_NO_MEMORY = 9
+} kb200_status;
+
+/* Weight encodings: the numbering of kadan::gguf::Encoding
+ * (IW/include/kadan/gguf_quantization.hpp:16-27), plus F32 rows, which the
+ * reference expresses as an empty std::optional<gguf::Encoding>. */
+typedef enum kb200_encoding {
+    KB200_F32 = -1,
+    KB200_Q3_K = 0,
+    KB200_Q4_K = 1,
+    KB200_Q8_0 = 2,
+    KB200_Q6_K = 3,
+    KB200_IQ3_XXS = 4,
+    KB200_IQ4_NL = 5,
+    KB200_IQ4_XS = 6,
+    KB200_IQ2_S = 7,
+    KB200_IQ3_S = 8,
+    KB200_BF16 = 9
+} kb200_encoding;
+
+/* Input rows one packed GEMV pass reduces, and the most rows a batch job may
+ * carry: DenseCompute::gguf_batch_rows / gguf_batch_max_rows
+ * (IW/include/kadan/dense_compute.hpp:197-201). */
+#define KB200_BATCH_ROWS 8
+#define KB200_BATCH_MAX_ROWS 4096
+
+KB200_API const char* kb200_status_name(int status);
+/* Text of the last failure on the calling thread. */
+KB200_API const char* kb200_last_error(void);
+KB200_API int kb200_version(void);
+/* 1 if `encoding` has a device decoder (gguf::supported, gguf_quantization.hpp:57-63). */
+KB200_API int kb200_encoding_supported(int encoding);
+KB200_API size_t kb200_block_values(int encoding);
+KB200_API size_t kb200_block_bytes(int encoding);
+
+/* ---------------------------------------------------------------------------
+ * Dequantisation. Replaces gguf_decode_kernel (IW/src/cuda/h3_compute.cu:76-95):
+ * out[i] = gguf::decode(encoding, packed + i/values*bytes, i%values) for
+ * i < count, bit-exact, with *status |= 1 when a decoded value is not finite.
+ * packed, out: device. status: device or NULL. */
+KB200_API int kb200_gguf_dequant(
+    int encoding,
+    const void* packed,
+    size_t count,
+    float* out,
+    unsigned* status,
+    void* stream
+);
+
+/* ---------------------------------------------------------------------------
+ * Packed GEMV. One job is the reference's MatvecJob (h3_compute.cu:110-121):
+ *   output[r*stride + c] = sum_k decode(W[c,k]) * input[r*in + k]
+ * for r < rows, c < columns; W has `columns` packed rows of row_bytes each.
+ * status: device word or NULL; bit 0 is set when a decoded weight of the job
+ * is not finite (NULL skips the check, as for bank-validated chunks). */
+typedef struct kb200_gemv_job {
+    const void* weights; /* device */
+    const float* input;  /* device, rows * in floats */
+    float* output;       /* device */
+    unsigned* status;    /* device or NULL */
+    size_t row_bytes;
+    size_t stride;
+    uint32_t in;
+    uint32_t columns;
+    uint32_t rows;
+    int32_t encoding; /* kb200_encoding */
+} kb200_gemv_job;
+
+/* Every job of the batch, one launch per encoding, no device scratch: the job
+ * table travels in the launch parameters. Replaces plan_matvec + launch_matvec +
+ * gguf_matvec_batch_kernel (h3_compute.cu:243-257, :325-382) and, for one job,
+ * gguf_matvec_kernel (:238-240, :294-307). Rows above KB200_BATCH_ROWS are
+ * processed as successive groups of rows, as append_row_groups does (:311-319).
+ * jobs: host array. */
+KB200_API int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream);
+
+/* Which kernel kb200_gguf_gemv_batch selects for a job: 1 = bulk-copy staged
+ * sm_100a kernel, 0 = generic kernel (unaligned rows), -1 = unsupported. */
+KB200_API int kb200_gemv_path(const kb200_gemv_job* job);
+
+/* ---------------------------------------------------------------------------
+ * Host-span boundary. A context owns one device, one CUDA stream, a device
+ * workspace and pinned staging that grow on demand; calls on one context must
+ * not overlap (the reference serialises DenseCompute with a mutex,
+ * IW/src/cuda/h3_compute.cu:1639). */
+typedef struct kb200_context kb200_context;
+
+KB200_API int kb200_context_create(int device, kb200_context** out);
+KB200_API void kb200_context_destroy(kb200_context* ctx);
+/* The context's cudaStream_t. */
+KB200_API void* kb200_context_stream(kb200_context* ctx);
+
+/* Device-resident packed rows (the weight bank the reference keeps per
+ * device, IW/include/kadan/device_weights.hpp:38): a synchronous upload of
+ * `bytes` host bytes into a 256-byte aligned device allocation. */
+KB200_API int kb200_weights_upload(kb200_context* ctx, const void* host, size_t bytes, void** device);
+KB200_API int kb200_weights_free(kb200_context* ctx, void* device);
+
+/* One projection of DenseCompute::GgufBatchJob
+ * (IW/include/kadan/dense_compute.hpp:205-213) over resident weights. */
+typedef struct kb200_host_job {
+    const void* weights; /* device (from kb200_weights_upload or any device buffer) */
+    const float* input;  /* host, rows * in floats */
+    float* output;       /* host, rows * out floats */
+    size_t row_bytes;
+    uint32_t in;
+    uint32_t out;
+    uint32_t rows;
+    int32_t encoding;  /* kb200_encoding */
+    int32_t validated; /* 1: these weights were already checked finite */
+} kb200_host_job;
+
+/* Result codes of kb200_dense_gguf_batch: ProjectionResult
+ * (IW/include/kadan/dense_compute.hpp:44-48). */
+#define KB200_RESULT_UNSUPPORTED 0
+#define KB200_RESULT_UNVALIDATED 1
+#define KB200_RESULT_FINITE 2
+
+/* DenseCompute::dense_gguf_batch (IW/src/cuda/h3_compute.cu:3963-4375):
+ * synchronous. Unsupported jobs return KB200_UNSUPPORTED (result
+ * UNSUPPORTED) before any read or write; identical input spans upload once;
+ * non-finite inputs fail with KB200_NONFINITE_INPUT, outputs overlapping any
+ * input with KB200_ALIAS; then one input upload, one launch per encoding, one
+ * download of outputs plus the weight status word, and KB200_NONFINITE_WEIGHT
+ * when an unvalidated weight decoded non-finite. *cancel (may be NULL) is
+ * polled between stages (KB200_CANCELLED). */
+KB200_API int kb200_dense_gguf_batch(
+    kb200_context* ctx,
+    const kb200_host_job* jobs,
+    size_t count,
+    const volatile int* cancel,
+    int* result
+);
+
+/* Device-side watchdog word: nonzero when a bounded wait inside a kernel gave up
+ * since the last call of this function, which also clears it. Synchronous. */
+KB200_API int kb200_take_device_error(unsigned* value);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,246 @@
+"""kadan_b200: the B200 (sm_100a) quantized-weight linear path.
+
+Python host mirror of the C ABI in include/kadan_b200.h. It exposes the
+operations of the Hikari worker's DenseCompute path
+(services/hikari/inference_worker/include/kadan/dense_compute.hpp) over
+device tensors:
+
+    gguf_dequant(encoding, packed, count, out)      gguf_decode_kernel
+    gguf_gemv_batch([GemvJob, ...])                  dense_gguf_batch's launch
+    dense_gguf_batch(jobs)                           host-span batch (sync)
+
+Every call goes through libkadan_b200.so. There is no CPU or PyTorch
+fallback: if the library cannot be loaded the import fails.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Optional, Sequence
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libkadan_b200.so"
+
+# kadan::gguf::Encoding numbering (gguf_quantization.hpp:16-27); F32 = no encoding.
+F32, Q3_K, Q4_K, Q8_0, Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS, IQ2_S, IQ3_S, BF16 = -1, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9
+ENCODING_NAMES = {F32: "f32", Q3_K: "q3_k", Q4_K: "q4_k", Q8_0: "q8_0", Q6_K: "q6_k",
+                  IQ4_NL: "iq4_nl", IQ4_XS: "iq4_xs", BF16: "bf16"}
+# ggml type ids of the same encodings (gguf_quantization.hpp:30-55).
+GGML_TYPE = {Q8_0: 8, Q3_K: 11, Q4_K: 12, Q6_K: 14, IQ4_NL: 20, IQ4_XS: 23, BF16: 30, F32: 0}
+
+OK, UNSUPPORTED, INVALID, CUDA, NONFINITE_WEIGHT, NONFINITE_INPUT, ALIAS, CANCELLED, TIMEOUT, NO_MEMORY = range(10)
+BATCH_ROWS = 8
+BATCH_MAX_ROWS = 4096
+
+
+class KadanError(RuntimeError):
+    """A failed kb200 call. `status` is the kb200_status code."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class Unsupported(KadanError):
+    """ProjectionResult::unsupported: nothing was read or written."""
+
+
+class GemvJob(ctypes.Structure):
+    """kb200_gemv_job (the reference's MatvecJob, h3_compute.cu:110-121)."""
+
+    _fields_ = [
+        ("weights", ctypes.c_void_p),
+        ("input", ctypes.c_void_p),
+        ("output", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("row_bytes", ctypes.c_size_t),
+        ("stride", ctypes.c_size_t),
+        ("in_", ctypes.c_uint32),
+        ("columns", ctypes.c_uint32),
+        ("rows", ctypes.c_uint32),
+        ("encoding", ctypes.c_int32),
+    ]
+
+
+class HostJob(ctypes.Structure):
+    """kb200_host_job (DenseCompute::GgufBatchJob over resident weights)."""
+
+    _fields_ = [
+        ("weights", ctypes.c_void_p),
+        ("input", ctypes.c_void_p),
+        ("output", ctypes.c_void_p),
+        ("row_bytes", ctypes.c_size_t),
+        ("in_", ctypes.c_uint32),
+        ("out", ctypes.c_uint32),
+        ("rows", ctypes.c_uint32),
+        ("encoding", ctypes.c_int32),
+        ("validated", ctypes.c_int32),
+    ]
+
+
+RESULT_UNSUPPORTED, RESULT_UNVALIDATED, RESULT_FINITE = 0, 1, 2
+
+
+def _load() -> ctypes.CDLL:
+    if os.environ.get("KADAN_B200_NO_BUILD") != "1":
+        from . import build as _build
+
+        if _build.stale():
+            _build.build()
+    if not LIB_PATH.exists():
+        raise ImportError(f"kadan_b200: CUDA library missing at {LIB_PATH}")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    c_int, c_size, vp = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p
+    lib.kb200_status_name.restype = ctypes.c_char_p
+    lib.kb200_status_name.argtypes = [c_int]
+    lib.kb200_last_error.restype = ctypes.c_char_p
+    lib.kb200_last_error.argtypes = []
+    lib.kb200_version.restype = c_int
+    lib.kb200_encoding_supported.argtypes = [c_int]
+    lib.kb200_block_values.restype = c_size
+    lib.kb200_block_values.argtypes = [c_int]
+    lib.kb200_block_bytes.restype = c_size
+    lib.kb200_block_bytes.argtypes = [c_int]
+    lib.kb200_gguf_dequant.argtypes = [c_int, vp, c_size, vp, vp, vp]
+    lib.kb200_gguf_gemv_batch.argtypes = [ctypes.POINTER(GemvJob), c_size, vp]
+    lib.kb200_gemv_path.argtypes = [ctypes.POINTER(GemvJob)]
+    lib.kb200_take_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint)]
+    lib.kb200_context_create.argtypes = [c_int, ctypes.POINTER(vp)]
+    lib.kb200_context_destroy.argtypes = [vp]
+    lib.kb200_context_destroy.restype = None
+    lib.kb200_context_stream.argtypes = [vp]
+    lib.kb200_context_stream.restype = vp
+    lib.kb200_weights_upload.argtypes = [vp, vp, c_size, ctypes.POINTER(vp)]
+    lib.kb200_weights_free.argtypes = [vp, vp]
+    lib.kb200_dense_gguf_batch.argtypes = [vp, ctypes.POINTER(HostJob), c_size, ctypes.POINTER(c_int),
+                                           ctypes.POINTER(c_int)]
+    return lib
+
+
+lib = _load()
+
+
+def check(status: int) -> None:
+    if status == OK:
+        return
+    message = lib.kb200_last_error().decode(errors="replace")
+    if status == UNSUPPORTED:
+        raise Unsupported(status, message)
+    raise KadanError(status, message)
+
+
+def block_values(encoding: int) -> int:
+    return int(lib.kb200_block_values(encoding))
+
+
+def block_bytes(encoding: int) -> int:
+    return int(lib.kb200_block_bytes(encoding))
+
+
+def row_bytes(encoding: int, in_: int) -> int:
+    return in_ // block_values(encoding) * block_bytes(encoding)
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream
+
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def gguf_dequant(encoding: int, packed, count: int, out, status=None, stream=None) -> None:
+    """out[:count] = exact decode of `packed` (device tensors)."""
+    check(lib.kb200_gguf_dequant(encoding, _ptr(packed), count, _ptr(out), _ptr(status), _stream_ptr(stream)))
+
+
+def gemv_job(encoding: int, weights, x, y, *, in_: int, columns: int, rows: int,
+             row_bytes_: Optional[int] = None, stride: Optional[int] = None, status=None) -> GemvJob:
+    rb = row_bytes_ if row_bytes_ is not None else (in_ * 4 if encoding == F32 else row_bytes(encoding, in_))
+    return GemvJob(_ptr(weights), _ptr(x), _ptr(y), _ptr(status), rb,
+                   columns if stride is None else stride, in_, columns, rows, encoding)
+
+
+def gguf_gemv_batch(jobs: Sequence[GemvJob], stream=None) -> None:
+    arr = (GemvJob * len(jobs))(*jobs)
+    check(lib.kb200_gguf_gemv_batch(arr, len(jobs), _stream_ptr(stream)))
+
+
+def gemv_path(job: GemvJob) -> int:
+    return int(lib.kb200_gemv_path(ctypes.byref(job)))
+
+
+def take_device_error() -> int:
+    v = ctypes.c_uint(0)
+    lib.kb200_take_device_error(ctypes.byref(v))
+    return int(v.value)
+
+
+def gguf_gemv(encoding: int, weights, x, *, in_: int, columns: int, out=None, status=None, stream=None):
+    """y[rows, columns] = x[rows, in] @ decode(W[columns, in])^T on the device."""
+    import torch
+
+    rows = x.numel() // in_
+    if out is None:
+        out = torch.empty(rows, columns, dtype=torch.float32, device=x.device)
+    gguf_gemv_batch([gemv_job(encoding, weights, x, out, in_=in_, columns=columns, rows=rows, status=status)], stream)
+    return out
+
+
+class Context:
+    """kb200_context: the synchronous host-span boundary on one device."""
+
+    def __init__(self, device: int = 0):
+        h = ctypes.c_void_p()
+        check(lib.kb200_context_create(device, ctypes.byref(h)))
+        self.handle = h
+        self.device = device
+
+    def close(self) -> None:
+        if self.handle:
+            lib.kb200_context_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream_ptr(self) -> int:
+        return int(lib.kb200_context_stream(self.handle))
+
+    def upload(self, host_bytes) -> int:
+        """Copy a host numpy array into a new device allocation; returns its address."""
+        import numpy as np
+
+        a = np.ascontiguousarray(host_bytes)
+        p = ctypes.c_void_p()
+        check(lib.kb200_weights_upload(self.handle, a.ctypes.data, a.nbytes, ctypes.byref(p)))
+        return int(p.value)
+
+    def free(self, ptr: int) -> None:
+        check(lib.kb200_weights_free(self.handle, ptr))
+
+    def dense_gguf_batch(self, jobs: Sequence[HostJob], cancel: Optional[ctypes.c_int] = None) -> int:
+        """Returns RESULT_UNVALIDATED; raises Unsupported / KadanError like the reference throws."""
+        arr = (HostJob * len(jobs))(*jobs)
+        result = ctypes.c_int(0)
+        check(lib.kb200_dense_gguf_batch(self.handle, arr, len(jobs),
+                                         None if cancel is None else ctypes.byref(cancel), ctypes.byref(result)))
+        return int(result.value)
+
+
+def host_job(encoding: int, weights_ptr: int, x, y, *, in_: int, out: int, validated: bool = False,
+             row_bytes_: Optional[int] = None) -> HostJob:
+    """x: float32 numpy [rows, in]; y: float32 numpy [rows, out] (written)."""
+    rows = x.size // in_
+    rb = row_bytes_ if row_bytes_ is not None else (in_ * 4 if encoding == F32 else row_bytes(encoding, in_))
+    return HostJob(weights_ptr, x.ctypes.data, y.ctypes.data, rb, in_, out, rows, encoding, int(validated))

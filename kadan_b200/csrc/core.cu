@@ -1,0 +1,137 @@
+// C-ABI housekeeping (status text, last error, watchdog word) and the exact
+// dequantisation kernel.
+#include <cstdio>
+#include <cstring>
+
+#include "gguf_formats.cuh"
+#include "kb200_device.cuh"
+#include "kb200_host.hpp"
+
+namespace kb200 {
+
+// Set (one bit per cause) by a kernel whose bounded wait ran out; read and
+// cleared by kb200_take_device_error(). A file-scope device variable.
+__device__ unsigned device_error = 0;
+
+namespace {
+thread_local char error_text[512];
+}
+
+unsigned* watchdog_word() {
+    static unsigned* cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return nullptr;
+    if (!cached[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, device_error) == cudaSuccess)
+            cached[dev] = static_cast<unsigned*>(p);
+    }
+    return cached[dev];
+}
+
+int fail(int status, const char* what) {
+    std::snprintf(error_text, sizeof(error_text), "%s: %s", kb200_status_name(status), what);
+    return status;
+}
+
+int cuda_fail(cudaError_t code, const char* where) {
+    std::snprintf(error_text, sizeof(error_text), "h3_cuda: %s (%s)", cudaGetErrorString(code), where);
+    return KB200_CUDA;
+}
+
+// Decode `count` values; each thread writes one value so stores stay coalesced.
+__global__ void dequant_kernel(
+    int encoding, const uint8_t* packed, size_t count, float* out, unsigned* status
+) {
+    const int values = block_values(encoding), bytes = block_bytes(encoding);
+    bool bad = false;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += size_t(gridDim.x) * blockDim.x) {
+        const float v = decode_value(encoding, packed + i / values * bytes, unsigned(i % values));
+        out[i] = v;
+        bad |= !isfinite(v);
+    }
+    if (bad && status)
+        atomicOr(status, 1u);
+}
+
+}  // namespace kb200
+
+using namespace kb200;
+
+extern "C" {
+
+const char* kb200_status_name(int status) {
+    switch (status) {
+    case KB200_OK: return "ok";
+    case KB200_UNSUPPORTED: return "unsupported";
+    case KB200_INVALID: return "h3_cuda_invalid_argument";
+    case KB200_CUDA: return "h3_cuda";
+    case KB200_NONFINITE_WEIGHT: return "h3_cuda_nonfinite_weight";
+    case KB200_NONFINITE_INPUT: return "h3_cuda_nonfinite_input";
+    case KB200_ALIAS: return "h3_cuda_alias";
+    case KB200_CANCELLED: return "h3_cuda_cancelled";
+    case KB200_TIMEOUT: return "kb200_device_wait_timeout";
+    case KB200_NO_MEMORY: return "h3_cuda_projection_scratch";
+    default: return "kb200_unknown_status";
+    }
+}
+
+const char* kb200_last_error(void) {
+    return error_text;
+}
+
+int kb200_version(void) {
+    return 1;
+}
+
+int kb200_encoding_supported(int encoding) {
+    return encoding == KB200_F32 || decodable(encoding) ? 1 : 0;
+}
+
+size_t kb200_block_values(int encoding) {
+    return kb200_encoding_supported(encoding) ? size_t(block_values(encoding)) : 0;
+}
+
+size_t kb200_block_bytes(int encoding) {
+    return kb200_encoding_supported(encoding) ? size_t(block_bytes(encoding)) : 0;
+}
+
+int kb200_take_device_error(unsigned* value) {
+    unsigned v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, device_error, sizeof(v));
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbol(device_error, &zero, sizeof(zero));
+    if (e != cudaSuccess)
+        return cuda_fail(e, "kb200_take_device_error");
+    if (value)
+        *value = v;
+    return v ? fail(KB200_TIMEOUT, "a bounded device wait gave up") : KB200_OK;
+}
+
+int kb200_gguf_dequant(
+    int encoding, const void* packed, size_t count, float* out, unsigned* status, void* stream
+) {
+    if (!decodable(encoding))
+        return fail(KB200_UNSUPPORTED, "encoding has no device decoder");
+    if (count % size_t(block_values(encoding)))
+        return fail(KB200_INVALID, "count is not whole blocks");
+    if (!count)
+        return KB200_OK;
+    if (!packed || !out)
+        return fail(KB200_INVALID, "null pointer");
+    const size_t packed_bytes = count / block_values(encoding) * block_bytes(encoding);
+    if (overlap(out, count * sizeof(float), packed, packed_bytes))
+        return fail(KB200_ALIAS, "output overlaps packed input");
+    const unsigned threads = 256;
+    const size_t want = (count + threads - 1) / threads;
+    const unsigned blocks = unsigned(want < 148u * 16u ? want : 148u * 16u);
+    dequant_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        encoding, static_cast<const uint8_t*>(packed), count, out, status
+    );
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "dequant_kernel launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,36 @@
+// Host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "kadan_b200.h"
+
+namespace kb200 {
+
+// Record `what` as the calling thread's last error and return `status`.
+int fail(int status, const char* what);
+int cuda_fail(cudaError_t code, const char* where);
+
+// Byte ranges [a, a+an) and [b, b+bn) share an address (the reference's
+// alias rule, IW/src/cuda/h3_compute.cu:60-66).
+inline bool overlap(const void* a, size_t an, const void* b, size_t bn) {
+    if (!an || !bn)
+        return false;
+    const auto x = reinterpret_cast<std::uintptr_t>(a), y = reinterpret_cast<std::uintptr_t>(b);
+    return x <= y ? y - x < an : x - y < bn;
+}
+
+inline bool aligned(const void* p, size_t to) {
+    return reinterpret_cast<std::uintptr_t>(p) % to == 0;
+}
+
+// Device address of the watchdog word (a file-scope __device__ variable of
+// core.cu) on the current device; kernels with bounded waits report there.
+unsigned* watchdog_word();
+
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count();
+
+}  // namespace kb200

@@ -1,0 +1,108 @@
+/* Test infrastructure only: a plain-C restatement of the reference worker's
+ * quantized-linear arithmetic, used by tests/, __graft_entry__.smoke() and the
+ * cpu_baseline leg of bench.py as the CHECKER of the CUDA path. Nothing in the
+ * kadan_b200 product links, loads or calls this library.
+ *
+ * Encoding numbers follow kadan::gguf::Encoding
+ * (services/hikari/inference_worker/include/kadan/gguf_quantization.hpp:16-27).
+ */
+#ifndef KADAN_ORACLE_H
+#define KADAN_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum orc_encoding {
+    ORC_Q3_K = 0,
+    ORC_Q4_K = 1,
+    ORC_Q8_0 = 2,
+    ORC_Q6_K = 3,
+    ORC_IQ4_NL = 5,
+    ORC_IQ4_XS = 6,
+    ORC_BF16 = 9
+};
+
+float orc_half(uint16_t bits);
+size_t orc_block_values(int encoding);
+size_t orc_block_bytes(int encoding);
+float orc_decode(int encoding, const uint8_t* block, size_t element);
+void orc_decode_stream(int encoding, const uint8_t* packed, size_t count, float* out);
+
+/* y[r*y_stride + c] = sum_k decode(W[c,k]) * x[r*in + k], double accumulation. */
+void orc_gemv_f64(
+    int encoding,
+    const uint8_t* weights,
+    size_t row_bytes,
+    size_t in,
+    size_t out,
+    const float* x,
+    size_t rows,
+    double* y,
+    size_t y_stride
+);
+
+/* MXFP4, safetensors expert layout: weights [rows, cols/2] low nibble first,
+ * scales [rows, cols/32] E8M0 (255 invalid). */
+float orc_e2m1(unsigned code);
+int orc_mxfp4_decode_rows(
+    size_t rows,
+    size_t cols,
+    const uint8_t* weights,
+    const uint8_t* scales,
+    size_t first,
+    size_t count,
+    float* out
+);
+/* GGUF block_mxfp4 (17-byte blocks: E8M0 then 16 code bytes). */
+void orc_mxfp4_gguf_decode(const uint8_t* blocks, size_t nblocks, float* out);
+
+/* Softmax router, top-k, renormalize (MoeLayer::forward semantics). */
+void orc_moe_route(
+    size_t tokens,
+    size_t experts,
+    size_t top_k,
+    const float* logits,
+    int32_t* chosen,
+    float* weight
+);
+
+enum orc_moe_activation {
+    ORC_SWIGLU_OAI = 0,   /* gate<=limit, up in [-limit,limit], gate*sigmoid(alpha*gate)*(up+1) */
+    ORC_SILU_MUL = 1      /* silu(gate)*up (the reference's MoeLayer) */
+};
+
+/* Full MXFP4 MoE layer. gate_up rows: 2*inter per expert; with interleaved=1
+ * gate is row 2i and up row 2i+1, else gate rows [0,inter) and up [inter,2inter).
+ * gu_bias [E,2*inter] and down_bias [E,hidden] may be NULL. round_act=1 rounds
+ * the activation fed to the down projection to bf16 (as the device does). */
+int orc_moe_forward(
+    size_t tokens,
+    size_t hidden,
+    size_t inter,
+    size_t experts,
+    size_t top_k,
+    const float* x,
+    const float* logits,
+    const uint8_t* gu_weights,
+    const uint8_t* gu_scales,
+    const float* gu_bias,
+    const uint8_t* down_weights,
+    const uint8_t* down_scales,
+    const float* down_bias,
+    int activation,
+    int interleaved,
+    float limit,
+    float alpha,
+    int round_act,
+    float* out
+);
+
+float orc_bf16_round(float v);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

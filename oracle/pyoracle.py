@@ -1,0 +1,249 @@
+"""Test infrastructure only: ctypes bindings of the CPU checkers.
+
+  ORACLE  liboracle.so            this repository's C restatement (oracle.c)
+  REF     _ref/libkadan_ref.so    the reference's own ggml / quantization /
+                                  CpuMatvec code compiled in place (Makefile)
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module, and only to check or time against the CUDA path.
+"""
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_LIB = HERE / "liboracle.so"
+REF_LIB = HERE / "_ref" / "libkadan_ref.so"
+REFERENCE_TREE = Path("/root/reference")
+
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_f64p = ctypes.POINTER(ctypes.c_double)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+
+
+def build(ref: bool = True) -> None:
+    """make the oracle (and the reference build when its sources are present)."""
+    subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
+    if ref and REFERENCE_TREE.exists():
+        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref"], check=True)
+
+
+def _p(a: np.ndarray, t):
+    return a.ctypes.data_as(t)
+
+
+class Oracle:
+    def __init__(self, path: Path = ORACLE_LIB):
+        if not path.exists():
+            build(ref=False)
+        L = ctypes.CDLL(str(path))
+        L.orc_half.restype = ctypes.c_float
+        L.orc_half.argtypes = [ctypes.c_uint16]
+        L.orc_decode.restype = ctypes.c_float
+        L.orc_decode.argtypes = [ctypes.c_int, _u8p, ctypes.c_size_t]
+        L.orc_decode_stream.argtypes = [ctypes.c_int, _u8p, ctypes.c_size_t, _f32p]
+        L.orc_block_values.restype = ctypes.c_size_t
+        L.orc_block_bytes.restype = ctypes.c_size_t
+        L.orc_gemv_f64.argtypes = [ctypes.c_int, _u8p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                                   _f32p, ctypes.c_size_t, _f64p, ctypes.c_size_t]
+        L.orc_e2m1.restype = ctypes.c_float
+        L.orc_mxfp4_decode_rows.argtypes = [ctypes.c_size_t, ctypes.c_size_t, _u8p, _u8p,
+                                            ctypes.c_size_t, ctypes.c_size_t, _f32p]
+        L.orc_mxfp4_gguf_decode.argtypes = [_u8p, ctypes.c_size_t, _f32p]
+        L.orc_moe_route.argtypes = [ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _f32p, _i32p, _f32p]
+        L.orc_moe_forward.argtypes = [ctypes.c_size_t] * 5 + [_f32p, _f32p, _u8p, _u8p, _f32p, _u8p, _u8p, _f32p,
+                                                              ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                                              ctypes.c_float, ctypes.c_int, _f32p]
+        L.orc_bf16_round.restype = ctypes.c_float
+        L.orc_bf16_round.argtypes = [ctypes.c_float]
+        self.L = L
+
+    def half(self, bits: int) -> float:
+        return self.L.orc_half(bits)
+
+    def block_values(self, e: int) -> int:
+        return int(self.L.orc_block_values(e))
+
+    def block_bytes(self, e: int) -> int:
+        return int(self.L.orc_block_bytes(e))
+
+    def decode(self, e: int, packed: np.ndarray, count: int) -> np.ndarray:
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        out = np.empty(count, dtype=np.float32)
+        self.L.orc_decode_stream(e, _p(packed, _u8p), count, _p(out, _f32p))
+        return out
+
+    def gemv_f64(self, e: int, weights: np.ndarray, x: np.ndarray, in_: int, out: int) -> np.ndarray:
+        """y[rows, out] in float64 (decode then double dot)."""
+        weights = np.ascontiguousarray(weights, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+        rows = x.size // in_
+        y = np.empty((rows, out), dtype=np.float64)
+        row_bytes = weights.size // out
+        self.L.orc_gemv_f64(e, _p(weights, _u8p), row_bytes, in_, out, _p(x, _f32p), rows, _p(y, _f64p), out)
+        return y
+
+    def mxfp4_decode_rows(self, weights, scales, rows, cols, first=0, count=None) -> np.ndarray:
+        count = rows - first if count is None else count
+        out = np.empty((count, cols), dtype=np.float32)
+        w = np.ascontiguousarray(weights, dtype=np.uint8)
+        s = np.ascontiguousarray(scales, dtype=np.uint8)
+        rc = self.L.orc_mxfp4_decode_rows(rows, cols, _p(w, _u8p), _p(s, _u8p), first, count, _p(out, _f32p))
+        if rc:
+            raise ValueError(f"orc_mxfp4_decode_rows failed: {rc}")
+        return out
+
+    def mxfp4_gguf_decode(self, blocks: np.ndarray) -> np.ndarray:
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        n = blocks.size // 17
+        out = np.empty(n * 32, dtype=np.float32)
+        self.L.orc_mxfp4_gguf_decode(_p(blocks, _u8p), n, _p(out, _f32p))
+        return out
+
+    def moe_route(self, logits: np.ndarray, top_k: int):
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        t, e = logits.shape
+        chosen = np.empty((t, top_k), dtype=np.int32)
+        weight = np.empty((t, top_k), dtype=np.float32)
+        self.L.orc_moe_route(t, e, top_k, _p(logits, _f32p), _p(chosen, _i32p), _p(weight, _f32p))
+        return chosen, weight
+
+    def moe_forward(self, x, logits, gu_w, gu_s, dn_w, dn_s, *, hidden, inter, experts, top_k,
+                    gu_bias=None, dn_bias=None, activation=0, interleaved=1, limit=7.0, alpha=1.702,
+                    round_act=1) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        tokens = x.size // hidden
+        out = np.empty((tokens, hidden), dtype=np.float32)
+        arrs = [np.ascontiguousarray(a, dtype=np.uint8) for a in (gu_w, gu_s, dn_w, dn_s)]
+        gb = None if gu_bias is None else np.ascontiguousarray(gu_bias, dtype=np.float32)
+        db = None if dn_bias is None else np.ascontiguousarray(dn_bias, dtype=np.float32)
+        rc = self.L.orc_moe_forward(
+            tokens, hidden, inter, experts, top_k, _p(x, _f32p),
+            _p(np.ascontiguousarray(logits, dtype=np.float32), _f32p),
+            _p(arrs[0], _u8p), _p(arrs[1], _u8p), None if gb is None else _p(gb, _f32p),
+            _p(arrs[2], _u8p), _p(arrs[3], _u8p), None if db is None else _p(db, _f32p),
+            activation, interleaved, limit, alpha, round_act, _p(out, _f32p))
+        if rc:
+            raise ValueError(f"orc_moe_forward failed: {rc}")
+        return out
+
+
+class Reference:
+    """The reference's own CPU code (oracle/_ref/libkadan_ref.so)."""
+
+    def __init__(self, path: Path = REF_LIB):
+        if not path.exists():
+            build(ref=True)
+        if not path.exists():
+            raise FileNotFoundError(f"reference build missing: {path}")
+        L = ctypes.CDLL(str(path))
+        L.ref_last_error.restype = ctypes.c_char_p
+        L.ref_gguf_decode.restype = ctypes.c_float
+        L.ref_gguf_decode.argtypes = [ctypes.c_int, _u8p, ctypes.c_size_t]
+        L.ref_gguf_decode_stream.argtypes = [ctypes.c_int, _u8p, ctypes.c_size_t, _f32p]
+        L.ref_gguf_decode_run_stream.argtypes = [ctypes.c_int, _u8p, ctypes.c_size_t, _f32p]
+        L.ref_gguf_encoding.argtypes = [ctypes.c_uint32]
+        L.ref_fp16_to_fp32.restype = ctypes.c_float
+        L.ref_fp16_to_fp32.argtypes = [ctypes.c_uint16]
+        L.ref_ggml_row_size.restype = ctypes.c_size_t
+        L.ref_ggml_row_size.argtypes = [ctypes.c_uint32, ctypes.c_int64]
+        L.ref_ggml_blck_size.restype = ctypes.c_int64
+        L.ref_ggml_type_size.restype = ctypes.c_size_t
+        L.ref_ggml_to_float.argtypes = [ctypes.c_uint32, ctypes.c_void_p, _f32p, ctypes.c_int64]
+        L.ref_ggml_quantize.restype = ctypes.c_size_t
+        L.ref_ggml_quantize.argtypes = [ctypes.c_uint32, _f32p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64]
+        L.ref_mxfp4_decode_rows.argtypes = [ctypes.c_size_t, ctypes.c_size_t, _u8p, _u8p,
+                                            ctypes.c_size_t, ctypes.c_size_t, _f32p]
+        L.ref_mxfp4_matvec.argtypes = [ctypes.c_size_t, ctypes.c_size_t, _u8p, _u8p, _f32p, _f32p]
+        L.ref_cpu_matvec_supported.argtypes = [ctypes.c_uint32, ctypes.c_size_t]
+        L.ref_cpu_matvec_create.restype = ctypes.c_void_p
+        L.ref_cpu_matvec_create.argtypes = [ctypes.c_uint32, _f32p, ctypes.c_size_t, ctypes.c_size_t]
+        L.ref_cpu_matvec_destroy.argtypes = [ctypes.c_void_p]
+        L.ref_cpu_matvec_run.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+                                         ctypes.c_size_t, _f32p, ctypes.c_size_t]
+        L.ref_cpu_matvec_parallel.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, _f32p,
+                                              ctypes.c_size_t, ctypes.c_int]
+        self.L = L
+
+    def error(self) -> str:
+        return self.L.ref_last_error().decode(errors="replace")
+
+    def decode(self, e: int, packed: np.ndarray, count: int) -> np.ndarray:
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        out = np.empty(count, dtype=np.float32)
+        self.L.ref_gguf_decode_stream(e, _p(packed, _u8p), count, _p(out, _f32p))
+        return out
+
+    def decode_runs(self, e: int, packed: np.ndarray, count: int) -> np.ndarray:
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        out = np.empty(count, dtype=np.float32)
+        self.L.ref_gguf_decode_run_stream(e, _p(packed, _u8p), count, _p(out, _f32p))
+        return out
+
+    def to_float(self, ggml_type: int, packed: np.ndarray, count: int) -> np.ndarray:
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        out = np.empty(count, dtype=np.float32)
+        self.L.ref_ggml_to_float(ggml_type, packed.ctypes.data, _p(out, _f32p), count)
+        return out
+
+    def quantize(self, ggml_type: int, values: np.ndarray, rows: int, per_row: int) -> np.ndarray:
+        values = np.ascontiguousarray(values, dtype=np.float32)
+        out = np.zeros(rows * self.L.ref_ggml_row_size(ggml_type, per_row), dtype=np.uint8)
+        self.L.ref_ggml_quantize(ggml_type, _p(values, _f32p), out.ctypes.data, rows, per_row)
+        return out.reshape(rows, -1)
+
+    def row_size(self, ggml_type: int, n: int) -> int:
+        return int(self.L.ref_ggml_row_size(ggml_type, n))
+
+    def mxfp4_decode_rows(self, weights, scales, rows, cols, first=0, count=None) -> np.ndarray:
+        count = rows - first if count is None else count
+        out = np.empty((count, cols), dtype=np.float32)
+        w = np.ascontiguousarray(weights, dtype=np.uint8)
+        s = np.ascontiguousarray(scales, dtype=np.uint8)
+        if self.L.ref_mxfp4_decode_rows(rows, cols, _p(w, _u8p), _p(s, _u8p), first, count, _p(out, _f32p)):
+            raise ValueError(self.error())
+        return out
+
+    def mxfp4_matvec(self, weights, scales, rows, cols, x) -> np.ndarray:
+        out = np.empty(rows, dtype=np.float32)
+        w = np.ascontiguousarray(weights, dtype=np.uint8)
+        s = np.ascontiguousarray(scales, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if self.L.ref_mxfp4_matvec(rows, cols, _p(w, _u8p), _p(s, _u8p), _p(x, _f32p), _p(out, _f32p)):
+            raise ValueError(self.error())
+        return out
+
+    def cpu_matvec(self, ggml_type: int, weights: np.ndarray, x: np.ndarray, in_: int, out: int,
+                   threads: int = 1) -> np.ndarray:
+        """kadan::text::CpuMatvec over 64-column units on `threads` workers."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+        rows = x.size // in_
+        h = self.L.ref_cpu_matvec_create(ggml_type, _p(x, _f32p), in_, rows)
+        if not h:
+            raise ValueError(self.error())
+        try:
+            y = np.empty((rows, out), dtype=np.float32)
+            w = np.ascontiguousarray(weights, dtype=np.uint8)
+            rc = self.L.ref_cpu_matvec_parallel(h, w.ctypes.data, w.size // out, _p(y, _f32p), out, threads)
+            if rc:
+                raise ValueError(self.error())
+            return y
+        finally:
+            self.L.ref_cpu_matvec_destroy(h)
+
+
+def xorshift32_stream(state: int, n: int) -> np.ndarray:
+    """The reference tests' xorshift32 generator (tests/gguf_quantization.cpp:93-98)."""
+    out = np.empty(n, dtype=np.uint32)
+    s = state & 0xFFFFFFFF
+    for i in range(n):
+        s ^= (s << 13) & 0xFFFFFFFF
+        s ^= s >> 17
+        s ^= (s << 5) & 0xFFFFFFFF
+        out[i] = s
+    return out

@@ -1,0 +1,244 @@
+// Test infrastructure only. A C entry layer over the reference worker's own
+// CPU code, compiled in place from the read-only reference tree (see Makefile),
+// so Python tests and bench.py's CPU baseline can call it through ctypes.
+//
+// Wrapped reference functions:
+//   kadan::gguf::decode / decode_run     IW/include/kadan/gguf_quantization.hpp:631-916
+//   ggml to_float / quantize_chunk       IW/third_party/ggml/src/ggml.c (type traits)
+//   kadan::quantization::decode_rows     IW/src/weights/quantization.cpp:193-205
+//   kadan::quantization::matvec          IW/src/weights/quantization.cpp:208-247
+//   kadan::text::CpuMatvec               IW/src/models/text/cpu_matvec.cpp:18-66
+// (IW = services/hikari/inference_worker). The 64-column work units of
+// ref_cpu_matvec_parallel follow GgufWeights::project's host split
+// (IW/src/models/text/gguf_weights.cpp:400-446).
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <span>
+#include <thread>
+#include <vector>
+
+#include "cpu_matvec.hpp"
+#include "kadan/gguf_quantization.hpp"
+#include "kadan/quantization.hpp"
+#include <ggml-cpu.h>
+#include <ggml.h>
+
+namespace {
+thread_local char last_error[256];
+
+int fail(const std::exception& e) {
+    std::strncpy(last_error, e.what(), sizeof(last_error) - 1);
+    return -1;
+}
+}  // namespace
+
+extern "C" {
+
+const char* ref_last_error() {
+    return last_error;
+}
+
+// kadan::gguf::Encoding numbering (q3_k=0, q4_k, q8_0, q6_k, iq3_xxs, iq4_nl,
+// iq4_xs, iq2_s, iq3_s, bf16=9).
+float ref_gguf_decode(int encoding, const unsigned char* block, size_t element) {
+    return kadan::gguf::decode(kadan::gguf::Encoding(encoding), block, element);
+}
+
+size_t ref_gguf_block_values(int encoding) {
+    return kadan::gguf::block_values(kadan::gguf::Encoding(encoding));
+}
+
+size_t ref_gguf_block_bytes(int encoding) {
+    return kadan::gguf::block_bytes(kadan::gguf::Encoding(encoding));
+}
+
+int ref_gguf_encoding(uint32_t ggml_type) {
+    const auto e = kadan::gguf::encoding(ggml_type);
+    return e ? int(*e) : -1;
+}
+
+// Elementwise decode of `count` values of a packed stream, as the reference's
+// gguf_decode_kernel does per thread (IW/src/cuda/h3_compute.cu:76-95).
+void ref_gguf_decode_stream(
+    int encoding, const unsigned char* packed, size_t count, float* out
+) {
+    const auto e = kadan::gguf::Encoding(encoding);
+    const auto values = kadan::gguf::block_values(e), bytes = kadan::gguf::block_bytes(e);
+    for (size_t i = 0; i < count; ++i)
+        out[i] = kadan::gguf::decode(e, packed + i / values * bytes, i % values);
+}
+
+// decode_run over every aligned run of eight of a packed stream.
+void ref_gguf_decode_run_stream(
+    int encoding, const unsigned char* packed, size_t count, float* out
+) {
+    const auto e = kadan::gguf::Encoding(encoding);
+    const auto values = kadan::gguf::block_values(e), bytes = kadan::gguf::block_bytes(e);
+    for (size_t i = 0; i < count; i += 8)
+        kadan::gguf::decode_run(e, packed + i / values * bytes, i % values, out + i);
+}
+
+float ref_fp16_to_fp32(uint16_t bits) {
+    return ggml_fp16_to_fp32(ggml_fp16_t(bits));
+}
+
+int64_t ref_ggml_blck_size(uint32_t type) {
+    return ggml_blck_size(ggml_type(type));
+}
+
+size_t ref_ggml_type_size(uint32_t type) {
+    return ggml_type_size(ggml_type(type));
+}
+
+size_t ref_ggml_row_size(uint32_t type, int64_t n) {
+    return ggml_row_size(ggml_type(type), n);
+}
+
+void ref_ggml_to_float(uint32_t type, const void* src, float* dst, int64_t n) {
+    ggml_get_type_traits(ggml_type(type))->to_float(src, dst, n);
+}
+
+size_t ref_ggml_quantize(
+    uint32_t type, const float* src, void* dst, int64_t rows, int64_t per_row
+) {
+    return ggml_quantize_chunk(ggml_type(type), src, dst, 0, rows, per_row, nullptr);
+}
+
+// kadan::quantization MXFP4 view over the safetensors expert layout.
+int ref_mxfp4_decode_rows(
+    size_t rows,
+    size_t columns,
+    const uint8_t* weights,
+    const uint8_t* scales,
+    size_t first,
+    size_t count,
+    float* out
+) {
+    try {
+        using namespace kadan::quantization;
+        Matrix m{
+            Encoding::mxfp4,
+            rows,
+            columns,
+            std::span(weights, rows * columns / 2),
+            std::span(scales, rows * columns / 32),
+            {}
+        };
+        const auto decoded = decode_rows(m, first, count, count * columns * sizeof(float));
+        std::memcpy(out, decoded.data(), decoded.size() * sizeof(float));
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_mxfp4_matvec(
+    size_t rows,
+    size_t columns,
+    const uint8_t* weights,
+    const uint8_t* scales,
+    const float* input,
+    float* out
+) {
+    try {
+        using namespace kadan::quantization;
+        Matrix m{
+            Encoding::mxfp4,
+            rows,
+            columns,
+            std::span(weights, rows * columns / 2),
+            std::span(scales, rows * columns / 32),
+            {}
+        };
+        matvec(m, std::span(input, columns), std::span(out, rows));
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_cpu_matvec_supported(uint32_t type, size_t in) {
+    return kadan::text::CpuMatvec::supported(type, in) ? 1 : 0;
+}
+
+void* ref_cpu_matvec_create(uint32_t type, const float* input, size_t in, size_t rows) {
+    try {
+        return new kadan::text::CpuMatvec(type, std::span(input, in * rows), in);
+    } catch (const std::exception& e) {
+        fail(e);
+        return nullptr;
+    }
+}
+
+void ref_cpu_matvec_destroy(void* handle) {
+    delete static_cast<kadan::text::CpuMatvec*>(handle);
+}
+
+int ref_cpu_matvec_run(
+    void* handle,
+    const void* weights,
+    size_t row_bytes,
+    size_t first,
+    size_t end,
+    float* output,
+    size_t out
+) {
+    try {
+        const auto* p = static_cast<const kadan::text::CpuMatvec*>(handle);
+        p->run(
+            static_cast<const std::byte*>(weights),
+            row_bytes,
+            first,
+            end,
+            std::span(output, p->rows() * out),
+            out
+        );
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// The worker's host split: 64-column units claimed by `threads` workers.
+int ref_cpu_matvec_parallel(
+    void* handle,
+    const void* weights,
+    size_t row_bytes,
+    float* output,
+    size_t out,
+    int threads
+) {
+    constexpr size_t unit_columns = 64;
+    const auto* p = static_cast<const kadan::text::CpuMatvec*>(handle);
+    const size_t units = (out + unit_columns - 1) / unit_columns;
+    std::atomic<size_t> next{0};
+    std::atomic<int> status{0};
+    auto work = [&] {
+        for (size_t u; (u = next.fetch_add(1)) < units;) {
+            const size_t first = u * unit_columns;
+            const size_t end = first + unit_columns < out ? first + unit_columns : out;
+            try {
+                p->run(
+                    static_cast<const std::byte*>(weights),
+                    row_bytes,
+                    first,
+                    end,
+                    std::span(output, p->rows() * out),
+                    out
+                );
+            } catch (const std::exception& e) {
+                status = fail(e);
+            }
+        }
+    };
+    std::vector<std::thread> pool;
+    for (int t = 1; t < threads; ++t)
+        pool.emplace_back(work);
+    work();
+    for (auto& t : pool)
+        t.join();
+    return status.load();
+}
+}

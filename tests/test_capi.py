@@ -1,0 +1,90 @@
+"""The C ABI library loads, exports every declared entry point, and rejects
+bad jobs on the host before touching the device (no GPU needed)."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared_symbols():
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        names |= set(re.findall(r"KB200_API\s+[\w\s\*]+?\b(kb200_\w+)\s*\(", header.read_text()))
+    return sorted(names)
+
+
+def test_every_declared_symbol_is_exported(kb):
+    names = declared_symbols()
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(kb.lib, name), name
+
+
+def test_status_names_follow_reference_messages(kb):
+    assert kb.lib.kb200_status_name(kb.NONFINITE_WEIGHT) == b"h3_cuda_nonfinite_weight"
+    assert kb.lib.kb200_status_name(kb.ALIAS) == b"h3_cuda_alias"
+    assert kb.lib.kb200_status_name(kb.CANCELLED) == b"h3_cuda_cancelled"
+
+
+def test_block_geometry_matches_oracle(kb, oracle):
+    for e in (kb.Q8_0, kb.Q4_K, kb.Q6_K, kb.Q3_K, kb.IQ4_NL, kb.IQ4_XS, kb.BF16):
+        assert kb.lib.kb200_encoding_supported(e) == 1
+        assert kb.block_values(e) == oracle.block_values(e)
+        assert kb.block_bytes(e) == oracle.block_bytes(e)
+    for e in (kb.IQ3_XXS, kb.IQ2_S, kb.IQ3_S, 42):
+        assert kb.lib.kb200_encoding_supported(e) == 0
+
+
+FAKE_W, FAKE_X, FAKE_Y = 0x10000000, 0x20000000, 0x30000000
+
+
+def job(kb, **kw):
+    base = dict(weights=FAKE_W, input=FAKE_X, output=FAKE_Y, status=None, row_bytes=2304, stride=64,
+                in_=4096, columns=64, rows=1, encoding=kb.Q4_K)
+    base.update(kw)
+    return kb.GemvJob(**base)
+
+
+def call(kb, jobs):
+    arr = (kb.GemvJob * len(jobs))(*jobs)
+    return kb.lib.kb200_gguf_gemv_batch(arr, len(jobs), None)
+
+
+def test_unsupported_before_any_launch(kb):
+    # gguf_batch_supported rules (IW/include/kadan/gguf_batch_partition.hpp:12-31).
+    assert call(kb, [job(kb, encoding=kb.IQ2_S)]) == kb.UNSUPPORTED
+    assert call(kb, [job(kb, in_=4100)]) == kb.UNSUPPORTED
+    assert call(kb, [job(kb, rows=0)]) == kb.UNSUPPORTED
+    assert call(kb, [job(kb, rows=4097)]) == kb.UNSUPPORTED
+    assert call(kb, [job(kb, in_=4096 + 128)]) == kb.UNSUPPORTED  # not whole Q4_K blocks
+    # one bad job rejects the whole batch
+    assert call(kb, [job(kb), job(kb, encoding=99)]) == kb.UNSUPPORTED
+
+
+def test_invalid_and_alias_are_reported(kb):
+    assert call(kb, [job(kb, weights=None)]) == kb.INVALID
+    assert call(kb, [job(kb, row_bytes=100)]) == kb.INVALID
+    assert call(kb, [job(kb, stride=10)]) == kb.INVALID
+    assert call(kb, [job(kb, output=FAKE_X + 64)]) == kb.ALIAS
+    # output of one job over the input of another
+    assert call(kb, [job(kb), job(kb, output=FAKE_X + 1024, input=0x50000000)]) == kb.ALIAS
+    assert b"alias" in kb.lib.kb200_last_error()
+
+
+def test_path_selection(kb):
+    assert kb.gemv_path(job(kb)) == 1
+    assert kb.gemv_path(job(kb, weights=FAKE_W + 2)) == 0          # unaligned base
+    assert kb.gemv_path(job(kb, encoding=kb.Q8_0, in_=160, row_bytes=170)) == 0
+    assert kb.gemv_path(job(kb, encoding=kb.Q3_K, row_bytes=16 * 110)) == 0
+    assert kb.gemv_path(job(kb, encoding=kb.F32, row_bytes=4096 * 4)) == 0
+    assert kb.gemv_path(job(kb, encoding=kb.IQ2_S)) == -1
+
+
+def test_dequant_rejects_partial_blocks(kb):
+    assert kb.lib.kb200_gguf_dequant(kb.Q4_K, FAKE_W, 100, FAKE_Y, None, None) == kb.INVALID
+    assert kb.lib.kb200_gguf_dequant(kb.IQ2_S, FAKE_W, 256, FAKE_Y, None, None) == kb.UNSUPPORTED
+    assert kb.lib.kb200_gguf_dequant(kb.Q4_K, FAKE_W, 256, FAKE_W + 16, None, None) == kb.ALIAS

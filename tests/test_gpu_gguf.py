@@ -1,0 +1,196 @@
+"""GPU parity of the GGUF dequant and GEMV kernels against the pinned oracle.
+
+Bars: dequant bit-exact (integer/byte work); GEMV outputs within the stated
+tolerance 1e-3 of the double-precision oracle, measured as
+max|y - ref| / max(max|ref|, 1) (the reference's GEMV check,
+IW/tests/gguf_text.cpp:247-250).
+"""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def to_dev(a, cuda):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+@pytest.mark.parametrize("name", ["q8_0", "q4_k", "q6_k", "q3_k", "iq4_nl", "iq4_xs", "bf16"])
+def test_dequant_bit_exact_reference_blocks(kb, oracle, cuda, name):
+    import torch
+
+    from golden.make_golden import canonical_digest, reference_blocks
+
+    spec = json.loads((GOLDEN / "gguf_blocks.json").read_text())["encodings"][name]
+    blocks = reference_blocks(spec["encoding"], spec["trials"])
+    n = blocks.shape[0] * kb.block_values(spec["encoding"])
+    out = torch.empty(n, dtype=torch.float32, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    kb.gguf_dequant(spec["encoding"], to_dev(blocks, cuda), n, out, status)
+    got = out.cpu().numpy()
+    assert canonical_digest(got) == spec["sha256_expected"]
+    want = oracle.decode(spec["encoding"], blocks, n)
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got.view(np.uint32)[~nan], want.view(np.uint32)[~nan])
+    assert int(status.item()) == (1 if spec["nan_count"] or np.isinf(want).any() else 0)
+
+
+def gemv_case(kb, oracle, cuda, enc, in_, out, rows, seed=0, x_dtype="f32"):
+    import torch
+
+    from kadan_b200 import synth
+
+    if enc in (kb.Q8_0, kb.Q4_K, kb.Q6_K):
+        w = synth.gguf(enc, out, in_, seed=seed)
+    else:
+        rng = np.random.default_rng(seed)
+        w = rng.integers(0, 256, size=(out, in_ // kb.block_values(enc) * kb.block_bytes(enc)), dtype=np.uint8)
+        if enc != kb.BF16:
+            # keep the fp16 scales finite and modest
+            bb, bv = kb.block_bytes(enc), kb.block_values(enc)
+            off = {kb.Q3_K: 108}.get(enc, 0)
+            blocks = w.reshape(-1, bb)
+            blocks[:, off:off + 2] = (np.abs(rng.standard_normal(len(blocks))) * 0.02).astype(np.float16).view(
+                np.uint8).reshape(-1, 2)
+        else:
+            w = (rng.standard_normal((out, in_)) * 0.05).astype(np.float32).view(np.uint32)
+            w = ((w >> 16).astype(np.uint16)).view(np.uint8).reshape(out, -1)
+    x = synth.activations(rows * in_, seed=seed + 1, dtype=x_dtype).reshape(rows, in_)
+    want = oracle.gemv_f64(enc, w, x, in_, out)
+    y = kb.gguf_gemv(enc, to_dev(w, cuda), to_dev(x, cuda), in_=in_, columns=out)
+    torch.cuda.synchronize()
+    return y.cpu().numpy(), want
+
+
+@pytest.mark.parametrize("enc_name", ["q8_0", "q4_k", "q6_k"])
+@pytest.mark.parametrize("in_,out", [(4096, 37), (4096, 1), (8192, 19), (14336, 64), (2048, 300), (256, 8)])
+@pytest.mark.parametrize("rows", [1, 2, 3])
+def test_gemv_staged_parity(kb, oracle, cuda, enc_name, in_, out, rows):
+    enc = {"q8_0": kb.Q8_0, "q4_k": kb.Q4_K, "q6_k": kb.Q6_K}[enc_name]
+    if enc == kb.Q6_K and (in_ // 256) % 8:
+        pytest.skip("Q6_K rows of this width are not 16-byte multiples (generic path covers them)")
+    y, want = gemv_case(kb, oracle, cuda, enc, in_, out, rows)
+    assert rel_err(y, want) <= TOL
+
+
+@pytest.mark.parametrize("rows", [8, 17])
+def test_gemv_row_groups(kb, oracle, cuda, rows):
+    y, want = gemv_case(kb, oracle, cuda, kb.Q4_K, 4096, 40, rows)
+    assert rel_err(y, want) <= TOL
+
+
+@pytest.mark.parametrize("enc_name,in_", [("q8_0", 160), ("q6_k", 256), ("q3_k", 512), ("iq4_nl", 96),
+                                          ("iq4_xs", 512), ("bf16", 200), ("q4_k", 512)])
+@pytest.mark.parametrize("rows", [1, 5])
+def test_gemv_generic_parity(kb, oracle, cuda, enc_name, in_, rows):
+    enc = getattr(kb, enc_name.upper())
+    y, want = gemv_case(kb, oracle, cuda, enc, in_, 23, rows)
+    assert rel_err(y, want) <= TOL
+
+
+def test_gemv_golden_cpu_matvec_fixture(kb, cuda):
+    import torch
+
+    g = np.load(GOLDEN / "cpu_matvec.npz")
+    x = to_dev(g["input"], cuda)
+    for name, enc in (("q8_0", kb.Q8_0), ("q4_k", kb.Q4_K), ("q6_k", kb.Q6_K)):
+        y = kb.gguf_gemv(enc, to_dev(g[f"{name}_packed"], cuda), x, in_=512, columns=37)
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), g[f"{name}_f64"]) <= TOL
+
+
+def test_config1_golden(kb, cuda):
+    import torch
+
+    from kadan_b200 import synth
+
+    g = np.load(GOLDEN / "config1_q8_0.npz")
+    w = to_dev(synth.q8_0(4096, 4096, seed=0), cuda)
+    y = kb.gguf_gemv(kb.Q8_0, w, to_dev(g["x"], cuda), in_=4096, columns=4096)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy()[0], g["y_f64"]) <= TOL
+
+
+def test_batch_mixed_encodings_shared_input(kb, oracle, cuda):
+    import torch
+
+    from kadan_b200 import synth
+
+    in_ = 4096
+    x = synth.activations(2 * in_, seed=9).reshape(2, in_)
+    xd = to_dev(x, cuda)
+    cases = [(kb.Q4_K, 100), (kb.Q8_0, 33), (kb.Q6_K, 65), (kb.Q4_K, 8)]
+    jobs, outs, wants = [], [], []
+    for i, (enc, out) in enumerate(cases):
+        w = synth.gguf(enc, out, in_, seed=20 + i)
+        wd = to_dev(w, cuda)
+        y = torch.full((2, out), float("nan"), device=cuda)
+        outs.append((wd, y))
+        jobs.append(kb.gemv_job(enc, wd, xd, y, in_=in_, columns=out, rows=2))
+        wants.append(oracle.gemv_f64(enc, w, x, in_, out))
+    kb.gguf_gemv_batch(jobs)
+    torch.cuda.synchronize()
+    for (_, y), want in zip(outs, wants):
+        assert rel_err(y.cpu().numpy(), want) <= TOL
+
+
+def test_strided_output_and_status(kb, oracle, cuda):
+    import torch
+
+    from kadan_b200 import synth
+
+    in_, out = 4096, 24
+    w = synth.q4_k(out, in_, seed=4)
+    x = synth.activations(2 * in_, seed=5).reshape(2, in_)
+    y = torch.full((2, 3 * out), -7.0, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    wd = to_dev(w, cuda)
+    kb.gguf_gemv_batch([kb.gemv_job(kb.Q4_K, wd, to_dev(x, cuda), y[:, out:], in_=in_, columns=out, rows=2,
+                                    stride=3 * out, status=status)])
+    torch.cuda.synchronize()
+    yy = y.cpu().numpy()
+    assert rel_err(yy[:, out:2 * out], oracle.gemv_f64(kb.Q4_K, w, x, in_, out)) <= TOL
+    assert np.all(yy[:, :out] == -7.0) and np.all(yy[:, 2 * out:] == -7.0)
+    assert status.item() == 0
+    # An infinite fp16 d in one block sets the job's status bit.
+    bad = w.copy()
+    bad[5, 144 * 3: 144 * 3 + 2] = [0x00, 0x7C]
+    kb.gguf_gemv_batch([kb.gemv_job(kb.Q4_K, to_dev(bad, cuda), to_dev(x, cuda), y[:, :out], in_=in_,
+                                    columns=out, rows=2, stride=3 * out, status=status)])
+    torch.cuda.synchronize()
+    assert status.item() == 1
+    assert kb.take_device_error() == 0
+
+
+def test_full_size_gate_projection_against_exact_dequant(kb, cuda):
+    """Config 2 gate (14336 x 4096 Q4_K) at full size: the GEMV equals the
+    float64 product of the bit-exact dequantised weights."""
+    import torch
+
+    from kadan_b200 import synth
+
+    out, in_ = 14336, 4096
+    wd = synth.device_gguf(kb.Q4_K, out, in_, seed=3, device=cuda)
+    x = torch.randn(1, in_, device=cuda, generator=torch.Generator(device=cuda).manual_seed(1)).half().float()
+    y = kb.gguf_gemv(kb.Q4_K, wd, x, in_=in_, columns=out)
+    dec = torch.empty(out * in_, dtype=torch.float32, device=cuda)
+    kb.gguf_dequant(kb.Q4_K, wd, out * in_, dec)
+    want = (dec.view(out, in_).double() @ x.double().T).T
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), want.cpu().numpy()) <= TOL
+    # Linearity in the input (size-independent property).
+    x2 = torch.randn(1, in_, device=cuda, generator=torch.Generator(device=cuda).manual_seed(2))
+    y2 = kb.gguf_gemv(kb.Q4_K, wd, x2, in_=in_, columns=out)
+    y3 = kb.gguf_gemv(kb.Q4_K, wd, (2.0 * x - x2).contiguous(), in_=in_, columns=out)
+    torch.cuda.synchronize()
+    assert rel_err(y3.cpu().numpy(), (2.0 * y - y2).cpu().numpy()) <= TOL
