@@ -116,8 +116,9 @@ typedef struct kb200_gemv_job {
  * jobs: host array. */
 KB200_API int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream);
 
-/* Which kernel kb200_gguf_gemv_batch selects for a job: 1 = bulk-copy staged
- * sm_100a kernel, 0 = generic kernel (unaligned rows), -1 = unsupported. */
+/* Which kernel kb200_gguf_gemv_batch selects for a job: 2 = tensor-pipe Q4_K
+ * kernel (TMA tiles + mma.sync), 1 = bulk-copy staged CUDA-core kernel,
+ * 0 = generic kernel (unaligned rows), -1 = unsupported. */
 KB200_API int kb200_gemv_path(const kb200_gemv_job* job);
 
 /* ---------------------------------------------------------------------------

@@ -32,6 +32,7 @@
 #include <mutex>
 #include <vector>
 
+#include "gemv_mma.hpp"
 #include "gguf_formats.cuh"
 #include "kb200_device.cuh"
 #include "kb200_host.hpp"
@@ -624,7 +625,11 @@ int check_job(const kb200_gemv_job& j) {
     return KB200_OK;
 }
 
+// 2 = tensor-pipe kernel (Q4_K), 1 = bulk-copy staged CUDA-core kernel,
+// 0 = generic kernel.
 int path_of(const kb200_gemv_job& j) {
+    if (q4k_mma_eligible(j))
+        return 2;
     return staged_format(j.encoding) && aligned(j.weights, 16) && j.row_bytes % 16 == 0
                    && aligned(j.input, 16)
                ? 1
@@ -671,7 +676,7 @@ int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream
     for (size_t i = 0; i < count; ++i) {
         const auto& j = jobs[i];
         const int path = path_of(j);
-        const int group = path ? (j.rows == 1 ? 1 : 2) : (j.rows == 1 ? 1 : KB200_BATCH_ROWS);
+        const int group = path == 2 ? 0 : path ? (j.rows == 1 ? 1 : 2) : (j.rows == 1 ? 1 : KB200_BATCH_ROWS);
         auto it = std::find_if(groups.begin(), groups.end(), [&](const auto& g) {
             return g.first.path == path && g.first.encoding == j.encoding && g.first.group == group;
         });
@@ -682,6 +687,11 @@ int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream
         it->second.push_back(&j);
     }
     for (const auto& [key, members] : groups) {
+        if (key.path == 2) {
+            if (const int s = launch_q4k_mma(members, stream))
+                return s;
+            continue;
+        }
         for (size_t first = 0; first < members.size(); first += kMaxJobs) {
             GemvParams p;
             std::memset(&p, 0, sizeof(p));

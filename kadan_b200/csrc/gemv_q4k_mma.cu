@@ -1,0 +1,639 @@
+// Q4_K decode GEMV on the tensor pipe (sm_100a), T <= 8 input rows per pass.
+//
+// Replaces gguf_matvec_batch_kernel<q4_k>
+// (services/hikari/inference_worker/src/cuda/h3_compute.cu:165-257) for
+// 16-byte aligned rows. The reference decodes every weight to fp32 on the
+// CUDA cores, several instructions per weight; at HBM speed that is more work
+// than an SM can issue. Here the products run on the integer tensor pipe:
+//
+//   Q4_K value :  w = d*sc_g*q - dmin*m_g   (q 4-bit, sc_g/m_g 6-bit per 32)
+//   A operand  :  low nibbles  q      = packed & 0x0F0F0F0F  (u8, 0..15)
+//                 high nibbles 16*q   = packed & 0xF0F0F0F0  (u8, 0..240)
+//   B operand  :  the activations of one super-block, quantised to two int8
+//                 levels, x ~= s*(h + l/256) with s = absmax/127 per 256
+//                 values and token (about 15 bits); h and l sit in adjacent
+//                 N columns, 4 input rows x {h, l} = 8 columns per MMA
+//   MMA        :  mma.m16n8k32.u8.s8 -> exact int32 sum over one sub-block
+//   scales     :  I = sum_g (16 sc_g) C_g(low) + sc_g C_g(high)   (IMAD)
+//   min term   :  sum_g m_g * sum_{k in g} x_k, one fp16 m16n8k8 MMA per block
+//                 (m exact, the fp32 group sums split into fp16 hi + lo)
+//   epilogue   :  acc += (d*s/16) * (I_h + I_l/256) - (256 dmin) * C_min
+//
+// CTA = 4 consumer warps + 1 producer lane. A tile is R weight rows (R = 64,
+// 32 or 16, chosen per launch so that small outputs still fill the GPU) over
+// all of K; with R < 64 the warps split K (2 or 4 ways) and reduce in shared
+// memory at the end. The producer streams each stage (R rows x 128/R
+// super-blocks, 18 KB) with one 3-D TMA tile load per super-block column into
+// a 3-stage ring; a 144-byte row pitch keeps every fragment load free of bank
+// conflicts. The activations of a whole K segment (all of K at decode shapes)
+// are quantised once per CTA and job, so consumer warps run without any
+// barrier between them: wait for a stage, issue its MMAs, release it.
+//
+// Launched with programmatic dependent launch: the producer starts streaming
+// weights while the previous kernel in the stream is still finishing; the
+// consumers wait (griddepcontrol.wait) before they read activations or write
+// outputs. Weights must therefore not be produced by the immediately
+// preceding kernel of the stream.
+#include <algorithm>
+#include <cstring>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <mutex>
+#include <vector>
+
+#include "gemv_mma.hpp"
+#include "gguf_formats.cuh"
+#include "kb200_device.cuh"
+#include "kb200_host.hpp"
+
+namespace kb200 {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kConsumerThreads = 32 * kWarps;
+constexpr int kThreadsQ = kConsumerThreads + 32;
+constexpr int kBlockBytes = 144;
+constexpr int kStageUnits = 128;  // rows x super-blocks per stage
+constexpr int kStages = 3;
+constexpr int kStageBytes = kStageUnits * kBlockBytes;  // 18432
+constexpr int kMaxJobsQ = 32;
+
+struct alignas(64) MmaJob {
+    CUtensorMap map;  // dims {18 x u64, blocks, rows}, box {18, 1, R}
+    const float* input;
+    float* output;
+    unsigned* status;
+    uint64_t stride;
+    uint32_t in, columns, rows, first_tile;
+    uint32_t row_groups, group_rows, nblocks, pad;
+};
+
+struct MmaParams {
+    MmaJob jobs[kMaxJobsQ];
+    uint32_t count, total_tiles;
+    uint32_t tile_rows;  // R: 64, 32 or 16
+    unsigned* watchdog;
+};
+
+// Activation segment: per super-block and token, the quantised h/l operands
+// in B-fragment order ([j][t][part][4 words], 512 bytes), the minimum-term B
+// operands ([part][t] fp16x2, 32 bytes) and the scale s (4 bytes).
+constexpr int kTokenBlockBytes = 512;
+constexpr int kMinBytes = 32;
+constexpr int kTokenBlockTotal = kTokenBlockBytes + kMinBytes + 4;
+constexpr int kSegBudget = 16 * 1024;
+
+struct Layout {
+    static constexpr int kStagesOff = 0;
+    static constexpr int kSegOff = kStages * kStageBytes;
+    static constexpr int kRedOff = kSegOff + kSegBudget;       // split-K partials
+    static constexpr int kRedBytes = kConsumerThreads * 4 * 4;  // [nt<=2][2][thread]
+    static constexpr int kBarOff = kRedOff + kRedBytes;
+    static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
+};
+
+// Segment of `rows` tokens: the most whole stages (multiples of `bps`
+// super-blocks) that fit kSegBudget; operands first, then minimum-term
+// operands, then scales. blocks == 0 means not even one stage fits (the host
+// never launches such a geometry, see segment_fits()).
+__host__ __device__ constexpr int segment_blocks(int rows, int bps) {
+    return kSegBudget / (rows * kTokenBlockTotal) / bps * bps;
+}
+
+struct Segment {
+    int blocks, rows;
+    __device__ Segment(int r, int bps) : blocks(segment_blocks(r, bps)), rows(r) {}
+    __device__ uint8_t* frag(uint8_t* smem) const { return smem + Layout::kSegOff; }
+    __device__ uint32_t* minb(uint8_t* smem) const {
+        return reinterpret_cast<uint32_t*>(smem + Layout::kSegOff + blocks * rows * kTokenBlockBytes);
+    }
+    __device__ float* scales(uint8_t* smem) const {
+        return reinterpret_cast<float*>(minb(smem) + blocks * rows * (kMinBytes / 4));
+    }
+};
+
+__device__ __forceinline__ int find_job(const MmaParams& p, uint32_t tile) {
+    int low = 0, high = int(p.count);
+    while (high - low > 1) {
+        const int mid = (low + high) / 2;
+        if (p.jobs[mid].first_tile <= tile)
+            low = mid;
+        else
+            high = mid;
+    }
+    return low;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+            smem_addr(dst)
+        ),
+        "l"(map),
+        "r"(c0),
+        "r"(c1),
+        "r"(c2),
+        "r"(smem_addr(bar))
+        : "memory"
+    );
+}
+
+__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+// C = A(16x32 u8) * B(32x8 s8), exact int32.
+__device__ __forceinline__ void imma(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0)
+    );
+}
+
+__device__ __forceinline__ void mma1688(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(b0)
+    );
+}
+
+__device__ __forceinline__ uint32_t pack_half2(__half2 h) {
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Round-to-nearest-even integer of |v| < 2^22 through the 1.5*2^23 bias.
+__device__ __forceinline__ int round_int(float v) {
+    return __float_as_int(v + 12582912.f) - 0x4B400000;
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return __byte_perm(__byte_perm(uint32_t(a), uint32_t(b), 0x0040u), __byte_perm(uint32_t(c), uint32_t(d), 0x0040u), 0x5410u);
+}
+
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_dependents_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Quantise the activations of super-blocks [blk0, blk0 + nblk) for the
+// segment's tokens. One warp per (block, token): lane L owns values
+// 8L..8L+7, which are the B registers b0 (k = 4t..4t+3 <-> values 8t..8t+3)
+// and b1 (k = 16+4t.. <-> values 8t+4..8t+7) of sub-block G = L/4, t = L%4.
+__device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, size_t in, int blk0, int nblk) {
+    const int rows = seg.rows;
+    auto* frag = reinterpret_cast<uint32_t*>(seg.frag(smem));
+    uint32_t* minb = seg.minb(smem);
+    float* scales = seg.scales(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = lane >> 2, t = lane & 3;
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (in & 3) == 0;
+    for (int item = warp; item < nblk * rows; item += kWarps) {
+        const int blk = item / rows, tok = item % rows;
+        const float* xr = x + size_t(tok) * in + size_t(blk0 + blk) * 256 + lane * 8;
+        float v[8];
+        if (vec) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(xr)), b = __ldg(reinterpret_cast<const float4*>(xr) + 1);
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                v[i] = __ldg(xr + i);
+        }
+        float m = 0.f, sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            m = fmaxf(m, fabsf(v[i]));
+            sum += v[i];
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1)
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        const float next = __shfl_xor_sync(0xffffffffu, sum, 4);  // sum of sub-block G ^ 1
+        const float inv = m > 0.f ? 127.f / m : 0.f;
+        int h[8], l[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float y = v[i] * inv;
+            h[i] = round_int(y);
+            l[i] = max(-127, min(127, round_int((y - float(h[i])) * 256.f)));
+        }
+        const int slot = blk * rows + tok;
+        uint32_t* base = frag + slot * (kTokenBlockBytes / 4);
+        const int idx = (((G >> 1) * 4 + t) * 2) * 4 + (G & 1) * 2;  // part h; part l is +4
+        base[idx] = pack4(h[0], h[1], h[2], h[3]);
+        base[idx + 1] = pack4(h[4], h[5], h[6], h[7]);
+        base[idx + 4] = pack4(l[0], l[1], l[2], l[3]);
+        base[idx + 5] = pack4(l[4], l[5], l[6], l[7]);
+        // Minimum term B' for lane (g, t') = sums of sub-blocks 2t', 2t'+1
+        // (scaled by 1/256) split into fp16 hi and lo: written by lanes 8t'.
+        if ((lane & 7) == 0) {
+            const float s0 = sum * (1.f / 256.f), s1 = next * (1.f / 256.f);
+            const __half2 hi = __floats2half2_rn(s0, s1);
+            const float2 hf = __half22float2(hi);
+            const __half2 lo = __floats2half2_rn(s0 - hf.x, s1 - hf.y);
+            uint32_t* mb = minb + slot * (kMinBytes / 4);
+            mb[lane >> 3] = pack_half2(hi);
+            mb[4 + (lane >> 3)] = pack_half2(lo);
+        }
+        if (lane == 0)
+            scales[slot] = m > 0.f ? m / 127.f : 0.f;
+    }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid_constant__ MmaParams p) {
+    using L = Layout;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // TMA destinations (no swizzle) want 128-byte alignment.
+    uint8_t* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
+    auto* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+    auto* empty = full + kStages;
+    auto* abort_flag = reinterpret_cast<int*>(empty + kStages);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int R = int(p.tile_rows), KS = 64 / R, BPS = kStageUnits / R;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+        // The next kernel of the stream may start its own weight streaming.
+        grid_dependents_launch();
+    }
+    __syncthreads();
+
+    if (warp == kWarps) {
+        // ------------------------------ producer ------------------------------
+        if (lane != 0)
+            return;
+        uint32_t it = 0;
+        for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+            const MmaJob& job = p.jobs[find_job(p, tile)];
+            const uint32_t local = tile - job.first_tile;
+            const int row0 = int((local / job.row_groups) * uint32_t(R));
+            const uint32_t stages = (job.nblocks + BPS - 1) / BPS;
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&job.map) : "memory");
+            for (uint32_t kc = 0; kc < stages; ++kc, ++it) {
+                const int slot = int(it % kStages);
+                if (it >= kStages && !mbar_wait(&empty[slot], ((it / kStages) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog))
+                    atomicExch(abort_flag, 1);
+                if (*reinterpret_cast<volatile int*>(abort_flag))
+                    goto drain;
+                const int nb = int(min(uint32_t(BPS), job.nblocks - kc * BPS));
+                mbar_expect_tx(&full[slot], uint32_t(nb * R * kBlockBytes));
+                for (int b = 0; b < nb; ++b)
+                    tma_load_3d(smem + L::kStagesOff + slot * kStageBytes + b * R * kBlockBytes, &job.map, 0,
+                                int(kc * BPS + b), row0, &full[slot]);
+            }
+        }
+    drain:
+        for (uint32_t k = 0; k < kStages && k < it; ++k) {
+            const uint32_t last = it - 1 - k;
+            mbar_wait(&full[last % kStages], (last / kStages) & 1u, watchdog_drain, p.watchdog);
+        }
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
+    // Activations (and the outputs this grid writes) may belong to the
+    // previous kernel of the stream.
+    grid_dependency_wait();
+    const int g = lane >> 2, t = lane & 3;
+    const int rg = warp / KS, ks = warp % KS;  // row group and K split of this warp
+    auto* red = reinterpret_cast<float*>(smem + L::kRedOff);
+    uint32_t it = 0;
+    // (input, rows, first block) of the activation segment held in shared memory.
+    const float* seg_x = nullptr;
+    int seg_rows = -1, seg_blk0 = -1;
+    for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+        const MmaJob& job = p.jobs[find_job(p, tile)];
+        const uint32_t local = tile - job.first_tile;
+        const uint32_t row0 = (local / job.row_groups) * uint32_t(R);
+        const uint32_t r0 = (local % job.row_groups) * job.group_rows;
+        const int rows = int(min(job.group_rows, job.rows - r0));
+        const uint32_t stages = (job.nblocks + BPS - 1) / BPS;
+        const float* x = job.input + size_t(r0) * job.in;
+        const Segment seg(rows, BPS);
+        if (seg.blocks == 0) {
+            // A stage's activations would overflow the segment buffer.
+            atomicExch(abort_flag, 1);
+            return;
+        }
+        const uint8_t* frag = seg.frag(smem);
+        const uint32_t* minb = seg.minb(smem);
+        const float* scales = seg.scales(smem);
+        const uint32_t my_row = row0 + 16 * rg + g;  // and my_row + 8
+        const bool valid_lo = my_row < job.columns, valid_hi = my_row + 8 < job.columns;
+        const bool check = job.status != nullptr;
+        bool finite = true;
+        float acc[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            acc[nt][0] = acc[nt][1] = 0.f;
+
+        for (uint32_t kc = 0; kc < stages; ++kc, ++it) {
+            const int slot = int(it % kStages);
+            const int nb = int(min(uint32_t(BPS), job.nblocks - kc * BPS));
+            const int blk_first = int(kc) * BPS;
+            const int seg0 = blk_first / seg.blocks * seg.blocks;
+            if (x != seg_x || rows != seg_rows || seg0 != seg_blk0) {
+                // Every warp is done with the previous segment before it is replaced.
+                named_sync(1, kConsumerThreads);
+                prep_segment(smem, seg, x, job.in, seg0, int(min(uint32_t(seg.blocks), job.nblocks - seg0)));
+                named_sync(1, kConsumerThreads);
+                seg_x = x, seg_rows = rows, seg_blk0 = seg0;
+            }
+            const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
+            if (!aborted && !mbar_wait(&full[slot], (it / kStages) & 1u, watchdog_full_barrier, p.watchdog))
+                atomicExch(abort_flag, 1);
+            if (!aborted) {
+                const uint8_t* stage = smem + L::kStagesOff + slot * kStageBytes;
+#pragma unroll
+                for (int bb = 0; bb < 2; ++bb) {
+                    const int b = 2 * ks + bb;  // this warp's super-blocks of the stage
+                    if (b >= nb)
+                        break;
+                    const int sblk = blk_first + b - seg0;  // block index within the segment
+                    const uint8_t* rgp = stage + b * R * kBlockBytes + (16 * rg + g) * kBlockBytes;
+                    const uint8_t* r8p = rgp + 8 * kBlockBytes;
+                    const uint4 hg = *reinterpret_cast<const uint4*>(rgp);
+                    const uint4 h8 = *reinterpret_cast<const uint4*>(r8p);
+                    const float dg = half_bits_to_float(hg.x & 0xffffu), mg = half_bits_to_float(hg.x >> 16);
+                    const float d8 = half_bits_to_float(h8.x & 0xffffu), m8 = half_bits_to_float(h8.x >> 16);
+                    if (check)
+                        finite = finite && (!valid_lo || (isfinite(dg) && isfinite(mg)))
+                                 && (!valid_hi || (isfinite(d8) && isfinite(m8)));
+                    // 6-bit scales of sub-blocks 0-3 / 4-7, one per byte.
+                    const uint32_t scLo_g = hg.y & 0x3F3F3F3Fu;
+                    const uint32_t scHi_g = (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u);
+                    const uint32_t scLo_8 = h8.y & 0x3F3F3F3Fu;
+                    const uint32_t scHi_8 = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
+                    // B operand rows of this lane: token (nt*4 + g/2) clamped to the
+                    // last present one (absent tokens only feed ignored columns).
+                    const uint8_t* bsrc[NT];
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const int tok = min(nt * 4 + (g >> 1), rows - 1);
+                        bsrc[nt] = frag + (sblk * rows + tok) * kTokenBlockBytes + t * 32 + (g & 1) * 16;
+                    }
+                    // int32 sums 16 * sum_g sc_g * C_g: [nt][row g / g+8][h, l].
+                    int I[NT][2][2];
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+                        I[nt][0][0] = I[nt][0][1] = I[nt][1][0] = I[nt][1][1] = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        // Code bytes 8t..8t+7 of 32-byte chunk j, rows g and g+8.
+                        const uint2 cg = *reinterpret_cast<const uint2*>(rgp + 16 + 32 * j + 8 * t);
+                        const uint2 c8 = *reinterpret_cast<const uint2*>(r8p + 16 + 32 * j + 8 * t);
+                        const uint32_t wg = j < 2 ? scLo_g : scHi_g, w8 = j < 2 ? scLo_8 : scHi_8;
+                        // bytes 2(j%2) (sub-block 2j) and 2(j%2)+1 (2j+1) of the scale word.
+                        const uint32_t selA = 0x4440u | (2u * uint32_t(j & 1)), selB = selA + 1u;
+                        const int scAg = int(__byte_perm(wg, 0u, selA)) << 4, scA8 = int(__byte_perm(w8, 0u, selA)) << 4;
+                        const int scBg = int(__byte_perm(wg, 0u, selB)), scB8 = int(__byte_perm(w8, 0u, selB));
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) {
+                            const uint4 bf = *reinterpret_cast<const uint4*>(bsrc[nt] + j * 128);
+                            int Ca[4], Cb[4];
+                            // Sub-block 2j: low nibbles (q); 2j+1: high nibbles in place (16 q).
+                            imma(Ca, cg.x & 0x0F0F0F0Fu, c8.x & 0x0F0F0F0Fu, cg.y & 0x0F0F0F0Fu, c8.y & 0x0F0F0F0Fu, bf.x, bf.y);
+                            imma(Cb, cg.x & 0xF0F0F0F0u, c8.x & 0xF0F0F0F0u, cg.y & 0xF0F0F0F0u, c8.y & 0xF0F0F0F0u, bf.z, bf.w);
+                            I[nt][0][0] += scAg * Ca[0] + scBg * Cb[0];
+                            I[nt][0][1] += scAg * Ca[1] + scBg * Cb[1];
+                            I[nt][1][0] += scA8 * Ca[2] + scB8 * Cb[2];
+                            I[nt][1][1] += scA8 * Ca[3] + scB8 * Cb[3];
+                        }
+                    }
+                    // Minimum term: A' = m of sub-blocks 2t, 2t+1 for rows g, g+8.
+                    const uint32_t mLo_g = hg.z & 0x3F3F3F3Fu;
+                    const uint32_t mHi_g = ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u);
+                    const uint32_t mLo_8 = h8.z & 0x3F3F3F3Fu;
+                    const uint32_t mHi_8 = ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u);
+                    const uint32_t mwg = t < 2 ? mLo_g : mHi_g, mw8 = t < 2 ? mLo_8 : mHi_8;
+                    const uint32_t mb = 2u * uint32_t(t & 1);
+                    // bytes [m(2t), 0x64, m(2t+1), 0x64] -> (m(2t), m(2t+1)).
+                    const uint32_t sel = (4u << 12) | ((mb + 1u) << 8) | (4u << 4) | mb;
+                    const uint32_t am_g = hadd2_u(__byte_perm(mwg, 0x64646464u, sel), 0xE400E400u);
+                    const uint32_t am_8 = hadd2_u(__byte_perm(mw8, 0x64646464u, sel), 0xE400E400u);
+                    const float mg256 = mg * 256.f, m8256 = m8 * 256.f;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const int tokb = min(nt * 4 + (g >> 1), rows - 1);
+                        const uint32_t bm = minb[(sblk * rows + tokb) * (kMinBytes / 4) + (g & 1) * 4 + t];
+                        float Cm[4] = {0.f, 0.f, 0.f, 0.f};
+                        mma1688(Cm, am_g, am_8, bm);
+                        // Columns 2t, 2t+1 = token nt*4 + t (h, l).
+                        const int tokc = min(nt * 4 + t, rows - 1);
+                        const float sc = scales[sblk * rows + tokc] * (1.f / 16.f);
+                        const float kg = dg * sc, k8 = d8 * sc;
+                        acc[nt][0] = fmaf(kg, fmaf(float(I[nt][0][1]), 1.f / 256.f, float(I[nt][0][0])), acc[nt][0]);
+                        acc[nt][0] = fmaf(-mg256, Cm[0] + Cm[1], acc[nt][0]);
+                        acc[nt][1] = fmaf(k8, fmaf(float(I[nt][1][1]), 1.f / 256.f, float(I[nt][1][0])), acc[nt][1]);
+                        acc[nt][1] = fmaf(-m8256, Cm[2] + Cm[3], acc[nt][1]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&empty[slot]);
+        }
+        if (check && !finite)
+            atomicOr(job.status, 1u);
+        if (KS > 1) {
+            // Sum the K splits of each row group: warp (rg, 0) collects.
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                red[(nt * 2 + 0) * kConsumerThreads + tid] = acc[nt][0];
+                red[(nt * 2 + 1) * kConsumerThreads + tid] = acc[nt][1];
+            }
+            named_sync(1, kConsumerThreads);
+            if (ks == 0) {
+                for (int k = 1; k < KS; ++k) {
+                    const int other = (warp + k) * 32 + lane;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        acc[nt][0] += red[(nt * 2 + 0) * kConsumerThreads + other];
+                        acc[nt][1] += red[(nt * 2 + 1) * kConsumerThreads + other];
+                    }
+                }
+            }
+            named_sync(1, kConsumerThreads);
+        }
+        if (ks == 0) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int tok = nt * 4 + t;
+                if (tok < rows) {
+                    float* out = job.output + size_t(r0 + tok) * job.stride;
+                    if (valid_lo)
+                        out[my_row] = acc[nt][0];
+                    if (valid_hi)
+                        out[my_row + 8] = acc[nt][1];
+                }
+            }
+        }
+        if (*reinterpret_cast<volatile int*>(abort_flag))
+            return;
+    }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess
+            && q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// CTA slots of the kernel on the current device (SMs x resident CTAs), or a
+// negative kb200_status.
+template <int NT> int kernel_slots() {
+    static int blocks_per_sm[64] = {};
+    static std::mutex lock;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    constexpr int smem = Layout::kTotal + 128;  // + alignment slack
+    std::lock_guard<std::mutex> guard(lock);
+    if (!blocks_per_sm[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_q4k_mma_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess)
+            return -cuda_fail(e, "gemv_q4k_mma_kernel attribute");
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q4k_mma_kernel<NT>, kThreadsQ, smem);
+        if (e != cudaSuccess)
+            return -cuda_fail(e, "gemv_q4k_mma_kernel occupancy");
+        blocks_per_sm[dev] = n > 0 ? n : 1;
+    }
+    return sm_count() * blocks_per_sm[dev];
+}
+
+template <int NT> int launch_q4k(const MmaParams& p, uint32_t slots, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min(p.total_tiles, slots));
+    cfg.blockDim = dim3(kThreadsQ);
+    cfg.dynamicSmemBytes = Layout::kTotal + 128;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_q4k_mma_kernel<NT>, p);
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "gemv_q4k_mma_kernel launch");
+}
+
+}  // namespace
+
+bool q4k_mma_eligible(const kb200_gemv_job& j) {
+    return j.encoding == KB200_Q4_K && aligned(j.weights, 16) && j.row_bytes % 16 == 0 && j.in % 256 == 0
+           && j.row_bytes >= size_t(j.in) / 256 * 144 && encode_fn() != nullptr;
+}
+
+int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream) {
+    auto encode = encode_fn();
+    if (!encode)
+        return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
+    // Rows per pass: up to 4 in one n-tile, up to 8 in two.
+    int max_rows = 1;
+    for (const auto* j : jobs)
+        max_rows = std::max(max_rows, int(std::min(j->rows, uint32_t(KB200_BATCH_ROWS))));
+    const int nt = max_rows <= 4 ? 1 : 2;
+    const uint32_t group_rows = uint32_t(4 * nt);
+    const int slots = nt == 1 ? kernel_slots<1>() : kernel_slots<2>();
+    if (slots <= 0)
+        return -slots;
+    for (size_t first = 0; first < jobs.size(); first += kMaxJobsQ) {
+        const size_t n = std::min(jobs.size() - first, size_t(kMaxJobsQ));
+        // Tile height: the tallest of 64/32/16 rows that still gives every
+        // CTA slot a tile; shorter tiles split K among the warps instead. A
+        // tile height is only allowed if one stage of activations (128/R
+        // super-blocks for every token) fits the segment buffer.
+        int tokens = 1;
+        for (size_t m = 0; m < n; ++m)
+            tokens = std::max(tokens, int(std::min(jobs[first + m]->rows, group_rows)));
+        if (segment_blocks(tokens, kStageUnits / 64) == 0)
+            return fail(KB200_UNSUPPORTED, "activation segment too small for this many rows");
+        uint32_t R = 64;
+        for (uint32_t cand : {64u, 32u, 16u}) {
+            if (segment_blocks(tokens, kStageUnits / int(cand)) == 0)
+                break;
+            R = cand;
+            if (cand == 16u)
+                break;
+            uint64_t tiles = 0;
+            for (size_t m = 0; m < n; ++m) {
+                const auto& j = *jobs[first + m];
+                tiles += (j.columns + cand - 1) / cand * ((j.rows + group_rows - 1) / group_rows);
+            }
+            if (tiles >= uint64_t(slots))
+                break;
+        }
+        MmaParams p;
+        std::memset(&p, 0, sizeof(p));
+        p.watchdog = watchdog_word();
+        p.tile_rows = R;
+        uint32_t tiles = 0;
+        for (size_t m = 0; m < n; ++m) {
+            const auto& j = *jobs[first + m];
+            MmaJob& d = p.jobs[m];
+            const cuuint64_t dims[3] = {18, j.in / 256, j.columns};
+            const cuuint64_t strides[2] = {144, j.row_bytes};
+            const cuuint32_t box[3] = {18, 1, R};
+            const cuuint32_t estr[3] = {1, 1, 1};
+            const CUresult r = encode(
+                &d.map,
+                CU_TENSOR_MAP_DATA_TYPE_UINT64,
+                3,
+                const_cast<void*>(j.weights),
+                dims,
+                strides,
+                box,
+                estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE
+            );
+            if (r != CUDA_SUCCESS)
+                return fail(KB200_INVALID, "cuTensorMapEncodeTiled rejected a Q4_K job");
+            d.input = j.input;
+            d.output = j.output;
+            d.status = j.status;
+            d.stride = j.stride;
+            d.in = j.in;
+            d.columns = j.columns;
+            d.rows = j.rows;
+            d.nblocks = j.in / 256;
+            d.group_rows = group_rows;
+            d.row_groups = (j.rows + group_rows - 1) / group_rows;
+            d.first_tile = tiles;
+            tiles += (j.columns + R - 1) / R * d.row_groups;
+        }
+        p.count = uint32_t(n);
+        p.total_tiles = tiles;
+        const int s = nt == 1 ? launch_q4k<1>(p, uint32_t(slots), stream) : launch_q4k<2>(p, uint32_t(slots), stream);
+        if (s)
+            return s;
+    }
+    return KB200_OK;
+}
+
+}  // namespace kb200

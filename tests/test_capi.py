@@ -76,7 +76,9 @@ def test_invalid_and_alias_are_reported(kb):
 
 
 def test_path_selection(kb):
-    assert kb.gemv_path(job(kb)) == 1
+    # 2 (tensor pipe) needs the driver's tensor-map encoder, absent without a GPU driver.
+    assert kb.gemv_path(job(kb)) in (1, 2)
+    assert kb.gemv_path(job(kb, encoding=kb.Q8_0, row_bytes=4352)) == 1
     assert kb.gemv_path(job(kb, weights=FAKE_W + 2)) == 0          # unaligned base
     assert kb.gemv_path(job(kb, encoding=kb.Q8_0, in_=160, row_bytes=170)) == 0
     assert kb.gemv_path(job(kb, encoding=kb.Q3_K, row_bytes=16 * 110)) == 0

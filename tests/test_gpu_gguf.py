@@ -83,7 +83,17 @@ def test_gemv_staged_parity(kb, oracle, cuda, enc_name, in_, out, rows):
     assert rel_err(y, want) <= TOL
 
 
-@pytest.mark.parametrize("rows", [8, 17])
+def test_q4k_uses_tensor_pipe_kernel(kb, cuda):
+    import torch
+
+    w = torch.zeros(64, 4352, dtype=torch.uint8, device=cuda)
+    x = torch.zeros(1, 4096, device=cuda)
+    y = torch.zeros(1, 64, device=cuda)
+    assert kb.gemv_path(kb.gemv_job(kb.Q4_K, w, x, y, in_=4096, columns=64, rows=1, row_bytes_=4352)) == 2
+    assert kb.gemv_path(kb.gemv_job(kb.Q8_0, w, x, y, in_=4096, columns=64, rows=1, row_bytes_=4352)) == 1
+
+
+@pytest.mark.parametrize("rows", [4, 5, 8, 17])
 def test_gemv_row_groups(kb, oracle, cuda, rows):
     y, want = gemv_case(kb, oracle, cuda, kb.Q4_K, 4096, 40, rows)
     assert rel_err(y, want) <= TOL
