@@ -435,9 +435,58 @@ def run_case(args):
                       "gbps": round(nbytes / (ms * 1e-3) / 1e9, 1), "weight_bytes": nbytes}), flush=True)
 
 
+def moe_layer_inputs(torch, kb, dev, tokens, seed=0):
+    """BASELINE config 3 (gpt-oss-20b MoE layer: H=2880, 32 experts, top-4,
+    I=2880, SwiGLU clamp 7): MXFP4 codes uniform over 16, E8M0 uniform in
+    118..126, bf16 N(0,1) activations and N(0,1) router logits, on `dev`."""
+    E, H, I, K = 32, 2880, 2880, 4
+    gen = torch.Generator(device=dev).manual_seed(seed)
+
+    def mx(rows, cols):
+        blocks = torch.randint(0, 256, (rows, cols // 2), dtype=torch.uint8, device=dev, generator=gen)
+        scales = torch.randint(118, 127, (rows, cols // 32), dtype=torch.uint8, device=dev, generator=gen)
+        return blocks, scales
+
+    gu_w, gu_s = mx(E * 2 * I, H)
+    dn_w, dn_s = mx(E * H, I)
+    w = kb.moe_weights(gu_w, gu_s, dn_w, dn_s, hidden=H, inter=I, experts=E, top_k=K)
+    x = torch.randn(tokens, H, device=dev, generator=gen).to(torch.bfloat16)
+    logits = torch.randn(tokens, E, device=dev, generator=gen)
+    weight_bytes = gu_w.numel() + gu_s.numel() + dn_w.numel() + dn_s.numel()
+    return w, (gu_w, gu_s, dn_w, dn_s), x, logits, weight_bytes
+
+
+def run_moe(args):
+    """--case moe: the config-3 MoE layer at --tokens T (tokens/s, TFLOP/s)."""
+    import torch
+
+    import kadan_b200 as kb
+
+    dev = torch.device("cuda:0")
+    T, H, I, K = args.tokens, 2880, 2880, 4
+    w, keep, x, logits, weight_bytes = moe_layer_inputs(torch, kb, dev, T)
+    out = torch.empty(T, H, device=dev)
+    ws = torch.empty(kb.moe_workspace_bytes(w, T), dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        kb.moe_forward(w, x, logits, out=out, workspace=ws)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        kb.moe_forward(w, x, logits, out=out, workspace=ws)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    flops = 2.0 * T * K * (2 * I * H + H * I)
+    print(json.dumps({"case": "moe-config3", "tokens": T, "ms_per_layer": round(ms, 4),
+                      "tokens_per_s": round(T / (ms * 1e-3), 1), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                      "weight_gbps": round(weight_bytes / (ms * 1e-3) / 1e9, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None, help="profiling case instead of the headline workload")
+    ap.add_argument("--tokens", type=int, default=4096, help="tokens for --case moe")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
@@ -450,7 +499,9 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
-    if args.case:
+    if args.case == "moe":
+        run_moe(args)
+    elif args.case:
         run_case(args)
     elif args.impl == "reference":
         if args.steps > 200:

@@ -175,6 +175,69 @@ KB200_API int kb200_dense_gguf_batch(
     int* result
 );
 
+/* ---------------------------------------------------------------------------
+ * MXFP4 mixture-of-experts layer (gpt-oss style), device pointers.
+ *
+ * The reference has no device path for this layer: its MoE semantics are
+ * MoeLayer::forward (IW/src/models/text/qwen_layers.cpp:378-492: softmax
+ * router, top-k, renormalise by max(sum, 2^-14), per-expert gather,
+ * gate/up, activation, down, weighted sum in selection order) and its MXFP4
+ * format is kadan::quantization (IW/src/weights/quantization.cpp:79-99) with
+ * the expert-row layout of Shard::load_mxfp4_expert_rows
+ * (IW/src/weights/checkpoint.cpp:669-730):
+ *   blocks [E, rows, cols/32, 16] (low nibble first), scales [E, rows, cols/32]
+ *   E8M0, value = e2m1(code) * 2^(scale - 127).
+ * Expert weights are used in fp16 on the tensor cores, exact for scale bytes
+ * 104..140; kb200_moe_forward flags others in *status (bit 1). */
+#define KB200_MOE_SWIGLU_OAI 0 /* gate<=limit, up in [-limit,limit], gate*sigmoid(alpha*gate)*(up+1) */
+#define KB200_MOE_SILU 1       /* silu(gate) * up (the reference MoeLayer) */
+
+typedef struct kb200_moe_weights {
+    const uint8_t* gate_up_blocks; /* device [E, 2*inter, hidden/2] */
+    const uint8_t* gate_up_scales; /* device [E, 2*inter, hidden/32] */
+    const float* gate_up_bias;     /* device [E, 2*inter] or NULL */
+    const uint8_t* down_blocks;    /* device [E, hidden, inter/2] */
+    const uint8_t* down_scales;    /* device [E, hidden, inter/32] */
+    const float* down_bias;        /* device [E, hidden] or NULL */
+    int32_t hidden, inter, experts, top_k;
+    int32_t activation;  /* KB200_MOE_* */
+    int32_t interleaved; /* 1: gate = row 2i, up = row 2i+1; 0: gate rows [0,inter), up [inter,2*inter) */
+    float limit, alpha;
+} kb200_moe_weights;
+
+/* Device scratch that kb200_moe_forward needs for `tokens` input rows. */
+KB200_API size_t kb200_moe_workspace_bytes(const kb200_moe_weights* w, size_t tokens);
+
+/* out[t, :] = sum_i weight[t,i] * down_e(act(gate_up_e(x[t]))) for the top_k
+ * experts e of logits[t] (fp32 [tokens, experts]); x is bf16 [tokens, hidden],
+ * out fp32 [tokens, hidden]. workspace: device, at least
+ * kb200_moe_workspace_bytes. status: device word or NULL (bit 1: a scale byte
+ * outside 104..140; bit 2: an activation outside the fp16 range). Calls that
+ * overlap on one workspace race. */
+KB200_API int kb200_moe_forward(
+    const kb200_moe_weights* w,
+    const uint16_t* x_bf16,
+    const float* logits,
+    size_t tokens,
+    float* out,
+    void* workspace,
+    size_t workspace_bytes,
+    unsigned* status,
+    void* stream
+);
+
+/* The routing stage alone (for tests): chosen [tokens, top_k] int32,
+ * weight [tokens, top_k] fp32, device. */
+KB200_API int kb200_moe_route(
+    const float* logits,
+    size_t tokens,
+    int32_t experts,
+    int32_t top_k,
+    int32_t* chosen,
+    float* weight,
+    void* stream
+);
+
 /* Device-side watchdog word: nonzero when a bounded wait inside a kernel gave up
  * since the last call of this function, which also clears it. Synchronous. */
 KB200_API int kb200_take_device_error(unsigned* value);

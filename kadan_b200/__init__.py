@@ -81,6 +81,28 @@ class HostJob(ctypes.Structure):
 
 
 RESULT_UNSUPPORTED, RESULT_UNVALIDATED, RESULT_FINITE = 0, 1, 2
+MOE_SWIGLU_OAI, MOE_SILU = 0, 1
+
+
+class MoeWeights(ctypes.Structure):
+    """kb200_moe_weights (device pointers to MXFP4 expert tensors)."""
+
+    _fields_ = [
+        ("gate_up_blocks", ctypes.c_void_p),
+        ("gate_up_scales", ctypes.c_void_p),
+        ("gate_up_bias", ctypes.c_void_p),
+        ("down_blocks", ctypes.c_void_p),
+        ("down_scales", ctypes.c_void_p),
+        ("down_bias", ctypes.c_void_p),
+        ("hidden", ctypes.c_int32),
+        ("inter", ctypes.c_int32),
+        ("experts", ctypes.c_int32),
+        ("top_k", ctypes.c_int32),
+        ("activation", ctypes.c_int32),
+        ("interleaved", ctypes.c_int32),
+        ("limit", ctypes.c_float),
+        ("alpha", ctypes.c_float),
+    ]
 
 
 def _load() -> ctypes.CDLL:
@@ -116,6 +138,10 @@ def _load() -> ctypes.CDLL:
     lib.kb200_weights_free.argtypes = [vp, vp]
     lib.kb200_dense_gguf_batch.argtypes = [vp, ctypes.POINTER(HostJob), c_size, ctypes.POINTER(c_int),
                                            ctypes.POINTER(c_int)]
+    lib.kb200_moe_workspace_bytes.restype = c_size
+    lib.kb200_moe_workspace_bytes.argtypes = [ctypes.POINTER(MoeWeights), c_size]
+    lib.kb200_moe_forward.argtypes = [ctypes.POINTER(MoeWeights), vp, vp, c_size, vp, vp, c_size, vp, vp]
+    lib.kb200_moe_route.argtypes = [vp, c_size, ctypes.c_int32, ctypes.c_int32, vp, vp, vp]
     return lib
 
 
@@ -244,3 +270,40 @@ def host_job(encoding: int, weights_ptr: int, x, y, *, in_: int, out: int, valid
     rows = x.size // in_
     rb = row_bytes_ if row_bytes_ is not None else (in_ * 4 if encoding == F32 else row_bytes(encoding, in_))
     return HostJob(weights_ptr, x.ctypes.data, y.ctypes.data, rb, in_, out, rows, encoding, int(validated))
+
+
+def moe_weights(gu_blocks, gu_scales, dn_blocks, dn_scales, *, hidden: int, inter: int, experts: int, top_k: int,
+                gu_bias=None, dn_bias=None, activation: int = MOE_SWIGLU_OAI, interleaved: bool = True,
+                limit: float = 7.0, alpha: float = 1.702) -> MoeWeights:
+    """Device tensors in the MXFP4 expert layout (blocks [E, rows, cols/2], scales [E, rows, cols/32])."""
+    return MoeWeights(_ptr(gu_blocks), _ptr(gu_scales), _ptr(gu_bias), _ptr(dn_blocks), _ptr(dn_scales),
+                      _ptr(dn_bias), hidden, inter, experts, top_k, activation, int(interleaved), limit, alpha)
+
+
+def moe_workspace_bytes(w: MoeWeights, tokens: int) -> int:
+    return int(lib.kb200_moe_workspace_bytes(ctypes.byref(w), tokens))
+
+
+def moe_forward(w: MoeWeights, x_bf16, logits, out=None, workspace=None, status=None, stream=None):
+    """out[T, hidden] fp32 = MXFP4 MoE layer of bf16 x [T, hidden] routed by fp32 logits [T, experts]."""
+    import torch
+
+    tokens = x_bf16.shape[0]
+    if out is None:
+        out = torch.empty(tokens, w.hidden, dtype=torch.float32, device=x_bf16.device)
+    need = moe_workspace_bytes(w, tokens)
+    if workspace is None:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=x_bf16.device)
+    check(lib.kb200_moe_forward(ctypes.byref(w), _ptr(x_bf16), _ptr(logits), tokens, _ptr(out), _ptr(workspace),
+                                workspace.numel(), _ptr(status), _stream_ptr(stream)))
+    return out
+
+
+def moe_route(logits, top_k: int, stream=None):
+    import torch
+
+    tokens, experts = logits.shape
+    chosen = torch.empty(tokens, top_k, dtype=torch.int32, device=logits.device)
+    weight = torch.empty(tokens, top_k, dtype=torch.float32, device=logits.device)
+    check(lib.kb200_moe_route(_ptr(logits), tokens, experts, top_k, _ptr(chosen), _ptr(weight), _stream_ptr(stream)))
+    return chosen, weight

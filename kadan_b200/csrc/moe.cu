@@ -1,0 +1,823 @@
+// MXFP4 mixture-of-experts layer on sm_100a.
+//
+// Semantics follow the reference MoeLayer::forward
+// (services/hikari/inference_worker/src/models/text/qwen_layers.cpp:378-492):
+// a max-subtracted softmax router whose sum is taken in double, top-k by
+// probability (ties to the lower expert index), renormalisation by
+// max(sum, 2^-14), a stable per-expert gather in slot order, gate/up, the
+// activation, down, and a weighted sum of the k expert outputs in selection
+// order. The MXFP4 values follow kadan::quantization::weight
+// (IW/src/weights/quantization.cpp:89-96): e2m1(code) * 2^(scale - 127).
+//
+// Device pipeline per call (all on one stream):
+//   route   one warp per token: softmax, top-k, weights, expert counts
+//   sort    one CTA: stable counting sort -> expert offsets, permutation,
+//           inverse positions and the per-expert 128-row m-tile prefix
+//   gather  token rows (bf16) -> expert-sorted rows (fp16)
+//   gemm    grouped GEMM on the tensor cores (tcgen05, TMEM accumulators),
+//           twice: gate/up with the activation in the epilogue (fp16 out),
+//           then down (fp32 out). Expert weights stay MXFP4 in HBM; four
+//           dequant warps turn each 128x64 code tile into fp16 with
+//           cvt.rn.f16x2.e2m1x2 and the block scale (exact for scale bytes
+//           104..140), straight into the 128-byte-swizzled operand layout.
+//   combine out[t] = sum_i w[t,i] * Y[pos(t,i)] in selection order (fp32)
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <mutex>
+
+#include "kb200_device.cuh"
+#include "kb200_host.hpp"
+#include "tcgen05.cuh"
+
+namespace kb200 {
+namespace {
+
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 32;
+
+// ---------------------------------------------------------------- routing
+// One warp per token; experts strided over lanes (<= 8 per lane).
+__global__ void moe_route_kernel(
+    const float* logits, int tokens, int E, int K, int* chosen, float* weight, int* counts
+) {
+    const int warp = int((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (warp >= tokens)
+        return;
+    const float* l = logits + size_t(warp) * E;
+    float v[8];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? l[e] : -INFINITY;
+        mx = fmaxf(mx, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float p[8];
+    double total = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        p[i] = lane + 32 * i < E ? expf(v[i] - mx) : 0.f;
+        total += double(p[i]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+        total += __shfl_xor_sync(0xffffffffu, total, o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        p[i] = float(double(p[i]) / total);
+    unsigned taken = 0;
+    float sum = 0.f, picked[kMaxTopK];
+    int idx[kMaxTopK];
+    for (int s = 0; s < K; ++s) {
+        float best = -1.f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E && !((taken >> i) & 1u) && (p[i] > best || (p[i] == best && e < bi)))
+                best = p[i], bi = e;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ob > best || (ob == best && oi < bi))
+                best = ob, bi = oi;
+        }
+        if ((bi & 31) == lane)
+            taken |= 1u << (bi >> 5);
+        picked[s] = best;
+        idx[s] = bi;
+        sum += best;
+    }
+    sum = fmaxf(sum, 6.103515625e-5f);
+    if (lane == 0)
+        for (int s = 0; s < K; ++s) {
+            chosen[size_t(warp) * K + s] = idx[s];
+            weight[size_t(warp) * K + s] = picked[s] / sum;
+            if (counts)
+                atomicAdd(&counts[idx[s]], 1);
+        }
+}
+
+// ------------------------------------------------------------------- sort
+// One CTA of 1024 threads: stable counting sort of the tokens*K slots by
+// expert (slot order within an expert), plus m-tile prefix sums.
+__global__ void __launch_bounds__(1024) moe_sort_kernel(
+    const int* chosen, int n, int E, const int* counts, int* offsets, int* perm, int* pos, int* mtile_prefix
+) {
+    __shared__ int off[kMaxExperts + 1], running[kMaxExperts], total[kMaxExperts];
+    __shared__ int warp_base[32][kMaxExperts];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        int acc = 0, tiles = 0;
+        for (int e = 0; e < E; ++e) {
+            off[e] = acc;
+            mtile_prefix[e] = tiles;
+            acc += counts[e];
+            tiles += (counts[e] + 127) / 128;
+        }
+        off[E] = acc;
+        mtile_prefix[E] = tiles;
+    }
+    for (int e = tid; e < E; e += blockDim.x)
+        running[e] = 0;
+    __syncthreads();
+    for (int e = tid; e <= E; e += blockDim.x)
+        offsets[e] = off[e];
+    for (int base = 0; base < n; base += 1024) {
+        for (int i = tid; i < 32 * E; i += 1024)
+            warp_base[i / E][i % E] = 0;
+        __syncthreads();
+        const int slot = base + tid;
+        const int e = slot < n ? chosen[slot] : -1;
+        const unsigned same = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(same & ((1u << lane) - 1u));
+        if (e >= 0 && rank == 0)
+            warp_base[warp][e] = __popc(same);
+        __syncthreads();
+        for (int x = tid; x < E; x += 1024) {
+            int acc = 0;
+            for (int w = 0; w < 32; ++w) {
+                const int c = warp_base[w][x];
+                warp_base[w][x] = acc;
+                acc += c;
+            }
+            total[x] = acc;
+        }
+        __syncthreads();
+        if (e >= 0) {
+            const int p = off[e] + running[e] + warp_base[warp][e] + rank;
+            perm[p] = slot;
+            pos[slot] = p;
+        }
+        __syncthreads();
+        for (int x = tid; x < E; x += 1024)
+            running[x] += total[x];
+        __syncthreads();
+    }
+}
+
+// ----------------------------------------------------------------- gather
+// Xs[p, :] = fp16(x[perm[p] / K, :]) for p < n, 8 values per thread.
+__global__ void moe_gather_kernel(
+    const __nv_bfloat16* x, const int* perm, int n, int K, int H, __half* xs, unsigned* status
+) {
+    const int per_row = H / 8;
+    const size_t total = size_t(n) * per_row;
+    bool bad = false;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        const int p = int(i / per_row), c = int(i % per_row);
+        const int token = perm[p] / K;
+        const uint4 raw = *reinterpret_cast<const uint4*>(x + size_t(token) * H + c * 8);
+        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        uint4 outv;
+        __half2* o = reinterpret_cast<__half2*>(&outv);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(b[k]);
+            bad |= fabsf(f.x) > 65504.f || fabsf(f.y) > 65504.f;
+            o[k] = __floats2half2_rn(f.x, f.y);
+        }
+        *reinterpret_cast<uint4*>(xs + size_t(p) * H + c * 8) = outv;
+    }
+    if (bad && status)
+        atomicOr(status, 4u);
+}
+
+// ---------------------------------------------------------------- combine
+__global__ void moe_combine_kernel(
+    const float* y, const float* weight, const int* pos, int tokens, int K, int H, float* out
+) {
+    const int per_row = H / 4;
+    const size_t total = size_t(tokens) * per_row;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        const int t = int(i / per_row), c = int(i % per_row);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < K; ++s) {
+            const float w = weight[size_t(t) * K + s];
+            const float4 v = *reinterpret_cast<const float4*>(y + size_t(pos[size_t(t) * K + s]) * H + c * 4);
+            acc.x = fmaf(w, v.x, acc.x), acc.y = fmaf(w, v.y, acc.y);
+            acc.z = fmaf(w, v.z, acc.z), acc.w = fmaf(w, v.w, acc.w);
+        }
+        *reinterpret_cast<float4*>(out + size_t(t) * H + c * 4) = acc;
+    }
+}
+
+// ----------------------------------------------------------- grouped GEMM
+constexpr int BM = 128, BN = 128, BK = 64, kStagesG = 4;
+constexpr int kABytes = BM * BK * 2, kBBytes = BN * BK * 2, kRawBytes = BN * BK / 2;
+constexpr int kMaxK = 4096;
+constexpr int kScaleBytes = BN * (kMaxK / 32);
+constexpr int kThreadsG = 320;  // producer, MMA, 4 dequant warps, 4 epilogue warps
+
+struct GroupParams {
+    CUtensorMap a_map;  // fp16 [rows, K], box {64, 128}, 128-byte swizzle
+    CUtensorMap b_map;  // u8 codes [E * Nrows, K/2], box {32, 128} or {32, 64} (split)
+    const uint8_t* scales;  // [E * Nrows, K/32]
+    const float* bias;      // [E * Nrows] or null
+    const int* offsets;     // [E + 1]
+    const int* mtile_prefix;
+    void* out;
+    int K, Nrows, E, n_tiles, split, epilogue, out_cols, act_kind;
+    float limit, alpha;
+    unsigned* status;
+    unsigned* watchdog;
+};
+
+struct GemmShared {
+    uint64_t tma_full[kStagesG], b_full[kStagesG], stage_empty[kStagesG];
+    uint64_t sc_full[2], sc_empty[2], acc_full[2], acc_empty[2];
+    uint32_t tmem_base;
+    int abort;
+};
+
+constexpr int kSmemA = 0;
+constexpr int kSmemB = kSmemA + kStagesG * kABytes;
+constexpr int kSmemRaw = kSmemB + kStagesG * kBBytes;
+constexpr int kSmemScale = kSmemRaw + kStagesG * kRawBytes;
+constexpr int kSmemShared = kSmemScale + 2 * kScaleBytes;
+constexpr int kSmemTotal = kSmemShared + int(sizeof(GemmShared)) + 1024;
+
+struct TileInfo {
+    int e, m0, mend, nt;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const GroupParams& p, int tile) {
+    const int mt = tile / p.n_tiles, nt = tile % p.n_tiles;
+    int lo = 0, hi = p.E;  // largest e with mtile_prefix[e] <= mt
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) / 2;
+        if (p.mtile_prefix[mid] <= mt)
+            lo = mid;
+        else
+            hi = mid;
+    }
+    TileInfo t;
+    t.e = lo;
+    t.m0 = p.offsets[lo] + (mt - p.mtile_prefix[lo]) * BM;
+    t.mend = p.offsets[lo + 1];
+    t.nt = nt;
+    return t;
+}
+
+// First weight row of the tile's lower and upper halves (split: gate and up).
+__device__ __forceinline__ void tile_rows(const GroupParams& p, const TileInfo& t, int& r_lo, int& r_hi) {
+    if (p.split) {
+        r_lo = t.e * p.Nrows + t.nt * (BN / 2);
+        r_hi = t.e * p.Nrows + p.Nrows / 2 + t.nt * (BN / 2);
+    } else {
+        r_lo = t.e * p.Nrows + t.nt * BN;
+        r_hi = r_lo + BN / 2;
+    }
+}
+
+// f16 2^(s-127), and whether s keeps every e2m1 * 2^(s-127) exact in fp16.
+__device__ __forceinline__ uint32_t e8m0_half2(uint32_t s, bool& ok) {
+    ok = s >= 104u && s <= 140u;
+    uint32_t h;
+    if (s >= 113u)
+        h = min(s - 112u, 30u) << 10;
+    else if (s >= 103u)
+        h = 1u << (s - 103u);
+    else
+        h = 0u;
+    return h | (h << 16);
+}
+
+__device__ __forceinline__ uint32_t e2m1x2_to_half2(uint32_t byte) {
+    uint32_t r;
+    asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(r) : "r"(byte));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ float act_fn(float gate, float up, int kind, float limit, float alpha) {
+    if (kind == KB200_MOE_SWIGLU_OAI) {
+        const float g = fminf(gate, limit);
+        const float u = fminf(fmaxf(up, -limit), limit);
+        return g / (1.f + expf(-alpha * g)) * (u + 1.f);
+    }
+    return gate / (1.f + expf(-gate)) * up;
+}
+
+__global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_constant__ GroupParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    auto* sh = reinterpret_cast<GemmShared*>(smem + kSmemShared);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int KS = p.K / BK, sc_row = p.K / 32;
+    const int total = p.mtile_prefix[p.E] * p.n_tiles;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStagesG; ++s) {
+            mbar_init(&sh->tma_full[s], 1);
+            mbar_init(&sh->b_full[s], 128);
+            mbar_init(&sh->stage_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sh->sc_full[b], 1);
+            mbar_init(&sh->sc_empty[b], 128);
+            mbar_init(&sh->acc_full[b], 1);
+            mbar_init(&sh->acc_empty[b], 4);
+        }
+        sh->abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&sh->tmem_base, 256);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sh->tmem_base;
+    volatile int* abort_flag = &sh->abort;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------ producer (TMA)
+        uint32_t it = 0, lt = 0;
+        uint32_t issued_sc = 0;
+        for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x, ++lt) {
+            const TileInfo t = tile_info(p, tile);
+            int r_lo, r_hi;
+            tile_rows(p, t, r_lo, r_hi);
+            const int sb = int(lt & 1u);
+            if (lt >= 2 && !mbar_wait(&sh->sc_empty[sb], ((lt >> 1) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog)) {
+                *abort_flag = 1;
+                break;
+            }
+            // Scale rows of the tile: two runs of 64 rows, clamped to the tensor.
+            const int limit_rows = p.E * p.Nrows;
+            const int n_lo = max(0, min(BN / 2, limit_rows - r_lo)), n_hi = max(0, min(BN / 2, limit_rows - r_hi));
+            mbar_expect_tx(&sh->sc_full[sb], uint32_t((n_lo + n_hi) * sc_row));
+            uint8_t* sdst = smem + kSmemScale + sb * kScaleBytes;
+            if (n_lo)
+                bulk_g2s(sdst, p.scales + size_t(r_lo) * sc_row, uint32_t(n_lo * sc_row), &sh->sc_full[sb]);
+            if (n_hi)
+                bulk_g2s(sdst + (BN / 2) * sc_row, p.scales + size_t(r_hi) * sc_row, uint32_t(n_hi * sc_row), &sh->sc_full[sb]);
+            ++issued_sc;
+            for (int ks = 0; ks < KS; ++ks, ++it) {
+                const int s = int(it % kStagesG);
+                if (it >= kStagesG
+                    && !mbar_wait(&sh->stage_empty[s], ((it / kStagesG) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_expect_tx(&sh->tma_full[s], uint32_t(kABytes + kRawBytes));
+                tma_load_2d(smem + kSmemA + s * kABytes, &p.a_map, ks * BK, t.m0, &sh->tma_full[s]);
+                uint8_t* raw = smem + kSmemRaw + s * kRawBytes;
+                if (p.split) {
+                    tma_load_2d(raw, &p.b_map, ks * (BK / 2), r_lo, &sh->tma_full[s]);
+                    tma_load_2d(raw + (BN / 2) * (BK / 2), &p.b_map, ks * (BK / 2), r_hi, &sh->tma_full[s]);
+                } else {
+                    tma_load_2d(raw, &p.b_map, ks * (BK / 2), r_lo, &sh->tma_full[s]);
+                }
+            }
+        }
+        // Drain: every copy this thread issued lands before the CTA can exit.
+        for (uint32_t k = 0; k < kStagesG && k < it; ++k) {
+            const uint32_t last = it - 1 - k;
+            mbar_wait(&sh->tma_full[last % kStagesG], (last / kStagesG) & 1u, watchdog_drain, p.watchdog);
+        }
+        for (uint32_t k = 0; k < 2 && k < issued_sc; ++k) {
+            const uint32_t last = issued_sc - 1 - k;
+            mbar_wait(&sh->sc_full[last & 1u], (last >> 1) & 1u, watchdog_drain, p.watchdog);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------- MMA issuer
+        const uint32_t idesc = idesc_f16(BM, BN);
+        uint32_t it = 0, lt = 0;
+        bool issued = false;
+        for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x, ++lt) {
+            const int acc = int(lt & 1u);
+            if (lt >= 2 && !mbar_wait(&sh->acc_empty[acc], ((lt >> 1) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog)) {
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            for (int ks = 0; ks < KS; ++ks, ++it) {
+                const int s = int(it % kStagesG);
+                const uint32_t ph = (it / kStagesG) & 1u;
+                if (!mbar_wait(&sh->tma_full[s], ph, watchdog_full_barrier, p.watchdog)
+                    || !mbar_wait(&sh->b_full[s], ph, watchdog_full_barrier, p.watchdog)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t ad = sw128_desc(smem_addr(smem + kSmemA + s * kABytes));
+                const uint64_t bd = sw128_desc(smem_addr(smem + kSmemB + s * kBBytes));
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk)
+                    umma_f16(tmem + uint32_t(acc * BN), ad + uint64_t(2 * kk), bd + uint64_t(2 * kk), idesc,
+                             (ks | kk) != 0);
+                umma_commit(&sh->stage_empty[s]);
+                issued = true;
+            }
+            umma_commit(&sh->acc_full[acc]);
+        }
+        if (issued && *abort_flag) {
+            // Let the MMAs in flight finish before TMEM is released.
+            const uint32_t last = it - 1;
+            mbar_wait(&sh->stage_empty[last % kStagesG], (last / kStagesG) & 1u, watchdog_drain, p.watchdog);
+        }
+    } else if (warp >= 2 && warp < 6) {
+        // ------------------------------------------------- dequant warps
+        const int r = tid - 64;  // B-operand row of this thread
+        uint32_t it = 0, lt = 0;
+        bool scale_ok = true;
+        for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x, ++lt) {
+            const int sb = int(lt & 1u);
+            if (!mbar_wait(&sh->sc_full[sb], (lt >> 1) & 1u, watchdog_full_barrier, p.watchdog)) {
+                *abort_flag = 1;
+                break;
+            }
+            const uint8_t* srow = smem + kSmemScale + sb * kScaleBytes + r * sc_row;
+            // Rows past the weight tensor were zero-filled and have no scale bytes.
+            int r_lo, r_hi;
+            tile_rows(p, tile_info(p, tile), r_lo, r_hi);
+            const bool row_in_tensor = (r < BN / 2 ? r_lo + r : r_hi + (r - BN / 2)) < p.E * p.Nrows;
+            for (int ks = 0; ks < KS; ++ks, ++it) {
+                const int s = int(it % kStagesG);
+                if (!mbar_wait(&sh->tma_full[s], (it / kStagesG) & 1u, watchdog_full_barrier, p.watchdog)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                const uint8_t* raw = smem + kSmemRaw + s * kRawBytes + r * (BK / 2);
+                const uint4 c0 = *reinterpret_cast<const uint4*>(raw);
+                const uint4 c1 = *reinterpret_cast<const uint4*>(raw + 16);
+                bool ok0, ok1;
+                const uint32_t s0 = e8m0_half2(srow[2 * ks], ok0), s1 = e8m0_half2(srow[2 * ks + 1], ok1);
+                scale_ok = scale_ok && (!row_in_tensor || (ok0 && ok1));
+                const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                uint8_t* brow = smem + kSmemB + s * kBBytes + r * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    // 16-byte chunk c = values 8c..8c+7 = code bytes 4c..4c+3.
+                    const uint32_t w = words[c], sc = c < 4 ? s0 : s1;
+                    uint4 h;
+                    h.x = hmul2_bits(e2m1x2_to_half2(w & 0xFFu), sc);
+                    h.y = hmul2_bits(e2m1x2_to_half2((w >> 8) & 0xFFu), sc);
+                    h.z = hmul2_bits(e2m1x2_to_half2((w >> 16) & 0xFFu), sc);
+                    h.w = hmul2_bits(e2m1x2_to_half2(w >> 24), sc);
+                    *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = h;
+                }
+                fence_proxy_async();
+                mbar_arrive(&sh->b_full[s]);
+            }
+            mbar_arrive(&sh->sc_empty[sb]);
+        }
+        if (!scale_ok && p.status)
+            atomicOr(p.status, 2u);
+    } else if (warp >= 6) {
+        // ------------------------------------------------- epilogue warps
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row = 32 * q + lane;
+        uint32_t lt = 0;
+        for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x, ++lt) {
+            const TileInfo t = tile_info(p, tile);
+            const int acc = int(lt & 1u);
+            if (!mbar_wait(&sh->acc_full[acc], (lt >> 1) & 1u, watchdog_full_barrier, p.watchdog)) {
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const int prow = t.m0 + row;
+            const bool valid = prow < t.mend;
+            const uint32_t taddr = tmem + uint32_t(acc * BN) + (uint32_t(32 * q) << 16);
+            if (p.epilogue == 0) {
+                // Activation of (gate, up) pairs -> fp16 act[prow, j].
+                auto* act = static_cast<__half*>(p.out);
+                const int I = p.Nrows / 2;
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t g[32], u[32];
+                    if (p.split) {
+                        tmem_ld32(taddr + uint32_t(32 * c), g);
+                        tmem_ld32(taddr + uint32_t(64 + 32 * c), u);
+                    } else {
+                        // Interleaved: column 2i gate, 2i+1 up.
+                        uint32_t a[32], b[32];
+                        tmem_ld32(taddr + uint32_t(64 * c), a);
+                        tmem_ld32(taddr + uint32_t(64 * c + 32), b);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            g[i] = a[2 * i], u[i] = a[2 * i + 1];
+                            g[16 + i] = b[2 * i], u[16 + i] = b[2 * i + 1];
+                        }
+                    }
+                    tmem_wait_ld();
+                    const int j0 = t.nt * (BN / 2) + 32 * c;
+                    if (valid && j0 < I) {
+                        __align__(16) __half vals[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int j = j0 + i;
+                            float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
+                            if (p.bias) {
+                                const int gr = p.split ? j : 2 * j, ur = p.split ? I + j : 2 * j + 1;
+                                gv += p.bias[size_t(t.e) * p.Nrows + gr];
+                                uv += p.bias[size_t(t.e) * p.Nrows + ur];
+                            }
+                            vals[i] = __float2half_rn(act_fn(gv, uv, p.act_kind, p.limit, p.alpha));
+                        }
+                        __half* dst = act + size_t(prow) * p.out_cols + j0;
+                        const int n = min(32, I - j0);
+                        if (n == 32) {
+#pragma unroll
+                            for (int v = 0; v < 4; ++v)
+                                reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(vals)[v];
+                        } else {
+                            for (int i = 0; i < n; ++i)
+                                dst[i] = vals[i];
+                        }
+                    }
+                }
+            } else {
+                auto* y = static_cast<float*>(p.out);
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + uint32_t(32 * c), v);
+                    tmem_wait_ld();
+                    const int n0 = t.nt * BN + 32 * c;
+                    if (valid && n0 < p.Nrows) {
+                        float* dst = y + size_t(prow) * p.out_cols + n0;
+                        const int n = min(32, p.Nrows - n0);
+                        __align__(16) float f[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            f[i] = __uint_as_float(v[i])
+                                   + (p.bias && i < n ? p.bias[size_t(t.e) * p.Nrows + n0 + i] : 0.f);
+                        if (n == 32) {
+#pragma unroll
+                            for (int k = 0; k < 8; ++k)
+                                reinterpret_cast<float4*>(dst)[k] = reinterpret_cast<const float4*>(f)[k];
+                        } else {
+                            for (int i = 0; i < n; ++i)
+                                dst[i] = f[i];
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&sh->acc_empty[acc]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess
+            && q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, int esize, const void* base, uint64_t inner, uint64_t rows,
+               uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+    auto enc = encoder();
+    if (!enc)
+        return false;
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {inner * uint64_t(esize)};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(map, type, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE)
+           == CUDA_SUCCESS;
+}
+
+size_t align_up(size_t v, size_t a) {
+    return (v + a - 1) / a * a;
+}
+
+struct Workspace {
+    int *chosen, *counts, *offsets, *perm, *pos, *mtile;
+    float* weight;
+    __half *xs, *act;
+    float* y;
+    size_t bytes;
+};
+
+Workspace carve(void* base, const kb200_moe_weights& w, size_t tokens) {
+    const size_t n = tokens * size_t(w.top_k), E = size_t(w.experts);
+    auto* b = static_cast<uint8_t*>(base);
+    size_t at = 0;
+    auto take = [&](size_t bytes) {
+        uint8_t* p = b ? b + at : nullptr;
+        at = align_up(at + bytes, 256);
+        return p;
+    };
+    Workspace ws;
+    ws.chosen = reinterpret_cast<int*>(take(n * 4));
+    ws.weight = reinterpret_cast<float*>(take(n * 4));
+    ws.counts = reinterpret_cast<int*>(take(E * 4));
+    ws.offsets = reinterpret_cast<int*>(take((E + 1) * 4));
+    ws.perm = reinterpret_cast<int*>(take(n * 4));
+    ws.pos = reinterpret_cast<int*>(take(n * 4));
+    ws.mtile = reinterpret_cast<int*>(take((E + 1) * 4));
+    ws.xs = reinterpret_cast<__half*>(take(n * size_t(w.hidden) * 2));
+    ws.act = reinterpret_cast<__half*>(take(n * size_t(w.inter) * 2));
+    ws.y = reinterpret_cast<float*>(take(n * size_t(w.hidden) * 4));
+    ws.bytes = at;
+    return ws;
+}
+
+int check_weights(const kb200_moe_weights* w) {
+    if (!w)
+        return fail(KB200_INVALID, "null MoE weights");
+    if (w->hidden <= 0 || w->inter <= 0 || w->experts <= 0 || w->top_k <= 0)
+        return fail(KB200_INVALID, "MoE shape must be positive");
+    if (w->hidden % 64 || w->inter % 64 || w->hidden > kMaxK || w->inter > kMaxK)
+        return fail(KB200_UNSUPPORTED, "hidden and inter must be multiples of 64, at most 4096");
+    if (w->experts > kMaxExperts || w->top_k > std::min(w->experts, kMaxTopK))
+        return fail(KB200_UNSUPPORTED, "at most 256 experts and top_k <= min(experts, 32)");
+    if (!w->gate_up_blocks || !w->gate_up_scales || !w->down_blocks || !w->down_scales)
+        return fail(KB200_INVALID, "null MoE weight pointer");
+    if (!aligned(w->gate_up_blocks, 16) || !aligned(w->down_blocks, 16) || !aligned(w->gate_up_scales, 16)
+        || !aligned(w->down_scales, 16))
+        return fail(KB200_INVALID, "MoE weights must be 16-byte aligned");
+    if (w->activation != KB200_MOE_SWIGLU_OAI && w->activation != KB200_MOE_SILU)
+        return fail(KB200_UNSUPPORTED, "unknown MoE activation");
+    return KB200_OK;
+}
+
+int gemm_slots() {
+    static int set[64] = {};
+    static std::mutex lock;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> guard(lock);
+    if (!set[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
+        if (e != cudaSuccess)
+            return -cuda_fail(e, "moe_gemm_kernel attribute");
+        set[dev] = 1;
+    }
+    return sm_count();
+}
+
+int launch_gemm(GroupParams& p, int max_tiles, cudaStream_t stream) {
+    const int slots = gemm_slots();
+    if (slots <= 0)
+        return -slots;
+    p.watchdog = watchdog_word();
+    const int grid = std::max(1, std::min(slots, max_tiles));
+    moe_gemm_kernel<<<grid, kThreadsG, kSmemTotal, stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_gemm_kernel launch");
+}
+
+}  // namespace
+}  // namespace kb200
+
+using namespace kb200;
+
+extern "C" {
+
+size_t kb200_moe_workspace_bytes(const kb200_moe_weights* w, size_t tokens) {
+    if (!w || check_weights(w) != KB200_OK)
+        return 0;
+    return carve(nullptr, *w, tokens).bytes;
+}
+
+int kb200_moe_route(const float* logits, size_t tokens, int32_t experts, int32_t top_k, int32_t* chosen, float* weight,
+                    void* stream) {
+    if (experts <= 0 || experts > kMaxExperts || top_k <= 0 || top_k > std::min(experts, kMaxTopK))
+        return fail(KB200_UNSUPPORTED, "routing shape");
+    if (!tokens)
+        return KB200_OK;
+    if (!logits || !chosen || !weight)
+        return fail(KB200_INVALID, "null pointer");
+    const int threads = 256, blocks = int((tokens * 32 + threads - 1) / threads);
+    moe_route_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(logits, int(tokens), experts, top_k,
+                                                                              chosen, weight, nullptr);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_route_kernel launch");
+}
+
+int kb200_moe_forward(const kb200_moe_weights* w, const uint16_t* x_bf16, const float* logits, size_t tokens, float* out,
+                      void* workspace, size_t workspace_bytes, unsigned* status, void* stream_ptr) {
+    if (const int s = check_weights(w))
+        return s;
+    if (!tokens)
+        return KB200_OK;
+    if (!x_bf16 || !logits || !out || !workspace)
+        return fail(KB200_INVALID, "null pointer");
+    if (!aligned(x_bf16, 16) || !aligned(out, 16) || !aligned(workspace, 256))
+        return fail(KB200_INVALID, "MoE activations must be 16-byte aligned, workspace 256-byte aligned");
+    const size_t n = tokens * size_t(w->top_k);
+    if (n > size_t(INT32_MAX) / 4)
+        return fail(KB200_UNSUPPORTED, "too many tokens");
+    const Workspace ws = carve(workspace, *w, tokens);
+    if (ws.bytes > workspace_bytes)
+        return fail(KB200_NO_MEMORY, "MoE workspace too small (see kb200_moe_workspace_bytes)");
+    if (!encoder())
+        return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const int H = w->hidden, I = w->inter, E = w->experts, K = w->top_k;
+    auto stream = static_cast<cudaStream_t>(stream_ptr);
+    cudaError_t e = cudaMemsetAsync(ws.counts, 0, size_t(E) * 4, stream);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "counts memset");
+    moe_route_kernel<<<int((tokens * 32 + 255) / 256), 256, 0, stream>>>(logits, int(tokens), E, K, ws.chosen, ws.weight,
+                                                                          ws.counts);
+    moe_sort_kernel<<<1, 1024, 0, stream>>>(ws.chosen, int(n), E, ws.counts, ws.offsets, ws.perm, ws.pos, ws.mtile);
+    {
+        const size_t work = n * size_t(H / 8);
+        const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
+        moe_gather_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x_bf16), ws.perm, int(n), K,
+                                                      H, ws.xs, status);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return cuda_fail(e, "MoE routing launches");
+    const int mtiles_max = int((n + BM - 1) / BM) + E;
+
+    // gate/up: [n, H] x [2I, H]^T per expert, activation in the epilogue.
+    GroupParams g1;
+    std::memset(&g1, 0, sizeof(g1));
+    const bool split = !w->interleaved;
+    if (!encode_2d(&g1.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws.xs, uint64_t(H), n, BK, BM,
+                   CU_TENSOR_MAP_SWIZZLE_128B)
+        || !encode_2d(&g1.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->gate_up_blocks, uint64_t(H / 2),
+                      uint64_t(E) * 2 * I, BK / 2, split ? BN / 2 : BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(KB200_INVALID, "tensor map encoding (gate/up)");
+    g1.scales = w->gate_up_scales;
+    g1.bias = w->gate_up_bias;
+    g1.offsets = ws.offsets;
+    g1.mtile_prefix = ws.mtile;
+    g1.out = ws.act;
+    g1.K = H;
+    g1.Nrows = 2 * I;
+    g1.E = E;
+    g1.n_tiles = split ? I / (BN / 2) : 2 * I / BN;
+    g1.split = split ? 1 : 0;
+    g1.epilogue = 0;
+    g1.out_cols = I;
+    g1.act_kind = w->activation;
+    g1.limit = w->limit;
+    g1.alpha = w->alpha;
+    g1.status = status;
+    if ((2 * I) % BN && !split)
+        return fail(KB200_UNSUPPORTED, "interleaved gate/up needs 2*inter to be a multiple of 128");
+    if (const int s = launch_gemm(g1, mtiles_max * g1.n_tiles, stream))
+        return s;
+
+    // down: [n, I] x [H, I]^T per expert -> fp32 rows.
+    GroupParams g2;
+    std::memset(&g2, 0, sizeof(g2));
+    if (!encode_2d(&g2.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws.act, uint64_t(I), n, BK, BM,
+                   CU_TENSOR_MAP_SWIZZLE_128B)
+        || !encode_2d(&g2.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->down_blocks, uint64_t(I / 2), uint64_t(E) * H,
+                      BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(KB200_INVALID, "tensor map encoding (down)");
+    g2.scales = w->down_scales;
+    g2.bias = w->down_bias;
+    g2.offsets = ws.offsets;
+    g2.mtile_prefix = ws.mtile;
+    g2.out = ws.y;
+    g2.K = I;
+    g2.Nrows = H;
+    g2.E = E;
+    g2.n_tiles = (H + BN - 1) / BN;
+    g2.split = 0;
+    g2.epilogue = 1;
+    g2.out_cols = H;
+    g2.status = status;
+    if (const int s = launch_gemm(g2, mtiles_max * g2.n_tiles, stream))
+        return s;
+
+    {
+        const size_t work = tokens * size_t(H / 4);
+        const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
+        moe_combine_kernel<<<blocks, 256, 0, stream>>>(ws.y, ws.weight, ws.pos, int(tokens), K, H, out);
+    }
+    e = cudaGetLastError();
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_combine_kernel launch");
+}
+
+}  // extern "C"

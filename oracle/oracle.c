@@ -306,11 +306,18 @@ void orc_moe_route(
     free(taken);
 }
 
+/* sum_c decode(w, s)[c] * x[c] in double; each weight is exactly
+ * e2m1(code) * 2^(E-127), applied per 32-value block. */
 static double mx_dot(const uint8_t* w, const uint8_t* s, size_t cols, const float* x) {
     double acc = 0;
-    for (size_t c = 0; c < cols; ++c) {
-        const unsigned code = (w[c / 2] >> (4 * (c % 2))) & 15u;
-        acc += ldexp((double)orc_e2m1(code), (int)s[c / 32] - 127) * (double)x[c];
+    for (size_t b = 0; b < cols / 32; ++b) {
+        const double scale = ldexp(1.0, (int)s[b] - 127);
+        double part = 0;
+        for (size_t c = 32 * b; c < 32 * b + 32; ++c) {
+            const unsigned code = (w[c / 2] >> (4 * (c % 2))) & 15u;
+            part += (double)orc_e2m1(code) * (double)x[c];
+        }
+        acc += part * scale;
     }
     return acc;
 }
@@ -373,7 +380,7 @@ int orc_moe_forward(
                 } else {
                     a = (float)(g / (1.0 + exp(-g)) * u);
                 }
-                act[j] = round_act ? orc_bf16_round(a) : a;
+                act[j] = round_act == 1 ? orc_bf16_round(a) : round_act == 2 ? (float)(_Float16)a : a;
             }
             const uint8_t* dw = dn_w + e * hidden * dn_row;
             const uint8_t* ds = dn_s + e * hidden * dn_srow;

@@ -76,8 +76,8 @@ enum orc_moe_activation {
 
 /* Full MXFP4 MoE layer. gate_up rows: 2*inter per expert; with interleaved=1
  * gate is row 2i and up row 2i+1, else gate rows [0,inter) and up [inter,2inter).
- * gu_bias [E,2*inter] and down_bias [E,hidden] may be NULL. round_act=1 rounds
- * the activation fed to the down projection to bf16 (as the device does). */
+ * gu_bias [E,2*inter] and down_bias [E,hidden] may be NULL. round_act rounds
+ * the activation fed to the down projection: 0 no, 1 to bf16, 2 to fp16. */
 int orc_moe_forward(
     size_t tokens,
     size_t hidden,
