@@ -226,6 +226,31 @@ KB200_API int kb200_moe_forward(
     void* stream
 );
 
+/* kb200_moe_forward without a caller workspace and without any allocation.
+ * No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory per call — code running inside CUDA stream capture
+ * (cudaMalloc/cudaFree are not capturable and synchronise the device) and
+ * workers whose device memory is fully admitted to a budget ledger, as the
+ * Hikari worker's resource accounting does. The scratch is one file-scope
+ * device array of KB200_MOE_STATIC_SCRATCH_BYTES (16 MiB) that every GPU
+ * loading the library holds until the process exits; calls whose
+ * kb200_moe_workspace_bytes exceeds it fail with KB200_NO_MEMORY before any
+ * work. The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * All calls on a device share the array and its contents persist between
+ * calls: calls that overlap on the GPU (other streams, other threads) race
+ * and must be serialised by the caller. */
+#define KB200_MOE_STATIC_SCRATCH_BYTES (16u << 20)
+KB200_API int kb200_moe_forward_noalloc(
+    const kb200_moe_weights* w,
+    const uint16_t* x_bf16,
+    const float* logits,
+    size_t tokens,
+    float* out,
+    unsigned* status,
+    void* stream
+);
+
 /* The routing stage alone (for tests): chosen [tokens, top_k] int32,
  * weight [tokens, top_k] fp32, device. */
 KB200_API int kb200_moe_route(

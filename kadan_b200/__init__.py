@@ -307,3 +307,21 @@ def moe_route(logits, top_k: int, stream=None):
     weight = torch.empty(tokens, top_k, dtype=torch.float32, device=logits.device)
     check(lib.kb200_moe_route(_ptr(logits), tokens, experts, top_k, _ptr(chosen), _ptr(weight), _stream_ptr(stream)))
     return chosen, weight
+
+
+def moe_forward_noalloc(w: MoeWeights, x_bf16, logits, out=None, status=None, stream=None):
+    """kb200_moe_forward_noalloc: the MoE layer on the library's fixed 16 MiB
+    device scratch, for callers that cannot allocate per call."""
+    import torch
+
+    tokens = x_bf16.shape[0]
+    if out is None:
+        out = torch.empty(tokens, w.hidden, dtype=torch.float32, device=x_bf16.device)
+    check(lib.kb200_moe_forward_noalloc(ctypes.byref(w), _ptr(x_bf16), _ptr(logits), tokens, _ptr(out), _ptr(status),
+                                        _stream_ptr(stream)))
+    return out
+
+
+lib.kb200_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+STATIC_MOE_SCRATCH_BYTES = 16 << 20

@@ -698,6 +698,42 @@ int launch_gemm(GroupParams& p, int max_tiles, cudaStream_t stream) {
 
 using namespace kb200;
 
+namespace kb200 {
+namespace {
+
+// Scratch of kb200_moe_forward_noalloc: a file-scope device array, so every
+// GPU that loads this library holds KB200_MOE_STATIC_SCRATCH_BYTES of it
+// until the process exits. Host code must not use the symbol itself as a
+// pointer (that is a host-side stand-in); static_scratch() returns the
+// device address.
+__device__ __align__(256) uint8_t moe_static_scratch[KB200_MOE_STATIC_SCRATCH_BYTES];
+
+// Device address of moe_static_scratch on the current device, looked up once
+// per device (with that device current) on its first use.
+int static_scratch(void** ptr) {
+    static void* address[64] = {};
+    static std::mutex lock;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64)
+        return fail(KB200_UNSUPPORTED, "device index above 63");
+    std::lock_guard<std::mutex> guard(lock);
+    if (!address[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, moe_static_scratch);
+        if (e != cudaSuccess)
+            return cuda_fail(e, "cudaGetSymbolAddress(moe_static_scratch)");
+        address[dev] = p;
+    }
+    *ptr = address[dev];
+    return KB200_OK;
+}
+
+}  // namespace
+}  // namespace kb200
+
 extern "C" {
 
 size_t kb200_moe_workspace_bytes(const kb200_moe_weights* w, size_t tokens) {
@@ -818,6 +854,26 @@ int kb200_moe_forward(const kb200_moe_weights* w, const uint16_t* x_bf16, const 
     }
     e = cudaGetLastError();
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_combine_kernel launch");
+}
+
+// For callers that cannot allocate device memory per call (stream capture,
+// ledger-admitted workers): the same layer on the library's fixed scratch.
+// Allocates nothing; only the counts it must clear are reset (by the
+// asynchronous memset inside kb200_moe_forward), everything else it reads is
+// first written by the same call.
+int kb200_moe_forward_noalloc(const kb200_moe_weights* w, const uint16_t* x_bf16, const float* logits, size_t tokens,
+                              float* out, unsigned* status, void* stream) {
+    if (const int s = check_weights(w))
+        return s;
+    if (!tokens)
+        return KB200_OK;
+    const size_t need = carve(nullptr, *w, tokens).bytes;
+    if (need > KB200_MOE_STATIC_SCRATCH_BYTES)
+        return fail(KB200_NO_MEMORY, "tokens need more than the 16 MiB static MoE scratch of kb200_moe_forward_noalloc");
+    void* scratch = nullptr;
+    if (const int s = static_scratch(&scratch))
+        return s;
+    return kb200_moe_forward(w, x_bf16, logits, tokens, out, scratch, KB200_MOE_STATIC_SCRATCH_BYTES, status, stream);
 }
 
 }  // extern "C"
