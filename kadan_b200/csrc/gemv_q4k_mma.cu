@@ -20,14 +20,30 @@
 //   epilogue   :  acc += (d*s/16) * (I_h + I_l/256) - (256 dmin) * C_min
 //
 // CTA = 4 consumer warps + 1 producer lane. A tile is R weight rows (R = 64,
-// 32 or 16, chosen per launch so that small outputs still fill the GPU) over
-// all of K; with R < 64 the warps split K (2 or 4 ways) and reduce in shared
-// memory at the end. The producer streams each stage (R rows x 128/R
-// super-blocks, 18 KB) with one 3-D TMA tile load per super-block column into
-// a 3-stage ring; a 144-byte row pitch keeps every fragment load free of bank
-// conflicts. The activations of a whole K segment (all of K at decode shapes)
-// are quantised once per CTA and job, so consumer warps run without any
-// barrier between them: wait for a stage, issue its MMAs, release it.
+// 32 or 16) for one group of input rows; with R < 64 the warps split K (2 or 4
+// ways) and reduce in shared memory at the end. The producer streams each
+// stage (R rows x 128/R super-blocks, 18 KB) with one 3-D TMA tile load per
+// super-block column into a 3-stage ring, optionally running an L2 prefetch
+// of the same boxes a few stages ahead; a 144-byte row pitch keeps every
+// fragment load free of bank conflicts. The activations of a K segment (all
+// of K at decode shapes) are quantised once per CTA and input, so consumer
+// warps run without any barrier between them: wait for a stage, issue its
+// MMAs, release it.
+//
+// Work split (balanced, "stream-K"): the launch's work is the sequence of
+// units (tile, super-block), tiles of all jobs in order, K innermost. CTA c of
+// G takes units [c*U/G, (c+1)*U/G), so every CTA streams the same number of
+// bytes and no CTA is left with a second wave (tiles are 64 rows). A tile cut
+// by CTA boundaries is computed in pieces. The CTA holding its first unit
+// reaches it last (it is that CTA's final piece) and writes the outputs; every
+// other piece is the first piece of a later CTA ("head piece"), done early:
+// its consumers store each partial sum with a "present" tag as one 64-bit
+// word (single-copy atomic, so no fence or flag is needed) in the CTA's slot
+// of a fixup buffer. The first CTA's consumers, at the end of their own
+// piece, read those words (re-reading any whose tag is not there yet), add
+// them in CTA order, so the sum does not depend on timing, and zero them for
+// the next launch. Without a fixup buffer (first use of a stream inside graph
+// capture) the launch falls back to whole tiles dealt round-robin.
 //
 // Launched with programmatic dependent launch: the producer starts streaming
 // weights while the previous kernel in the stream is still finishing; the
@@ -35,10 +51,12 @@
 // outputs. Weights must therefore not be produced by the immediately
 // preceding kernel of the stream.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -64,17 +82,62 @@ struct alignas(64) MmaJob {
     const float* input;
     float* output;
     unsigned* status;
-    uint64_t stride;
-    uint32_t in, columns, rows, first_tile;
-    uint32_t row_groups, group_rows, nblocks, pad;
+    uint32_t stride, in, columns, rows;
+    uint32_t first_tile, first_unit;  // prefix of tiles / of tiles x nblocks
+    uint32_t row_groups, group_rows, nblocks;
 };
+
+// Partial sums of one piece: acc[NT <= 2][2] of each consumer thread.
+constexpr int kSlotFloats = 2 * 2 * kConsumerThreads;
+// Fewest 64-row x 1 super-block units per CTA for which the balanced split
+// pays for its fixup (a round trip to L2 at the end of each cut tile).
+constexpr int kMinUnitsPerCta = 6;
 
 struct MmaParams {
     MmaJob jobs[kMaxJobsQ];
     uint32_t count, total_tiles;
-    uint32_t tile_rows;  // R: 64, 32 or 16
+    uint32_t tile_rows;    // R: 64, 32 or 16
+    uint32_t total_units;  // balanced split over units; 0 = whole tiles round-robin
+    uint32_t prefetch;     // L2 prefetch distance in stages (0 = off)
+    // [gridDim.x][kSlotFloats] head-piece partial sums as {fp32 bits, 1}
+    // words; zero between launches.
+    unsigned long long* partials;
     unsigned* watchdog;
 };
+
+// Relaxed 64-bit global accesses: single-copy atomic, so a partial sum and
+// its "present" tag, stored as one word, are seen together or not at all.
+__device__ __forceinline__ void store_relaxed(unsigned long long* at, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(at), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long load_relaxed(const unsigned long long* at) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(at) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long tagged(float v) {
+    return (1ull << 32) | __float_as_uint(v);
+}
+
+// A contiguous run of one tile's super-blocks [k0, k1) taken by this CTA.
+struct Piece {
+    int job;
+    uint32_t tile;            // tile within the job: column tile * row_groups + row group
+    uint32_t k0, k1;
+    bool whole;               // k0 == 0 && k1 == nblocks
+    uint32_t c_first, c_last; // CTAs holding the tile's first / last unit (cut tiles)
+};
+
+__device__ __forceinline__ uint32_t range_begin(uint32_t total_units, uint32_t cta) {
+    return uint32_t(uint64_t(cta) * total_units / gridDim.x);
+}
+
+// CTA whose unit range holds unit x (every range is non-empty: G <= U).
+__device__ __forceinline__ uint32_t cta_of(uint32_t total_units, uint32_t x) {
+    return uint32_t((uint64_t(x + 1) * gridDim.x - 1) / total_units);
+}
 
 // Activation segment: per super-block and token, the quantised h/l operands
 // in B-fragment order ([j][t][part][4 words], 512 bytes), the minimum-term B
@@ -89,14 +152,14 @@ struct Layout {
     static constexpr int kSegOff = kStages * kStageBytes;
     static constexpr int kRedOff = kSegOff + kSegBudget;       // split-K partials
     static constexpr int kRedBytes = kConsumerThreads * 4 * 4;  // [nt<=2][2][thread]
-    static constexpr int kBarOff = kRedOff + kRedBytes;
+    static constexpr int kBarOff = kRedOff + kRedBytes;  // full[], empty[], abort flag
     static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
 };
 
 // Segment of `rows` tokens: the most whole stages (multiples of `bps`
 // super-blocks) that fit kSegBudget; operands first, then minimum-term
 // operands, then scales. blocks == 0 means not even one stage fits (the host
-// never launches such a geometry, see segment_fits()).
+// never launches such a geometry).
 __host__ __device__ constexpr int segment_blocks(int rows, int bps) {
     return kSegBudget / (rows * kTokenBlockTotal) / bps * bps;
 }
@@ -113,17 +176,95 @@ struct Segment {
     }
 };
 
-__device__ __forceinline__ int find_job(const MmaParams& p, uint32_t tile) {
+// Last job whose first tile (units = false) or first unit (units = true) is <= at.
+__device__ __forceinline__ int find_job(const MmaParams& p, uint32_t at, bool units) {
     int low = 0, high = int(p.count);
     while (high - low > 1) {
         const int mid = (low + high) / 2;
-        if (p.jobs[mid].first_tile <= tile)
+        if ((units ? p.jobs[mid].first_unit : p.jobs[mid].first_tile) <= at)
             low = mid;
         else
             high = mid;
     }
     return low;
 }
+
+// The pieces of this CTA in order. Producer, prefetcher and consumers each
+// walk their own copy and see the same sequence.
+struct PieceIter {
+    uint32_t cur, end;
+
+    __device__ explicit PieceIter(const MmaParams& p) {
+        if (p.total_units) {
+            cur = range_begin(p.total_units, blockIdx.x);
+            end = range_begin(p.total_units, blockIdx.x + 1);
+        } else {
+            cur = blockIdx.x;
+            end = p.total_tiles;
+        }
+    }
+
+    __device__ bool next(const MmaParams& p, Piece& pc) {
+        if (cur >= end)
+            return false;
+        if (!p.total_units) {
+            pc.job = find_job(p, cur, false);
+            pc.tile = cur - p.jobs[pc.job].first_tile;
+            pc.k0 = 0;
+            pc.k1 = p.jobs[pc.job].nblocks;
+            pc.whole = true;
+            cur += gridDim.x;
+            return true;
+        }
+        pc.job = find_job(p, cur, true);
+        const MmaJob& job = p.jobs[pc.job];
+        const uint32_t local = cur - job.first_unit, nb = job.nblocks;
+        pc.tile = local / nb;
+        pc.k0 = local % nb;
+        pc.k1 = min(nb, pc.k0 + (end - cur));
+        pc.whole = pc.k0 == 0 && pc.k1 == nb;
+        if (!pc.whole) {
+            const uint32_t x0 = cur - pc.k0;
+            pc.c_first = cta_of(p.total_units, x0);
+            pc.c_last = cta_of(p.total_units, x0 + nb - 1);
+        }
+        cur += pc.k1 - pc.k0;
+        return true;
+    }
+};
+
+__device__ __forceinline__ void prefetch_l2_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(c0), "r"(c1), "r"(c2)
+        : "memory"
+    );
+}
+
+// L2 prefetch cursor: walks the producer's stage sequence ahead of it.
+struct Prefetcher {
+    PieceIter pieces;
+    Piece pc;
+    uint32_t b0 = 0;
+    bool live = false;
+
+    __device__ explicit Prefetcher(const MmaParams& p) : pieces(p) {}
+
+    // Prefetch the next stage (BPS super-blocks of R rows) into L2.
+    __device__ void step(const MmaParams& p, int R, int BPS) {
+        if (!live || b0 >= pc.k1) {
+            if (!pieces.next(p, pc))
+                return;
+            live = true;
+            b0 = pc.k0;
+        }
+        const MmaJob& job = p.jobs[pc.job];
+        const int row0 = int((pc.tile / job.row_groups) * uint32_t(R));
+        const uint32_t stop = min(pc.k1, b0 + uint32_t(BPS));
+        for (uint32_t b = b0; b < stop; ++b)
+            prefetch_l2_3d(&job.map, 0, int(b), row0);
+        b0 = stop;
+    }
+};
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
     asm volatile(
@@ -195,58 +336,79 @@ __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = lane >> 2, t = lane & 3;
     const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (in & 3) == 0;
-    for (int item = warp; item < nblk * rows; item += kWarps) {
-        const int blk = item / rows, tok = item % rows;
-        const float* xr = x + size_t(tok) * in + size_t(blk0 + blk) * 256 + lane * 8;
-        float v[8];
-        if (vec) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(xr)), b = __ldg(reinterpret_cast<const float4*>(xr) + 1);
-            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-        } else {
+    const int items = nblk * rows;
+    // kBatch items per warp at a time, without branches between them: all
+    // their loads are in flight before the first is used (the activations
+    // come from L2, a microsecond away under full HBM load) and the four
+    // reduction chains interleave.
+    constexpr int kBatch = 4;
+    for (int base = warp; base < items; base += kWarps * kBatch) {
+        float v[kBatch][8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                v[i] = __ldg(xr + i);
-        }
-        float m = 0.f, sum = 0.f;
+        for (int q = 0; q < kBatch; ++q) {
+            const int item = min(base + q * kWarps, items - 1);  // past the end: reload the last, store nothing
+            const int blk = item / rows, tok = item % rows;
+            const float* xr = x + size_t(tok) * in + size_t(blk0 + blk) * 256 + lane * 8;
+            if (vec) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(xr)), b = __ldg(reinterpret_cast<const float4*>(xr) + 1);
+                v[q][0] = a.x, v[q][1] = a.y, v[q][2] = a.z, v[q][3] = a.w;
+                v[q][4] = b.x, v[q][5] = b.y, v[q][6] = b.z, v[q][7] = b.w;
+            } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            m = fmaxf(m, fabsf(v[i]));
-            sum += v[i];
+                for (int i = 0; i < 8; ++i)
+                    v[q][i] = __ldg(xr + i);
+            }
+        }
+        float m[kBatch], sum[kBatch], next[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            m[q] = 0.f, sum[q] = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                m[q] = fmaxf(m[q], fabsf(v[q][i]));
+                sum[q] += v[q][i];
+            }
+            // Non-negative floats order as their bit patterns.
+            m[q] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m[q])));
+            sum[q] += __shfl_xor_sync(0xffffffffu, sum[q], 1);
+            sum[q] += __shfl_xor_sync(0xffffffffu, sum[q], 2);
+            next[q] = __shfl_xor_sync(0xffffffffu, sum[q], 4);  // sum of sub-block G ^ 1
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1)
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        const float next = __shfl_xor_sync(0xffffffffu, sum, 4);  // sum of sub-block G ^ 1
-        const float inv = m > 0.f ? 127.f / m : 0.f;
-        int h[8], l[8];
+        for (int q = 0; q < kBatch; ++q) {
+            const int item = base + q * kWarps;
+            if (item >= items)
+                break;
+            const int blk = item / rows, tok = item % rows;
+            const float inv = m[q] > 0.f ? 127.f / m[q] : 0.f;
+            int h[8], l[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float y = v[i] * inv;
-            h[i] = round_int(y);
-            l[i] = max(-127, min(127, round_int((y - float(h[i])) * 256.f)));
+            for (int i = 0; i < 8; ++i) {
+                const float y = v[q][i] * inv;
+                h[i] = round_int(y);
+                l[i] = max(-127, min(127, round_int((y - float(h[i])) * 256.f)));
+            }
+            const int slot = blk * rows + tok;
+            uint32_t* dst = frag + slot * (kTokenBlockBytes / 4);
+            const int idx = (((G >> 1) * 4 + t) * 2) * 4 + (G & 1) * 2;  // part h; part l is +4
+            dst[idx] = pack4(h[0], h[1], h[2], h[3]);
+            dst[idx + 1] = pack4(h[4], h[5], h[6], h[7]);
+            dst[idx + 4] = pack4(l[0], l[1], l[2], l[3]);
+            dst[idx + 5] = pack4(l[4], l[5], l[6], l[7]);
+            // Minimum term B' for lane (g, t') = sums of sub-blocks 2t', 2t'+1
+            // (scaled by 1/256) split into fp16 hi and lo: written by lanes 8t'.
+            if ((lane & 7) == 0) {
+                const float s0 = sum[q] * (1.f / 256.f), s1 = next[q] * (1.f / 256.f);
+                const __half2 hi = __floats2half2_rn(s0, s1);
+                const float2 hf = __half22float2(hi);
+                const __half2 lo = __floats2half2_rn(s0 - hf.x, s1 - hf.y);
+                uint32_t* mb = minb + slot * (kMinBytes / 4);
+                mb[lane >> 3] = pack_half2(hi);
+                mb[4 + (lane >> 3)] = pack_half2(lo);
+            }
+            if (lane == 0)
+                scales[slot] = m[q] > 0.f ? m[q] / 127.f : 0.f;
         }
-        const int slot = blk * rows + tok;
-        uint32_t* base = frag + slot * (kTokenBlockBytes / 4);
-        const int idx = (((G >> 1) * 4 + t) * 2) * 4 + (G & 1) * 2;  // part h; part l is +4
-        base[idx] = pack4(h[0], h[1], h[2], h[3]);
-        base[idx + 1] = pack4(h[4], h[5], h[6], h[7]);
-        base[idx + 4] = pack4(l[0], l[1], l[2], l[3]);
-        base[idx + 5] = pack4(l[4], l[5], l[6], l[7]);
-        // Minimum term B' for lane (g, t') = sums of sub-blocks 2t', 2t'+1
-        // (scaled by 1/256) split into fp16 hi and lo: written by lanes 8t'.
-        if ((lane & 7) == 0) {
-            const float s0 = sum * (1.f / 256.f), s1 = next * (1.f / 256.f);
-            const __half2 hi = __floats2half2_rn(s0, s1);
-            const float2 hf = __half22float2(hi);
-            const __half2 lo = __floats2half2_rn(s0 - hf.x, s1 - hf.y);
-            uint32_t* mb = minb + slot * (kMinBytes / 4);
-            mb[lane >> 3] = pack_half2(hi);
-            mb[4 + (lane >> 3)] = pack_half2(lo);
-        }
-        if (lane == 0)
-            scales[slot] = m > 0.f ? m / 127.f : 0.f;
     }
 }
 
@@ -261,6 +423,7 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
     auto* abort_flag = reinterpret_cast<int*>(empty + kStages);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int R = int(p.tile_rows), KS = 64 / R, BPS = kStageUnits / R;
+    auto* red = reinterpret_cast<float*>(smem + L::kRedOff);
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -279,23 +442,28 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
         if (lane != 0)
             return;
         uint32_t it = 0;
-        for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
-            const MmaJob& job = p.jobs[find_job(p, tile)];
-            const uint32_t local = tile - job.first_tile;
-            const int row0 = int((local / job.row_groups) * uint32_t(R));
-            const uint32_t stages = (job.nblocks + BPS - 1) / BPS;
+        PieceIter pieces(p);
+        Prefetcher ahead(p);
+        for (uint32_t i = 0; i < p.prefetch; ++i)
+            ahead.step(p, R, BPS);
+        Piece pc;
+        while (pieces.next(p, pc)) {
+            const MmaJob& job = p.jobs[pc.job];
+            const int row0 = int((pc.tile / job.row_groups) * uint32_t(R));
             asm volatile("prefetch.tensormap [%0];" ::"l"(&job.map) : "memory");
-            for (uint32_t kc = 0; kc < stages; ++kc, ++it) {
+            for (uint32_t b0 = pc.k0; b0 < pc.k1; b0 += BPS, ++it) {
                 const int slot = int(it % kStages);
                 if (it >= kStages && !mbar_wait(&empty[slot], ((it / kStages) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog))
                     atomicExch(abort_flag, 1);
                 if (*reinterpret_cast<volatile int*>(abort_flag))
                     goto drain;
-                const int nb = int(min(uint32_t(BPS), job.nblocks - kc * BPS));
+                const int nb = int(min(uint32_t(BPS), pc.k1 - b0));
                 mbar_expect_tx(&full[slot], uint32_t(nb * R * kBlockBytes));
                 for (int b = 0; b < nb; ++b)
                     tma_load_3d(smem + L::kStagesOff + slot * kStageBytes + b * R * kBlockBytes, &job.map, 0,
-                                int(kc * BPS + b), row0, &full[slot]);
+                                int(b0 + b), row0, &full[slot]);
+                if (p.prefetch)
+                    ahead.step(p, R, BPS);
             }
         }
     drain:
@@ -312,25 +480,21 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
     grid_dependency_wait();
     const int g = lane >> 2, t = lane & 3;
     const int rg = warp / KS, ks = warp % KS;  // row group and K split of this warp
-    auto* red = reinterpret_cast<float*>(smem + L::kRedOff);
     uint32_t it = 0;
-    // (input, rows, first block) of the activation segment held in shared memory.
+    // (input, rows, first block, blocks) of the activation segment held in shared memory.
     const float* seg_x = nullptr;
-    int seg_rows = -1, seg_blk0 = -1;
-    for (uint32_t tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
-        const MmaJob& job = p.jobs[find_job(p, tile)];
-        const uint32_t local = tile - job.first_tile;
-        const uint32_t row0 = (local / job.row_groups) * uint32_t(R);
-        const uint32_t r0 = (local % job.row_groups) * job.group_rows;
+    int seg_rows = -1, seg_blk0 = -1, seg_nblk = 0;
+    PieceIter pieces(p);
+    Piece pc;
+    while (pieces.next(p, pc)) {
+        const MmaJob& job = p.jobs[pc.job];
+        const uint32_t row0 = (pc.tile / job.row_groups) * uint32_t(R);
+        const uint32_t r0 = (pc.tile % job.row_groups) * job.group_rows;
         const int rows = int(min(job.group_rows, job.rows - r0));
-        const uint32_t stages = (job.nblocks + BPS - 1) / BPS;
         const float* x = job.input + size_t(r0) * job.in;
         const Segment seg(rows, BPS);
-        if (seg.blocks == 0) {
-            // A stage's activations would overflow the segment buffer.
+        if (seg.blocks < BPS)  // a stage's activations would overflow the segment buffer
             atomicExch(abort_flag, 1);
-            return;
-        }
         const uint8_t* frag = seg.frag(smem);
         const uint32_t* minb = seg.minb(smem);
         const float* scales = seg.scales(smem);
@@ -343,17 +507,20 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
         for (int nt = 0; nt < NT; ++nt)
             acc[nt][0] = acc[nt][1] = 0.f;
 
-        for (uint32_t kc = 0; kc < stages; ++kc, ++it) {
+        for (uint32_t b0 = pc.k0; b0 < pc.k1; b0 += BPS, ++it) {
             const int slot = int(it % kStages);
-            const int nb = int(min(uint32_t(BPS), job.nblocks - kc * BPS));
-            const int blk_first = int(kc) * BPS;
-            const int seg0 = blk_first / seg.blocks * seg.blocks;
-            if (x != seg_x || rows != seg_rows || seg0 != seg_blk0) {
+            const int nb = int(min(uint32_t(BPS), pc.k1 - b0));
+            const int blk_first = int(b0);
+            if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
+                && seg.blocks >= BPS) {
+                // The window covers this stage and the rest of the piece, as
+                // far as the segment buffer reaches.
+                const int count = min(seg.blocks, int(pc.k1) - blk_first);
                 // Every warp is done with the previous segment before it is replaced.
                 named_sync(1, kConsumerThreads);
-                prep_segment(smem, seg, x, job.in, seg0, int(min(uint32_t(seg.blocks), job.nblocks - seg0)));
+                prep_segment(smem, seg, x, job.in, blk_first, count);
                 named_sync(1, kConsumerThreads);
-                seg_x = x, seg_rows = rows, seg_blk0 = seg0;
+                seg_x = x, seg_rows = rows, seg_blk0 = blk_first, seg_nblk = count;
             }
             const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
             if (!aborted && !mbar_wait(&full[slot], (it / kStages) & 1u, watchdog_full_barrier, p.watchdog))
@@ -365,7 +532,7 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
                     const int b = 2 * ks + bb;  // this warp's super-blocks of the stage
                     if (b >= nb)
                         break;
-                    const int sblk = blk_first + b - seg0;  // block index within the segment
+                    const int sblk = blk_first + b - seg_blk0;  // block index within the segment
                     const uint8_t* rgp = stage + b * R * kBlockBytes + (16 * rg + g) * kBlockBytes;
                     const uint8_t* r8p = rgp + 8 * kBlockBytes;
                     const uint4 hg = *reinterpret_cast<const uint4*>(rgp);
@@ -471,7 +638,65 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
             }
             named_sync(1, kConsumerThreads);
         }
-        if (ks == 0) {
+        bool write = ks == 0;
+        if (!pc.whole && pc.k0 > 0) {
+            // Head piece of a cut tile (R = 64, every warp holds final sums):
+            // store the partial sums; the fixup lanes publish them.
+            // store the tagged partial sums (the slot was zeroed by the previous
+            // launch, which finished before the grid-dependency wait).
+            unsigned long long* mine = p.partials + size_t(blockIdx.x) * kSlotFloats;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                store_relaxed(mine + (nt * 2 + 0) * kConsumerThreads + tid, tagged(acc[nt][0]));
+                store_relaxed(mine + (nt * 2 + 1) * kConsumerThreads + tid, tagged(acc[nt][1]));
+            }
+            write = false;
+        } else if (!pc.whole) {
+            // Tail piece holding the tile's first unit: add the later pieces'
+            // sums in CTA order as their tags appear, and zero the words for
+            // the next launch on this stream.
+            constexpr int kAhead = 4;  // CTAs whose words are in flight together
+            const uint32_t others = pc.c_last - pc.c_first;
+            for (uint32_t c0 = 0; c0 < others; c0 += kAhead) {
+                unsigned long long w[kAhead][NT][2];
+#pragma unroll
+                for (int q = 0; q < kAhead; ++q) {
+                    const uint32_t c = pc.c_first + 1 + min(c0 + q, others - 1);
+                    const unsigned long long* part = p.partials + size_t(c) * kSlotFloats;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        w[q][nt][0] = load_relaxed(part + (nt * 2 + 0) * kConsumerThreads + tid);
+                        w[q][nt][1] = load_relaxed(part + (nt * 2 + 1) * kConsumerThreads + tid);
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < kAhead; ++q) {
+                    if (c0 + q >= others)
+                        break;
+                    unsigned long long* part = p.partials + size_t(pc.c_first + 1 + c0 + q) * kSlotFloats;
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                        for (int hl = 0; hl < 2; ++hl) {
+                            unsigned long long* at = part + (nt * 2 + hl) * kConsumerThreads + tid;
+                            unsigned long long v = w[q][nt][hl];
+                            for (uint32_t poll = 0; (v >> 32) != 1ull; ++poll) {
+                                if (poll == wait_polls) {
+                                    atomicOr(p.watchdog, watchdog_fixup);
+                                    atomicExch(abort_flag, 1);
+                                    break;
+                                }
+                                __nanosleep(32);
+                                v = load_relaxed(at);
+                            }
+                            acc[nt][hl] += __uint_as_float(uint32_t(v));
+                            store_relaxed(at, 0ull);
+                        }
+                    }
+                }
+            }
+        }
+        if (write) {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const int tok = nt * 4 + t;
@@ -484,8 +709,8 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
                 }
             }
         }
-        if (*reinterpret_cast<volatile int*>(abort_flag))
-            return;
+        // After an abort the remaining pieces still run (without waits or
+        // MMAs) so that every cut tile's counter is re-armed.
     }
 }
 
@@ -525,9 +750,66 @@ template <int NT> int kernel_slots() {
     return sm_count() * blocks_per_sm[dev];
 }
 
-template <int NT> int launch_q4k(const MmaParams& p, uint32_t slots, cudaStream_t stream) {
+// Fixup buffer of the balanced split for one (device, stream). Launches on one
+// stream run in order, and a launch touches the buffer only after its
+// grid-dependency wait, so every launch of the stream can share it.
+struct Fixup {
+    unsigned long long* partials = nullptr;
+    uint32_t ctas = 0;
+};
+
+// The stream's fixup buffer, allocated (and zeroed on the stream) by the
+// first call outside graph capture; null when none can be had.
+const Fixup* fixup_for(cudaStream_t stream) {
+    static std::mutex lock;
+    static std::map<std::pair<int, cudaStream_t>, Fixup> table;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return nullptr;
+    std::lock_guard<std::mutex> guard(lock);
+    Fixup& f = table[{dev, stream}];
+    if (f.ctas)
+        return &f;
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess || capture != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    // At most 4 CTAs of this kernel fit on an SM (shared memory).
+    const uint32_t ctas = uint32_t(sm_count()) * 4u;
+    Fixup made;
+    const size_t bytes = size_t(ctas) * kSlotFloats * sizeof(unsigned long long);
+    if (cudaMalloc(&made.partials, bytes) != cudaSuccess
+        || cudaMemsetAsync(made.partials, 0, bytes, stream) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(made.partials);
+        return nullptr;
+    }
+    made.ctas = ctas;
+    f = made;
+    return &f;
+}
+
+struct Tuning {
+    bool balanced = true;  // KB200_GEMV_BALANCED=0: whole tiles round-robin
+    uint32_t prefetch = 0; // KB200_GEMV_L2_PREFETCH=<stages>
+};
+
+const Tuning& tuning() {
+    static const Tuning t = [] {
+        Tuning v;
+        if (const char* s = std::getenv("KB200_GEMV_BALANCED"))
+            v.balanced = std::atoi(s) != 0;
+        if (const char* s = std::getenv("KB200_GEMV_L2_PREFETCH"))
+            v.prefetch = uint32_t(std::max(0, std::min(64, std::atoi(s))));
+        return v;
+    }();
+    return t;
+}
+
+template <int NT> int launch_q4k(const MmaParams& p, uint32_t grid, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::min(p.total_tiles, slots));
+    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreadsQ);
     cfg.dynamicSmemBytes = Layout::kTotal + 128;
     cfg.stream = stream;
@@ -544,7 +826,7 @@ template <int NT> int launch_q4k(const MmaParams& p, uint32_t slots, cudaStream_
 
 bool q4k_mma_eligible(const kb200_gemv_job& j) {
     return j.encoding == KB200_Q4_K && aligned(j.weights, 16) && j.row_bytes % 16 == 0 && j.in % 256 == 0
-           && j.row_bytes >= size_t(j.in) / 256 * 144 && encode_fn() != nullptr;
+           && j.row_bytes >= size_t(j.in) / 256 * 144 && j.stride <= 0xffffffffu && encode_fn() != nullptr;
 }
 
 int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream) {
@@ -560,37 +842,52 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     const int slots = nt == 1 ? kernel_slots<1>() : kernel_slots<2>();
     if (slots <= 0)
         return -slots;
+    const Fixup* fixup = tuning().balanced ? fixup_for(stream) : nullptr;
     for (size_t first = 0; first < jobs.size(); first += kMaxJobsQ) {
         const size_t n = std::min(jobs.size() - first, size_t(kMaxJobsQ));
-        // Tile height: the tallest of 64/32/16 rows that still gives every
+        int tokens = 1;
+        uint64_t units64 = 0;
+        for (size_t m = 0; m < n; ++m) {
+            const auto& j = *jobs[first + m];
+            tokens = std::max(tokens, int(std::min(j.rows, group_rows)));
+            units64 += uint64_t((j.columns + 63) / 64) * ((j.rows + group_rows - 1) / group_rows) * (j.in / 256);
+        }
+        if (segment_blocks(tokens, kStageUnits / 64) == 0)
+            return fail(KB200_UNSUPPORTED, "activation segment too small for this many rows");
+        // Whole tiles: the tallest of 64/32/16 rows that still gives every
         // CTA slot a tile; shorter tiles split K among the warps instead. A
         // tile height is only allowed if one stage of activations (128/R
         // super-blocks for every token) fits the segment buffer.
-        int tokens = 1;
-        for (size_t m = 0; m < n; ++m)
-            tokens = std::max(tokens, int(std::min(jobs[first + m]->rows, group_rows)));
-        if (segment_blocks(tokens, kStageUnits / 64) == 0)
-            return fail(KB200_UNSUPPORTED, "activation segment too small for this many rows");
         uint32_t R = 64;
+        uint64_t rr_tiles = 0;
         for (uint32_t cand : {64u, 32u, 16u}) {
             if (segment_blocks(tokens, kStageUnits / int(cand)) == 0)
                 break;
             R = cand;
-            if (cand == 16u)
-                break;
-            uint64_t tiles = 0;
+            rr_tiles = 0;
             for (size_t m = 0; m < n; ++m) {
                 const auto& j = *jobs[first + m];
-                tiles += (j.columns + cand - 1) / cand * ((j.rows + group_rows - 1) / group_rows);
+                rr_tiles += (j.columns + cand - 1) / cand * ((j.rows + group_rows - 1) / group_rows);
             }
-            if (tiles >= uint64_t(slots))
+            if (rr_tiles >= uint64_t(slots))
                 break;
         }
+        // Balanced split (64-row tiles, the same number of units per CTA)
+        // when whole tiles would leave more than a tenth of the CTA slots of
+        // their waves idle and every CTA gets enough units to pay for the
+        // fixup of its cut tiles.
+        const uint64_t waves = (rr_tiles + slots - 1) / uint64_t(slots);
+        const bool ragged = rr_tiles * 10 < waves * uint64_t(slots) * 9;
+        const bool balanced = fixup && fixup->ctas >= uint32_t(slots) && ragged
+                              && units64 >= uint64_t(kMinUnitsPerCta) * uint64_t(slots) && units64 < (1ull << 31);
+        if (balanced)
+            R = 64;
         MmaParams p;
         std::memset(&p, 0, sizeof(p));
         p.watchdog = watchdog_word();
         p.tile_rows = R;
-        uint32_t tiles = 0;
+        p.prefetch = tuning().prefetch;
+        uint32_t tiles = 0, units = 0;
         for (size_t m = 0; m < n; ++m) {
             const auto& j = *jobs[first + m];
             MmaJob& d = p.jobs[m];
@@ -617,7 +914,7 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             d.input = j.input;
             d.output = j.output;
             d.status = j.status;
-            d.stride = j.stride;
+            d.stride = uint32_t(j.stride);
             d.in = j.in;
             d.columns = j.columns;
             d.rows = j.rows;
@@ -625,11 +922,20 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             d.group_rows = group_rows;
             d.row_groups = (j.rows + group_rows - 1) / group_rows;
             d.first_tile = tiles;
-            tiles += (j.columns + R - 1) / R * d.row_groups;
+            d.first_unit = units;
+            const uint32_t job_tiles = (j.columns + R - 1) / R * d.row_groups;
+            tiles += job_tiles;
+            units += job_tiles * d.nblocks;
         }
         p.count = uint32_t(n);
         p.total_tiles = tiles;
-        const int s = nt == 1 ? launch_q4k<1>(p, uint32_t(slots), stream) : launch_q4k<2>(p, uint32_t(slots), stream);
+        uint32_t grid = std::min(tiles, uint32_t(slots));
+        if (balanced) {
+            grid = std::min(units, uint32_t(slots));
+            p.total_units = units;
+            p.partials = fixup->partials;
+        }
+        const int s = nt == 1 ? launch_q4k<1>(p, grid, stream) : launch_q4k<2>(p, grid, stream);
         if (s)
             return s;
     }

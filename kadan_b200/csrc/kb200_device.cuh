@@ -12,6 +12,7 @@ enum : unsigned {
     watchdog_full_barrier = 1u,
     watchdog_empty_barrier = 2u,
     watchdog_drain = 4u,
+    watchdog_fixup = 8u,  // a cut tile's other pieces never arrived
 };
 
 // Upper bound on polls of one mbarrier phase. mbarrier.try_wait suspends the
@@ -47,6 +48,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory"
+    );
+    return done != 0;
+}
+
+// Non-blocking check that phase `parity` completed (try_wait, in contrast,
+// suspends the thread for a hardware time slice before it gives up).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
         : "r"(smem_addr(bar)), "r"(parity)

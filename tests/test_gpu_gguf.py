@@ -204,3 +204,73 @@ def test_full_size_gate_projection_against_exact_dequant(kb, cuda):
     y3 = kb.gguf_gemv(kb.Q4_K, wd, (2.0 * x - x2).contiguous(), in_=in_, columns=out)
     torch.cuda.synchronize()
     assert rel_err(y3.cpu().numpy(), (2.0 * y - y2).cpu().numpy()) <= TOL
+
+
+def _dequant_product(kb, wd, x, in_, out):
+    """float64 product of the bit-exact dequantised weights (device)."""
+    import torch
+
+    dec = torch.empty(out * in_, dtype=torch.float32, device=x.device)
+    kb.gguf_dequant(kb.Q4_K, wd, out * in_, dec)
+    return (dec.view(out, in_).double() @ x.double().T).T
+
+
+@pytest.mark.parametrize("rows", [1, 3, 8])
+def test_q4k_balanced_split_ragged_batch_deterministic(kb, cuda, rows):
+    """One launch over Q4_K jobs of different widths and heights: the balanced
+    split cuts tiles at CTA boundaries (K = 56 super-blocks, 40-column tails,
+    a K = 4 job with fewer units than CTAs). Every output matches the exact
+    product, and three launches agree bit for bit (the cut tiles are summed in
+    a fixed order whatever piece finishes last; the counters re-arm)."""
+    import torch
+
+    from kadan_b200 import synth
+
+    shapes = [(4096, 6144), (14336, 4096), (4096, 40), (1024, 999), (2048, 64)]
+    gen = torch.Generator(device=cuda).manual_seed(7)
+    mats, jobs, outs, xs = [], [], [], []
+    for i, (in_, out) in enumerate(shapes):
+        wd = synth.device_gguf(kb.Q4_K, out, in_, seed=40 + i, device=cuda)
+        x = torch.randn(rows, in_, device=cuda, generator=gen).half().float()
+        y = torch.full((rows, out), float("nan"), device=cuda)
+        mats.append(wd), xs.append(x), outs.append(y)
+        jobs.append(kb.gemv_job(kb.Q4_K, wd, x, y, in_=in_, columns=out, rows=rows))
+    runs = []
+    for _ in range(3):
+        for y in outs:
+            y.fill_(float("nan"))
+        kb.gguf_gemv_batch(jobs)
+        torch.cuda.synchronize()
+        runs.append([y.cpu().numpy().copy() for y in outs])
+    for (in_, out), wd, x, got in zip(shapes, mats, xs, runs[0]):
+        want = _dequant_product(kb, wd, x, in_, out)
+        assert rel_err(got, want.cpu().numpy()) <= TOL, (in_, out)
+    for other in runs[1:]:
+        for a, b in zip(runs[0], other):
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert kb.take_device_error() == 0
+
+
+def test_q4k_streams_share_nothing(kb, cuda):
+    """Launches on two streams run concurrently, each with its own fixup
+    buffer: both results match a single-stream run bit for bit."""
+    import torch
+
+    from kadan_b200 import synth
+
+    in_, out = 14336, 4096
+    wd = synth.device_gguf(kb.Q4_K, out, in_, seed=61, device=cuda)
+    xa = torch.randn(1, in_, device=cuda, generator=torch.Generator(device=cuda).manual_seed(3))
+    xb = torch.randn(1, in_, device=cuda, generator=torch.Generator(device=cuda).manual_seed(4))
+    ref_a = kb.gguf_gemv(kb.Q4_K, wd, xa, in_=in_, columns=out)
+    ref_b = kb.gguf_gemv(kb.Q4_K, wd, xb, in_=in_, columns=out)
+    torch.cuda.synchronize()
+    s1, s2 = torch.cuda.Stream(cuda), torch.cuda.Stream(cuda)
+    ya, yb = torch.empty_like(ref_a), torch.empty_like(ref_b)
+    ja = kb.gemv_job(kb.Q4_K, wd, xa, ya, in_=in_, columns=out, rows=1)
+    jb = kb.gemv_job(kb.Q4_K, wd, xb, yb, in_=in_, columns=out, rows=1)
+    for _ in range(4):
+        kb.gguf_gemv_batch([ja], stream=s1)
+        kb.gguf_gemv_batch([jb], stream=s2)
+    torch.cuda.synchronize()
+    assert torch.equal(ya, ref_a) and torch.equal(yb, ref_b)
