@@ -42,6 +42,9 @@ GROUPS = [[("q", HIDDEN, HIDDEN), ("k", KV, HIDDEN), ("v", KV, HIDDEN)],
           [("down", HIDDEN, FFN)]]
 Q4K_BLOCK, Q4K_VALUES = 144, 256
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) of one [gate, up] launch, from an ncu capture of
+# that launch (the profile summary of gemv_q4k_mma_kernel holds the command).
+GATE_UP_TRAFFIC = 66961408  # 66,165,248 read + 796,160 written
 
 
 def weight_bytes(out: int, in_: int) -> int:
@@ -294,10 +297,12 @@ def run_ours(args, rank, world, local_rank):
         "hbm_frac": round(value / world / peak, 4),
         "gpu_launches": len(calls) * args.steps,
         "gpu_launches_note": "kernel launches of the timed graph replays (one per encoding per group)",
-        "roofline": {"bound": "hbm", "kernel": "gemv_staged_kernel<Q4K,1> (gate+up launch)",
+        "roofline": {"bound": "hbm", "kernel": "gemv_q4k_mma_kernel<1> ([gate, up] launch, balanced split)",
                      "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                     "traffic": None,
+                     "traffic": GATE_UP_TRAFFIC,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch "
+                                       "(one-pass capture, bench.py --steps 3 --warmup 3)",
                      "algorithmic_bytes_per_launch": gate_up_bytes},
         "e2e": e2e,
         "clocks": clock,

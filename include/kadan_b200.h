@@ -108,12 +108,17 @@ typedef struct kb200_gemv_job {
     int32_t encoding; /* kb200_encoding */
 } kb200_gemv_job;
 
-/* Every job of the batch, one launch per encoding, no device scratch: the job
- * table travels in the launch parameters. Replaces plan_matvec + launch_matvec +
+/* Every job of the batch, one launch per encoding: the job table travels in
+ * the launch parameters. Replaces plan_matvec + launch_matvec +
  * gguf_matvec_batch_kernel (h3_compute.cu:243-257, :325-382) and, for one job,
  * gguf_matvec_kernel (:238-240, :294-307). Rows above KB200_BATCH_ROWS are
  * processed as successive groups of rows, as append_row_groups does (:311-319).
- * jobs: host array. */
+ * jobs: host array. The Q4_K kernel splits large launches evenly over its
+ * CTAs and keeps, per (device, stream), a small device buffer for the tiles
+ * it cuts (allocated by the first call on the stream outside graph capture;
+ * inside capture without one it deals whole tiles instead). Launches on one
+ * stream share it in stream order; a graph captured on a stream must not be
+ * replayed concurrently with other work of that stream's Q4_K launches. */
 KB200_API int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream);
 
 /* Which kernel kb200_gguf_gemv_batch selects for a job: 2 = tensor-pipe Q4_K
@@ -264,7 +269,9 @@ KB200_API int kb200_moe_route(
 );
 
 /* Device-side watchdog word: nonzero when a bounded wait inside a kernel gave up
- * since the last call of this function, which also clears it. Synchronous. */
+ * since the last call of this function, which also clears it. Synchronous.
+ * Bits: 1 a stage never arrived, 2 a stage was never released, 4 the final
+ * copies never landed, 8 a cut tile's other pieces never arrived (Q4_K GEMV). */
 KB200_API int kb200_take_device_error(unsigned* value);
 
 #ifdef __cplusplus

@@ -107,6 +107,9 @@ int kb200_take_device_error(unsigned* value) {
         return cuda_fail(e, "kb200_take_device_error");
     if (value)
         *value = v;
+    // A launch that gave up may have left partial sums of cut tiles behind.
+    if (v)
+        clear_gemv_fixups();
     return v ? fail(KB200_TIMEOUT, "a bounded device wait gave up") : KB200_OK;
 }
 

@@ -760,14 +760,23 @@ struct Fixup {
 
 // The stream's fixup buffer, allocated (and zeroed on the stream) by the
 // first call outside graph capture; null when none can be had.
+struct FixupTable {
+    std::mutex lock;
+    std::map<std::pair<int, cudaStream_t>, Fixup> table;
+};
+
+FixupTable& fixups() {
+    static FixupTable t;
+    return t;
+}
+
 const Fixup* fixup_for(cudaStream_t stream) {
-    static std::mutex lock;
-    static std::map<std::pair<int, cudaStream_t>, Fixup> table;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess)
         return nullptr;
-    std::lock_guard<std::mutex> guard(lock);
-    Fixup& f = table[{dev, stream}];
+    FixupTable& t = fixups();
+    std::lock_guard<std::mutex> guard(t.lock);
+    Fixup& f = t.table[{dev, stream}];
     if (f.ctas)
         return &f;
     cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
@@ -823,6 +832,19 @@ template <int NT> int launch_q4k(const MmaParams& p, uint32_t grid, cudaStream_t
 }
 
 }  // namespace
+
+void clear_gemv_fixups() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return;
+    FixupTable& t = fixups();
+    std::lock_guard<std::mutex> guard(t.lock);
+    cudaDeviceSynchronize();
+    for (auto& [key, f] : t.table)
+        if (key.first == dev && f.ctas)
+            cudaMemset(f.partials, 0, size_t(f.ctas) * kSlotFloats * sizeof(unsigned long long));
+    cudaDeviceSynchronize();
+}
 
 bool q4k_mma_eligible(const kb200_gemv_job& j) {
     return j.encoding == KB200_Q4_K && aligned(j.weights, 16) && j.row_bytes % 16 == 0 && j.in % 256 == 0

@@ -33,4 +33,8 @@ unsigned* watchdog_word();
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 
+// Zero every fixup buffer of the Q4_K GEMV on the current device (after a
+// launch gave up, its cut tiles' partial words may be left behind). Synchronous.
+void clear_gemv_fixups();
+
 }  // namespace kb200
