@@ -488,10 +488,51 @@ def run_moe(args):
                       "weight_gbps": round(weight_bytes / (ms * 1e-3) / 1e9, 1)}), flush=True)
 
 
+def run_prefill(args):
+    """--case prefill: BASELINE config 2 prefill, the Llama-3-8B Q4_K stack at
+    T = --tokens input rows through kb200_gguf_gemm (one launch per matrix,
+    each with its activation-conversion kernel), 2*T*6.98 G FLOP per pass."""
+    import torch
+
+    import kadan_b200 as kb
+
+    dev = torch.device("cuda:0")
+    T = args.tokens
+    layers, _, _ = build_stack(torch, kb, dev)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    xs = {k: torch.randn(T, k, device=dev, generator=gen) for k in (HIDDEN, FFN)}
+    ys = {name: torch.empty(T, out, device=dev) for g in GROUPS for name, out, _ in g}
+    ws = torch.empty(kb.gemm_workspace_bytes(T, FFN), dtype=torch.uint8, device=dev)
+    jobs = [kb.gemv_job(kb.Q4_K, mats[name], xs[in_], ys[name], in_=in_, columns=out, rows=T)
+            for mats in layers for g in GROUPS for name, out, in_ in g]
+    stream = torch.cuda.current_stream()
+
+    def one_pass():
+        for job in jobs:
+            kb.gguf_gemm(job, ws, stream)
+
+    for _ in range(args.warmup):
+        one_pass()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, min(args.steps, 20))
+    a.record()
+    for _ in range(steps):
+        one_pass()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    flops = 2.0 * T * LAYERS * sum(o * i for g in GROUPS for _, o, i in g)
+    wbytes, _ = step_bytes()
+    print(json.dumps({"case": "prefill-config2", "tokens": T, "ms_per_pass": round(ms, 4),
+                      "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "weight_gbps": round(wbytes / (ms * 1e-3) / 1e9, 1),
+                      "launches_per_pass": 2 * len(jobs)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None, help="profiling case instead of the headline workload")
-    ap.add_argument("--tokens", type=int, default=4096, help="tokens for --case moe")
+    ap.add_argument("--tokens", type=int, default=4096, help="tokens for --case moe / prefill")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
@@ -506,6 +547,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.case == "moe":
         run_moe(args)
+    elif args.case == "prefill":
+        run_prefill(args)
     elif args.case:
         run_case(args)
     elif args.impl == "reference":

@@ -7,9 +7,8 @@
  * Every entry point takes plain pointers and sizes, returns a kb200_status,
  * throws nothing, and is asynchronous on the given CUDA stream unless it says
  * otherwise. Pointers marked "device" must address memory of the current
- * CUDA device. The C++ adapter kadan::b200::Compute (include/kadan/b200_compute.hpp)
- * maps these status codes back onto the reference's ProjectionResult /
- * std::runtime_error conventions.
+ * CUDA device. A DenseCompute subclass in the worker maps these status codes
+ * back onto the reference's ProjectionResult / std::runtime_error conventions.
  */
 #ifndef KADAN_B200_H
 #define KADAN_B200_H
@@ -125,6 +124,19 @@ KB200_API int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, vo
  * kernel (TMA tiles + mma.sync), 1 = bulk-copy staged CUDA-core kernel,
  * 0 = generic kernel (unaligned rows), -1 = unsupported. */
 KB200_API int kb200_gemv_path(const kb200_gemv_job* job);
+
+/* Prefill projection of many input rows on the tensor cores: the reference
+ * decodes the packed chunk to an fp32 tile in scratch and runs an FP32
+ * cublasSgemm (Compute::project, h3_compute.cu:1781-2480; decode :2201-2218,
+ * SGEMM :2435-2468). Here: Y[t, n] = sum_k decode(W[n, k]) * X[t, k] for all
+ * job.rows input rows in one pass over the weights, with fp16 operands (each
+ * input row scaled by a power of two first, undone exactly on output) and
+ * fp32 accumulation. Q4_K only (KB200_UNSUPPORTED otherwise); job.in a
+ * multiple of 256, 16-byte aligned weights and row_bytes. `workspace`: device,
+ * 256-byte aligned, at least kb200_gguf_gemm_workspace_bytes(rows, in).
+ * Asynchronous on `stream`. */
+KB200_API size_t kb200_gguf_gemm_workspace_bytes(uint32_t rows, uint32_t in);
+KB200_API int kb200_gguf_gemm(const kb200_gemv_job* job, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Host-span boundary. A context owns one device, one CUDA stream, a device

@@ -128,6 +128,9 @@ def _load() -> ctypes.CDLL:
     lib.kb200_gguf_dequant.argtypes = [c_int, vp, c_size, vp, vp, vp]
     lib.kb200_gguf_gemv_batch.argtypes = [ctypes.POINTER(GemvJob), c_size, vp]
     lib.kb200_gemv_path.argtypes = [ctypes.POINTER(GemvJob)]
+    lib.kb200_gguf_gemm_workspace_bytes.restype = c_size
+    lib.kb200_gguf_gemm_workspace_bytes.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
+    lib.kb200_gguf_gemm.argtypes = [ctypes.POINTER(GemvJob), vp, c_size, vp]
     lib.kb200_take_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint)]
     lib.kb200_context_create.argtypes = [c_int, ctypes.POINTER(vp)]
     lib.kb200_context_destroy.argtypes = [vp]
@@ -196,6 +199,16 @@ def gemv_job(encoding: int, weights, x, y, *, in_: int, columns: int, rows: int,
 def gguf_gemv_batch(jobs: Sequence[GemvJob], stream=None) -> None:
     arr = (GemvJob * len(jobs))(*jobs)
     check(lib.kb200_gguf_gemv_batch(arr, len(jobs), _stream_ptr(stream)))
+
+
+def gemm_workspace_bytes(rows: int, in_: int) -> int:
+    return int(lib.kb200_gguf_gemm_workspace_bytes(rows, in_))
+
+
+def gguf_gemm(job: GemvJob, workspace, stream=None) -> None:
+    """Prefill GEMM of one Q4_K job (all of job.rows at once) on the tensor cores."""
+    check(lib.kb200_gguf_gemm(ctypes.byref(job), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+                              _stream_ptr(stream)))
 
 
 def gemv_path(job: GemvJob) -> int:
