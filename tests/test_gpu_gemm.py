@@ -36,7 +36,7 @@ def run_gemm(kb, cuda, w_dev, x_dev, rows, in_, out, stride=None, y=None, status
 
 
 @pytest.mark.parametrize("rows,in_,out", [(9, 512, 37), (64, 1024, 200), (130, 512, 129), (257, 256, 64),
-                                          (16, 2048, 300)])
+                                          (16, 2048, 300), (300, 512, 12840)])
 def test_gemm_matches_oracle(kb, oracle, cuda, rows, in_, out):
     import torch
 
