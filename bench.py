@@ -485,7 +485,7 @@ def run_moe(args):
     flops = 2.0 * T * K * (2 * I * H + H * I)
     print(json.dumps({"case": "moe-config3", "tokens": T, "ms_per_layer": round(ms, 4),
                       "tokens_per_s": round(T / (ms * 1e-3), 1), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
-                      "weight_gbps": round(weight_bytes / (ms * 1e-3) / 1e9, 1)}), flush=True)
+                      "all_expert_weight_gbps": round(weight_bytes / (ms * 1e-3) / 1e9, 1)}), flush=True)
 
 
 def run_prefill(args):

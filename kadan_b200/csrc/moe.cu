@@ -20,9 +20,13 @@
 //           dequant warps turn each 128x64 code tile into fp16 with
 //           cvt.rn.f16x2.e2m1x2 and the block scale (exact for scale bytes
 //           104..140), straight into the 128-byte-swizzled operand layout.
+//           With at most 8 token rows per expert on average (decode sizes)
+//           the two GEMMs are replaced by a grouped GEMV (moe_gemv_kernel)
+//           that streams only the routed experts' weights.
 //   combine out[t] = sum_i w[t,i] * Y[pos(t,i)] in selection order (fp32)
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -584,6 +588,165 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
         tmem_dealloc(tmem, 256);
 }
 
+// ----------------------------------------------------------- grouped GEMV
+// Decode-sized batches (a few tokens per expert): the layer is a weight
+// stream. Items are (expert, 16 weight rows), dealt round-robin over the CTAs
+// and skipped for experts without tokens; the four warps of a CTA split the
+// item's K range and add their partial sums through shared memory. Rows are
+// multiplied by the expert's tokens 8 at a time with mma.m16n8k16 (fp16
+// operands, fp32 accumulation). Lane (g, t) loads, per 128 columns, MXFP4
+// block t of its rows g and g+8 (16 contiguous code bytes each) and the 32
+// matching activations of token g; inside each MMA the k order is the same
+// permutation on both operands (slot pair 2t,2t+1 of MMA m <- block values
+// 4m, 4m+1; pair 2t+8,2t+9 <- 4m+2, 4m+3), so no data crosses lanes. For
+// gate/up the item's MMA rows are gate rows of 8 outputs (rows 0-7) and the
+// matching up rows (8-15), so each lane finishes its outputs in registers.
+// Weights decode exactly as in the GEMM (cvt.rn.f16x2.e2m1x2 times the
+// power-of-two block scale).
+constexpr int kGemvWarps = 4;
+
+struct GemvParams {
+    const uint8_t* blocks;  // [E, Nrows, K/2]
+    const uint8_t* scales;  // [E, Nrows, K/32]
+    const float* bias;      // [E, Nrows] or null
+    const __half* x;        // [n, K], expert-sorted rows
+    const int* offsets;     // [E + 1]
+    void* out;              // epilogue 0: fp16 act [n, out_cols]; 1: fp32 y [n, out_cols]
+    int K, Nrows, E, chunks, epilogue, split, out_cols, act_kind;
+    float limit, alpha;
+    unsigned* status;
+};
+
+__device__ __forceinline__ void hmma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1)
+    );
+}
+
+// Weight row of MMA row i (0..15) of item chunk c. Gate/up: rows 0-7 are the
+// gate rows of outputs 8c..8c+7, rows 8-15 the matching up rows.
+__device__ __forceinline__ int gemv_row(const GemvParams& p, int c, int i) {
+    if (p.epilogue == 0) {
+        const int j = 8 * c + (i & 7);
+        const bool up = i >= 8;
+        return p.split ? (up ? p.Nrows / 2 + j : j) : 2 * j + (up ? 1 : 0);
+    }
+    return 16 * c + i;
+}
+
+__global__ void __launch_bounds__(32 * kGemvWarps) moe_gemv_kernel(const __grid_constant__ GemvParams p) {
+    __shared__ float4 part[kGemvWarps][32];  // each lane's four accumulators, per warp
+    __shared__ int off[kMaxExperts + 1];     // expert row offsets: the skip test costs no global load
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int blocks_per_row = p.K / 32, iters = (p.K + 127) / 128;
+    for (int i = threadIdx.x; i <= p.E; i += blockDim.x)
+        off[i] = p.offsets[i];
+    __syncthreads();
+    bool scale_ok = true;
+    for (int item = blockIdx.x; item < p.E * p.chunks; item += gridDim.x) {
+        const int e = item / p.chunks, c = item % p.chunks;
+        const int p0 = off[e], count = off[e + 1] - p0;
+        if (count == 0)
+            continue;
+        const int r0 = gemv_row(p, c, g), r1 = gemv_row(p, c, g + 8);
+        const uint8_t* code0 = p.blocks + (size_t(e) * p.Nrows + r0) * (p.K / 2);
+        const uint8_t* code1 = p.blocks + (size_t(e) * p.Nrows + r1) * (p.K / 2);
+        const uint8_t* sc0 = p.scales + (size_t(e) * p.Nrows + r0) * blocks_per_row;
+        const uint8_t* sc1 = p.scales + (size_t(e) * p.Nrows + r1) * blocks_per_row;
+        for (int q = 0; q < count; q += 8) {
+            const int tok = min(q + g, count - 1);  // B column g: token q+g (clamped; unused columns ignored)
+            const __half* xr = p.x + size_t(p0 + tok) * p.K;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            // One step's operands (this lane's block of rows r0/r1 and the
+            // token's 32 activations); steps it = warp, warp + 4, ... of this
+            // warp, each loaded a step ahead of its MMAs.
+            struct Step {
+                uint4 w0, w1, x0, x1, x2, x3;
+                uint32_t s0, s1;  // E8M0 scale bytes (decoded at MMA time, so no load is waited on early)
+                bool live;
+            };
+            auto load = [&](int it, Step& st) {
+                const int k0 = 128 * it + 32 * t;  // first column of this lane's block
+                // Past K (K % 128 == 64 leaves lanes t = 2, 3 without a block
+                // in the last step): zeros, since every lane takes part in the MMAs.
+                const bool live = it < iters && k0 < p.K;
+                const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+                st.w0 = live ? __ldg(reinterpret_cast<const uint4*>(code0 + k0 / 2)) : zero;
+                st.w1 = live ? __ldg(reinterpret_cast<const uint4*>(code1 + k0 / 2)) : zero;
+                st.live = live;
+                st.s0 = live ? uint32_t(sc0[k0 / 32]) : 127u;
+                st.s1 = live ? uint32_t(sc1[k0 / 32]) : 127u;
+                const uint4* xq = reinterpret_cast<const uint4*>(xr + (live ? k0 : 0));
+                st.x0 = live ? __ldg(xq) : zero, st.x1 = live ? __ldg(xq + 1) : zero;
+                st.x2 = live ? __ldg(xq + 2) : zero, st.x3 = live ? __ldg(xq + 3) : zero;
+            };
+            auto mma = [&](const Step& st) {
+                bool ok0, ok1;
+                const uint32_t s0 = e8m0_half2(st.s0, ok0), s1 = e8m0_half2(st.s1, ok1);
+                scale_ok = scale_ok && ((ok0 && ok1) || !st.live);
+                const uint32_t cw0[4] = {st.w0.x, st.w0.y, st.w0.z, st.w0.w}, cw1[4] = {st.w1.x, st.w1.y, st.w1.z, st.w1.w};
+                const uint32_t xw[16] = {st.x0.x, st.x0.y, st.x0.z, st.x0.w, st.x1.x, st.x1.y, st.x1.z, st.x1.w,
+                                         st.x2.x, st.x2.y, st.x2.z, st.x2.w, st.x3.x, st.x3.y, st.x3.z, st.x3.w};
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    // Code bytes 2m, 2m+1 of the block: values 4m..4m+3.
+                    const uint32_t wa = cw0[m >> 1] >> (16 * (m & 1)), wb = cw1[m >> 1] >> (16 * (m & 1));
+                    const uint32_t a0 = hmul2_bits(e2m1x2_to_half2(wa & 0xFFu), s0);
+                    const uint32_t a2 = hmul2_bits(e2m1x2_to_half2((wa >> 8) & 0xFFu), s0);
+                    const uint32_t a1 = hmul2_bits(e2m1x2_to_half2(wb & 0xFFu), s1);
+                    const uint32_t a3 = hmul2_bits(e2m1x2_to_half2((wb >> 8) & 0xFFu), s1);
+                    hmma16816(acc, a0, a1, a2, a3, xw[2 * m], xw[2 * m + 1]);
+                }
+            };
+            Step cur, nxt;
+            load(warp, cur);
+            for (int it = warp; it < iters; it += 2 * kGemvWarps) {
+                load(it + kGemvWarps, nxt);
+                mma(cur);
+                load(it + 2 * kGemvWarps, cur);
+                if (it + kGemvWarps < iters)
+                    mma(nxt);
+            }
+            // Sum the warps' K ranges (fixed order), then warp 0 finishes.
+            part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            __syncthreads();
+            if (warp == 0) {
+                float4 sum = part[0][lane];
+                for (int w = 1; w < kGemvWarps; ++w) {
+                    const float4 o = part[w][lane];
+                    sum.x += o.x, sum.y += o.y, sum.z += o.z, sum.w += o.w;
+                }
+                // sum: (row r0: tokens q+2t, q+2t+1), (row r1: same tokens)
+                const float b0 = p.bias ? p.bias[size_t(e) * p.Nrows + r0] : 0.f;
+                const float b1 = p.bias ? p.bias[size_t(e) * p.Nrows + r1] : 0.f;
+                const float v0[2] = {sum.x + b0, sum.y + b0}, v1[2] = {sum.z + b1, sum.w + b1};
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int tl = q + 2 * t + h;
+                    if (tl >= count)
+                        continue;
+                    if (p.epilogue == 1) {
+                        auto* y = static_cast<float*>(p.out);
+                        y[size_t(p0 + tl) * p.out_cols + r0] = v0[h];
+                        y[size_t(p0 + tl) * p.out_cols + r1] = v1[h];
+                    } else {
+                        // r0 is the gate row, r1 the up row of output 8c + g.
+                        auto* act = static_cast<__half*>(p.out);
+                        act[size_t(p0 + tl) * p.out_cols + 8 * c + g] =
+                            __float2half_rn(act_fn(v0[h], v1[h], p.act_kind, p.limit, p.alpha));
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (!scale_ok && p.status)
+        atomicOr(p.status, 2u);
+}
+
 // ------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -793,6 +956,50 @@ int kb200_moe_forward(const kb200_moe_weights* w, const uint16_t* x_bf16, const 
         return cuda_fail(e, "MoE routing launches");
     const int mtiles_max = int((n + BM - 1) / BM) + E;
 
+    // Decode-sized batches (at most 8 token rows per expert on average) are a
+    // weight stream: the grouped GEMV reads each routed expert once per 8 of
+    // its rows. KB200_MOE_PATH=gemm|gemv overrides the choice.
+    bool gemv = n <= size_t(8) * size_t(E);
+    if (const char* path = std::getenv("KB200_MOE_PATH"))
+        gemv = std::strcmp(path, "gemv") == 0 ? true : std::strcmp(path, "gemm") == 0 ? false : gemv;
+    if (gemv) {
+        const int grid_cap = sm_count() * 8;
+        GemvParams v;
+        std::memset(&v, 0, sizeof(v));
+        v.blocks = w->gate_up_blocks;
+        v.scales = w->gate_up_scales;
+        v.bias = w->gate_up_bias;
+        v.x = ws.xs;
+        v.offsets = ws.offsets;
+        v.out = ws.act;
+        v.K = H;
+        v.Nrows = 2 * I;
+        v.E = E;
+        v.chunks = I / 8;
+        v.epilogue = 0;
+        v.split = w->interleaved ? 0 : 1;
+        v.out_cols = I;
+        v.act_kind = w->activation;
+        v.limit = w->limit;
+        v.alpha = w->alpha;
+        v.status = status;
+        moe_gemv_kernel<<<std::min(E * v.chunks, grid_cap), 32 * kGemvWarps, 0, stream>>>(v);
+        v.blocks = w->down_blocks;
+        v.scales = w->down_scales;
+        v.bias = w->down_bias;
+        v.x = ws.act;
+        v.out = ws.y;
+        v.K = I;
+        v.Nrows = H;
+        v.chunks = H / 16;
+        v.epilogue = 1;
+        v.split = 0;
+        v.out_cols = H;
+        moe_gemv_kernel<<<std::min(E * v.chunks, grid_cap), 32 * kGemvWarps, 0, stream>>>(v);
+        if ((e = cudaGetLastError()) != cudaSuccess)
+            return cuda_fail(e, "moe_gemv_kernel launch");
+    } else {
+
     // gate/up: [n, H] x [2I, H]^T per expert, activation in the epilogue.
     GroupParams g1;
     std::memset(&g1, 0, sizeof(g1));
@@ -846,6 +1053,7 @@ int kb200_moe_forward(const kb200_moe_weights* w, const uint16_t* x_bf16, const 
     g2.status = status;
     if (const int s = launch_gemm(g2, mtiles_max * g2.n_tiles, stream))
         return s;
+    }
 
     {
         const size_t work = tokens * size_t(H / 4);

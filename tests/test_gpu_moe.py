@@ -134,3 +134,28 @@ def test_moe_config3_full_batch_vs_torch_fp32(kb, oracle, cuda):
         ref.index_add_(0, tok, wt[:, None] * y)
     torch.cuda.synchronize()
     assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) <= 1e-3
+
+
+@pytest.mark.parametrize("T,E,H,I,K,interleaved,bias", [(3, 8, 256, 128, 2, True, True), (4, 32, 2880, 2880, 4, False, False),
+                                                       (37, 16, 512, 192, 4, False, True)])
+def test_moe_gemv_and_gemm_paths_agree(kb, oracle, cuda, monkeypatch, T, E, H, I, K, interleaved, bias):
+    """The decode-size grouped GEMV and the tcgen05 grouped GEMM compute the
+    same layer: both within 1e-3 of the oracle with fp16 activation rounding,
+    and within 1e-3 of each other."""
+    import torch
+
+    w, dev, host = layer(kb, cuda, E=E, H=H, I=I, K=K, seed=T + E, interleaved=interleaved, bias=bias)
+    x, logits, xb, ld = inputs(cuda, T, H, E, seed=T + 3)
+    outs = {}
+    for path in ("gemv", "gemm"):
+        monkeypatch.setenv("KB200_MOE_PATH", path)
+        status = torch.zeros(1, dtype=torch.int32, device=cuda)
+        outs[path] = kb.moe_forward(w, xb, ld, status=status)
+        torch.cuda.synchronize()
+        assert status.item() == 0
+    args = dict(hidden=H, inter=I, experts=E, top_k=K, gu_bias=host["gu_b"], dn_bias=host["dn_b"], activation=0,
+                interleaved=int(interleaved))
+    ref16 = oracle.moe_forward(x, logits, host["gu_w"], host["gu_s"], host["dn_w"], host["dn_s"], round_act=2, **args)
+    for path in ("gemv", "gemm"):
+        assert rel_err(outs[path].cpu().numpy(), ref16) <= 1e-3, path
+    assert rel_err(outs["gemv"].cpu().numpy(), outs["gemm"].cpu().numpy()) <= 1e-3
