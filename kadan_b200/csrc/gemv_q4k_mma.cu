@@ -10,14 +10,14 @@
 //   A operand  :  low nibbles  q      = packed & 0x0F0F0F0F  (u8, 0..15)
 //                 high nibbles 16*q   = packed & 0xF0F0F0F0  (u8, 0..240)
 //   B operand  :  the activations of one super-block, quantised to two int8
-//                 levels, x ~= s*(h + l/256) with s = absmax/127 per 256
+//                 levels, x ~= s*(h + l/254) with s = absmax/127 per 256
 //                 values and token (about 15 bits); h and l sit in adjacent
 //                 N columns, 4 input rows x {h, l} = 8 columns per MMA
 //   MMA        :  mma.m16n8k32.u8.s8 -> exact int32 sum over one sub-block
 //   scales     :  I = sum_g (16 sc_g) C_g(low) + sc_g C_g(high)   (IMAD)
 //   min term   :  sum_g m_g * sum_{k in g} x_k, one fp16 m16n8k8 MMA per block
 //                 (m exact, the fp32 group sums split into fp16 hi + lo)
-//   epilogue   :  acc += (d*s/16) * (I_h + I_l/256) - (256 dmin) * C_min
+//   epilogue   :  acc += (d*s/16) * (I_h + I_l/254) - (256 dmin) * C_min
 //
 // CTA = 4 consumer warps + 1 producer lane. A tile is R weight rows (R = 64,
 // 32 or 16) for one group of input rows; with R < 64 the warps split K (2 or 4
@@ -307,9 +307,28 @@ __device__ __forceinline__ uint32_t pack_half2(__half2 h) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Round-to-nearest-even integer of |v| < 2^22 through the 1.5*2^23 bias.
-__device__ __forceinline__ int round_int(float v) {
-    return __float_as_int(v + 12582912.f) - 0x4B400000;
+// 1.5 * 2^23: for |y| < 2^22, the low mantissa bits of y + kMagic hold
+// round-to-nearest-even(y) as a two's-complement integer.
+constexpr float kMagic = 12582912.f;
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
+    return *reinterpret_cast<float2*>(&d);
+}
+
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+    return add2(a, make_float2(-b.x, -b.y));
+}
+
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
+    return *reinterpret_cast<float2*>(&d);
 }
 
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
@@ -381,20 +400,29 @@ __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, 
                 break;
             const int blk = item / rows, tok = item % rows;
             const float inv = m[q] > 0.f ? 127.f / m[q] : 0.f;
-            int h[8], l[8];
+            // Pairs of values at a time: y = v/s, r1 = y + M (M = 1.5 * 2^23,
+            // so r1's low bits are round(y) as an integer), d = y - round(y)
+            // in [-1/2, 1/2] (exact), r2 = d * 254 + M (low bits round(254 d),
+            // within [-127, 127]). The int8 codes are the low bytes of r1, r2.
+            const float2 inv2 = make_float2(inv, inv), magic = make_float2(kMagic, kMagic);
+            const float2 neg_magic = make_float2(-kMagic, -kMagic), k254 = make_float2(254.f, 254.f);
+            uint32_t h[8], l[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float y = v[q][i] * inv;
-                h[i] = round_int(y);
-                l[i] = max(-127, min(127, round_int((y - float(h[i])) * 256.f)));
+            for (int i = 0; i < 8; i += 2) {
+                const float2 y = mul2(make_float2(v[q][i], v[q][i + 1]), inv2);
+                const float2 r1 = add2(y, magic);
+                const float2 d = sub2(y, add2(r1, neg_magic));
+                const float2 r2 = fma2(d, k254, magic);
+                h[i] = __float_as_uint(r1.x), h[i + 1] = __float_as_uint(r1.y);
+                l[i] = __float_as_uint(r2.x), l[i + 1] = __float_as_uint(r2.y);
             }
             const int slot = blk * rows + tok;
             uint32_t* dst = frag + slot * (kTokenBlockBytes / 4);
             const int idx = (((G >> 1) * 4 + t) * 2) * 4 + (G & 1) * 2;  // part h; part l is +4
-            dst[idx] = pack4(h[0], h[1], h[2], h[3]);
-            dst[idx + 1] = pack4(h[4], h[5], h[6], h[7]);
-            dst[idx + 4] = pack4(l[0], l[1], l[2], l[3]);
-            dst[idx + 5] = pack4(l[4], l[5], l[6], l[7]);
+            dst[idx] = pack4(int(h[0]), int(h[1]), int(h[2]), int(h[3]));
+            dst[idx + 1] = pack4(int(h[4]), int(h[5]), int(h[6]), int(h[7]));
+            dst[idx + 4] = pack4(int(l[0]), int(l[1]), int(l[2]), int(l[3]));
+            dst[idx + 5] = pack4(int(l[4]), int(l[5]), int(l[6]), int(l[7]));
             // Minimum term B' for lane (g, t') = sums of sub-blocks 2t', 2t'+1
             // (scaled by 1/256) split into fp16 hi and lo: written by lanes 8t'.
             if ((lane & 7) == 0) {
@@ -605,9 +633,9 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
                         const int tokc = min(nt * 4 + t, rows - 1);
                         const float sc = scales[sblk * rows + tokc] * (1.f / 16.f);
                         const float kg = dg * sc, k8 = d8 * sc;
-                        acc[nt][0] = fmaf(kg, fmaf(float(I[nt][0][1]), 1.f / 256.f, float(I[nt][0][0])), acc[nt][0]);
+                        acc[nt][0] = fmaf(kg, fmaf(float(I[nt][0][1]), 1.f / 254.f, float(I[nt][0][0])), acc[nt][0]);
                         acc[nt][0] = fmaf(-mg256, Cm[0] + Cm[1], acc[nt][0]);
-                        acc[nt][1] = fmaf(k8, fmaf(float(I[nt][1][1]), 1.f / 256.f, float(I[nt][1][0])), acc[nt][1]);
+                        acc[nt][1] = fmaf(k8, fmaf(float(I[nt][1][1]), 1.f / 254.f, float(I[nt][1][0])), acc[nt][1]);
                         acc[nt][1] = fmaf(-m8256, Cm[2] + Cm[3], acc[nt][1]);
                     }
                 }
@@ -802,6 +830,8 @@ const Fixup* fixup_for(cudaStream_t stream) {
 struct Tuning {
     bool balanced = true;  // KB200_GEMV_BALANCED=0: whole tiles round-robin
     uint32_t prefetch = 0; // KB200_GEMV_L2_PREFETCH=<stages>
+    uint32_t min_units = kMinUnitsPerCta;  // KB200_GEMV_MIN_UNITS=<units per CTA>
+    int ctas_per_sm = 0;                   // KB200_GEMV_CTAS_PER_SM=<n>: grid slots per SM (0: all that fit)
 };
 
 const Tuning& tuning() {
@@ -809,6 +839,10 @@ const Tuning& tuning() {
         Tuning v;
         if (const char* s = std::getenv("KB200_GEMV_BALANCED"))
             v.balanced = std::atoi(s) != 0;
+        if (const char* s = std::getenv("KB200_GEMV_CTAS_PER_SM"))
+            v.ctas_per_sm = std::max(0, std::atoi(s));
+        if (const char* s = std::getenv("KB200_GEMV_MIN_UNITS"))
+            v.min_units = uint32_t(std::max(1, std::atoi(s)));
         if (const char* s = std::getenv("KB200_GEMV_L2_PREFETCH"))
             v.prefetch = uint32_t(std::max(0, std::min(64, std::atoi(s))));
         return v;
@@ -861,9 +895,11 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         max_rows = std::max(max_rows, int(std::min(j->rows, uint32_t(KB200_BATCH_ROWS))));
     const int nt = max_rows <= 4 ? 1 : 2;
     const uint32_t group_rows = uint32_t(4 * nt);
-    const int slots = nt == 1 ? kernel_slots<1>() : kernel_slots<2>();
+    int slots = nt == 1 ? kernel_slots<1>() : kernel_slots<2>();
     if (slots <= 0)
         return -slots;
+    if (tuning().ctas_per_sm > 0)
+        slots = std::min(slots, sm_count() * tuning().ctas_per_sm);
     const Fixup* fixup = tuning().balanced ? fixup_for(stream) : nullptr;
     for (size_t first = 0; first < jobs.size(); first += kMaxJobsQ) {
         const size_t n = std::min(jobs.size() - first, size_t(kMaxJobsQ));
@@ -901,7 +937,7 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         const uint64_t waves = (rr_tiles + slots - 1) / uint64_t(slots);
         const bool ragged = rr_tiles * 10 < waves * uint64_t(slots) * 9;
         const bool balanced = fixup && fixup->ctas >= uint32_t(slots) && ragged
-                              && units64 >= uint64_t(kMinUnitsPerCta) * uint64_t(slots) && units64 < (1ull << 31);
+                              && units64 >= uint64_t(tuning().min_units) * uint64_t(slots) && units64 < (1ull << 31);
         if (balanced)
             R = 64;
         MmaParams p;
