@@ -503,9 +503,17 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
     }
 
     // ------------------------------ consumers ------------------------------
-    // Activations (and the outputs this grid writes) may belong to the
-    // previous kernel of the stream.
-    grid_dependency_wait();
+    // Activations, outputs and the fixup words may belong to the previous
+    // kernel of the stream: the grid-dependency wait comes right before the
+    // first of those accesses, so walking the job table (constant-cache misses
+    // at kernel start) overlaps the previous kernel's tail.
+    bool dependency_met = false;
+    auto await_dependency = [&] {
+        if (!dependency_met) {
+            grid_dependency_wait();
+            dependency_met = true;
+        }
+    };
     const int g = lane >> 2, t = lane & 3;
     const int rg = warp / KS, ks = warp % KS;  // row group and K split of this warp
     uint32_t it = 0;
@@ -544,6 +552,7 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
                 // The window covers this stage and the rest of the piece, as
                 // far as the segment buffer reaches.
                 const int count = min(seg.blocks, int(pc.k1) - blk_first);
+                await_dependency();
                 // Every warp is done with the previous segment before it is replaced.
                 named_sync(1, kConsumerThreads);
                 prep_segment(smem, seg, x, job.in, blk_first, count);
@@ -666,6 +675,7 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
             }
             named_sync(1, kConsumerThreads);
         }
+        await_dependency();
         bool write = ks == 0;
         if (!pc.whole && pc.k0 > 0) {
             // Head piece of a cut tile (R = 64, every warp holds final sums):
