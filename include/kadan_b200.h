@@ -139,6 +139,28 @@ KB200_API size_t kb200_gguf_gemm_workspace_bytes(uint32_t rows, uint32_t in);
 KB200_API int kb200_gguf_gemm(const kb200_gemv_job* job, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Multi-device column partition (host only). The reference splits every
+ * projection's output columns across devices in proportion to their weight
+ * capacity and chunks each device's slice as a single projection on that
+ * device would (weight_boundary, IW/include/kadan/device_placement.hpp:341-357;
+ * gguf_batch_partition, IW/include/kadan/gguf_batch_partition.hpp:44-83, with
+ * the plans of device_placement.hpp:76-142); these return the same geometry.
+ * encoding: kb200_encoding, KB200_F32 for fp32 rows. Failures are the
+ * reference's std::invalid_argument cases (KB200_INVALID with its message). */
+typedef struct kb200_partition {
+    size_t first, count, chunk_columns;
+} kb200_partition;
+
+KB200_API size_t kb200_weight_boundary(size_t units, const uint64_t* capacities, size_t devices, size_t index);
+KB200_API int kb200_gguf_batch_partition(size_t in, size_t out, int encoding, const uint64_t* capacities,
+                                         size_t devices, size_t device, uint64_t scratch_limit,
+                                         kb200_partition* result);
+/* output[r*out + first + c] = local[r*count + c] for r < rows, c < count
+ * (GgufBatchPartition::scatter, gguf_batch_partition.hpp:53-66). */
+KB200_API void kb200_partition_scatter(const kb200_partition* partition, const float* local, size_t rows,
+                                       float* output, size_t out);
+
+/* ---------------------------------------------------------------------------
  * Host-span boundary. A context owns one device, one CUDA stream, a device
  * workspace and pinned staging that grow on demand; calls on one context must
  * not overlap (the reference serialises DenseCompute with a mutex,

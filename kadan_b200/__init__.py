@@ -131,6 +131,12 @@ def _load() -> ctypes.CDLL:
     lib.kb200_gguf_gemm_workspace_bytes.restype = c_size
     lib.kb200_gguf_gemm_workspace_bytes.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
     lib.kb200_gguf_gemm.argtypes = [ctypes.POINTER(GemvJob), vp, c_size, vp]
+    lib.kb200_weight_boundary.restype = c_size
+    lib.kb200_weight_boundary.argtypes = [c_size, ctypes.POINTER(ctypes.c_uint64), c_size, c_size]
+    lib.kb200_gguf_batch_partition.argtypes = [c_size, c_size, c_int, ctypes.POINTER(ctypes.c_uint64), c_size,
+                                               c_size, ctypes.c_uint64, vp]
+    lib.kb200_partition_scatter.restype = None
+    lib.kb200_partition_scatter.argtypes = [vp, vp, c_size, vp, c_size]
     lib.kb200_take_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint)]
     lib.kb200_context_create.argtypes = [c_int, ctypes.POINTER(vp)]
     lib.kb200_context_destroy.argtypes = [vp]
@@ -209,6 +215,29 @@ def gguf_gemm(job: GemvJob, workspace, stream=None) -> None:
     """Prefill GEMM of one Q4_K job (all of job.rows at once) on the tensor cores."""
     check(lib.kb200_gguf_gemm(ctypes.byref(job), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
                               _stream_ptr(stream)))
+
+
+class Partition(ctypes.Structure):
+    _fields_ = [("first", ctypes.c_size_t), ("count", ctypes.c_size_t), ("chunk_columns", ctypes.c_size_t)]
+
+
+def weight_boundary(units: int, capacities, index: int) -> int:
+    caps = (ctypes.c_uint64 * max(1, len(capacities)))(*capacities)
+    return int(lib.kb200_weight_boundary(units, caps, len(capacities), index))
+
+
+def gguf_batch_partition(in_: int, out: int, encoding: int, capacities, device: int, scratch_limit: int) -> Partition:
+    """Column slice and chunk width of device `device` (the worker's multi-device split)."""
+    caps = (ctypes.c_uint64 * max(1, len(capacities)))(*capacities)
+    p = Partition()
+    check(lib.kb200_gguf_batch_partition(in_, out, encoding, caps, len(capacities), device, scratch_limit,
+                                         ctypes.byref(p)))
+    return p
+
+
+def partition_scatter(p: Partition, local, rows: int, output, out: int) -> None:
+    """Host fp32 arrays (numpy): output[r, first + c] = local[r, c]."""
+    lib.kb200_partition_scatter(ctypes.byref(p), local.ctypes.data, rows, output.ctypes.data, out)
 
 
 def gemv_path(job: GemvJob) -> int:

@@ -168,10 +168,28 @@ class Reference:
                                          ctypes.c_size_t, _f32p, ctypes.c_size_t]
         L.ref_cpu_matvec_parallel.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, _f32p,
                                               ctypes.c_size_t, ctypes.c_int]
+        L.ref_weight_boundary.restype = ctypes.c_size_t
+        L.ref_weight_boundary.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t,
+                                          ctypes.c_size_t]
+        L.ref_gguf_batch_partition.argtypes = [ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int,
+                                               ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.c_size_t,
+                                               ctypes.c_uint64, ctypes.POINTER(ctypes.c_size_t)]
         self.L = L
 
     def error(self) -> str:
         return self.L.ref_last_error().decode(errors="replace")
+
+    def weight_boundary(self, units: int, capacities, index: int) -> int:
+        caps = (ctypes.c_uint64 * max(1, len(capacities)))(*capacities)
+        return int(self.L.ref_weight_boundary(units, caps, len(capacities), index))
+
+    def gguf_batch_partition(self, in_: int, out: int, encoding: int, capacities, device: int, scratch_limit: int):
+        """(first, count, chunk_columns), or the reference's exception text."""
+        caps = (ctypes.c_uint64 * max(1, len(capacities)))(*capacities)
+        res = (ctypes.c_size_t * 3)()
+        if self.L.ref_gguf_batch_partition(in_, out, encoding, caps, len(capacities), device, scratch_limit, res):
+            return self.error()
+        return tuple(int(v) for v in res)
 
     def decode(self, e: int, packed: np.ndarray, count: int) -> np.ndarray:
         packed = np.ascontiguousarray(packed, dtype=np.uint8)

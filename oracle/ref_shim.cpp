@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "cpu_matvec.hpp"
+#include "kadan/gguf_batch_partition.hpp"
 #include "kadan/gguf_quantization.hpp"
 #include "kadan/quantization.hpp"
 #include <ggml-cpu.h>
@@ -241,4 +242,24 @@ int ref_cpu_matvec_parallel(
         t.join();
     return status.load();
 }
+
+// Column partition (IW/include/kadan/gguf_batch_partition.hpp, device_placement.hpp).
+size_t ref_weight_boundary(size_t units, const uint64_t* capacities, size_t devices, size_t index) {
+    return kadan::weight_boundary(units, std::span<const kadan::Bytes>(capacities, devices), index);
 }
+
+int ref_gguf_batch_partition(size_t in, size_t out, int encoding, const uint64_t* capacities, size_t devices,
+                             size_t device, uint64_t scratch_limit, size_t* result) {
+    try {
+        std::optional<kadan::gguf::Encoding> enc;
+        if (encoding >= 0)
+            enc = static_cast<kadan::gguf::Encoding>(encoding);
+        const auto p = kadan::gguf_batch_partition(in, out, enc, std::span<const kadan::Bytes>(capacities, devices),
+                                                   device, scratch_limit);
+        result[0] = p.first, result[1] = p.count, result[2] = p.chunk_columns;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+}  // extern "C"

@@ -1,0 +1,69 @@
+"""Multi-device column partition (host only) against the reference's own code.
+
+The reference's kadan::gguf_batch_partition / weight_boundary
+(IW/include/kadan/gguf_batch_partition.hpp:44-83, device_placement.hpp:76-142,
+:341-357) are compiled from its headers into oracle/_ref; the library must
+return the same geometry and fail in the same cases. The sweep follows the
+reference's own test (IW/tests/gguf_batch_partition.cpp:102-187) and adds
+larger capacities, widths and scratch limits.
+"""
+from __future__ import annotations
+
+import itertools
+
+import numpy as np
+import pytest
+
+ENCODINGS = [-1, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9]  # F32 rows, then kadan::gguf::Encoding
+CAPACITIES = [[7], [1, 1], [1, 3], [0, 1, 0], [0, 0, 0], [183_359 << 20] * 8,
+              [80 << 30, 80 << 30, 40 << 30], [1, 2, 3, 4, 5, 6, 7, 8]]
+
+
+def test_weight_boundary_matches_reference(kb, ref):
+    for caps in CAPACITIES:
+        for units in (0, 1, 19, 100, 10003, 28672, 1 << 20, (1 << 40) + 7):
+            for index in range(len(caps) + 2):
+                assert kb.weight_boundary(units, caps, index) == ref.weight_boundary(units, caps, index)
+    # The reference's worked values (IW/tests/worker_compute.cpp:699-704).
+    assert kb.weight_boundary(100, [1, 3], 1) == 25 and kb.weight_boundary(100, [3, 1], 1) == 75
+    assert kb.weight_boundary(100, [0, 0], 1) == 50 and kb.weight_boundary(100, [1, 3], 2) == 100
+
+
+@pytest.mark.parametrize("caps", CAPACITIES)
+def test_batch_partition_matches_reference(kb, ref, caps):
+    limits = [64 << 20, 1 << 30, (16 << 20) + 300, (8 << 20) + 5000, 17 << 20]
+    for in_, out, enc, limit in itertools.product([256, 4096, 14336], [1, 19, 10003, 28672], ENCODINGS, limits):
+        for device in range(len(caps)):
+            want = ref.gguf_batch_partition(in_, out, enc, caps, device, limit)
+            if isinstance(want, str):
+                with pytest.raises(kb.KadanError) as err:
+                    kb.gguf_batch_partition(in_, out, enc, caps, device, limit)
+                assert str(err.value).endswith(": " + want), (in_, out, enc, limit, caps, device)
+                continue
+            got = kb.gguf_batch_partition(in_, out, enc, caps, device, limit)
+            assert (got.first, got.count, got.chunk_columns) == want, (in_, out, enc, limit, caps, device)
+
+
+@pytest.mark.parametrize("caps", CAPACITIES[:5])
+def test_partition_covers_every_column_once_and_scatters(kb, caps):
+    """Slices are contiguous, in device order, cover [0, out) exactly once, and
+    scatter puts each device's local rows back in place (the reference test's
+    ownership and scatter checks)."""
+    for rows, out in itertools.product([1, 8], [1, 19, 10003]):
+        output = np.full((rows, out), -1.0, dtype=np.float32)
+        owners = np.zeros(out, dtype=np.int64)
+        previous = 0
+        for device in range(len(caps)):
+            p = kb.gguf_batch_partition(256, out, 1, caps, device, 64 << 20)
+            assert p.first == previous == kb.weight_boundary(out, caps, device)
+            previous += p.count
+            if not p.count:
+                assert p.chunk_columns == 0
+                continue
+            owners[p.first:p.first + p.count] += 1
+            local = np.array([[r * out + p.first + c for c in range(p.count)] for r in range(rows)],
+                             dtype=np.float32)
+            kb.partition_scatter(p, np.ascontiguousarray(local), rows, output, out)
+        assert previous == out
+        assert np.all(owners == 1)
+        assert np.array_equal(output.ravel(), np.arange(rows * out, dtype=np.float32))
