@@ -529,6 +529,106 @@ def run_prefill(args):
                       "launches_per_pass": 2 * len(jobs)}), flush=True)
 
 
+def run_tp(args, rank, world, local_rank):
+    """--case tp70b: BASELINE config 4, the Llama-3-70B mixed Q6_K/Q4_K decode
+    stack (80 layers, 46.46 GB of weights), tensor-parallel over the ranks of
+    torchrun: q/k/v (by heads) and gate/up split by output columns, o and
+    down split along K with an NCCL all-reduce of the partial sums (two per
+    layer). --tokens T rows per step (1..32). A step is captured in one CUDA
+    graph (GEMV launches and collectives). value = the whole stack's weight
+    and activation bytes per step / step time (max over ranks): total work
+    is fixed as N grows (strong scaling)."""
+    import datetime
+
+    import torch
+
+    import kadan_b200 as kb
+    from kadan_b200 import tensor_parallel as tp
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    tokens = args.tokens if args.tokens <= 32 else 1
+    layers = args.layers or 80
+    groups = tp.llama3_70b_projections()
+    weights = tp.synth_shards(groups, layers, world, rank, device)
+    stack = tp.DecodeStack(groups, weights, tokens, world, rank, device, group=group)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        stack.launch(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        stack.launch(stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = min(args.steps, 200)
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    ar_us = None
+    if dist:
+        # The collective alone (same sizes, same count per step), for the
+        # breakdown; not part of the value.
+        t = torch.zeros(tokens, 8192, device=device)
+        for _ in range(20):
+            dist.all_reduce(t)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(400):
+            dist.all_reduce(t)
+        b.record()
+        torch.cuda.synchronize()
+        ar_us = a.elapsed_time(b) / 400 * 1e3
+        m = torch.tensor([ms], device=device)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    wbytes = tp.full_weight_bytes(groups, layers)
+    local_bytes = stack.weight_bytes()
+    abytes = layers * tokens * 4 * sum(g[0].in_ + sum(p.out for p in g) for g in groups)
+    clock = clocks.summary()
+    peak, peak_kind = peaks()
+    graph = None
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank:
+        return
+    value = (wbytes + abytes) / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": METRIC, "case": "tp70b", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "strong", "dtype": "q6_k/q4_k weights, bf16-valued fp32 activations, fp32 accumulation",
+        "data": "synthetic (seeded shards drawn on each device)",
+        "config": {"workload": f"BASELINE config 4 decode: Llama-3-70B Q6_K/Q4_K, {layers} layers, T={tokens}",
+                   "weight_bytes_per_step": wbytes, "weight_bytes_per_rank": local_bytes,
+                   "parallelism": f"tp{world}", "collective": "NCCL all-reduce (fp32) after o and down",
+                   "l2": "inputs larger than L2"},
+        "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / peak, 4), "peak_gbs": peak,
+        "peak_source": f"{peak_kind} hbm_gbs",
+        "allreduce_us_alone": None if ar_us is None else round(ar_us, 2),
+        "allreduces_per_step": 2 * layers if world > 1 else 0,
+        "gpu_launches": steps * len(stack.calls), "clocks": clock}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None, help="profiling case instead of the headline workload")
@@ -539,6 +639,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="layers for --case tp70b (default 80)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -549,6 +650,8 @@ def main():
         run_moe(args)
     elif args.case == "prefill":
         run_prefill(args)
+    elif args.case == "tp70b":
+        run_tp(args, rank, world, local_rank)
     elif args.case:
         run_case(args)
     elif args.impl == "reference":

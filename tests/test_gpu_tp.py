@@ -1,0 +1,147 @@
+"""Tensor-parallel decode on the GPU against the oracle's full projections.
+
+One rank (always) and two NCCL ranks (when the machine shows two GPUs): a
+two-layer stack with the Llama-3-70B block structure at reduced width
+(hidden 1024, 8 q / 2 kv heads of 128, ffn 3584; Q6_K attention and down,
+Q4_K gate/up). Every rank checks its outputs — its column slice of q/k/v and
+gate/up, the all-reduced o and down — against the fp64 product of the oracle's
+decode of the full matrices, within 1e-3 (max|y - ref| / max(max|ref|, 1)),
+after an eager step and after a CUDA-graph replay of the step.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+TOKENS = 3
+
+
+def small_groups():
+    from kadan_b200 import Q4_K, Q6_K
+    from kadan_b200.tensor_parallel import Projection
+
+    h, kv, ffn, head = 1024, 256, 3584, 128
+    return [[Projection("q", Q6_K, h, h, "column", head), Projection("k", Q6_K, kv, h, "column", head),
+             Projection("v", Q6_K, kv, h, "column", head)],
+            [Projection("o", Q6_K, h, h, "row")],
+            [Projection("gate", Q4_K, ffn, h, "column"), Projection("up", Q4_K, ffn, h, "column")],
+            [Projection("down", Q6_K, h, ffn, "row")]]
+
+
+def run_rank(rank: int, world: int, port: int) -> dict:
+    import torch
+
+    from kadan_b200 import synth
+    from kadan_b200 import tensor_parallel as tp
+    from oracle.pyoracle import Oracle
+
+    device = torch.device("cuda", rank)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
+                                timeout=datetime.timedelta(seconds=60))
+    try:
+        groups = small_groups()
+        orc = Oracle()
+        layers, full, weights = 2, [], []
+        for layer in range(layers):
+            mats, local = {}, {}
+            for gi, g in enumerate(groups):
+                for i, p in enumerate(g):
+                    mats[p.name] = synth.gguf(p.encoding, p.out, p.in_, seed=100 * layer + 10 * gi + i)
+                    local[p.name] = torch.from_numpy(tp.shard_packed(p, mats[p.name], world, rank)).to(device)
+            full.append(mats)
+            weights.append(local)
+        xs = {g[0].name: synth.activations(TOKENS * g[0].in_, seed=7 + gi, dtype="bf16").reshape(TOKENS, g[0].in_)
+              for gi, g in enumerate(groups)}
+        stack = tp.DecodeStack(groups, weights, TOKENS, world, rank, device,
+                               inputs={k: torch.from_numpy(v).to(device) for k, v in xs.items()})
+        # The stack writes each projection's output once per layer; the last
+        # layer's values remain.
+        want = {}
+        for g in groups:
+            for p in g:
+                w = orc.decode(p.encoding, full[-1][p.name], p.out * p.in_).reshape(p.out, p.in_)
+                y = xs[g[0].name].astype(np.float64) @ w.astype(np.float64).T
+                s = tp.shard(p, world, rank)
+                want[p.name] = y[:, s.out_first:s.out_first + s.out_count]
+        errs = {}
+        stream = torch.cuda.Stream(device)
+        with torch.cuda.stream(stream):
+            stack.launch(stream)
+        torch.cuda.synchronize()
+        for name, y in want.items():
+            errs[f"eager/{name}"] = _rel(stack.outputs[name].cpu().numpy(), y)
+        for t in stack.outputs.values():
+            t.fill_(float("nan"))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            stack.launch(stream)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        torch.cuda.synchronize()
+        for name, y in want.items():
+            errs[f"graph/{name}"] = _rel(stack.outputs[name].cpu().numpy(), y)
+        graph = None
+        return errs
+    finally:
+        if dist:
+            dist.destroy_process_group()
+
+
+def _rel(got, want) -> float:
+    if not np.isfinite(got).all():
+        return float("inf")
+    return float(np.max(np.abs(got - want)) / max(1.0, float(np.max(np.abs(want)))))
+
+
+def _child(rank, world, port, results):
+    results[rank] = run_rank(rank, world, port)
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_tp_one_rank_matches_oracle(cuda):
+    errs = run_rank(0, 1, 0)
+    bad = {k: v for k, v in errs.items() if not v < TOL}
+    assert not bad, bad
+
+
+def test_tp_two_ranks_match_oracle(cuda):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("two GPUs needed")
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        results = manager.dict()
+        port = _port()
+        procs = [ctx.Process(target=_child, args=(r, 2, port, results)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+        codes = [p.exitcode for p in procs]
+        for p in procs:
+            if p.exitcode is None:
+                p.kill()
+        assert codes == [0, 0], codes
+        for r in range(2):
+            bad = {k: v for k, v in results[r].items() if not v < TOL}
+            assert not bad, (r, bad)
