@@ -629,6 +629,92 @@ def run_tp(args, rank, world, local_rank):
         "gpu_launches": steps * len(stack.calls), "clocks": clock}), flush=True)
 
 
+def run_ep(args, rank, world, local_rank):
+    """--case ep120b: BASELINE config 5, the gpt-oss-120b MoE stack (36
+    layers, H=I=2880, 128 experts, top-4, SwiGLU clamp 7, MXFP4 experts)
+    with 8192 bf16 tokens per step, expert-parallel over the torchrun ranks:
+    each rank holds 128/N experts of every layer and routes 8192/N of the
+    tokens; rows travel to their expert's rank and back with NCCL
+    all-to-alls. value = 8192 tokens / step time (max over ranks); total
+    work fixed as N grows (strong scaling)."""
+    import datetime
+
+    import torch
+
+    import kadan_b200 as kb
+    from kadan_b200 import expert_parallel as ep
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    E, H, I, K, T = 128, 2880, 2880, 4, 8192
+    layers = args.layers or 36
+    tokens = T // world
+    first, end = ep.expert_range(E, world, rank)
+    el = end - first
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    stack = []
+    for _ in range(layers):
+        gu_w = torch.randint(0, 256, (el, 2 * I, H // 2), dtype=torch.uint8, device=device, generator=gen)
+        gu_s = torch.randint(118, 127, (el, 2 * I, H // 32), dtype=torch.uint8, device=device, generator=gen)
+        dn_w = torch.randint(0, 256, (el, H, I // 2), dtype=torch.uint8, device=device, generator=gen)
+        dn_s = torch.randint(118, 127, (el, H, I // 32), dtype=torch.uint8, device=device, generator=gen)
+        w = kb.moe_weights(gu_w, gu_s, dn_w, dn_s, hidden=H, inter=I, experts=el, top_k=K)
+        stack.append((ep.ExpertParallelMoE(w, E, world, rank), (gu_w, gu_s, dn_w, dn_s)))
+    tgen = torch.Generator(device=device).manual_seed(7 + rank)
+    x = torch.randn(tokens, H, device=device, generator=tgen).to(torch.bfloat16)
+    logits = [torch.randn(tokens, E, device=device, generator=tgen) for _ in range(layers)]
+    out = torch.empty(tokens, H, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def step():
+        for (layer, _), lg in zip(stack, logits):
+            layer.forward(x, lg, out=out, status=status)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    steps = max(1, min(args.steps, 10))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if dist:
+        m = torch.tensor([ms], device=device)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+        dist.barrier()
+        dist.destroy_process_group()
+    clock = clocks.summary()
+    if rank:
+        return
+    flops = 2.0 * T * K * (2 * I * H + H * I) * layers
+    tflops = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": METRIC, "case": "ep120b", "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong",
+        "dtype": "mxfp4 weights, fp16 tensor-core operands, fp32 accumulation",
+        "data": "synthetic (MXFP4 codes uniform, E8M0 118..126, bf16 N(0,1) tokens, N(0,1) logits)",
+        "config": {"workload": f"BASELINE config 5: gpt-oss-120b MoE, {layers} layers, E=128, top-4, "
+                               f"{T} tokens per step", "parallelism": f"ep{world}",
+                   "tokens_per_rank": tokens, "experts_per_rank": el,
+                   "collective": "NCCL all-to-all (counts, fp16 rows out, fp32 rows back)"},
+        "tflops": round(tflops, 1), "tflops_per_gpu": round(tflops / world, 1),
+        "status": int(status.item()) if world == 1 else None, "clocks": clock}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None, help="profiling case instead of the headline workload")
@@ -639,7 +725,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--layers", type=int, default=0, help="layers for --case tp70b (default 80)")
+    ap.add_argument("--layers", type=int, default=0, help="layers for --case tp70b / ep120b (default 80 / 36)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -652,6 +738,8 @@ def main():
         run_prefill(args)
     elif args.case == "tp70b":
         run_tp(args, rank, world, local_rank)
+    elif args.case == "ep120b":
+        run_ep(args, rank, world, local_rank)
     elif args.case:
         run_case(args)
     elif args.impl == "reference":

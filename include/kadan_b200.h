@@ -290,6 +290,59 @@ KB200_API int kb200_moe_forward_noalloc(
     void* stream
 );
 
+/* ---------------------------------------------------------------------------
+ * The MoE layer in stages, for expert parallelism: experts split over the
+ * ranks of a node, tokens sent to the rank that holds their expert and back
+ * (an all-to-all each way, issued by the caller between the stages).
+ * kb200_moe_forward == dispatch_rows -> experts -> combine on one device.
+ *
+ * Dispatch: route each token (the steps of MoeLayer::forward,
+ * qwen_layers.cpp:397-431), sort the tokens * top_k (token, choice) slots
+ * stably by expert and gather their rows as fp16 into expert-major order.
+ * The result points into `workspace` (at least
+ * kb200_moe_dispatch_workspace_bytes): rows of expert e are
+ * [offsets[e], offsets[e+1]); pos[t * top_k + i] is the row of choice i of
+ * token t; weight the renormalised routing weights. Experts are contiguous
+ * per rank, so rank r's rows are one contiguous range. */
+typedef struct kb200_moe_dispatch {
+    int32_t* offsets; /* device [experts + 1] */
+    int32_t* pos;     /* device [tokens * top_k] */
+    float* weight;    /* device [tokens * top_k] */
+    uint16_t* rows;   /* device fp16 [tokens * top_k, hidden] */
+    size_t count;     /* tokens * top_k */
+} kb200_moe_dispatch;
+
+KB200_API size_t kb200_moe_dispatch_workspace_bytes(size_t tokens, int32_t hidden, int32_t experts, int32_t top_k);
+KB200_API int kb200_moe_dispatch_rows(
+    const float* logits, const uint16_t* x_bf16, size_t tokens, int32_t hidden, int32_t experts, int32_t top_k,
+    void* workspace, size_t workspace_bytes, kb200_moe_dispatch* result, unsigned* status, void* stream
+);
+
+/* Expert stage: y[r] = down_e(act(gate_up_e(rows[r]))) for rows grouped by
+ * expert, offsets device [w->experts + 1] (w describes the experts this
+ * device holds; its top_k is not used). rows fp16 [rows, hidden], y fp32
+ * [rows, hidden], workspace at least kb200_moe_experts_workspace_bytes. */
+KB200_API size_t kb200_moe_experts_workspace_bytes(const kb200_moe_weights* w, size_t rows);
+KB200_API int kb200_moe_experts(
+    const kb200_moe_weights* w, const uint16_t* rows_f16, const int32_t* offsets, size_t rows, float* y,
+    void* workspace, size_t workspace_bytes, unsigned* status, void* stream
+);
+
+/* Combine: out[t] = sum_i weight[t, i] * y[pos[t, i]] in selection order
+ * (qwen_layers.cpp:466-491), fp32. */
+KB200_API int kb200_moe_combine(
+    const float* y, const float* weight, const int32_t* pos, size_t tokens, int32_t top_k, int32_t hidden,
+    float* out, void* stream
+);
+
+/* Row permutation by segments: dst rows [d, d+n) = src rows [s, s+n) for
+ * each {s, d, n} of `segments` (device int64 [count][3]); row_bytes a
+ * multiple of 16; max_rows the longest segment (sizes the grid). Used to
+ * regroup rows received from each rank (source-major) into expert-major
+ * order and back. */
+KB200_API int kb200_rows_regroup(const void* src, void* dst, size_t row_bytes, const int64_t* segments, size_t count,
+                                 size_t max_rows, void* stream);
+
 /* The routing stage alone (for tests): chosen [tokens, top_k] int32,
  * weight [tokens, top_k] fp32, device. */
 KB200_API int kb200_moe_route(

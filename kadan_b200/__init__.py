@@ -364,6 +364,56 @@ def moe_forward_noalloc(w: MoeWeights, x_bf16, logits, out=None, status=None, st
     return out
 
 
+class MoeDispatch(ctypes.Structure):
+    """kb200_moe_dispatch: device pointers into the dispatch workspace."""
+
+    _fields_ = [("offsets", ctypes.c_void_p), ("pos", ctypes.c_void_p), ("weight", ctypes.c_void_p),
+                ("rows", ctypes.c_void_p), ("count", ctypes.c_size_t)]
+
+
+lib.kb200_moe_dispatch_workspace_bytes.restype = ctypes.c_size_t
+lib.kb200_moe_dispatch_workspace_bytes.argtypes = [ctypes.c_size_t, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
+lib.kb200_moe_dispatch_rows.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t,
+                                        ctypes.POINTER(MoeDispatch), ctypes.c_void_p, ctypes.c_void_p]
+lib.kb200_moe_experts_workspace_bytes.restype = ctypes.c_size_t
+lib.kb200_moe_experts_workspace_bytes.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_size_t]
+lib.kb200_moe_experts.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
+lib.kb200_moe_combine.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32,
+                                  ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+lib.kb200_rows_regroup.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                   ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p]
+
+
+def moe_dispatch_rows(logits, x_bf16, top_k: int, workspace, status=None, stream=None) -> MoeDispatch:
+    """Route, sort by expert and gather fp16 rows (kb200_moe_dispatch_rows)."""
+    tokens, experts = logits.shape
+    d = MoeDispatch()
+    check(lib.kb200_moe_dispatch_rows(_ptr(logits), _ptr(x_bf16), tokens, x_bf16.shape[1], experts, top_k,
+                                      _ptr(workspace), workspace.numel(), ctypes.byref(d), _ptr(status),
+                                      _stream_ptr(stream)))
+    return d
+
+
+def moe_experts(w: MoeWeights, rows_f16, offsets, y, workspace, status=None, stream=None) -> None:
+    """y[r] = expert FFN of rows grouped by expert (kb200_moe_experts)."""
+    check(lib.kb200_moe_experts(ctypes.byref(w), _ptr(rows_f16), _ptr(offsets), rows_f16.shape[0], _ptr(y),
+                                _ptr(workspace), workspace.numel(), _ptr(status), _stream_ptr(stream)))
+
+
+def moe_combine(y, weight_ptr: int, pos_ptr: int, tokens: int, top_k: int, out, stream=None) -> None:
+    check(lib.kb200_moe_combine(_ptr(y), weight_ptr, pos_ptr, tokens, top_k, out.shape[1], _ptr(out),
+                                _stream_ptr(stream)))
+
+
+def rows_regroup(src, dst, segments, max_rows: int, stream=None) -> None:
+    """dst rows [d, d+n) = src rows [s, s+n) per segment row {s, d, n} (device int64 [count, 3])."""
+    row_bytes = src.shape[1] * src.element_size()
+    check(lib.kb200_rows_regroup(_ptr(src), _ptr(dst), row_bytes, _ptr(segments), segments.shape[0], max_rows,
+                                 _stream_ptr(stream)))
+
+
 lib.kb200_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
 STATIC_MOE_SCRATCH_BYTES = 16 << 20

@@ -787,8 +787,10 @@ struct Workspace {
     size_t bytes;
 };
 
-Workspace carve(void* base, const kb200_moe_weights& w, size_t tokens) {
-    const size_t n = tokens * size_t(w.top_k), E = size_t(w.experts);
+// Workspace of the whole layer for `tokens` tokens. The dispatch stage uses
+// the part up to xs (carve with inter = 0 and no y for it alone).
+Workspace carve_shape(void* base, size_t tokens, size_t hidden, size_t inter, size_t experts, size_t top_k, bool y) {
+    const size_t n = tokens * top_k, E = experts;
     auto* b = static_cast<uint8_t*>(base);
     size_t at = 0;
     auto take = [&](size_t bytes) {
@@ -804,22 +806,56 @@ Workspace carve(void* base, const kb200_moe_weights& w, size_t tokens) {
     ws.perm = reinterpret_cast<int*>(take(n * 4));
     ws.pos = reinterpret_cast<int*>(take(n * 4));
     ws.mtile = reinterpret_cast<int*>(take((E + 1) * 4));
-    ws.xs = reinterpret_cast<__half*>(take(n * size_t(w.hidden) * 2));
-    ws.act = reinterpret_cast<__half*>(take(n * size_t(w.inter) * 2));
-    ws.y = reinterpret_cast<float*>(take(n * size_t(w.hidden) * 4));
+    ws.xs = reinterpret_cast<__half*>(take(n * hidden * 2));
+    ws.act = inter ? reinterpret_cast<__half*>(take(n * inter * 2)) : nullptr;
+    ws.y = y ? reinterpret_cast<float*>(take(n * hidden * 4)) : nullptr;
     ws.bytes = at;
     return ws;
 }
 
-int check_weights(const kb200_moe_weights* w) {
+Workspace carve(void* base, const kb200_moe_weights& w, size_t tokens) {
+    return carve_shape(base, tokens, size_t(w.hidden), size_t(w.inter), size_t(w.experts), size_t(w.top_k), true);
+}
+
+// Workspace of the expert stage alone over `rows` grouped rows: the m-tile
+// prefix and the fp16 activations between the two GEMMs.
+struct ExpertWs {
+    int* mtile;
+    __half* act;
+    size_t bytes;
+};
+
+ExpertWs carve_experts(void* base, const kb200_moe_weights& w, size_t rows) {
+    auto* b = static_cast<uint8_t*>(base);
+    ExpertWs ws;
+    ws.mtile = reinterpret_cast<int*>(b);
+    const size_t act_at = align_up(size_t(w.experts + 1) * 4, 256);
+    ws.act = b ? reinterpret_cast<__half*>(b + act_at) : nullptr;
+    ws.bytes = act_at + align_up(rows * size_t(w.inter) * 2, 256);
+    return ws;
+}
+
+int check_shape(int hidden, int experts, int top_k) {
+    if (hidden <= 0 || experts <= 0 || top_k <= 0)
+        return fail(KB200_INVALID, "MoE shape must be positive");
+    if (hidden % 64 || hidden > kMaxK)
+        return fail(KB200_UNSUPPORTED, "hidden and inter must be multiples of 64, at most 4096");
+    if (experts > kMaxExperts || top_k > std::min(experts, kMaxTopK))
+        return fail(KB200_UNSUPPORTED, "at most 256 experts and top_k <= min(experts, 32)");
+    return KB200_OK;
+}
+
+// routed: the weights route tokens themselves (top_k is checked); the
+// expert stage alone ignores top_k (a rank may hold fewer experts than k).
+int check_weights(const kb200_moe_weights* w, bool routed = true) {
     if (!w)
         return fail(KB200_INVALID, "null MoE weights");
-    if (w->hidden <= 0 || w->inter <= 0 || w->experts <= 0 || w->top_k <= 0)
+    if (const int s = check_shape(w->hidden, w->experts, routed ? w->top_k : 1))
+        return s;
+    if (w->inter <= 0)
         return fail(KB200_INVALID, "MoE shape must be positive");
-    if (w->hidden % 64 || w->inter % 64 || w->hidden > kMaxK || w->inter > kMaxK)
+    if (w->inter % 64 || w->inter > kMaxK)
         return fail(KB200_UNSUPPORTED, "hidden and inter must be multiples of 64, at most 4096");
-    if (w->experts > kMaxExperts || w->top_k > std::min(w->experts, kMaxTopK))
-        return fail(KB200_UNSUPPORTED, "at most 256 experts and top_k <= min(experts, 32)");
     if (!w->gate_up_blocks || !w->gate_up_scales || !w->down_blocks || !w->down_scales)
         return fail(KB200_INVALID, "null MoE weight pointer");
     if (!aligned(w->gate_up_blocks, 16) || !aligned(w->down_blocks, 16) || !aligned(w->gate_up_scales, 16)
@@ -897,6 +933,173 @@ int static_scratch(void** ptr) {
 }  // namespace
 }  // namespace kb200
 
+namespace kb200 {
+namespace {
+
+// m-tile prefix of caller-grouped rows: mtile[e] = sum over e' < e of
+// ceil(rows(e') / 128).
+__global__ void moe_mtile_kernel(const int* offsets, int E, int* mtile) {
+    if (threadIdx.x || blockIdx.x)
+        return;
+    int tiles = 0;
+    for (int e = 0; e < E; ++e) {
+        mtile[e] = tiles;
+        tiles += (offsets[e + 1] - offsets[e] + 127) / 128;
+    }
+    mtile[E] = tiles;
+}
+
+// dst rows [d, d + n) = src rows [s, s + n) for each segment {s, d, n}
+// (blockIdx.y); 16-byte words, grid-stride over the segment.
+__global__ void rows_regroup_kernel(const uint4* src, uint4* dst, size_t row_words, const long long* seg) {
+    const long long s = seg[3 * blockIdx.y], d = seg[3 * blockIdx.y + 1], n = seg[3 * blockIdx.y + 2];
+    const size_t words = size_t(n) * row_words;
+    const uint4* from = src + size_t(s) * row_words;
+    uint4* to = dst + size_t(d) * row_words;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < words; i += size_t(gridDim.x) * blockDim.x)
+        to[i] = from[i];
+}
+
+// Routing, stable sort by expert and the gather of the sorted fp16 rows.
+int dispatch_launch(const float* logits, const uint16_t* x_bf16, size_t tokens, int H, int E, int K,
+                    const Workspace& ws, unsigned* status, cudaStream_t stream) {
+    const size_t n = tokens * size_t(K);
+    cudaError_t e = cudaMemsetAsync(ws.counts, 0, size_t(E) * 4, stream);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "counts memset");
+    moe_route_kernel<<<int((tokens * 32 + 255) / 256), 256, 0, stream>>>(logits, int(tokens), E, K, ws.chosen, ws.weight,
+                                                                          ws.counts);
+    moe_sort_kernel<<<1, 1024, 0, stream>>>(ws.chosen, int(n), E, ws.counts, ws.offsets, ws.perm, ws.pos, ws.mtile);
+    const size_t work = n * size_t(H / 8);
+    const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
+    moe_gather_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x_bf16), ws.perm, int(n), K, H,
+                                                  ws.xs, status);
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return cuda_fail(e, "MoE routing launches");
+    return KB200_OK;
+}
+
+// The expert stage over n rows grouped by expert (offsets[E + 1], mtile[E + 1]
+// on the device): gate/up with the activation, then down into y (fp32 [n, H]).
+int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offsets, const int* mtile, size_t n,
+                   __half* act, float* y, unsigned* status, cudaStream_t stream) {
+    if (!encoder())
+        return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const int H = w->hidden, I = w->inter, E = w->experts;
+    cudaError_t e;
+    const int mtiles_max = int((n + BM - 1) / BM) + E;
+
+    // Decode-sized batches (at most 8 token rows per expert on average) are a
+    // weight stream: the grouped GEMV reads each routed expert once per 8 of
+    // its rows. KB200_MOE_PATH=gemm|gemv overrides the choice.
+    bool gemv = n <= size_t(8) * size_t(E);
+    if (const char* path = std::getenv("KB200_MOE_PATH"))
+        gemv = std::strcmp(path, "gemv") == 0 ? true : std::strcmp(path, "gemm") == 0 ? false : gemv;
+    if (gemv) {
+        const int grid_cap = sm_count() * 8;
+        GemvParams v;
+        std::memset(&v, 0, sizeof(v));
+        v.blocks = w->gate_up_blocks;
+        v.scales = w->gate_up_scales;
+        v.bias = w->gate_up_bias;
+        v.x = xs;
+        v.offsets = offsets;
+        v.out = act;
+        v.K = H;
+        v.Nrows = 2 * I;
+        v.E = E;
+        v.chunks = I / 8;
+        v.epilogue = 0;
+        v.split = w->interleaved ? 0 : 1;
+        v.out_cols = I;
+        v.act_kind = w->activation;
+        v.limit = w->limit;
+        v.alpha = w->alpha;
+        v.status = status;
+        moe_gemv_kernel<<<std::min(E * v.chunks, grid_cap), 32 * kGemvWarps, 0, stream>>>(v);
+        v.blocks = w->down_blocks;
+        v.scales = w->down_scales;
+        v.bias = w->down_bias;
+        v.x = act;
+        v.out = y;
+        v.K = I;
+        v.Nrows = H;
+        v.chunks = H / 16;
+        v.epilogue = 1;
+        v.split = 0;
+        v.out_cols = H;
+        moe_gemv_kernel<<<std::min(E * v.chunks, grid_cap), 32 * kGemvWarps, 0, stream>>>(v);
+        if ((e = cudaGetLastError()) != cudaSuccess)
+            return cuda_fail(e, "moe_gemv_kernel launch");
+        return KB200_OK;
+    }
+
+    // gate/up: [n, H] x [2I, H]^T per expert, activation in the epilogue.
+    GroupParams g1;
+    std::memset(&g1, 0, sizeof(g1));
+    const bool split = !w->interleaved;
+    if (!encode_2d(&g1.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xs, uint64_t(H), n, BK, BM,
+                   CU_TENSOR_MAP_SWIZZLE_128B)
+        || !encode_2d(&g1.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->gate_up_blocks, uint64_t(H / 2),
+                      uint64_t(E) * 2 * I, BK / 2, split ? BN / 2 : BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(KB200_INVALID, "tensor map encoding (gate/up)");
+    g1.scales = w->gate_up_scales;
+    g1.bias = w->gate_up_bias;
+    g1.offsets = offsets;
+    g1.mtile_prefix = mtile;
+    g1.out = act;
+    g1.K = H;
+    g1.Nrows = 2 * I;
+    g1.E = E;
+    g1.n_tiles = split ? I / (BN / 2) : 2 * I / BN;
+    g1.split = split ? 1 : 0;
+    g1.epilogue = 0;
+    g1.out_cols = I;
+    g1.act_kind = w->activation;
+    g1.limit = w->limit;
+    g1.alpha = w->alpha;
+    g1.status = status;
+    if ((2 * I) % BN && !split)
+        return fail(KB200_UNSUPPORTED, "interleaved gate/up needs 2*inter to be a multiple of 128");
+    if (const int s = launch_gemm(g1, mtiles_max * g1.n_tiles, stream))
+        return s;
+
+    // down: [n, I] x [H, I]^T per expert -> fp32 rows.
+    GroupParams g2;
+    std::memset(&g2, 0, sizeof(g2));
+    if (!encode_2d(&g2.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, act, uint64_t(I), n, BK, BM,
+                   CU_TENSOR_MAP_SWIZZLE_128B)
+        || !encode_2d(&g2.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->down_blocks, uint64_t(I / 2), uint64_t(E) * H,
+                      BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(KB200_INVALID, "tensor map encoding (down)");
+    g2.scales = w->down_scales;
+    g2.bias = w->down_bias;
+    g2.offsets = offsets;
+    g2.mtile_prefix = mtile;
+    g2.out = y;
+    g2.K = I;
+    g2.Nrows = H;
+    g2.E = E;
+    g2.n_tiles = (H + BN - 1) / BN;
+    g2.split = 0;
+    g2.epilogue = 1;
+    g2.out_cols = H;
+    g2.status = status;
+    return launch_gemm(g2, mtiles_max * g2.n_tiles, stream);
+}
+
+int combine_launch(const float* y, const float* weight, const int* pos, size_t tokens, int K, int H, float* out,
+                   cudaStream_t stream) {
+    const size_t work = tokens * size_t(H / 4);
+    const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
+    moe_combine_kernel<<<blocks, 256, 0, stream>>>(y, weight, pos, int(tokens), K, H, out);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_combine_kernel launch");
+}
+
+}  // namespace
+}  // namespace kb200
+
 extern "C" {
 
 size_t kb200_moe_workspace_bytes(const kb200_moe_weights* w, size_t tokens) {
@@ -938,130 +1141,108 @@ int kb200_moe_forward(const kb200_moe_weights* w, const uint16_t* x_bf16, const 
         return fail(KB200_NO_MEMORY, "MoE workspace too small (see kb200_moe_workspace_bytes)");
     if (!encoder())
         return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
-    const int H = w->hidden, I = w->inter, E = w->experts, K = w->top_k;
     auto stream = static_cast<cudaStream_t>(stream_ptr);
-    cudaError_t e = cudaMemsetAsync(ws.counts, 0, size_t(E) * 4, stream);
+    if (const int s = dispatch_launch(logits, x_bf16, tokens, w->hidden, w->experts, w->top_k, ws, status, stream))
+        return s;
+    if (const int s = experts_launch(w, ws.xs, ws.offsets, ws.mtile, n, ws.act, ws.y, status, stream))
+        return s;
+    return combine_launch(ws.y, ws.weight, ws.pos, tokens, w->top_k, w->hidden, out, stream);
+}
+
+size_t kb200_moe_dispatch_workspace_bytes(size_t tokens, int32_t hidden, int32_t experts, int32_t top_k) {
+    if (check_shape(hidden, experts, top_k) != KB200_OK)
+        return 0;
+    return carve_shape(nullptr, tokens, size_t(hidden), 0, size_t(experts), size_t(top_k), false).bytes;
+}
+
+int kb200_moe_dispatch_rows(const float* logits, const uint16_t* x_bf16, size_t tokens, int32_t hidden,
+                            int32_t experts, int32_t top_k, void* workspace, size_t workspace_bytes,
+                            kb200_moe_dispatch* result, unsigned* status, void* stream) {
+    if (const int s = check_shape(hidden, experts, top_k))
+        return s;
+    if (!result)
+        return fail(KB200_INVALID, "null dispatch result");
+    if (!tokens) {
+        *result = {nullptr, nullptr, nullptr, nullptr, 0};
+        return KB200_OK;
+    }
+    if (!x_bf16 || !logits || !workspace)
+        return fail(KB200_INVALID, "null pointer");
+    if (!aligned(x_bf16, 16) || !aligned(workspace, 256))
+        return fail(KB200_INVALID, "MoE activations must be 16-byte aligned, workspace 256-byte aligned");
+    const size_t n = tokens * size_t(top_k);
+    if (n > size_t(INT32_MAX) / 4)
+        return fail(KB200_UNSUPPORTED, "too many tokens");
+    const Workspace ws = carve_shape(workspace, tokens, size_t(hidden), 0, size_t(experts), size_t(top_k), false);
+    if (ws.bytes > workspace_bytes)
+        return fail(KB200_NO_MEMORY, "dispatch workspace too small (see kb200_moe_dispatch_workspace_bytes)");
+    if (const int s = dispatch_launch(logits, x_bf16, tokens, hidden, experts, top_k, ws, status,
+                                      static_cast<cudaStream_t>(stream)))
+        return s;
+    *result = {ws.offsets, ws.pos, ws.weight, reinterpret_cast<uint16_t*>(ws.xs), n};
+    return KB200_OK;
+}
+
+size_t kb200_moe_experts_workspace_bytes(const kb200_moe_weights* w, size_t rows) {
+    if (!w || check_weights(w, false) != KB200_OK)
+        return 0;
+    return carve_experts(nullptr, *w, rows).bytes;
+}
+
+int kb200_moe_experts(const kb200_moe_weights* w, const uint16_t* rows_f16, const int32_t* offsets, size_t rows,
+                      float* y, void* workspace, size_t workspace_bytes, unsigned* status, void* stream_ptr) {
+    if (const int s = check_weights(w, false))
+        return s;
+    if (!rows)
+        return KB200_OK;
+    if (!rows_f16 || !offsets || !y || !workspace)
+        return fail(KB200_INVALID, "null pointer");
+    if (!aligned(rows_f16, 16) || !aligned(y, 16) || !aligned(workspace, 256))
+        return fail(KB200_INVALID, "MoE rows must be 16-byte aligned, workspace 256-byte aligned");
+    if (rows > size_t(INT32_MAX) / 4)
+        return fail(KB200_UNSUPPORTED, "too many rows");
+    const ExpertWs ws = carve_experts(workspace, *w, rows);
+    if (ws.bytes > workspace_bytes)
+        return fail(KB200_NO_MEMORY, "expert workspace too small (see kb200_moe_experts_workspace_bytes)");
+    auto stream = static_cast<cudaStream_t>(stream_ptr);
+    moe_mtile_kernel<<<1, 32, 0, stream>>>(offsets, w->experts, ws.mtile);
+    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
-        return cuda_fail(e, "counts memset");
-    moe_route_kernel<<<int((tokens * 32 + 255) / 256), 256, 0, stream>>>(logits, int(tokens), E, K, ws.chosen, ws.weight,
-                                                                          ws.counts);
-    moe_sort_kernel<<<1, 1024, 0, stream>>>(ws.chosen, int(n), E, ws.counts, ws.offsets, ws.perm, ws.pos, ws.mtile);
-    {
-        const size_t work = n * size_t(H / 8);
-        const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
-        moe_gather_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x_bf16), ws.perm, int(n), K,
-                                                      H, ws.xs, status);
-    }
-    if ((e = cudaGetLastError()) != cudaSuccess)
-        return cuda_fail(e, "MoE routing launches");
-    const int mtiles_max = int((n + BM - 1) / BM) + E;
+        return cuda_fail(e, "moe_mtile_kernel launch");
+    return experts_launch(w, reinterpret_cast<const __half*>(rows_f16), offsets, ws.mtile, rows, ws.act, y, status,
+                          stream);
+}
 
-    // Decode-sized batches (at most 8 token rows per expert on average) are a
-    // weight stream: the grouped GEMV reads each routed expert once per 8 of
-    // its rows. KB200_MOE_PATH=gemm|gemv overrides the choice.
-    bool gemv = n <= size_t(8) * size_t(E);
-    if (const char* path = std::getenv("KB200_MOE_PATH"))
-        gemv = std::strcmp(path, "gemv") == 0 ? true : std::strcmp(path, "gemm") == 0 ? false : gemv;
-    if (gemv) {
-        const int grid_cap = sm_count() * 8;
-        GemvParams v;
-        std::memset(&v, 0, sizeof(v));
-        v.blocks = w->gate_up_blocks;
-        v.scales = w->gate_up_scales;
-        v.bias = w->gate_up_bias;
-        v.x = ws.xs;
-        v.offsets = ws.offsets;
-        v.out = ws.act;
-        v.K = H;
-        v.Nrows = 2 * I;
-        v.E = E;
-        v.chunks = I / 8;
-        v.epilogue = 0;
-        v.split = w->interleaved ? 0 : 1;
-        v.out_cols = I;
-        v.act_kind = w->activation;
-        v.limit = w->limit;
-        v.alpha = w->alpha;
-        v.status = status;
-        moe_gemv_kernel<<<std::min(E * v.chunks, grid_cap), 32 * kGemvWarps, 0, stream>>>(v);
-        v.blocks = w->down_blocks;
-        v.scales = w->down_scales;
-        v.bias = w->down_bias;
-        v.x = ws.act;
-        v.out = ws.y;
-        v.K = I;
-        v.Nrows = H;
-        v.chunks = H / 16;
-        v.epilogue = 1;
-        v.split = 0;
-        v.out_cols = H;
-        moe_gemv_kernel<<<std::min(E * v.chunks, grid_cap), 32 * kGemvWarps, 0, stream>>>(v);
-        if ((e = cudaGetLastError()) != cudaSuccess)
-            return cuda_fail(e, "moe_gemv_kernel launch");
-    } else {
+int kb200_moe_combine(const float* y, const float* weight, const int32_t* pos, size_t tokens, int32_t top_k,
+                      int32_t hidden, float* out, void* stream) {
+    if (top_k <= 0 || top_k > kMaxTopK || hidden <= 0 || hidden % 4)
+        return fail(KB200_UNSUPPORTED, "combine shape");
+    if (!tokens)
+        return KB200_OK;
+    if (!y || !weight || !pos || !out)
+        return fail(KB200_INVALID, "null pointer");
+    if (!aligned(y, 16) || !aligned(out, 16))
+        return fail(KB200_INVALID, "combine rows must be 16-byte aligned");
+    return combine_launch(y, weight, pos, tokens, top_k, hidden, out, static_cast<cudaStream_t>(stream));
+}
 
-    // gate/up: [n, H] x [2I, H]^T per expert, activation in the epilogue.
-    GroupParams g1;
-    std::memset(&g1, 0, sizeof(g1));
-    const bool split = !w->interleaved;
-    if (!encode_2d(&g1.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws.xs, uint64_t(H), n, BK, BM,
-                   CU_TENSOR_MAP_SWIZZLE_128B)
-        || !encode_2d(&g1.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->gate_up_blocks, uint64_t(H / 2),
-                      uint64_t(E) * 2 * I, BK / 2, split ? BN / 2 : BN, CU_TENSOR_MAP_SWIZZLE_NONE))
-        return fail(KB200_INVALID, "tensor map encoding (gate/up)");
-    g1.scales = w->gate_up_scales;
-    g1.bias = w->gate_up_bias;
-    g1.offsets = ws.offsets;
-    g1.mtile_prefix = ws.mtile;
-    g1.out = ws.act;
-    g1.K = H;
-    g1.Nrows = 2 * I;
-    g1.E = E;
-    g1.n_tiles = split ? I / (BN / 2) : 2 * I / BN;
-    g1.split = split ? 1 : 0;
-    g1.epilogue = 0;
-    g1.out_cols = I;
-    g1.act_kind = w->activation;
-    g1.limit = w->limit;
-    g1.alpha = w->alpha;
-    g1.status = status;
-    if ((2 * I) % BN && !split)
-        return fail(KB200_UNSUPPORTED, "interleaved gate/up needs 2*inter to be a multiple of 128");
-    if (const int s = launch_gemm(g1, mtiles_max * g1.n_tiles, stream))
-        return s;
-
-    // down: [n, I] x [H, I]^T per expert -> fp32 rows.
-    GroupParams g2;
-    std::memset(&g2, 0, sizeof(g2));
-    if (!encode_2d(&g2.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ws.act, uint64_t(I), n, BK, BM,
-                   CU_TENSOR_MAP_SWIZZLE_128B)
-        || !encode_2d(&g2.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->down_blocks, uint64_t(I / 2), uint64_t(E) * H,
-                      BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
-        return fail(KB200_INVALID, "tensor map encoding (down)");
-    g2.scales = w->down_scales;
-    g2.bias = w->down_bias;
-    g2.offsets = ws.offsets;
-    g2.mtile_prefix = ws.mtile;
-    g2.out = ws.y;
-    g2.K = I;
-    g2.Nrows = H;
-    g2.E = E;
-    g2.n_tiles = (H + BN - 1) / BN;
-    g2.split = 0;
-    g2.epilogue = 1;
-    g2.out_cols = H;
-    g2.status = status;
-    if (const int s = launch_gemm(g2, mtiles_max * g2.n_tiles, stream))
-        return s;
-    }
-
-    {
-        const size_t work = tokens * size_t(H / 4);
-        const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
-        moe_combine_kernel<<<blocks, 256, 0, stream>>>(ws.y, ws.weight, ws.pos, int(tokens), K, H, out);
-    }
-    e = cudaGetLastError();
-    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_combine_kernel launch");
+int kb200_rows_regroup(const void* src, void* dst, size_t row_bytes, const int64_t* segments, size_t count,
+                       size_t max_rows, void* stream) {
+    if (!count)
+        return KB200_OK;
+    if (!src || !dst || !segments)
+        return fail(KB200_INVALID, "null pointer");
+    if (row_bytes % 16 || !aligned(src, 16) || !aligned(dst, 16) || !aligned(segments, 8))
+        return fail(KB200_INVALID, "rows must be whole 16-byte words and 16-byte aligned");
+    if (count > 65535)
+        return fail(KB200_UNSUPPORTED, "at most 65535 segments");
+    const size_t words = std::max<size_t>(1, max_rows) * (row_bytes / 16);
+    const dim3 grid(unsigned(std::min<size_t>((words + 255) / 256, 64)), unsigned(count));
+    rows_regroup_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(src), static_cast<uint4*>(dst), row_bytes / 16,
+        reinterpret_cast<const long long*>(segments));
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "rows_regroup_kernel launch");
 }
 
 // For callers that cannot allocate device memory per call (stream capture,

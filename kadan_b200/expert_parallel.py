@@ -1,0 +1,184 @@
+"""Expert-parallel MXFP4 MoE layer across the GPUs of one node.
+
+The reference runs the whole MoE layer on one host (MoeLayer::forward,
+IW/src/models/text/qwen_layers.cpp:378-492) and has no multi-device split of
+its experts. Here the experts are split evenly and contiguously over the ranks
+of a process group (rank r holds experts [r*E/N, (r+1)*E/N)); every rank
+routes its own tokens and the rows travel to the rank of their expert and
+back:
+
+  1. dispatch (kb200_moe_dispatch_rows): route, stable sort of the
+     (token, choice) slots by expert, gather fp16 rows in expert-major order.
+     Experts are contiguous per rank, so the rows for rank r are one range.
+  2. exchange counts (all-to-all of the per-expert counts) and rows
+     (all-to-all of the fp16 rows; NCCL over NVLink).
+  3. regroup the received rows from source-major to expert-major order
+     (kb200_rows_regroup), run the local experts (kb200_moe_experts), and
+     put the fp32 results back in source-major order.
+  4. all-to-all the results back; combine in selection order
+     (kb200_moe_combine).
+
+Each rank's output equals the single-device layer on the same tokens: the
+same routing, the same expert arithmetic per row, the same combine order.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import (MoeWeights, check, moe_combine, moe_dispatch_rows, moe_experts, moe_weights, lib, rows_regroup)
+
+
+def expert_range(experts: int, world: int, rank: int) -> Tuple[int, int]:
+    """[first, end) of the experts rank `rank` holds (even split)."""
+    if experts % world:
+        raise ValueError(f"{experts} experts do not split evenly over {world} ranks")
+    per = experts // world
+    return rank * per, (rank + 1) * per
+
+
+def send_counts(expert_counts: np.ndarray, world: int) -> np.ndarray:
+    """Rows this rank sends to each rank: its per-expert counts summed per owner."""
+    return expert_counts.reshape(world, -1).sum(axis=1)
+
+
+def regroup_segments(recv_counts: np.ndarray) -> Tuple[np.ndarray, np.ndarray]:
+    """Segments {src_row, dst_row, rows} that turn rows received source-major
+    (for each source rank, its rows of local experts 0..E_l-1 in order) into
+    expert-major order (for each local expert, the rows of source 0..N-1),
+    and the local expert offsets [E_l + 1] of the result.
+
+    recv_counts[s, e]: rows of local expert e received from rank s."""
+    world, local = recv_counts.shape
+    src_start = np.zeros((world, local), dtype=np.int64)
+    flat = recv_counts.reshape(-1).astype(np.int64)
+    src_start.reshape(-1)[1:] = np.cumsum(flat)[:-1]
+    segs = []
+    offsets = np.zeros(local + 1, dtype=np.int32)
+    dst = 0
+    for e in range(local):
+        offsets[e] = dst
+        for s in range(world):
+            n = int(recv_counts[s, e])
+            if n:
+                segs.append((int(src_start[s, e]), dst, n))
+            dst += n
+    offsets[local] = dst
+    return np.array(segs, dtype=np.int64).reshape(-1, 3), offsets
+
+
+class ExpertParallelMoE:
+    """One MoE layer whose experts are split over the ranks of `group`.
+
+    weights: kb200 MoeWeights of the experts this rank holds (experts = E/N,
+    top_k = the model's k), built over device tensors the caller keeps
+    alive. experts: the model's total expert count E."""
+
+    def __init__(self, local: MoeWeights, experts: int, world: int, rank: int, group=None):
+        import torch.distributed as dist
+
+        self.w, self.experts, self.world, self.rank, self.group = local, experts, world, rank, group
+        self.top_k = local.top_k
+        self.local = experts // world
+        if local.experts != self.local:
+            raise ValueError("local weights must hold experts / world experts")
+        self.dist = dist if world > 1 else None
+        self._buffers = {}
+
+    def _buffer(self, name: str, nbytes: int, device):
+        import torch
+
+        buf = self._buffers.get(name)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            self._buffers[name] = buf
+        return buf
+
+    def forward(self, x_bf16, logits, out=None, status=None):
+        """out[T, H] fp32 for this rank's tokens x (bf16 [T, H]) routed by
+        fp32 logits [T, E]. Collective: every rank calls it for the layer."""
+        import torch
+
+        dev = x_bf16.device
+        tokens, hidden = x_bf16.shape
+        k, world = self.top_k, self.world
+        if out is None:
+            out = torch.empty(tokens, hidden, dtype=torch.float32, device=dev)
+        need = int(lib.kb200_moe_dispatch_workspace_bytes(tokens, hidden, self.experts, k))
+        dws = self._buffer("dispatch", need, dev)
+        d = moe_dispatch_rows(logits, x_bf16, k, dws, status)
+        n = tokens * k
+        base = dws.data_ptr()
+
+        def view(ptr, count, dtype, elem):
+            off = ptr - base
+            return dws[off:off + count * elem].view(dtype)
+
+        offsets = view(d.offsets, self.experts + 1, torch.int32, 4) if n else torch.zeros(
+            self.experts + 1, dtype=torch.int32, device=dev)
+        rows = view(d.rows, n * hidden, torch.float16, 2).view(n, hidden) if n else torch.empty(
+            0, hidden, dtype=torch.float16, device=dev)
+        counts = (offsets[1:] - offsets[:-1]).to(torch.int64)
+        if self.dist:
+            recv = torch.empty_like(counts)
+            self.dist.all_to_all_single(recv, counts, group=self.group)
+            host = torch.cat([counts, recv]).cpu().numpy()
+            mine, recv_counts = host[:self.experts], host[self.experts:].reshape(world, self.local)
+        else:
+            mine = counts.cpu().numpy()
+            recv_counts = mine.reshape(1, self.local)
+        sends = send_counts(mine, world).tolist()
+        recvs = recv_counts.sum(axis=1).tolist()
+        r_total = int(sum(recvs))
+        if self.dist:
+            arrived = torch.empty(r_total, hidden, dtype=torch.float16, device=dev)
+            self.dist.all_to_all_single(arrived, rows, output_split_sizes=recvs, input_split_sizes=sends,
+                                        group=self.group)
+        else:
+            arrived = rows
+        segs, local_offsets = regroup_segments(recv_counts)
+        seg_dev = torch.from_numpy(segs).to(dev, non_blocking=False) if len(segs) else None
+        max_rows = int(segs[:, 2].max()) if len(segs) else 0
+        grouped = torch.empty(r_total, hidden, dtype=torch.float16, device=dev)
+        y_grouped = torch.empty(r_total, hidden, dtype=torch.float32, device=dev)
+        if r_total:
+            rows_regroup(arrived, grouped, seg_dev, max_rows)
+            off_dev = torch.from_numpy(local_offsets).to(dev)
+            ews = self._buffer("experts", int(lib.kb200_moe_experts_workspace_bytes(
+                self._wref(), r_total)), dev)
+            moe_experts(self.w, grouped, off_dev, y_grouped, ews, status)
+            back_segs = segs[:, [1, 0, 2]].copy()
+            y_arrived = torch.empty(r_total, hidden, dtype=torch.float32, device=dev)
+            rows_regroup(y_grouped, y_arrived, torch.from_numpy(back_segs).to(dev), max_rows)
+        else:
+            y_arrived = y_grouped
+        if self.dist:
+            y_sent = torch.empty(n, hidden, dtype=torch.float32, device=dev)
+            self.dist.all_to_all_single(y_sent, y_arrived, output_split_sizes=sends, input_split_sizes=recvs,
+                                        group=self.group)
+        else:
+            y_sent = y_arrived
+        if tokens:
+            moe_combine(y_sent, d.weight, d.pos, tokens, k, out)
+        return out
+
+    def _wref(self):
+        import ctypes
+
+        return ctypes.byref(self.w)
+
+
+def local_weights(gu_blocks, gu_scales, dn_blocks, dn_scales, *, hidden: int, inter: int, experts: int, top_k: int,
+                  world: int, rank: int, gu_bias=None, dn_bias=None, **kw) -> Tuple[MoeWeights, List[object]]:
+    """MoeWeights over this rank's experts, cut from full device tensors
+    [E, ...] (views, no copy). Returns the struct and the views to keep alive."""
+    first, end = expert_range(experts, world, rank)
+    parts = [t[first:end] if t is not None else None for t in (gu_blocks, gu_scales, dn_blocks, dn_scales,
+                                                               gu_bias, dn_bias)]
+    for t in parts:
+        if t is not None and not t.is_contiguous():
+            raise ValueError("expert tensors must be contiguous")
+    w = moe_weights(parts[0], parts[1], parts[2], parts[3], hidden=hidden, inter=inter, experts=end - first,
+                    top_k=top_k, gu_bias=parts[4], dn_bias=parts[5], **kw)
+    return w, parts
