@@ -557,7 +557,12 @@ def run_tp(args, rank, world, local_rank):
     layers = args.layers or 80
     groups = tp.llama3_70b_projections()
     weights = tp.synth_shards(groups, layers, world, rank, device)
-    stack = tp.DecodeStack(groups, weights, tokens, world, rank, device, group=group)
+    reducer = None
+    if dist and args.collective == "peer":
+        from kadan_b200.collectives import PeerAllReduce
+
+        reducer = PeerAllReduce(tokens * 8192)
+    stack = tp.DecodeStack(groups, weights, tokens, world, rank, device, group=group, collective=reducer)
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):
         stack.launch(stream)
@@ -588,13 +593,22 @@ def run_tp(args, rank, world, local_rank):
         # The collective alone (same sizes, same count per step), for the
         # breakdown; not part of the value.
         t = torch.zeros(tokens, 8192, device=device)
+        cur = torch.cuda.current_stream()
+
+        def one():
+            if reducer:
+                reducer(t, cur)
+            else:
+                dist.all_reduce(t)
+
         for _ in range(20):
-            dist.all_reduce(t)
+            one()
         torch.cuda.synchronize()
+        dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(400):
-            dist.all_reduce(t)
+            one()
         b.record()
         torch.cuda.synchronize()
         ar_us = a.elapsed_time(b) / 400 * 1e3
@@ -608,6 +622,8 @@ def run_tp(args, rank, world, local_rank):
     peak, peak_kind = peaks()
     graph = None
     if dist:
+        if reducer:
+            reducer.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank:
@@ -620,7 +636,9 @@ def run_tp(args, rank, world, local_rank):
         "data": "synthetic (seeded shards drawn on each device)",
         "config": {"workload": f"BASELINE config 4 decode: Llama-3-70B Q6_K/Q4_K, {layers} layers, T={tokens}",
                    "weight_bytes_per_step": wbytes, "weight_bytes_per_rank": local_bytes,
-                   "parallelism": f"tp{world}", "collective": "NCCL all-reduce (fp32) after o and down",
+                   "parallelism": f"tp{world}",
+                   "collective": ("peer-memory all-reduce kernel (fp32, NVLink stores)" if reducer else
+                                  "NCCL all-reduce (fp32)") + " after o and down",
                    "l2": "inputs larger than L2"},
         "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / peak, 4), "peak_gbs": peak,
         "peak_source": f"{peak_kind} hbm_gbs",
@@ -725,6 +743,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
+                    help="all-reduce of --case tp70b at N > 1")
     ap.add_argument("--layers", type=int, default=0, help="layers for --case tp70b / ep120b (default 80 / 36)")
     args = ap.parse_args()
     if args.warmup < 3:

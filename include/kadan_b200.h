@@ -343,6 +343,33 @@ KB200_API int kb200_moe_combine(
 KB200_API int kb200_rows_regroup(const void* src, void* dst, size_t row_bytes, const int64_t* segments, size_t count,
                                  size_t max_rows, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Peer-memory all-reduce for tensor parallelism (one process per GPU).
+ *
+ * The reference adds nothing across devices: its column slices are gathered
+ * on the host (gguf_batch_partition.hpp:48-59). Row-parallel projections
+ * here leave each GPU a partial sum of the whole output, which
+ * kb200_peer_allreduce_f32 adds over the ranks in one kernel: every rank
+ * stores its chunks into every peer's buffer over NVLink, flags them with a
+ * system-scope release, waits (bounded by timeout_s) for the peers' flags
+ * and sums in rank order, so all ranks hold the same bits.
+ *
+ * Setup: each rank allocates kb200_peer_buffer_bytes(world, max_count) with
+ * kb200_device_alloc (zeroed), exports it with kb200_ipc_handle, sends the
+ * handle to the others, opens theirs with kb200_ipc_open and passes all
+ * buffer addresses (its own at [rank]) as `peers`. Every rank must make the
+ * same sequence of calls. A wait that runs out sets bit 16 of the device
+ * watchdog word (kb200_take_device_error) and leaves data unreduced. */
+#define KB200_IPC_HANDLE_BYTES 64
+KB200_API size_t kb200_peer_buffer_bytes(int world, size_t max_count);
+KB200_API int kb200_device_alloc(size_t bytes, void** ptr);
+KB200_API int kb200_device_free(void* ptr);
+KB200_API int kb200_ipc_handle(const void* ptr, void* handle);
+KB200_API int kb200_ipc_open(const void* handle, void** ptr);
+KB200_API int kb200_ipc_close(void* ptr);
+KB200_API int kb200_peer_allreduce_f32(float* data, size_t count, void* const* peers, int world, int rank,
+                                       size_t max_count, double timeout_s, void* stream);
+
 /* The routing stage alone (for tests): chosen [tokens, top_k] int32,
  * weight [tokens, top_k] fp32, device. */
 KB200_API int kb200_moe_route(
@@ -358,7 +385,8 @@ KB200_API int kb200_moe_route(
 /* Device-side watchdog word: nonzero when a bounded wait inside a kernel gave up
  * since the last call of this function, which also clears it. Synchronous.
  * Bits: 1 a stage never arrived, 2 a stage was never released, 4 the final
- * copies never landed, 8 a cut tile's other pieces never arrived (Q4_K GEMV). */
+ * copies never landed, 8 a cut tile's other pieces never arrived (Q4_K GEMV),
+ * 16 a peer's chunk never arrived (peer all-reduce). */
 KB200_API int kb200_take_device_error(unsigned* value);
 
 #ifdef __cplusplus

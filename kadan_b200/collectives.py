@@ -1,0 +1,80 @@
+"""Collectives of the tensor-parallel path over NVLink peer memory.
+
+PeerAllReduce maps every rank's exchange buffer into every other rank (CUDA
+IPC handles, swapped once over the process group) and adds fp32 vectors with
+one kernel per call (kb200_peer_allreduce_f32); no library collective runs on
+the data path. The process group is only used at setup and teardown.
+"""
+from __future__ import annotations
+
+import ctypes
+
+from . import check, lib
+
+lib.kb200_peer_buffer_bytes.restype = ctypes.c_size_t
+lib.kb200_peer_buffer_bytes.argtypes = [ctypes.c_int, ctypes.c_size_t]
+lib.kb200_device_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]
+lib.kb200_device_free.argtypes = [ctypes.c_void_p]
+lib.kb200_ipc_handle.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+lib.kb200_ipc_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+lib.kb200_ipc_close.argtypes = [ctypes.c_void_p]
+lib.kb200_peer_allreduce_f32.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int,
+                                         ctypes.c_int, ctypes.c_size_t, ctypes.c_double, ctypes.c_void_p]
+IPC_HANDLE_BYTES = 64
+
+
+class PeerAllReduce:
+    """Sum fp32 device tensors of up to `max_count` elements over the ranks of
+    `group` (every rank calls with the same sizes in the same order)."""
+
+    def __init__(self, max_count: int, group=None, timeout_s: float = 2.0):
+        import torch.distributed as dist
+
+        self.dist, self.group = dist, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_count = int(max_count)
+        self.timeout_s = float(timeout_s)
+        nbytes = int(lib.kb200_peer_buffer_bytes(self.world, self.max_count))
+        if not nbytes:
+            raise ValueError("peer all-reduce supports 1..8 ranks")
+        own = ctypes.c_void_p()
+        check(lib.kb200_device_alloc(nbytes, ctypes.byref(own)))
+        self.own = own.value
+        handle = (ctypes.c_char * IPC_HANDLE_BYTES)()
+        check(lib.kb200_ipc_handle(self.own, handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self.own)
+                continue
+            buf = (ctypes.c_char * IPC_HANDLE_BYTES).from_buffer_copy(h)
+            p = ctypes.c_void_p()
+            check(lib.kb200_ipc_open(buf, ctypes.byref(p)))
+            self.opened.append(p.value)
+            ptrs.append(p.value)
+        self.peers = (ctypes.c_void_p * self.world)(*ptrs)
+        dist.barrier(group=group)
+
+    def __call__(self, tensor, stream) -> None:
+        """In place on `tensor` (fp32, contiguous), enqueued on `stream`."""
+        check(lib.kb200_peer_allreduce_f32(tensor.data_ptr(), tensor.numel(), self.peers, self.world, self.rank,
+                                           self.max_count, self.timeout_s, ctypes.c_void_p(stream.cuda_stream)))
+
+    def close(self) -> None:
+        """Collective: every rank's kernels are done before any buffer goes."""
+        if self.own is None:
+            return
+        import torch
+
+        torch.cuda.synchronize()
+        self.dist.barrier(group=self.group)
+        for p in self.opened:
+            check(lib.kb200_ipc_close(p))
+        self.opened = []
+        self.dist.barrier(group=self.group)
+        check(lib.kb200_device_free(self.own))
+        self.own = None

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace kb200 {

@@ -15,7 +15,8 @@ process group instead, and the split follows the transformer block:
   the K-quants), so every rank holds whole blocks: each packed row is cut at
   a byte offset of whole blocks and no block straddles two ranks. Each rank
   produces a partial sum of the full output and the ranks add them with one
-  all-reduce over NVLink (NCCL) — two per layer.
+  all-reduce over NVLink — two per layer: the peer-memory kernel of
+  collectives.PeerAllReduce, or NCCL through torch.distributed.
 
 Column and block splits use the same proportional boundary as the reference
 (kb200_weight_boundary, equal capacities here), so N ranks of one projection
@@ -137,13 +138,17 @@ class DecodeStack:
     graph (NCCL collectives are capturable)."""
 
     def __init__(self, groups: Sequence[Sequence[Projection]], weights: Sequence[Dict[str, object]], tokens: int,
-                 world: int, rank: int, device, group=None, seed: int = 0, inputs: Optional[Dict[str, object]] = None):
+                 world: int, rank: int, device, group=None, seed: int = 0, inputs: Optional[Dict[str, object]] = None,
+                 collective=None):
         """inputs: full fp32 activations [tokens, in] per group, keyed by the
         group's first projection; by default bf16-representable N(0,1) drawn
-        from `seed` (the same on every rank)."""
+        from `seed` (the same on every rank). collective: a callable
+        (tensor, stream) that sums a tensor over the ranks in place, such as
+        collectives.PeerAllReduce; None uses torch.distributed.all_reduce."""
         import torch
 
         self.groups, self.world, self.rank, self.group, self.tokens = groups, world, rank, group, tokens
+        self.collective = collective
         self.weights = weights
         gen = torch.Generator(device=device).manual_seed(seed + 7)
         self.inputs: Dict[str, object] = dict(inputs or {})
@@ -184,7 +189,10 @@ class DecodeStack:
         for arr, n, reduce in self.calls:
             check(lib.kb200_gguf_gemv_batch(arr, n, sptr))
             for t in reduce:
-                dist.all_reduce(t, group=self.group)
+                if self.collective is not None:
+                    self.collective(t, stream)
+                else:
+                    dist.all_reduce(t, group=self.group)
 
     def weight_bytes(self) -> int:
         """Packed weight bytes this rank streams per step."""

@@ -33,7 +33,7 @@ def small_groups():
             [Projection("down", Q6_K, h, ffn, "row")]]
 
 
-def run_rank(rank: int, world: int, port: int) -> dict:
+def run_rank(rank: int, world: int, port: int, collective: str = "nccl") -> dict:
     import torch
 
     from kadan_b200 import synth
@@ -65,8 +65,14 @@ def run_rank(rank: int, world: int, port: int) -> dict:
             weights.append(local)
         xs = {g[0].name: synth.activations(TOKENS * g[0].in_, seed=7 + gi, dtype="bf16").reshape(TOKENS, g[0].in_)
               for gi, g in enumerate(groups)}
+        reducer = None
+        if world > 1 and collective == "peer":
+            from kadan_b200.collectives import PeerAllReduce
+
+            reducer = PeerAllReduce(TOKENS * 1024)
         stack = tp.DecodeStack(groups, weights, TOKENS, world, rank, device,
-                               inputs={k: torch.from_numpy(v).to(device) for k, v in xs.items()})
+                               inputs={k: torch.from_numpy(v).to(device) for k, v in xs.items()},
+                               collective=reducer)
         # The stack writes each projection's output once per layer; the last
         # layer's values remain.
         want = {}
@@ -94,6 +100,8 @@ def run_rank(rank: int, world: int, port: int) -> dict:
         for name, y in want.items():
             errs[f"graph/{name}"] = _rel(stack.outputs[name].cpu().numpy(), y)
         graph = None
+        if reducer:
+            reducer.close()
         return errs
     finally:
         if dist:
@@ -106,8 +114,70 @@ def _rel(got, want) -> float:
     return float(np.max(np.abs(got - want)) / max(1.0, float(np.max(np.abs(want)))))
 
 
-def _child(rank, world, port, results):
-    results[rank] = run_rank(rank, world, port)
+def _child(rank, world, port, collective, results):
+    results[rank] = run_rank(rank, world, port, collective)
+
+
+def allreduce_rank(rank: int, world: int, port: int) -> dict:
+    """Peer all-reduce of seeded vectors, several sizes back to back (eager
+    and replayed from a CUDA graph): each result must equal the fp32 sum in
+    rank order computed on the host, bit for bit."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from kadan_b200.collectives import PeerAllReduce
+
+    device = torch.device("cuda", rank)
+    torch.cuda.set_device(device)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
+                            timeout=datetime.timedelta(seconds=60))
+    res = {}
+    try:
+        sizes = [4, 8192, 1028, 262144, 8192, 96, 300000, 8192]
+        red = PeerAllReduce(max(sizes))
+        stream = torch.cuda.current_stream()
+
+        def data(n, r, salt):
+            g = np.random.default_rng(1000 * salt + 17 * r + n)
+            return g.standard_normal(n).astype(np.float32)
+
+        def want(n, salt):
+            acc = data(n, 0, salt)
+            for r in range(1, world):
+                acc = acc + data(n, r, salt)
+            return acc
+
+        for i, n in enumerate(sizes):
+            t = torch.from_numpy(data(n, rank, i)).to(device)
+            red(t, stream)
+            res[f"eager/{i}/{n}"] = bool(np.array_equal(t.cpu().numpy().view(np.uint32), want(n, i).view(np.uint32)))
+        bufs = [torch.from_numpy(data(n, rank, 50 + i)).to(device) for i, n in enumerate(sizes[:3])]
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(device)
+        with torch.cuda.graph(graph, stream=side):
+            for b in bufs:
+                red(b, side)
+        for rep in range(3):
+            for i, n in enumerate(sizes[:3]):
+                bufs[i].copy_(torch.from_numpy(data(n, rank, 100 * rep + i)).to(device))
+            torch.cuda.synchronize()
+            graph.replay()
+            torch.cuda.synchronize()
+            for i, n in enumerate(sizes[:3]):
+                ok = np.array_equal(bufs[i].cpu().numpy().view(np.uint32), want(n, 100 * rep + i).view(np.uint32))
+                res[f"graph/{rep}/{n}"] = bool(ok)
+        graph = None
+        red.close()
+    finally:
+        dist.destroy_process_group()
+    return res
+
+
+def _ar_child(rank, world, port, results):
+    results[rank] = allreduce_rank(rank, world, port)
 
 
 def _port() -> int:
@@ -122,6 +192,48 @@ def test_tp_one_rank_matches_oracle(cuda):
     assert not bad, bad
 
 
+def _spawn(target, args_of, world=2):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        results = manager.dict()
+        port = _port()
+        procs = [ctx.Process(target=target, args=args_of(r, port) + (results,)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+        codes = [p.exitcode for p in procs]
+        for p in procs:
+            if p.exitcode is None:
+                p.kill()
+        assert codes == [0] * world, codes
+        return dict(results)
+
+
+def test_peer_allreduce_two_ranks_bitwise(cuda):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("two GPUs needed")
+    results = _spawn(_ar_child, lambda r, port: (r, 2, port))
+    for r in range(2):
+        bad = [k for k, ok in results[r].items() if not ok]
+        assert not bad, (r, bad)
+
+
+def test_tp_two_ranks_peer_collective_match_oracle(cuda):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("two GPUs needed")
+    results = _spawn(_child, lambda r, port: (r, 2, port, "peer"))
+    for r in range(2):
+        bad = {k: v for k, v in results[r].items() if not v < TOL}
+        assert not bad, (r, bad)
+
+
 def test_tp_two_ranks_match_oracle(cuda):
     import torch
     import torch.multiprocessing as mp
@@ -132,7 +244,7 @@ def test_tp_two_ranks_match_oracle(cuda):
     with ctx.Manager() as manager:
         results = manager.dict()
         port = _port()
-        procs = [ctx.Process(target=_child, args=(r, 2, port, results)) for r in range(2)]
+        procs = [ctx.Process(target=_child, args=(r, 2, port, "nccl", results)) for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:
