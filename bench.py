@@ -601,17 +601,30 @@ def run_tp(args, rank, world, local_rank):
             else:
                 dist.all_reduce(t)
 
+        side = torch.cuda.Stream(device)
         for _ in range(20):
             one()
         torch.cuda.synchronize()
+        # 2 * layers collectives back to back in one CUDA graph: device time
+        # per collective without host launch cost.
+        ar_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ar_graph, stream=side):
+            cur = side
+            for _ in range(2 * layers):
+                one()
+        torch.cuda.synchronize()
         dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(400):
-            one()
-        b.record()
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                ar_graph.replay()
+            a.record(side)
+            for _ in range(10):
+                ar_graph.replay()
+            b.record(side)
         torch.cuda.synchronize()
-        ar_us = a.elapsed_time(b) / 400 * 1e3
+        ar_us = a.elapsed_time(b) / (10 * 2 * layers) * 1e3
+        ar_graph = None
         m = torch.tensor([ms], device=device)
         dist.all_reduce(m, op=dist.ReduceOp.MAX)
         ms = float(m.item())

@@ -625,10 +625,10 @@ int check_job(const kb200_gemv_job& j) {
     return KB200_OK;
 }
 
-// 2 = tensor-pipe kernel (Q4_K), 1 = bulk-copy staged CUDA-core kernel,
+// 2 = tensor-pipe kernel (Q4_K, Q6_K), 1 = bulk-copy staged CUDA-core kernel,
 // 0 = generic kernel.
 int path_of(const kb200_gemv_job& j) {
-    if (q4k_mma_eligible(j))
+    if (mma_eligible(j))
         return 2;
     return staged_format(j.encoding) && aligned(j.weights, 16) && j.row_bytes % 16 == 0
                    && aligned(j.input, 16)
@@ -688,7 +688,7 @@ int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream
     }
     for (const auto& [key, members] : groups) {
         if (key.path == 2) {
-            if (const int s = launch_q4k_mma(members, stream))
+            if (const int s = launch_mma(members, stream))
                 return s;
             continue;
         }

@@ -7,10 +7,11 @@
 
 namespace kb200 {
 
-// Q4_K job that the mma.sync kernel can take: 16-byte aligned rows of whole
-// super-blocks, and the driver's tensor-map encoder is available.
-bool q4k_mma_eligible(const kb200_gemv_job& job);
-// One launch per 32 jobs; rows above KB200_BATCH_ROWS become row groups.
-int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream);
+// Q4_K or Q6_K job that the mma.sync kernels can take: 16-byte aligned rows
+// of whole super-blocks, and the driver's tensor-map encoder is available.
+bool mma_eligible(const kb200_gemv_job& job);
+// Jobs of one encoding: one launch per 32 jobs; rows above the kernel's rows
+// per pass (8 for Q4_K, 4 for Q6_K) become row groups.
+int launch_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream);
 
 }  // namespace kb200

@@ -160,13 +160,13 @@ struct Layout {
 // super-blocks) that fit kSegBudget; operands first, then minimum-term
 // operands, then scales. blocks == 0 means not even one stage fits (the host
 // never launches such a geometry).
-__host__ __device__ constexpr int segment_blocks(int rows, int bps) {
-    return kSegBudget / (rows * kTokenBlockTotal) / bps * bps;
+__host__ __device__ constexpr int segment_blocks(int rows, int bps, int budget = kSegBudget) {
+    return budget / (rows * kTokenBlockTotal) / bps * bps;
 }
 
 struct Segment {
     int blocks, rows;
-    __device__ Segment(int r, int bps) : blocks(segment_blocks(r, bps)), rows(r) {}
+    __device__ Segment(int r, int bps, int budget = kSegBudget) : blocks(segment_blocks(r, bps, budget)), rows(r) {}
     __device__ uint8_t* frag(uint8_t* smem) const { return smem + Layout::kSegOff; }
     __device__ uint32_t* minb(uint8_t* smem) const {
         return reinterpret_cast<uint32_t*>(smem + Layout::kSegOff + blocks * rows * kTokenBlockBytes);
@@ -347,6 +347,11 @@ __device__ __forceinline__ void grid_dependents_launch() {
 // segment's tokens. One warp per (block, token): lane L owns values
 // 8L..8L+7, which are the B registers b0 (k = 4t..4t+3 <-> values 8t..8t+3)
 // and b1 (k = 16+4t.. <-> values 8t+4..8t+7) of sub-block G = L/4, t = L%4.
+//
+// kQ6: the Q6_K kernel's operand order instead (m16n8k16, sub-blocks of 16):
+// words [block][sub-block s][token][h, l][t'] with t' = values 4t'..4t'+3 of
+// the sub-block, and no minimum-term operands.
+template <bool kQ6 = false>
 __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, size_t in, int blk0, int nblk) {
     const int rows = seg.rows;
     auto* frag = reinterpret_cast<uint32_t*>(seg.frag(smem));
@@ -417,15 +422,23 @@ __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, 
                 l[i] = __float_as_uint(r2.x), l[i + 1] = __float_as_uint(r2.y);
             }
             const int slot = blk * rows + tok;
-            uint32_t* dst = frag + slot * (kTokenBlockBytes / 4);
-            const int idx = (((G >> 1) * 4 + t) * 2) * 4 + (G & 1) * 2;  // part h; part l is +4
+            uint32_t* dst;
+            int idx;
+            if constexpr (kQ6) {
+                // Lane L: values 8L..8L+7 = words 2(L&1), 2(L&1)+1 of sub-block L/2.
+                dst = frag + blk * rows * (kTokenBlockBytes / 4);
+                idx = (((lane >> 1) * rows + tok) * 2) * 4 + 2 * (lane & 1);
+            } else {
+                dst = frag + slot * (kTokenBlockBytes / 4);
+                idx = (((G >> 1) * 4 + t) * 2) * 4 + (G & 1) * 2;  // part h; part l is +4
+            }
             dst[idx] = pack4(int(h[0]), int(h[1]), int(h[2]), int(h[3]));
             dst[idx + 1] = pack4(int(h[4]), int(h[5]), int(h[6]), int(h[7]));
             dst[idx + 4] = pack4(int(l[0]), int(l[1]), int(l[2]), int(l[3]));
             dst[idx + 5] = pack4(int(l[4]), int(l[5]), int(l[6]), int(l[7]));
             // Minimum term B' for lane (g, t') = sums of sub-blocks 2t', 2t'+1
             // (scaled by 1/256) split into fp16 hi and lo: written by lanes 8t'.
-            if ((lane & 7) == 0) {
+            if (!kQ6 && (lane & 7) == 0) {
                 const float s0 = sum[q] * (1.f / 256.f), s1 = next[q] * (1.f / 256.f);
                 const __half2 hi = __floats2half2_rn(s0, s1);
                 const float2 hf = __half22float2(hi);
@@ -436,6 +449,110 @@ __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, 
             }
             if (lane == 0)
                 scales[slot] = m[q] > 0.f ? m[q] / 127.f : 0.f;
+        }
+    }
+}
+
+// End of a piece, common to the K-quant kernels: sum the K-split warps of
+// each row group, then either publish the partial sums (head piece of a cut
+// tile), add the later pieces' sums in CTA order (tail piece), or write the
+// outputs (whole tile or tail piece). acc[nt][0/1]: rows my_row, my_row + 8
+// for token nt*4 + t.
+template <int NT, class Await>
+__device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc, const MmaJob& job, float (&acc)[NT][2],
+                                             int KS, int ks, int tid, uint32_t my_row, bool valid_lo, bool valid_hi,
+                                             uint32_t r0, int rows, float* red, int* abort_flag, Await& await_dependency) {
+    const int warp = tid >> 5, lane = tid & 31, t = lane & 3;
+    if (KS > 1) {
+        // Sum the K splits of each row group: warp (rg, 0) collects.
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            red[(nt * 2 + 0) * kConsumerThreads + tid] = acc[nt][0];
+            red[(nt * 2 + 1) * kConsumerThreads + tid] = acc[nt][1];
+        }
+        named_sync(1, kConsumerThreads);
+        if (ks == 0) {
+            for (int k = 1; k < KS; ++k) {
+                const int other = (warp + k) * 32 + lane;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    acc[nt][0] += red[(nt * 2 + 0) * kConsumerThreads + other];
+                    acc[nt][1] += red[(nt * 2 + 1) * kConsumerThreads + other];
+                }
+            }
+        }
+        named_sync(1, kConsumerThreads);
+    }
+    await_dependency();
+    bool write = ks == 0;
+    if (!pc.whole && pc.k0 > 0) {
+        // Head piece of a cut tile (R = 64, every warp holds final sums):
+        // store the partial sums; the fixup lanes publish them.
+        // store the tagged partial sums (the slot was zeroed by the previous
+        // launch, which finished before the grid-dependency wait).
+        unsigned long long* mine = p.partials + size_t(blockIdx.x) * kSlotFloats;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            store_relaxed(mine + (nt * 2 + 0) * kConsumerThreads + tid, tagged(acc[nt][0]));
+            store_relaxed(mine + (nt * 2 + 1) * kConsumerThreads + tid, tagged(acc[nt][1]));
+        }
+        write = false;
+    } else if (!pc.whole) {
+        // Tail piece holding the tile's first unit: add the later pieces'
+        // sums in CTA order as their tags appear, and zero the words for
+        // the next launch on this stream.
+        constexpr int kAhead = 4;  // CTAs whose words are in flight together
+        const uint32_t others = pc.c_last - pc.c_first;
+        for (uint32_t c0 = 0; c0 < others; c0 += kAhead) {
+            unsigned long long w[kAhead][NT][2];
+#pragma unroll
+            for (int q = 0; q < kAhead; ++q) {
+                const uint32_t c = pc.c_first + 1 + min(c0 + q, others - 1);
+                const unsigned long long* part = p.partials + size_t(c) * kSlotFloats;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    w[q][nt][0] = load_relaxed(part + (nt * 2 + 0) * kConsumerThreads + tid);
+                    w[q][nt][1] = load_relaxed(part + (nt * 2 + 1) * kConsumerThreads + tid);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < kAhead; ++q) {
+                if (c0 + q >= others)
+                    break;
+                unsigned long long* part = p.partials + size_t(pc.c_first + 1 + c0 + q) * kSlotFloats;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                    for (int hl = 0; hl < 2; ++hl) {
+                        unsigned long long* at = part + (nt * 2 + hl) * kConsumerThreads + tid;
+                        unsigned long long v = w[q][nt][hl];
+                        for (uint32_t poll = 0; (v >> 32) != 1ull; ++poll) {
+                            if (poll == wait_polls) {
+                                atomicOr(p.watchdog, watchdog_fixup);
+                                atomicExch(abort_flag, 1);
+                                break;
+                            }
+                            __nanosleep(32);
+                            v = load_relaxed(at);
+                        }
+                        acc[nt][hl] += __uint_as_float(uint32_t(v));
+                        store_relaxed(at, 0ull);
+                    }
+                }
+            }
+        }
+    }
+    if (write) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int tok = nt * 4 + t;
+            if (tok < rows) {
+                float* out = job.output + size_t(r0 + tok) * job.stride;
+                if (valid_lo)
+                    out[my_row] = acc[nt][0];
+                if (valid_hi)
+                    out[my_row + 8] = acc[nt][1];
+            }
         }
     }
 }
@@ -655,100 +772,268 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
         }
         if (check && !finite)
             atomicOr(job.status, 1u);
-        if (KS > 1) {
-            // Sum the K splits of each row group: warp (rg, 0) collects.
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                red[(nt * 2 + 0) * kConsumerThreads + tid] = acc[nt][0];
-                red[(nt * 2 + 1) * kConsumerThreads + tid] = acc[nt][1];
-            }
-            named_sync(1, kConsumerThreads);
-            if (ks == 0) {
-                for (int k = 1; k < KS; ++k) {
-                    const int other = (warp + k) * 32 + lane;
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        acc[nt][0] += red[(nt * 2 + 0) * kConsumerThreads + other];
-                        acc[nt][1] += red[(nt * 2 + 1) * kConsumerThreads + other];
-                    }
-                }
-            }
-            named_sync(1, kConsumerThreads);
-        }
-        await_dependency();
-        bool write = ks == 0;
-        if (!pc.whole && pc.k0 > 0) {
-            // Head piece of a cut tile (R = 64, every warp holds final sums):
-            // store the partial sums; the fixup lanes publish them.
-            // store the tagged partial sums (the slot was zeroed by the previous
-            // launch, which finished before the grid-dependency wait).
-            unsigned long long* mine = p.partials + size_t(blockIdx.x) * kSlotFloats;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                store_relaxed(mine + (nt * 2 + 0) * kConsumerThreads + tid, tagged(acc[nt][0]));
-                store_relaxed(mine + (nt * 2 + 1) * kConsumerThreads + tid, tagged(acc[nt][1]));
-            }
-            write = false;
-        } else if (!pc.whole) {
-            // Tail piece holding the tile's first unit: add the later pieces'
-            // sums in CTA order as their tags appear, and zero the words for
-            // the next launch on this stream.
-            constexpr int kAhead = 4;  // CTAs whose words are in flight together
-            const uint32_t others = pc.c_last - pc.c_first;
-            for (uint32_t c0 = 0; c0 < others; c0 += kAhead) {
-                unsigned long long w[kAhead][NT][2];
-#pragma unroll
-                for (int q = 0; q < kAhead; ++q) {
-                    const uint32_t c = pc.c_first + 1 + min(c0 + q, others - 1);
-                    const unsigned long long* part = p.partials + size_t(c) * kSlotFloats;
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        w[q][nt][0] = load_relaxed(part + (nt * 2 + 0) * kConsumerThreads + tid);
-                        w[q][nt][1] = load_relaxed(part + (nt * 2 + 1) * kConsumerThreads + tid);
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < kAhead; ++q) {
-                    if (c0 + q >= others)
-                        break;
-                    unsigned long long* part = p.partials + size_t(pc.c_first + 1 + c0 + q) * kSlotFloats;
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-                        for (int hl = 0; hl < 2; ++hl) {
-                            unsigned long long* at = part + (nt * 2 + hl) * kConsumerThreads + tid;
-                            unsigned long long v = w[q][nt][hl];
-                            for (uint32_t poll = 0; (v >> 32) != 1ull; ++poll) {
-                                if (poll == wait_polls) {
-                                    atomicOr(p.watchdog, watchdog_fixup);
-                                    atomicExch(abort_flag, 1);
-                                    break;
-                                }
-                                __nanosleep(32);
-                                v = load_relaxed(at);
-                            }
-                            acc[nt][hl] += __uint_as_float(uint32_t(v));
-                            store_relaxed(at, 0ull);
-                        }
-                    }
-                }
-            }
-        }
-        if (write) {
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const int tok = nt * 4 + t;
-                if (tok < rows) {
-                    float* out = job.output + size_t(r0 + tok) * job.stride;
-                    if (valid_lo)
-                        out[my_row] = acc[nt][0];
-                    if (valid_hi)
-                        out[my_row + 8] = acc[nt][1];
-                }
-            }
-        }
+        finish_piece<NT>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0, rows, red, abort_flag,
+                         await_dependency);
         // After an abort the remaining pieces still run (without waits or
         // MMAs) so that every cut tile's counter is re-armed.
+    }
+}
+
+// ------------------------------------------------------------------- Q6_K
+// Q6_K value: w = d * sc_s * (q - 32), q 6-bit (low 4 bits in ql, high 2 in
+// qh), sc_s int8 per sub-block of 16 (IW/include/kadan/gguf_quantization.hpp
+// decode of q6_k; ggml-common.h block_q6_K: ql[128], qh[64], scales[16], d).
+// Sub-block s = 8 ip + 2 qt + h holds values 128 ip + 32 qt + 16 h + i
+// (i < 16): low bits = nibble (qt >> 1) of ql[64 ip + 32 (qt & 1) + 16 h + i],
+// high bits = bits 2 qt..2 qt+1 of qh[32 ip + 16 h + i].
+//
+//   A operand : q - 32 as s8, built per 4 values with two masks, one add and
+//               one xor ((q + 96) ^ 128 = q - 32 mod 256, no carries since
+//               q + 96 < 256)
+//   MMA       : mma.m16n8k16.s8.s8 -> exact int32 sum over one sub-block
+//   scales    : I = sum_s sc_s C_s (IMAD, exact)
+//   epilogue  : acc += d * s_x * (I_h + I_l / 254)
+// A 210-byte block is not a whole number of 16-byte words, so the TMA unit
+// is a chunk of 8 blocks (1680 bytes) of 16 rows, one 2-D box per stage;
+// blocks at odd positions of a chunk start 2 bytes off a word boundary and
+// are read as half-word pairs.
+constexpr int kQ6Block = 210;
+constexpr int kQ6Chunk = 8;                       // blocks per TMA unit
+constexpr int kQ6Rows = 16;                       // rows per tile
+constexpr int kQ6StageBytes = kQ6Rows * kQ6Chunk * kQ6Block;  // 26880
+constexpr int kQ6SegBudget = 4 * kQ6Chunk * kTokenBlockTotal;  // one chunk of 4 tokens
+constexpr uint32_t kQ6MinUnitsPerCta = 2;
+
+struct Q6Layout {
+    static constexpr int kStagesOff = 0;
+    static constexpr int kSegOff = kStages * kQ6StageBytes;
+    static constexpr int kRedOff = kSegOff + kQ6SegBudget;
+    static constexpr int kRedBytes = kConsumerThreads * 4 * 4;
+    static constexpr int kBarOff = kRedOff + kRedBytes;
+    static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
+};
+static_assert(Q6Layout::kSegOff - Q6Layout::kStagesOff == 3 * kQ6StageBytes, "stage ring");
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)
+        ),
+        "l"(map),
+        "r"(c0),
+        "r"(c1),
+        "r"(smem_addr(bar))
+        : "memory"
+    );
+}
+
+// C = A(16x16 s8) * B(16x8 s8), exact int32.
+__device__ __forceinline__ void imma16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(0)
+    );
+}
+
+// 4 bytes at p: one word load when p is word aligned, else two half-words
+// (p is always 2-byte aligned here).
+template <bool kOdd> __device__ __forceinline__ uint32_t ld_word(const uint8_t* p) {
+    if constexpr (kOdd) {
+        const uint32_t lo = *reinterpret_cast<const uint16_t*>(p), hi = *reinterpret_cast<const uint16_t*>(p + 2);
+        return lo | (hi << 16);
+    } else {
+        return *reinterpret_cast<const uint32_t*>(p);
+    }
+}
+
+// One block of rows g (bg) and g + 8 (b8) for one n-tile of tokens: adds the
+// block's contribution to acc. bq: this lane's B words of the block, indexed
+// [(s * rows + tok) * 2 + part] * 4 + t.
+template <bool kOdd>
+__device__ __forceinline__ void q6k_block(const uint8_t* bg, const uint8_t* b8, const uint32_t* bq, int rows, int tokb,
+                                          int part, int t, float sc_tok, float (&acc)[2], bool& finite_g, bool& finite_8) {
+    const float dg = half_bits_to_float(*reinterpret_cast<const uint16_t*>(bg + 208));
+    const float d8 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b8 + 208));
+    finite_g = finite_g && isfinite(dg);
+    finite_8 = finite_8 && isfinite(d8);
+    uint32_t scg[4], sc8[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        scg[w] = ld_word<kOdd>(bg + 192 + 4 * w);
+        sc8[w] = ld_word<kOdd>(b8 + 192 + 4 * w);
+    }
+    int Ig[2] = {0, 0}, I8[2] = {0, 0};
+#pragma unroll
+    for (int ip = 0; ip < 2; ++ip)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int o = 64 * ip + 16 * h + 4 * t, oh = 128 + 32 * ip + 16 * h + 4 * t;
+            const uint32_t qa_g = ld_word<kOdd>(bg + o), qb_g = ld_word<kOdd>(bg + o + 32), qh_g = ld_word<kOdd>(bg + oh);
+            const uint32_t qa_8 = ld_word<kOdd>(b8 + o), qb_8 = ld_word<kOdd>(b8 + o + 32), qh_8 = ld_word<kOdd>(b8 + oh);
+#pragma unroll
+            for (int qt = 0; qt < 4; ++qt) {
+                const int sb = 8 * ip + 2 * qt + h;
+                const uint32_t ng = ((qt & 1) ? qb_g : qa_g) >> (4 * (qt >> 1));
+                const uint32_t n8 = ((qt & 1) ? qb_8 : qa_8) >> (4 * (qt >> 1));
+                // Bits 2qt, 2qt+1 of each qh byte moved to bits 4, 5.
+                const uint32_t hg = qt == 3 ? qh_g >> 2 : qh_g << (4 - 2 * qt);
+                const uint32_t h8 = qt == 3 ? qh_8 >> 2 : qh_8 << (4 - 2 * qt);
+                const uint32_t vg = (((ng & 0x0F0F0F0Fu) | (hg & 0x30303030u)) + 0x60606060u) ^ 0x80808080u;
+                const uint32_t v8 = (((n8 & 0x0F0F0F0Fu) | (h8 & 0x30303030u)) + 0x60606060u) ^ 0x80808080u;
+                const uint32_t b = bq[((sb * rows + tokb) * 2 + part) * 4 + t];
+                int C[4];
+                imma16(C, vg, v8, b);
+                const int sg = int(int8_t(scg[sb >> 2] >> (8 * (sb & 3))));
+                const int s8 = int(int8_t(sc8[sb >> 2] >> (8 * (sb & 3))));
+                Ig[0] += sg * C[0], Ig[1] += sg * C[1];
+                I8[0] += s8 * C[2], I8[1] += s8 * C[3];
+            }
+        }
+    acc[0] = fmaf(dg * sc_tok, fmaf(float(Ig[1]), 1.f / 254.f, float(Ig[0])), acc[0]);
+    acc[1] = fmaf(d8 * sc_tok, fmaf(float(I8[1]), 1.f / 254.f, float(I8[0])), acc[1]);
+}
+
+// Q6_K decode GEMV, T <= 4 input rows per pass. Tiles of 16 rows; a unit of
+// the balanced split is (tile, chunk of 8 blocks); each stage is one chunk,
+// its 8 blocks split over the 4 consumer warps (2 each), which add up in
+// shared memory at the end of a piece. Everything else (pieces, fixup,
+// programmatic dependent launch) is the Q4_K kernel's.
+template <int NT>
+__global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid_constant__ MmaParams p) {
+    using L = Q6Layout;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
+    auto* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+    auto* empty = full + kStages;
+    auto* abort_flag = reinterpret_cast<int*>(empty + kStages);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int KS = kWarps;
+    auto* red = reinterpret_cast<float*>(smem + L::kRedOff);
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+        grid_dependents_launch();
+    }
+    __syncthreads();
+
+    if (warp == kWarps) {
+        // ------------------------------ producer ------------------------------
+        if (lane != 0)
+            return;
+        uint32_t it = 0;
+        PieceIter pieces(p);
+        Piece pc;
+        while (pieces.next(p, pc)) {
+            const MmaJob& job = p.jobs[pc.job];
+            const int row0 = int((pc.tile / job.row_groups) * uint32_t(kQ6Rows));
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&job.map) : "memory");
+            for (uint32_t ch = pc.k0; ch < pc.k1; ++ch, ++it) {
+                const int slot = int(it % kStages);
+                if (it >= kStages && !mbar_wait(&empty[slot], ((it / kStages) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog))
+                    atomicExch(abort_flag, 1);
+                if (*reinterpret_cast<volatile int*>(abort_flag))
+                    goto drain;
+                // The whole box lands (rows and blocks past the matrix are zero-filled).
+                mbar_expect_tx(&full[slot], uint32_t(kQ6StageBytes));
+                tma_load_2d(smem + L::kStagesOff + slot * kQ6StageBytes, &job.map, int(ch) * (kQ6Chunk * kQ6Block / 8),
+                            row0, &full[slot]);
+            }
+        }
+    drain:
+        for (uint32_t k = 0; k < kStages && k < it; ++k) {
+            const uint32_t last = it - 1 - k;
+            mbar_wait(&full[last % kStages], (last / kStages) & 1u, watchdog_drain, p.watchdog);
+        }
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
+    bool dependency_met = false;
+    auto await_dependency = [&] {
+        if (!dependency_met) {
+            grid_dependency_wait();
+            dependency_met = true;
+        }
+    };
+    const int g = lane >> 2, t = lane & 3, ks = warp;
+    uint32_t it = 0;
+    const float* seg_x = nullptr;
+    int seg_rows = -1, seg_blk0 = -1, seg_nblk = 0;
+    PieceIter pieces(p);
+    Piece pc;
+    while (pieces.next(p, pc)) {
+        const MmaJob& job = p.jobs[pc.job];
+        const uint32_t row0 = (pc.tile / job.row_groups) * uint32_t(kQ6Rows);
+        const uint32_t r0 = (pc.tile % job.row_groups) * job.group_rows;
+        const int rows = int(min(job.group_rows, job.rows - r0));
+        const int nblocks = int(job.in / 256);
+        const float* x = job.input + size_t(r0) * job.in;
+        const Segment seg(rows, kQ6Chunk, kQ6SegBudget);
+        if (seg.blocks < kQ6Chunk)
+            atomicExch(abort_flag, 1);
+        const uint32_t* frag = reinterpret_cast<const uint32_t*>(seg.frag(smem));
+        const float* scales = seg.scales(smem);
+        const uint32_t my_row = row0 + g;
+        const bool valid_lo = my_row < job.columns, valid_hi = my_row + 8 < job.columns;
+        const bool check = job.status != nullptr;
+        bool finite_g = true, finite_8 = true;
+        float acc[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            acc[nt][0] = acc[nt][1] = 0.f;
+
+        for (uint32_t ch = pc.k0; ch < pc.k1; ++ch, ++it) {
+            const int slot = int(it % kStages);
+            const int blk_first = int(ch) * kQ6Chunk;
+            const int nb = min(kQ6Chunk, nblocks - blk_first);
+            if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
+                && seg.blocks >= kQ6Chunk) {
+                const int count = min(seg.blocks, nblocks - blk_first);
+                await_dependency();
+                named_sync(1, kConsumerThreads);
+                prep_segment<true>(smem, seg, x, job.in, blk_first, count);
+                named_sync(1, kConsumerThreads);
+                seg_x = x, seg_rows = rows, seg_blk0 = blk_first, seg_nblk = count;
+            }
+            const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
+            if (!aborted && !mbar_wait(&full[slot], (it / kStages) & 1u, watchdog_full_barrier, p.watchdog))
+                atomicExch(abort_flag, 1);
+            if (!aborted) {
+                const uint8_t* stage = smem + L::kStagesOff + slot * kQ6StageBytes;
+#pragma unroll
+                for (int bb = 0; bb < 2; ++bb) {
+                    const int b = 2 * ks + bb;  // block of the chunk; odd b sits 2 bytes off a word
+                    if (b >= nb)
+                        break;
+                    const int sblk = blk_first + b - seg_blk0;
+                    const uint8_t* bg = stage + g * (kQ6Chunk * kQ6Block) + b * kQ6Block;
+                    const uint8_t* b8 = bg + 8 * (kQ6Chunk * kQ6Block);
+                    const uint32_t* bq = frag + sblk * rows * (kTokenBlockBytes / 4);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const int tokb = min(nt * 4 + (g >> 1), rows - 1);
+                        const float sc_tok = scales[sblk * rows + min(nt * 4 + t, rows - 1)];
+                        if (bb)
+                            q6k_block<true>(bg, b8, bq, rows, tokb, g & 1, t, sc_tok, acc[nt], finite_g, finite_8);
+                        else
+                            q6k_block<false>(bg, b8, bq, rows, tokb, g & 1, t, sc_tok, acc[nt], finite_g, finite_8);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&empty[slot]);
+        }
+        if (check && !((finite_g || !valid_lo) && (finite_8 || !valid_hi)))
+            atomicOr(job.status, 1u);
+        finish_piece<NT>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0, rows, red, abort_flag,
+                         await_dependency);
     }
 }
 
@@ -860,6 +1145,26 @@ const Tuning& tuning() {
     return t;
 }
 
+int q6k_slots() {
+    static int blocks_per_sm[64] = {};
+    static std::mutex lock;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    constexpr int smem = Q6Layout::kTotal + 128;
+    std::lock_guard<std::mutex> guard(lock);
+    if (!blocks_per_sm[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess)
+            return -cuda_fail(e, "gemv_q6k_mma_kernel attribute");
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_mma_kernel<1>, kThreadsQ, smem);
+        if (e != cudaSuccess)
+            return -cuda_fail(e, "gemv_q6k_mma_kernel occupancy");
+        blocks_per_sm[dev] = n > 0 ? n : 1;
+    }
+    return sm_count() * blocks_per_sm[dev];
+}
+
 template <int NT> int launch_q4k(const MmaParams& p, uint32_t grid, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -890,9 +1195,102 @@ void clear_gemv_fixups() {
     cudaDeviceSynchronize();
 }
 
-bool q4k_mma_eligible(const kb200_gemv_job& j) {
-    return j.encoding == KB200_Q4_K && aligned(j.weights, 16) && j.row_bytes % 16 == 0 && j.in % 256 == 0
-           && j.row_bytes >= size_t(j.in) / 256 * 144 && j.stride <= 0xffffffffu && encode_fn() != nullptr;
+bool q6k_mma_enabled() {
+    static const bool on = [] {
+        const char* s = std::getenv("KB200_GEMV_Q6K_MMA");
+        return !s || std::atoi(s) != 0;
+    }();
+    return on;
+}
+
+bool mma_eligible(const kb200_gemv_job& j) {
+    if (!aligned(j.weights, 16) || j.row_bytes % 16 || j.in % 256 || j.stride > 0xffffffffu || !encode_fn())
+        return false;
+    if (j.encoding == KB200_Q4_K)
+        return j.row_bytes >= size_t(j.in) / 256 * 144;
+    if (j.encoding == KB200_Q6_K)
+        return q6k_mma_enabled() && j.row_bytes >= size_t(j.in) / 256 * kQ6Block;
+    return false;
+}
+
+// Q6_K: 16-row tiles, units of (tile, chunk of 8 blocks), up to 4 input rows
+// per pass (more rows become row groups), balanced split when whole tiles
+// would leave a tenth of the CTA slots idle.
+int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream) {
+    auto encode = encode_fn();
+    if (!encode)
+        return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
+    constexpr uint32_t group_rows = 4;
+    int slots = q6k_slots();
+    if (slots <= 0)
+        return -slots;
+    if (tuning().ctas_per_sm > 0)
+        slots = std::min(slots, sm_count() * tuning().ctas_per_sm);
+    const Fixup* fixup = tuning().balanced ? fixup_for(stream) : nullptr;
+    for (size_t first = 0; first < jobs.size(); first += kMaxJobsQ) {
+        const size_t n = std::min(jobs.size() - first, size_t(kMaxJobsQ));
+        MmaParams p;
+        std::memset(&p, 0, sizeof(p));
+        p.watchdog = watchdog_word();
+        p.tile_rows = kQ6Rows;
+        uint32_t tiles = 0, units = 0;
+        for (size_t m = 0; m < n; ++m) {
+            const auto& j = *jobs[first + m];
+            MmaJob& d = p.jobs[m];
+            // Rows as u64 words (the pitch is a multiple of 16 bytes); one box
+            // is 8 blocks (210 words) of 16 rows.
+            const cuuint64_t dims[2] = {j.row_bytes / 8, j.columns};
+            const cuuint64_t strides[1] = {j.row_bytes};
+            const cuuint32_t box[2] = {kQ6Chunk * kQ6Block / 8, kQ6Rows};
+            const cuuint32_t estr[2] = {1, 1};
+            const CUresult r = encode(&d.map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(j.weights), dims,
+                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS)
+                return fail(KB200_INVALID, "cuTensorMapEncodeTiled rejected a Q6_K job");
+            d.input = j.input;
+            d.output = j.output;
+            d.status = j.status;
+            d.stride = uint32_t(j.stride);
+            d.in = j.in;
+            d.columns = j.columns;
+            d.rows = j.rows;
+            d.nblocks = (j.in / 256 + kQ6Chunk - 1) / kQ6Chunk;  // units (chunks) per tile
+            d.group_rows = group_rows;
+            d.row_groups = (j.rows + group_rows - 1) / group_rows;
+            d.first_tile = tiles;
+            d.first_unit = units;
+            const uint32_t job_tiles = (j.columns + kQ6Rows - 1) / kQ6Rows * d.row_groups;
+            tiles += job_tiles;
+            units += job_tiles * d.nblocks;
+        }
+        p.count = uint32_t(n);
+        p.total_tiles = tiles;
+        const uint64_t waves = (tiles + uint64_t(slots) - 1) / uint64_t(slots);
+        const bool ragged = uint64_t(tiles) * 10 < waves * uint64_t(slots) * 9;
+        const bool balanced = fixup && fixup->ctas >= uint32_t(slots) && ragged
+                              && uint64_t(units) >= uint64_t(kQ6MinUnitsPerCta) * uint64_t(slots);
+        uint32_t grid = std::min(tiles, uint32_t(slots));
+        if (balanced) {
+            grid = std::min(units, uint32_t(slots));
+            p.total_units = units;
+            p.partials = fixup->partials;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kThreadsQ);
+        cfg.dynamicSmemBytes = Q6Layout::kTotal + 128;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1>, p);
+        if (e != cudaSuccess)
+            return cuda_fail(e, "gemv_q6k_mma_kernel launch");
+    }
+    return KB200_OK;
 }
 
 int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream) {
@@ -1008,6 +1406,12 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             return s;
     }
     return KB200_OK;
+}
+
+int launch_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream) {
+    if (jobs.empty())
+        return KB200_OK;
+    return jobs.front()->encoding == KB200_Q6_K ? launch_q6k_mma(jobs, stream) : launch_q4k_mma(jobs, stream);
 }
 
 }  // namespace kb200

@@ -274,3 +274,49 @@ def test_q4k_streams_share_nothing(kb, cuda):
         kb.gguf_gemv_batch([jb], stream=s2)
     torch.cuda.synchronize()
     assert torch.equal(ya, ref_a) and torch.equal(yb, ref_b)
+
+
+@pytest.mark.parametrize("in_,out,rows", [(8192, 40, 1), (3584, 131, 1), (1024, 8192, 1), (256, 33, 3), (28672, 64, 2),
+                                          (8192, 1280, 4), (14336, 17, 5), (2048, 4096, 8), (4096, 29, 7)])
+def test_q6k_tensor_pipe_parity(kb, oracle, cuda, in_, out, rows):
+    """Q6_K on the integer tensor pipe: rows padded to a 16-byte pitch (as the
+    tensor-parallel shards are), chunks of 8 blocks with ragged last chunks,
+    up to 4 input rows per pass and row groups beyond, balanced and
+    whole-tile launches."""
+    import torch
+
+    from kadan_b200 import synth
+    from kadan_b200.tensor_parallel import pad_rows
+
+    w = synth.q6_k(out, in_, seed=in_ + out + rows)
+    pitch = (w.shape[1] + 15) // 16 * 16
+    wd = to_dev(pad_rows(w, pitch), cuda)
+    x = synth.activations(rows * in_, seed=rows + 3, dtype="bf16").reshape(rows, in_)
+    y = torch.full((rows, out), float("nan"), device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    job = kb.gemv_job(kb.Q6_K, wd, to_dev(x, cuda), y, in_=in_, columns=out, rows=rows, row_bytes_=pitch,
+                      status=status)
+    assert kb.gemv_path(job) == 2
+    kb.gguf_gemv_batch([job])
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), oracle.gemv_f64(kb.Q6_K, w, x, in_, out)) <= TOL
+    assert status.item() == 0
+    assert kb.take_device_error() == 0
+
+
+def test_q6k_tensor_pipe_nonfinite_scale_sets_status(kb, cuda):
+    import torch
+
+    from kadan_b200 import synth
+
+    in_, out = 2048, 48
+    w = synth.q6_k(out, in_, seed=1)
+    w.reshape(-1, 210)[5 * (in_ // 256) + 3, 208:210] = np.array([0x7C00], dtype=np.uint16).view(np.uint8)  # +inf d
+    x = synth.activations(in_, seed=2).reshape(1, in_)
+    y = torch.zeros(1, out, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    job = kb.gemv_job(kb.Q6_K, to_dev(w, cuda), to_dev(x, cuda), y, in_=in_, columns=out, rows=1, status=status)
+    assert kb.gemv_path(job) == 2
+    kb.gguf_gemv_batch([job])
+    torch.cuda.synchronize()
+    assert status.item() == 1
