@@ -164,12 +164,14 @@ __host__ __device__ constexpr int segment_blocks(int rows, int bps, int budget =
     return budget / (rows * kTokenBlockTotal) / bps * bps;
 }
 
+// off: byte offset of the segment buffer in the kernel's shared memory.
 struct Segment {
-    int blocks, rows;
-    __device__ Segment(int r, int bps, int budget = kSegBudget) : blocks(segment_blocks(r, bps, budget)), rows(r) {}
-    __device__ uint8_t* frag(uint8_t* smem) const { return smem + Layout::kSegOff; }
+    int blocks, rows, off;
+    __device__ Segment(int r, int bps, int budget = kSegBudget, int offset = Layout::kSegOff)
+        : blocks(segment_blocks(r, bps, budget)), rows(r), off(offset) {}
+    __device__ uint8_t* frag(uint8_t* smem) const { return smem + off; }
     __device__ uint32_t* minb(uint8_t* smem) const {
-        return reinterpret_cast<uint32_t*>(smem + Layout::kSegOff + blocks * rows * kTokenBlockBytes);
+        return reinterpret_cast<uint32_t*>(smem + off + blocks * rows * kTokenBlockBytes);
     }
     __device__ float* scales(uint8_t* smem) const {
         return reinterpret_cast<float*>(minb(smem) + blocks * rows * (kMinBytes / 4));
@@ -974,7 +976,7 @@ __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid
         const int rows = int(min(job.group_rows, job.rows - r0));
         const int nblocks = int(job.in / 256);
         const float* x = job.input + size_t(r0) * job.in;
-        const Segment seg(rows, kQ6Chunk, kQ6SegBudget);
+        const Segment seg(rows, kQ6Chunk, kQ6SegBudget, L::kSegOff);
         if (seg.blocks < kQ6Chunk)
             atomicExch(abort_flag, 1);
         const uint32_t* frag = reinterpret_cast<const uint32_t*>(seg.frag(smem));
