@@ -350,9 +350,10 @@ KB200_API int kb200_rows_regroup(const void* src, void* dst, size_t row_bytes, c
  * on the host (gguf_batch_partition.hpp:48-59). Row-parallel projections
  * here leave each GPU a partial sum of the whole output, which
  * kb200_peer_allreduce_f32 adds over the ranks in one kernel: every rank
- * stores its chunks into every peer's buffer over NVLink, flags them with a
- * system-scope release, waits (bounded by timeout_s) for the peers' flags
- * and sums in rank order, so all ranks hold the same bits.
+ * stores its values, each tagged with the call's epoch in one 64-bit word,
+ * into every peer's buffer over NVLink, reads the peers' words for the same
+ * elements until their tags match (bounded by timeout_s) and sums in rank
+ * order, so all ranks hold the same bits. count: even; data 8-byte aligned.
  *
  * Setup: each rank allocates kb200_peer_buffer_bytes(world, max_count) with
  * kb200_device_alloc (zeroed), exports it with kb200_ipc_handle, sends the

@@ -2,29 +2,30 @@
 //
 // Tensor-parallel decode adds the row-parallel projections' partial outputs
 // across ranks twice per layer (after o and after down): T x hidden fp32,
-// 32 KB at T = 1. At that size a library all-reduce is bound by its
-// protocol's latency, not by NVLink bandwidth. Here every rank's buffer is
-// mapped into every other rank's address space (CUDA IPC, one process per
-// GPU), and one kernel does the exchange:
+// 32 KB at T = 1. At that size an all-reduce is bound by latency, not by
+// NVLink bandwidth. Every rank's exchange buffer is mapped into every other
+// rank's address space (CUDA IPC, one process per GPU) and one kernel does
+// the exchange with self-validating words:
 //
-//   CTA c of every rank owns chunk c of the vector. It stores its chunk into
-//   slot [rank] of every peer's receive area (plain peer stores over NVLink),
-//   then publishes flag [rank][c] = epoch at each peer with a system-scope
-//   release. It waits (acquire, bounded by a time limit) until every peer's
-//   flag [src][c] in its own buffer shows the epoch, and sums the chunk over
-//   ranks in rank order 0..N-1, so every rank gets the same bits.
+//   each float travels as one 64-bit word {epoch, value bits}; a thread
+//   stores its elements into slot [rank] of every peer's buffer (plain
+//   64-bit stores over NVLink, two per 16-byte vector), then reads the same
+//   elements from every peer's slot in its own buffer until their epoch
+//   halves show this call, and sums over ranks in rank order 0..N-1, so all
+//   ranks hold the same bits. A 64-bit access is single-copy atomic, so a
+//   word with the right epoch carries the right value: no fence and no
+//   separate flag are needed, and no thread waits for another.
 //
 // The epoch is the number of the call, counted on the device (a graph replay
-// needs no new parameters; every rank makes the same calls). Receive areas
-// and flags alternate between two banks by epoch parity: a rank's call k
-// starts after its call k-1 finished, for which CTA 0 saw every peer's call
-// k-1 flag, so every peer has finished call k-2 and reads bank (k-1)&1 at
-// most; call k writes bank k&1.
+// needs no new parameters; every rank makes the same calls). Receive slots
+// alternate between two banks by epoch parity: a rank's call k starts after
+// its call k-1 finished, for which it read every peer's call k-1 words, so
+// every peer has finished call k-2 and reads bank (k-1)&1 at most while call
+// k writes bank k&1.
 //
 // Buffer of one rank (same layout on every rank, zeroed at allocation):
-//   flags  [2][kMaxRanks][kMaxCtas] u32   written by peers
-//   epochs [kMaxCtas] u32                 this rank's call counters
-//   data   [2][kMaxRanks][max_count] f32  written by peers
+//   epochs [kMaxCtas] u32                     this rank's call counters
+//   words  [2][kMaxRanks][max_count] u64      written by peers
 // No TMA and no multicast: peer memory is only touched by plain loads and
 // stores.
 #include <algorithm>
@@ -39,37 +40,28 @@ namespace {
 constexpr int kMaxRanks = 8;
 constexpr int kMaxCtas = 256;
 constexpr int kArThreads = 256;
-constexpr size_t kChunkFloats = 1024;
-constexpr size_t kFlagsBytes = size_t(2) * kMaxRanks * kMaxCtas * 4;
-constexpr size_t kEpochOff = kFlagsBytes;
-constexpr size_t kDataOff = (kEpochOff + kMaxCtas * 4 + 255) / 256 * 256;
-constexpr unsigned watchdog_peer = 16u;  // a peer's chunk never arrived
+constexpr size_t kWordsOff = 4096;  // after the epoch counters
+constexpr unsigned watchdog_peer = 16u;  // a peer's words never arrived
 
 struct ArParams {
     uint8_t* peers[kMaxRanks];  // every rank's buffer, this rank's included
     float* data;                // in/out, count floats
-    size_t count, max_count, per_cta;
+    size_t count, max_count;
     int rank, world;
     unsigned long long timeout_ns;
     unsigned* watchdog;
 };
 
-__device__ __forceinline__ uint32_t* flag_at(uint8_t* base, uint32_t bank, int src, int cta) {
-    return reinterpret_cast<uint32_t*>(base) + (size_t(bank) * kMaxRanks + src) * kMaxCtas + cta;
+__device__ __forceinline__ unsigned long long* words_at(uint8_t* base, uint32_t bank, int src, size_t max_count) {
+    return reinterpret_cast<unsigned long long*>(base + kWordsOff) + (size_t(bank) * kMaxRanks + src) * max_count;
 }
 
-__device__ __forceinline__ float* data_at(uint8_t* base, uint32_t bank, int src, size_t max_count) {
-    return reinterpret_cast<float*>(base + kDataOff) + (size_t(bank) * kMaxRanks + src) * max_count;
+__device__ __forceinline__ void store_pair(unsigned long long* at, unsigned long long a, unsigned long long b) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(at), "l"(a), "l"(b) : "memory");
 }
 
-__device__ __forceinline__ void store_release_sys(uint32_t* at, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(at), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* at) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(at) : "memory");
-    return v;
+__device__ __forceinline__ void load_pair(const unsigned long long* at, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(at) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -80,69 +72,66 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(const __grid_constant__ ArParams p) {
     __shared__ uint32_t epoch_s;
-    __shared__ int ok_s;
     const int c = blockIdx.x, tid = threadIdx.x;
     // The partial sums come from the previous kernel of the stream.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     uint8_t* mine = p.peers[p.rank];
-    uint32_t* epochs = reinterpret_cast<uint32_t*>(mine + kEpochOff);
-    if (tid == 0) {
+    uint32_t* epochs = reinterpret_cast<uint32_t*>(mine);
+    if (tid == 0)
         epoch_s = epochs[c] + 1u;
-        ok_s = 1;
-    }
     __syncthreads();
     // Every counter holds the number of calls so far, whatever the grid size
     // of each call: this CTA advances counters c, c + grid, c + 2 grid, ...
-    for (int i = c + int(gridDim.x) * tid; i < kMaxCtas && tid < kMaxCtas; i += int(gridDim.x) * kArThreads)
+    for (int i = c + int(gridDim.x) * tid; i < kMaxCtas; i += int(gridDim.x) * kArThreads)
         epochs[i] = epoch_s;
     const uint32_t e = epoch_s, bank = e & 1u;
-    const size_t begin = size_t(c) * p.per_cta, end = min(p.count, begin + p.per_cta);
-    const size_t v0 = begin / 4, v1 = end / 4;  // float4 index range (count and per_cta are multiples of 4)
-    const float4* src = reinterpret_cast<const float4*>(p.data);
+    const unsigned long long tag = (unsigned long long)e << 32;
+    auto* pairs = reinterpret_cast<float2*>(p.data);
+    const size_t npairs = p.count / 2;
+    const size_t stride = size_t(gridDim.x) * kArThreads;
 
-    // 1. Push this rank's chunk into slot [rank] of every peer.
-    for (int q = 0; q < p.world; ++q) {
-        if (q == p.rank)
-            continue;
-        float4* dst = reinterpret_cast<float4*>(data_at(p.peers[q], bank, p.rank, p.max_count));
-        for (size_t i = v0 + tid; i < v1; i += kArThreads)
-            dst[i] = src[i];
+    // 1. Push: this rank's elements into slot [rank] of every peer.
+    for (size_t i = size_t(c) * kArThreads + tid; i < npairs; i += stride) {
+        const float2 v = pairs[i];
+        const unsigned long long w0 = tag | __float_as_uint(v.x), w1 = tag | __float_as_uint(v.y);
+        for (int q = 0; q < p.world; ++q)
+            if (q != p.rank)
+                store_pair(words_at(p.peers[q], bank, p.rank, p.max_count) + 2 * i, w0, w1);
     }
-    __threadfence_system();
-    __syncthreads();
-    if (tid < p.world && tid != p.rank)
-        store_release_sys(flag_at(p.peers[tid], bank, p.rank, c), e);
-
-    // 2. Wait for every peer's chunk (one thread per source, bounded).
-    if (tid < p.world && tid != p.rank) {
-        const uint32_t* flag = flag_at(mine, bank, tid, c);
-        const unsigned long long start = global_ns();
-        while (load_acquire_sys(flag) != e) {
-            if (global_ns() - start > p.timeout_ns) {
-                atomicOr(p.watchdog, watchdog_peer);
-                ok_s = 0;
-                break;
-            }
-            __nanosleep(64);
-        }
-    }
-    __syncthreads();
-    if (!ok_s)
-        return;
-
-    // 3. Sum over ranks in rank order; this rank's term is its own data.
-    float4* out = reinterpret_cast<float4*>(p.data);
-    for (size_t i = v0 + tid; i < v1; i += kArThreads) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    // 2. Gather the same elements from every peer's slot and sum in rank order.
+    bool ok = true;
+    for (size_t i = size_t(c) * kArThreads + tid; i < npairs; i += stride) {
+        const float2 own = pairs[i];
+        float2 acc = make_float2(0.f, 0.f);
         for (int s = 0; s < p.world; ++s) {
-            const float4 v = s == p.rank ? src[i] : reinterpret_cast<const float4*>(data_at(mine, bank, s, p.max_count))[i];
+            float2 v = own;
+            if (s != p.rank) {
+                const unsigned long long* at = words_at(mine, bank, s, p.max_count) + 2 * i;
+                unsigned long long a, b;
+                load_pair(at, a, b);
+                if ((a >> 32) != e || (b >> 32) != e) {
+                    const unsigned long long start = global_ns();
+                    do {
+                        if (!ok || global_ns() - start > p.timeout_ns) {
+                            ok = false;
+                            break;
+                        }
+                        __nanosleep(32);
+                        load_pair(at, a, b);
+                    } while ((a >> 32) != e || (b >> 32) != e);
+                }
+                v = make_float2(__uint_as_float(uint32_t(a)), __uint_as_float(uint32_t(b)));
+            }
             if (s == 0)
                 acc = v;
             else
-                acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+                acc.x += v.x, acc.y += v.y;
         }
-        out[i] = acc;
+        if (ok)
+            pairs[i] = acc;
     }
+    if (!ok)
+        atomicOr(p.watchdog, watchdog_peer);
 }
 
 }  // namespace
@@ -155,7 +144,7 @@ extern "C" {
 size_t kb200_peer_buffer_bytes(int world, size_t max_count) {
     if (world < 1 || world > kMaxRanks)
         return 0;
-    return kDataOff + size_t(2) * kMaxRanks * max_count * sizeof(float);
+    return kWordsOff + size_t(2) * kMaxRanks * max_count * sizeof(unsigned long long);
 }
 
 int kb200_device_alloc(size_t bytes, void** ptr) {
@@ -212,8 +201,8 @@ int kb200_peer_allreduce_f32(float* data, size_t count, void* const* peers, int 
         return KB200_OK;
     if (!data || !peers)
         return fail(KB200_INVALID, "null pointer");
-    if (count % 4 || !aligned(data, 16) || count > max_count)
-        return fail(KB200_INVALID, "count must be a multiple of 4 floats within the buffer, data 16-byte aligned");
+    if (count % 2 || !aligned(data, 8) || count > max_count || max_count % 2)
+        return fail(KB200_INVALID, "count must be an even number of floats within the buffer, data 8-byte aligned");
     ArParams p;
     std::memset(&p, 0, sizeof(p));
     for (int r = 0; r < world; ++r) {
@@ -221,8 +210,7 @@ int kb200_peer_allreduce_f32(float* data, size_t count, void* const* peers, int 
             return fail(KB200_INVALID, "peer buffers must be 256-byte aligned");
         p.peers[r] = static_cast<uint8_t*>(peers[r]);
     }
-    const size_t ctas = std::min<size_t>(kMaxCtas, (count + kChunkFloats - 1) / kChunkFloats);
-    p.per_cta = ((count + ctas - 1) / ctas + 3) / 4 * 4;
+    const size_t ctas = std::min<size_t>(kMaxCtas, (count / 2 + kArThreads - 1) / kArThreads);
     p.data = data;
     p.count = count;
     p.max_count = max_count;
@@ -231,7 +219,7 @@ int kb200_peer_allreduce_f32(float* data, size_t count, void* const* peers, int 
     p.timeout_ns = static_cast<unsigned long long>(std::max(0.001, timeout_s) * 1e9);
     p.watchdog = watchdog_word();
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned((count + p.per_cta - 1) / p.per_cta));
+    cfg.gridDim = dim3(unsigned(ctas));
     cfg.blockDim = dim3(kArThreads);
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
