@@ -91,18 +91,16 @@ struct alignas(64) MmaJob {
 constexpr int kSlotFloats = 2 * 2 * kConsumerThreads;
 // Dynamic split limits (one scheduling buffer per device and stream).
 constexpr uint32_t kMaxGrid = 1024;     // CTAs of one launch
-constexpr uint32_t kMaxGrains = 8192;   // grains of one launch
-constexpr uint32_t kMaxTiles = 16384;   // tiles of one launch
+constexpr uint32_t kMaxGrains = 4096;   // grains of one launch
 constexpr uint32_t kGrainEnd = 0xffffffffu;
 constexpr int kGrainRing = 8;           // grain ids in flight from producer to consumers
 
 // Device memory of the dynamic split, zeroed when allocated; every launch
 // leaves it as it found it except for the launch counters.
 struct Sched {
-    unsigned* epochs;    // [kMaxGrid] dynamic launches so far on this stream
-    unsigned* tickets;   // [2] grain tickets, by launch parity
-    unsigned* counters;  // [kMaxTiles][kConsumerThreads] finished pieces of a cut tile
-    float* partials;     // [kMaxGrains][2][kSlotFloats] partial sums of cut pieces
+    unsigned* epochs;              // [kMaxGrid] dynamic launches so far on this stream
+    unsigned* tickets;             // [2] grain tickets, by launch parity
+    unsigned long long* partials;  // [kMaxGrains][2][kSlotFloats] tagged partial sums of cut pieces
 };
 
 struct MmaParams {
@@ -116,16 +114,20 @@ struct MmaParams {
     unsigned* watchdog;
 };
 
-__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* at, unsigned v) {
-    unsigned old;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(at), "r"(v) : "memory");
-    return old;
+// Relaxed 64-bit global accesses: single-copy atomic, so a partial sum and
+// its "present" tag, stored as one word, are seen together or not at all.
+__device__ __forceinline__ void store_relaxed(unsigned long long* at, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(at), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ float load_relaxed_f32(const float* at) {
-    float v;
-    asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(at) : "memory");
+__device__ __forceinline__ unsigned long long load_relaxed(const unsigned long long* at) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(at) : "memory");
     return v;
+}
+
+__device__ __forceinline__ unsigned long long tagged(float v) {
+    return (1ull << 32) | __float_as_uint(v);
 }
 
 // A contiguous run of one tile's units [k0, k1) (super-blocks; Q6_K: chunks).
@@ -267,8 +269,13 @@ __device__ void produce_pieces(const MmaParams& p, const GrainRing& ring, Stream
     };
     unsigned* ticket = nullptr;
     bool ok = true;
+    uint32_t next = 0;
     for (uint32_t grain = blockIdx.x; ok && grain < p.total_grains;) {
         push(grain);
+        // Draw the following grain now: the ticket's round trip then
+        // overlaps this grain's stages instead of stalling the ring.
+        if (ticket)
+            next = gridDim.x + atomicAdd(ticket, 1u);
         PieceIter pieces(p, grain);
         Piece pc;
         while (ok && pieces.next(p, pc))
@@ -286,8 +293,9 @@ __device__ void produce_pieces(const MmaParams& p, const GrainRing& ring, Stream
             ticket = p.sched.tickets + (id & 1u);
             if (blockIdx.x == 0)
                 p.sched.tickets[(id + 1u) & 1u] = 0u;
+            next = gridDim.x + atomicAdd(ticket, 1u);
         }
-        grain = gridDim.x + atomicAdd(ticket, 1u);
+        grain = next;
     }
     push(kGrainEnd);
 }
@@ -501,8 +509,8 @@ __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, 
 }
 
 // End of a piece, common to the K-quant kernels: sum the K-split warps of
-// each row group, then write the outputs (whole tile), or count the piece of
-// a cut tile and, for the piece that completes it, add all pieces' sums and
+// each row group, then write the outputs (whole tile), or publish the sums of
+// a piece of a cut tile, or (the tile's last grain) add all pieces' sums and
 // write. acc[nt][0/1]: rows my_row, my_row + 8 for token nt*4 + t.
 template <int NT, class Await>
 __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc, const MmaJob& job, float (&acc)[NT][2],
@@ -534,36 +542,57 @@ __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc
         return;  // the warps of K split 0 hold the row group's sums
     bool write = true;
     if (!pc.whole) {
-        // A cut tile: store this piece's sums in its grain's slot, count the
-        // piece on this thread's counter of the tile (release), and the
-        // thread that completes the count (acquire) adds every piece's sums
-        // in grain order, so the result does not depend on timing, writes
-        // the outputs and re-arms the counter for the next launch. A grain
-        // spans at most two tiles: slot 1 holds its piece of the second.
+        // A cut tile: the pieces come from grains gf..gl, and a grain spans
+        // at most two tiles (slot 1 holds its piece of the second). Every
+        // piece but the last grain's stores its sums as tagged words in its
+        // slot (the slot is zero between launches); the last grain's piece,
+        // usually the last to finish, adds them in grain order as their tags
+        // appear, then its own, so the result does not depend on timing, and
+        // zeroes the words for the next launch on this stream.
         const uint32_t W = p.grain_units, nb = job.nblocks;
         const uint32_t gf = pc.x0 / W, gl = (pc.x0 + nb - 1) / W;
-        float* slots = p.sched.partials;
-        float* mine = slots + (size_t(pc.grain) * 2 + (pc.grain * W < pc.x0 ? 1 : 0)) * kSlotFloats;
+        auto slot_of = [&](uint32_t gr) {
+            return p.sched.partials + (size_t(gr) * 2 + (gr * W < pc.x0 ? 1 : 0)) * kSlotFloats;
+        };
+        if (pc.grain != gl) {
+            unsigned long long* mine = slot_of(pc.grain);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            mine[(nt * 2 + 0) * kConsumerThreads + tid] = acc[nt][0];
-            mine[(nt * 2 + 1) * kConsumerThreads + tid] = acc[nt][1];
-        }
-        unsigned* counter = p.sched.counters + size_t(job.first_tile + pc.tile) * kConsumerThreads + tid;
-        write = atom_add_acq_rel(counter, 1u) == gl - gf;
-        if (write) {
+            for (int nt = 0; nt < NT; ++nt) {
+                store_relaxed(mine + (nt * 2 + 0) * kConsumerThreads + tid, tagged(acc[nt][0]));
+                store_relaxed(mine + (nt * 2 + 1) * kConsumerThreads + tid, tagged(acc[nt][1]));
+            }
+            write = false;
+        } else {
+            float sum[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
-                acc[nt][0] = acc[nt][1] = 0.f;
-            for (uint32_t gr = gf; gr <= gl; ++gr) {
-                const float* part = slots + (size_t(gr) * 2 + (gr * W < pc.x0 ? 1 : 0)) * kSlotFloats;
+                sum[nt][0] = sum[nt][1] = 0.f;
+            for (uint32_t gr = gf; gr < gl; ++gr) {
+                unsigned long long* part = slot_of(gr);
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    acc[nt][0] += load_relaxed_f32(part + (nt * 2 + 0) * kConsumerThreads + tid);
-                    acc[nt][1] += load_relaxed_f32(part + (nt * 2 + 1) * kConsumerThreads + tid);
-                }
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int hl = 0; hl < 2; ++hl) {
+                        unsigned long long* at = part + (nt * 2 + hl) * kConsumerThreads + tid;
+                        unsigned long long v = load_relaxed(at);
+                        for (uint32_t poll = 0; (v >> 32) != 1ull; ++poll) {
+                            if (poll == wait_polls) {
+                                atomicOr(p.watchdog, watchdog_fixup);
+                                atomicExch(abort_flag, 1);
+                                break;
+                            }
+                            __nanosleep(32);
+                            v = load_relaxed(at);
+                        }
+                        sum[nt][hl] += __uint_as_float(uint32_t(v));
+                        store_relaxed(at, 0ull);
+                    }
             }
-            *reinterpret_cast<volatile unsigned*>(counter) = 0u;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                acc[nt][0] = sum[nt][0] + acc[nt][0];
+                acc[nt][1] = sum[nt][1] + acc[nt][1];
+            }
         }
     }
     if (write) {
@@ -1104,9 +1133,8 @@ struct SchedBuffer {
 
 constexpr size_t kEpochBytes = kMaxGrid * 4;
 constexpr size_t kTicketOff = kEpochBytes;
-constexpr size_t kCounterOff = kTicketOff + 256;
-constexpr size_t kPartialOff = kCounterOff + size_t(kMaxTiles) * kConsumerThreads * 4;
-constexpr size_t kSchedBytes = kPartialOff + size_t(kMaxGrains) * 2 * kSlotFloats * 4;
+constexpr size_t kPartialOff = kTicketOff + 256;
+constexpr size_t kSchedBytes = kPartialOff + size_t(kMaxGrains) * 2 * kSlotFloats * 8;
 
 struct SchedTable {
     std::mutex lock;
@@ -1144,8 +1172,7 @@ const Sched* sched_for(cudaStream_t stream) {
     b.base = base;
     b.sched.epochs = reinterpret_cast<unsigned*>(bytes);
     b.sched.tickets = reinterpret_cast<unsigned*>(bytes + kTicketOff);
-    b.sched.counters = reinterpret_cast<unsigned*>(bytes + kCounterOff);
-    b.sched.partials = reinterpret_cast<float*>(bytes + kPartialOff);
+    b.sched.partials = reinterpret_cast<unsigned long long*>(bytes + kPartialOff);
     return &b.sched;
 }
 
@@ -1186,7 +1213,7 @@ uint32_t grain_units(uint64_t units, uint32_t grid, uint32_t floor_units, uint32
 uint32_t plan_split(MmaParams& p, uint32_t tiles, uint32_t units, uint32_t min_tile_units, uint32_t floor_units,
                     uint32_t slots, bool ragged, uint32_t min_units_per_cta, const Sched* sched) {
     uint32_t grid = std::min(tiles, slots);
-    if (!sched || !ragged || tiles > kMaxTiles || slots > kMaxGrid
+    if (!sched || !ragged || slots > kMaxGrid
         || uint64_t(units) < uint64_t(min_units_per_cta) * slots)
         return grid;
     const uint32_t W = grain_units(units, slots, floor_units, min_tile_units);
@@ -1246,7 +1273,7 @@ void clear_gemv_fixups() {
     cudaDeviceSynchronize();
     for (auto& [key, b] : t.table)
         if (key.first == dev && b.base)
-            cudaMemset(b.base, 0, kPartialOff);  // launch counters, tickets, tile counters
+            cudaMemset(b.base, 0, kSchedBytes);  // launch counters, tickets, partial words
     cudaDeviceSynchronize();
 }
 
