@@ -23,27 +23,27 @@
 // 32 or 16) for one group of input rows; with R < 64 the warps split K (2 or 4
 // ways) and reduce in shared memory at the end. The producer streams each
 // stage (R rows x 128/R super-blocks, 18 KB) with one 3-D TMA tile load per
-// super-block column into a 3-stage ring; a 144-byte row pitch keeps every
+// super-block column into a 3-stage ring, optionally running an L2 prefetch
+// of the same boxes a few stages ahead; a 144-byte row pitch keeps every
 // fragment load free of bank conflicts. The activations of a K segment (all
 // of K at decode shapes) are quantised once per CTA and input, so consumer
 // warps run without any barrier between them: wait for a stage, issue its
 // MMAs, release it.
 //
-// Work split. Whole tiles are dealt round-robin when that fills the CTA
-// slots' waves. Otherwise the split is dynamic: the launch's work is the
-// sequence of units (tile, super-block), tiles of all jobs in order, K
-// innermost, cut into grains of W units (W at most a tile, so a grain spans
-// at most two tiles). CTA c starts with grain c (no counter needed, so its
-// weights stream while the previous kernel finishes) and then draws grains
-// from the launch's ticket counter, so CTAs that the memory system serves
-// faster take more of the work and all finish together. A tile cut by grain
-// boundaries is computed in pieces: each piece's partial sums go to its
-// grain's slot, each thread counts the piece on its own counter of the tile
-// (release/acquire atomics), and the thread that completes the count adds all
-// pieces' sums in grain order (so the result does not depend on timing),
-// writes the outputs and re-arms the counter. Nothing waits on another CTA.
-// Without a scheduling buffer (first use of a stream inside graph capture)
-// the launch deals whole tiles.
+// Work split (balanced, "stream-K"): the launch's work is the sequence of
+// units (tile, super-block), tiles of all jobs in order, K innermost. CTA c of
+// G takes units [c*U/G, (c+1)*U/G), so every CTA streams the same number of
+// bytes and no CTA is left with a second wave (tiles are 64 rows). A tile cut
+// by CTA boundaries is computed in pieces. The CTA holding its first unit
+// reaches it last (it is that CTA's final piece) and writes the outputs; every
+// other piece is the first piece of a later CTA ("head piece"), done early:
+// its consumers store each partial sum with a "present" tag as one 64-bit
+// word (single-copy atomic, so no fence or flag is needed) in the CTA's slot
+// of a fixup buffer. The first CTA's consumers, at the end of their own
+// piece, read those words (re-reading any whose tag is not there yet), add
+// them in CTA order, so the sum does not depend on timing, and zero them for
+// the next launch. Without a fixup buffer (first use of a stream inside graph
+// capture) the launch falls back to whole tiles dealt round-robin.
 //
 // Launched with programmatic dependent launch: the producer starts streaming
 // weights while the previous kernel in the stream is still finishing; the
@@ -89,28 +89,19 @@ struct alignas(64) MmaJob {
 
 // Partial sums of one piece: acc[NT <= 2][2] of each consumer thread.
 constexpr int kSlotFloats = 2 * 2 * kConsumerThreads;
-// Dynamic split limits (one scheduling buffer per device and stream).
-constexpr uint32_t kMaxGrid = 1024;     // CTAs of one launch
-constexpr uint32_t kMaxGrains = 4096;   // grains of one launch
-constexpr uint32_t kGrainEnd = 0xffffffffu;
-constexpr int kGrainRing = 8;           // grain ids in flight from producer to consumers
-
-// Device memory of the dynamic split, zeroed when allocated; every launch
-// leaves it as it found it except for the launch counters.
-struct Sched {
-    unsigned* epochs;              // [kMaxGrid] dynamic launches so far on this stream
-    unsigned* tickets;             // [2] grain tickets, by launch parity
-    unsigned long long* partials;  // [kMaxGrains][2][kSlotFloats] tagged partial sums of cut pieces
-};
+// Fewest 64-row x 1 super-block units per CTA for which the balanced split
+// pays for its fixup (a round trip to L2 at the end of each cut tile).
+constexpr int kMinUnitsPerCta = 6;
 
 struct MmaParams {
     MmaJob jobs[kMaxJobsQ];
     uint32_t count, total_tiles;
-    uint32_t tile_rows;    // R: 64, 32 or 16 (Q6_K: 16)
-    uint32_t total_units;  // dynamic split over units; 0 = whole tiles round-robin
-    uint32_t grain_units;  // W: units per grain (at most the units of a tile)
-    uint32_t total_grains;
-    Sched sched;
+    uint32_t tile_rows;    // R: 64, 32 or 16
+    uint32_t total_units;  // balanced split over units; 0 = whole tiles round-robin
+    uint32_t prefetch;     // L2 prefetch distance in stages (0 = off)
+    // [gridDim.x][kSlotFloats] head-piece partial sums as {fp32 bits, 1}
+    // words; zero between launches.
+    unsigned long long* partials;
     unsigned* watchdog;
 };
 
@@ -130,15 +121,23 @@ __device__ __forceinline__ unsigned long long tagged(float v) {
     return (1ull << 32) | __float_as_uint(v);
 }
 
-// A contiguous run of one tile's units [k0, k1) (super-blocks; Q6_K: chunks).
+// A contiguous run of one tile's super-blocks [k0, k1) taken by this CTA.
 struct Piece {
     int job;
-    uint32_t tile;     // tile within the job: column tile * row_groups + row group
+    uint32_t tile;            // tile within the job: column tile * row_groups + row group
     uint32_t k0, k1;
-    bool whole;        // k0 == 0 && k1 == units of the tile
-    uint32_t x0;       // the tile's first unit in the launch
-    uint32_t grain;    // grain of the piece's first unit (dynamic split)
+    bool whole;               // k0 == 0 && k1 == nblocks
+    uint32_t c_first, c_last; // CTAs holding the tile's first / last unit (cut tiles)
 };
+
+__device__ __forceinline__ uint32_t range_begin(uint32_t total_units, uint32_t cta) {
+    return uint32_t(uint64_t(cta) * total_units / gridDim.x);
+}
+
+// CTA whose unit range holds unit x (every range is non-empty: G <= U).
+__device__ __forceinline__ uint32_t cta_of(uint32_t total_units, uint32_t x) {
+    return uint32_t((uint64_t(x + 1) * gridDim.x - 1) / total_units);
+}
 
 // Activation segment: per super-block and token, the quantised h/l operands
 // in B-fragment order ([j][t][part][4 words], 512 bytes), the minimum-term B
@@ -154,8 +153,7 @@ struct Layout {
     static constexpr int kRedOff = kSegOff + kSegBudget;       // split-K partials
     static constexpr int kRedBytes = kConsumerThreads * 4 * 4;  // [nt<=2][2][thread]
     static constexpr int kBarOff = kRedOff + kRedBytes;  // full[], empty[], abort flag
-    static constexpr int kRingOff = kBarOff + 2 * kStages * 8 + 16;  // grain ring: barriers, ids
-    static constexpr int kTotal = kRingOff + kGrainRing * 12;
+    static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
 };
 
 // Segment of `rows` tokens: the most whole stages (multiples of `bps`
@@ -193,24 +191,20 @@ __device__ __forceinline__ int find_job(const MmaParams& p, uint32_t at, bool un
     return low;
 }
 
-__device__ __forceinline__ void grid_dependency_wait() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-__device__ __forceinline__ void grid_dependents_launch() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-// Pieces of whole tiles dealt round-robin over the CTAs, or of one grain
-// (units [grain W, (grain + 1) W) of the launch's sequence: tiles of all jobs
-// in order, units innermost). Producer and consumers walk their own copies
-// and see the same sequence.
+// The pieces of this CTA in order. Producer, prefetcher and consumers each
+// walk their own copy and see the same sequence.
 struct PieceIter {
     uint32_t cur, end;
 
-    __device__ explicit PieceIter(const MmaParams& p) : cur(blockIdx.x), end(p.total_tiles) {}
-    __device__ PieceIter(const MmaParams& p, uint32_t grain)
-        : cur(grain * p.grain_units), end(min(p.total_units, (grain + 1) * p.grain_units)) {}
+    __device__ explicit PieceIter(const MmaParams& p) {
+        if (p.total_units) {
+            cur = range_begin(p.total_units, blockIdx.x);
+            end = range_begin(p.total_units, blockIdx.x + 1);
+        } else {
+            cur = blockIdx.x;
+            end = p.total_tiles;
+        }
+    }
 
     __device__ bool next(const MmaParams& p, Piece& pc) {
         if (cur >= end)
@@ -231,103 +225,48 @@ struct PieceIter {
         pc.k0 = local % nb;
         pc.k1 = min(nb, pc.k0 + (end - cur));
         pc.whole = pc.k0 == 0 && pc.k1 == nb;
-        pc.x0 = cur - pc.k0;
-        pc.grain = cur / p.grain_units;
+        if (!pc.whole) {
+            const uint32_t x0 = cur - pc.k0;
+            pc.c_first = cta_of(p.total_units, x0);
+            pc.c_last = cta_of(p.total_units, x0 + nb - 1);
+        }
         cur += pc.k1 - pc.k0;
         return true;
     }
 };
 
-// Grain ids from the producer lane to the consumer warps.
-struct GrainRing {
-    uint64_t* full;  // [kGrainRing] mbarriers, one arrival each
-    uint32_t* id;    // [kGrainRing]
-};
+__device__ __forceinline__ void prefetch_l2_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(c0), "r"(c1), "r"(c2)
+        : "memory"
+    );
+}
 
-// The producer's walk: whole tiles, or grains: grain blockIdx.x first (it
-// needs no counter, so its weights stream while the previous kernel of the
-// stream finishes), then grains drawn from the launch's ticket counter once
-// the grid-dependency wait has passed. Every grain id, then kGrainEnd, goes
-// to the consumers through the ring; the ring cannot overrun: the producer
-// runs at most kStages stages, hence kStages + 1 grains, ahead of the
-// slowest consumer warp. stream(pc) issues a piece's stages; false = abort.
-template <class Stream>
-__device__ void produce_pieces(const MmaParams& p, const GrainRing& ring, Stream&& stream) {
-    if (!p.total_units) {
-        PieceIter pieces(p);
-        Piece pc;
-        while (pieces.next(p, pc))
-            if (!stream(pc))
+// L2 prefetch cursor: walks the producer's stage sequence ahead of it.
+struct Prefetcher {
+    PieceIter pieces;
+    Piece pc;
+    uint32_t b0 = 0;
+    bool live = false;
+
+    __device__ explicit Prefetcher(const MmaParams& p) : pieces(p) {}
+
+    // Prefetch the next stage (BPS super-blocks of R rows) into L2.
+    __device__ void step(const MmaParams& p, int R, int BPS) {
+        if (!live || b0 >= pc.k1) {
+            if (!pieces.next(p, pc))
                 return;
-        return;
-    }
-    uint32_t pushed = 0;
-    auto push = [&](uint32_t v) {
-        ring.id[pushed % kGrainRing] = v;
-        mbar_arrive(&ring.full[pushed % kGrainRing]);
-        ++pushed;
-    };
-    unsigned* ticket = nullptr;
-    bool ok = true;
-    uint32_t next = 0;
-    for (uint32_t grain = blockIdx.x; ok && grain < p.total_grains;) {
-        push(grain);
-        // Draw the following grain now: the ticket's round trip then
-        // overlaps this grain's stages instead of stalling the ring.
-        if (ticket)
-            next = gridDim.x + atomicAdd(ticket, 1u);
-        PieceIter pieces(p, grain);
-        Piece pc;
-        while (ok && pieces.next(p, pc))
-            ok = stream(pc);
-        if (!ticket) {
-            // The previous kernel has finished: its counters are settled.
-            // The launch's number is the count of dynamic launches so far
-            // (every CTA advances its share of the counters, so all read the
-            // same); launches alternate between two ticket counters, and the
-            // first CTA clears the one the next launch will use.
-            grid_dependency_wait();
-            const unsigned id = p.sched.epochs[blockIdx.x] + 1u;
-            for (uint32_t i = blockIdx.x; i < kMaxGrid; i += gridDim.x)
-                p.sched.epochs[i] = id;
-            ticket = p.sched.tickets + (id & 1u);
-            if (blockIdx.x == 0)
-                p.sched.tickets[(id + 1u) & 1u] = 0u;
-            next = gridDim.x + atomicAdd(ticket, 1u);
+            live = true;
+            b0 = pc.k0;
         }
-        grain = next;
+        const MmaJob& job = p.jobs[pc.job];
+        const int row0 = int((pc.tile / job.row_groups) * uint32_t(R));
+        const uint32_t stop = min(pc.k1, b0 + uint32_t(BPS));
+        for (uint32_t b = b0; b < stop; ++b)
+            prefetch_l2_3d(&job.map, 0, int(b), row0);
+        b0 = stop;
     }
-    push(kGrainEnd);
-}
-
-// The consumers' walk, in the producer's order. run(pc) processes a piece.
-template <class Run>
-__device__ void consume_pieces(const MmaParams& p, const GrainRing& ring, int* abort_flag, Run&& run) {
-    if (!p.total_units) {
-        PieceIter pieces(p);
-        Piece pc;
-        while (pieces.next(p, pc))
-            run(pc);
-        return;
-    }
-    for (uint32_t popped = 0;; ++popped) {
-        const int slot = int(popped % kGrainRing);
-        bool arrived = false;
-        for (int tries = 0; tries < 4 && !arrived; ++tries)
-            arrived = mbar_wait(&ring.full[slot], (popped / kGrainRing) & 1u, watchdog_full_barrier, p.watchdog);
-        if (!arrived) {
-            atomicExch(abort_flag, 1);
-            return;
-        }
-        const uint32_t grain = ring.id[slot];
-        if (grain == kGrainEnd)
-            return;
-        PieceIter pieces(p, grain);
-        Piece pc;
-        while (pieces.next(p, pc))
-            run(pc);
-    }
-}
+};
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
     asm volatile(
@@ -396,6 +335,14 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
 
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
     return __byte_perm(__byte_perm(uint32_t(a), uint32_t(b), 0x0040u), __byte_perm(uint32_t(c), uint32_t(d), 0x0040u), 0x5410u);
+}
+
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_dependents_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // Quantise the activations of super-blocks [blk0, blk0 + nblk) for the
@@ -509,9 +456,10 @@ __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, 
 }
 
 // End of a piece, common to the K-quant kernels: sum the K-split warps of
-// each row group, then write the outputs (whole tile), or publish the sums of
-// a piece of a cut tile, or (the tile's last grain) add all pieces' sums and
-// write. acc[nt][0/1]: rows my_row, my_row + 8 for token nt*4 + t.
+// each row group, then either publish the partial sums (head piece of a cut
+// tile), add the later pieces' sums in CTA order (tail piece), or write the
+// outputs (whole tile or tail piece). acc[nt][0/1]: rows my_row, my_row + 8
+// for token nt*4 + t.
 template <int NT, class Await>
 __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc, const MmaJob& job, float (&acc)[NT][2],
                                              int KS, int ks, int tid, uint32_t my_row, bool valid_lo, bool valid_hi,
@@ -538,43 +486,48 @@ __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc
         named_sync(1, kConsumerThreads);
     }
     await_dependency();
-    if (ks != 0)
-        return;  // the warps of K split 0 hold the row group's sums
-    bool write = true;
-    if (!pc.whole) {
-        // A cut tile: the pieces come from grains gf..gl, and a grain spans
-        // at most two tiles (slot 1 holds its piece of the second). Every
-        // piece but the last grain's stores its sums as tagged words in its
-        // slot (the slot is zero between launches); the last grain's piece,
-        // usually the last to finish, adds them in grain order as their tags
-        // appear, then its own, so the result does not depend on timing, and
-        // zeroes the words for the next launch on this stream.
-        const uint32_t W = p.grain_units, nb = job.nblocks;
-        const uint32_t gf = pc.x0 / W, gl = (pc.x0 + nb - 1) / W;
-        auto slot_of = [&](uint32_t gr) {
-            return p.sched.partials + (size_t(gr) * 2 + (gr * W < pc.x0 ? 1 : 0)) * kSlotFloats;
-        };
-        if (pc.grain != gl) {
-            unsigned long long* mine = slot_of(pc.grain);
+    bool write = ks == 0;
+    if (!pc.whole && pc.k0 > 0) {
+        // Head piece of a cut tile (R = 64, every warp holds final sums):
+        // store the partial sums; the fixup lanes publish them.
+        // store the tagged partial sums (the slot was zeroed by the previous
+        // launch, which finished before the grid-dependency wait).
+        unsigned long long* mine = p.partials + size_t(blockIdx.x) * kSlotFloats;
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                store_relaxed(mine + (nt * 2 + 0) * kConsumerThreads + tid, tagged(acc[nt][0]));
-                store_relaxed(mine + (nt * 2 + 1) * kConsumerThreads + tid, tagged(acc[nt][1]));
+        for (int nt = 0; nt < NT; ++nt) {
+            store_relaxed(mine + (nt * 2 + 0) * kConsumerThreads + tid, tagged(acc[nt][0]));
+            store_relaxed(mine + (nt * 2 + 1) * kConsumerThreads + tid, tagged(acc[nt][1]));
+        }
+        write = false;
+    } else if (!pc.whole) {
+        // Tail piece holding the tile's first unit: add the later pieces'
+        // sums in CTA order as their tags appear, and zero the words for
+        // the next launch on this stream.
+        constexpr int kAhead = 4;  // CTAs whose words are in flight together
+        const uint32_t others = pc.c_last - pc.c_first;
+        for (uint32_t c0 = 0; c0 < others; c0 += kAhead) {
+            unsigned long long w[kAhead][NT][2];
+#pragma unroll
+            for (int q = 0; q < kAhead; ++q) {
+                const uint32_t c = pc.c_first + 1 + min(c0 + q, others - 1);
+                const unsigned long long* part = p.partials + size_t(c) * kSlotFloats;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    w[q][nt][0] = load_relaxed(part + (nt * 2 + 0) * kConsumerThreads + tid);
+                    w[q][nt][1] = load_relaxed(part + (nt * 2 + 1) * kConsumerThreads + tid);
+                }
             }
-            write = false;
-        } else {
-            float sum[NT][2];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-                sum[nt][0] = sum[nt][1] = 0.f;
-            for (uint32_t gr = gf; gr < gl; ++gr) {
-                unsigned long long* part = slot_of(gr);
+            for (int q = 0; q < kAhead; ++q) {
+                if (c0 + q >= others)
+                    break;
+                unsigned long long* part = p.partials + size_t(pc.c_first + 1 + c0 + q) * kSlotFloats;
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
                     for (int hl = 0; hl < 2; ++hl) {
                         unsigned long long* at = part + (nt * 2 + hl) * kConsumerThreads + tid;
-                        unsigned long long v = load_relaxed(at);
+                        unsigned long long v = w[q][nt][hl];
                         for (uint32_t poll = 0; (v >> 32) != 1ull; ++poll) {
                             if (poll == wait_polls) {
                                 atomicOr(p.watchdog, watchdog_fixup);
@@ -584,14 +537,10 @@ __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc
                             __nanosleep(32);
                             v = load_relaxed(at);
                         }
-                        sum[nt][hl] += __uint_as_float(uint32_t(v));
+                        acc[nt][hl] += __uint_as_float(uint32_t(v));
                         store_relaxed(at, 0ull);
                     }
-            }
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                acc[nt][0] = sum[nt][0] + acc[nt][0];
-                acc[nt][1] = sum[nt][1] + acc[nt][1];
+                }
             }
         }
     }
@@ -623,15 +572,11 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
     const int R = int(p.tile_rows), KS = 64 / R, BPS = kStageUnits / R;
     auto* red = reinterpret_cast<float*>(smem + L::kRedOff);
 
-    const GrainRing ring{reinterpret_cast<uint64_t*>(smem + L::kRingOff),
-                         reinterpret_cast<uint32_t*>(smem + L::kRingOff + kGrainRing * 8)};
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kWarps);
         }
-        for (int s = 0; s < kGrainRing; ++s)
-            mbar_init(&ring.full[s], 1);
         *abort_flag = 0;
         fence_barrier_init();
         // The next kernel of the stream may start its own weight streaming.
@@ -644,7 +589,12 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
         if (lane != 0)
             return;
         uint32_t it = 0;
-        produce_pieces(p, ring, [&](const Piece& pc) -> bool {
+        PieceIter pieces(p);
+        Prefetcher ahead(p);
+        for (uint32_t i = 0; i < p.prefetch; ++i)
+            ahead.step(p, R, BPS);
+        Piece pc;
+        while (pieces.next(p, pc)) {
             const MmaJob& job = p.jobs[pc.job];
             const int row0 = int((pc.tile / job.row_groups) * uint32_t(R));
             asm volatile("prefetch.tensormap [%0];" ::"l"(&job.map) : "memory");
@@ -653,15 +603,17 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
                 if (it >= kStages && !mbar_wait(&empty[slot], ((it / kStages) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog))
                     atomicExch(abort_flag, 1);
                 if (*reinterpret_cast<volatile int*>(abort_flag))
-                    return false;
+                    goto drain;
                 const int nb = int(min(uint32_t(BPS), pc.k1 - b0));
                 mbar_expect_tx(&full[slot], uint32_t(nb * R * kBlockBytes));
                 for (int b = 0; b < nb; ++b)
                     tma_load_3d(smem + L::kStagesOff + slot * kStageBytes + b * R * kBlockBytes, &job.map, 0,
                                 int(b0 + b), row0, &full[slot]);
+                if (p.prefetch)
+                    ahead.step(p, R, BPS);
             }
-            return true;
-        });
+        }
+    drain:
         for (uint32_t k = 0; k < kStages && k < it; ++k) {
             const uint32_t last = it - 1 - k;
             mbar_wait(&full[last % kStages], (last / kStages) & 1u, watchdog_drain, p.watchdog);
@@ -687,7 +639,9 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
     // (input, rows, first block, blocks) of the activation segment held in shared memory.
     const float* seg_x = nullptr;
     int seg_rows = -1, seg_blk0 = -1, seg_nblk = 0;
-    consume_pieces(p, ring, abort_flag, [&](const Piece& pc) {
+    PieceIter pieces(p);
+    Piece pc;
+    while (pieces.next(p, pc)) {
         const MmaJob& job = p.jobs[pc.job];
         const uint32_t row0 = (pc.tile / job.row_groups) * uint32_t(R);
         const uint32_t r0 = (pc.tile % job.row_groups) * job.group_rows;
@@ -714,15 +668,18 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
             const int blk_first = int(b0);
             if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
                 && seg.blocks >= BPS) {
-                // The window covers this stage and the rest of the piece, as
-                // far as the segment buffer reaches.
-                const int count = min(seg.blocks, int(pc.k1) - blk_first);
+                // The window covers all of K when the segment buffer holds
+                // it (one quantisation per input however the work is cut),
+                // else this stage and what follows, as far as it reaches.
+                const int nbk = int(job.nblocks);
+                const int start = nbk <= seg.blocks ? 0 : blk_first;
+                const int count = min(seg.blocks, nbk - start);
                 await_dependency();
                 // Every warp is done with the previous segment before it is replaced.
                 named_sync(1, kConsumerThreads);
-                prep_segment(smem, seg, x, job.in, blk_first, count);
+                prep_segment(smem, seg, x, job.in, start, count);
                 named_sync(1, kConsumerThreads);
-                seg_x = x, seg_rows = rows, seg_blk0 = blk_first, seg_nblk = count;
+                seg_x = x, seg_rows = rows, seg_blk0 = start, seg_nblk = count;
             }
             const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
             if (!aborted && !mbar_wait(&full[slot], (it / kStages) & 1u, watchdog_full_barrier, p.watchdog))
@@ -823,8 +780,8 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
         finish_piece<NT>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0, rows, red, abort_flag,
                          await_dependency);
         // After an abort the remaining pieces still run (without waits or
-        // MMAs) so that every cut tile's counter is completed and re-armed.
-    });
+        // MMAs) so that every cut tile's counter is re-armed.
+    }
 }
 
 // ------------------------------------------------------------------- Q6_K
@@ -858,8 +815,7 @@ struct Q6Layout {
     static constexpr int kRedOff = kSegOff + kQ6SegBudget;
     static constexpr int kRedBytes = kConsumerThreads * 4 * 4;
     static constexpr int kBarOff = kRedOff + kRedBytes;
-    static constexpr int kRingOff = kBarOff + 2 * kStages * 8 + 16;
-    static constexpr int kTotal = kRingOff + kGrainRing * 12;
+    static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
 };
 static_assert(Q6Layout::kSegOff - Q6Layout::kStagesOff == 3 * kQ6StageBytes, "stage ring");
 
@@ -960,15 +916,11 @@ __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid
     constexpr int KS = kWarps;
     auto* red = reinterpret_cast<float*>(smem + L::kRedOff);
 
-    const GrainRing ring{reinterpret_cast<uint64_t*>(smem + L::kRingOff),
-                         reinterpret_cast<uint32_t*>(smem + L::kRingOff + kGrainRing * 8)};
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kWarps);
         }
-        for (int s = 0; s < kGrainRing; ++s)
-            mbar_init(&ring.full[s], 1);
         *abort_flag = 0;
         fence_barrier_init();
         grid_dependents_launch();
@@ -980,7 +932,9 @@ __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid
         if (lane != 0)
             return;
         uint32_t it = 0;
-        produce_pieces(p, ring, [&](const Piece& pc) -> bool {
+        PieceIter pieces(p);
+        Piece pc;
+        while (pieces.next(p, pc)) {
             const MmaJob& job = p.jobs[pc.job];
             const int row0 = int((pc.tile / job.row_groups) * uint32_t(kQ6Rows));
             asm volatile("prefetch.tensormap [%0];" ::"l"(&job.map) : "memory");
@@ -989,14 +943,14 @@ __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid
                 if (it >= kStages && !mbar_wait(&empty[slot], ((it / kStages) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog))
                     atomicExch(abort_flag, 1);
                 if (*reinterpret_cast<volatile int*>(abort_flag))
-                    return false;
+                    goto drain;
                 // The whole box lands (rows and blocks past the matrix are zero-filled).
                 mbar_expect_tx(&full[slot], uint32_t(kQ6StageBytes));
                 tma_load_2d(smem + L::kStagesOff + slot * kQ6StageBytes, &job.map, int(ch) * (kQ6Chunk * kQ6Block / 8),
                             row0, &full[slot]);
             }
-            return true;
-        });
+        }
+    drain:
         for (uint32_t k = 0; k < kStages && k < it; ++k) {
             const uint32_t last = it - 1 - k;
             mbar_wait(&full[last % kStages], (last / kStages) & 1u, watchdog_drain, p.watchdog);
@@ -1016,7 +970,9 @@ __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid
     uint32_t it = 0;
     const float* seg_x = nullptr;
     int seg_rows = -1, seg_blk0 = -1, seg_nblk = 0;
-    consume_pieces(p, ring, abort_flag, [&](const Piece& pc) {
+    PieceIter pieces(p);
+    Piece pc;
+    while (pieces.next(p, pc)) {
         const MmaJob& job = p.jobs[pc.job];
         const uint32_t row0 = (pc.tile / job.row_groups) * uint32_t(kQ6Rows);
         const uint32_t r0 = (pc.tile % job.row_groups) * job.group_rows;
@@ -1043,12 +999,13 @@ __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid
             const int nb = min(kQ6Chunk, nblocks - blk_first);
             if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
                 && seg.blocks >= kQ6Chunk) {
-                const int count = min(seg.blocks, nblocks - blk_first);
+                const int start = nblocks <= seg.blocks ? 0 : blk_first;
+                const int count = min(seg.blocks, nblocks - start);
                 await_dependency();
                 named_sync(1, kConsumerThreads);
-                prep_segment<true>(smem, seg, x, job.in, blk_first, count);
+                prep_segment<true>(smem, seg, x, job.in, start, count);
                 named_sync(1, kConsumerThreads);
-                seg_x = x, seg_rows = rows, seg_blk0 = blk_first, seg_nblk = count;
+                seg_x = x, seg_rows = rows, seg_blk0 = start, seg_nblk = count;
             }
             const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
             if (!aborted && !mbar_wait(&full[slot], (it / kStages) & 1u, watchdog_full_barrier, p.watchdog))
@@ -1083,7 +1040,7 @@ __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid
             atomicOr(job.status, 1u);
         finish_piece<NT>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0, rows, red, abort_flag,
                          await_dependency);
-    });
+    }
 }
 
 // ------------------------------------------------------------------ host side
@@ -1122,109 +1079,76 @@ template <int NT> int kernel_slots() {
     return sm_count() * blocks_per_sm[dev];
 }
 
-// Scheduling buffer of the dynamic split for one (device, stream). Launches
-// on one stream run in order and touch the buffer only after their
-// grid-dependency wait (so after the previous launch finished), which lets
-// every launch of the stream share it.
-struct SchedBuffer {
-    void* base = nullptr;
-    Sched sched{};
+// Fixup buffer of the balanced split for one (device, stream). Launches on one
+// stream run in order, and a launch touches the buffer only after its
+// grid-dependency wait, so every launch of the stream can share it.
+struct Fixup {
+    unsigned long long* partials = nullptr;
+    uint32_t ctas = 0;
 };
 
-constexpr size_t kEpochBytes = kMaxGrid * 4;
-constexpr size_t kTicketOff = kEpochBytes;
-constexpr size_t kPartialOff = kTicketOff + 256;
-constexpr size_t kSchedBytes = kPartialOff + size_t(kMaxGrains) * 2 * kSlotFloats * 8;
-
-struct SchedTable {
+// The stream's fixup buffer, allocated (and zeroed on the stream) by the
+// first call outside graph capture; null when none can be had.
+struct FixupTable {
     std::mutex lock;
-    std::map<std::pair<int, cudaStream_t>, SchedBuffer> table;
+    std::map<std::pair<int, cudaStream_t>, Fixup> table;
 };
 
-SchedTable& scheds() {
-    static SchedTable t;
+FixupTable& fixups() {
+    static FixupTable t;
     return t;
 }
 
-// The stream's scheduling buffer, allocated (and zeroed on the stream) by the
-// first call outside graph capture; null when none can be had.
-const Sched* sched_for(cudaStream_t stream) {
+const Fixup* fixup_for(cudaStream_t stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess)
         return nullptr;
-    SchedTable& t = scheds();
+    FixupTable& t = fixups();
     std::lock_guard<std::mutex> guard(t.lock);
-    SchedBuffer& b = t.table[{dev, stream}];
-    if (b.base)
-        return &b.sched;
+    Fixup& f = t.table[{dev, stream}];
+    if (f.ctas)
+        return &f;
     cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess || capture != cudaStreamCaptureStatusNone) {
         cudaGetLastError();
         return nullptr;
     }
-    void* base = nullptr;
-    if (cudaMalloc(&base, kSchedBytes) != cudaSuccess || cudaMemsetAsync(base, 0, kSchedBytes, stream) != cudaSuccess) {
+    // At most 4 CTAs of this kernel fit on an SM (shared memory).
+    const uint32_t ctas = uint32_t(sm_count()) * 4u;
+    Fixup made;
+    const size_t bytes = size_t(ctas) * kSlotFloats * sizeof(unsigned long long);
+    if (cudaMalloc(&made.partials, bytes) != cudaSuccess
+        || cudaMemsetAsync(made.partials, 0, bytes, stream) != cudaSuccess) {
         cudaGetLastError();
-        cudaFree(base);
+        cudaFree(made.partials);
         return nullptr;
     }
-    auto* bytes = static_cast<uint8_t*>(base);
-    b.base = base;
-    b.sched.epochs = reinterpret_cast<unsigned*>(bytes);
-    b.sched.tickets = reinterpret_cast<unsigned*>(bytes + kTicketOff);
-    b.sched.partials = reinterpret_cast<unsigned long long*>(bytes + kPartialOff);
-    return &b.sched;
+    made.ctas = ctas;
+    f = made;
+    return &f;
 }
 
 struct Tuning {
-    bool dynamic = true;         // KB200_GEMV_DYNAMIC=0: whole tiles round-robin only
-    uint32_t min_units = 6;      // KB200_GEMV_MIN_UNITS: Q4_K units per CTA below which tiles stay whole
-    uint32_t grains_per_cta = 3; // KB200_GEMV_GRAINS: grains per CTA slot (dynamic split granularity)
-    int ctas_per_sm = 0;         // KB200_GEMV_CTAS_PER_SM=<n>: grid slots per SM (0: all that fit)
+    bool balanced = true;  // KB200_GEMV_BALANCED=0: whole tiles round-robin
+    uint32_t prefetch = 0; // KB200_GEMV_L2_PREFETCH=<stages>
+    uint32_t min_units = kMinUnitsPerCta;  // KB200_GEMV_MIN_UNITS=<units per CTA>
+    int ctas_per_sm = 0;                   // KB200_GEMV_CTAS_PER_SM=<n>: grid slots per SM (0: all that fit)
 };
 
 const Tuning& tuning() {
     static const Tuning t = [] {
         Tuning v;
-        if (const char* s = std::getenv("KB200_GEMV_DYNAMIC"))
-            v.dynamic = std::atoi(s) != 0;
+        if (const char* s = std::getenv("KB200_GEMV_BALANCED"))
+            v.balanced = std::atoi(s) != 0;
         if (const char* s = std::getenv("KB200_GEMV_CTAS_PER_SM"))
             v.ctas_per_sm = std::max(0, std::atoi(s));
         if (const char* s = std::getenv("KB200_GEMV_MIN_UNITS"))
             v.min_units = uint32_t(std::max(1, std::atoi(s)));
-        if (const char* s = std::getenv("KB200_GEMV_GRAINS"))
-            v.grains_per_cta = uint32_t(std::max(1, std::min(64, std::atoi(s))));
+        if (const char* s = std::getenv("KB200_GEMV_L2_PREFETCH"))
+            v.prefetch = uint32_t(std::max(0, std::min(64, std::atoi(s))));
         return v;
     }();
     return t;
-}
-
-// Grain size W for `units` units over `grid` CTAs: about grains_per_cta
-// grains per CTA, at least `floor_units` (a few stages, so a grain outlasts
-// its own pipeline fill) and at most the units of the smallest tile (a
-// grain then spans at most two tiles).
-uint32_t grain_units(uint64_t units, uint32_t grid, uint32_t floor_units, uint32_t tile_units) {
-    const uint64_t want = (units + uint64_t(grid) * tuning().grains_per_cta - 1) / (uint64_t(grid) * tuning().grains_per_cta);
-    return uint32_t(std::max<uint64_t>(1, std::min<uint64_t>(tile_units, std::max<uint64_t>(want, floor_units))));
-}
-
-// Fill in the dynamic split of p (units already summed) or leave whole tiles.
-// Returns the grid.
-uint32_t plan_split(MmaParams& p, uint32_t tiles, uint32_t units, uint32_t min_tile_units, uint32_t floor_units,
-                    uint32_t slots, bool ragged, uint32_t min_units_per_cta, const Sched* sched) {
-    uint32_t grid = std::min(tiles, slots);
-    if (!sched || !ragged || slots > kMaxGrid
-        || uint64_t(units) < uint64_t(min_units_per_cta) * slots)
-        return grid;
-    const uint32_t W = grain_units(units, slots, floor_units, min_tile_units);
-    const uint32_t grains = (units + W - 1) / W;
-    if (grains > kMaxGrains)
-        return grid;
-    p.total_units = units;
-    p.grain_units = W;
-    p.total_grains = grains;
-    p.sched = *sched;
-    return std::min(grains, slots);
 }
 
 int q6k_slots() {
@@ -1268,12 +1192,12 @@ void clear_gemv_fixups() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess)
         return;
-    SchedTable& t = scheds();
+    FixupTable& t = fixups();
     std::lock_guard<std::mutex> guard(t.lock);
     cudaDeviceSynchronize();
-    for (auto& [key, b] : t.table)
-        if (key.first == dev && b.base)
-            cudaMemset(b.base, 0, kSchedBytes);  // launch counters, tickets, partial words
+    for (auto& [key, f] : t.table)
+        if (key.first == dev && f.ctas)
+            cudaMemset(f.partials, 0, size_t(f.ctas) * kSlotFloats * sizeof(unsigned long long));
     cudaDeviceSynchronize();
 }
 
@@ -1308,14 +1232,14 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         return -slots;
     if (tuning().ctas_per_sm > 0)
         slots = std::min(slots, sm_count() * tuning().ctas_per_sm);
-    const Sched* sched = tuning().dynamic ? sched_for(stream) : nullptr;
+    const Fixup* fixup = tuning().balanced ? fixup_for(stream) : nullptr;
     for (size_t first = 0; first < jobs.size(); first += kMaxJobsQ) {
         const size_t n = std::min(jobs.size() - first, size_t(kMaxJobsQ));
         MmaParams p;
         std::memset(&p, 0, sizeof(p));
         p.watchdog = watchdog_word();
         p.tile_rows = kQ6Rows;
-        uint32_t tiles = 0, units = 0, min_tile_units = ~0u;
+        uint32_t tiles = 0, units = 0;
         for (size_t m = 0; m < n; ++m) {
             const auto& j = *jobs[first + m];
             MmaJob& d = p.jobs[m];
@@ -1345,15 +1269,19 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             const uint32_t job_tiles = (j.columns + kQ6Rows - 1) / kQ6Rows * d.row_groups;
             tiles += job_tiles;
             units += job_tiles * d.nblocks;
-            min_tile_units = std::min(min_tile_units, d.nblocks);
         }
         p.count = uint32_t(n);
         p.total_tiles = tiles;
         const uint64_t waves = (tiles + uint64_t(slots) - 1) / uint64_t(slots);
         const bool ragged = uint64_t(tiles) * 10 < waves * uint64_t(slots) * 9;
-        // A grain of at least 3 chunks (3 stages) when the tiles allow.
-        const uint32_t grid = plan_split(p, tiles, units, min_tile_units, 3, uint32_t(slots), ragged,
-                                         kQ6MinUnitsPerCta, sched);
+        const bool balanced = fixup && fixup->ctas >= uint32_t(slots) && ragged
+                              && uint64_t(units) >= uint64_t(kQ6MinUnitsPerCta) * uint64_t(slots);
+        uint32_t grid = std::min(tiles, uint32_t(slots));
+        if (balanced) {
+            grid = std::min(units, uint32_t(slots));
+            p.total_units = units;
+            p.partials = fixup->partials;
+        }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
         cfg.blockDim = dim3(kThreadsQ);
@@ -1386,7 +1314,7 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         return -slots;
     if (tuning().ctas_per_sm > 0)
         slots = std::min(slots, sm_count() * tuning().ctas_per_sm);
-    const Sched* sched = tuning().dynamic ? sched_for(stream) : nullptr;
+    const Fixup* fixup = tuning().balanced ? fixup_for(stream) : nullptr;
     for (size_t first = 0; first < jobs.size(); first += kMaxJobsQ) {
         const size_t n = std::min(jobs.size() - first, size_t(kMaxJobsQ));
         int tokens = 1;
@@ -1416,20 +1344,22 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             if (rr_tiles >= uint64_t(slots))
                 break;
         }
-        // Dynamic split (64-row tiles cut into grains) when whole tiles would
-        // leave more than a tenth of the CTA slots of their waves idle and
-        // every CTA gets enough units to pay for the sums of its cut tiles.
+        // Balanced split (64-row tiles, the same number of units per CTA)
+        // when whole tiles would leave more than a tenth of the CTA slots of
+        // their waves idle and every CTA gets enough units to pay for the
+        // fixup of its cut tiles.
         const uint64_t waves = (rr_tiles + slots - 1) / uint64_t(slots);
         const bool ragged = rr_tiles * 10 < waves * uint64_t(slots) * 9;
-        const bool dynamic = sched && ragged && units64 >= uint64_t(tuning().min_units) * uint64_t(slots)
-                             && units64 < (1ull << 31);
-        if (dynamic)
+        const bool balanced = fixup && fixup->ctas >= uint32_t(slots) && ragged
+                              && units64 >= uint64_t(tuning().min_units) * uint64_t(slots) && units64 < (1ull << 31);
+        if (balanced)
             R = 64;
         MmaParams p;
         std::memset(&p, 0, sizeof(p));
         p.watchdog = watchdog_word();
         p.tile_rows = R;
-        uint32_t tiles = 0, units = 0, min_tile_units = ~0u;
+        p.prefetch = tuning().prefetch;
+        uint32_t tiles = 0, units = 0;
         for (size_t m = 0; m < n; ++m) {
             const auto& j = *jobs[first + m];
             MmaJob& d = p.jobs[m];
@@ -1468,14 +1398,15 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             const uint32_t job_tiles = (j.columns + R - 1) / R * d.row_groups;
             tiles += job_tiles;
             units += job_tiles * d.nblocks;
-            min_tile_units = std::min(min_tile_units, d.nblocks);
         }
         p.count = uint32_t(n);
         p.total_tiles = tiles;
-        // A grain of at least 3 stages (2 super-blocks each at R = 64).
-        const uint32_t grid = dynamic ? plan_split(p, tiles, units, min_tile_units, 6, uint32_t(slots), true,
-                                                   tuning().min_units, sched)
-                                      : std::min(tiles, uint32_t(slots));
+        uint32_t grid = std::min(tiles, uint32_t(slots));
+        if (balanced) {
+            grid = std::min(units, uint32_t(slots));
+            p.total_units = units;
+            p.partials = fixup->partials;
+        }
         const int s = nt == 1 ? launch_q4k<1>(p, grid, stream) : launch_q4k<2>(p, grid, stream);
         if (s)
             return s;
