@@ -198,8 +198,10 @@ def gguf_dequant(encoding: int, packed, count: int, out, status=None, stream=Non
 def gemv_job(encoding: int, weights, x, y, *, in_: int, columns: int, rows: int,
              row_bytes_: Optional[int] = None, stride: Optional[int] = None, status=None) -> GemvJob:
     rb = row_bytes_ if row_bytes_ is not None else (in_ * 4 if encoding == F32 else row_bytes(encoding, in_))
-    return GemvJob(_ptr(weights), _ptr(x), _ptr(y), _ptr(status), rb,
-                   columns if stride is None else stride, in_, columns, rows, encoding)
+    job = GemvJob(_ptr(weights), _ptr(x), _ptr(y), _ptr(status), rb,
+                  columns if stride is None else stride, in_, columns, rows, encoding)
+    job._keep = (weights, x, y, status)  # the job holds raw pointers: keep the tensors alive with it
+    return job
 
 
 def gguf_gemv_batch(jobs: Sequence[GemvJob], stream=None) -> None:
