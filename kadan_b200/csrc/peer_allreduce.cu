@@ -99,17 +99,25 @@ __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(const __grid
                 store_pair(words_at(p.peers[q], bank, p.rank, p.max_count) + 2 * i, w0, w1);
     }
     // 2. Gather the same elements from every peer's slot and sum in rank order.
+    // All sources' words are loaded at once (one round trip, not one per
+    // rank); only words that have not arrived yet are polled again.
     bool ok = true;
     for (size_t i = size_t(c) * kArThreads + tid; i < npairs; i += stride) {
+        unsigned long long a[kMaxRanks], b[kMaxRanks];
+#pragma unroll
+        for (int s = 0; s < kMaxRanks; ++s)
+            if (s < p.world && s != p.rank)
+                load_pair(words_at(mine, bank, s, p.max_count) + 2 * i, a[s], b[s]);
         const float2 own = pairs[i];
         float2 acc = make_float2(0.f, 0.f);
-        for (int s = 0; s < p.world; ++s) {
+#pragma unroll
+        for (int s = 0; s < kMaxRanks; ++s) {
+            if (s >= p.world)
+                break;
             float2 v = own;
             if (s != p.rank) {
-                const unsigned long long* at = words_at(mine, bank, s, p.max_count) + 2 * i;
-                unsigned long long a, b;
-                load_pair(at, a, b);
-                if ((a >> 32) != e || (b >> 32) != e) {
+                if ((a[s] >> 32) != e || (b[s] >> 32) != e) {
+                    const unsigned long long* at = words_at(mine, bank, s, p.max_count) + 2 * i;
                     const unsigned long long start = global_ns();
                     do {
                         if (!ok || global_ns() - start > p.timeout_ns) {
@@ -117,10 +125,10 @@ __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(const __grid
                             break;
                         }
                         __nanosleep(32);
-                        load_pair(at, a, b);
-                    } while ((a >> 32) != e || (b >> 32) != e);
+                        load_pair(at, a[s], b[s]);
+                    } while ((a[s] >> 32) != e || (b[s] >> 32) != e);
                 }
-                v = make_float2(__uint_as_float(uint32_t(a)), __uint_as_float(uint32_t(b)));
+                v = make_float2(__uint_as_float(uint32_t(a[s])), __uint_as_float(uint32_t(b[s])));
             }
             if (s == 0)
                 acc = v;

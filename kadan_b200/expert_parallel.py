@@ -23,11 +23,11 @@ same routing, the same expert arithmetic per row, the same combine order.
 """
 from __future__ import annotations
 
-from typing import List, Optional, Sequence, Tuple
+from typing import List, Tuple
 
 import numpy as np
 
-from . import (MoeWeights, check, moe_combine, moe_dispatch_rows, moe_experts, moe_weights, lib, rows_regroup)
+from . import MoeWeights, lib, moe_combine, moe_dispatch_rows, moe_experts, moe_weights, rows_regroup
 
 
 def expert_range(experts: int, world: int, rank: int) -> Tuple[int, int]:
@@ -138,19 +138,17 @@ class ExpertParallelMoE:
         else:
             arrived = rows
         segs, local_offsets = regroup_segments(recv_counts)
-        seg_dev = torch.from_numpy(segs).to(dev, non_blocking=False) if len(segs) else None
         max_rows = int(segs[:, 2].max()) if len(segs) else 0
         grouped = torch.empty(r_total, hidden, dtype=torch.float16, device=dev)
         y_grouped = torch.empty(r_total, hidden, dtype=torch.float32, device=dev)
         if r_total:
+            seg_dev, back_dev, off_dev = self._tables(segs, local_offsets, dev)
             rows_regroup(arrived, grouped, seg_dev, max_rows)
-            off_dev = torch.from_numpy(local_offsets).to(dev)
             ews = self._buffer("experts", int(lib.kb200_moe_experts_workspace_bytes(
                 self._wref(), r_total)), dev)
             moe_experts(self.w, grouped, off_dev, y_grouped, ews, status)
-            back_segs = segs[:, [1, 0, 2]].copy()
             y_arrived = torch.empty(r_total, hidden, dtype=torch.float32, device=dev)
-            rows_regroup(y_grouped, y_arrived, torch.from_numpy(back_segs).to(dev), max_rows)
+            rows_regroup(y_grouped, y_arrived, back_dev, max_rows)
         else:
             y_arrived = y_grouped
         if self.dist:
@@ -162,6 +160,33 @@ class ExpertParallelMoE:
         if tokens:
             moe_combine(y_sent, d.weight, d.pos, tokens, k, out)
         return out
+
+    def _tables(self, segs, offsets, device):
+        """Regroup segments (forward and back) and local expert offsets on the
+        device, staged through one pinned buffer and copied asynchronously
+        (a pageable copy would synchronise the stream). The staging buffer is
+        rewritten only by the next call, after its count read-back, which
+        waits for this copy."""
+        import numpy as np
+        import torch
+
+        cap = self.world * self.local
+        nbytes = 2 * cap * 24 + (self.local + 1) * 4
+        if getattr(self, "_staging", None) is None:
+            self._staging = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+            self._tables_dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        host = self._staging.numpy()
+        fwd = host[:cap * 24].view(np.int64).reshape(cap, 3)
+        back = host[cap * 24:2 * cap * 24].view(np.int64).reshape(cap, 3)
+        count = len(segs)
+        fwd[:count] = segs
+        back[:count] = segs[:, [1, 0, 2]]
+        host[2 * cap * 24:].view(np.int32)[:] = offsets
+        self._tables_dev.copy_(self._staging, non_blocking=True)
+        d = self._tables_dev
+        return (d[:cap * 24].view(torch.int64).view(cap, 3)[:count],
+                d[cap * 24:2 * cap * 24].view(torch.int64).view(cap, 3)[:count],
+                d[2 * cap * 24:].view(torch.int32))
 
     def _wref(self):
         import ctypes
