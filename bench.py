@@ -558,10 +558,10 @@ def run_tp(args, rank, world, local_rank):
     groups = tp.llama3_70b_projections()
     weights = tp.synth_shards(groups, layers, world, rank, device)
     reducer = None
-    if dist and args.collective == "peer":
+    if dist and args.collective in ("fused", "peer"):
         from kadan_b200.collectives import PeerAllReduce
 
-        reducer = PeerAllReduce(tokens * 8192)
+        reducer = PeerAllReduce(tokens * 8192, fused=args.collective == "fused")
     stack = tp.DecodeStack(groups, weights, tokens, world, rank, device, group=group, collective=reducer)
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):
@@ -650,7 +650,9 @@ def run_tp(args, rank, world, local_rank):
         "config": {"workload": f"BASELINE config 4 decode: Llama-3-70B Q6_K/Q4_K, {layers} layers, T={tokens}",
                    "weight_bytes_per_step": wbytes, "weight_bytes_per_rank": local_bytes,
                    "parallelism": f"tp{world}",
-                   "collective": ("peer-memory all-reduce kernel (fp32, NVLink stores)" if reducer else
+                   "collective": ("GEMV epilogue stores to peers + gather-sum kernel (fp32, NVLink)"
+                                  if reducer and reducer.fused else
+                                  "peer-memory all-reduce kernel (fp32, NVLink stores)" if reducer else
                                   "NCCL all-reduce (fp32)") + " after o and down",
                    "l2": "inputs larger than L2"},
         "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / peak, 4), "peak_gbs": peak,
@@ -756,8 +758,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
-                    help="all-reduce of --case tp70b at N > 1")
+    ap.add_argument("--collective", choices=["fused", "peer", "nccl"], default="fused",
+                    help="all-reduce of --case tp70b at N > 1: GEMV+exchange fused, peer kernel after the GEMV, NCCL")
     ap.add_argument("--layers", type=int, default=0, help="layers for --case tp70b / ep120b (default 80 / 36)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -371,6 +371,18 @@ KB200_API int kb200_ipc_close(void* ptr);
 KB200_API int kb200_peer_allreduce_f32(float* data, size_t count, void* const* peers, int world, int rank,
                                        size_t max_count, double timeout_s, void* stream);
 
+/* A row-parallel projection plus the all-reduce of its output in one call
+ * (tensor parallelism): job as for kb200_gguf_gemv_batch with contiguous
+ * output rows (stride == columns, rows * columns even and <= max_count);
+ * peers/world/rank/max_count/timeout_s as for kb200_peer_allreduce_f32, whose
+ * call sequence it shares. On the tensor-pipe path (kb200_gemv_path == 2)
+ * the GEMV stores each finished output straight into every peer's buffer
+ * and a gather kernel adds them; otherwise the GEMV is followed by the full
+ * all-reduce. On return (stream order) every rank's output holds the sum over
+ * the ranks, the same bits on each. */
+KB200_API int kb200_gguf_gemv_allreduce(const kb200_gemv_job* job, void* const* peers, int world, int rank,
+                                        size_t max_count, double timeout_s, void* stream);
+
 /* The routing stage alone (for tests): chosen [tokens, top_k] int32,
  * weight [tokens, top_k] fp32, device. */
 KB200_API int kb200_moe_route(

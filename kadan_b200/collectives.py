@@ -20,6 +20,8 @@ lib.kb200_ipc_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
 lib.kb200_ipc_close.argtypes = [ctypes.c_void_p]
 lib.kb200_peer_allreduce_f32.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int,
                                          ctypes.c_int, ctypes.c_size_t, ctypes.c_double, ctypes.c_void_p]
+lib.kb200_gguf_gemv_allreduce.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_size_t,
+                                          ctypes.c_double, ctypes.c_void_p]
 IPC_HANDLE_BYTES = 64
 
 
@@ -27,7 +29,10 @@ class PeerAllReduce:
     """Sum fp32 device tensors of up to `max_count` elements over the ranks of
     `group` (every rank calls with the same sizes in the same order)."""
 
-    def __init__(self, max_count: int, group=None, timeout_s: float = 2.0):
+    def __init__(self, max_count: int, group=None, timeout_s: float = 2.0, fused: bool = True):
+        """fused: row-parallel projections run as kb200_gguf_gemv_allreduce
+        (the GEMV pushes its outputs to the peers itself) instead of a GEMV
+        launch followed by the all-reduce."""
         import torch.distributed as dist
 
         self.dist, self.group = dist, group
@@ -35,6 +40,7 @@ class PeerAllReduce:
         self.rank = dist.get_rank(group)
         self.max_count = int(max_count)
         self.timeout_s = float(timeout_s)
+        self.fused = bool(fused)
         nbytes = int(lib.kb200_peer_buffer_bytes(self.world, self.max_count))
         if not nbytes:
             raise ValueError("peer all-reduce supports 1..8 ranks")
@@ -63,6 +69,12 @@ class PeerAllReduce:
         """In place on `tensor` (fp32, contiguous), enqueued on `stream`."""
         check(lib.kb200_peer_allreduce_f32(tensor.data_ptr(), tensor.numel(), self.peers, self.world, self.rank,
                                            self.max_count, self.timeout_s, ctypes.c_void_p(stream.cuda_stream)))
+
+    def gemv_allreduce(self, job, stream) -> None:
+        """One row-parallel GEMV job (kadan_b200.GemvJob) whose output is then
+        summed over the ranks, enqueued on `stream`."""
+        check(lib.kb200_gguf_gemv_allreduce(ctypes.byref(job), self.peers, self.world, self.rank, self.max_count,
+                                            self.timeout_s, ctypes.c_void_p(stream.cuda_stream)))
 
     def close(self) -> None:
         """Collective: every rank's kernels are done before any buffer goes."""

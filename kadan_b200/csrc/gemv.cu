@@ -740,4 +740,42 @@ int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream
     return KB200_OK;
 }
 
+// A row-parallel projection and the sum of its partial outputs over the
+// group in one call: on the tensor-pipe path the GEMV's epilogue stores each
+// finished output into every peer's buffer as it is written (so the exchange
+// overlaps the rest of the GEMV) and the peer all-reduce kernel only gathers
+// and adds; other paths run the GEMV and then the full all-reduce.
+int kb200_gguf_gemv_allreduce(const kb200_gemv_job* job, void* const* peers, int world, int rank, size_t max_count,
+                              double timeout_s, void* stream_ptr) {
+    if (!job)
+        return fail(KB200_INVALID, "null job");
+    if (const int s = check_job(*job))
+        return s;
+    if (world < 1 || world > kPeerMaxRanks || rank < 0 || rank >= world)
+        return fail(KB200_UNSUPPORTED, "1..8 ranks");
+    if (job->stride != job->columns)
+        return fail(KB200_INVALID, "the all-reduced output must be contiguous rows");
+    const size_t count = size_t(job->rows) * job->columns;
+    if (world > 1 && (!peers || count % 2 || count > max_count))
+        return fail(KB200_INVALID, "output must be an even number of floats within the peer buffers");
+    auto stream = static_cast<cudaStream_t>(stream_ptr);
+    if (world == 1)
+        return kb200_gguf_gemv_batch(job, 1, stream_ptr);
+    PeerOut g;
+    std::memset(&g, 0, sizeof(g));
+    for (int r = 0; r < world; ++r)
+        g.peers[r] = static_cast<uint8_t*>(peers[r]);
+    g.max_count = max_count;
+    g.rank = rank;
+    g.world = world;
+    const bool fused = path_of(*job) == 2;
+    if (fused) {
+        if (const int s = launch_mma({job}, stream, &g))
+            return s;
+    } else if (const int s = kb200_gguf_gemv_batch(job, 1, stream_ptr)) {
+        return s;
+    }
+    return launch_peer_allreduce(job->output, count, g, timeout_s, !fused, stream);
+}
+
 }  // extern "C"

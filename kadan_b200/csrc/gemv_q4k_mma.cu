@@ -103,7 +103,23 @@ struct MmaParams {
     // words; zero between launches.
     unsigned long long* partials;
     unsigned* watchdog;
+    // Tensor-parallel exchange (world > 1): the outputs of the launch's one
+    // job also go to slot [rank] of every peer's buffer, as words tagged
+    // with the group's next call number.
+    PeerOut peer;
 };
+
+// One output value into slot [rank] of every peer: 64-bit {call, value}
+// words, which the gather kernel of the same call reads and adds.
+__device__ __forceinline__ void push_peers(const PeerOut& g, uint32_t call, size_t index, float v) {
+    const unsigned long long w = (unsigned long long)call << 32 | __float_as_uint(v);
+    const size_t slot = (size_t(call & 1u) * kPeerMaxRanks + g.rank) * g.max_count + index;
+    for (int q = 0; q < g.world; ++q)
+        if (q != g.rank) {
+            unsigned long long* at = reinterpret_cast<unsigned long long*>(g.peers[q] + kPeerWordsOff) + slot;
+            asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(at), "l"(w) : "memory");
+        }
+}
 
 // Relaxed 64-bit global accesses: single-copy atomic, so a partial sum and
 // its "present" tag, stored as one word, are seen together or not at all.
@@ -545,15 +561,26 @@ __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc
         }
     }
     if (write) {
+        // The group's call number: the gather kernels of earlier calls have
+        // finished (grid-dependency wait above), and each advanced the counters.
+        const bool push = p.peer.world > 1;
+        const uint32_t call = push ? reinterpret_cast<const uint32_t*>(p.peer.peers[p.peer.rank])[0] + 1u : 0u;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int tok = nt * 4 + t;
             if (tok < rows) {
-                float* out = job.output + size_t(r0 + tok) * job.stride;
-                if (valid_lo)
+                const size_t row = size_t(r0 + tok) * job.stride;
+                float* out = job.output + row;
+                if (valid_lo) {
                     out[my_row] = acc[nt][0];
-                if (valid_hi)
+                    if (push)
+                        push_peers(p.peer, call, row + my_row, acc[nt][0]);
+                }
+                if (valid_hi) {
                     out[my_row + 8] = acc[nt][1];
+                    if (push)
+                        push_peers(p.peer, call, row + my_row + 8, acc[nt][1]);
+                }
             }
         }
     }
@@ -1222,7 +1249,7 @@ bool mma_eligible(const kb200_gemv_job& j) {
 // Q6_K: 16-row tiles, units of (tile, chunk of 8 blocks), up to 4 input rows
 // per pass (more rows become row groups), balanced split when whole tiles
 // would leave a tenth of the CTA slots idle.
-int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream) {
+int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer) {
     auto encode = encode_fn();
     if (!encode)
         return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -1239,6 +1266,8 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         std::memset(&p, 0, sizeof(p));
         p.watchdog = watchdog_word();
         p.tile_rows = kQ6Rows;
+        if (peer)
+            p.peer = *peer;
         uint32_t tiles = 0, units = 0;
         for (size_t m = 0; m < n; ++m) {
             const auto& j = *jobs[first + m];
@@ -1299,7 +1328,7 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     return KB200_OK;
 }
 
-int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream) {
+int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer) {
     auto encode = encode_fn();
     if (!encode)
         return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -1358,6 +1387,8 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         std::memset(&p, 0, sizeof(p));
         p.watchdog = watchdog_word();
         p.tile_rows = R;
+        if (peer)
+            p.peer = *peer;
         p.prefetch = tuning().prefetch;
         uint32_t tiles = 0, units = 0;
         for (size_t m = 0; m < n; ++m) {
@@ -1414,10 +1445,13 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     return KB200_OK;
 }
 
-int launch_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream) {
+int launch_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer) {
     if (jobs.empty())
         return KB200_OK;
-    return jobs.front()->encoding == KB200_Q6_K ? launch_q6k_mma(jobs, stream) : launch_q4k_mma(jobs, stream);
+    if (peer && peer->world > 1 && (jobs.size() != 1 || jobs.front()->stride != jobs.front()->columns))
+        return fail(KB200_INVALID, "a peer exchange takes one job with contiguous output rows");
+    return jobs.front()->encoding == KB200_Q6_K ? launch_q6k_mma(jobs, stream, peer)
+                                                : launch_q4k_mma(jobs, stream, peer);
 }
 
 }  // namespace kb200

@@ -31,16 +31,17 @@
 #include <algorithm>
 #include <cstring>
 
+#include "gemv_mma.hpp"
 #include "kb200_device.cuh"
 #include "kb200_host.hpp"
 
 namespace kb200 {
 namespace {
 
-constexpr int kMaxRanks = 8;
+constexpr int kMaxRanks = kPeerMaxRanks;
 constexpr int kMaxCtas = 256;
 constexpr int kArThreads = 256;
-constexpr size_t kWordsOff = 4096;  // after the epoch counters
+constexpr size_t kWordsOff = kPeerWordsOff;  // after the epoch counters
 constexpr unsigned watchdog_peer = 16u;  // a peer's words never arrived
 
 struct ArParams {
@@ -48,6 +49,7 @@ struct ArParams {
     float* data;                // in/out, count floats
     size_t count, max_count;
     int rank, world;
+    int push;  // 0: the values are already in the peers' slots (fused GEMV)
     unsigned long long timeout_ns;
     unsigned* watchdog;
 };
@@ -91,7 +93,7 @@ __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(const __grid
     const size_t stride = size_t(gridDim.x) * kArThreads;
 
     // 1. Push: this rank's elements into slot [rank] of every peer.
-    for (size_t i = size_t(c) * kArThreads + tid; i < npairs; i += stride) {
+    for (size_t i = size_t(c) * kArThreads + tid; p.push && i < npairs; i += stride) {
         const float2 v = pairs[i];
         const unsigned long long w0 = tag | __float_as_uint(v.x), w1 = tag | __float_as_uint(v.y);
         for (int q = 0; q < p.world; ++q)
@@ -207,29 +209,48 @@ int kb200_peer_allreduce_f32(float* data, size_t count, void* const* peers, int 
         return fail(KB200_UNSUPPORTED, "1..8 ranks");
     if (!count || world == 1)
         return KB200_OK;
-    if (!data || !peers)
+    if (!peers)
         return fail(KB200_INVALID, "null pointer");
-    if (count % 2 || !aligned(data, 8) || count > max_count || max_count % 2)
+    PeerOut g;
+    std::memset(&g, 0, sizeof(g));
+    for (int r = 0; r < world; ++r)
+        g.peers[r] = static_cast<uint8_t*>(peers[r]);
+    g.max_count = max_count;
+    g.rank = rank;
+    g.world = world;
+    return launch_peer_allreduce(data, count, g, timeout_s, true, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+namespace kb200 {
+
+int launch_peer_allreduce(float* data, size_t count, const PeerOut& g, double timeout_s, bool push,
+                          cudaStream_t stream) {
+    if (!data)
+        return fail(KB200_INVALID, "null pointer");
+    if (count % 2 || !aligned(data, 8) || count > g.max_count || g.max_count % 2)
         return fail(KB200_INVALID, "count must be an even number of floats within the buffer, data 8-byte aligned");
     ArParams p;
     std::memset(&p, 0, sizeof(p));
-    for (int r = 0; r < world; ++r) {
-        if (!peers[r] || !aligned(peers[r], 256))
+    for (int r = 0; r < g.world; ++r) {
+        if (!g.peers[r] || !aligned(g.peers[r], 256))
             return fail(KB200_INVALID, "peer buffers must be 256-byte aligned");
-        p.peers[r] = static_cast<uint8_t*>(peers[r]);
+        p.peers[r] = g.peers[r];
     }
     const size_t ctas = std::min<size_t>(kMaxCtas, (count / 2 + kArThreads - 1) / kArThreads);
     p.data = data;
     p.count = count;
-    p.max_count = max_count;
-    p.rank = rank;
-    p.world = world;
+    p.max_count = g.max_count;
+    p.rank = g.rank;
+    p.world = g.world;
+    p.push = push ? 1 : 0;
     p.timeout_ns = static_cast<unsigned long long>(std::max(0.001, timeout_s) * 1e9);
     p.watchdog = watchdog_word();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(ctas));
     cfg.blockDim = dim3(kArThreads);
-    cfg.stream = static_cast<cudaStream_t>(stream);
+    cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -239,4 +260,4 @@ int kb200_peer_allreduce_f32(float* data, size_t count, void* const* peers, int 
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "peer_allreduce_kernel launch");
 }
 
-}  // extern "C"
+}  // namespace kb200

@@ -186,7 +186,11 @@ class DecodeStack:
         import torch.distributed as dist
 
         sptr = ctypes.c_void_p(stream.cuda_stream)
+        fused = getattr(self.collective, "fused", False)
         for arr, n, reduce in self.calls:
+            if fused and reduce and n == 1:
+                self.collective.gemv_allreduce(arr[0], stream)
+                continue
             check(lib.kb200_gguf_gemv_batch(arr, n, sptr))
             for t in reduce:
                 if self.collective is not None:

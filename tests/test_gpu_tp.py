@@ -66,10 +66,10 @@ def run_rank(rank: int, world: int, port: int, collective: str = "nccl") -> dict
         xs = {g[0].name: synth.activations(TOKENS * g[0].in_, seed=7 + gi, dtype="bf16").reshape(TOKENS, g[0].in_)
               for gi, g in enumerate(groups)}
         reducer = None
-        if world > 1 and collective == "peer":
+        if world > 1 and collective in ("peer", "fused"):
             from kadan_b200.collectives import PeerAllReduce
 
-            reducer = PeerAllReduce(TOKENS * 1024)
+            reducer = PeerAllReduce(TOKENS * 1024, fused=collective == "fused")
         stack = tp.DecodeStack(groups, weights, TOKENS, world, rank, device,
                                inputs={k: torch.from_numpy(v).to(device) for k, v in xs.items()},
                                collective=reducer)
@@ -100,6 +100,17 @@ def run_rank(rank: int, world: int, port: int, collective: str = "nccl") -> dict
         for name, y in want.items():
             errs[f"graph/{name}"] = _rel(stack.outputs[name].cpu().numpy(), y)
         graph = None
+        if reducer is not None and reducer.fused:
+            # The fused GEMV + exchange and the GEMV followed by the all-reduce
+            # kernel add the same values in the same order: same bits.
+            fused_out = {k: v.clone() for k, v in stack.outputs.items()}
+            reducer.fused = False
+            with torch.cuda.stream(stream):
+                stack.launch(stream)
+            torch.cuda.synchronize()
+            for name in ("o", "down"):
+                same = torch.equal(fused_out[name].view(torch.int32), stack.outputs[name].view(torch.int32))
+                errs[f"bitwise/{name}"] = 0.0 if same else float("inf")
         if reducer:
             reducer.close()
         return errs
@@ -232,6 +243,18 @@ def test_tp_two_ranks_peer_collective_match_oracle(cuda):
     for r in range(2):
         bad = {k: v for k, v in results[r].items() if not v < TOL}
         assert not bad, (r, bad)
+
+
+def test_tp_two_ranks_fused_gemv_allreduce_match_oracle(cuda):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("two GPUs needed")
+    results = _spawn(_child, lambda r, port: (r, 2, port, "fused"))
+    for r in range(2):
+        bad = {k: v for k, v in results[r].items() if not v < TOL}
+        assert not bad, (r, bad)
+        assert "bitwise/o" in results[r] and "bitwise/down" in results[r]
 
 
 def test_tp_two_ranks_match_oracle(cuda):
