@@ -1158,8 +1158,9 @@ const Fixup* fixup_for(cudaStream_t stream) {
 struct Tuning {
     bool balanced = true;  // KB200_GEMV_BALANCED=0: whole tiles round-robin
     uint32_t prefetch = 0; // KB200_GEMV_L2_PREFETCH=<stages>
-    uint32_t min_units = kMinUnitsPerCta;  // KB200_GEMV_MIN_UNITS=<units per CTA>
-    int ctas_per_sm = 0;                   // KB200_GEMV_CTAS_PER_SM=<n>: grid slots per SM (0: all that fit)
+    uint32_t min_units = kMinUnitsPerCta;       // KB200_GEMV_MIN_UNITS=<units per CTA>
+    uint32_t q6_min_units = kQ6MinUnitsPerCta;  // KB200_GEMV_Q6K_MIN_UNITS=<units per CTA>
+    int ctas_per_sm = 0;                        // KB200_GEMV_CTAS_PER_SM=<n>: grid slots per SM (0: all that fit)
 };
 
 const Tuning& tuning() {
@@ -1171,6 +1172,8 @@ const Tuning& tuning() {
             v.ctas_per_sm = std::max(0, std::atoi(s));
         if (const char* s = std::getenv("KB200_GEMV_MIN_UNITS"))
             v.min_units = uint32_t(std::max(1, std::atoi(s)));
+        if (const char* s = std::getenv("KB200_GEMV_Q6K_MIN_UNITS"))
+            v.q6_min_units = uint32_t(std::max(1, std::atoi(s)));
         if (const char* s = std::getenv("KB200_GEMV_L2_PREFETCH"))
             v.prefetch = uint32_t(std::max(0, std::min(64, std::atoi(s))));
         return v;
@@ -1304,7 +1307,7 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         const uint64_t waves = (tiles + uint64_t(slots) - 1) / uint64_t(slots);
         const bool ragged = uint64_t(tiles) * 10 < waves * uint64_t(slots) * 9;
         const bool balanced = fixup && fixup->ctas >= uint32_t(slots) && ragged
-                              && uint64_t(units) >= uint64_t(kQ6MinUnitsPerCta) * uint64_t(slots);
+                              && uint64_t(units) >= uint64_t(tuning().q6_min_units) * uint64_t(slots);
         uint32_t grid = std::min(tiles, uint32_t(slots));
         if (balanced) {
             grid = std::min(units, uint32_t(slots));
