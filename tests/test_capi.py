@@ -90,3 +90,75 @@ def test_dequant_rejects_partial_blocks(kb):
     assert kb.lib.kb200_gguf_dequant(kb.Q4_K, FAKE_W, 100, FAKE_Y, None, None) == kb.INVALID
     assert kb.lib.kb200_gguf_dequant(kb.IQ2_S, FAKE_W, 256, FAKE_Y, None, None) == kb.UNSUPPORTED
     assert kb.lib.kb200_gguf_dequant(kb.Q4_K, FAKE_W, 256, FAKE_W + 16, None, None) == kb.ALIAS
+
+
+def test_gemv_allreduce_rejects_bad_groups_before_any_launch(kb):
+    from kadan_b200 import collectives  # noqa: F401  (declares the argument types)
+
+    peers = (ctypes.c_void_p * 2)(0x40000000, 0x48000000)
+
+    def ar(j, world=2, rank=0, peers_=peers, max_count=1 << 20):
+        return kb.lib.kb200_gguf_gemv_allreduce(None if j is None else ctypes.byref(j), peers_, world, rank,
+                                                max_count, 2.0, None)
+
+    assert ar(None) == kb.INVALID
+    assert ar(job(kb, encoding=kb.IQ2_S)) == kb.UNSUPPORTED
+    assert ar(job(kb), world=9) == kb.UNSUPPORTED
+    assert ar(job(kb), rank=2) == kb.UNSUPPORTED
+    assert ar(job(kb, stride=128)) == kb.INVALID  # output rows must be contiguous
+    assert ar(job(kb), peers_=None) == kb.INVALID
+    assert ar(job(kb, columns=63, stride=63)) == kb.INVALID  # odd number of values
+    assert ar(job(kb, rows=4, stride=64), max_count=128) == kb.INVALID  # more values than the buffers hold
+
+
+def test_peer_allreduce_host_checks(kb):
+    from kadan_b200 import collectives  # noqa: F401
+
+    assert kb.lib.kb200_peer_buffer_bytes(0, 1024) == 0
+    assert kb.lib.kb200_peer_buffer_bytes(9, 1024) == 0
+    assert kb.lib.kb200_peer_buffer_bytes(2, 8192) == 4096 + 2 * 8 * 8192 * 8
+    peers = (ctypes.c_void_p * 2)(0x40000000, 0x48000000)
+    f = kb.lib.kb200_peer_allreduce_f32
+    assert f(FAKE_Y, 8192, peers, 9, 0, 8192, 2.0, None) == kb.UNSUPPORTED
+    assert f(FAKE_Y, 8192, peers, 1, 0, 8192, 2.0, None) == kb.OK  # one rank: nothing to add
+    assert f(FAKE_Y, 8191, peers, 2, 0, 8192, 2.0, None) == kb.INVALID
+    assert f(FAKE_Y, 16384, peers, 2, 0, 8192, 2.0, None) == kb.INVALID
+    assert f(FAKE_Y, 8192, None, 2, 0, 8192, 2.0, None) == kb.INVALID
+    misaligned = (ctypes.c_void_p * 2)(0x40000000, 0x48000010)
+    assert f(FAKE_Y, 8192, misaligned, 2, 0, 8192, 2.0, None) == kb.INVALID
+
+
+def test_moe_stages_host_checks(kb):
+    lib = kb.lib
+    assert lib.kb200_moe_dispatch_workspace_bytes(64, 100, 32, 4) == 0  # hidden not a multiple of 64
+    assert lib.kb200_moe_dispatch_workspace_bytes(64, 2880, 32, 4) > 64 * 4 * 2880 * 2
+    d = kb.MoeDispatch()
+    ws = 0x60000000
+    assert lib.kb200_moe_dispatch_rows(FAKE_X, FAKE_Y, 64, 2880, 32, 4, ws, 1 << 30, None, None, None) == kb.INVALID
+    assert lib.kb200_moe_dispatch_rows(FAKE_X, FAKE_Y, 0, 2880, 32, 4, ws, 1 << 30, ctypes.byref(d), None,
+                                       None) == kb.OK
+    assert d.count == 0
+    assert lib.kb200_moe_dispatch_rows(FAKE_X, FAKE_Y, 64, 2880, 32, 40, ws, 1 << 30, ctypes.byref(d), None,
+                                       None) == kb.UNSUPPORTED  # top_k above 32
+    assert lib.kb200_moe_dispatch_rows(None, FAKE_Y, 64, 2880, 32, 4, ws, 1 << 30, ctypes.byref(d), None,
+                                       None) == kb.INVALID
+    assert lib.kb200_moe_dispatch_rows(FAKE_X, FAKE_Y, 64, 2880, 32, 4, ws, 1024, ctypes.byref(d), None,
+                                       None) == kb.NO_MEMORY
+    w = kb.MoeWeights(0x70000000, 0x71000000, None, 0x72000000, 0x73000000, None, 2880, 2880, 2, 4, 0, 1, 7.0, 1.702)
+    # The expert stage ignores top_k (a rank may hold fewer experts than k).
+    assert lib.kb200_moe_experts_workspace_bytes(ctypes.byref(w), 100) > 0
+    assert lib.kb200_moe_experts(ctypes.byref(w), FAKE_X, FAKE_Y, 0, FAKE_Y, ws, 1 << 30, None, None) == kb.OK
+    assert lib.kb200_moe_experts(ctypes.byref(w), None, FAKE_Y, 10, FAKE_Y, ws, 1 << 30, None, None) == kb.INVALID
+    assert lib.kb200_moe_experts(ctypes.byref(w), FAKE_X, FAKE_Y, 10, FAKE_Y, ws, 16, None, None) == kb.NO_MEMORY
+    c = lib.kb200_moe_combine
+    assert c(FAKE_X, FAKE_Y, FAKE_W, 10, 0, 2880, FAKE_Y, None) == kb.UNSUPPORTED
+    assert c(FAKE_X, FAKE_Y, FAKE_W, 10, 4, 2882, FAKE_Y, None) == kb.UNSUPPORTED
+    assert c(FAKE_X, FAKE_Y, FAKE_W, 0, 4, 2880, FAKE_Y, None) == kb.OK
+    assert c(None, FAKE_Y, FAKE_W, 10, 4, 2880, FAKE_Y, None) == kb.INVALID
+    assert c(FAKE_X + 4, FAKE_Y, FAKE_W, 10, 4, 2880, FAKE_Y, None) == kb.INVALID
+    r = lib.kb200_rows_regroup
+    segs = 0x74000000
+    assert r(FAKE_X, FAKE_Y, 5760, segs, 0, 0, None) == kb.OK
+    assert r(FAKE_X, FAKE_Y, 5762, segs, 4, 10, None) == kb.INVALID
+    assert r(None, FAKE_Y, 5760, segs, 4, 10, None) == kb.INVALID
+    assert r(FAKE_X, FAKE_Y, 5760, segs, 70000, 10, None) == kb.UNSUPPORTED
