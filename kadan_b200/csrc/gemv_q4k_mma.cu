@@ -833,18 +833,26 @@ constexpr int kQ6Block = 210;
 constexpr int kQ6Chunk = 8;                       // blocks per TMA unit
 constexpr int kQ6Rows = 16;                       // rows per tile
 constexpr int kQ6StageBytes = kQ6Rows * kQ6Chunk * kQ6Block;  // 26880
-constexpr int kQ6SegBudget = 4 * kQ6Chunk * kTokenBlockTotal;  // one chunk of 4 tokens
+// Activation segment: one chunk of 4 * NT tokens.
+template <int NT> constexpr int q6_seg_budget() {
+    return 4 * NT * kQ6Chunk * kTokenBlockTotal;
+}
 constexpr uint32_t kQ6MinUnitsPerCta = 2;
 
-struct Q6Layout {
+// NT = 1 (4 rows per pass): 3 stages; NT = 2 (8 rows): 2 stages, so that the
+// twice larger activation segment still leaves room for two CTAs per SM.
+template <int NT> struct Q6Layout {
+    static constexpr int kStages = NT == 1 ? 3 : 2;
+    static constexpr int kSegBudget = q6_seg_budget<NT>();
     static constexpr int kStagesOff = 0;
     static constexpr int kSegOff = kStages * kQ6StageBytes;
-    static constexpr int kRedOff = kSegOff + kQ6SegBudget;
+    static constexpr int kRedOff = kSegOff + kSegBudget;
     static constexpr int kRedBytes = kConsumerThreads * 4 * 4;
     static constexpr int kBarOff = kRedOff + kRedBytes;
     static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
 };
-static_assert(Q6Layout::kSegOff - Q6Layout::kStagesOff == 3 * kQ6StageBytes, "stage ring");
+static_assert(2 * (Q6Layout<1>::kTotal + 128 + 1024) <= 228 * 1024, "two Q6_K CTAs per SM (NT = 1)");
+static_assert(2 * (Q6Layout<2>::kTotal + 128 + 1024) <= 228 * 1024, "two Q6_K CTAs per SM (NT = 2)");
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
     asm volatile(
@@ -882,9 +890,10 @@ template <bool kOdd> __device__ __forceinline__ uint32_t ld_word(const uint8_t* 
 // One block of rows g (bg) and g + 8 (b8) for one n-tile of tokens: adds the
 // block's contribution to acc. bq: this lane's B words of the block, indexed
 // [(s * rows + tok) * 2 + part] * 4 + t.
-template <bool kOdd>
-__device__ __forceinline__ void q6k_block(const uint8_t* bg, const uint8_t* b8, const uint32_t* bq, int rows, int tokb,
-                                          int part, int t, float sc_tok, float (&acc)[2], bool& finite_g, bool& finite_8) {
+template <bool kOdd, int NT>
+__device__ __forceinline__ void q6k_block(const uint8_t* bg, const uint8_t* b8, const uint32_t* bq, int rows,
+                                          const int (&tokb)[NT], int part, int t, const float (&sc_tok)[NT],
+                                          float (&acc)[NT][2], bool& finite_g, bool& finite_8) {
     const float dg = half_bits_to_float(*reinterpret_cast<const uint16_t*>(bg + 208));
     const float d8 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b8 + 208));
     finite_g = finite_g && isfinite(dg);
@@ -895,7 +904,11 @@ __device__ __forceinline__ void q6k_block(const uint8_t* bg, const uint8_t* b8, 
         scg[w] = ld_word<kOdd>(bg + 192 + 4 * w);
         sc8[w] = ld_word<kOdd>(b8 + 192 + 4 * w);
     }
-    int Ig[2] = {0, 0}, I8[2] = {0, 0};
+    // int32 sums sum_s sc_s C_s: [nt][h, l] for rows g and g + 8.
+    int Ig[NT][2], I8[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+        Ig[nt][0] = Ig[nt][1] = I8[nt][0] = I8[nt][1] = 0;
 #pragma unroll
     for (int ip = 0; ip < 2; ++ip)
 #pragma unroll
@@ -913,17 +926,24 @@ __device__ __forceinline__ void q6k_block(const uint8_t* bg, const uint8_t* b8, 
                 const uint32_t h8 = qt == 3 ? qh_8 >> 2 : qh_8 << (4 - 2 * qt);
                 const uint32_t vg = (((ng & 0x0F0F0F0Fu) | (hg & 0x30303030u)) + 0x60606060u) ^ 0x80808080u;
                 const uint32_t v8 = (((n8 & 0x0F0F0F0Fu) | (h8 & 0x30303030u)) + 0x60606060u) ^ 0x80808080u;
-                const uint32_t b = bq[((sb * rows + tokb) * 2 + part) * 4 + t];
-                int C[4];
-                imma16(C, vg, v8, b);
                 const int sg = int(int8_t(scg[sb >> 2] >> (8 * (sb & 3))));
                 const int s8 = int(int8_t(sc8[sb >> 2] >> (8 * (sb & 3))));
-                Ig[0] += sg * C[0], Ig[1] += sg * C[1];
-                I8[0] += s8 * C[2], I8[1] += s8 * C[3];
+                // One A operand (the weights) for every n-tile of tokens.
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const uint32_t b = bq[((sb * rows + tokb[nt]) * 2 + part) * 4 + t];
+                    int C[4];
+                    imma16(C, vg, v8, b);
+                    Ig[nt][0] += sg * C[0], Ig[nt][1] += sg * C[1];
+                    I8[nt][0] += s8 * C[2], I8[nt][1] += s8 * C[3];
+                }
             }
         }
-    acc[0] = fmaf(dg * sc_tok, fmaf(float(Ig[1]), 1.f / 254.f, float(Ig[0])), acc[0]);
-    acc[1] = fmaf(d8 * sc_tok, fmaf(float(I8[1]), 1.f / 254.f, float(I8[0])), acc[1]);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        acc[nt][0] = fmaf(dg * sc_tok[nt], fmaf(float(Ig[nt][1]), 1.f / 254.f, float(Ig[nt][0])), acc[nt][0]);
+        acc[nt][1] = fmaf(d8 * sc_tok[nt], fmaf(float(I8[nt][1]), 1.f / 254.f, float(I8[nt][0])), acc[nt][1]);
+    }
 }
 
 // Q6_K decode GEMV, T <= 4 input rows per pass. Tiles of 16 rows; a unit of
@@ -933,7 +953,8 @@ __device__ __forceinline__ void q6k_block(const uint8_t* bg, const uint8_t* b8, 
 // programmatic dependent launch) is the Q4_K kernel's.
 template <int NT>
 __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid_constant__ MmaParams p) {
-    using L = Q6Layout;
+    using L = Q6Layout<NT>;
+    constexpr int kStages = L::kStages;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
     auto* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -1006,7 +1027,7 @@ __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid
         const int rows = int(min(job.group_rows, job.rows - r0));
         const int nblocks = int(job.in / 256);
         const float* x = job.input + size_t(r0) * job.in;
-        const Segment seg(rows, kQ6Chunk, kQ6SegBudget, L::kSegOff);
+        const Segment seg(rows, kQ6Chunk, L::kSegBudget, L::kSegOff);
         if (seg.blocks < kQ6Chunk)
             atomicExch(abort_flag, 1);
         const uint32_t* frag = reinterpret_cast<const uint32_t*>(seg.frag(smem));
@@ -1048,15 +1069,17 @@ __global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid
                     const uint8_t* bg = stage + g * (kQ6Chunk * kQ6Block) + b * kQ6Block;
                     const uint8_t* b8 = bg + 8 * (kQ6Chunk * kQ6Block);
                     const uint32_t* bq = frag + sblk * rows * (kTokenBlockBytes / 4);
+                    int tokb[NT];
+                    float sc_tok[NT];
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
-                        const int tokb = min(nt * 4 + (g >> 1), rows - 1);
-                        const float sc_tok = scales[sblk * rows + min(nt * 4 + t, rows - 1)];
-                        if (bb)
-                            q6k_block<true>(bg, b8, bq, rows, tokb, g & 1, t, sc_tok, acc[nt], finite_g, finite_8);
-                        else
-                            q6k_block<false>(bg, b8, bq, rows, tokb, g & 1, t, sc_tok, acc[nt], finite_g, finite_8);
+                        tokb[nt] = min(nt * 4 + (g >> 1), rows - 1);
+                        sc_tok[nt] = scales[sblk * rows + min(nt * 4 + t, rows - 1)];
                     }
+                    if (bb)
+                        q6k_block<true, NT>(bg, b8, bq, rows, tokb, g & 1, t, sc_tok, acc, finite_g, finite_8);
+                    else
+                        q6k_block<false, NT>(bg, b8, bq, rows, tokb, g & 1, t, sc_tok, acc, finite_g, finite_8);
                 }
             }
             __syncwarp();
@@ -1181,19 +1204,19 @@ const Tuning& tuning() {
     return t;
 }
 
-int q6k_slots() {
+template <int NT> int q6k_slots() {
     static int blocks_per_sm[64] = {};
     static std::mutex lock;
     int dev = 0;
     cudaGetDevice(&dev);
-    constexpr int smem = Q6Layout::kTotal + 128;
+    constexpr int smem = Q6Layout<NT>::kTotal + 128;
     std::lock_guard<std::mutex> guard(lock);
     if (!blocks_per_sm[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_mma_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_mma_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_mma_kernel attribute");
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_mma_kernel<1>, kThreadsQ, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_mma_kernel<NT>, kThreadsQ, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_mma_kernel occupancy");
         blocks_per_sm[dev] = n > 0 ? n : 1;
@@ -1256,8 +1279,13 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     auto encode = encode_fn();
     if (!encode)
         return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
-    constexpr uint32_t group_rows = 4;
-    int slots = q6k_slots();
+    // Rows per pass: up to 4 in one n-tile, up to 8 in two.
+    int max_rows = 1;
+    for (const auto* j : jobs)
+        max_rows = std::max(max_rows, int(std::min(j->rows, uint32_t(KB200_BATCH_ROWS))));
+    const int nt = max_rows <= 4 ? 1 : 2;
+    const uint32_t group_rows = uint32_t(4 * nt);
+    int slots = nt == 1 ? q6k_slots<1>() : q6k_slots<2>();
     if (slots <= 0)
         return -slots;
     if (tuning().ctas_per_sm > 0)
@@ -1317,14 +1345,15 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
         cfg.blockDim = dim3(kThreadsQ);
-        cfg.dynamicSmemBytes = Q6Layout::kTotal + 128;
+        cfg.dynamicSmemBytes = (nt == 1 ? Q6Layout<1>::kTotal : Q6Layout<2>::kTotal) + 128;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1>, p);
+        const cudaError_t e = nt == 1 ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1>, p)
+                                      : cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<2>, p);
         if (e != cudaSuccess)
             return cuda_fail(e, "gemv_q6k_mma_kernel launch");
     }
