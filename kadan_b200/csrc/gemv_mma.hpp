@@ -26,7 +26,7 @@ struct PeerOut {
 // of whole super-blocks, and the driver's tensor-map encoder is available.
 bool mma_eligible(const kb200_gemv_job& job);
 // Jobs of one encoding: one launch per 32 jobs; rows above the kernel's rows
-// per pass (8 for Q4_K, 4 for Q6_K) become row groups. With `peer`, the
+// per pass (8) become row groups. With `peer`, the
 // single job's outputs (rows x columns, contiguous) also go, as words tagged
 // with the group's next call number, to slot [rank] of every peer's buffer.
 int launch_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer = nullptr);
