@@ -946,7 +946,7 @@ __device__ __forceinline__ void q6k_block(const uint8_t* bg, const uint8_t* b8, 
     }
 }
 
-// Q6_K decode GEMV, T <= 4 input rows per pass. Tiles of 16 rows; a unit of
+// Q6_K decode GEMV, T <= 4 NT input rows per pass. Tiles of 16 rows; a unit of
 // the balanced split is (tile, chunk of 8 blocks); each stage is one chunk,
 // its 8 blocks split over the 4 consumer warps (2 each), which add up in
 // shared memory at the end of a piece. Everything else (pieces, fixup,
@@ -1272,7 +1272,7 @@ bool mma_eligible(const kb200_gemv_job& j) {
     return false;
 }
 
-// Q6_K: 16-row tiles, units of (tile, chunk of 8 blocks), up to 4 input rows
+// Q6_K: 16-row tiles, units of (tile, chunk of 8 blocks), up to 8 input rows
 // per pass (more rows become row groups), balanced split when whole tiles
 // would leave a tenth of the CTA slots idle.
 int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer) {
