@@ -217,22 +217,15 @@ __global__ void moe_combine_kernel(
 }
 
 // ----------------------------------------------------------- grouped GEMM
-// Weight tiles of BN = 256 rows (128 when there are too few tiles to fill the
-// SMs): the activation tiles stream in at a bounded rate per SM (the same
-// limit the Q4_K prefill GEMM measured), so a taller weight tile halves the
-// activation bytes per FLOP. Separate rings for activation tiles (TMA), raw
-// MXFP4 codes (TMA) and dequantised fp16 weight tiles, as in the prefill GEMM.
-constexpr int BM = 128, BK = 64;
-constexpr int kABytes = BM * BK * 2;
+constexpr int BM = 128, BN = 128, BK = 64, kStagesG = 4;
+constexpr int kABytes = BM * BK * 2, kBBytes = BN * BK * 2, kRawBytes = BN * BK / 2;
 constexpr int kMaxK = 4096;
-constexpr int kDequantWarps = 8;
-constexpr int kDequantThreads = 32 * kDequantWarps;
-constexpr int kThreadsG = 64 + kDequantThreads + 128;  // producer, MMA, dequant warps, 4 epilogue warps
-constexpr int kMaxStagesG = 4;
+constexpr int kScaleBytes = BN * (kMaxK / 32);
+constexpr int kThreadsG = 320;  // producer, MMA, 4 dequant warps, 4 epilogue warps
 
 struct GroupParams {
     CUtensorMap a_map;  // fp16 [rows, K], box {64, 128}, 128-byte swizzle
-    CUtensorMap b_map;  // u8 codes [E * Nrows, K/2], box {32, BN} or {32, BN/2} (split)
+    CUtensorMap b_map;  // u8 codes [E * Nrows, K/2], box {32, 128} or {32, 64} (split)
     const uint8_t* scales;  // [E * Nrows, K/32]
     const float* bias;      // [E * Nrows] or null
     const int* offsets;     // [E + 1]
@@ -245,28 +238,18 @@ struct GroupParams {
 };
 
 struct GemmShared {
-    uint64_t a_full[kMaxStagesG], a_empty[kMaxStagesG], b_full[kMaxStagesG], b_empty[kMaxStagesG];
-    uint64_t raw_full[kMaxStagesG], raw_empty[kMaxStagesG];
+    uint64_t tma_full[kStagesG], b_full[kStagesG], stage_empty[kStagesG];
     uint64_t sc_full[2], sc_empty[2], acc_full[2], acc_empty[2];
     uint32_t tmem_base;
     int abort;
 };
 
-template <int BN> struct GTile {
-    static constexpr int kAStages = 4;
-    static constexpr int kBStages = BN == 256 ? 2 : 4;
-    static constexpr int kRawStages = BN == 256 ? 3 : 4;
-    static constexpr int kBBytes = BN * BK * 2, kRawBytes = BN * BK / 2;
-    static constexpr int kScaleBytes = BN * (kMaxK / 32);
-    static constexpr int kThreadsPerRow = kDequantThreads / BN;  // 1 or 2
-    static constexpr int kSmemA = 0;
-    static constexpr int kSmemB = kSmemA + kAStages * kABytes;
-    static constexpr int kSmemRaw = kSmemB + kBStages * kBBytes;
-    static constexpr int kSmemScale = kSmemRaw + kRawStages * kRawBytes;
-    static constexpr int kSmemShared = kSmemScale + 2 * kScaleBytes;
-    static constexpr int kSmemTotal = kSmemShared + int(sizeof(GemmShared)) + 1024;  // + alignment slack
-};
-static_assert(GTile<256>::kSmemTotal <= 232448 && GTile<128>::kSmemTotal <= 232448, "shared memory per CTA");
+constexpr int kSmemA = 0;
+constexpr int kSmemB = kSmemA + kStagesG * kABytes;
+constexpr int kSmemRaw = kSmemB + kStagesG * kBBytes;
+constexpr int kSmemScale = kSmemRaw + kStagesG * kRawBytes;
+constexpr int kSmemShared = kSmemScale + 2 * kScaleBytes;
+constexpr int kSmemTotal = kSmemShared + int(sizeof(GemmShared)) + 1024;
 
 struct TileInfo {
     int e, m0, mend, nt;
@@ -291,7 +274,6 @@ __device__ __forceinline__ TileInfo tile_info(const GroupParams& p, int tile) {
 }
 
 // First weight row of the tile's lower and upper halves (split: gate and up).
-template <int BN>
 __device__ __forceinline__ void tile_rows(const GroupParams& p, const TileInfo& t, int& r_lo, int& r_hi) {
     if (p.split) {
         r_lo = t.e * p.Nrows + t.nt * (BN / 2);
@@ -336,32 +318,23 @@ __device__ __forceinline__ float act_fn(float gate, float up, int kind, float li
     return gate / (1.f + expf(-gate)) * up;
 }
 
-template <int BN>
 __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_constant__ GroupParams p) {
-    using C = GTile<BN>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-    auto* sh = reinterpret_cast<GemmShared*>(smem + C::kSmemShared);
+    auto* sh = reinterpret_cast<GemmShared*>(smem + kSmemShared);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int KS = p.K / BK, sc_row = p.K / 32;
     const int total = p.mtile_prefix[p.E] * p.n_tiles;
 
     if (tid == 0) {
-        for (int s = 0; s < C::kAStages; ++s) {
-            mbar_init(&sh->a_full[s], 1);
-            mbar_init(&sh->a_empty[s], 1);
-        }
-        for (int s = 0; s < C::kBStages; ++s) {
-            mbar_init(&sh->b_full[s], kDequantThreads);
-            mbar_init(&sh->b_empty[s], 1);
-        }
-        for (int s = 0; s < C::kRawStages; ++s) {
-            mbar_init(&sh->raw_full[s], 1);
-            mbar_init(&sh->raw_empty[s], kDequantWarps);
+        for (int s = 0; s < kStagesG; ++s) {
+            mbar_init(&sh->tma_full[s], 1);
+            mbar_init(&sh->b_full[s], 128);
+            mbar_init(&sh->stage_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&sh->sc_full[b], 1);
-            mbar_init(&sh->sc_empty[b], kDequantThreads);
+            mbar_init(&sh->sc_empty[b], 128);
             mbar_init(&sh->acc_full[b], 1);
             mbar_init(&sh->acc_empty[b], 4);
         }
@@ -369,7 +342,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
         fence_barrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(&sh->tmem_base, 2 * BN);
+        tmem_alloc(&sh->tmem_base, 256);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -380,64 +353,49 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------ producer (TMA)
-        // Per tile: its weight rows' scale bytes; per 64-wide K step: the
-        // activation tile (A ring) and the weight codes (raw ring).
         uint32_t it = 0, lt = 0;
         uint32_t issued_sc = 0;
         for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x, ++lt) {
             const TileInfo t = tile_info(p, tile);
             int r_lo, r_hi;
-            tile_rows<BN>(p, t, r_lo, r_hi);
+            tile_rows(p, t, r_lo, r_hi);
             const int sb = int(lt & 1u);
             if (lt >= 2 && !mbar_wait(&sh->sc_empty[sb], ((lt >> 1) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog)) {
                 *abort_flag = 1;
                 break;
             }
-            // Scale rows of the tile: two runs of BN/2 rows, clamped to the tensor.
+            // Scale rows of the tile: two runs of 64 rows, clamped to the tensor.
             const int limit_rows = p.E * p.Nrows;
             const int n_lo = max(0, min(BN / 2, limit_rows - r_lo)), n_hi = max(0, min(BN / 2, limit_rows - r_hi));
             mbar_expect_tx(&sh->sc_full[sb], uint32_t((n_lo + n_hi) * sc_row));
-            uint8_t* sdst = smem + C::kSmemScale + sb * C::kScaleBytes;
+            uint8_t* sdst = smem + kSmemScale + sb * kScaleBytes;
             if (n_lo)
                 bulk_g2s(sdst, p.scales + size_t(r_lo) * sc_row, uint32_t(n_lo * sc_row), &sh->sc_full[sb]);
             if (n_hi)
-                bulk_g2s(sdst + (BN / 2) * sc_row, p.scales + size_t(r_hi) * sc_row, uint32_t(n_hi * sc_row),
-                         &sh->sc_full[sb]);
+                bulk_g2s(sdst + (BN / 2) * sc_row, p.scales + size_t(r_hi) * sc_row, uint32_t(n_hi * sc_row), &sh->sc_full[sb]);
             ++issued_sc;
             for (int ks = 0; ks < KS; ++ks, ++it) {
-                const int sr = int(it % C::kRawStages), sa = int(it % C::kAStages);
-                if (it >= uint32_t(C::kRawStages)
-                    && !mbar_wait(&sh->raw_empty[sr], ((it / C::kRawStages) & 1u) ^ 1u, watchdog_empty_barrier,
-                                  p.watchdog)) {
+                const int s = int(it % kStagesG);
+                if (it >= kStagesG
+                    && !mbar_wait(&sh->stage_empty[s], ((it / kStagesG) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog)) {
                     *abort_flag = 1;
                     break;
                 }
-                mbar_expect_tx(&sh->raw_full[sr], uint32_t(C::kRawBytes));
-                uint8_t* raw = smem + C::kSmemRaw + sr * C::kRawBytes;
+                mbar_expect_tx(&sh->tma_full[s], uint32_t(kABytes + kRawBytes));
+                tma_load_2d(smem + kSmemA + s * kABytes, &p.a_map, ks * BK, t.m0, &sh->tma_full[s]);
+                uint8_t* raw = smem + kSmemRaw + s * kRawBytes;
                 if (p.split) {
-                    tma_load_2d(raw, &p.b_map, ks * (BK / 2), r_lo, &sh->raw_full[sr]);
-                    tma_load_2d(raw + (BN / 2) * (BK / 2), &p.b_map, ks * (BK / 2), r_hi, &sh->raw_full[sr]);
+                    tma_load_2d(raw, &p.b_map, ks * (BK / 2), r_lo, &sh->tma_full[s]);
+                    tma_load_2d(raw + (BN / 2) * (BK / 2), &p.b_map, ks * (BK / 2), r_hi, &sh->tma_full[s]);
                 } else {
-                    tma_load_2d(raw, &p.b_map, ks * (BK / 2), r_lo, &sh->raw_full[sr]);
+                    tma_load_2d(raw, &p.b_map, ks * (BK / 2), r_lo, &sh->tma_full[s]);
                 }
-                if (it >= uint32_t(C::kAStages)
-                    && !mbar_wait(&sh->a_empty[sa], ((it / C::kAStages) & 1u) ^ 1u, watchdog_empty_barrier,
-                                  p.watchdog)) {
-                    *abort_flag = 1;
-                    break;
-                }
-                mbar_expect_tx(&sh->a_full[sa], uint32_t(kABytes));
-                tma_load_2d(smem + C::kSmemA + sa * kABytes, &p.a_map, ks * BK, t.m0, &sh->a_full[sa]);
             }
         }
         // Drain: every copy this thread issued lands before the CTA can exit.
-        for (uint32_t k = 0; k < uint32_t(C::kAStages) && k < it; ++k) {
+        for (uint32_t k = 0; k < kStagesG && k < it; ++k) {
             const uint32_t last = it - 1 - k;
-            mbar_wait(&sh->a_full[last % C::kAStages], (last / C::kAStages) & 1u, watchdog_drain, p.watchdog);
-        }
-        for (uint32_t k = 0; k < uint32_t(C::kRawStages) && k < it; ++k) {
-            const uint32_t last = it - 1 - k;
-            mbar_wait(&sh->raw_full[last % C::kRawStages], (last / C::kRawStages) & 1u, watchdog_drain, p.watchdog);
+            mbar_wait(&sh->tma_full[last % kStagesG], (last / kStagesG) & 1u, watchdog_drain, p.watchdog);
         }
         for (uint32_t k = 0; k < 2 && k < issued_sc; ++k) {
             const uint32_t last = issued_sc - 1 - k;
@@ -456,21 +414,21 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
             }
             tc_fence_after();
             for (int ks = 0; ks < KS; ++ks, ++it) {
-                const int sa = int(it % C::kAStages), sb = int(it % C::kBStages);
-                if (!mbar_wait(&sh->a_full[sa], (it / C::kAStages) & 1u, watchdog_full_barrier, p.watchdog)
-                    || !mbar_wait(&sh->b_full[sb], (it / C::kBStages) & 1u, watchdog_full_barrier, p.watchdog)) {
+                const int s = int(it % kStagesG);
+                const uint32_t ph = (it / kStagesG) & 1u;
+                if (!mbar_wait(&sh->tma_full[s], ph, watchdog_full_barrier, p.watchdog)
+                    || !mbar_wait(&sh->b_full[s], ph, watchdog_full_barrier, p.watchdog)) {
                     *abort_flag = 1;
                     break;
                 }
                 tc_fence_after();
-                const uint64_t ad = sw128_desc(smem_addr(smem + C::kSmemA + sa * kABytes));
-                const uint64_t bd = sw128_desc(smem_addr(smem + C::kSmemB + sb * C::kBBytes));
+                const uint64_t ad = sw128_desc(smem_addr(smem + kSmemA + s * kABytes));
+                const uint64_t bd = sw128_desc(smem_addr(smem + kSmemB + s * kBBytes));
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk)
                     umma_f16(tmem + uint32_t(acc * BN), ad + uint64_t(2 * kk), bd + uint64_t(2 * kk), idesc,
                              (ks | kk) != 0);
-                umma_commit(&sh->a_empty[sa]);
-                umma_commit(&sh->b_empty[sb]);
+                umma_commit(&sh->stage_empty[s]);
                 issued = true;
             }
             umma_commit(&sh->acc_full[acc]);
@@ -478,18 +436,11 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
         if (issued && *abort_flag) {
             // Let the MMAs in flight finish before TMEM is released.
             const uint32_t last = it - 1;
-            mbar_wait(&sh->b_empty[last % C::kBStages], (last / C::kBStages) & 1u, watchdog_drain, p.watchdog);
+            mbar_wait(&sh->stage_empty[last % kStagesG], (last / kStagesG) & 1u, watchdog_drain, p.watchdog);
         }
-    } else if (warp >= 2 && warp < 2 + kDequantWarps) {
+    } else if (warp >= 2 && warp < 6) {
         // ------------------------------------------------- dequant warps
-        // Thread (r, half): B-operand row r and, for 128-row tiles (two threads
-        // per row), values 32 half .. 32 half + 31 of each 64-wide K step (one
-        // MXFP4 block and its scale); for 256-row tiles all 64 values (two
-        // blocks). Codes are read into registers and their raw slot released
-        // before the thread waits for its B slot.
-        constexpr int kTpr = C::kThreadsPerRow;
-        constexpr int kChunks = 8 / kTpr;  // 16-byte B chunks (8 values) per thread and K step
-        const int r = (tid - 64) / kTpr, half = kTpr == 2 ? (tid - 64) & 1 : 0;
+        const int r = tid - 64;  // B-operand row of this thread
         uint32_t it = 0, lt = 0;
         bool scale_ok = true;
         for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x, ++lt) {
@@ -498,44 +449,29 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                 *abort_flag = 1;
                 break;
             }
-            const uint8_t* srow = smem + C::kSmemScale + sb * C::kScaleBytes + r * sc_row;
+            const uint8_t* srow = smem + kSmemScale + sb * kScaleBytes + r * sc_row;
             // Rows past the weight tensor were zero-filled and have no scale bytes.
             int r_lo, r_hi;
-            tile_rows<BN>(p, tile_info(p, tile), r_lo, r_hi);
+            tile_rows(p, tile_info(p, tile), r_lo, r_hi);
             const bool row_in_tensor = (r < BN / 2 ? r_lo + r : r_hi + (r - BN / 2)) < p.E * p.Nrows;
             for (int ks = 0; ks < KS; ++ks, ++it) {
-                const int sr = int(it % C::kRawStages), s = int(it % C::kBStages);
-                if (!mbar_wait(&sh->raw_full[sr], (it / C::kRawStages) & 1u, watchdog_full_barrier, p.watchdog)) {
+                const int s = int(it % kStagesG);
+                if (!mbar_wait(&sh->tma_full[s], (it / kStagesG) & 1u, watchdog_full_barrier, p.watchdog)) {
                     *abort_flag = 1;
                     break;
                 }
-                const uint8_t* raw = smem + C::kSmemRaw + sr * C::kRawBytes + r * (BK / 2) + 16 * half;
-                uint32_t words[kChunks];
-#pragma unroll
-                for (int v = 0; v < kChunks / 4; ++v) {
-                    const uint4 cw = *reinterpret_cast<const uint4*>(raw + 16 * v);
-                    words[4 * v] = cw.x, words[4 * v + 1] = cw.y, words[4 * v + 2] = cw.z, words[4 * v + 3] = cw.w;
-                }
-                __syncwarp();
-                if (lane == 0)
-                    mbar_arrive(&sh->raw_empty[sr]);
-                bool ok0, ok1 = true;
-                const uint32_t s0 = e8m0_half2(srow[2 * ks + half], ok0);
-                const uint32_t s1 = kTpr == 1 ? e8m0_half2(srow[2 * ks + 1], ok1) : s0;
+                const uint8_t* raw = smem + kSmemRaw + s * kRawBytes + r * (BK / 2);
+                const uint4 c0 = *reinterpret_cast<const uint4*>(raw);
+                const uint4 c1 = *reinterpret_cast<const uint4*>(raw + 16);
+                bool ok0, ok1;
+                const uint32_t s0 = e8m0_half2(srow[2 * ks], ok0), s1 = e8m0_half2(srow[2 * ks + 1], ok1);
                 scale_ok = scale_ok && (!row_in_tensor || (ok0 && ok1));
-                // The B slot is free once the MMAs of its previous use completed.
-                if (it >= uint32_t(C::kBStages)
-                    && !mbar_wait(&sh->b_empty[s], ((it / C::kBStages) & 1u) ^ 1u, watchdog_empty_barrier,
-                                  p.watchdog)) {
-                    *abort_flag = 1;
-                    break;
-                }
-                uint8_t* brow = smem + C::kSmemB + s * C::kBBytes + r * 128;
+                const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                uint8_t* brow = smem + kSmemB + s * kBBytes + r * 128;
 #pragma unroll
-                for (int cc = 0; cc < kChunks; ++cc) {
+                for (int c = 0; c < 8; ++c) {
                     // 16-byte chunk c = values 8c..8c+7 = code bytes 4c..4c+3.
-                    const int c = kChunks * half + cc;
-                    const uint32_t w = words[cc], sc = c < 4 ? s0 : s1;
+                    const uint32_t w = words[c], sc = c < 4 ? s0 : s1;
                     uint4 h;
                     h.x = hmul2_bits(e2m1x2_to_half2(w & 0xFFu), sc);
                     h.y = hmul2_bits(e2m1x2_to_half2((w >> 8) & 0xFFu), sc);
@@ -550,7 +486,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
         }
         if (!scale_ok && p.status)
             atomicOr(p.status, 2u);
-    } else if (warp >= 2 + kDequantWarps) {
+    } else if (warp >= 6) {
         // ------------------------------------------------- epilogue warps
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row = 32 * q + lane;
@@ -570,11 +506,11 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                 // Activation of (gate, up) pairs -> fp16 act[prow, j].
                 auto* act = static_cast<__half*>(p.out);
                 const int I = p.Nrows / 2;
-                for (int c = 0; c < BN / 64; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     uint32_t g[32], u[32];
                     if (p.split) {
                         tmem_ld32(taddr + uint32_t(32 * c), g);
-                        tmem_ld32(taddr + uint32_t(BN / 2 + 32 * c), u);
+                        tmem_ld32(taddr + uint32_t(64 + 32 * c), u);
                     } else {
                         // Interleaved: column 2i gate, 2i+1 up.
                         uint32_t a[32], b[32];
@@ -649,7 +585,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     if (warp == 1)
-        tmem_dealloc(tmem, 2 * BN);
+        tmem_dealloc(tmem, 256);
 }
 
 // ----------------------------------------------------------- grouped GEMV
@@ -930,15 +866,14 @@ int check_weights(const kb200_moe_weights* w, bool routed = true) {
     return KB200_OK;
 }
 
-template <int BN> int gemm_slots() {
+int gemm_slots() {
     static int set[64] = {};
     static std::mutex lock;
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> guard(lock);
     if (!set[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   GTile<BN>::kSmemTotal);
+        const cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTotal);
         if (e != cudaSuccess)
             return -cuda_fail(e, "moe_gemm_kernel attribute");
         set[dev] = 1;
@@ -946,26 +881,15 @@ template <int BN> int gemm_slots() {
     return sm_count();
 }
 
-template <int BN> int launch_gemm(GroupParams& p, int max_tiles, cudaStream_t stream) {
-    const int slots = gemm_slots<BN>();
+int launch_gemm(GroupParams& p, int max_tiles, cudaStream_t stream) {
+    const int slots = gemm_slots();
     if (slots <= 0)
         return -slots;
     p.watchdog = watchdog_word();
     const int grid = std::max(1, std::min(slots, max_tiles));
-    moe_gemm_kernel<BN><<<grid, kThreadsG, GTile<BN>::kSmemTotal, stream>>>(p);
+    moe_gemm_kernel<<<grid, kThreadsG, kSmemTotal, stream>>>(p);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_gemm_kernel launch");
-}
-
-// Weight-tile height of the grouped GEMMs: 256 rows when the gate/up GEMM
-// still has a tile for every SM, else 128. KB200_MOE_BN=128|256 overrides.
-int moe_tile_rows(size_t n, int E, int I) {
-    const long mtiles = long((n + BM - 1) / BM);
-    int bn = mtiles * long((2 * I + 255) / 256) >= sm_count() ? 256 : 128;
-    if (const char* s = std::getenv("KB200_MOE_BN"))
-        bn = std::atoi(s) == 128 ? 128 : std::atoi(s) == 256 ? 256 : bn;
-    (void)E;
-    return bn;
 }
 
 }  // namespace
@@ -1111,16 +1035,13 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
     }
 
     // gate/up: [n, H] x [2I, H]^T per expert, activation in the epilogue.
-    // Tiles past an expert's rows (I or H not a multiple of the tile) read
-    // the next rows of the tensor (or zero fill) and are masked on output.
-    const int BN = moe_tile_rows(n, E, I);
     GroupParams g1;
     std::memset(&g1, 0, sizeof(g1));
     const bool split = !w->interleaved;
     if (!encode_2d(&g1.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xs, uint64_t(H), n, BK, BM,
                    CU_TENSOR_MAP_SWIZZLE_128B)
         || !encode_2d(&g1.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->gate_up_blocks, uint64_t(H / 2),
-                      uint64_t(E) * 2 * I, BK / 2, uint32_t(split ? BN / 2 : BN), CU_TENSOR_MAP_SWIZZLE_NONE))
+                      uint64_t(E) * 2 * I, BK / 2, split ? BN / 2 : BN, CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(KB200_INVALID, "tensor map encoding (gate/up)");
     g1.scales = w->gate_up_scales;
     g1.bias = w->gate_up_bias;
@@ -1130,7 +1051,7 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
     g1.K = H;
     g1.Nrows = 2 * I;
     g1.E = E;
-    g1.n_tiles = split ? (I + BN / 2 - 1) / (BN / 2) : (2 * I + BN - 1) / BN;
+    g1.n_tiles = split ? I / (BN / 2) : 2 * I / BN;
     g1.split = split ? 1 : 0;
     g1.epilogue = 0;
     g1.out_cols = I;
@@ -1138,8 +1059,9 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
     g1.limit = w->limit;
     g1.alpha = w->alpha;
     g1.status = status;
-    if (const int s = BN == 256 ? launch_gemm<256>(g1, mtiles_max * g1.n_tiles, stream)
-                                : launch_gemm<128>(g1, mtiles_max * g1.n_tiles, stream))
+    if ((2 * I) % BN && !split)
+        return fail(KB200_UNSUPPORTED, "interleaved gate/up needs 2*inter to be a multiple of 128");
+    if (const int s = launch_gemm(g1, mtiles_max * g1.n_tiles, stream))
         return s;
 
     // down: [n, I] x [H, I]^T per expert -> fp32 rows.
@@ -1148,7 +1070,7 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
     if (!encode_2d(&g2.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, act, uint64_t(I), n, BK, BM,
                    CU_TENSOR_MAP_SWIZZLE_128B)
         || !encode_2d(&g2.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->down_blocks, uint64_t(I / 2), uint64_t(E) * H,
-                      BK / 2, uint32_t(BN), CU_TENSOR_MAP_SWIZZLE_NONE))
+                      BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(KB200_INVALID, "tensor map encoding (down)");
     g2.scales = w->down_scales;
     g2.bias = w->down_bias;
@@ -1163,8 +1085,7 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
     g2.epilogue = 1;
     g2.out_cols = H;
     g2.status = status;
-    return BN == 256 ? launch_gemm<256>(g2, mtiles_max * g2.n_tiles, stream)
-                     : launch_gemm<128>(g2, mtiles_max * g2.n_tiles, stream);
+    return launch_gemm(g2, mtiles_max * g2.n_tiles, stream);
 }
 
 int combine_launch(const float* y, const float* weight, const int* pos, size_t tokens, int K, int H, float* out,
