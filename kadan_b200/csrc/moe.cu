@@ -250,6 +250,7 @@ constexpr int kSmemRaw = kSmemB + kStagesG * kBBytes;
 constexpr int kSmemScale = kSmemRaw + kStagesG * kRawBytes;
 constexpr int kSmemShared = kSmemScale + 2 * kScaleBytes;
 constexpr int kSmemTotal = kSmemShared + int(sizeof(GemmShared)) + 1024;
+static_assert(kSmemTotal <= 232448, "shared memory per CTA");
 
 struct TileInfo {
     int e, m0, mend, nt;
