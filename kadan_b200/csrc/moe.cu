@@ -274,6 +274,15 @@ __device__ __forceinline__ TileInfo tile_info(const GroupParams& p, int tile) {
     return t;
 }
 
+// The K step a tile takes at position ks of its walk: each weight tile
+// starts at a different K step, so the CTAs that share an activation tile at
+// the same time read different columns of it instead of queueing on the same
+// L2 lines. The order is fixed per tile, so results are reproducible.
+__device__ __forceinline__ int k_step(int ks, int nt, int KS) {
+    const int k = ks + nt % KS;
+    return k < KS ? k : k - KS;
+}
+
 // First weight row of the tile's lower and upper halves (split: gate and up).
 __device__ __forceinline__ void tile_rows(const GroupParams& p, const TileInfo& t, int& r_lo, int& r_hi) {
     if (p.split) {
@@ -382,14 +391,15 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                     *abort_flag = 1;
                     break;
                 }
+                const int kx = k_step(ks, t.nt, KS);
                 mbar_expect_tx(&sh->tma_full[s], uint32_t(kABytes + kRawBytes));
-                tma_load_2d(smem + kSmemA + s * kABytes, &p.a_map, ks * BK, t.m0, &sh->tma_full[s]);
+                tma_load_2d(smem + kSmemA + s * kABytes, &p.a_map, kx * BK, t.m0, &sh->tma_full[s]);
                 uint8_t* raw = smem + kSmemRaw + s * kRawBytes;
                 if (p.split) {
-                    tma_load_2d(raw, &p.b_map, ks * (BK / 2), r_lo, &sh->tma_full[s]);
-                    tma_load_2d(raw + (BN / 2) * (BK / 2), &p.b_map, ks * (BK / 2), r_hi, &sh->tma_full[s]);
+                    tma_load_2d(raw, &p.b_map, kx * (BK / 2), r_lo, &sh->tma_full[s]);
+                    tma_load_2d(raw + (BN / 2) * (BK / 2), &p.b_map, kx * (BK / 2), r_hi, &sh->tma_full[s]);
                 } else {
-                    tma_load_2d(raw, &p.b_map, ks * (BK / 2), r_lo, &sh->tma_full[s]);
+                    tma_load_2d(raw, &p.b_map, kx * (BK / 2), r_lo, &sh->tma_full[s]);
                 }
             }
         }
@@ -453,7 +463,8 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
             const uint8_t* srow = smem + kSmemScale + sb * kScaleBytes + r * sc_row;
             // Rows past the weight tensor were zero-filled and have no scale bytes.
             int r_lo, r_hi;
-            tile_rows(p, tile_info(p, tile), r_lo, r_hi);
+            const TileInfo ti = tile_info(p, tile);
+            tile_rows(p, ti, r_lo, r_hi);
             const bool row_in_tensor = (r < BN / 2 ? r_lo + r : r_hi + (r - BN / 2)) < p.E * p.Nrows;
             for (int ks = 0; ks < KS; ++ks, ++it) {
                 const int s = int(it % kStagesG);
@@ -465,7 +476,8 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                 const uint4 c0 = *reinterpret_cast<const uint4*>(raw);
                 const uint4 c1 = *reinterpret_cast<const uint4*>(raw + 16);
                 bool ok0, ok1;
-                const uint32_t s0 = e8m0_half2(srow[2 * ks], ok0), s1 = e8m0_half2(srow[2 * ks + 1], ok1);
+                const int kx = k_step(ks, ti.nt, KS);
+                const uint32_t s0 = e8m0_half2(srow[2 * kx], ok0), s1 = e8m0_half2(srow[2 * kx + 1], ok1);
                 scale_ok = scale_ok && (!row_in_tensor || (ok0 && ok1));
                 const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
                 uint8_t* brow = smem + kSmemB + s * kBBytes + r * 128;
