@@ -280,3 +280,47 @@ def test_tp_two_ranks_match_oracle(cuda):
         for r in range(2):
             bad = {k: v for k, v in results[r].items() if not v < TOL}
             assert not bad, (r, bad)
+
+
+def test_peer_allreduce_wait_ends_with_status_when_no_peer_writes(kb, cuda):
+    """A bounded wait, run out on purpose without any fault: the "peer" is a
+    second buffer on this GPU that nothing writes, so the words the kernel
+    waits for never arrive. It must give up after its time limit, report
+    watchdog bit 16 to the host, leave the data as it was, and leave the
+    context usable for the next launch."""
+    import ctypes
+
+    import torch
+
+    from kadan_b200 import collectives  # noqa: F401  (argument types)
+
+    count = 8192
+    nbytes = int(kb.lib.kb200_peer_buffer_bytes(2, count))
+    bufs = []
+    for _ in range(2):
+        p = ctypes.c_void_p()
+        kb.check(kb.lib.kb200_device_alloc(nbytes, ctypes.byref(p)))
+        bufs.append(p.value)
+    try:
+        assert kb.take_device_error() == 0
+        data = torch.arange(count, dtype=torch.float32, device=cuda)
+        peers = (ctypes.c_void_p * 2)(*bufs)
+        stream = torch.cuda.current_stream()
+        kb.check(kb.lib.kb200_peer_allreduce_f32(data.data_ptr(), count, peers, 2, 0, count, 0.05,
+                                                 ctypes.c_void_p(stream.cuda_stream)))
+        torch.cuda.synchronize()
+        assert kb.take_device_error() & 16
+        assert torch.equal(data, torch.arange(count, dtype=torch.float32, device=cuda))
+        # The context still runs kernels.
+        from kadan_b200 import synth
+
+        w = synth.gguf(kb.Q4_K, 64, 256, seed=1)
+        x = synth.activations(256, seed=2).reshape(1, 256)
+        y = kb.gguf_gemv(kb.Q4_K, torch.from_numpy(w).to(cuda), torch.from_numpy(x).to(cuda), in_=256, columns=64)
+        torch.cuda.synchronize()
+        assert torch.isfinite(y).all()
+        assert kb.take_device_error() == 0
+    finally:
+        torch.cuda.synchronize()
+        for b in bufs:
+            kb.lib.kb200_device_free(b)
