@@ -680,9 +680,18 @@ def run_ep(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     dist = None
-    if world > 1:
+    if world > 1 or args.exchange == "peer":
+        import socket
+
         import torch.distributed as dist
 
+        if world == 1:  # the peer buffers are set up over a (one-rank) process group
+            with socket.socket() as sk:
+                sk.bind(("127.0.0.1", 0))
+                os.environ.setdefault("MASTER_PORT", str(sk.getsockname()[1]))
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("RANK", "0")
+            os.environ.setdefault("WORLD_SIZE", "1")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     E, H, I, K, T = 128, 2880, 2880, 4, 8192
     layers = args.layers or 36
@@ -697,7 +706,8 @@ def run_ep(args, rank, world, local_rank):
         dn_w = torch.randint(0, 256, (el, H, I // 2), dtype=torch.uint8, device=device, generator=gen)
         dn_s = torch.randint(118, 127, (el, H, I // 32), dtype=torch.uint8, device=device, generator=gen)
         w = kb.moe_weights(gu_w, gu_s, dn_w, dn_s, hidden=H, inter=I, experts=el, top_k=K)
-        stack.append((ep.ExpertParallelMoE(w, E, world, rank), (gu_w, gu_s, dn_w, dn_s)))
+        stack.append((ep.ExpertParallelMoE(w, E, world, rank, exchange=args.exchange, max_tokens=tokens,
+                                           device=device), (gu_w, gu_s, dn_w, dn_s)))
     tgen = torch.Generator(device=device).manual_seed(7 + rank)
     x = torch.randn(tokens, H, device=device, generator=tgen).to(torch.bfloat16)
     logits = [torch.randn(tokens, E, device=device, generator=tgen) for _ in range(layers)]
@@ -723,10 +733,13 @@ def run_ep(args, rank, world, local_rank):
         b.record()
         torch.cuda.synchronize()
     ms = a.elapsed_time(b) / steps
+    watchdog = kb.take_device_error()
     if dist:
         m = torch.tensor([ms], device=device)
         dist.all_reduce(m, op=dist.ReduceOp.MAX)
         ms = float(m.item())
+        for layer, _ in stack:
+            layer.close()
         dist.barrier()
         dist.destroy_process_group()
     clock = clocks.summary()
@@ -743,7 +756,10 @@ def run_ep(args, rank, world, local_rank):
         "config": {"workload": f"BASELINE config 5: gpt-oss-120b MoE, {layers} layers, E=128, top-4, "
                                f"{T} tokens per step", "parallelism": f"ep{world}",
                    "tokens_per_rank": tokens, "experts_per_rank": el,
-                   "collective": "NCCL all-to-all (counts, fp16 rows out, fp32 rows back)"},
+                   "collective": ("peer-memory exchange kernels (counts, fp16 rows out, fp32 rows back; no host sync)"
+                                  if args.exchange == "peer" else
+                                  "NCCL all-to-all (counts, fp16 rows out, fp32 rows back)")},
+        "watchdog": watchdog,
         "tflops": round(tflops, 1), "tflops_per_gpu": round(tflops / world, 1),
         "status": int(status.item()) if world == 1 else None, "clocks": clock}), flush=True)
 
@@ -760,6 +776,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--collective", choices=["fused", "peer", "nccl"], default="fused",
                     help="all-reduce of --case tp70b at N > 1: GEMV+exchange fused, peer kernel after the GEMV, NCCL")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
+                    help="token exchange of --case ep120b")
     ap.add_argument("--layers", type=int, default=0, help="layers for --case tp70b / ep120b (default 80 / 36)")
     args = ap.parse_args()
     if args.warmup < 3:

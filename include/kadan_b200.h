@@ -383,6 +383,35 @@ KB200_API int kb200_peer_allreduce_f32(float* data, size_t count, void* const* p
 KB200_API int kb200_gguf_gemv_allreduce(const kb200_gemv_job* job, void* const* peers, int world, int rank,
                                         size_t max_count, double timeout_s, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Expert-parallel exchange over NVLink peer memory (one process per GPU),
+ * with no count read-back on the host. Each rank allocates
+ * kb200_ep_buffer_bytes(world, experts, hidden, capacity, local_capacity)
+ * with kb200_device_alloc, exchanges it by CUDA IPC (kb200_ipc_handle /
+ * kb200_ipc_open) and passes all buffers as `peers` (its own at [rank]).
+ * capacity: rows any rank can receive (at most the group's tokens * top_k);
+ * local_capacity: this rank's tokens * top_k at most.
+ *
+ * kb200_ep_dispatch: after kb200_moe_dispatch_rows (offsets and rows of its
+ * result), stores every row into its expert owner's receive area
+ * (kb200_ep_rows_area of the owner's buffer), expert-major (for each local
+ * expert, the rows of source 0..N-1), and writes local_offsets (device
+ * [experts/world + 1]) for kb200_moe_experts on that area with
+ * rows = capacity. kb200_ep_return: stores the expert results (fp32
+ * [capacity, hidden] in receive order) into each source's return area
+ * (kb200_ep_return_area) in the source's dispatch order, for
+ * kb200_moe_combine. Every rank makes the same calls in the same order;
+ * waits are bounded by timeout_s and report watchdog bit 32. */
+KB200_API size_t kb200_ep_buffer_bytes(int world, int experts, int hidden, size_t capacity, size_t local_capacity);
+KB200_API void* kb200_ep_rows_area(void* buffer);
+KB200_API void* kb200_ep_return_area(void* buffer, size_t capacity, int hidden);
+KB200_API int kb200_ep_dispatch(const int32_t* offsets, const uint16_t* rows, int hidden, int experts, int world,
+                                int rank, void* const* peers, size_t capacity, size_t local_capacity,
+                                int32_t* local_offsets, double timeout_s, void* stream);
+KB200_API int kb200_ep_return(const float* results, int hidden, int experts, int world, int rank,
+                              void* const* peers, size_t capacity, size_t local_capacity, double timeout_s,
+                              void* stream);
+
 /* The routing stage alone (for tests): chosen [tokens, top_k] int32,
  * weight [tokens, top_k] fp32, device. */
 KB200_API int kb200_moe_route(
@@ -399,7 +428,8 @@ KB200_API int kb200_moe_route(
  * since the last call of this function, which also clears it. Synchronous.
  * Bits: 1 a stage never arrived, 2 a stage was never released, 4 the final
  * copies never landed, 8 a cut tile's other pieces never arrived (Q4_K GEMV),
- * 16 a peer's chunk never arrived (peer all-reduce). */
+ * 16 a peer's chunk never arrived (peer all-reduce), 32 a peer's counts or
+ * rows never arrived (expert-parallel exchange). */
 KB200_API int kb200_take_device_error(unsigned* value);
 
 #ifdef __cplusplus

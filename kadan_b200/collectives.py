@@ -1,9 +1,11 @@
 """Collectives of the tensor-parallel path over NVLink peer memory.
 
-PeerAllReduce maps every rank's exchange buffer into every other rank (CUDA
-IPC handles, swapped once over the process group) and adds fp32 vectors with
-one kernel per call (kb200_peer_allreduce_f32); no library collective runs on
-the data path. The process group is only used at setup and teardown.
+PeerBuffers maps one buffer per rank into every other rank (CUDA IPC handles,
+swapped once over the process group). PeerAllReduce adds fp32 vectors over
+them with one kernel per call (kb200_peer_allreduce_f32, or fused into a
+row-parallel GEMV); the expert-parallel layer exchanges rows over them
+(kadan_b200.expert_parallel). No library collective runs on the data path:
+the process group is only used at setup and teardown.
 """
 from __future__ import annotations
 
@@ -22,7 +24,66 @@ lib.kb200_peer_allreduce_f32.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctype
                                          ctypes.c_int, ctypes.c_size_t, ctypes.c_double, ctypes.c_void_p]
 lib.kb200_gguf_gemv_allreduce.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_size_t,
                                           ctypes.c_double, ctypes.c_void_p]
+lib.kb200_ep_buffer_bytes.restype = ctypes.c_size_t
+lib.kb200_ep_buffer_bytes.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_size_t, ctypes.c_size_t]
+lib.kb200_ep_rows_area.restype = ctypes.c_void_p
+lib.kb200_ep_rows_area.argtypes = [ctypes.c_void_p]
+lib.kb200_ep_return_area.restype = ctypes.c_void_p
+lib.kb200_ep_return_area.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+lib.kb200_ep_dispatch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
+                                  ctypes.c_double, ctypes.c_void_p]
+lib.kb200_ep_return.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_double, ctypes.c_void_p]
 IPC_HANDLE_BYTES = 64
+
+
+class PeerBuffers:
+    """One device buffer per rank, mapped into every other rank of `group`
+    (allocated zeroed, handles swapped once over the process group).
+    `peers` is the ctypes array of every rank's address, this rank's at [rank]."""
+
+    def __init__(self, nbytes: int, group=None):
+        import torch.distributed as dist
+
+        self.dist, self.group = dist, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        own = ctypes.c_void_p()
+        check(lib.kb200_device_alloc(int(nbytes), ctypes.byref(own)))
+        self.own = own.value
+        handle = (ctypes.c_char * IPC_HANDLE_BYTES)()
+        check(lib.kb200_ipc_handle(self.own, handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self.own)
+                continue
+            buf = (ctypes.c_char * IPC_HANDLE_BYTES).from_buffer_copy(h)
+            p = ctypes.c_void_p()
+            check(lib.kb200_ipc_open(buf, ctypes.byref(p)))
+            self.opened.append(p.value)
+            ptrs.append(p.value)
+        self.peers = (ctypes.c_void_p * self.world)(*ptrs)
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        """Collective: every rank's kernels are done before any buffer goes."""
+        if self.own is None:
+            return
+        import torch
+
+        torch.cuda.synchronize()
+        self.dist.barrier(group=self.group)
+        for p in self.opened:
+            check(lib.kb200_ipc_close(p))
+        self.opened = []
+        self.dist.barrier(group=self.group)
+        check(lib.kb200_device_free(self.own))
+        self.own = None
 
 
 class PeerAllReduce:
@@ -44,26 +105,8 @@ class PeerAllReduce:
         nbytes = int(lib.kb200_peer_buffer_bytes(self.world, self.max_count))
         if not nbytes:
             raise ValueError("peer all-reduce supports 1..8 ranks")
-        own = ctypes.c_void_p()
-        check(lib.kb200_device_alloc(nbytes, ctypes.byref(own)))
-        self.own = own.value
-        handle = (ctypes.c_char * IPC_HANDLE_BYTES)()
-        check(lib.kb200_ipc_handle(self.own, handle))
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        self.opened = []
-        ptrs = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(self.own)
-                continue
-            buf = (ctypes.c_char * IPC_HANDLE_BYTES).from_buffer_copy(h)
-            p = ctypes.c_void_p()
-            check(lib.kb200_ipc_open(buf, ctypes.byref(p)))
-            self.opened.append(p.value)
-            ptrs.append(p.value)
-        self.peers = (ctypes.c_void_p * self.world)(*ptrs)
-        dist.barrier(group=group)
+        self.buffers = PeerBuffers(nbytes, group)
+        self.peers = self.buffers.peers
 
     def __call__(self, tensor, stream) -> None:
         """In place on `tensor` (fp32, contiguous), enqueued on `stream`."""
@@ -78,15 +121,4 @@ class PeerAllReduce:
 
     def close(self) -> None:
         """Collective: every rank's kernels are done before any buffer goes."""
-        if self.own is None:
-            return
-        import torch
-
-        torch.cuda.synchronize()
-        self.dist.barrier(group=self.group)
-        for p in self.opened:
-            check(lib.kb200_ipc_close(p))
-        self.opened = []
-        self.dist.barrier(group=self.group)
-        check(lib.kb200_device_free(self.own))
-        self.own = None
+        self.buffers.close()

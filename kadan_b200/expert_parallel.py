@@ -27,7 +27,7 @@ from typing import List, Tuple
 
 import numpy as np
 
-from . import MoeWeights, lib, moe_combine, moe_dispatch_rows, moe_experts, moe_weights, rows_regroup
+from . import MoeWeights, check, lib, moe_combine, moe_dispatch_rows, moe_experts, moe_weights, rows_regroup
 
 
 def expert_range(experts: int, world: int, rank: int) -> Tuple[int, int]:
@@ -75,7 +75,14 @@ class ExpertParallelMoE:
     top_k = the model's k), built over device tensors the caller keeps
     alive. experts: the model's total expert count E."""
 
-    def __init__(self, local: MoeWeights, experts: int, world: int, rank: int, group=None):
+    def __init__(self, local: MoeWeights, experts: int, world: int, rank: int, group=None, exchange: str = "nccl",
+                 max_tokens: int = 0, device=None, timeout_s: float = 2.0):
+        """exchange: "nccl" (all-to-alls sized by a count read-back on the
+        host) or "peer" (kb200_ep_dispatch / kb200_ep_return over buffers
+        mapped by CUDA IPC; no host synchronisation; needs max_tokens, the
+        most tokens any rank routes per call, and a process group even for
+        one rank)."""
+        import torch
         import torch.distributed as dist
 
         self.w, self.experts, self.world, self.rank, self.group = local, experts, world, rank, group
@@ -85,6 +92,28 @@ class ExpertParallelMoE:
             raise ValueError("local weights must hold experts / world experts")
         self.dist = dist if world > 1 else None
         self._buffers = {}
+        self.exchange = exchange
+        if exchange == "peer":
+            from .collectives import PeerBuffers
+
+            if max_tokens <= 0:
+                raise ValueError("the peer exchange needs max_tokens")
+            hidden = local.hidden
+            self.max_tokens = int(max_tokens)
+            self.capacity = world * self.max_tokens * self.top_k
+            self.local_capacity = self.max_tokens * self.top_k
+            nbytes = int(lib.kb200_ep_buffer_bytes(world, experts, hidden, self.capacity, self.local_capacity))
+            if not nbytes:
+                raise ValueError("shape outside the peer exchange (at most 8 ranks, 256 experts)")
+            self.timeout_s = float(timeout_s)
+            self.peer = PeerBuffers(nbytes, group)
+            self.rows_area = int(lib.kb200_ep_rows_area(self.peer.own))
+            self.return_area = int(lib.kb200_ep_return_area(self.peer.own, self.capacity, hidden))
+            self.local_offsets = torch.zeros(self.local + 1, dtype=torch.int32, device=device)
+            self.zero_offsets = torch.zeros(experts + 1, dtype=torch.int32, device=device)
+            self.results = torch.empty(self.capacity, hidden, dtype=torch.float32, device=device)
+        elif exchange != "nccl":
+            raise ValueError(f"unknown exchange {exchange!r}")
 
     def _buffer(self, name: str, nbytes: int, device):
         import torch
@@ -99,6 +128,9 @@ class ExpertParallelMoE:
         """out[T, H] fp32 for this rank's tokens x (bf16 [T, H]) routed by
         fp32 logits [T, E]. Collective: every rank calls it for the layer."""
         import torch
+
+        if self.exchange == "peer":
+            return self._forward_peer(x_bf16, logits, out, status)
 
         dev = x_bf16.device
         tokens, hidden = x_bf16.shape
@@ -160,6 +192,47 @@ class ExpertParallelMoE:
         if tokens:
             moe_combine(y_sent, d.weight, d.pos, tokens, k, out)
         return out
+
+    def _forward_peer(self, x_bf16, logits, out, status):
+        """Dispatch, exchange, experts, return and combine, all enqueued on the
+        current stream: nothing waits on the host."""
+        import ctypes
+
+        import torch
+
+        dev = x_bf16.device
+        tokens, hidden = x_bf16.shape
+        k = self.top_k
+        if tokens > self.max_tokens:
+            raise ValueError("more tokens than the exchange buffers were sized for")
+        if out is None:
+            out = torch.empty(tokens, hidden, dtype=torch.float32, device=dev)
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        sptr = None if status is None else status.data_ptr()
+        if tokens:
+            need = int(lib.kb200_moe_dispatch_workspace_bytes(tokens, hidden, self.experts, k))
+            dws = self._buffer("dispatch", need, dev)
+            d = moe_dispatch_rows(logits, x_bf16, k, dws, status)
+            offsets, rows = d.offsets, d.rows
+        else:  # a rank without tokens still takes part in the exchange
+            d, offsets, rows = None, self.zero_offsets.data_ptr(), self.rows_area
+        check(lib.kb200_ep_dispatch(offsets, rows, hidden, self.experts, self.world, self.rank, self.peer.peers,
+                                    self.capacity, self.local_capacity, self.local_offsets.data_ptr(),
+                                    self.timeout_s, stream))
+        ews = self._buffer("experts", int(lib.kb200_moe_experts_workspace_bytes(self._wref(), self.capacity)), dev)
+        check(lib.kb200_moe_experts(self._wref(), self.rows_area, self.local_offsets.data_ptr(), self.capacity,
+                                    self.results.data_ptr(), ews.data_ptr(), ews.numel(), sptr, stream))
+        check(lib.kb200_ep_return(self.results.data_ptr(), hidden, self.experts, self.world, self.rank,
+                                  self.peer.peers, self.capacity, self.local_capacity, self.timeout_s, stream))
+        if tokens:
+            check(lib.kb200_moe_combine(self.return_area, d.weight, d.pos, tokens, k, hidden, out.data_ptr(), stream))
+        return out
+
+    def close(self) -> None:
+        """Collective (peer exchange): release the mapped buffers."""
+        if self.exchange == "peer" and self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def _tables(self, segs, offsets, device):
         """Regroup segments (forward and back) and local expert offsets on the

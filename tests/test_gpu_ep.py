@@ -21,7 +21,7 @@ pytestmark = pytest.mark.gpu
 E, H, I, K = 8, 256, 128, 2
 
 
-def run_rank(rank: int, world: int, port: int, tokens: int) -> dict:
+def run_rank(rank: int, world: int, port: int, tokens: int, exchange: str = "nccl") -> dict:
     import torch
 
     import kadan_b200 as kb
@@ -32,7 +32,7 @@ def run_rank(rank: int, world: int, port: int, tokens: int) -> dict:
     device = torch.device("cuda", rank)
     torch.cuda.set_device(device)
     dist = None
-    if world > 1:
+    if world > 1 or exchange == "peer":
         import datetime
 
         import torch.distributed as dist
@@ -47,7 +47,8 @@ def run_rank(rank: int, world: int, port: int, tokens: int) -> dict:
         shaped = [full[0].view(E, 2 * I, H // 2), full[1].view(E, 2 * I, H // 32),
                   full[2].view(E, H, I // 2), full[3].view(E, H, I // 32)]
         local, keep = ep.local_weights(*shaped, hidden=H, inter=I, experts=E, top_k=K, world=world, rank=rank)
-        layer = ep.ExpertParallelMoE(local, E, world, rank)
+        layer = ep.ExpertParallelMoE(local, E, world, rank, exchange=exchange, max_tokens=tokens + 3 * (world - 1),
+                                     device=device)
         # Rank r's tokens: its own seed, a different count per rank.
         t = tokens + 3 * rank
         x = synth.activations(t * H, seed=50 + rank, dtype="bf16").reshape(t, H)
@@ -63,6 +64,12 @@ def run_rank(rank: int, world: int, port: int, tokens: int) -> dict:
         ref16 = orc.moe_forward(x, logits, gu_w, gu_s, dn_w, dn_s, round_act=2, **args)
         ref = orc.moe_forward(x, logits, gu_w, gu_s, dn_w, dn_s, round_act=0, **args)
         res = {"tight": rel_err(got, ref16), "loose": rel_err(got, ref), "status": int(status.item())}
+        if exchange == "peer":
+            # A second layer call on the same buffers (the next epoch and bank).
+            again = layer.forward(xb, ld).cpu().numpy()
+            res["repeat"] = bool(np.array_equal(again.view(np.uint32), got.view(np.uint32)))
+            res["watchdog"] = kb.take_device_error()
+            layer.close()
         if world == 1:
             wfull = kb.moe_weights(*full, hidden=H, inter=I, experts=E, top_k=K)
             single = kb.moe_forward(wfull, xb, ld).cpu().numpy()
@@ -73,8 +80,8 @@ def run_rank(rank: int, world: int, port: int, tokens: int) -> dict:
             dist.destroy_process_group()
 
 
-def _child(rank, world, port, tokens, results):
-    results[rank] = run_rank(rank, world, port, tokens)
+def _child(rank, world, port, tokens, exchange, results):
+    results[rank] = run_rank(rank, world, port, tokens, exchange)
 
 
 def _port() -> int:
@@ -85,17 +92,21 @@ def _port() -> int:
 
 def _check(res):
     assert res["tight"] <= 1e-3 and res["loose"] <= 2e-2 and res["status"] == 0, res
+    if "repeat" in res:
+        assert res["repeat"] and res["watchdog"] == 0, res
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
 @pytest.mark.parametrize("tokens", [5, 300])
-def test_ep_one_rank(cuda, tokens):
-    res = run_rank(0, 1, 0, tokens)
+def test_ep_one_rank(cuda, tokens, exchange):
+    res = run_rank(0, 1, _port(), tokens, exchange)
     _check(res)
     assert res["bitwise"], res
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
 @pytest.mark.parametrize("tokens", [5, 300])
-def test_ep_two_ranks(cuda, tokens):
+def test_ep_two_ranks(cuda, tokens, exchange):
     import torch
     import torch.multiprocessing as mp
 
@@ -105,7 +116,7 @@ def test_ep_two_ranks(cuda, tokens):
     with ctx.Manager() as manager:
         results = manager.dict()
         port = _port()
-        procs = [ctx.Process(target=_child, args=(r, 2, port, tokens, results)) for r in range(2)]
+        procs = [ctx.Process(target=_child, args=(r, 2, port, tokens, exchange, results)) for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:
