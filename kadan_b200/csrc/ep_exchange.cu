@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(const __grid_cons
     __syncthreads();
     if (tid < p.world)
         store_release_sys(row_flag(p.peers[tid], kBackFlagOff, bank, p.rank, blockIdx.x), e);
-    // Every CTA waits for the results of this rank's rows, so the combine that
+    // CTA 0 waits for the results of this rank's rows, so the combine that
     // follows in the stream sees them all.
     if (blockIdx.x == 0) {
         uint8_t* mine = p.peers[p.rank];
