@@ -313,8 +313,8 @@ int ep_check(int hidden, int experts, int world, int rank, void* const* peers, s
     if (!peers || !capacity || !local_capacity)
         return fail(KB200_INVALID, "null peers or empty areas");
     for (int r = 0; r < world; ++r)
-        if (!peers[r] || !aligned(peers[r], 4096))
-            return fail(KB200_INVALID, "exchange buffers must be 4096-byte aligned");
+        if (!peers[r] || !aligned(peers[r], 256))
+            return fail(KB200_INVALID, "exchange buffers must be 256-byte aligned");
     return KB200_OK;
 }
 
