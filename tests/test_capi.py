@@ -162,3 +162,31 @@ def test_moe_stages_host_checks(kb):
     assert r(FAKE_X, FAKE_Y, 5762, segs, 4, 10, None) == kb.INVALID
     assert r(None, FAKE_Y, 5760, segs, 4, 10, None) == kb.INVALID
     assert r(FAKE_X, FAKE_Y, 5760, segs, 70000, 10, None) == kb.UNSUPPORTED
+
+
+def test_expert_exchange_host_checks(kb):
+    from kadan_b200 import collectives  # noqa: F401
+
+    lib = kb.lib
+    assert lib.kb200_ep_buffer_bytes(9, 128, 2880, 1024, 256) == 0
+    assert lib.kb200_ep_buffer_bytes(2, 300, 2880, 1024, 256) == 0
+    assert lib.kb200_ep_buffer_bytes(2, 128, 2880, 1024, 256) > 1024 * 2880 * 2 + 256 * 2880 * 4
+    assert lib.kb200_ep_rows_area(None) is None
+    peers = (ctypes.c_void_p * 2)(0x40000000, 0x48000000)
+    lo = 0x76000000
+
+    def dispatch(world=2, rank=0, experts=128, hidden=2880, peers_=peers, rows=FAKE_X, offsets=FAKE_W):
+        return lib.kb200_ep_dispatch(offsets, rows, hidden, experts, world, rank, peers_, 1024, 256, lo, 2.0, None)
+
+    assert dispatch(world=9) == kb.UNSUPPORTED
+    assert dispatch(rank=2) == kb.UNSUPPORTED
+    assert dispatch(experts=127) == kb.UNSUPPORTED  # not an even split over 2 ranks
+    assert dispatch(hidden=2890) == kb.UNSUPPORTED
+    assert dispatch(peers_=None) == kb.INVALID
+    assert dispatch(peers_=(ctypes.c_void_p * 2)(0x40000000, 0x48000040)) == kb.INVALID
+    assert dispatch(rows=None) == kb.INVALID
+    assert dispatch(rows=FAKE_X + 8) == kb.INVALID
+    ret = lib.kb200_ep_return
+    assert ret(None, 2880, 128, 2, 0, peers, 1024, 256, 2.0, None) == kb.INVALID
+    assert ret(FAKE_Y + 4, 2880, 128, 2, 0, peers, 1024, 256, 2.0, None) == kb.INVALID
+    assert ret(FAKE_Y, 2880, 128, 2, 0, peers, 0, 256, 2.0, None) == kb.INVALID
