@@ -5,7 +5,6 @@ from __future__ import annotations
 import ctypes
 import re
 
-
 from conftest import ROOT
 
 
