@@ -44,11 +44,38 @@ namespace {
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 32;
 
+// Programmatic dependent launch between the layer's kernels: each lets the
+// next kernel of the stream start launching, then waits until the previous
+// one has completed and its writes are visible before touching them. Launch
+// latency overlaps; the order of the work does not change. Without the launch
+// attribute both instructions do nothing.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <class... Params, class... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // ---------------------------------------------------------------- routing
 // One warp per token; experts strided over lanes (<= 8 per lane).
 __global__ void moe_route_kernel(
     const float* logits, int tokens, int E, int K, int* chosen, float* weight, int* counts
 ) {
+    pdl_enter();
     const int warp = int((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     if (warp >= tokens)
         return;
@@ -120,6 +147,7 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(
 ) {
     __shared__ int off[kMaxExperts + 1], running[kMaxExperts], total[kMaxExperts];
     __shared__ int warp_base[32][kMaxExperts];
+    pdl_enter();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         int acc = 0, tiles = 0;
@@ -175,6 +203,7 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(
 __global__ void moe_gather_kernel(
     const __nv_bfloat16* x, const int* perm, int n, int K, int H, __half* xs, unsigned* status
 ) {
+    pdl_enter();
     const int per_row = H / 8;
     const size_t total = size_t(n) * per_row;
     bool bad = false;
@@ -201,6 +230,7 @@ __global__ void moe_gather_kernel(
 __global__ void moe_combine_kernel(
     const float* y, const float* weight, const int* pos, int tokens, int K, int H, float* out
 ) {
+    pdl_enter();
     const int per_row = H / 4;
     const size_t total = size_t(tokens) * per_row;
     for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
@@ -330,6 +360,7 @@ __device__ __forceinline__ float act_fn(float gate, float up, int kind, float li
 
 __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_constant__ GroupParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
+    pdl_enter();
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     auto* sh = reinterpret_cast<GemmShared*>(smem + kSmemShared);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -653,6 +684,7 @@ __device__ __forceinline__ int gemv_row(const GemvParams& p, int c, int i) {
 __global__ void __launch_bounds__(32 * kGemvWarps) moe_gemv_kernel(const __grid_constant__ GemvParams p) {
     __shared__ float4 part[kGemvWarps][32];  // each lane's four accumulators, per warp
     __shared__ int off[kMaxExperts + 1];     // expert row offsets: the skip test costs no global load
+    pdl_enter();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int blocks_per_row = p.K / 32, iters = (p.K + 127) / 128;
     for (int i = threadIdx.x; i <= p.E; i += blockDim.x)
@@ -900,8 +932,7 @@ int launch_gemm(GroupParams& p, int max_tiles, cudaStream_t stream) {
         return -slots;
     p.watchdog = watchdog_word();
     const int grid = std::max(1, std::min(slots, max_tiles));
-    moe_gemm_kernel<<<grid, kThreadsG, kSmemTotal, stream>>>(p);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(moe_gemm_kernel, dim3(grid), dim3(kThreadsG), kSmemTotal, stream, p);
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_gemm_kernel launch");
 }
 
@@ -980,14 +1011,18 @@ int dispatch_launch(const float* logits, const uint16_t* x_bf16, size_t tokens, 
     cudaError_t e = cudaMemsetAsync(ws.counts, 0, size_t(E) * 4, stream);
     if (e != cudaSuccess)
         return cuda_fail(e, "counts memset");
-    moe_route_kernel<<<int((tokens * 32 + 255) / 256), 256, 0, stream>>>(logits, int(tokens), E, K, ws.chosen, ws.weight,
-                                                                          ws.counts);
-    moe_sort_kernel<<<1, 1024, 0, stream>>>(ws.chosen, int(n), E, ws.counts, ws.offsets, ws.perm, ws.pos, ws.mtile);
+    e = launch_pdl(moe_route_kernel, dim3(unsigned((tokens * 32 + 255) / 256)), dim3(256), 0, stream, logits,
+                   int(tokens), E, K, ws.chosen, ws.weight, ws.counts);
+    if (e == cudaSuccess)
+        e = launch_pdl(moe_sort_kernel, dim3(1), dim3(1024), 0, stream, static_cast<const int*>(ws.chosen), int(n), E,
+                       static_cast<const int*>(ws.counts), ws.offsets, ws.perm, ws.pos, ws.mtile);
     const size_t work = n * size_t(H / 8);
     const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
-    moe_gather_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x_bf16), ws.perm, int(n), K, H,
-                                                  ws.xs, status);
-    if ((e = cudaGetLastError()) != cudaSuccess)
+    if (e == cudaSuccess)
+        e = launch_pdl(moe_gather_kernel, dim3(blocks), dim3(256), 0, stream,
+                       reinterpret_cast<const __nv_bfloat16*>(x_bf16), static_cast<const int*>(ws.perm), int(n), K, H,
+                       ws.xs, status);
+    if (e != cudaSuccess || (e = cudaGetLastError()) != cudaSuccess)
         return cuda_fail(e, "MoE routing launches");
     return KB200_OK;
 }
@@ -1029,7 +1064,9 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
         v.limit = w->limit;
         v.alpha = w->alpha;
         v.status = status;
-        moe_gemv_kernel<<<std::min(E * v.chunks, grid_cap), 32 * kGemvWarps, 0, stream>>>(v);
+        e = launch_pdl(moe_gemv_kernel, dim3(std::min(E * v.chunks, grid_cap)), dim3(32 * kGemvWarps), 0, stream, v);
+        if (e != cudaSuccess)
+            return cuda_fail(e, "moe_gemv_kernel launch");
         v.blocks = w->down_blocks;
         v.scales = w->down_scales;
         v.bias = w->down_bias;
@@ -1041,8 +1078,8 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
         v.epilogue = 1;
         v.split = 0;
         v.out_cols = H;
-        moe_gemv_kernel<<<std::min(E * v.chunks, grid_cap), 32 * kGemvWarps, 0, stream>>>(v);
-        if ((e = cudaGetLastError()) != cudaSuccess)
+        e = launch_pdl(moe_gemv_kernel, dim3(std::min(E * v.chunks, grid_cap)), dim3(32 * kGemvWarps), 0, stream, v);
+        if (e != cudaSuccess)
             return cuda_fail(e, "moe_gemv_kernel launch");
         return KB200_OK;
     }
@@ -1105,8 +1142,8 @@ int combine_launch(const float* y, const float* weight, const int* pos, size_t t
                    cudaStream_t stream) {
     const size_t work = tokens * size_t(H / 4);
     const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
-    moe_combine_kernel<<<blocks, 256, 0, stream>>>(y, weight, pos, int(tokens), K, H, out);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(moe_combine_kernel, dim3(blocks), dim3(256), 0, stream, y, weight, pos,
+                                     int(tokens), K, H, out);
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_combine_kernel launch");
 }
 
