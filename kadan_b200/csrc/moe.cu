@@ -932,7 +932,10 @@ int launch_gemm(GroupParams& p, int max_tiles, cudaStream_t stream) {
         return -slots;
     p.watchdog = watchdog_word();
     const int grid = std::max(1, std::min(slots, max_tiles));
-    const cudaError_t e = launch_pdl(moe_gemm_kernel, dim3(grid), dim3(kThreadsG), kSmemTotal, stream, p);
+    // A plain launch: GEMM CTAs launched early would hold SMs (176 KB of
+    // shared memory each) that the gather kernel before them still needs.
+    moe_gemm_kernel<<<grid, kThreadsG, kSmemTotal, stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_gemm_kernel launch");
 }
 
