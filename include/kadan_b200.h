@@ -39,7 +39,8 @@ typedef enum kb200_status {
     KB200_ALIAS = 6,             /* "h3_cuda_alias": output overlaps an input */
     KB200_CANCELLED = 7,         /* "h3_cuda_cancelled" */
     KB200_TIMEOUT = 8,           /* a bounded device-side wait ran out */
-    KB200_NO_MEMORY = 9
+    KB200_NO_MEMORY = 9,
+    KB200_QUARANTINED = 10       /* "weight_cleanup_unconfirmed": a weight bank's cleanup failed */
 } kb200_status;
 
 /* Weight encodings: the numbering of kadan::gguf::Encoding
@@ -431,6 +432,136 @@ KB200_API int kb200_moe_route(
  * 16 a peer's chunk never arrived (peer all-reduce), 32 a peer's counts or
  * rows never arrived (expert-parallel exchange). */
 KB200_API int kb200_take_device_error(unsigned* value);
+
+/* ---------------------------------------------------------------------------
+ * Resident weight bank: kadan::DeviceWeights
+ * (IW/include/kadan/device_weights.hpp:35-486). One bank per device, owned by
+ * one thread (calls must not overlap). Entries are immutable packed tiles keyed
+ * by the tensor's file identity and a block range; a miss is admitted only
+ * inside the bank's byte envelope and the device's free memory, copied in
+ * 1 MiB pieces with the cancel word polled before each, synchronised, and only
+ * then published. A failed admission rolls back; a rollback or a release whose
+ * synchronise or free fails quarantines the bank (KB200_QUARANTINED from every
+ * later call except kb200_bank_state and kb200_bank_destroy). */
+
+/* kadan::WeightIdentity (IW/include/kadan/weight_identity.hpp:7-19). */
+typedef struct kb200_weight_identity {
+    uint64_t device, inode, file_size;
+    uint64_t modified_seconds, modified_nanoseconds;
+    uint64_t changed_seconds, changed_nanoseconds;
+    uint64_t payload_begin, payload_end;
+} kb200_weight_identity;
+
+/* DeviceWeights::Key (device_weights.hpp:40-44): `count` blocks of `width`
+ * bytes from block `first` of the tensor. */
+typedef struct kb200_weight_key {
+    kb200_weight_identity source;
+    uint64_t first, count, width;
+} kb200_weight_key;
+
+/* WeightDeviceOperations (device_weights.hpp:19-32) as a table of callbacks;
+ * each returns a kb200_status. `allocate` returning KB200_OK with *out NULL is a
+ * confirmed out-of-memory refusal. Both copies write dst + offset from
+ * src + offset. */
+typedef struct kb200_weight_ops {
+    void* user;
+    int (*available)(void* user, uint64_t* bytes);
+    int (*allocate)(void* user, uint64_t bytes, void** out);
+    int (*copy_host)(void* user, void* dst, uint64_t offset, const void* src, uint64_t bytes);
+    int (*copy_device)(void* user, void* dst, uint64_t offset, const void* src, uint64_t bytes);
+    int (*release)(void* user, void* ptr);
+    int (*synchronize)(void* user);
+} kb200_weight_ops;
+
+/* Why kb200_bank_retain returned no pointer with KB200_OK (the reference's
+ * trace_refusal reasons, device_weights.hpp:199-231). */
+#define KB200_BANK_ADMITTED 0
+#define KB200_BANK_EMPTY 1
+#define KB200_BANK_ENVELOPE 2
+#define KB200_BANK_PHYSICAL 3
+#define KB200_BANK_ALLOCATION 4
+
+typedef struct kb200_bank_state {
+    uint64_t capacity;         /* current envelope (DeviceWeights::capacity) */
+    uint64_t maximum_capacity; /* envelope given at creation */
+    uint64_t allocated;        /* bytes held by entries */
+    uint64_t reserved;         /* envelope charged since the first admission, else 0 */
+    uint64_t entries;
+    int32_t quarantined;
+} kb200_bank_state;
+
+typedef struct kb200_bank kb200_bank;
+
+/* A bank over caller-supplied operations (copied; `user` must outlive the bank). */
+KB200_API int kb200_bank_create(uint64_t limit, const kb200_weight_ops* ops, kb200_bank** out);
+/* A bank over CUDA memory of `device`: cudaMalloc'd entries, copies on a
+ * stream of the bank's own, available = free device memory minus `scratch`. */
+KB200_API int kb200_bank_create_cuda(int device, uint64_t limit, uint64_t scratch, kb200_bank** out);
+/* Releases every entry (best effort when quarantined) and frees the bank. */
+KB200_API void kb200_bank_destroy(kb200_bank* bank);
+KB200_API int kb200_bank_state_get(const kb200_bank* bank, kb200_bank_state* state);
+/* DeviceWeights::find: *ptr = the published entry or NULL. */
+KB200_API int kb200_bank_find(kb200_bank* bank, const kb200_weight_key* key, void** ptr);
+/* DeviceWeights::retain / retain_device: `bytes` must equal count * width.
+ * A hit returns the entry without a copy; a refusal returns KB200_OK with
+ * *ptr NULL and *refusal set (refusal may be NULL). `src` is host memory for
+ * kb200_bank_retain and device memory for kb200_bank_retain_device. */
+KB200_API int kb200_bank_retain(kb200_bank* bank, const kb200_weight_key* key, const void* src, uint64_t bytes,
+                                const volatile int* cancel, void** ptr, int* refusal);
+KB200_API int kb200_bank_retain_device(kb200_bank* bank, const kb200_weight_key* key, const void* src,
+                                       uint64_t bytes, const volatile int* cancel, void** ptr, int* refusal);
+/* DeviceWeights::release_sources: drop every entry of these tensors, keep the
+ * envelope; *released = bytes freed (may be NULL). Not cancellable. */
+KB200_API int kb200_bank_release_sources(kb200_bank* bank, const kb200_weight_identity* sources, size_t count,
+                                         uint64_t* released);
+/* DeviceWeights::release: drop every entry and the envelope's charge. */
+KB200_API int kb200_bank_release(kb200_bank* bank);
+/* DeviceWeights::bound: envelope = min(maximum, bytes); KB200_INVALID once
+ * anything was admitted since the last release. */
+KB200_API int kb200_bank_bound(kb200_bank* bank, uint64_t bytes);
+
+/* ---------------------------------------------------------------------------
+ * Host-span batch over packed-row sources and the bank.
+ *
+ * GgufWeightSource (IW/include/kadan/dense_compute.hpp:172): write `bytes`
+ * bytes of whole packed rows, starting at row `first_row`, to `dst`; return a
+ * kb200_status (nonzero fails the call with that status). */
+typedef int (*kb200_row_source)(void* user, uint64_t first_row, void* dst, uint64_t bytes);
+
+/* DenseCompute::GgufBatchJob (dense_compute.hpp:205-213). */
+typedef struct kb200_source_job {
+    const kb200_weight_identity* identity;
+    kb200_row_source source;
+    void* source_user;
+    const float* input; /* host, rows * in floats */
+    float* output;      /* host, rows * out floats */
+    uint32_t in;
+    uint32_t out;
+    uint32_t rows;
+    int32_t encoding; /* kb200_encoding, KB200_F32 for fp32 rows */
+    int32_t retain_misses;
+} kb200_source_job;
+
+/* Staging of kb200_dense_gguf_source_batch: two halves of this many bytes,
+ * pinned on the host and on the device. */
+#define KB200_SOURCE_STAGING_HALF (16u * 1024u * 1024u)
+
+/* DenseCompute::dense_gguf_batch with packed sources on one device
+ * (IW/src/cuda/h3_compute.cu:3963-4375). Each job's columns are cut into the
+ * reference's chunks (kb200_gguf_batch_partition for one device and
+ * `scratch_limit` bytes of projection scratch) and keyed like the reference's
+ * bank entries ({identity, first block, blocks, block bytes}). Chunks found in
+ * `bank` run from it; the others are read through their source into pinned
+ * staging, one group per staging half (the next group is read while the device
+ * multiplies the previous one), multiplied with a finite check, and then,
+ * for jobs with retain_misses, admitted into `bank` (a refusal is not an
+ * error). `bank` may be NULL: every chunk streams and nothing is kept. The
+ * bank must hold memory of the context's device. Unsupported, input, alias,
+ * cancel and result rules are those of kb200_dense_gguf_batch; sources are
+ * called on the calling thread. */
+KB200_API int kb200_dense_gguf_source_batch(kb200_context* ctx, kb200_bank* bank, const kb200_source_job* jobs,
+                                            size_t count, uint64_t scratch_limit, const volatile int* cancel,
+                                            int* result);
 
 #ifdef __cplusplus
 }

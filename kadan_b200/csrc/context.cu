@@ -1,8 +1,10 @@
-// Host-span boundary: kb200_context and kb200_dense_gguf_batch, the
-// reference's DenseCompute::dense_gguf_batch contract
-// (services/hikari/inference_worker/src/cuda/h3_compute.cu:3963-4375) over
-// device-resident weights. One input upload, one launch per encoding, one
-// download, one stream synchronisation per call.
+// Host-span boundary: kb200_context, kb200_dense_gguf_batch and
+// kb200_dense_gguf_source_batch, the reference's DenseCompute::dense_gguf_batch
+// contract (services/hikari/inference_worker/src/cuda/h3_compute.cu:3963-4375).
+// Over device-resident weights: one input upload, one launch per encoding, one
+// download, one stream synchronisation per call. Over packed-row sources:
+// bank hits as one launch, misses streamed through two pinned staging halves
+// and admitted into the bank once they decoded finite.
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -19,25 +21,11 @@ struct kb200_context {
     size_t workspace_bytes = 0;
     void* pinned = nullptr;
     size_t pinned_bytes = 0;
+    cudaEvent_t staged[2] = {nullptr, nullptr};  // source batch: staging half done
 };
 
 namespace kb200 {
 namespace {
-
-struct DeviceScope {
-    int previous = -1;
-    explicit DeviceScope(int device) {
-        cudaGetDevice(&previous);
-        if (previous != device)
-            cudaSetDevice(device);
-    }
-    ~DeviceScope() {
-        int now = -1;
-        cudaGetDevice(&now);
-        if (previous >= 0 && now != previous)
-            cudaSetDevice(previous);
-    }
-};
 
 int ensure(kb200_context* c, size_t device_bytes, size_t host_bytes) {
     if (device_bytes > c->workspace_bytes) {
@@ -69,6 +57,62 @@ bool cancelled(const volatile int* cancel) {
 
 size_t up16(size_t v) {
     return (v + 15) / 16 * 16;
+}
+
+size_t up256(size_t v) {
+    return (v + 255) / 256 * 256;
+}
+
+// Input spans of a batch on the device. Jobs sharing a span (same pointer and
+// length) upload and check it once (h3_compute.cu:3972-3991); every span
+// starts 64-byte aligned. `owner[j]` marks the job that uploads its span.
+struct InputLayout {
+    std::vector<size_t> at;
+    std::vector<char> owner;
+    size_t floats = 0;
+};
+
+template <class Job>
+int layout_inputs(const Job* jobs, size_t count, InputLayout& l) {
+    l.at.assign(count, 0);
+    l.owner.assign(count, 0);
+    l.floats = 0;
+    for (size_t j = 0; j < count; ++j) {
+        const size_t n = size_t(jobs[j].rows) * jobs[j].in;
+        size_t shared = 0;
+        while (shared < j
+               && (jobs[shared].input != jobs[j].input || size_t(jobs[shared].rows) * jobs[shared].in != n))
+            ++shared;
+        if (shared < j) {
+            l.at[j] = l.at[shared];
+            continue;
+        }
+        for (size_t i = 0; i < n; ++i)
+            if (!std::isfinite(jobs[j].input[i]))
+                return fail(KB200_NONFINITE_INPUT, "non-finite input value");
+        l.at[j] = l.floats;
+        l.owner[j] = 1;
+        l.floats += up16(n);
+    }
+    return KB200_OK;
+}
+
+// No output may overlap any input (the reference's alias rule).
+template <class Job>
+int check_aliases(const Job* jobs, size_t count) {
+    for (size_t j = 0; j < count; ++j)
+        for (size_t k = 0; k < count; ++k)
+            if (overlap(jobs[j].output, size_t(jobs[j].rows) * jobs[j].out * sizeof(float), jobs[k].input,
+                        size_t(jobs[k].rows) * jobs[k].in * sizeof(float)))
+                return fail(KB200_ALIAS, "output overlaps an input");
+    return KB200_OK;
+}
+
+template <class Job>
+void stage_inputs(const Job* jobs, size_t count, const InputLayout& l, uint8_t* host) {
+    for (size_t j = 0; j < count; ++j)
+        if (l.owner[j])
+            std::memcpy(host + l.at[j] * sizeof(float), jobs[j].input, size_t(jobs[j].rows) * jobs[j].in * sizeof(float));
 }
 
 }  // namespace
@@ -105,6 +149,9 @@ void kb200_context_destroy(kb200_context* c) {
         cudaFree(c->workspace);
     if (c->pinned)
         cudaFreeHost(c->pinned);
+    for (cudaEvent_t e : c->staged)
+        if (e)
+            cudaEventDestroy(e);
     cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -156,55 +203,28 @@ int kb200_dense_gguf_batch(
             || job.row_bytes < size_t(job.in) / block_values(job.encoding) * block_bytes(job.encoding))
             return fail(KB200_UNSUPPORTED, "job outside the batched GEMV contract");
     }
-    // Jobs sharing an input span upload and check it once (h3_compute.cu:3972-3991).
-    std::vector<size_t> input_at(count);
-    size_t inputs = 0, outputs = 0;
-    for (size_t j = 0; j < count; ++j) {
-        size_t shared = 0;
-        while (shared < j
-               && (jobs[shared].input != jobs[j].input
-                   || size_t(jobs[shared].rows) * jobs[shared].in != size_t(jobs[j].rows) * jobs[j].in))
-            ++shared;
-        if (shared < j) {
-            input_at[j] = input_at[shared];
-            continue;
-        }
-        const size_t n = size_t(jobs[j].rows) * jobs[j].in;
-        for (size_t i = 0; i < n; ++i)
-            if (!std::isfinite(jobs[j].input[i]))
-                return fail(KB200_NONFINITE_INPUT, "non-finite input value");
-        input_at[j] = inputs;
-        inputs += up16(n);  // keep every input 64-byte aligned on the device
-    }
+    InputLayout inputs;
+    if (const int s = layout_inputs(jobs, count, inputs))
+        return s;
     std::vector<size_t> output_at(count);
+    size_t outputs = 0;
     for (size_t j = 0; j < count; ++j) {
         output_at[j] = outputs;
         outputs += size_t(jobs[j].rows) * jobs[j].out;
     }
-    for (size_t j = 0; j < count; ++j)
-        for (size_t k = 0; k < count; ++k)
-            if (overlap(jobs[j].output, size_t(jobs[j].rows) * jobs[j].out * sizeof(float), jobs[k].input,
-                        size_t(jobs[k].rows) * jobs[k].in * sizeof(float)))
-                return fail(KB200_ALIAS, "output overlaps an input");
+    if (const int s = check_aliases(jobs, count))
+        return s;
 
     DeviceScope scope(c->device);
     // Device layout: [inputs][outputs][status]; host staging mirrors it.
-    const size_t in_bytes = inputs * sizeof(float), out_bytes = outputs * sizeof(float);
+    const size_t in_bytes = inputs.floats * sizeof(float), out_bytes = outputs * sizeof(float);
     const size_t status_at = up16(in_bytes + out_bytes);
     const size_t total = status_at + 16;
     if (const int s = ensure(c, total, total))
         return s;
     auto* dev = static_cast<uint8_t*>(c->workspace);
     auto* host = static_cast<uint8_t*>(c->pinned);
-    for (size_t j = 0; j < count; ++j) {
-        bool first = true;
-        for (size_t k = 0; k < j; ++k)
-            if (input_at[k] == input_at[j])
-                first = false;
-        if (first)
-            std::memcpy(host + input_at[j] * sizeof(float), jobs[j].input,
-                        size_t(jobs[j].rows) * jobs[j].in * sizeof(float));
-    }
+    stage_inputs(jobs, count, inputs, host);
     std::memset(host + status_at, 0, sizeof(unsigned));
     cudaError_t e = cudaMemcpyAsync(dev, host, in_bytes, cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess)
@@ -221,7 +241,7 @@ int kb200_dense_gguf_batch(
         const auto& job = jobs[j];
         device_jobs[j] = kb200_gemv_job{
             job.weights,
-            reinterpret_cast<const float*>(dev) + input_at[j],
+            reinterpret_cast<const float*>(dev) + inputs.at[j],
             reinterpret_cast<float*>(dev + in_bytes) + output_at[j],
             job.validated ? nullptr : status,
             job.row_bytes,
@@ -247,6 +267,219 @@ int kb200_dense_gguf_batch(
     std::memcpy(&invalid, host + status_at, sizeof(invalid));
     if (invalid)
         return fail(KB200_NONFINITE_WEIGHT, "a decoded weight is not finite");
+    for (size_t j = 0; j < count; ++j)
+        std::memcpy(jobs[j].output, host + in_bytes + output_at[j] * sizeof(float),
+                    size_t(jobs[j].rows) * jobs[j].out * sizeof(float));
+    if (result)
+        *result = KB200_RESULT_UNVALIDATED;
+    return KB200_OK;
+}
+
+}  // extern "C"
+
+namespace kb200 {
+namespace {
+
+constexpr size_t kHalf = KB200_SOURCE_STAGING_HALF;
+
+// One column chunk of a source job: its bank key, its place in the output
+// and, when it streams, its byte offset inside a staging half.
+struct Chunk {
+    size_t job;
+    uint64_t first_col, cols, bytes, row_bytes;
+    kb200_weight_key key;
+    const void* resident;
+    size_t offset;
+};
+
+// Misses [begin, end) share one staging half; `used` bytes of it.
+struct Group {
+    size_t begin, end, used;
+};
+
+}  // namespace
+}  // namespace kb200
+
+extern "C" {
+
+int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb200_source_job* jobs, size_t count,
+                                  uint64_t scratch_limit, const volatile int* cancel, int* result) {
+    if (result)
+        *result = KB200_RESULT_UNSUPPORTED;
+    if (!c || !jobs || !count)
+        return fail(KB200_UNSUPPORTED, "empty batch");
+    if (cancelled(cancel))
+        return fail(KB200_CANCELLED, "cancelled before start");
+    // Unsupported precedes every source read and output write (gguf_batch_supported).
+    for (size_t j = 0; j < count; ++j) {
+        const auto& job = jobs[j];
+        if (!kb200_encoding_supported(job.encoding) || !job.identity || !job.source || !job.input || !job.output
+            || !job.in || !job.out || !job.rows || job.rows > KB200_BATCH_MAX_ROWS || job.in % 8
+            || job.in % kb200_block_values(job.encoding))
+            return fail(KB200_UNSUPPORTED, "job outside the batched GEMV contract");
+    }
+    // The reference's chunk geometry on one device (gguf_batch_partition.hpp:44-83).
+    const uint64_t one_device = 1, limit = scratch_limit ? scratch_limit : (uint64_t(1) << 30);
+    std::vector<kb200_partition> parts(count);
+    for (size_t j = 0; j < count; ++j)
+        if (const int s = kb200_gguf_batch_partition(jobs[j].in, jobs[j].out, jobs[j].encoding, &one_device, 1, 0,
+                                                     limit, &parts[j]))
+            return s;
+    InputLayout inputs;
+    if (const int s = layout_inputs(jobs, count, inputs))
+        return s;
+    std::vector<size_t> output_at(count);
+    size_t outputs = 0;
+    for (size_t j = 0; j < count; ++j) {
+        output_at[j] = outputs;
+        outputs += size_t(jobs[j].rows) * jobs[j].out;
+    }
+    if (const int s = check_aliases(jobs, count))
+        return s;
+
+    DeviceScope scope(c->device);
+    // Bank lookups (h3_compute.cu:4063-4115): hits run from the bank, misses stream.
+    std::vector<Chunk> hits, misses;
+    for (size_t j = 0; j < count; ++j) {
+        const auto& job = jobs[j];
+        const uint64_t values = kb200_block_values(job.encoding), width = kb200_block_bytes(job.encoding);
+        const uint64_t blocks_per_row = job.in / values, row_bytes = blocks_per_row * width;
+        const auto& part = parts[j];
+        for (uint64_t off = 0; off < part.count; off += part.chunk_columns) {
+            const uint64_t cols = std::min<uint64_t>(part.chunk_columns, part.count - off), first = part.first + off;
+            Chunk ch{j, first, cols, cols * row_bytes, row_bytes,
+                     kb200_weight_key{*job.identity, first * blocks_per_row, cols * blocks_per_row, width},
+                     nullptr, 0};
+            void* hit = nullptr;
+            if (bank)
+                if (const int s = kb200_bank_find(bank, &ch.key, &hit))
+                    return s;
+            ch.resident = hit;
+            (hit ? hits : misses).push_back(ch);
+        }
+    }
+    std::vector<Group> groups;
+    for (size_t k = 0; k < misses.size();) {
+        Group g{k, k, 0};
+        while (g.end < misses.size() && (g.end == g.begin || g.used + up256(misses[g.end].bytes) <= kHalf)) {
+            if (misses[g.end].bytes > kHalf)
+                return fail(KB200_INVALID, "gguf_projection_layout");
+            misses[g.end].offset = g.used;
+            g.used += up256(misses[g.end].bytes);
+            ++g.end;
+        }
+        groups.push_back(g);
+        k = g.end;
+    }
+
+    // Device layout: [inputs][outputs][2 status words][staging half 0][half 1];
+    // the pinned host buffer mirrors it.
+    const size_t in_bytes = up256(inputs.floats * sizeof(float)), out_bytes = up256(outputs * sizeof(float));
+    const size_t status_at = in_bytes + out_bytes, staging_at = status_at + 256;
+    const size_t total = staging_at + (groups.empty() ? 0 : 2 * kHalf);
+    if (const int s = ensure(c, total, total))
+        return s;
+    for (cudaEvent_t& e : c->staged)
+        if (!e)
+            if (const cudaError_t err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming))
+                return cuda_fail(err, "cudaEventCreate");
+    auto* dev = static_cast<uint8_t*>(c->workspace);
+    auto* host = static_cast<uint8_t*>(c->pinned);
+    auto* dev_in = reinterpret_cast<const float*>(dev);
+    auto* dev_out = reinterpret_cast<float*>(dev + in_bytes);
+    auto* dev_status = reinterpret_cast<unsigned*>(dev + status_at);
+    auto* host_status = reinterpret_cast<volatile unsigned*>(host + status_at);
+    uint8_t* dev_stage = dev + staging_at;
+    uint8_t* host_stage = host + staging_at;
+    auto abandon = [&](int status) {
+        cudaStreamSynchronize(c->stream);
+        return status;
+    };
+    auto device_job = [&](const Chunk& ch, const void* weights, unsigned* status) {
+        const auto& job = jobs[ch.job];
+        return kb200_gemv_job{weights, dev_in + inputs.at[ch.job], dev_out + output_at[ch.job] + ch.first_col,
+                              status, size_t(ch.row_bytes), job.out, job.in, uint32_t(ch.cols), job.rows,
+                              job.encoding};
+    };
+
+    stage_inputs(jobs, count, inputs, host);
+    if (const cudaError_t e = cudaMemcpyAsync(dev, host, inputs.floats * sizeof(float), cudaMemcpyHostToDevice,
+                                              c->stream))
+        return abandon(cuda_fail(e, "input upload"));
+    if (!hits.empty()) {
+        // Bank entries were checked finite when they were admitted.
+        std::vector<kb200_gemv_job> launch;
+        for (const Chunk& ch : hits)
+            launch.push_back(device_job(ch, ch.resident, nullptr));
+        if (const int s = kb200_gguf_gemv_batch(launch.data(), launch.size(), c->stream))
+            return abandon(s);
+    }
+    // Group g uses half g % 2; before it is refilled, group g - 2 is finished:
+    // its status read, and its chunks admitted while their bytes are still staged.
+    auto finish = [&](size_t g) -> int {
+        const size_t half = g % 2;
+        if (const cudaError_t e = cudaEventSynchronize(c->staged[half]))
+            return cuda_fail(e, "streamed group");
+        if (host_status[half])
+            return fail(KB200_NONFINITE_WEIGHT, "a decoded weight is not finite");
+        if (cancelled(cancel))
+            return fail(KB200_CANCELLED, "cancelled after a streamed group");
+        if (!bank)
+            return KB200_OK;
+        for (size_t k = groups[g].begin; k < groups[g].end; ++k) {
+            const Chunk& m = misses[k];
+            if (!jobs[m.job].retain_misses)
+                continue;
+            void* kept = nullptr;
+            int refusal = 0;
+            if (const int s = kb200_bank_retain_device(bank, &m.key, dev_stage + half * kHalf + m.offset, m.bytes,
+                                                       cancel, &kept, &refusal))
+                return s;
+        }
+        return KB200_OK;
+    };
+    for (size_t g = 0; g < groups.size(); ++g) {
+        const size_t half = g % 2;
+        if (g >= 2)
+            if (const int s = finish(g - 2))
+                return abandon(s);
+        if (cancelled(cancel))
+            return abandon(fail(KB200_CANCELLED, "cancelled before a streamed group"));
+        uint8_t* staged = host_stage + half * kHalf;
+        std::vector<kb200_gemv_job> launch;
+        for (size_t k = groups[g].begin; k < groups[g].end; ++k) {
+            const Chunk& m = misses[k];
+            const auto& job = jobs[m.job];
+            if (const int s = job.source(job.source_user, m.first_col, staged + m.offset, m.bytes))
+                return abandon(fail(s, "packed-row source failed"));
+            launch.push_back(device_job(m, dev_stage + half * kHalf + m.offset, dev_status + half));
+        }
+        cudaError_t e = cudaMemcpyAsync(dev_stage + half * kHalf, staged, groups[g].used, cudaMemcpyHostToDevice,
+                                        c->stream);
+        if (e == cudaSuccess)
+            e = cudaMemsetAsync(dev_status + half, 0, sizeof(unsigned), c->stream);
+        if (e != cudaSuccess)
+            return abandon(cuda_fail(e, "staging upload"));
+        if (const int s = kb200_gguf_gemv_batch(launch.data(), launch.size(), c->stream))
+            return abandon(s);
+        e = cudaMemcpyAsync(const_cast<unsigned*>(host_status + half), dev_status + half, sizeof(unsigned),
+                            cudaMemcpyDeviceToHost, c->stream);
+        if (e == cudaSuccess)
+            e = cudaEventRecord(c->staged[half], c->stream);
+        if (e != cudaSuccess)
+            return abandon(cuda_fail(e, "staging status"));
+    }
+    for (size_t g = groups.size() >= 2 ? groups.size() - 2 : 0; g < groups.size(); ++g)
+        if (const int s = finish(g))
+            return abandon(s);
+    cudaError_t e = cudaMemcpyAsync(host + in_bytes, dev_out, outputs * sizeof(float), cudaMemcpyDeviceToHost,
+                                    c->stream);
+    if (e == cudaSuccess)
+        e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess)
+        return abandon(cuda_fail(e, "output download"));
+    if (cancelled(cancel))
+        return fail(KB200_CANCELLED, "cancelled after download");
     for (size_t j = 0; j < count; ++j)
         std::memcpy(jobs[j].output, host + in_bytes + output_at[j] * sizeof(float),
                     size_t(jobs[j].rows) * jobs[j].out * sizeof(float));

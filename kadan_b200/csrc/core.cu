@@ -74,6 +74,7 @@ const char* kb200_status_name(int status) {
     case KB200_CANCELLED: return "h3_cuda_cancelled";
     case KB200_TIMEOUT: return "kb200_device_wait_timeout";
     case KB200_NO_MEMORY: return "h3_cuda_projection_scratch";
+    case KB200_QUARANTINED: return "weight_cleanup_unconfirmed";
     default: return "kb200_unknown_status";
     }
 }

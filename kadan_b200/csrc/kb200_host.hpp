@@ -26,6 +26,24 @@ inline bool aligned(const void* p, size_t to) {
     return reinterpret_cast<std::uintptr_t>(p) % to == 0;
 }
 
+// Makes `device` current for the scope and restores the previous device.
+struct DeviceScope {
+    int previous = -1;
+    explicit DeviceScope(int device) {
+        cudaGetDevice(&previous);
+        if (previous != device)
+            cudaSetDevice(device);
+    }
+    ~DeviceScope() {
+        int now = -1;
+        cudaGetDevice(&now);
+        if (previous >= 0 && now != previous)
+            cudaSetDevice(previous);
+    }
+    DeviceScope(const DeviceScope&) = delete;
+    DeviceScope& operator=(const DeviceScope&) = delete;
+};
+
 // Device address of the watchdog word (a file-scope __device__ variable of
 // core.cu) on the current device; kernels with bounded waits report there.
 unsigned* watchdog_word();

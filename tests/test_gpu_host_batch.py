@@ -1,0 +1,243 @@
+"""GPU tests of the host-span boundary: kb200_dense_gguf_batch over resident
+weights, the CUDA weight bank, and kb200_dense_gguf_source_batch (bank hits,
+streamed misses through the two staging halves, admission after the finite
+check), against the pinned oracle. Tolerance 1e-3 as max|y - ref| /
+max(max|ref|, 1) (IW/tests/gguf_text.cpp:247-250)."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+class DeviceBytes:
+    """A uint8 view of `n` device bytes at `ptr` for torch.as_tensor."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+def device_bytes(ptr, n):
+    import torch
+
+    return torch.as_tensor(DeviceBytes(ptr, n), device="cuda:0").cpu().numpy()
+
+
+def weights(kb, enc, out, in_, seed):
+    from kadan_b200 import synth
+
+    if enc == kb.F32:
+        rng = np.random.default_rng(seed)
+        return (rng.standard_normal((out, in_)) * 0.05).astype(np.float32).view(np.uint8).reshape(out, -1)
+    return synth.gguf(enc, out, in_, seed=seed)
+
+
+def reference(kb, oracle, enc, w, x, in_, out):
+    if enc == kb.F32:
+        return x.astype(np.float64) @ w.view(np.float32).reshape(out, in_).astype(np.float64).T
+    return oracle.gemv_f64(enc, w, x, in_, out)
+
+
+def test_dense_gguf_batch_parity_and_errors(kb, oracle, cuda):
+    from kadan_b200 import synth
+
+    ctx = kb.Context(0)
+    try:
+        cases = [(kb.Q4_K, 4096, 1024, 1), (kb.Q6_K, 4096, 512, 2), (kb.Q8_0, 2048, 300, 3), (kb.F32, 256, 64, 1)]
+        ptrs, jobs, want = [], [], []
+        for i, (enc, in_, out, rows) in enumerate(cases):
+            w = weights(kb, enc, out, in_, seed=10 + i)
+            x = synth.activations(rows * in_, seed=20 + i, dtype="f32").reshape(rows, in_)
+            y = np.full((rows, out), np.nan, dtype=np.float32)
+            p = ctx.upload(w)
+            ptrs.append(p)
+            jobs.append((kb.host_job(enc, p, x, y, in_=in_, out=out), x, y))
+            want.append(reference(kb, oracle, enc, w, x, in_, out))
+        assert ctx.dense_gguf_batch([j for j, _, _ in jobs]) == kb.RESULT_UNVALIDATED
+        for (_, _, y), ref in zip(jobs, want):
+            assert rel_err(y, ref) < TOL
+        # Errors: non-finite input, aliasing output, cancel, unsupported shape.
+        j0, x0, y0 = jobs[0]
+        x0[0, 5] = np.inf
+        with pytest.raises(kb.KadanError) as e:
+            ctx.dense_gguf_batch([j0])
+        assert e.value.status == kb.NONFINITE_INPUT
+        x0[0, 5] = 0.0
+        alias = kb.HostJob(j0.weights, j0.input, j0.input, j0.row_bytes, j0.in_, 8, 1, j0.encoding, 0)
+        with pytest.raises(kb.KadanError) as e:
+            ctx.dense_gguf_batch([alias])
+        assert e.value.status == kb.ALIAS
+        with pytest.raises(kb.KadanError) as e:
+            ctx.dense_gguf_batch([j0], cancel=ctypes.c_int(1))
+        assert e.value.status == kb.CANCELLED
+        bad = kb.HostJob(j0.weights, j0.input, j0.output, j0.row_bytes, 100, j0.out, 1, j0.encoding, 0)
+        with pytest.raises(kb.Unsupported):
+            ctx.dense_gguf_batch([bad])
+    finally:
+        for p in ptrs:
+            ctx.free(p)
+        ctx.close()
+
+
+def test_cuda_bank_round_trip(cuda):
+    import torch
+
+    from kadan_b200.weight_bank import ENVELOPE, WeightBank, WeightIdentity, WeightKey
+
+    bank = WeightBank.cuda(0, 8 << 20)
+    try:
+        rng = np.random.default_rng(3)
+        host = rng.integers(0, 256, size=3 * (1 << 20) + 100, dtype=np.uint8)
+        k = WeightKey(WeightIdentity(inode=5), 0, host.size, 1)
+        p = bank.retain(k, host.ctypes.data, host.size)
+        assert p and bank.find(k) == p and p % 256 == 0
+        assert np.array_equal(device_bytes(p, host.size), host)
+        dev = torch.from_numpy(rng.integers(0, 256, size=(1 << 20) + 48, dtype=np.uint8)).to(cuda)
+        kd = WeightKey(WeightIdentity(inode=6), 0, dev.numel() // 16, 16)
+        q = bank.retain_device(kd, dev.data_ptr(), dev.numel())
+        assert q and np.array_equal(device_bytes(q, dev.numel()), dev.cpu().numpy())
+        assert bank.allocated() == host.size + dev.numel()
+        big = WeightKey(WeightIdentity(inode=7), 0, 5 << 20, 1)
+        assert bank.retain_device(big, dev.data_ptr(), 5 << 20) is None and bank.last_refusal == ENVELOPE
+        assert bank.release_sources([WeightIdentity(inode=5)]) == host.size
+        assert bank.find(k) is None and bank.find(kd) == q
+        bank.release()
+        assert bank.allocated() == 0 and bank.reserved() == 0
+    finally:
+        bank.close()
+
+
+def source_jobs(kb, oracle, specs):
+    """SourceJobs over numpy packed rows; returns (jobs, references)."""
+    from kadan_b200 import synth
+    from kadan_b200.weight_bank import SourceJob, WeightIdentity
+
+    jobs, refs = [], []
+    for i, (enc, in_, out, rows) in enumerate(specs):
+        w = weights(kb, enc, out, in_, seed=40 + i)
+        x = synth.activations(rows * in_, seed=50 + i, dtype="f32").reshape(rows, in_)
+        y = np.full((rows, out), np.nan, dtype=np.float32)
+        row_bytes = w.shape[1]
+
+        def read(first_row, nbytes, w=w, row_bytes=row_bytes):
+            assert nbytes % row_bytes == 0
+            return w[first_row:first_row + nbytes // row_bytes]
+
+        jobs.append(SourceJob(WeightIdentity(device=9, inode=100 + i, payload_end=w.nbytes), read, x, y, in_, out,
+                              enc))
+        refs.append(reference(kb, oracle, enc, w, x, in_, out))
+    return jobs, refs
+
+
+# Q8_0 4096 x 8192: 4352-byte rows, chunks of 3855 columns (three chunks, each
+# nearly a whole staging half: three groups over both halves); Q4_K 4096 x
+# 14336: two chunks; Q6_K one chunk; F32 rows.
+SPECS = [(2, 4096, 8192, 1), (1, 4096, 14336, 2), (3, 4096, 4096, 1), (-1, 512, 96, 3)]
+
+
+def test_source_batch_streams_then_hits(kb, oracle, cuda):
+    from kadan_b200.weight_bank import WeightBank, dense_gguf_source_batch
+
+    jobs, refs = source_jobs(kb, oracle, SPECS)
+    ctx = kb.Context(0)
+    bank = WeightBank.cuda(0, 256 << 20)
+    try:
+        assert dense_gguf_source_batch(ctx, bank, jobs) == kb.RESULT_UNVALIDATED
+        for job, ref in zip(jobs, refs):
+            assert rel_err(job.y, ref) < TOL
+        assert [len(j.reads) for j in jobs] == [3, 2, 1, 1]
+        assert [r[0] for r in jobs[0].reads] == [0, 3855, 7710]
+        total = sum(j.y.shape[1] * (j.in_ * 4 if j.encoding == kb.F32 else kb.row_bytes(j.encoding, j.in_))
+                    for j in jobs)
+        assert bank.entries() == 7 and bank.allocated() == total
+        # Second call: every chunk is a bank hit, no source is read.
+        for j in jobs:
+            j.reads.clear()
+            j.y[:] = np.nan
+        assert dense_gguf_source_batch(ctx, bank, jobs) == kb.RESULT_UNVALIDATED
+        assert all(not j.reads for j in jobs)
+        for job, ref in zip(jobs, refs):
+            assert rel_err(job.y, ref) < TOL
+    finally:
+        bank.close()
+        ctx.close()
+
+
+def test_source_batch_without_retention(kb, oracle, cuda):
+    from kadan_b200.weight_bank import WeightBank, dense_gguf_source_batch
+
+    jobs, refs = source_jobs(kb, oracle, SPECS[:2])
+    jobs[1].retain_misses = False
+    ctx = kb.Context(0)
+    small = WeightBank.cuda(0, 20 << 20)
+    try:
+        for bank in (None, small):
+            for j in jobs:
+                j.reads.clear()
+                j.y[:] = np.nan
+            dense_gguf_source_batch(ctx, bank, jobs)
+            for job, ref in zip(jobs, refs):
+                assert rel_err(job.y, ref) < TOL
+            assert [len(j.reads) for j in jobs] == [3, 2]
+        # Q8_0 chunks 1 (16.8 MB) and 3 (2.1 MB) fit the envelope, chunk 2 is
+        # refused; the Q4_K job keeps nothing.
+        assert small.entries() == 2 and small.allocated() == (3855 + 482) * 4352
+        # The next call hits those two chunks and streams the rest.
+        for j in jobs:
+            j.reads.clear()
+        dense_gguf_source_batch(ctx, small, jobs)
+        assert [len(j.reads) for j in jobs] == [1, 2] and jobs[0].reads[0][0] == 3855
+        for job, ref in zip(jobs, refs):
+            assert rel_err(job.y, ref) < TOL
+    finally:
+        small.close()
+        ctx.close()
+
+
+def test_source_batch_failures_keep_nothing(kb, oracle, cuda):
+    from kadan_b200.weight_bank import WeightBank, dense_gguf_source_batch
+
+    jobs, _ = source_jobs(kb, oracle, [SPECS[0]])
+    job = jobs[0]
+    ctx = kb.Context(0)
+    bank = WeightBank.cuda(0, 256 << 20)
+    try:
+        # A non-finite scale in the second chunk: the call fails, the first
+        # chunk (finite, finished before it) may be kept, the bad one never is.
+        w = job.read(0, 8192 * 4352).copy()
+        w[5000, 0:2] = np.frombuffer(np.float16(np.inf).tobytes(), dtype=np.uint8)
+        job.read = lambda first, n: w[first:first + n // 4352]
+        y_before = job.y.copy()
+        with pytest.raises(kb.KadanError) as e:
+            dense_gguf_source_batch(ctx, bank, jobs)
+        assert e.value.status == kb.NONFINITE_WEIGHT
+        assert np.array_equal(np.isnan(job.y), np.isnan(y_before))
+        assert bank.entries() <= 1
+        from kadan_b200.weight_bank import WeightKey
+
+        second = WeightKey(job.identity, 3855 * 128, 3855 * 128, 34)
+        assert bank.find(second) is None
+        # Cancellation raised while a source is read.
+        cancel = ctypes.c_int(0)
+
+        def cancelling(first, n):
+            cancel.value = 1
+            return w[first:first + n // 4352]
+
+        job.read = cancelling
+        with pytest.raises(kb.KadanError) as e:
+            dense_gguf_source_batch(ctx, bank, jobs, cancel=cancel)
+        assert e.value.status == kb.CANCELLED
+        # A failing source fails the call.
+        job.read = lambda first, n: b"short"
+        with pytest.raises(kb.KadanError):
+            dense_gguf_source_batch(ctx, None, jobs)
+    finally:
+        bank.close()
+        ctx.close()
