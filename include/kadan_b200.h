@@ -206,12 +206,16 @@ typedef struct kb200_host_job {
  * input with KB200_ALIAS; then one input upload, one launch per encoding, one
  * download of outputs plus the weight status word, and KB200_NONFINITE_WEIGHT
  * when an unvalidated weight decoded non-finite. *cancel (may be NULL) is
- * polled between stages (KB200_CANCELLED). */
+ * polled between stages (KB200_CANCELLED).
+ *
+ * Every `cancel` of this ABI is one byte, nonzero once the call should stop:
+ * the storage of the worker's std::atomic_bool (lock-free and one byte on its
+ * platforms) can be passed as is. */
 KB200_API int kb200_dense_gguf_batch(
     kb200_context* ctx,
     const kb200_host_job* jobs,
     size_t count,
-    const volatile int* cancel,
+    const volatile uint8_t* cancel,
     int* result
 );
 
@@ -507,9 +511,9 @@ KB200_API int kb200_bank_find(kb200_bank* bank, const kb200_weight_key* key, voi
  * *ptr NULL and *refusal set (refusal may be NULL). `src` is host memory for
  * kb200_bank_retain and device memory for kb200_bank_retain_device. */
 KB200_API int kb200_bank_retain(kb200_bank* bank, const kb200_weight_key* key, const void* src, uint64_t bytes,
-                                const volatile int* cancel, void** ptr, int* refusal);
+                                const volatile uint8_t* cancel, void** ptr, int* refusal);
 KB200_API int kb200_bank_retain_device(kb200_bank* bank, const kb200_weight_key* key, const void* src,
-                                       uint64_t bytes, const volatile int* cancel, void** ptr, int* refusal);
+                                       uint64_t bytes, const volatile uint8_t* cancel, void** ptr, int* refusal);
 /* DeviceWeights::release_sources: drop every entry of these tensors, keep the
  * envelope; *released = bytes freed (may be NULL). Not cancellable. */
 KB200_API int kb200_bank_release_sources(kb200_bank* bank, const kb200_weight_identity* sources, size_t count,
@@ -560,7 +564,7 @@ typedef struct kb200_source_job {
  * cancel and result rules are those of kb200_dense_gguf_batch; sources are
  * called on the calling thread. */
 KB200_API int kb200_dense_gguf_source_batch(kb200_context* ctx, kb200_bank* bank, const kb200_source_job* jobs,
-                                            size_t count, uint64_t scratch_limit, const volatile int* cancel,
+                                            size_t count, uint64_t scratch_limit, const volatile uint8_t* cancel,
                                             int* result);
 
 #ifdef __cplusplus

@@ -146,7 +146,7 @@ def _load() -> ctypes.CDLL:
     lib.kb200_context_stream.restype = vp
     lib.kb200_weights_upload.argtypes = [vp, vp, c_size, ctypes.POINTER(vp)]
     lib.kb200_weights_free.argtypes = [vp, vp]
-    lib.kb200_dense_gguf_batch.argtypes = [vp, ctypes.POINTER(HostJob), c_size, ctypes.POINTER(c_int),
+    lib.kb200_dense_gguf_batch.argtypes = [vp, ctypes.POINTER(HostJob), c_size, ctypes.POINTER(ctypes.c_ubyte),
                                            ctypes.POINTER(c_int)]
     lib.kb200_moe_workspace_bytes.restype = c_size
     lib.kb200_moe_workspace_bytes.argtypes = [ctypes.POINTER(MoeWeights), c_size]
@@ -300,8 +300,9 @@ class Context:
     def free(self, ptr: int) -> None:
         check(lib.kb200_weights_free(self.handle, ptr))
 
-    def dense_gguf_batch(self, jobs: Sequence[HostJob], cancel: Optional[ctypes.c_int] = None) -> int:
-        """Returns RESULT_UNVALIDATED; raises Unsupported / KadanError like the reference throws."""
+    def dense_gguf_batch(self, jobs: Sequence[HostJob], cancel: Optional[ctypes.c_ubyte] = None) -> int:
+        """Returns RESULT_UNVALIDATED; raises Unsupported / KadanError like the reference throws.
+        `cancel`: a ctypes.c_ubyte another thread may set (the worker's atomic_bool)."""
         arr = (HostJob * len(jobs))(*jobs)
         result = ctypes.c_int(0)
         check(lib.kb200_dense_gguf_batch(self.handle, arr, len(jobs),

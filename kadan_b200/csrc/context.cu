@@ -51,7 +51,7 @@ int ensure(kb200_context* c, size_t device_bytes, size_t host_bytes) {
     return KB200_OK;
 }
 
-bool cancelled(const volatile int* cancel) {
+bool cancelled(const volatile uint8_t* cancel) {
     return cancel && *cancel;
 }
 
@@ -186,7 +186,7 @@ int kb200_weights_free(kb200_context* c, void* device) {
 }
 
 int kb200_dense_gguf_batch(
-    kb200_context* c, const kb200_host_job* jobs, size_t count, const volatile int* cancel, int* result
+    kb200_context* c, const kb200_host_job* jobs, size_t count, const volatile uint8_t* cancel, int* result
 ) {
     if (result)
         *result = KB200_RESULT_UNSUPPORTED;
@@ -303,7 +303,7 @@ struct Group {
 extern "C" {
 
 int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb200_source_job* jobs, size_t count,
-                                  uint64_t scratch_limit, const volatile int* cancel, int* result) {
+                                  uint64_t scratch_limit, const volatile uint8_t* cancel, int* result) {
     if (result)
         *result = KB200_RESULT_UNSUPPORTED;
     if (!c || !jobs || !count)

@@ -88,7 +88,7 @@ int report(const Failure& f) {
     return fail(f.status, f.what.c_str());
 }
 
-bool stopped(const volatile int* cancel) {
+bool stopped(const volatile uint8_t* cancel) {
     return cancel && *cancel;
 }
 
@@ -124,7 +124,7 @@ int healthy(const kb200_bank* b) {
 
 // DeviceWeights::retain_bytes (device_weights.hpp:181-270).
 int retain_bytes(kb200_bank* b, const kb200_weight_key* key, const void* src, uint64_t bytes, bool device_source,
-                 const volatile int* cancel, void** ptr, int* refusal) {
+                 const volatile uint8_t* cancel, void** ptr, int* refusal) {
     if (!ptr)
         return fail(KB200_INVALID, "null output");
     *ptr = nullptr;
@@ -359,12 +359,12 @@ int kb200_bank_find(kb200_bank* b, const kb200_weight_key* key, void** ptr) {
 }
 
 int kb200_bank_retain(kb200_bank* b, const kb200_weight_key* key, const void* src, uint64_t bytes,
-                      const volatile int* cancel, void** ptr, int* refusal) {
+                      const volatile uint8_t* cancel, void** ptr, int* refusal) {
     return retain_bytes(b, key, src, bytes, false, cancel, ptr, refusal);
 }
 
 int kb200_bank_retain_device(kb200_bank* b, const kb200_weight_key* key, const void* src, uint64_t bytes,
-                             const volatile int* cancel, void** ptr, int* refusal) {
+                             const volatile uint8_t* cancel, void** ptr, int* refusal) {
     return retain_bytes(b, key, src, bytes, true, cancel, ptr, refusal);
 }
 

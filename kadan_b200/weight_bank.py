@@ -18,7 +18,7 @@ from typing import Iterable, Optional
 
 from . import CANCELLED, CUDA, OK, KadanError, check, lib
 
-c_u64, vp, c_int = ctypes.c_uint64, ctypes.c_void_p, ctypes.c_int
+c_u64, vp, c_int, c_u8 = ctypes.c_uint64, ctypes.c_void_p, ctypes.c_int, ctypes.c_ubyte
 
 ADMITTED, EMPTY, ENVELOPE, PHYSICAL, ALLOCATION = range(5)
 REFUSAL_NAMES = {EMPTY: "empty", ENVELOPE: "envelope", PHYSICAL: "physical", ALLOCATION: "allocation"}
@@ -58,7 +58,7 @@ lib.kb200_bank_destroy.restype = None
 lib.kb200_bank_state_get.argtypes = [vp, ctypes.POINTER(BankStateC)]
 lib.kb200_bank_find.argtypes = [vp, ctypes.POINTER(WeightKeyC), ctypes.POINTER(vp)]
 for _fn in (lib.kb200_bank_retain, lib.kb200_bank_retain_device):
-    _fn.argtypes = [vp, ctypes.POINTER(WeightKeyC), vp, c_u64, ctypes.POINTER(c_int), ctypes.POINTER(vp),
+    _fn.argtypes = [vp, ctypes.POINTER(WeightKeyC), vp, c_u64, ctypes.POINTER(c_u8), ctypes.POINTER(vp),
                     ctypes.POINTER(c_int)]
 lib.kb200_bank_release_sources.argtypes = [vp, ctypes.POINTER(WeightIdentityC), ctypes.c_size_t,
                                            ctypes.POINTER(c_u64)]
@@ -192,18 +192,18 @@ class WeightBank:
 
     def _retain(self, fn, key: WeightKey, src: Optional[int], nbytes: int, cancel) -> Optional[int]:
         p, why = vp(), c_int(0)
-        cancel_ptr = ctypes.pointer(cancel) if isinstance(cancel, c_int) else None
+        cancel_ptr = None if cancel is None else ctypes.pointer(cancel)
         check(fn(self._h, ctypes.byref(key.c()), src, nbytes, cancel_ptr, ctypes.byref(p), ctypes.byref(why)))
         self.last_refusal = why.value
         return p.value
 
-    def retain(self, key: WeightKey, src: Optional[int], nbytes: int, cancel: Optional[ctypes.c_int] = None):
+    def retain(self, key: WeightKey, src: Optional[int], nbytes: int, cancel: Optional[ctypes.c_ubyte] = None):
         """Admit `nbytes` of host memory at address `src` (or return the hit);
         None when the bank refuses (reason in `last_refusal`)."""
         return self._retain(lib.kb200_bank_retain, key, src, nbytes, cancel)
 
     def retain_device(self, key: WeightKey, src: Optional[int], nbytes: int,
-                      cancel: Optional[ctypes.c_int] = None):
+                      cancel: Optional[ctypes.c_ubyte] = None):
         """As `retain`, copying from device memory at `src`."""
         return self._retain(lib.kb200_bank_retain_device, key, src, nbytes, cancel)
 
@@ -245,7 +245,7 @@ class SourceJobC(ctypes.Structure):
 
 
 lib.kb200_dense_gguf_source_batch.argtypes = [vp, vp, ctypes.POINTER(SourceJobC), ctypes.c_size_t, c_u64,
-                                              ctypes.POINTER(c_int), ctypes.POINTER(c_int)]
+                                              ctypes.POINTER(c_u8), ctypes.POINTER(c_int)]
 SOURCE_STAGING_HALF = 16 << 20
 
 
@@ -268,7 +268,7 @@ class SourceJob:
 
 
 def dense_gguf_source_batch(ctx, bank: Optional[WeightBank], jobs, scratch_limit: int = 0,
-                            cancel: Optional[ctypes.c_int] = None) -> int:
+                            cancel: Optional[ctypes.c_ubyte] = None) -> int:
     """Run the jobs (kb200_dense_gguf_source_batch); returns the ProjectionResult code."""
     keep = []
     arr = (SourceJobC * len(jobs))()

@@ -74,7 +74,7 @@ def test_dense_gguf_batch_parity_and_errors(kb, oracle, cuda):
             ctx.dense_gguf_batch([alias])
         assert e.value.status == kb.ALIAS
         with pytest.raises(kb.KadanError) as e:
-            ctx.dense_gguf_batch([j0], cancel=ctypes.c_int(1))
+            ctx.dense_gguf_batch([j0], cancel=ctypes.c_ubyte(1))
         assert e.value.status == kb.CANCELLED
         bad = kb.HostJob(j0.weights, j0.input, j0.output, j0.row_bytes, 100, j0.out, 1, j0.encoding, 0)
         with pytest.raises(kb.Unsupported):
@@ -224,7 +224,7 @@ def test_source_batch_failures_keep_nothing(kb, oracle, cuda):
         second = WeightKey(job.identity, 3855 * 128, 3855 * 128, 34)
         assert bank.find(second) is None
         # Cancellation raised while a source is read.
-        cancel = ctypes.c_int(0)
+        cancel = ctypes.c_ubyte(0)
 
         def cancelling(first, n):
             cancel.value = 1

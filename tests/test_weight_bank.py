@@ -35,7 +35,7 @@ class Fake:
         self.fail = set()
         self.oom = False
         self.synchronized = False
-        self.cancel = None  # a ctypes.c_int the copies set, if given
+        self.cancel = None  # a ctypes.c_ubyte the copies set, if given
         self.on_copy = None
         self.on_sync = None
         self.breaches = []
@@ -223,7 +223,7 @@ def test_cancel_between_pieces_rolls_back(wb):
     bank = wb.WeightBank(4 * PIECE, gpu)
     k = key(wb, count=(2 * PIECE + 32) // 4, width=4)
     scratch, addr = buffer(k.count * k.width)
-    cancel = ctypes.c_int(0)
+    cancel = ctypes.c_ubyte(0)
     gpu.cancel = cancel
     raises(CANCELLED, lambda: bank.retain_device(k, addr, k.count * k.width, cancel))
     assert cancel.value == 1 and len(gpu.device_copies) == 1 and gpu.device_copies[0][1] == PIECE
@@ -231,7 +231,7 @@ def test_cancel_between_pieces_rolls_back(wb):
     # Cancellation observed after the last piece and the synchronise rolls back too.
     gpu = Fake()
     bank = wb.WeightBank(64, gpu)
-    cancel = ctypes.c_int(0)
+    cancel = ctypes.c_ubyte(0)
     gpu.cancel = cancel
     raises(CANCELLED, lambda: bank.retain(key(wb), addr, 32, cancel))
     assert bank.allocated() == 0 and not gpu.pointers
@@ -244,7 +244,7 @@ def test_argument_checks_precede_device_work(wb):
     bank = wb.WeightBank(64, gpu)
     k = key(wb)
     scratch, addr = buffer(32)
-    raises(CANCELLED, lambda: bank.retain_device(k, addr, 32, ctypes.c_int(1)))
+    raises(CANCELLED, lambda: bank.retain_device(k, addr, 32, ctypes.c_ubyte(1)))
     assert "weight_device_source" in raises(INVALID, lambda: bank.retain_device(k, None, 32))
     assert "weight_representation_size" in raises(INVALID, lambda: bank.retain_device(k, addr, 31))
     huge = key(wb, count=2**63, width=144)
@@ -285,7 +285,7 @@ def test_keys_separate_widths_sources_and_rows(wb):
     assert gpu.host_copies == 6 and bank.allocated() == 1024
     # Retirement is not cancellable and drops exactly that tensor's tiles.
     assert bank.release_sources([expert.source]) == 440
-    raises(CANCELLED, lambda: bank.retain(key(wb, count=2, width=4), addr, 8, ctypes.c_int(1)))
+    raises(CANCELLED, lambda: bank.retain(key(wb, count=2, width=4), addr, 8, ctypes.c_ubyte(1)))
     assert bank.find(key(wb, count=2, width=4)) == got[-1]
     raises(INVALID, lambda: bank.retain(key(wb, count=2, width=110), addr, 219))
     assert bank.allocated() == 584 and gpu.host_copies == 6
