@@ -764,6 +764,74 @@ def run_ep(args, rank, world, local_rank):
         "status": int(status.item()) if world == 1 else None, "clocks": clock}), flush=True)
 
 
+def run_source(args):
+    """--case source-batch: the config-2 stack (--layers, default 4 layers =
+    491 MB of Q4_K, more than L2) through kb200_dense_gguf_source_batch, one
+    call per dependency group with host fp32 inputs and outputs. "cold": no
+    bank, every chunk is read from its host source, staged, uploaded and
+    multiplied; "admit": the first pass into an empty bank (streams and admits
+    every chunk); "warm": every chunk is a bank hit. Host wall clock around
+    the synchronous calls; GB/s counts packed weight bytes."""
+    import numpy as np
+    import torch
+
+    import kadan_b200 as kb
+    from kadan_b200 import synth
+    from kadan_b200.weight_bank import SourceJob, WeightBank, WeightIdentity, dense_gguf_source_batch
+
+    dev = torch.device("cuda:0")
+    n_layers = args.layers or 4
+    host_in = {n: torch.randn(1, k).half().float().numpy() for n, k in (("x", HIDDEN), ("attn", HIDDEN),
+                                                                        ("h", HIDDEN), ("g", FFN))}
+    inputs = ["x", "attn", "h", "g"]
+    calls, total = [], 0
+    for layer in range(n_layers):
+        for gi, g in enumerate(GROUPS):
+            jobs = []
+            for name, out, in_ in g:
+                w = synth.device_gguf(kb.Q4_K, out, in_, layer * 16 + len(calls) * 4 + len(jobs), dev).cpu().numpy()
+                rb = w.shape[1]
+                total += w.nbytes
+                jobs.append(SourceJob(WeightIdentity(device=1, inode=1000 + layer, payload_begin=gi * 8 + len(jobs),
+                                                     payload_end=gi * 8 + len(jobs) + 1),
+                                      lambda first, n, w=w, rb=rb: w[first:first + n // rb], host_in[inputs[gi]],
+                                      np.empty((1, out), dtype=np.float32), in_, out, kb.Q4_K))
+            calls.append(jobs)
+    ctx = kb.Context(0)
+    bank = WeightBank.cuda(0, 2 * total)
+
+    def step(b):
+        for jobs in calls:
+            for j in jobs:
+                j.reads.clear()
+            dense_gguf_source_batch(ctx, b, jobs)
+
+    def timed(b, steps):
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step(b)
+        return (time.perf_counter() - t0) / steps
+
+    steps = max(1, min(args.steps, 10))
+    step(None)
+    cold = timed(None, steps)
+    admit = timed(bank, 1)
+    reads_after_admit = sum(len(j.reads) for jobs in calls for j in jobs)
+    warm = timed(bank, steps)
+    warm_reads = sum(len(j.reads) for jobs in calls for j in jobs)
+    line = {"case": "source-batch", "layers": n_layers, "calls_per_step": len(calls),
+            "weight_bytes_per_step": total, "bank_entries": bank.entries(),
+            "cold": {"ms_per_step": round(cold * 1e3, 3), "gbps": round(total / cold / 1e9, 2)},
+            "admit": {"ms_per_step": round(admit * 1e3, 3), "gbps": round(total / admit / 1e9, 2),
+                      "source_reads": reads_after_admit},
+            "warm": {"ms_per_step": round(warm * 1e3, 3), "gbps": round(total / warm / 1e9, 2),
+                     "source_reads": warm_reads},
+            "timing": "host wall clock around synchronous calls"}
+    bank.close()
+    ctx.close()
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None, help="profiling case instead of the headline workload")
@@ -793,6 +861,8 @@ def main():
         run_tp(args, rank, world, local_rank)
     elif args.case == "ep120b":
         run_ep(args, rank, world, local_rank)
+    elif args.case == "source-batch":
+        run_source(args)
     elif args.case:
         run_case(args)
     elif args.impl == "reference":

@@ -16,6 +16,8 @@ import ctypes
 from dataclasses import dataclass, field
 from typing import Iterable, Optional
 
+import numpy as np
+
 from . import CANCELLED, CUDA, OK, KadanError, check, lib
 
 c_u64, vp, c_int, c_u8 = ctypes.c_uint64, ctypes.c_void_p, ctypes.c_int, ctypes.c_ubyte
@@ -275,10 +277,10 @@ def dense_gguf_source_batch(ctx, bank: Optional[WeightBank], jobs, scratch_limit
     for i, job in enumerate(jobs):
         def read(_user, first_row, dst, nbytes, job=job):
             try:
-                data = memoryview(job.read(int(first_row), int(nbytes))).cast("B")
+                data = np.ascontiguousarray(np.frombuffer(job.read(int(first_row), int(nbytes)), dtype=np.uint8))
                 if data.nbytes != nbytes:
                     return CUDA
-                ctypes.memmove(dst, (ctypes.c_ubyte * nbytes).from_buffer_copy(data), nbytes)
+                ctypes.memmove(dst, data.ctypes.data, nbytes)
                 job.reads.append((int(first_row), int(nbytes)))
                 return OK
             except Exception:  # noqa: BLE001 - a failing source fails the call
