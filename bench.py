@@ -771,7 +771,8 @@ def run_source(args):
     bank, every chunk is read from its host source, staged, uploaded and
     multiplied; "admit": the first pass into an empty bank (streams and admits
     every chunk); "warm": every chunk is a bank hit. Host wall clock around
-    the synchronous calls; GB/s counts packed weight bytes."""
+    the synchronous calls; GB/s counts packed weight bytes. The cold pass is
+    also timed with 1, 8 and 16 source-read lanes (default 4)."""
     import numpy as np
     import torch
 
@@ -813,15 +814,20 @@ def run_source(args):
         return (time.perf_counter() - t0) / steps
 
     steps = max(1, min(args.steps, 10))
-    step(None)
-    cold = timed(None, steps)
+    cold_by_lanes = {}
+    for lanes in (1, 8, 16, 4):  # the default, 4, last: admit and warm run with it
+        ctx.set_read_lanes(lanes)
+        step(None)
+        cold_by_lanes[lanes] = timed(None, steps)
+    cold = cold_by_lanes[4]
     admit = timed(bank, 1)
     reads_after_admit = sum(len(j.reads) for jobs in calls for j in jobs)
     warm = timed(bank, steps)
     warm_reads = sum(len(j.reads) for jobs in calls for j in jobs)
     line = {"case": "source-batch", "layers": n_layers, "calls_per_step": len(calls),
             "weight_bytes_per_step": total, "bank_entries": bank.entries(),
-            "cold": {"ms_per_step": round(cold * 1e3, 3), "gbps": round(total / cold / 1e9, 2)},
+            "cold": {"ms_per_step": round(cold * 1e3, 3), "gbps": round(total / cold / 1e9, 2), "read_lanes": 4,
+                     "gbps_by_read_lanes": {k: round(total / v / 1e9, 2) for k, v in sorted(cold_by_lanes.items())}},
             "admit": {"ms_per_step": round(admit * 1e3, 3), "gbps": round(total / admit / 1e9, 2),
                       "source_reads": reads_after_admit},
             "warm": {"ms_per_step": round(warm * 1e3, 3), "gbps": round(total / warm / 1e9, 2),

@@ -172,6 +172,11 @@ KB200_API int kb200_context_create(int device, kb200_context** out);
 KB200_API void kb200_context_destroy(kb200_context* ctx);
 /* The context's cudaStream_t. */
 KB200_API void* kb200_context_stream(kb200_context* ctx);
+/* Host threads that read packed-row sources in kb200_dense_gguf_source_batch,
+ * the caller included (1..64; default 4, the reference's PackedReadTeam of
+ * three workers and the caller, IW/include/kadan/packed_read_team.hpp:22-275).
+ * Sources may then run concurrently on disjoint rows. */
+KB200_API int kb200_context_set_read_lanes(kb200_context* ctx, int lanes);
 
 /* Device-resident packed rows (the weight bank the reference keeps per
  * device, IW/include/kadan/device_weights.hpp:38): a synchronous upload of

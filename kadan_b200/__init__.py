@@ -144,6 +144,7 @@ def _load() -> ctypes.CDLL:
     lib.kb200_context_destroy.restype = None
     lib.kb200_context_stream.argtypes = [vp]
     lib.kb200_context_stream.restype = vp
+    lib.kb200_context_set_read_lanes.argtypes = [vp, c_int]
     lib.kb200_weights_upload.argtypes = [vp, vp, c_size, ctypes.POINTER(vp)]
     lib.kb200_weights_free.argtypes = [vp, vp]
     lib.kb200_dense_gguf_batch.argtypes = [vp, ctypes.POINTER(HostJob), c_size, ctypes.POINTER(ctypes.c_ubyte),
@@ -287,6 +288,10 @@ class Context:
     @property
     def stream_ptr(self) -> int:
         return int(lib.kb200_context_stream(self.handle))
+
+    def set_read_lanes(self, lanes: int) -> None:
+        """Host threads (caller included) that read packed-row sources."""
+        check(lib.kb200_context_set_read_lanes(self.handle, lanes))
 
     def upload(self, host_bytes) -> int:
         """Copy a host numpy array into a new device allocation; returns its address."""

@@ -13,6 +13,7 @@
 
 #include "gguf_formats.cuh"
 #include "kb200_host.hpp"
+#include "read_team.hpp"
 
 struct kb200_context {
     int device = 0;
@@ -22,6 +23,8 @@ struct kb200_context {
     void* pinned = nullptr;
     size_t pinned_bytes = 0;
     cudaEvent_t staged[2] = {nullptr, nullptr};  // source batch: staging half done
+    int read_lanes = 4;                           // source reads: 3 workers + the caller
+    kb200::ReadTeam* team = nullptr;              // created by the first source batch
 };
 
 namespace kb200 {
@@ -152,12 +155,24 @@ void kb200_context_destroy(kb200_context* c) {
     for (cudaEvent_t e : c->staged)
         if (e)
             cudaEventDestroy(e);
+    delete c->team;
     cudaStreamDestroy(c->stream);
     delete c;
 }
 
 void* kb200_context_stream(kb200_context* c) {
     return c ? static_cast<void*>(c->stream) : nullptr;
+}
+
+int kb200_context_set_read_lanes(kb200_context* c, int lanes) {
+    if (!c || lanes < 1 || lanes > 64)
+        return fail(KB200_INVALID, "read lanes must be 1..64");
+    if (c->team && c->team->lanes() != lanes) {
+        delete c->team;
+        c->team = nullptr;
+    }
+    c->read_lanes = lanes;
+    return KB200_OK;
 }
 
 int kb200_weights_upload(kb200_context* c, const void* host, size_t bytes, void** device) {
@@ -438,6 +453,14 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
         }
         return KB200_OK;
     };
+    if (!groups.empty() && !c->team) {
+        try {
+            c->team = new ReadTeam(c->read_lanes);
+        } catch (...) {
+            return abandon(fail(KB200_NO_MEMORY, "read team threads"));
+        }
+    }
+    std::vector<ReadItem> reads;
     for (size_t g = 0; g < groups.size(); ++g) {
         const size_t half = g % 2;
         if (g >= 2)
@@ -447,13 +470,16 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
             return abandon(fail(KB200_CANCELLED, "cancelled before a streamed group"));
         uint8_t* staged = host_stage + half * kHalf;
         std::vector<kb200_gemv_job> launch;
+        reads.clear();
         for (size_t k = groups[g].begin; k < groups[g].end; ++k) {
             const Chunk& m = misses[k];
             const auto& job = jobs[m.job];
-            if (const int s = job.source(job.source_user, m.first_col, staged + m.offset, m.bytes))
-                return abandon(fail(s, "packed-row source failed"));
+            split_read(reads, job.source, job.source_user, m.first_col, m.cols, m.row_bytes, staged + m.offset,
+                       c->read_lanes);
             launch.push_back(device_job(m, dev_stage + half * kHalf + m.offset, dev_status + half));
         }
+        if (const int s = c->team->run(reads))
+            return abandon(fail(s, "packed-row source failed"));
         cudaError_t e = cudaMemcpyAsync(dev_stage + half * kHalf, staged, groups[g].used, cudaMemcpyHostToDevice,
                                         c->stream);
         if (e == cudaSuccess)

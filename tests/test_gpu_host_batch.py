@@ -135,6 +135,18 @@ def source_jobs(kb, oracle, specs):
     return jobs, refs
 
 
+def rows_read(job):
+    """How many times each packed row of the job was read from its source."""
+    import kadan_b200 as kb
+
+    rb = job.in_ * 4 if job.encoding == kb.F32 else kb.row_bytes(job.encoding, job.in_)
+    counts = np.zeros(job.out, dtype=np.int64)
+    for first, n in job.reads:
+        assert n % rb == 0
+        counts[first:first + n // rb] += 1
+    return counts
+
+
 # Q8_0 4096 x 8192: 4352-byte rows, chunks of 3855 columns (three chunks, each
 # nearly a whole staging half: three groups over both halves); Q4_K 4096 x
 # 14336: two chunks; Q6_K one chunk; F32 rows.
@@ -151,8 +163,10 @@ def test_source_batch_streams_then_hits(kb, oracle, cuda):
         assert dense_gguf_source_batch(ctx, bank, jobs) == kb.RESULT_UNVALIDATED
         for job, ref in zip(jobs, refs):
             assert rel_err(job.y, ref) < TOL
-        assert [len(j.reads) for j in jobs] == [3, 2, 1, 1]
-        assert [r[0] for r in jobs[0].reads] == [0, 3855, 7710]
+        # Every packed row is read exactly once; with the default four read
+        # lanes a chunk of 2 MiB or more is read in four row runs.
+        assert all((rows_read(j) == 1).all() for j in jobs)
+        assert [len(j.reads) for j in jobs] == [12, 8, 4, 1]
         total = sum(j.y.shape[1] * (j.in_ * 4 if j.encoding == kb.F32 else kb.row_bytes(j.encoding, j.in_))
                     for j in jobs)
         assert bank.entries() == 7 and bank.allocated() == total
@@ -184,7 +198,7 @@ def test_source_batch_without_retention(kb, oracle, cuda):
             dense_gguf_source_batch(ctx, bank, jobs)
             for job, ref in zip(jobs, refs):
                 assert rel_err(job.y, ref) < TOL
-            assert [len(j.reads) for j in jobs] == [3, 2]
+            assert all((rows_read(j) == 1).all() for j in jobs)
         # Q8_0 chunks 1 (16.8 MB) and 3 (2.1 MB) fit the envelope, chunk 2 is
         # refused; the Q4_K job keeps nothing.
         assert small.entries() == 2 and small.allocated() == (3855 + 482) * 4352
@@ -192,7 +206,9 @@ def test_source_batch_without_retention(kb, oracle, cuda):
         for j in jobs:
             j.reads.clear()
         dense_gguf_source_batch(ctx, small, jobs)
-        assert [len(j.reads) for j in jobs] == [1, 2] and jobs[0].reads[0][0] == 3855
+        q8 = rows_read(jobs[0])
+        assert (q8[3855:7710] == 1).all() and q8[:3855].sum() == 0 and q8[7710:].sum() == 0
+        assert (rows_read(jobs[1]) == 1).all()
         for job, ref in zip(jobs, refs):
             assert rel_err(job.y, ref) < TOL
     finally:
@@ -240,4 +256,28 @@ def test_source_batch_failures_keep_nothing(kb, oracle, cuda):
             dense_gguf_source_batch(ctx, None, jobs)
     finally:
         bank.close()
+        ctx.close()
+
+
+def test_source_batch_read_lanes(kb, oracle, cuda):
+    from kadan_b200.weight_bank import dense_gguf_source_batch
+
+    jobs, refs = source_jobs(kb, oracle, [SPECS[0]])
+    job = jobs[0]
+    ctx = kb.Context(0)
+    try:
+        for bad in (0, 65):
+            with pytest.raises(kb.KadanError) as e:
+                ctx.set_read_lanes(bad)
+            assert e.value.status == kb.INVALID
+        for lanes, pieces in ((1, 3), (8, 24), (4, 12)):
+            ctx.set_read_lanes(lanes)
+            job.reads.clear()
+            job.y[:] = np.nan
+            dense_gguf_source_batch(ctx, None, jobs)
+            assert rel_err(job.y, refs[0]) < TOL
+            assert len(job.reads) == pieces and (rows_read(job) == 1).all()
+            if lanes == 1:
+                assert [r[0] for r in job.reads] == [0, 3855, 7710]
+    finally:
         ctx.close()
