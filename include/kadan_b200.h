@@ -40,7 +40,8 @@ typedef enum kb200_status {
     KB200_CANCELLED = 7,         /* "h3_cuda_cancelled" */
     KB200_TIMEOUT = 8,           /* a bounded device-side wait ran out */
     KB200_NO_MEMORY = 9,
-    KB200_QUARANTINED = 10       /* "weight_cleanup_unconfirmed": a weight bank's cleanup failed */
+    KB200_QUARANTINED = 10,      /* "weight_cleanup_unconfirmed": a weight bank's cleanup failed */
+    KB200_IO = 11                /* a checkpoint file could not be opened or read */
 } kb200_status;
 
 /* Weight encodings: the numbering of kadan::gguf::Encoding
@@ -571,6 +572,73 @@ typedef struct kb200_source_job {
 KB200_API int kb200_dense_gguf_source_batch(kb200_context* ctx, kb200_bank* bank, const kb200_source_job* jobs,
                                             size_t count, uint64_t scratch_limit, const volatile uint8_t* cancel,
                                             int* result);
+
+/* ---------------------------------------------------------------------------
+ * GGUF checkpoint reader: kadan::checkpoint::GgufCheckpoint
+ * (IW/include/kadan/gguf_checkpoint.hpp:53-103, IW/src/weights/gguf_checkpoint.cpp).
+ * `root` is a directory holding one unsplit GGUF v3 file or a numbered split
+ * set (<prefix>-00001-of-0000N.gguf ...). Opening reads bounded metadata only
+ * and accepts what the reference accepts: F32 tensors and every
+ * kadan::gguf::Encoding, ranks 1-3, tensors laid out contiguously at the
+ * file's alignment. Failures return KB200_INVALID (or KB200_IO for open/read
+ * errors, KB200_CANCELLED) with the reference's message ("gguf_version",
+ * "gguf_missing_tensor", "gguf_row_range", "gguf_checkpoint_changed", ...). */
+typedef struct kb200_gguf kb200_gguf;
+
+typedef struct kb200_gguf_tensor {
+    uint64_t shape[3];  /* ggml order: values per row, rows, experts; absent dimensions are 1 */
+    uint32_t rank;
+    uint32_t ggml_type;
+    int32_t encoding;   /* kb200_encoding, KB200_F32 for F32 */
+    uint32_t file;      /* index of the split file holding it */
+    uint64_t bytes;     /* all rows of all experts */
+    uint64_t row_bytes;
+    uint64_t offset;    /* absolute byte offset of the payload in its file */
+} kb200_gguf_tensor;
+
+KB200_API int kb200_gguf_open(const char* root, const volatile uint8_t* cancel, kb200_gguf** out);
+KB200_API void kb200_gguf_close(kb200_gguf* file);
+KB200_API size_t kb200_gguf_tensor_count(const kb200_gguf* file);
+/* Tensors in name order; *name stays valid until kb200_gguf_close. */
+KB200_API int kb200_gguf_tensor_at(const kb200_gguf* file, size_t index, kb200_gguf_tensor* info, const char** name);
+KB200_API int kb200_gguf_find_tensor(const kb200_gguf* file, const char* name, kb200_gguf_tensor* info);
+/* GgufCheckpoint::identity: the file's identity and the payload interval of
+ * one expert of the tensor (expert 0 for ordinary matrices). */
+KB200_API int kb200_gguf_identity(const kb200_gguf* file, const char* name, uint64_t expert,
+                                  kb200_weight_identity* identity);
+/* "gguf_checkpoint_changed" when a file's size, mtime or ctime moved since opening. */
+KB200_API int kb200_gguf_check_unchanged(const kb200_gguf* file);
+/* GgufCheckpoint::read_packed_rows: `bytes` (whole rows) of expert `expert`
+ * from row `first_row`, copied without decoding, in 1 MiB preads with the
+ * cancel byte polled before each. Safe to call concurrently on disjoint outputs. */
+KB200_API int kb200_gguf_read_packed_rows(const kb200_gguf* file, const char* name, uint64_t expert,
+                                          uint64_t first_row, void* output, uint64_t bytes,
+                                          const volatile uint8_t* cancel);
+/* Metadata of the first file (GgufCheckpoint::has / integer / number /
+ * boolean / string / integers / numbers). `integers` and `numbers` copy at
+ * most `capacity` values and report the array's length in *count. */
+KB200_API int kb200_gguf_has(const kb200_gguf* file, const char* key);
+KB200_API int kb200_gguf_integer(const kb200_gguf* file, const char* key, uint64_t* value);
+KB200_API int kb200_gguf_number(const kb200_gguf* file, const char* key, double* value);
+KB200_API int kb200_gguf_boolean(const kb200_gguf* file, const char* key, int* value);
+KB200_API int kb200_gguf_string(const kb200_gguf* file, const char* key, const char** value, size_t* length);
+KB200_API int kb200_gguf_integers(const kb200_gguf* file, const char* key, int64_t* values, size_t capacity,
+                                  size_t* count);
+KB200_API int kb200_gguf_numbers(const kb200_gguf* file, const char* key, double* values, size_t capacity,
+                                 size_t* count);
+
+/* One tensor (and expert) of an open checkpoint as a kb200_row_source:
+ * bind it, then pass kb200_gguf_rows_source as a source job's `source` and
+ * the bound struct as its `source_user` (rows are whole packed rows of that
+ * expert). The struct must outlive the calls; the file must stay open. */
+typedef struct kb200_gguf_rows {
+    const kb200_gguf* file;
+    uint64_t tensor;
+    uint64_t expert;
+} kb200_gguf_rows;
+
+KB200_API int kb200_gguf_rows_bind(const kb200_gguf* file, const char* name, uint64_t expert, kb200_gguf_rows* rows);
+KB200_API int kb200_gguf_rows_source(void* rows, uint64_t first_row, void* dst, uint64_t bytes);
 
 #ifdef __cplusplus
 }

@@ -75,6 +75,7 @@ const char* kb200_status_name(int status) {
     case KB200_TIMEOUT: return "kb200_device_wait_timeout";
     case KB200_NO_MEMORY: return "h3_cuda_projection_scratch";
     case KB200_QUARANTINED: return "weight_cleanup_unconfirmed";
+    case KB200_IO: return "gguf_io";
     default: return "kb200_unknown_status";
     }
 }

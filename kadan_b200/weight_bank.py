@@ -255,7 +255,9 @@ SOURCE_STAGING_HALF = 16 << 20
 class SourceJob:
     """DenseCompute::GgufBatchJob with its GgufWeightSource: `read(first_row,
     nbytes)` returns `nbytes` bytes of whole packed rows from `first_row`
-    (anything exposing the buffer protocol). x: float32 numpy [rows, in];
+    (anything exposing the buffer protocol), or `read` is a native source
+    from gguf_file.GgufCheckpoint.rows(...) (read by the C library with no
+    Python call; `reads` then stays empty). x: float32 numpy [rows, in];
     y: float32 numpy [rows, out], written."""
 
     identity: WeightIdentity
@@ -272,6 +274,8 @@ class SourceJob:
 def dense_gguf_source_batch(ctx, bank: Optional[WeightBank], jobs, scratch_limit: int = 0,
                             cancel: Optional[ctypes.c_ubyte] = None) -> int:
     """Run the jobs (kb200_dense_gguf_source_batch); returns the ProjectionResult code."""
+    from .gguf_file import ROWS_SOURCE_ADDRESS, GgufRows
+
     keep = []
     arr = (SourceJobC * len(jobs))()
     for i, job in enumerate(jobs):
@@ -287,10 +291,13 @@ def dense_gguf_source_batch(ctx, bank: Optional[WeightBank], jobs, scratch_limit
                 return CUDA
 
         ident = job.identity.c()
-        cb = _ROW_SOURCE(read)
-        keep += [ident, cb]
+        if isinstance(job.read, GgufRows):
+            cb, user = _ROW_SOURCE(ROWS_SOURCE_ADDRESS), job.read.user
+        else:
+            cb, user = _ROW_SOURCE(read), None
+        keep += [ident, cb, job.read]
         rows = job.x.size // job.in_
-        arr[i] = SourceJobC(ctypes.pointer(ident), cb, None, job.x.ctypes.data, job.y.ctypes.data, job.in_, job.out,
+        arr[i] = SourceJobC(ctypes.pointer(ident), cb, user, job.x.ctypes.data, job.y.ctypes.data, job.in_, job.out,
                             rows, job.encoding, int(job.retain_misses))
     result = c_int(0)
     check(lib.kb200_dense_gguf_source_batch(ctx.handle, None if bank is None else bank._h, arr, len(jobs),

@@ -174,7 +174,82 @@ class Reference:
         L.ref_gguf_batch_partition.argtypes = [ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int,
                                                ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.c_size_t,
                                                ctypes.c_uint64, ctypes.POINTER(ctypes.c_size_t)]
+        vp, u64p = ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)
+        L.ref_gguf_checkpoint_open.restype = vp
+        L.ref_gguf_checkpoint_open.argtypes = [ctypes.c_char_p]
+        L.ref_gguf_checkpoint_close.argtypes = [vp]
+        L.ref_gguf_checkpoint_tensor_count.restype = ctypes.c_size_t
+        L.ref_gguf_checkpoint_tensor_count.argtypes = [vp]
+        L.ref_gguf_checkpoint_tensor.argtypes = [vp, ctypes.c_char_p, u64p]
+        L.ref_gguf_checkpoint_tensor_name.restype = ctypes.c_char_p
+        L.ref_gguf_checkpoint_tensor_name.argtypes = [vp, ctypes.c_size_t]
+        L.ref_gguf_checkpoint_identity.argtypes = [vp, ctypes.c_char_p, ctypes.c_uint64, u64p]
+        L.ref_gguf_checkpoint_read_packed_rows.argtypes = [vp, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_uint64,
+                                                           vp, ctypes.c_size_t]
+        L.ref_gguf_checkpoint_check_unchanged.argtypes = [vp]
+        L.ref_gguf_checkpoint_integer.argtypes = [vp, ctypes.c_char_p, u64p]
+        L.ref_gguf_checkpoint_number.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]
+        L.ref_gguf_checkpoint_boolean.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)]
+        L.ref_gguf_checkpoint_string.restype = ctypes.c_int64
+        L.ref_gguf_checkpoint_string.argtypes = [vp, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]
+        L.ref_gguf_checkpoint_has.argtypes = [vp, ctypes.c_char_p]
         self.L = L
+
+    # -- kadan::checkpoint::GgufCheckpoint (IW/src/weights/gguf_checkpoint.cpp)
+    def gguf_open(self, root: str):
+        """A checkpoint handle, or the reference's exception text (str)."""
+        h = self.L.ref_gguf_checkpoint_open(str(root).encode())
+        return h if h else self.error()
+
+    def gguf_close(self, h) -> None:
+        self.L.ref_gguf_checkpoint_close(h)
+
+    def gguf_tensors(self, h) -> dict:
+        """name -> (shape[3], rank, ggml type, bytes), in the reader's order."""
+        out = {}
+        for i in range(int(self.L.ref_gguf_checkpoint_tensor_count(h))):
+            name = self.L.ref_gguf_checkpoint_tensor_name(h, i)
+            info = (ctypes.c_uint64 * 6)()
+            if self.L.ref_gguf_checkpoint_tensor(h, name, info):
+                raise RuntimeError(self.error())
+            out[name.decode()] = (tuple(int(v) for v in info[:3]), int(info[3]), int(info[4]), int(info[5]))
+        return out
+
+    def gguf_identity(self, h, name: str, expert: int = 0):
+        ident = (ctypes.c_uint64 * 9)()
+        if self.L.ref_gguf_checkpoint_identity(h, name.encode(), expert, ident):
+            return self.error()
+        return tuple(int(v) for v in ident)
+
+    def gguf_read_packed_rows(self, h, name: str, expert: int, first_row: int, nbytes: int):
+        buf = np.zeros(nbytes, dtype=np.uint8)
+        if self.L.ref_gguf_checkpoint_read_packed_rows(h, name.encode(), expert, first_row,
+                                                       buf.ctypes.data if nbytes else None, nbytes):
+            return self.error()
+        return buf
+
+    def gguf_check_unchanged(self, h):
+        return None if self.L.ref_gguf_checkpoint_check_unchanged(h) == 0 else self.error()
+
+    def gguf_integer(self, h, key: str):
+        v = ctypes.c_uint64()
+        return self.error() if self.L.ref_gguf_checkpoint_integer(h, key.encode(), ctypes.byref(v)) else int(v.value)
+
+    def gguf_number(self, h, key: str):
+        v = ctypes.c_double()
+        return self.error() if self.L.ref_gguf_checkpoint_number(h, key.encode(), ctypes.byref(v)) else v.value
+
+    def gguf_boolean(self, h, key: str):
+        v = ctypes.c_int()
+        return self.error() if self.L.ref_gguf_checkpoint_boolean(h, key.encode(), ctypes.byref(v)) else bool(v.value)
+
+    def gguf_string(self, h, key: str):
+        buf = ctypes.create_string_buffer(1 << 20)
+        n = self.L.ref_gguf_checkpoint_string(h, key.encode(), buf, len(buf))
+        return self.error() if n < 0 else buf.raw[:n].decode()
+
+    def gguf_has(self, h, key: str) -> bool:
+        return bool(self.L.ref_gguf_checkpoint_has(h, key.encode()))
 
     def error(self) -> str:
         return self.L.ref_last_error().decode(errors="replace")

@@ -8,6 +8,7 @@
 //   kadan::quantization::decode_rows     IW/src/weights/quantization.cpp:193-205
 //   kadan::quantization::matvec          IW/src/weights/quantization.cpp:208-247
 //   kadan::text::CpuMatvec               IW/src/models/text/cpu_matvec.cpp:18-66
+//   kadan::checkpoint::GgufCheckpoint    IW/src/weights/gguf_checkpoint.cpp:441-674
 // (IW = services/hikari/inference_worker). The 64-column work units of
 // ref_cpu_matvec_parallel follow GgufWeights::project's host split
 // (IW/src/models/text/gguf_weights.cpp:400-446).
@@ -21,6 +22,7 @@
 
 #include "cpu_matvec.hpp"
 #include "kadan/gguf_batch_partition.hpp"
+#include "kadan/gguf_checkpoint.hpp"
 #include "kadan/gguf_quantization.hpp"
 #include "kadan/quantization.hpp"
 #include <ggml-cpu.h>
@@ -261,5 +263,126 @@ int ref_gguf_batch_partition(size_t in, size_t out, int encoding, const uint64_t
     } catch (const std::exception& e) {
         return fail(e);
     }
+}
+
+// GGUF checkpoint reader (IW/include/kadan/gguf_checkpoint.hpp:53-103).
+void* ref_gguf_checkpoint_open(const char* root) {
+    try {
+        static const std::atomic_bool never{false};
+        return new kadan::checkpoint::GgufCheckpoint(root, never);
+    } catch (const std::exception& e) {
+        fail(e);
+        return nullptr;
+    }
+}
+
+void ref_gguf_checkpoint_close(void* checkpoint) {
+    delete static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint);
+}
+
+size_t ref_gguf_checkpoint_tensor_count(void* checkpoint) {
+    return static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->tensor_count();
+}
+
+// info: shape[3], rank, type, bytes.
+int ref_gguf_checkpoint_tensor(void* checkpoint, const char* name, uint64_t* info) {
+    try {
+        const auto& t = static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->tensor(name);
+        info[0] = t.shape[0], info[1] = t.shape[1], info[2] = t.shape[2];
+        info[3] = t.rank, info[4] = t.type, info[5] = t.bytes;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+const char* ref_gguf_checkpoint_tensor_name(void* checkpoint, size_t index) {
+    try {
+        return static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->tensor_at(index).name.c_str();
+    } catch (const std::exception& e) {
+        fail(e);
+        return nullptr;
+    }
+}
+
+// identity: the nine WeightIdentity fields in declaration order.
+int ref_gguf_checkpoint_identity(void* checkpoint, const char* name, uint64_t expert, uint64_t* identity) {
+    try {
+        const auto id = static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->identity(name, expert);
+        const uint64_t v[9] = {id.device, id.inode, id.file_size, id.modified_seconds, id.modified_nanoseconds,
+                               id.changed_seconds, id.changed_nanoseconds, id.payload_begin, id.payload_end};
+        std::memcpy(identity, v, sizeof(v));
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_gguf_checkpoint_read_packed_rows(void* checkpoint, const char* name, uint64_t expert, uint64_t first_row,
+                                         void* output, size_t bytes) {
+    try {
+        static const std::atomic_bool never{false};
+        static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->read_packed_rows(
+            name, expert, first_row, std::span<std::byte>(static_cast<std::byte*>(output), bytes), never);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_gguf_checkpoint_check_unchanged(void* checkpoint) {
+    try {
+        static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->check_unchanged();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_gguf_checkpoint_integer(void* checkpoint, const char* key, uint64_t* value) {
+    try {
+        *value = static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->integer(key);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_gguf_checkpoint_number(void* checkpoint, const char* key, double* value) {
+    try {
+        *value = static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->number(key);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_gguf_checkpoint_boolean(void* checkpoint, const char* key, int* value) {
+    try {
+        *value = static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->boolean(key) ? 1 : 0;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// Copies the string (NUL-terminated, truncated to capacity - 1); returns its full length or -1.
+int64_t ref_gguf_checkpoint_string(void* checkpoint, const char* key, char* buffer, size_t capacity) {
+    try {
+        const auto s = static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->string(key);
+        if (capacity) {
+            const size_t n = s.size() < capacity - 1 ? s.size() : capacity - 1;
+            std::memcpy(buffer, s.data(), n);
+            buffer[n] = '\0';
+        }
+        return int64_t(s.size());
+    } catch (const std::exception& e) {
+        fail(e);
+        return -1;
+    }
+}
+
+int ref_gguf_checkpoint_has(void* checkpoint, const char* key) {
+    return static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->has(key) ? 1 : 0;
 }
 }  // extern "C"
