@@ -640,6 +640,64 @@ typedef struct kb200_gguf_rows {
 KB200_API int kb200_gguf_rows_bind(const kb200_gguf* file, const char* name, uint64_t expert, kb200_gguf_rows* rows);
 KB200_API int kb200_gguf_rows_source(void* rows, uint64_t first_row, void* dst, uint64_t bytes);
 
+/* ---------------------------------------------------------------------------
+ * Safetensors shard reader: kadan::checkpoint::Shard
+ * (IW/include/kadan/checkpoint.hpp:91-178, IW/src/weights/checkpoint.cpp:449-730)
+ * for the gpt-oss MXFP4 expert tensors. `name` is one file basename in the
+ * directory `root`. The header must tile the payload exactly; failures return
+ * KB200_INVALID (KB200_IO for open/read errors) with the reference's message
+ * ("header_size", "json_syntax", "tensor_gap_or_overlap", "missing_tensor",
+ * "mxfp4_expert_shape", "invalid_block_scale", "checkpoint_changed", ...). */
+typedef struct kb200_shard kb200_shard;
+
+/* checkpoint::Dtype, in its order. */
+#define KB200_DTYPE_U8 0
+#define KB200_DTYPE_F8_E4M3 1
+#define KB200_DTYPE_F32 2
+#define KB200_DTYPE_BF16 3
+#define KB200_DTYPE_F16 4
+#define KB200_DTYPE_I8 5
+#define KB200_DTYPE_U32 6
+
+/* checkpoint::Limits; a NULL pointer means the reference's defaults
+ * (16 MiB of header, 65536 tensors, 512-byte metadata values). */
+typedef struct kb200_shard_limits {
+    uint64_t header_bytes, tensors, metadata_value_bytes;
+} kb200_shard_limits;
+
+typedef struct kb200_shard_tensor {
+    uint64_t shape[8];
+    uint32_t rank;
+    int32_t dtype;   /* KB200_DTYPE_* */
+    uint64_t bytes;
+    uint64_t offset; /* absolute byte offset of the payload in the file */
+} kb200_shard_tensor;
+
+KB200_API int kb200_shard_open(const char* root, const char* name, const kb200_shard_limits* limits,
+                               kb200_shard** out);
+KB200_API void kb200_shard_close(kb200_shard* shard);
+KB200_API size_t kb200_shard_tensor_count(const kb200_shard* shard);
+/* Tensors in name order; *name stays valid until kb200_shard_close. */
+KB200_API int kb200_shard_tensor_at(const kb200_shard* shard, size_t index, kb200_shard_tensor* info,
+                                    const char** name);
+KB200_API int kb200_shard_find_tensor(const kb200_shard* shard, const char* name, kb200_shard_tensor* info);
+KB200_API int kb200_shard_identity(const kb200_shard* shard, const char* name, kb200_weight_identity* identity);
+KB200_API int kb200_shard_check_unchanged(const kb200_shard* shard);
+/* Shard::read_tensor: `bytes` bytes of the tensor from byte `offset`. */
+KB200_API int kb200_shard_read_tensor(const kb200_shard* shard, const char* name, uint64_t offset, void* output,
+                                      uint64_t bytes);
+/* Shard::load_mxfp4_expert_rows: rows [first, first + count) of one expert
+ * of <prefix>_blocks (U8 [experts, rows, groups, 16]) and <prefix>_scales
+ * (U8 [experts, rows, groups]), still packed: `weights` receives
+ * count * groups * 16 code bytes and `scales` count * groups E8M0 bytes, the
+ * per-expert layout kb200_moe_weights takes. *columns = groups * 32. The
+ * reads are checked against payload_budget (code + scale bytes) first; after a
+ * failure ("invalid_block_scale" included) the outputs must be discarded. */
+KB200_API int kb200_shard_load_mxfp4_expert_rows(const kb200_shard* shard, const char* prefix, uint64_t expert,
+                                                 uint64_t first, uint64_t count, uint64_t payload_budget,
+                                                 void* weights, uint64_t weights_capacity, void* scales,
+                                                 uint64_t scales_capacity, uint64_t* columns);
+
 #ifdef __cplusplus
 }
 #endif

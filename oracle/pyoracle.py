@@ -193,7 +193,65 @@ class Reference:
         L.ref_gguf_checkpoint_string.restype = ctypes.c_int64
         L.ref_gguf_checkpoint_string.argtypes = [vp, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]
         L.ref_gguf_checkpoint_has.argtypes = [vp, ctypes.c_char_p]
+        L.ref_shard_open.restype = vp
+        L.ref_shard_open.argtypes = [ctypes.c_char_p, ctypes.c_char_p]
+        L.ref_shard_close.argtypes = [vp]
+        L.ref_shard_tensor_count.restype = ctypes.c_size_t
+        L.ref_shard_tensor_count.argtypes = [vp]
+        L.ref_shard_tensor_at.argtypes = [vp, ctypes.c_size_t, u64p, ctypes.POINTER(ctypes.c_void_p),
+                                          ctypes.POINTER(ctypes.c_size_t)]
+        L.ref_shard_identity.argtypes = [vp, ctypes.c_char_p, u64p]
+        L.ref_shard_read_tensor.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, vp, ctypes.c_size_t]
+        L.ref_shard_check_unchanged.argtypes = [vp]
+        L.ref_shard_load_mxfp4_expert_rows.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_size_t,
+                                                       ctypes.c_size_t, ctypes.c_size_t, vp, ctypes.c_size_t, vp,
+                                                       ctypes.c_size_t, u64p]
         self.L = L
+
+    # -- kadan::checkpoint::Shard (IW/src/weights/checkpoint.cpp)
+    def shard_open(self, root: str, name: str):
+        h = self.L.ref_shard_open(str(root).encode(), name.encode())
+        return h if h else self.error()
+
+    def shard_close(self, h) -> None:
+        self.L.ref_shard_close(h)
+
+    def shard_tensors(self, h) -> dict:
+        """name -> (dtype index, rank, bytes, shape tuple), in the reader's order."""
+        out = {}
+        for i in range(int(self.L.ref_shard_tensor_count(h))):
+            info, name, n = (ctypes.c_uint64 * 11)(), ctypes.c_void_p(), ctypes.c_size_t()
+            if self.L.ref_shard_tensor_at(h, i, info, ctypes.byref(name), ctypes.byref(n)):
+                raise RuntimeError(self.error())
+            key = ctypes.string_at(name, n.value).decode()
+            rank = int(info[1])
+            out[key] = (int(info[0]), rank, int(info[2]), tuple(int(v) for v in info[3:3 + rank]))
+        return out
+
+    def shard_identity(self, h, name: str):
+        ident = (ctypes.c_uint64 * 9)()
+        if self.L.ref_shard_identity(h, name.encode(), ident):
+            return self.error()
+        return tuple(int(v) for v in ident)
+
+    def shard_read_tensor(self, h, name: str, offset: int, nbytes: int):
+        buf = np.zeros(max(1, nbytes), dtype=np.uint8)
+        if self.L.ref_shard_read_tensor(h, name.encode(), offset, buf.ctypes.data, nbytes):
+            return self.error()
+        return buf[:nbytes]
+
+    def shard_check_unchanged(self, h):
+        return None if self.L.ref_shard_check_unchanged(h) == 0 else self.error()
+
+    def shard_load_mxfp4_expert_rows(self, h, prefix: str, expert: int, first: int, count: int, budget: int,
+                                     capacity: int = 1 << 24):
+        """(weights uint8, scales uint8, rows, columns), or the reference's exception text."""
+        w, sc, shape = np.zeros(capacity, np.uint8), np.zeros(capacity, np.uint8), (ctypes.c_uint64 * 2)()
+        if self.L.ref_shard_load_mxfp4_expert_rows(h, prefix.encode(), expert, first, count, budget,
+                                                   w.ctypes.data, capacity, sc.ctypes.data, capacity, shape):
+            return self.error()
+        rows, cols = int(shape[0]), int(shape[1])
+        return w[:rows * cols // 2], sc[:rows * cols // 32], rows, cols
 
     # -- kadan::checkpoint::GgufCheckpoint (IW/src/weights/gguf_checkpoint.cpp)
     def gguf_open(self, root: str):

@@ -9,6 +9,7 @@
 //   kadan::quantization::matvec          IW/src/weights/quantization.cpp:208-247
 //   kadan::text::CpuMatvec               IW/src/models/text/cpu_matvec.cpp:18-66
 //   kadan::checkpoint::GgufCheckpoint    IW/src/weights/gguf_checkpoint.cpp:441-674
+//   kadan::checkpoint::Shard             IW/src/weights/checkpoint.cpp:449-730
 // (IW = services/hikari/inference_worker). The 64-column work units of
 // ref_cpu_matvec_parallel follow GgufWeights::project's host split
 // (IW/src/models/text/gguf_weights.cpp:400-446).
@@ -22,6 +23,7 @@
 
 #include "cpu_matvec.hpp"
 #include "kadan/gguf_batch_partition.hpp"
+#include "kadan/checkpoint.hpp"
 #include "kadan/gguf_checkpoint.hpp"
 #include "kadan/gguf_quantization.hpp"
 #include "kadan/quantization.hpp"
@@ -384,5 +386,90 @@ int64_t ref_gguf_checkpoint_string(void* checkpoint, const char* key, char* buff
 
 int ref_gguf_checkpoint_has(void* checkpoint, const char* key) {
     return static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->has(key) ? 1 : 0;
+}
+
+// Safetensors shard (IW/include/kadan/checkpoint.hpp:91-178), default Limits,
+// a 1 GiB metadata budget.
+void* ref_shard_open(const char* root, const char* name) {
+    try {
+        return new kadan::checkpoint::Shard(root, name, std::make_shared<kadan::checkpoint::MemoryBudget>(1ull << 30));
+    } catch (const std::exception& e) {
+        fail(e);
+        return nullptr;
+    }
+}
+
+void ref_shard_close(void* shard) {
+    delete static_cast<kadan::checkpoint::Shard*>(shard);
+}
+
+size_t ref_shard_tensor_count(void* shard) {
+    return static_cast<kadan::checkpoint::Shard*>(shard)->tensor_count();
+}
+
+// info: dtype, rank, bytes, shape[8]; *name: the tensor's name (valid while the shard lives).
+int ref_shard_tensor_at(void* shard, size_t index, uint64_t* info, const char** name, size_t* name_length) {
+    try {
+        const auto t = static_cast<kadan::checkpoint::Shard*>(shard)->tensor_at(index);
+        info[0] = uint64_t(t.dtype), info[1] = t.rank, info[2] = t.bytes;
+        for (int d = 0; d < 8; ++d)
+            info[3 + d] = t.shape[d];
+        *name = t.name.data();
+        *name_length = t.name.size();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_shard_identity(void* shard, const char* name, uint64_t* identity) {
+    try {
+        const auto id = static_cast<kadan::checkpoint::Shard*>(shard)->tensor_identity(name);
+        const uint64_t v[9] = {id.device, id.inode, id.file_size, id.modified_seconds, id.modified_nanoseconds,
+                               id.changed_seconds, id.changed_nanoseconds, id.payload_begin, id.payload_end};
+        std::memcpy(identity, v, sizeof(v));
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_shard_read_tensor(void* shard, const char* name, size_t offset, void* output, size_t bytes) {
+    try {
+        static_cast<kadan::checkpoint::Shard*>(shard)->read_tensor(
+            name, offset, std::span<uint8_t>(static_cast<uint8_t*>(output), bytes));
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_shard_check_unchanged(void* shard) {
+    try {
+        static_cast<kadan::checkpoint::Shard*>(shard)->check_unchanged();
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+// Shard::load_mxfp4_expert_rows; copies the projection's packed codes and
+// E8M0 scales out (capacities in bytes) and returns rows and columns in shape[2].
+int ref_shard_load_mxfp4_expert_rows(void* shard, const char* prefix, size_t expert, size_t first, size_t count,
+                                     size_t budget, uint8_t* weights, size_t weights_capacity, uint8_t* scales,
+                                     size_t scales_capacity, uint64_t* shape) {
+    try {
+        const auto p = static_cast<kadan::checkpoint::Shard*>(shard)->load_mxfp4_expert_rows(prefix, expert, first,
+                                                                                            count, budget);
+        const auto v = p.view();
+        if (v.weights.size() > weights_capacity || v.block_scales.size() > scales_capacity)
+            throw std::length_error("shim_capacity");
+        std::memcpy(weights, v.weights.data(), v.weights.size());
+        std::memcpy(scales, v.block_scales.data(), v.block_scales.size());
+        shape[0] = v.rows, shape[1] = v.columns;
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
 }
 }  // extern "C"
