@@ -351,6 +351,8 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
     }
     if (const int s = check_aliases(jobs, count))
         return s;
+    if (bank && bank_device(bank) >= 0 && bank_device(bank) != c->device)
+        return fail(KB200_INVALID, "the weight bank holds another device's memory");
 
     DeviceScope scope(c->device);
     // Bank lookups (h3_compute.cu:4063-4115): hits run from the bank, misses stream.

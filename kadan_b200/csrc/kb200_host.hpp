@@ -55,4 +55,8 @@ int sm_count();
 // launch gave up, its cut tiles' partial words may be left behind). Synchronous.
 void clear_gemv_fixups();
 
+// The CUDA device whose memory a weight bank holds, or -1 for a bank over
+// caller-supplied operations.
+int bank_device(const kb200_bank* bank);
+
 }  // namespace kb200

@@ -269,6 +269,14 @@ int cuda_synchronize(void* user) {
 }  // namespace
 }  // namespace kb200
 
+namespace kb200 {
+
+int bank_device(const kb200_bank* bank) {
+    return bank && bank->cuda ? bank->cuda->device : -1;
+}
+
+}  // namespace kb200
+
 using namespace kb200;
 
 extern "C" {
