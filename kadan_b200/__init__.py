@@ -7,7 +7,13 @@ device tensors:
 
     gguf_dequant(encoding, packed, count, out)      gguf_decode_kernel
     gguf_gemv_batch([GemvJob, ...])                  dense_gguf_batch's launch
-    dense_gguf_batch(jobs)                           host-span batch (sync)
+    Context.dense_gguf_batch(jobs)                   host-span batch (sync)
+    gguf_gemm(job, workspace)                        prefill projection
+    moe_forward(weights, x, logits)                  MXFP4 MoE layer
+
+and, in submodules: weight_bank (DeviceWeights and the packed-source batch),
+gguf_file (GgufCheckpoint), shard (the safetensors Shard with MXFP4 expert
+rows), tensor_parallel / expert_parallel / collectives (one process per GPU).
 
 Every call goes through libkadan_b200.so. There is no CPU or PyTorch
 fallback: if the library cannot be loaded the import fails.
