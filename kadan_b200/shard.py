@@ -135,4 +135,82 @@ class Shard:
         return weights[:count * c // 2].reshape(count, c // 2), scales[:count * c // 32].reshape(count, c // 32), c
 
 
-__all__ = ["Shard", "ShardTensor", "DTYPES"]
+def _bf16_to_f32(raw: np.ndarray) -> np.ndarray:
+    """BF16 bytes -> float32, exactly (the 16 bits become the high half)."""
+    return (raw.view("<u2").astype(np.uint32) << 16).view(np.float32)
+
+
+def _float_tensor(shard: Shard, name: str) -> np.ndarray:
+    t = shard.tensor(name)
+    raw = shard.read_tensor(name, 0, t.bytes)
+    if t.dtype == "BF16":
+        return _bf16_to_f32(raw).reshape(t.shape)
+    if t.dtype == "F32":
+        return raw.view("<f4").reshape(t.shape).copy()
+    if t.dtype == "F16":
+        return raw.view("<f2").astype(np.float32).reshape(t.shape)
+    raise ValueError(f"{name}: {t.dtype} is not a float tensor")
+
+
+@dataclass
+class MoeLayerArrays:
+    """One gpt-oss MoE layer in the layout kb200_moe_weights takes (interleaved
+    gate/up rows), for experts [first, first + count) of the layer."""
+
+    gate_up_blocks: np.ndarray  # uint8 [E, 2I, H/2]
+    gate_up_scales: np.ndarray  # uint8 [E, 2I, H/32]
+    down_blocks: np.ndarray     # uint8 [E, H, I/2]
+    down_scales: np.ndarray     # uint8 [E, H, I/32]
+    gate_up_bias: Optional[np.ndarray]  # float32 [E, 2I]
+    down_bias: Optional[np.ndarray]     # float32 [E, H]
+    router_weight: Optional[np.ndarray]  # float32 [all experts, H]
+    router_bias: Optional[np.ndarray]    # float32 [all experts]
+    hidden: int
+    inter: int
+    first: int
+    count: int
+
+
+def load_moe_layer(shard: Shard, prefix: str, first: int = 0, count: Optional[int] = None,
+                   payload_budget: int = 1 << 40) -> MoeLayerArrays:
+    """Experts [first, first + count) of the MoE layer under `prefix` (e.g.
+    "model.layers.0.mlp"): <prefix>.experts.gate_up_proj_{blocks,scales,bias},
+    <prefix>.experts.down_proj_{blocks,scales,bias} and, when present,
+    <prefix>.router.{weight,bias}. Each expert's rows are loaded in place by
+    kb200_shard_load_mxfp4_expert_rows; biases and the router are widened to
+    float32 exactly."""
+    gu, dn = prefix + ".experts.gate_up_proj", prefix + ".experts.down_proj"
+    gu_shape, dn_shape = shard.tensor(gu + "_blocks").shape, shard.tensor(dn + "_blocks").shape
+    if len(gu_shape) != 4 or len(dn_shape) != 4:
+        raise ValueError("MXFP4 expert blocks must be [experts, rows, groups, 16]")
+    experts, two_i, hidden = gu_shape[0], gu_shape[1], gu_shape[2] * 32
+    inter = dn_shape[2] * 32
+    if two_i != 2 * inter or dn_shape[:2] != (experts, hidden):
+        raise ValueError("gate/up and down expert shapes disagree")
+    count = experts - first if count is None else count
+    arrays = {}
+    for name, rows, cols in ((gu, two_i, hidden), (dn, hidden, inter)):
+        blocks = np.empty((count, rows, cols // 2), dtype=np.uint8)
+        scales = np.empty((count, rows, cols // 32), dtype=np.uint8)
+        for e in range(count):
+            shard.load_mxfp4_expert_rows(name, first + e, 0, rows, payload_budget, weights=blocks[e], scales=scales[e])
+        arrays[name] = (blocks, scales)
+
+    from . import KadanError
+
+    def optional(name, sl=None):
+        try:
+            shard.tensor(name)
+        except KadanError:  # absent
+            return None
+        v = _float_tensor(shard, name)
+        return v if sl is None else np.ascontiguousarray(v[sl])
+
+    experts_slice = slice(first, first + count)
+    return MoeLayerArrays(arrays[gu][0], arrays[gu][1], arrays[dn][0], arrays[dn][1],
+                          optional(gu + "_bias", experts_slice), optional(dn + "_bias", experts_slice),
+                          optional(prefix + ".router.weight"), optional(prefix + ".router.bias"),
+                          hidden, inter, first, count)
+
+
+__all__ = ["Shard", "ShardTensor", "DTYPES", "MoeLayerArrays", "load_moe_layer"]

@@ -159,3 +159,41 @@ def test_moe_gemv_and_gemm_paths_agree(kb, oracle, cuda, monkeypatch, T, E, H, I
     for path in ("gemv", "gemm"):
         assert rel_err(outs[path].cpu().numpy(), ref16) <= 1e-3, path
     assert rel_err(outs["gemv"].cpu().numpy(), outs["gemm"].cpu().numpy()) <= 1e-3
+
+
+def test_moe_layer_from_safetensors_shard(kb, oracle, cuda, tmp_path):
+    """A gpt-oss MoE layer written as safetensors (MXFP4 experts, BF16 biases
+    and router), loaded by kadan_b200.shard.load_moe_layer, runs through
+    kb200_moe_forward within the layer tolerances."""
+    import torch
+
+    from kadan_b200 import shard as sh
+    from kadan_b200 import synth
+    from test_shard import gpt_oss_layer_tensors, write_shard
+
+    E, H, I, K, T = 8, 256, 128, 2, 64
+    prefix = "model.layers.0.mlp"
+    tensors, _ = gpt_oss_layer_tensors(prefix, E, H, I, seed=9)
+    write_shard(tmp_path / "model.safetensors", tensors)
+    layer = sh.load_moe_layer(sh.Shard(tmp_path, "model.safetensors"), prefix)
+
+    def dev(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+    gu_w, gu_s, dn_w, dn_s = map(dev, (layer.gate_up_blocks, layer.gate_up_scales, layer.down_blocks,
+                                       layer.down_scales))
+    gu_b, dn_b = dev(layer.gate_up_bias), dev(layer.down_bias)
+    w = kb.moe_weights(gu_w, gu_s, dn_w, dn_s, hidden=H, inter=I, experts=E, top_k=K, gu_bias=gu_b, dn_bias=dn_b,
+                       activation=kb.MOE_SILU, interleaved=True)
+    x = synth.activations(T * H, seed=3, dtype="bf16").reshape(T, H)
+    logits = (x @ layer.router_weight.T + layer.router_bias).astype(np.float32)
+    xb = torch.from_numpy(x).to(cuda).to(torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = kb.moe_forward(w, xb, dev(logits), status=status)
+    torch.cuda.synchronize()
+    args = dict(hidden=H, inter=I, experts=E, top_k=K, gu_bias=layer.gate_up_bias, dn_bias=layer.down_bias,
+                activation=kb.MOE_SILU, interleaved=1)
+    ref16 = oracle.moe_forward(x, logits, layer.gate_up_blocks, layer.gate_up_scales, layer.down_blocks,
+                               layer.down_scales, round_act=2, **args)
+    assert rel_err(out.cpu().numpy(), ref16) <= 1e-3
+    assert status.item() == 0

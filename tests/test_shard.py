@@ -202,3 +202,55 @@ def test_changed_shard(sh, ref, tmp_path):
         assert outcome(lambda: ours.read_tensor("t", 0, 4)) == ref.shard_read_tensor(h, "t", 0, 4)
     finally:
         ref.shard_close(h)
+
+
+def gpt_oss_layer_tensors(prefix, E, H, I, seed):
+    """A gpt-oss MoE layer as its safetensors tensors (MXFP4 experts with BF16
+    biases and a BF16 router), and the arrays they hold."""
+    rng = np.random.default_rng(seed)
+    gu, gu_b, gu_s = mxfp4_tensors(prefix + ".experts.gate_up_proj", E, 2 * I, H // 32, seed)
+    dn, dn_b, dn_s = mxfp4_tensors(prefix + ".experts.down_proj", E, H, I // 32, seed + 1)
+
+    def bf16(shape):
+        return (rng.standard_normal(shape).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+    gu_bias, dn_bias, router_w, router_b = bf16((E, 2 * I)), bf16((E, H)), bf16((E, H)), bf16((E,))
+    tensors = gu + dn + [(prefix + ".experts.gate_up_proj_bias", "BF16", gu_bias.shape, gu_bias.tobytes()),
+                         (prefix + ".experts.down_proj_bias", "BF16", dn_bias.shape, dn_bias.tobytes()),
+                         (prefix + ".router.weight", "BF16", router_w.shape, router_w.tobytes()),
+                         (prefix + ".router.bias", "BF16", router_b.shape, router_b.tobytes())]
+    widen = lambda a: (a.astype(np.uint32) << 16).view(np.float32)  # noqa: E731
+    arrays = dict(gu_w=gu_b.reshape(E, 2 * I, H // 2), gu_s=gu_s, dn_w=dn_b.reshape(E, H, I // 2), dn_s=dn_s,
+                  gu_bias=widen(gu_bias), dn_bias=widen(dn_bias), router_w=widen(router_w), router_b=widen(router_b))
+    return tensors, arrays
+
+
+def test_load_moe_layer(sh, oracle, tmp_path):
+    E, H, I, K, T = 8, 256, 128, 2, 9
+    prefix = "model.layers.3.mlp"
+    tensors, want = gpt_oss_layer_tensors(prefix, E, H, I, seed=5)
+    write_shard(tmp_path / "model-00002-of-00003.safetensors", tensors)
+    shard = sh.Shard(tmp_path, "model-00002-of-00003.safetensors")
+    layer = sh.load_moe_layer(shard, prefix)
+    assert (layer.hidden, layer.inter, layer.first, layer.count) == (H, I, 0, E)
+    for got, key in ((layer.gate_up_blocks, "gu_w"), (layer.gate_up_scales, "gu_s"), (layer.down_blocks, "dn_w"),
+                     (layer.down_scales, "dn_s"), (layer.gate_up_bias, "gu_bias"), (layer.down_bias, "dn_bias"),
+                     (layer.router_weight, "router_w"), (layer.router_bias, "router_b")):
+        assert np.array_equal(got, want[key]), key
+    # An expert-parallel slice is the matching slice of the whole layer.
+    part = sh.load_moe_layer(shard, prefix, first=2, count=3)
+    assert np.array_equal(part.gate_up_blocks, layer.gate_up_blocks[2:5])
+    assert np.array_equal(part.down_scales, layer.down_scales[2:5])
+    assert np.array_equal(part.down_bias, layer.down_bias[2:5])
+    assert np.array_equal(part.router_weight, layer.router_weight)
+    # The loaded layer runs through the oracle exactly as the arrays it came from.
+    from kadan_b200 import synth
+
+    x = synth.activations(T * H, seed=1, dtype="bf16").reshape(T, H)
+    logits = (x @ layer.router_weight.T + layer.router_bias).astype(np.float32)
+    args = dict(hidden=H, inter=I, experts=E, top_k=K, activation=1, interleaved=1)
+    a = oracle.moe_forward(x, logits, layer.gate_up_blocks, layer.gate_up_scales, layer.down_blocks,
+                           layer.down_scales, gu_bias=layer.gate_up_bias, dn_bias=layer.down_bias, **args)
+    b = oracle.moe_forward(x, logits, want["gu_w"], want["gu_s"], want["dn_w"], want["dn_s"], gu_bias=want["gu_bias"],
+                           dn_bias=want["dn_bias"], **args)
+    assert np.array_equal(a, b)
