@@ -23,6 +23,7 @@ import argparse
 import ctypes
 import json
 import os
+import shutil
 import statistics
 import subprocess
 import sys
@@ -772,7 +773,10 @@ def run_source(args):
     multiplied; "admit": the first pass into an empty bank (streams and admits
     every chunk); "warm": every chunk is a bank hit. Host wall clock around
     the synchronous calls; GB/s counts packed weight bytes. The cold pass is
-    also timed with 1, 8 and 16 source-read lanes (default 4)."""
+    also timed with 1, 8 and 16 source-read lanes (default 4). --source
+    python reads rows through Python callbacks over host arrays; --source gguf
+    writes the stack to a GGUF file in a temporary directory and reads it
+    with the library's own packed-row source (kb200_gguf_rows_source)."""
     import numpy as np
     import torch
 
@@ -785,19 +789,38 @@ def run_source(args):
     host_in = {n: torch.randn(1, k).half().float().numpy() for n, k in (("x", HIDDEN), ("attn", HIDDEN),
                                                                         ("h", HIDDEN), ("g", FFN))}
     inputs = ["x", "attn", "h", "g"]
-    calls, total = [], 0
+    mats, total = [], 0
     for layer in range(n_layers):
         for gi, g in enumerate(GROUPS):
-            jobs = []
+            group = []
             for name, out, in_ in g:
-                w = synth.device_gguf(kb.Q4_K, out, in_, layer * 16 + len(calls) * 4 + len(jobs), dev).cpu().numpy()
-                rb = w.shape[1]
+                w = synth.device_gguf(kb.Q4_K, out, in_, layer * 16 + gi * 4 + len(group), dev).cpu().numpy()
                 total += w.nbytes
-                jobs.append(SourceJob(WeightIdentity(device=1, inode=1000 + layer, payload_begin=gi * 8 + len(jobs),
-                                                     payload_end=gi * 8 + len(jobs) + 1),
-                                      lambda first, n, w=w, rb=rb: w[first:first + n // rb], host_in[inputs[gi]],
-                                      np.empty((1, out), dtype=np.float32), in_, out, kb.Q4_K))
-            calls.append(jobs)
+                group.append((f"blk.{layer}.{name}.weight", out, in_, w))
+            mats.append((gi, group))
+    ckpt = tmpdir = None
+    if args.source == "gguf":
+        # The stack as one GGUF file on local disk, read by the library itself.
+        from kadan_b200 import gguf_write
+        from kadan_b200.gguf_file import GgufCheckpoint
+
+        tmpdir = Path(tempfile.mkdtemp(prefix="kb200_ckpt_"))
+        gguf_write.write_arrays(tmpdir / "stack.gguf", [("general.architecture", gguf_write.STRING, "llama")],
+                                [(n, [in_, out], 12, w) for _, group in mats for n, out, in_, w in group])
+        ckpt = GgufCheckpoint(tmpdir)
+    calls = []
+    for gi, group in mats:
+        jobs = []
+        for n, out, in_, w in group:
+            if ckpt is not None:
+                ident, read = ckpt.identity(n), ckpt.rows(n)
+            else:
+                ident = WeightIdentity(device=1, inode=1000 + len(calls), payload_begin=len(jobs),
+                                       payload_end=len(jobs) + 1)
+                read = (lambda first, nb, w=w, rb=w.shape[1]: w[first:first + nb // rb])
+            jobs.append(SourceJob(ident, read, host_in[inputs[gi]], np.empty((1, out), dtype=np.float32), in_, out,
+                                  kb.Q4_K))
+        calls.append(jobs)
     ctx = kb.Context(0)
     bank = WeightBank.cuda(0, 2 * total)
 
@@ -824,7 +847,7 @@ def run_source(args):
     reads_after_admit = sum(len(j.reads) for jobs in calls for j in jobs)
     warm = timed(bank, steps)
     warm_reads = sum(len(j.reads) for jobs in calls for j in jobs)
-    line = {"case": "source-batch", "layers": n_layers, "calls_per_step": len(calls),
+    line = {"case": "source-batch", "source": args.source, "layers": n_layers, "calls_per_step": len(calls),
             "weight_bytes_per_step": total, "bank_entries": bank.entries(),
             "cold": {"ms_per_step": round(cold * 1e3, 3), "gbps": round(total / cold / 1e9, 2), "read_lanes": 4,
                      "gbps_by_read_lanes": {k: round(total / v / 1e9, 2) for k, v in sorted(cold_by_lanes.items())}},
@@ -835,6 +858,9 @@ def run_source(args):
             "timing": "host wall clock around synchronous calls"}
     bank.close()
     ctx.close()
+    if ckpt is not None:
+        ckpt.close()
+        shutil.rmtree(tmpdir, ignore_errors=True)
     print(json.dumps(line), flush=True)
 
 
@@ -853,6 +879,8 @@ def main():
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
                     help="token exchange of --case ep120b")
     ap.add_argument("--layers", type=int, default=0, help="layers for --case tp70b / ep120b (default 80 / 36)")
+    ap.add_argument("--source", choices=["python", "gguf"], default="python",
+                    help="packed-row source for --case source-batch")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

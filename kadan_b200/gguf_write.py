@@ -1,7 +1,8 @@
-"""Test helper: writes GGUF v3 files from the published layout (magic "GGUF",
-u32 version, u64 tensor and key-value counts, typed key-value pairs, tensor
+"""Writes GGUF v3 files from the published layout (magic "GGUF", u32
+version, u64 tensor and key-value counts, typed key-value pairs, tensor
 descriptors, padding to the alignment, then tensor payloads each padded to
-the alignment). Overrides let a test write malformed files on purpose."""
+the alignment), for synthetic checkpoints in the benchmark and the tests.
+Keyword overrides write malformed files on purpose (reader tests)."""
 from __future__ import annotations
 
 import struct
@@ -82,3 +83,30 @@ def write(path: Path, kvs, tensors, **kw):
     data, payloads = build(kvs, tensors, **kw)
     Path(path).write_bytes(data)
     return payloads
+
+
+def write_arrays(path: Path, kvs, tensors, alignment: int = 32) -> dict:
+    """A well-formed file from large payloads, streamed to disk.
+    tensors: [(name, ne, ggml_type, array or bytes)]. Returns {name: absolute
+    payload offset}."""
+    head = b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(kvs))
+    for key, vtype, v in kvs:
+        head += text(key) + struct.pack("<I", vtype) + value(vtype, v)
+    running, offsets = 0, {}
+    for name, ne, gtype, data in tensors:
+        n = memoryview(data).nbytes
+        if n != payload_bytes(ne, gtype):
+            raise ValueError(f"{name}: {n} payload bytes for shape {ne} of type {gtype}")
+        head += text(name) + struct.pack("<I", len(ne)) + b"".join(struct.pack("<Q", d) for d in ne)
+        head += struct.pack("<IQ", gtype, running)
+        offsets[name] = running
+        running += pad(n, alignment)
+    start = pad(len(head), alignment) if tensors else len(head)
+    with open(path, "wb") as f:
+        f.write(head)
+        f.write(b"\0" * (start - len(head)))
+        for name, ne, gtype, data in tensors:
+            mv = memoryview(data).cast("B")
+            f.write(mv)
+            f.write(b"\0" * (pad(mv.nbytes, alignment) - mv.nbytes))
+    return {k: start + v for k, v in offsets.items()}

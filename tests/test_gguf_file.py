@@ -11,8 +11,8 @@ import os
 import numpy as np
 import pytest
 
-import gguf_write as gw
-from gguf_write import ARRAY, BOOL, F32, F64, I8, I32, I64, STRING, U8, U16, U32, U64
+from kadan_b200 import gguf_write as gw
+from kadan_b200.gguf_write import ARRAY, BOOL, F32, F64, I8, I32, I64, STRING, U8, U16, U32, U64
 
 Q8_0, Q3_K, Q4_K, Q6_K, BF16, F32T = 8, 11, 12, 14, 30, 0
 
@@ -304,3 +304,20 @@ def test_reader_without_reference(gg, tmp_path):
     assert ours.integer("llama.context_length") == 8192
     assert ours.number("llama.rope.freq_base") == 500000.0
     assert ours.boolean("llama.use_parallel_residual") is True
+
+
+def test_source_pointer_the_batch_receives(gg, tmp_path):
+    """The kb200_row_source pointer that weight_bank.dense_gguf_source_batch
+    hands the library for a bound GgufRows reads the same rows when called."""
+    from kadan_b200.weight_bank import _ROW_SOURCE
+
+    root, payloads = single(tmp_path)
+    ours = gg.GgufCheckpoint(root)
+    name = "blk.0.attn_q.weight"
+    t = ours.tensor(name)
+    src = ours.rows(name)
+    fn = _ROW_SOURCE(gg.ROWS_SOURCE_ADDRESS)
+    buf = (ctypes.c_ubyte * (3 * t.row_bytes))()
+    assert fn(src.user, 2, ctypes.addressof(buf), 3 * t.row_bytes) == 0
+    assert bytes(buf) == payloads[name][2 * t.row_bytes:5 * t.row_bytes]
+    assert fn(src.user, t.shape[1] - 1, ctypes.addressof(buf), 3 * t.row_bytes) != 0

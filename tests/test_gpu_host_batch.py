@@ -281,3 +281,43 @@ def test_source_batch_read_lanes(kb, oracle, cuda):
                 assert [r[0] for r in job.reads] == [0, 3855, 7710]
     finally:
         ctx.close()
+
+
+def test_source_batch_reads_a_gguf_checkpoint(kb, oracle, cuda, tmp_path):
+    """Packed rows read from a GGUF file by the library's own source
+    (kb200_gguf_rows_source, on the read team's threads) give the oracle's
+    outputs, first streamed, then from the bank."""
+    from kadan_b200 import gguf_write as gw
+    from kadan_b200 import synth
+    from kadan_b200.gguf_file import GgufCheckpoint
+    from kadan_b200.weight_bank import SourceJob, WeightBank, dense_gguf_source_batch
+
+    # (name, encoding, ggml type, in, out): Q4_K in 2 chunks (7281 + 911
+    # columns), Q8_0 in 2 chunks (3855 + 241).
+    specs = [("blk.0.ffn_up.weight", kb.Q4_K, 12, 4096, 8192), ("blk.0.attn_q.weight", kb.Q8_0, 8, 4096, 4096)]
+    weights = {name: synth.gguf(enc, out, in_, seed=60 + i) for i, (name, enc, _, in_, out) in enumerate(specs)}
+    root = tmp_path / "ckpt"
+    root.mkdir()
+    gw.write_arrays(root / "model.gguf", [("general.architecture", gw.STRING, "llama")],
+                    [(name, [in_, out], gtype, weights[name]) for name, _, gtype, in_, out in specs])
+    ckpt = GgufCheckpoint(root)
+    jobs, refs = [], []
+    for i, (name, enc, _, in_, out) in enumerate(specs):
+        x = synth.activations(in_, seed=70 + i, dtype="f32").reshape(1, in_)
+        jobs.append(SourceJob(ckpt.identity(name), ckpt.rows(name), x, np.full((1, out), np.nan, np.float32), in_,
+                              out, enc))
+        refs.append(oracle.gemv_f64(enc, weights[name], x, in_, out))
+    ctx = kb.Context(0)
+    bank = WeightBank.cuda(0, 256 << 20)
+    try:
+        for _ in range(2):
+            for j in jobs:
+                j.y[:] = np.nan
+            assert dense_gguf_source_batch(ctx, bank, jobs) == kb.RESULT_UNVALIDATED
+            for j, ref in zip(jobs, refs):
+                assert rel_err(j.y, ref) < TOL
+        assert bank.entries() == 4
+    finally:
+        bank.close()
+        ctx.close()
+        ckpt.close()
