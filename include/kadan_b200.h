@@ -41,7 +41,9 @@ typedef enum kb200_status {
     KB200_TIMEOUT = 8,           /* a bounded device-side wait ran out */
     KB200_NO_MEMORY = 9,
     KB200_QUARANTINED = 10,      /* "weight_cleanup_unconfirmed": a weight bank's cleanup failed */
-    KB200_IO = 11                /* a checkpoint file could not be opened or read */
+    KB200_IO = 11,               /* a checkpoint file could not be opened or read */
+    KB200_NONFINITE_BIAS = 12,   /* "h3_cuda_nonfinite_bias" */
+    KB200_NONFINITE_OUTPUT = 13  /* "h3_cuda_nonfinite_output" */
 } kb200_status;
 
 /* Weight encodings: the numbering of kadan::gguf::Encoding
@@ -572,6 +574,20 @@ typedef struct kb200_source_job {
 KB200_API int kb200_dense_gguf_source_batch(kb200_context* ctx, kb200_bank* bank, const kb200_source_job* jobs,
                                             size_t count, uint64_t scratch_limit, const volatile uint8_t* cancel,
                                             int* result);
+
+/* DenseCompute::dense_gguf_source (IW/include/kadan/dense_compute.hpp:180-194,
+ * IW/src/cuda/h3_compute.cu:3503-3536): one projection of a packed source with
+ * an optional fp32 bias [out]. Unsupported jobs (as for the batch, and every
+ * `precise` call: the reference widens to an fp64 GEMM there, which is not
+ * offered here) return KB200_UNSUPPORTED before any read or write; a
+ * non-finite bias fails with KB200_NONFINITE_BIAS before any source read; then
+ * the job runs as a one-job kb200_dense_gguf_source_batch, the bias is added
+ * (one fp32 addition per output, as the reference's add_bias), and every
+ * output is checked finite: KB200_NONFINITE_OUTPUT (outputs to be discarded)
+ * or *result = KB200_RESULT_FINITE. */
+KB200_API int kb200_dense_gguf_source(kb200_context* ctx, kb200_bank* bank, const kb200_source_job* job,
+                                      const float* bias, uint64_t scratch_limit, int precise,
+                                      const volatile uint8_t* cancel, int* result);
 
 /* ---------------------------------------------------------------------------
  * GGUF checkpoint reader: kadan::checkpoint::GgufCheckpoint

@@ -37,7 +37,7 @@ ENCODING_NAMES = {F32: "f32", Q3_K: "q3_k", Q4_K: "q4_k", Q8_0: "q8_0", Q6_K: "q
 GGML_TYPE = {Q8_0: 8, Q3_K: 11, Q4_K: 12, Q6_K: 14, IQ4_NL: 20, IQ4_XS: 23, BF16: 30, F32: 0}
 
 (OK, UNSUPPORTED, INVALID, CUDA, NONFINITE_WEIGHT, NONFINITE_INPUT, ALIAS, CANCELLED, TIMEOUT, NO_MEMORY,
- QUARANTINED, IO) = range(12)
+ QUARANTINED, IO, NONFINITE_BIAS, NONFINITE_OUTPUT) = range(14)
 BATCH_ROWS = 8
 BATCH_MAX_ROWS = 4096
 

@@ -312,6 +312,12 @@ struct Group {
     size_t begin, end, used;
 };
 
+bool source_job_supported(const kb200_source_job& job) {
+    return kb200_encoding_supported(job.encoding) && job.identity && job.source && job.input && job.output && job.in
+           && job.out && job.rows && job.rows <= KB200_BATCH_MAX_ROWS && job.in % 8 == 0
+           && job.in % kb200_block_values(job.encoding) == 0;
+}
+
 }  // namespace
 }  // namespace kb200
 
@@ -326,13 +332,9 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
     if (cancelled(cancel))
         return fail(KB200_CANCELLED, "cancelled before start");
     // Unsupported precedes every source read and output write (gguf_batch_supported).
-    for (size_t j = 0; j < count; ++j) {
-        const auto& job = jobs[j];
-        if (!kb200_encoding_supported(job.encoding) || !job.identity || !job.source || !job.input || !job.output
-            || !job.in || !job.out || !job.rows || job.rows > KB200_BATCH_MAX_ROWS || job.in % 8
-            || job.in % kb200_block_values(job.encoding))
+    for (size_t j = 0; j < count; ++j)
+        if (!source_job_supported(jobs[j]))
             return fail(KB200_UNSUPPORTED, "job outside the batched GEMV contract");
-    }
     // The reference's chunk geometry on one device (gguf_batch_partition.hpp:44-83).
     const uint64_t one_device = 1, limit = scratch_limit ? scratch_limit : (uint64_t(1) << 30);
     std::vector<kb200_partition> parts(count);
@@ -513,6 +515,36 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
                     size_t(jobs[j].rows) * jobs[j].out * sizeof(float));
     if (result)
         *result = KB200_RESULT_UNVALIDATED;
+    return KB200_OK;
+}
+
+int kb200_dense_gguf_source(kb200_context* c, kb200_bank* bank, const kb200_source_job* job, const float* bias,
+                            uint64_t scratch_limit, int precise, const volatile uint8_t* cancel, int* result) {
+    if (result)
+        *result = KB200_RESULT_UNSUPPORTED;
+    if (!c || !job || !source_job_supported(*job))
+        return fail(KB200_UNSUPPORTED, "job outside the projection contract");
+    if (precise)
+        return fail(KB200_UNSUPPORTED, "fp64 (precise) projections are not offered");
+    if (bias)
+        for (uint32_t o = 0; o < job->out; ++o)
+            if (!std::isfinite(bias[o]))
+                return fail(KB200_NONFINITE_BIAS, "non-finite bias value");
+    if (bias && overlap(job->output, size_t(job->rows) * job->out * sizeof(float), bias, size_t(job->out) * sizeof(float)))
+        return fail(KB200_ALIAS, "output overlaps the bias");
+    int batch_result = KB200_RESULT_UNSUPPORTED;
+    if (const int s = kb200_dense_gguf_source_batch(c, bank, job, 1, scratch_limit, cancel, &batch_result))
+        return s;
+    const size_t n = size_t(job->rows) * job->out;
+    for (size_t i = 0; i < n; ++i) {
+        float& y = job->output[i];
+        if (bias)
+            y += bias[i % job->out];
+        if (!std::isfinite(y))
+            return fail(KB200_NONFINITE_OUTPUT, "a projection output is not finite");
+    }
+    if (result)
+        *result = KB200_RESULT_FINITE;
     return KB200_OK;
 }
 

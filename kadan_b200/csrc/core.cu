@@ -76,6 +76,8 @@ const char* kb200_status_name(int status) {
     case KB200_NO_MEMORY: return "h3_cuda_projection_scratch";
     case KB200_QUARANTINED: return "weight_cleanup_unconfirmed";
     case KB200_IO: return "gguf_io";
+    case KB200_NONFINITE_BIAS: return "h3_cuda_nonfinite_bias";
+    case KB200_NONFINITE_OUTPUT: return "h3_cuda_nonfinite_output";
     default: return "kb200_unknown_status";
     }
 }

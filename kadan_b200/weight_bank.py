@@ -248,6 +248,8 @@ class SourceJobC(ctypes.Structure):
 
 lib.kb200_dense_gguf_source_batch.argtypes = [vp, vp, ctypes.POINTER(SourceJobC), ctypes.c_size_t, c_u64,
                                               ctypes.POINTER(c_u8), ctypes.POINTER(c_int)]
+lib.kb200_dense_gguf_source.argtypes = [vp, vp, ctypes.POINTER(SourceJobC), vp, c_u64, c_int, ctypes.POINTER(c_u8),
+                                        ctypes.POINTER(c_int)]
 SOURCE_STAGING_HALF = 16 << 20
 
 
@@ -271,9 +273,8 @@ class SourceJob:
     reads: list = field(default_factory=list)  # (first_row, nbytes) of every source call
 
 
-def dense_gguf_source_batch(ctx, bank: Optional[WeightBank], jobs, scratch_limit: int = 0,
-                            cancel: Optional[ctypes.c_ubyte] = None) -> int:
-    """Run the jobs (kb200_dense_gguf_source_batch); returns the ProjectionResult code."""
+def _source_jobs_c(jobs):
+    """The kb200_source_job array for `jobs` and the objects it points into."""
     from .gguf_file import ROWS_SOURCE_ADDRESS, GgufRows
 
     keep = []
@@ -299,6 +300,13 @@ def dense_gguf_source_batch(ctx, bank: Optional[WeightBank], jobs, scratch_limit
         rows = job.x.size // job.in_
         arr[i] = SourceJobC(ctypes.pointer(ident), cb, user, job.x.ctypes.data, job.y.ctypes.data, job.in_, job.out,
                             rows, job.encoding, int(job.retain_misses))
+    return arr, keep
+
+
+def dense_gguf_source_batch(ctx, bank: Optional[WeightBank], jobs, scratch_limit: int = 0,
+                            cancel: Optional[ctypes.c_ubyte] = None) -> int:
+    """Run the jobs (kb200_dense_gguf_source_batch); returns the ProjectionResult code."""
+    arr, keep = _source_jobs_c(jobs)
     result = c_int(0)
     check(lib.kb200_dense_gguf_source_batch(ctx.handle, None if bank is None else bank._h, arr, len(jobs),
                                             scratch_limit, None if cancel is None else ctypes.pointer(cancel),
@@ -307,5 +315,19 @@ def dense_gguf_source_batch(ctx, bank: Optional[WeightBank], jobs, scratch_limit
     return int(result.value)
 
 
-__all__ = ["WeightBank", "SourceJob", "dense_gguf_source_batch", "WeightKey", "WeightIdentity", "KadanError", "CANCELLED", "ADMITTED", "EMPTY",
+def dense_gguf_source(ctx, bank: Optional[WeightBank], job: SourceJob, bias=None, scratch_limit: int = 0,
+                      precise: bool = False, cancel: Optional[ctypes.c_ubyte] = None) -> int:
+    """DenseCompute::dense_gguf_source (kb200_dense_gguf_source): one job plus
+    an optional float32 bias [out]; returns RESULT_FINITE."""
+    arr, keep = _source_jobs_c([job])
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    result = c_int(0)
+    check(lib.kb200_dense_gguf_source(ctx.handle, None if bank is None else bank._h, arr,
+                                      None if b is None else b.ctypes.data, scratch_limit, int(precise),
+                                      None if cancel is None else ctypes.pointer(cancel), ctypes.byref(result)))
+    del keep
+    return int(result.value)
+
+
+__all__ = ["WeightBank", "SourceJob", "dense_gguf_source_batch", "dense_gguf_source", "WeightKey", "WeightIdentity", "KadanError", "CANCELLED", "ADMITTED", "EMPTY",
            "ENVELOPE", "PHYSICAL", "ALLOCATION", "REFUSAL_NAMES"]

@@ -321,3 +321,33 @@ def test_source_batch_reads_a_gguf_checkpoint(kb, oracle, cuda, tmp_path):
         bank.close()
         ctx.close()
         ckpt.close()
+
+
+def test_single_source_projection_with_bias(kb, oracle, cuda):
+    """kb200_dense_gguf_source: bias added once per output, outputs certified
+    finite; a non-finite bias and `precise` stop the call before any read."""
+    from kadan_b200.weight_bank import WeightBank, dense_gguf_source
+
+    jobs, refs = source_jobs(kb, oracle, [(kb.Q8_0, 2048, 300, 3)])
+    job = jobs[0]
+    bias = np.linspace(-1, 1, 300).astype(np.float32)
+    ctx = kb.Context(0)
+    bank = WeightBank.cuda(0, 64 << 20)
+    try:
+        assert dense_gguf_source(ctx, bank, job, bias=bias) == kb.RESULT_FINITE
+        assert rel_err(job.y, refs[0] + bias) < TOL
+        job.reads.clear()
+        bad = bias.copy()
+        bad[7] = np.nan
+        with pytest.raises(kb.KadanError) as e:
+            dense_gguf_source(ctx, bank, job, bias=bad)
+        assert e.value.status == kb.NONFINITE_BIAS
+        with pytest.raises(kb.Unsupported):
+            dense_gguf_source(ctx, bank, job, bias=bias, precise=True)
+        assert not job.reads
+        # Served from the bank on the second call.
+        assert dense_gguf_source(ctx, bank, job) == kb.RESULT_FINITE
+        assert not job.reads and rel_err(job.y, refs[0]) < TOL
+    finally:
+        bank.close()
+        ctx.close()

@@ -426,3 +426,23 @@ def test_source_batch_checks_precede_reads(wb):
     with pytest.raises(Unsupported):
         wb.dense_gguf_source_batch(NoContext(), None, [job])
     assert not calls
+
+
+def test_single_source_checks_precede_reads(wb):
+    """kb200_dense_gguf_source: unsupported jobs and `precise` calls return
+    unsupported before any source read."""
+    import numpy as np
+
+    from kadan_b200 import Q8_0, Unsupported
+
+    calls = []
+
+    class NoContext:
+        handle = None
+
+    job = wb.SourceJob(wb.WeightIdentity(inode=1), lambda first, n: calls.append(first) or bytes(n),
+                       np.zeros((1, 64), np.float32), np.zeros((1, 8), np.float32), 64, 8, Q8_0)
+    for precise in (False, True):
+        with pytest.raises(Unsupported):
+            wb.dense_gguf_source(NoContext(), None, job, bias=np.zeros(8, np.float32), precise=precise)
+    assert not calls
