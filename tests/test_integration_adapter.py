@@ -1,0 +1,33 @@
+"""The worker-side adapter include/kadan_b200_dense_compute.hpp compiles
+against the reference's own kadan/dense_compute.hpp (its overrides match the
+reference's virtual signatures) and links against libkadan_b200.so with no
+undefined symbol. Needs the reference tree; no GPU."""
+from __future__ import annotations
+
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from conftest import ROOT
+
+IW = Path("/root/reference/services/hikari/inference_worker")
+
+
+def test_adapter_compiles_against_reference_interface(kb, tmp_path):
+    cxx = shutil.which("g++")
+    if cxx is None or not (IW / "include" / "kadan" / "dense_compute.hpp").exists():
+        pytest.skip("needs the reference headers and a host C++ compiler")
+    tu = tmp_path / "adapter.cpp"
+    tu.write_text(
+        '#include "kadan_b200_dense_compute.hpp"\n'
+        "std::unique_ptr<kadan::DenseCompute> make(std::shared_ptr<kadan::DenseCompute> f) {\n"
+        "    return std::make_unique<kadan::b200::Compute>(std::move(f), 0, 1ull << 30, 1ull << 30);\n"
+        "}\n")
+    lib = Path(kb.LIB_PATH)
+    cmd = [cxx, "-std=c++20", "-Wall", "-Wextra", "-Werror", "-shared", "-fPIC", f"-I{ROOT / 'include'}",
+           f"-I{IW / 'include'}", f"-I{IW / 'third_party' / 'ggml' / 'include'}", str(tu), f"-L{lib.parent}",
+           "-lkadan_b200", "-Wl,--no-undefined", "-o", str(tmp_path / "adapter.so")]
+    run = subprocess.run(cmd, capture_output=True, text=True)
+    assert run.returncode == 0, run.stderr
