@@ -11,8 +11,9 @@ from pathlib import Path
 import pytest
 
 from conftest import ROOT
+from oracle.pyoracle import REFERENCE_TREE
 
-IW = Path("/root/reference/services/hikari/inference_worker")
+IW = REFERENCE_TREE / "services" / "hikari" / "inference_worker"
 
 
 def test_adapter_compiles_against_reference_interface(kb, tmp_path):
