@@ -25,7 +25,7 @@
 #include <unistd.h>
 #include <vector>
 
-#include "gguf_formats.cuh"
+#include "gguf_geometry.hpp"
 #include "kb200_host.hpp"
 
 namespace kb200 {

@@ -11,41 +11,10 @@
 #include <cstdint>
 #include <cuda_fp16.h>
 
+#include "gguf_geometry.hpp"
 #include "kadan_b200.h"
 
 namespace kb200 {
-
-__host__ __device__ constexpr int block_values(int e) {
-    return e == KB200_BF16 ? 1 : (e == KB200_Q8_0 || e == KB200_IQ4_NL) ? 32 : e == KB200_F32 ? 1 : 256;
-}
-
-__host__ __device__ constexpr int block_bytes(int e) {
-    switch (e) {
-    case KB200_Q3_K: return 110;
-    case KB200_Q4_K: return 144;
-    case KB200_Q8_0: return 34;
-    case KB200_Q6_K: return 210;
-    case KB200_IQ4_NL: return 18;
-    case KB200_IQ4_XS: return 136;
-    case KB200_IQ3_XXS: return 98;  // geometry only: no device decoder here
-    case KB200_IQ2_S: return 82;    // geometry only
-    case KB200_IQ3_S: return 110;   // geometry only
-    case KB200_BF16: return 2;
-    case KB200_F32: return 4;
-    default: return 0;
-    }
-}
-
-// Encodings GGUF geometry is known for (the reference's gguf::supported set).
-__host__ __device__ constexpr bool gguf_geometry(int e) {
-    return e >= KB200_Q3_K && e <= KB200_BF16;
-}
-
-// Encodings with a device decoder here.
-__host__ __device__ constexpr bool decodable(int e) {
-    return e == KB200_Q3_K || e == KB200_Q4_K || e == KB200_Q8_0 || e == KB200_Q6_K
-           || e == KB200_IQ4_NL || e == KB200_IQ4_XS || e == KB200_BF16;
-}
 
 // binary16 -> binary32 by integer operations, exact for every pattern
 // including subnormals and NaN payloads.

@@ -12,7 +12,7 @@
 #include <algorithm>
 #include <cstdint>
 
-#include "gguf_formats.cuh"
+#include "gguf_geometry.hpp"
 #include "kb200_host.hpp"
 
 namespace kb200 {
