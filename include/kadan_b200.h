@@ -181,9 +181,10 @@ KB200_API void* kb200_context_stream(kb200_context* ctx);
  * Sources may then run concurrently on disjoint rows. */
 KB200_API int kb200_context_set_read_lanes(kb200_context* ctx, int lanes);
 
-/* Device-resident packed rows (the weight bank the reference keeps per
- * device, IW/include/kadan/device_weights.hpp:38): a synchronous upload of
- * `bytes` host bytes into a 256-byte aligned device allocation. */
+/* Caller-managed device-resident packed rows for kb200_dense_gguf_batch: a
+ * synchronous upload of `bytes` host bytes into a 256-byte aligned device
+ * allocation. (kb200_bank_* keeps resident rows with the reference's
+ * DeviceWeights rules instead; kb200_dense_gguf_source_batch uses it.) */
 KB200_API int kb200_weights_upload(kb200_context* ctx, const void* host, size_t bytes, void** device);
 KB200_API int kb200_weights_free(kb200_context* ctx, void* device);
 
