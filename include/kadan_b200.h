@@ -631,6 +631,11 @@ KB200_API int kb200_gguf_check_unchanged(const kb200_gguf* file);
 KB200_API int kb200_gguf_read_packed_rows(const kb200_gguf* file, const char* name, uint64_t expert,
                                           uint64_t first_row, void* output, uint64_t bytes,
                                           const volatile uint8_t* cancel);
+/* GgufCheckpoint::read_vector: a whole F32 tensor of any rank (`count` its
+ * element count), every value finite ("gguf_vector_shape",
+ * "gguf_nonfinite_weight"); the output is to be discarded after a failure. */
+KB200_API int kb200_gguf_read_vector(const kb200_gguf* file, const char* name, float* output, uint64_t count,
+                                     const volatile uint8_t* cancel);
 /* Metadata of the first file (GgufCheckpoint::has / integer / number /
  * boolean / string / integers / numbers). `integers` and `numbers` copy at
  * most `capacity` values and report the array's length in *count. */

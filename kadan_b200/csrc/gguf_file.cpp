@@ -632,6 +632,31 @@ int kb200_gguf_read_packed_rows(const kb200_gguf* g, const char* name, uint64_t 
     return guarded([&] { read_rows(g, find_tensor(g, name), expert, first_row, output, bytes, cancel); });
 }
 
+// GgufCheckpoint::read_vector (gguf_checkpoint.cpp:676-701).
+int kb200_gguf_read_vector(const kb200_gguf* g, const char* name, float* output, uint64_t count,
+                           const volatile uint8_t* cancel) {
+    if (!g)
+        return fail(KB200_INVALID, "null checkpoint");
+    return guarded([&] {
+        stop(cancel);
+        const TensorEntry& t = find_tensor(g, name);
+        require(t.type == 0 && count == t.shape[0] * t.shape[1] * t.shape[2] && count * sizeof(float) == t.bytes,
+                "gguf_vector_shape");
+        require(output != nullptr || count == 0, "gguf_vector_shape");
+        const File& file = g->files[t.file];
+        file.unchanged();
+        auto* raw = reinterpret_cast<uint8_t*>(output);
+        for (uint64_t at = 0; at < t.bytes; at += 65536) {
+            stop(cancel);
+            file.read(add(t.begin, at), raw + at, std::min<uint64_t>(65536, t.bytes - at), nullptr);
+        }
+        for (uint64_t i = 0; i < count; ++i)
+            require(std::isfinite(output[i]), "gguf_nonfinite_weight");
+        file.unchanged();
+        stop(cancel);
+    });
+}
+
 int kb200_gguf_has(const kb200_gguf* g, const char* key) {
     return g && key && std::strlen(key) <= 256 && g->kv.count(key) ? 1 : 0;
 }

@@ -45,6 +45,7 @@ lib.kb200_gguf_identity.argtypes = [vp, ctypes.c_char_p, c_u64, ctypes.POINTER(W
 lib.kb200_gguf_check_unchanged.argtypes = [vp]
 lib.kb200_gguf_read_packed_rows.argtypes = [vp, ctypes.c_char_p, c_u64, c_u64, vp, c_u64, ctypes.POINTER(c_u8)]
 lib.kb200_gguf_has.argtypes = [vp, ctypes.c_char_p]
+lib.kb200_gguf_read_vector.argtypes = [vp, ctypes.c_char_p, vp, c_u64, ctypes.POINTER(c_u8)]
 lib.kb200_gguf_integer.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(c_u64)]
 lib.kb200_gguf_number.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]
 lib.kb200_gguf_boolean.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)]
@@ -144,6 +145,12 @@ class GgufCheckpoint:
                                               out.ctypes.data if nbytes else None, nbytes,
                                               None if cancel is None else ctypes.pointer(cancel)))
         return out
+
+    def read_vector(self, name: str, count: int, cancel: Optional[ctypes.c_ubyte] = None) -> np.ndarray:
+        out = np.empty(max(1, count), dtype=np.float32)
+        check(lib.kb200_gguf_read_vector(self._h, name.encode(), out.ctypes.data, count,
+                                         None if cancel is None else ctypes.pointer(cancel)))
+        return out[:count]
 
     def rows(self, name: str, expert: int = 0) -> GgufRows:
         return GgufRows(self, name, expert)

@@ -187,6 +187,7 @@ class Reference:
         L.ref_gguf_checkpoint_read_packed_rows.argtypes = [vp, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_uint64,
                                                            vp, ctypes.c_size_t]
         L.ref_gguf_checkpoint_check_unchanged.argtypes = [vp]
+        L.ref_gguf_checkpoint_read_vector.argtypes = [vp, ctypes.c_char_p, _f32p, ctypes.c_size_t]
         L.ref_gguf_checkpoint_integer.argtypes = [vp, ctypes.c_char_p, u64p]
         L.ref_gguf_checkpoint_number.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]
         L.ref_gguf_checkpoint_boolean.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)]
@@ -285,6 +286,12 @@ class Reference:
                                                        buf.ctypes.data if nbytes else None, nbytes):
             return self.error()
         return buf
+
+    def gguf_read_vector(self, h, name: str, count: int):
+        out = np.zeros(max(1, count), dtype=np.float32)
+        if self.L.ref_gguf_checkpoint_read_vector(h, name.encode(), _p(out, _f32p), count):
+            return self.error()
+        return out[:count]
 
     def gguf_check_unchanged(self, h):
         return None if self.L.ref_gguf_checkpoint_check_unchanged(h) == 0 else self.error()

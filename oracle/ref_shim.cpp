@@ -332,6 +332,17 @@ int ref_gguf_checkpoint_read_packed_rows(void* checkpoint, const char* name, uin
     }
 }
 
+int ref_gguf_checkpoint_read_vector(void* checkpoint, const char* name, float* output, size_t count) {
+    try {
+        static const std::atomic_bool never{false};
+        static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->read_vector(
+            name, std::span<float>(output, count), never);
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
 int ref_gguf_checkpoint_check_unchanged(void* checkpoint) {
     try {
         static_cast<kadan::checkpoint::GgufCheckpoint*>(checkpoint)->check_unchanged();

@@ -321,3 +321,24 @@ def test_source_pointer_the_batch_receives(gg, tmp_path):
     assert fn(src.user, 2, ctypes.addressof(buf), 3 * t.row_bytes) == 0
     assert bytes(buf) == payloads[name][2 * t.row_bytes:5 * t.row_bytes]
     assert fn(src.user, t.shape[1] - 1, ctypes.addressof(buf), 3 * t.row_bytes) != 0
+
+
+def test_read_vector_matches_reference(gg, ref, tmp_path):
+    vec = np.arange(24, dtype=np.float32).reshape(2, 3, 4) * 0.5
+    bad = np.array([1.0, np.nan, 3.0, 4.0], dtype=np.float32)
+    root = tmp_path / "v"
+    root.mkdir()
+    gw.write_arrays(root / "m.gguf", [("general.architecture", STRING, "x")],
+                    [("norm", [4, 3, 2], F32T, vec), ("bad", [4], F32T, bad),
+                     ("q", [256, 2], Q4_K, np.zeros((2, 144), np.uint8))])
+    ours = gg.GgufCheckpoint(root)
+    h = ref.gguf_open(root)
+    try:
+        got = ours.read_vector("norm", 24)
+        assert np.array_equal(got, vec.reshape(-1)) and np.array_equal(got, ref.gguf_read_vector(h, "norm", 24))
+        for name, count in (("norm", 23), ("bad", 4), ("q", 512), ("missing", 1)):
+            want = ref.gguf_read_vector(h, name, count)
+            assert isinstance(want, str)
+            assert message_of_call(lambda: ours.read_vector(name, count)) == want, (name, want)
+    finally:
+        ref.gguf_close(h)
