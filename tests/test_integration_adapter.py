@@ -32,3 +32,21 @@ def test_adapter_compiles_against_reference_interface(kb, tmp_path):
            "-lkadan_b200", "-Wl,--no-undefined", "-o", str(tmp_path / "adapter.so")]
     run = subprocess.run(cmd, capture_output=True, text=True)
     assert run.returncode == 0, run.stderr
+
+
+def test_adapter_overrides_every_virtual():
+    """Every virtual of the reference's DenseCompute is overridden, so the
+    adapter can take the place of the worker's compute object without turning
+    any of its features off."""
+    import re
+
+    header = IW / "include" / "kadan" / "dense_compute.hpp"
+    if not header.exists():
+        pytest.skip("needs the reference headers")
+    text = header.read_text()
+    body = text[text.index("class DenseCompute {"):]
+    names = set(re.findall(r"virtual\s+(?:[\w:<>,\s]+?\s+)?(\w+)\s*\(", body)) - {"~DenseCompute"}
+    adapter = (ROOT / "include" / "kadan_b200_dense_compute.hpp").read_text()
+    overridden = set(re.findall(r"(\w+)\s*\([^;{]*?\)\s*(?:const\s*)?override", adapter, re.S))
+    assert len(names) >= 20
+    assert names <= overridden, sorted(names - overridden)
