@@ -5,6 +5,7 @@
 // download, one stream synchronisation per call. Over packed-row sources:
 // bank hits as one launch, misses streamed through two pinned staging halves
 // and admitted into the bank once they decoded finite.
+#include <climits>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -312,10 +313,16 @@ struct Group {
     size_t begin, end, used;
 };
 
+// gguf_batch_supported (IW/include/kadan/gguf_batch_partition.hpp:14-37): a
+// row must fit one 16 MiB staging buffer, sizes fit an int, and the encoding
+// has a decoder here.
 bool source_job_supported(const kb200_source_job& job) {
-    return kb200_encoding_supported(job.encoding) && job.identity && job.source && job.input && job.output && job.in
-           && job.out && job.rows && job.rows <= KB200_BATCH_MAX_ROWS && job.in % 8 == 0
-           && job.in % kb200_block_values(job.encoding) == 0;
+    if (!kb200_encoding_supported(job.encoding) || !job.identity || !job.source || !job.input || !job.output
+        || !job.in || !job.out || job.in > uint32_t(INT_MAX) || job.out > uint32_t(INT_MAX) || !job.rows
+        || job.rows > KB200_BATCH_MAX_ROWS || job.in % 8)
+        return false;
+    const uint64_t values = kb200_block_values(job.encoding), width = kb200_block_bytes(job.encoding);
+    return job.in % values == 0 && job.in / values <= kHalf / width;
 }
 
 }  // namespace
