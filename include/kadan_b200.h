@@ -555,6 +555,14 @@ typedef struct kb200_source_job {
     int32_t retain_misses;
 } kb200_source_job;
 
+/* 1 if kb200_dense_gguf_source_batch accepts `job` (gguf_batch_supported,
+ * IW/include/kadan/gguf_batch_partition.hpp:14-37, for one job: sizes within
+ * an int, rows within KB200_BATCH_MAX_ROWS, `in` a multiple of 8 and of the
+ * block, a row within one staging half, and an encoding with a decoder here);
+ * host only. A caller that splits a batch over several devices checks every
+ * job first, so that unsupported still precedes any source read. */
+KB200_API int kb200_source_job_supported(const kb200_source_job* job);
+
 /* Staging of kb200_dense_gguf_source_batch: two halves of this many bytes,
  * pinned on the host and on the device. */
 #define KB200_SOURCE_STAGING_HALF (16u * 1024u * 1024u)

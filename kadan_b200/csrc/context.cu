@@ -525,6 +525,10 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
     return KB200_OK;
 }
 
+int kb200_source_job_supported(const kb200_source_job* job) {
+    return job && source_job_supported(*job) ? 1 : 0;
+}
+
 int kb200_dense_gguf_source(kb200_context* c, kb200_bank* bank, const kb200_source_job* job, const float* bias,
                             uint64_t scratch_limit, int precise, const volatile uint8_t* cancel, int* result) {
     if (result)

@@ -174,6 +174,7 @@ class Reference:
         L.ref_gguf_batch_partition.argtypes = [ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int,
                                                ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, ctypes.c_size_t,
                                                ctypes.c_uint64, ctypes.POINTER(ctypes.c_size_t)]
+        L.ref_gguf_batch_supported.argtypes = [ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int]
         vp, u64p = ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)
         L.ref_gguf_checkpoint_open.restype = vp
         L.ref_gguf_checkpoint_open.argtypes = [ctypes.c_char_p]
@@ -253,6 +254,9 @@ class Reference:
             return self.error()
         rows, cols = int(shape[0]), int(shape[1])
         return w[:rows * cols // 2], sc[:rows * cols // 32], rows, cols
+
+    def gguf_batch_supported(self, in_: int, out: int, rows: int, encoding: int) -> bool:
+        return bool(self.L.ref_gguf_batch_supported(in_, out, rows, encoding))
 
     # -- kadan::checkpoint::GgufCheckpoint (IW/src/weights/gguf_checkpoint.cpp)
     def gguf_open(self, root: str):

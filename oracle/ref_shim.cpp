@@ -267,6 +267,18 @@ int ref_gguf_batch_partition(size_t in, size_t out, int encoding, const uint64_t
     }
 }
 
+// gguf_batch_supported (IW/include/kadan/gguf_batch_partition.hpp:14-37) for
+// one job with `rows` input rows; encoding < 0 means F32 rows.
+int ref_gguf_batch_supported(size_t in, size_t out, size_t rows, int encoding) {
+    static const kadan::WeightIdentity identity{};
+    static const kadan::DenseCompute::GgufWeightSource source = [](size_t, std::span<std::byte>) {};
+    std::vector<float> input(in * rows), output(out * rows);
+    kadan::DenseCompute::GgufBatchJob job{&identity, std::nullopt, &source, input, in, out, output, true};
+    if (encoding >= 0)
+        job.encoding = static_cast<kadan::gguf::Encoding>(encoding);
+    return kadan::gguf_batch_supported(std::span(&job, 1), 1) ? 1 : 0;
+}
+
 // GGUF checkpoint reader (IW/include/kadan/gguf_checkpoint.hpp:53-103).
 void* ref_gguf_checkpoint_open(const char* root) {
     try {

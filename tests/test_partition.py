@@ -67,3 +67,39 @@ def test_partition_covers_every_column_once_and_scatters(kb, caps):
         assert previous == out
         assert np.all(owners == 1)
         assert np.array_equal(output.ravel(), np.arange(rows * out, dtype=np.float32))
+
+
+def test_source_job_support_matches_reference(kb, ref):
+    """kb200_source_job_supported agrees with the reference's
+    gguf_batch_supported on every job shape, except for the encodings that
+    have no device decoder here (IQ3_XXS, IQ2_S, IQ3_S), which it declines."""
+    import ctypes
+
+    from kadan_b200.weight_bank import SourceJobC, WeightIdentityC, _ROW_SOURCE
+
+    kb.lib.kb200_source_job_supported.argtypes = [ctypes.POINTER(SourceJobC)]
+    ident = WeightIdentityC()
+    src = _ROW_SOURCE(lambda *a: 0)
+    no_decoder = {kb.IQ3_XXS, kb.IQ2_S, kb.IQ3_S}
+    checked = 0
+    for enc in (kb.F32, kb.Q3_K, kb.Q4_K, kb.Q8_0, kb.Q6_K, kb.IQ3_XXS, kb.IQ4_NL, kb.IQ4_XS, kb.IQ2_S, kb.IQ3_S,
+                kb.BF16):
+        values = 1 if enc in (kb.F32, kb.BF16) else 32 if enc in (kb.Q8_0, kb.IQ4_NL) else 256
+        ins = {8, 32, 40, 256, 264, 4096, 4100, 14336}
+        if enc == kb.F32:
+            ins |= {4 << 20, (4 << 20) + 8}
+        elif values == 256:
+            ins |= {(16 << 20) // 144 * 256, ((16 << 20) // 144 + 1) * 256}
+        for in_ in sorted(ins):
+            for out, rows in ((1, 1), (19, 3), (4096, 8), (5, 4096), (5, 4097)):
+                if in_ * rows > (1 << 24):
+                    continue
+                want = ref.gguf_batch_supported(in_, out, rows, enc)
+                job = SourceJobC(ctypes.pointer(ident), src, None, 0x1000, 0x2000, in_, out, rows, enc, 1)
+                got = bool(kb.lib.kb200_source_job_supported(ctypes.byref(job)))
+                if enc in no_decoder:
+                    assert not got
+                else:
+                    assert got == want, (enc, in_, out, rows, want)
+                checked += 1
+    assert checked > 300
