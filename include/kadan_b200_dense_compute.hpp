@@ -20,6 +20,8 @@
 #include <mutex>
 #include <span>
 #include <stdexcept>
+#include <string>
+#include <thread>
 #include <vector>
 
 #include "kadan/dense_compute.hpp"
@@ -29,22 +31,33 @@ namespace kadan::b200 {
 
 class Compute final : public DenseCompute {
 public:
-    // `fallback` serves every virtual this adapter does not override.
-    // `bank_bytes`: envelope of the resident weight bank on `device`;
-    // `scratch_bytes`: device memory kept free for projection workspaces.
-    Compute(std::shared_ptr<DenseCompute> fallback, int device, std::uint64_t bank_bytes,
+    // `fallback` serves every virtual this adapter does not override. One
+    // context and one resident weight bank per device in `devices`;
+    // `bank_bytes`: each bank's envelope; `scratch_bytes`: device memory kept
+    // free for projection workspaces. With several devices every job's output
+    // columns are split across them in proportion to the banks' envelopes, as
+    // the reference splits them (kb200_gguf_batch_partition).
+    Compute(std::shared_ptr<DenseCompute> fallback, std::vector<int> devices, std::uint64_t bank_bytes,
             std::uint64_t scratch_bytes)
-        : fallback_(std::move(fallback)), device_(device), scratch_(scratch_bytes) {
-        check(kb200_context_create(device, &ctx_));
-        if (const int s = kb200_bank_create_cuda(device, bank_bytes, scratch_bytes, &bank_)) {
-            kb200_context_destroy(ctx_);
-            check(s);
+        : fallback_(std::move(fallback)), scratch_(scratch_bytes) {
+        if (devices.empty())
+            throw std::invalid_argument("b200_devices");
+        for (const int d : devices) {
+            Device dev{d};
+            int s = kb200_context_create(d, &dev.ctx);
+            if (s == KB200_OK && (s = kb200_bank_create_cuda(d, bank_bytes, scratch_bytes, &dev.bank)) != KB200_OK)
+                kb200_context_destroy(dev.ctx);
+            if (s != KB200_OK) {
+                const std::string error = kb200_last_error();
+                close();
+                throw std::runtime_error(error);
+            }
+            devices_.push_back(dev);
         }
     }
 
     ~Compute() override {
-        kb200_bank_destroy(bank_);
-        kb200_context_destroy(ctx_);
+        close();
     }
 
     Compute(const Compute&) = delete;
@@ -55,21 +68,22 @@ public:
         Sources sources;
         std::vector<kb200_weight_identity> ids(jobs.size());
         std::vector<Source> users(jobs.size());
-        std::vector<kb200_source_job> out(jobs.size());
+        std::vector<kb200_source_job> full(jobs.size());
         for (std::size_t i = 0; i < jobs.size(); ++i) {
             const auto& j = jobs[i];
-            if (!j.identity || !j.source || !j.in || j.input.size() % j.in)
+            if (!j.identity || !j.source || !j.in || j.input.size() % j.in
+                || j.output.size() != j.input.size() / j.in * j.out)
                 return ProjectionResult::unsupported;
             ids[i] = identity(*j.identity);
             users[i] = {j.source, &sources};
-            out[i] = {&ids[i], &read_rows, &users[i], j.input.data(), j.output.data(),
-                      std::uint32_t(j.in), std::uint32_t(j.out), std::uint32_t(j.input.size() / j.in),
-                      j.encoding ? std::int32_t(*j.encoding) : KB200_F32, j.retain_misses ? 1 : 0};
+            full[i] = {&ids[i], &read_rows, &users[i], j.input.data(), j.output.data(), std::uint32_t(j.in),
+                       std::uint32_t(j.out), std::uint32_t(j.input.size() / j.in),
+                       j.encoding ? std::int32_t(*j.encoding) : KB200_F32, j.retain_misses ? 1 : 0};
+            // Every job is checked before any device reads a source.
+            if (!kb200_source_job_supported(&full[i]))
+                return ProjectionResult::unsupported;
         }
-        int result = KB200_RESULT_UNSUPPORTED;
-        const int s = kb200_dense_gguf_source_batch(ctx_, bank_, out.data(), out.size(), scratch_, cancel_byte(cancel),
-                                                    &result);
-        return finish(s, result, sources);
+        return run(full, nullptr, false, cancel, sources);
     }
 
     ProjectionResult dense_gguf_source(const WeightIdentity& id, gguf::Encoding encoding,
@@ -78,7 +92,8 @@ public:
                                        std::span<float> output, const std::atomic_bool& cancel, bool precise,
                                        bool retain_misses) override {
         std::lock_guard lock(mutex_);
-        if (!in || input.size() % in || (!bias.empty() && bias.size() != out))
+        if (!in || input.size() % in || output.size() != input.size() / in * out
+            || (!bias.empty() && bias.size() != out))
             return ProjectionResult::unsupported;
         Sources sources;
         Source user{&source, &sources};
@@ -86,10 +101,10 @@ public:
         const kb200_source_job job{&ident, &read_rows, &user, input.data(), output.data(), std::uint32_t(in),
                                    std::uint32_t(out), std::uint32_t(input.size() / in), std::int32_t(encoding),
                                    retain_misses ? 1 : 0};
-        int result = KB200_RESULT_UNSUPPORTED;
-        const int s = kb200_dense_gguf_source(ctx_, bank_, &job, bias.empty() ? nullptr : bias.data(), scratch_,
-                                              precise ? 1 : 0, cancel_byte(cancel), &result);
-        return finish(s, result, sources);
+        // The reference's fp64 path is not offered: unsupported, before any read.
+        if (precise || !kb200_source_job_supported(&job))
+            return ProjectionResult::unsupported;
+        return run(std::span(&job, 1), bias.empty() ? nullptr : bias.data(), true, cancel, sources);
     }
 
     void dense(std::span<const float> weights, std::span<const float> bias, std::span<const float> input,
@@ -98,30 +113,36 @@ public:
         fallback_->dense(weights, bias, input, in, out, output, cancel, precise);
     }
 
-    // -- weight residency: the bank's entries of these tensors retire too.
+    // -- weight residency: the banks' entries of these tensors retire too.
     Bytes release_weights(std::span<const WeightIdentity> sources) override {
         Bytes released = fallback_->release_weights(sources);
         std::lock_guard lock(mutex_);
         std::vector<kb200_weight_identity> ids;
         for (const auto& w : sources)
             ids.push_back(identity(w));
-        std::uint64_t ours = 0;
-        check(kb200_bank_release_sources(bank_, ids.data(), ids.size(), &ours));
-        return released + ours;
+        for (const auto& d : devices_) {
+            std::uint64_t ours = 0;
+            check(kb200_bank_release_sources(d.bank, ids.data(), ids.size(), &ours));
+            released += ours;
+        }
+        return released;
     }
 
     std::vector<DeviceWeightPlacement> weight_placement() const override {
         auto placement = fallback_->weight_placement();
-        kb200_bank_state st{};
-        if (kb200_bank_state_get(bank_, &st) == KB200_OK)
-            placement.push_back({device_, Bytes(st.capacity), Bytes(st.allocated)});
+        for (const auto& d : devices_) {
+            kb200_bank_state st{};
+            if (kb200_bank_state_get(d.bank, &st) == KB200_OK)
+                placement.push_back({d.id, Bytes(st.capacity), Bytes(st.allocated)});
+        }
         return placement;
     }
 
     void release_devices() override {
         {
             std::lock_guard lock(mutex_);
-            check(kb200_bank_release(bank_));
+            for (const auto& d : devices_)
+                check(kb200_bank_release(d.bank));
         }
         fallback_->release_devices();
     }
@@ -201,6 +222,12 @@ public:
     }
 
 private:
+    struct Device {
+        int id = 0;
+        kb200_context* ctx = nullptr;
+        kb200_bank* bank = nullptr;
+    };
+
     // The first exception a source threw during one call.
     struct Sources {
         std::mutex mutex;
@@ -210,6 +237,116 @@ private:
         const GgufWeightSource* fn = nullptr;
         Sources* sources = nullptr;
     };
+
+    // One job's columns on one device: the source shifted to the slice's
+    // first row and the slice's outputs staged for the scatter.
+    struct Slice {
+        std::size_t job = 0;
+        kb200_partition part{};
+        kb200_row_source fn = nullptr;
+        void* user = nullptr;
+        std::vector<float> staged;
+    };
+    struct Part {
+        std::vector<Slice> slices;
+        std::vector<kb200_source_job> jobs;
+        int status = KB200_OK, result = KB200_RESULT_UNSUPPORTED;
+        std::string error;
+    };
+
+    static int shifted_rows(void* user, std::uint64_t first_row, void* dst, std::uint64_t bytes) {
+        const auto* s = static_cast<const Slice*>(user);
+        return s->fn(s->user, s->part.first + first_row, dst, bytes);
+    }
+
+    void close() noexcept {
+        for (auto& d : devices_) {
+            kb200_bank_destroy(d.bank);
+            kb200_context_destroy(d.ctx);
+        }
+        devices_.clear();
+    }
+
+    // Runs supported jobs (one job with an optional bias when `single`), on
+    // one device directly, or split over the devices: each device's slices
+    // run on a thread of their own, every thread is joined, and only then are
+    // failures reported and outputs scattered (h3_compute.cu's device threads
+    // likewise finish before the call returns or throws).
+    ProjectionResult run(std::span<const kb200_source_job> jobs, const float* bias, bool single,
+                         const std::atomic_bool& cancel, Sources& sources) {
+        if (devices_.size() == 1) {
+            const Device& d = devices_[0];
+            int result = KB200_RESULT_UNSUPPORTED;
+            const int s = single ? kb200_dense_gguf_source(d.ctx, d.bank, jobs.data(), bias, scratch_, 0,
+                                                           cancel_byte(cancel), &result)
+                                 : kb200_dense_gguf_source_batch(d.ctx, d.bank, jobs.data(), jobs.size(), scratch_,
+                                                                 cancel_byte(cancel), &result);
+            return finish(s, result, sources);
+        }
+        std::vector<std::uint64_t> capacities;
+        for (const auto& d : devices_) {
+            kb200_bank_state st{};
+            check(kb200_bank_state_get(d.bank, &st));
+            capacities.push_back(st.capacity);
+        }
+        std::vector<Part> parts(devices_.size());
+        for (std::size_t d = 0; d < devices_.size(); ++d) {
+            Part& part = parts[d];
+            part.slices.reserve(jobs.size());  // slices are pointed at: no reallocation
+            for (std::size_t j = 0; j < jobs.size(); ++j) {
+                const auto& job = jobs[j];
+                Slice slice{j, {}, job.source, job.source_user, {}};
+                check(kb200_gguf_batch_partition(job.in, job.out, job.encoding, capacities.data(), capacities.size(),
+                                                 d, scratch_, &slice.part));
+                if (!slice.part.count)
+                    continue;
+                slice.staged.resize(std::size_t(job.rows) * slice.part.count);
+                part.slices.push_back(std::move(slice));
+                Slice& placed = part.slices.back();
+                kb200_source_job shifted = job;
+                shifted.source = &shifted_rows;
+                shifted.source_user = &placed;
+                shifted.output = placed.staged.data();
+                shifted.out = std::uint32_t(placed.part.count);
+                part.jobs.push_back(shifted);
+            }
+        }
+        std::vector<std::thread> threads;
+        for (std::size_t d = 0; d < devices_.size(); ++d) {
+            if (parts[d].jobs.empty())
+                continue;
+            threads.emplace_back([&, d] {
+                Part& part = parts[d];
+                const Device& dev = devices_[d];
+                const float* slice_bias = bias ? bias + part.slices[0].part.first : nullptr;
+                part.status = single ? kb200_dense_gguf_source(dev.ctx, dev.bank, part.jobs.data(), slice_bias,
+                                                               scratch_, 0, cancel_byte(cancel), &part.result)
+                                     : kb200_dense_gguf_source_batch(dev.ctx, dev.bank, part.jobs.data(),
+                                                                     part.jobs.size(), scratch_, cancel_byte(cancel),
+                                                                     &part.result);
+                if (part.status != KB200_OK)
+                    part.error = kb200_last_error();
+            });
+        }
+        for (auto& t : threads)
+            t.join();
+        if (sources.error)
+            std::rethrow_exception(sources.error);
+        bool finite = true;
+        for (const auto& part : parts) {
+            if (part.jobs.empty())
+                continue;
+            if (part.status != KB200_OK)
+                throw std::runtime_error(part.error);
+            finite = finite && part.result == KB200_RESULT_FINITE;
+        }
+        for (const auto& part : parts)
+            for (const auto& slice : part.slices) {
+                const auto& job = jobs[slice.job];
+                kb200_partition_scatter(&slice.part, slice.staged.data(), job.rows, job.output, job.out);
+            }
+        return finite ? ProjectionResult::finite : ProjectionResult::unvalidated;
+    }
 
     static_assert(sizeof(std::atomic_bool) == 1 && std::atomic_bool::is_always_lock_free,
                   "the ABI reads the cancel flag as one byte");
@@ -253,10 +390,8 @@ private:
     }
 
     std::shared_ptr<DenseCompute> fallback_;
-    int device_;
     std::uint64_t scratch_;
-    kb200_context* ctx_ = nullptr;
-    kb200_bank* bank_ = nullptr;
+    std::vector<Device> devices_;
     mutable std::mutex mutex_;  // the reference serialises DenseCompute calls (h3_compute.cu:1639)
 };
 

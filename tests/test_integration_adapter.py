@@ -24,7 +24,8 @@ def test_adapter_compiles_against_reference_interface(kb, tmp_path):
     tu.write_text(
         '#include "kadan_b200_dense_compute.hpp"\n'
         "std::unique_ptr<kadan::DenseCompute> make(std::shared_ptr<kadan::DenseCompute> f) {\n"
-        "    return std::make_unique<kadan::b200::Compute>(std::move(f), 0, 1ull << 30, 1ull << 30);\n"
+        "    return std::make_unique<kadan::b200::Compute>(std::move(f), std::vector<int>{0, 1}, 1ull << 30,\n"
+        "                                                  1ull << 30);\n"
         "}\n")
     lib = Path(kb.LIB_PATH)
     cmd = [cxx, "-std=c++20", "-Wall", "-Wextra", "-Werror", "-shared", "-fPIC", f"-I{ROOT / 'include'}",
