@@ -188,3 +188,40 @@ def test_expert_exchange_host_checks(kb):
     assert ret(None, 2880, 128, 2, 0, peers, 1024, 256, 2.0, None) == kb.INVALID
     assert ret(FAKE_Y + 4, 2880, 128, 2, 0, peers, 1024, 256, 2.0, None) == kb.INVALID
     assert ret(FAKE_Y, 2880, 128, 2, 0, peers, 0, 256, 2.0, None) == kb.INVALID
+
+
+def test_new_entry_points_reject_bad_arguments_on_host(kb):
+    """Bank, reader, shard and source-batch entry points refuse null handles
+    and bad arguments on the host, with a status and no crash."""
+    import ctypes
+
+    from kadan_b200 import gguf_file, shard, weight_bank  # noqa: F401 - declares the prototypes
+
+    L = kb.lib
+    out = ctypes.c_void_p()
+    assert L.kb200_bank_create(1024, None, ctypes.byref(out)) == kb.INVALID and not out.value
+    assert L.kb200_bank_find(None, None, ctypes.byref(out)) == kb.INVALID
+    assert L.kb200_bank_release(None) == kb.INVALID
+    assert L.kb200_bank_bound(None, 5) == kb.INVALID
+    assert L.kb200_bank_release_sources(None, None, 0, None) == kb.INVALID
+    L.kb200_bank_destroy(None)
+    assert L.kb200_gguf_open(None, None, ctypes.byref(out)) != kb.OK and not out.value
+    assert L.kb200_gguf_open(b"/nonexistent-dir-for-kb200", None, ctypes.byref(out)) == kb.IO
+    assert L.kb200_gguf_tensor_count(None) == 0
+    assert L.kb200_gguf_read_packed_rows(None, b"x", 0, 0, None, 0, None) == kb.INVALID
+    assert L.kb200_gguf_rows_source(None, 0, None, 0) == kb.INVALID
+    L.kb200_gguf_close(None)
+    assert L.kb200_shard_open(b"/nonexistent-dir-for-kb200", b"s.safetensors", None, ctypes.byref(out)) == kb.IO
+    assert L.kb200_shard_open(b".", b"../escape", None, ctypes.byref(out)) == kb.INVALID
+    assert L.kb200_shard_tensor_count(None) == 0
+    assert L.kb200_shard_load_mxfp4_expert_rows(None, b"p", 0, 0, 1, 1, None, 0, None, 0, None) == kb.INVALID
+    L.kb200_shard_close(None)
+    result = ctypes.c_int(7)
+    assert L.kb200_dense_gguf_source_batch(None, None, None, 0, 0, None, ctypes.byref(result)) == kb.UNSUPPORTED
+    assert result.value == kb.RESULT_UNSUPPORTED
+    assert L.kb200_dense_gguf_source(None, None, None, None, 0, 0, None, ctypes.byref(result)) == kb.UNSUPPORTED
+    assert L.kb200_context_set_read_lanes(None, 4) == kb.INVALID
+    assert L.kb200_source_job_supported(None) == 0
+    assert kb.lib.kb200_status_name(kb.QUARANTINED) == b"weight_cleanup_unconfirmed"
+    assert kb.lib.kb200_status_name(kb.NONFINITE_BIAS) == b"h3_cuda_nonfinite_bias"
+    assert kb.lib.kb200_status_name(kb.NONFINITE_OUTPUT) == b"h3_cuda_nonfinite_output"
