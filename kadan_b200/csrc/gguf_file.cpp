@@ -754,7 +754,8 @@ int kb200_gguf_rows_bind(const kb200_gguf* g, const char* name, uint64_t expert,
         return fail(KB200_INVALID, "null checkpoint or rows");
     return guarded([&] {
         const TensorEntry& t = find_tensor(g, name);
-        require(t.rank >= 2 && expert < t.shape[2], "gguf_expert_range");
+        require(t.rank >= 2, "gguf_row_range");
+        require(expert < t.shape[2], "gguf_expert_range");
         *rows = kb200_gguf_rows{g, uint64_t(&t - g->tensors.data()), expert};
     });
 }
