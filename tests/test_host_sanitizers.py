@@ -105,3 +105,20 @@ def test_readers_on_mutated_files_sanitized(tmp_path):
         args.append(f"shard:{e}/s.safetensors")
     out = run(exe, *args)
     assert out.strip().endswith("ok") and int(out.split()[0]) > 0
+
+
+def test_host_sources_build_warning_free(tmp_path):
+    """The host-only sources compile with -Wall -Wextra -Wpedantic -Werror,
+    the warning level the reference builds with."""
+    cxx, cuda_include = compiler()
+    for src in ("gguf_file.cpp", "safetensors.cpp", "weight_bank.cpp", "partition.cpp"):
+        cmd = [cxx, "-std=c++17", "-Wall", "-Wextra", "-Wpedantic", "-Werror", "-fsyntax-only", f"-I{ROOT / 'include'}",
+               f"-I{CSRC}", f"-I{cuda_include}", str(CSRC / src)]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        assert r.returncode == 0, (src, r.stderr[-2000:])
+    for header in ("read_team.hpp", "gguf_geometry.hpp"):
+        tu = tmp_path / "h.cpp"
+        tu.write_text(f'#include "{header}"\nint main() {{ return 0; }}\n')
+        r = subprocess.run([cxx, "-std=c++17", "-Wall", "-Wextra", "-Wpedantic", "-Werror", "-fsyntax-only",
+                            f"-I{ROOT / 'include'}", f"-I{CSRC}", str(tu)], capture_output=True, text=True)
+        assert r.returncode == 0, (header, r.stderr[-2000:])
