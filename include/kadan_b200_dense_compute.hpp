@@ -9,7 +9,9 @@
 // weight_placement also cover the B200 weight bank. Status codes map onto the
 // reference's conventions: KB200_UNSUPPORTED -> ProjectionResult::unsupported
 // (nothing read or written), KB200_OK -> the call's result, any other status
-// -> std::runtime_error with the library's message. An exception thrown by a
+// -> std::runtime_error: the reference's own message where the status stands
+// for one ("h3_cuda_cancelled", "h3_cuda_nonfinite_weight", ...), else the
+// library's text. An exception thrown by a
 // GgufWeightSource is rethrown after the call, as the reference propagates it.
 #pragma once
 
@@ -337,7 +339,7 @@ private:
             if (part.jobs.empty())
                 continue;
             if (part.status != KB200_OK)
-                throw std::runtime_error(part.error);
+                throw std::runtime_error(message(part.status, part.error.c_str()));
             finite = finite && part.result == KB200_RESULT_FINITE;
         }
         for (const auto& part : parts)
@@ -384,9 +386,26 @@ private:
         return result == KB200_RESULT_FINITE ? ProjectionResult::finite : ProjectionResult::unvalidated;
     }
 
+    // Statuses that stand for one of the reference's exception messages throw
+    // exactly that message (callers compare it); others carry the library's text.
+    static std::string message(int status, const char* detail) {
+        switch (status) {
+        case KB200_NONFINITE_WEIGHT:
+        case KB200_NONFINITE_INPUT:
+        case KB200_NONFINITE_BIAS:
+        case KB200_NONFINITE_OUTPUT:
+        case KB200_ALIAS:
+        case KB200_CANCELLED:
+        case KB200_QUARANTINED:
+            return kb200_status_name(status);
+        default:
+            return detail;
+        }
+    }
+
     static void check(int status) {
         if (status != KB200_OK)
-            throw std::runtime_error(kb200_last_error());
+            throw std::runtime_error(message(status, kb200_last_error()));
     }
 
     std::shared_ptr<DenseCompute> fallback_;
