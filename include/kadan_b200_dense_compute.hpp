@@ -11,8 +11,8 @@
 // (nothing read or written), KB200_OK -> the call's result, any other status
 // -> std::runtime_error: the reference's own message where the status stands
 // for one ("h3_cuda_cancelled", "h3_cuda_nonfinite_weight", ...), else the
-// library's text. An exception thrown by a
-// GgufWeightSource is rethrown after the call, as the reference propagates it.
+// library's text. An exception thrown by a GgufWeightSource is rethrown after
+// the call, as the reference propagates it.
 #pragma once
 
 #include <atomic>
