@@ -864,6 +864,81 @@ def run_source(args):
     print(json.dumps(line), flush=True)
 
 
+def run_h3_reference(args):
+    """--case h3-reference: the reference worker's own device GEMV
+    (IW/src/cuda/h3_compute.cu, built from the reference sources for sm_100a
+    into oracle/_ref/libh3_ref.so by the oracle recipe) over the config-2
+    decode stack: per dependency group, its job table copied and one launch per
+    encoding on the legacy stream, as dense_gguf_batch launches resident
+    chunks. Device time per step (CUDA events), the headline's bytes; also the
+    largest relative difference between its [gate, up] outputs of the last
+    layer and this library's."""
+    import torch
+
+    import kadan_b200 as kb
+
+    path = ROOT / "oracle" / "_ref" / "libh3_ref.so"
+    try:
+        L = ctypes.CDLL(str(path))
+    except OSError as e:
+        print(json.dumps({"case": "h3-reference", "unavailable": f"{path.name}: {e}"}), flush=True)
+        return
+    vp, sz, u32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint
+    L.h3ref_last_error.restype = ctypes.c_char_p
+    L.h3ref_job_bytes.restype = sz
+    L.h3ref_matvec_batch.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.POINTER(sz),
+                                     ctypes.POINTER(u32), ctypes.POINTER(u32), ctypes.POINTER(u32),
+                                     ctypes.POINTER(ctypes.c_int), sz, vp]
+    device = torch.device("cuda:0")
+    layers, acts, outs = build_stack(torch, kb, device)
+    inputs = ["x", "attn", "h", "g"]
+    calls = []
+    for mats in layers:
+        for gi, g in enumerate(GROUPS):
+            n = len(g)
+            calls.append(((vp * n)(*[mats[name].data_ptr() for name, _, _ in g]),
+                          (vp * n)(*[acts[inputs[gi]].data_ptr()] * n),
+                          (vp * n)(*[outs[name].data_ptr() for name, _, _ in g]),
+                          (sz * n)(*[weight_bytes(o, i) // o for _, o, i in g]),
+                          (u32 * n)(*[i for _, _, i in g]), (u32 * n)(*[o for _, o, _ in g]), (u32 * n)(*[1] * n),
+                          (ctypes.c_int * n)(*[kb.Q4_K] * n), n))
+    table = torch.empty(int(L.h3ref_job_bytes()) * 8, dtype=torch.uint8, device=device)
+
+    def step():
+        for c in calls:
+            if L.h3ref_matvec_batch(*c, table.data_ptr()):
+                raise RuntimeError(L.h3ref_last_error().decode())
+
+    # Parity of the baseline with this library on the last layer's [gate, up]
+    # (the outputs a step leaves behind).
+    step()
+    torch.cuda.synchronize()
+    theirs = {n: outs[n].clone() for n in ("gate", "up")}
+    jobs = [kb.gemv_job(kb.Q4_K, layers[-1][n], acts["h"], outs[n], in_=HIDDEN, columns=FFN, rows=1)
+            for n in ("gate", "up")]
+    kb.gguf_gemv_batch(jobs, torch.cuda.default_stream(device))
+    torch.cuda.synchronize()
+    diff = max(float((outs[n] - theirs[n]).abs().max() / max(float(theirs[n].abs().max()), 1.0))
+               for n in ("gate", "up"))
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 20))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    wbytes, abytes = step_bytes()
+    print(json.dumps({"case": "h3-reference", "ms_per_step": round(ms, 3),
+                      "gbps": round((wbytes + abytes) / (ms * 1e-3) / 1e9, 1), "steps": steps,
+                      "max_rel_diff_vs_ours": diff,
+                      "what": "reference device GEMV (gguf_matvec_batch_kernel, job table copied per group, legacy "
+                              "stream) over the config-2 decode stack"}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None, help="profiling case instead of the headline workload")
@@ -897,6 +972,8 @@ def main():
         run_ep(args, rank, world, local_rank)
     elif args.case == "source-batch":
         run_source(args)
+    elif args.case == "h3-reference":
+        run_h3_reference(args)
     elif args.case:
         run_case(args)
     elif args.impl == "reference":

@@ -31,6 +31,10 @@ def build(ref: bool = True) -> None:
     subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
     if ref and REFERENCE_TREE.exists():
         subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref"], check=True)
+        # The reference's device GEMV (a benchmark baseline only): best effort.
+        r = subprocess.run(["make", "-s", "-C", str(HERE), "ref-gpu"], capture_output=True, text=True)
+        if r.returncode:
+            print("oracle: reference GPU baseline not built:", r.stderr[-500:])
 
 
 def _p(a: np.ndarray, t):
