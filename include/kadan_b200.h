@@ -281,10 +281,11 @@ KB200_API int kb200_moe_forward(
 
 /* kb200_moe_forward without a caller workspace and without any allocation.
  * No counterpart in the reference: it exists for callers that cannot
- * allocate device memory per call — code running inside CUDA stream capture
- * (cudaMalloc/cudaFree are not capturable and synchronise the device) and
- * workers whose device memory is fully admitted to a budget ledger, as the
- * Hikari worker's resource accounting does. The scratch is one file-scope
+ * allocate device memory per call — workers whose device memory is fully
+ * admitted to a budget ledger before use, as the Hikari worker's resource
+ * accounting does, so an unplanned cudaMalloc would break their accounting,
+ * and callers that must not stall other streams (cudaMalloc and cudaFree can
+ * synchronise the whole device). The scratch is one file-scope
  * device array of KB200_MOE_STATIC_SCRATCH_BYTES (16 MiB) that every GPU
  * loading the library holds until the process exits; calls whose
  * kb200_moe_workspace_bytes exceeds it fail with KB200_NO_MEMORY before any

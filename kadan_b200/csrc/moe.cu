@@ -1298,8 +1298,10 @@ int kb200_rows_regroup(const void* src, void* dst, size_t row_bytes, const int64
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "rows_regroup_kernel launch");
 }
 
-// For callers that cannot allocate device memory per call (stream capture,
-// ledger-admitted workers): the same layer on the library's fixed scratch.
+// For callers that cannot allocate device memory per call (workers whose
+// device memory is admitted to a ledger in advance, callers that must not let
+// an allocation synchronise the device): the same layer on the library's
+// fixed scratch.
 // Allocates nothing; only the counts it must clear are reset (by the
 // asynchronous memset inside kb200_moe_forward), everything else it reads is
 // first written by the same call.

@@ -1,7 +1,7 @@
 """kb200_moe_forward_noalloc: the MoE layer for callers that cannot allocate
-device memory per call (code inside CUDA stream capture, where cudaMalloc is
-not capturable and synchronises the device, and workers whose device memory is
-fully admitted to a budget ledger). It must give the same result as
+device memory per call (workers whose device memory is fully admitted to a
+budget ledger before use, and callers that must not let cudaMalloc/cudaFree
+synchronise the device). It must give the same result as
 kb200_moe_forward with a caller workspace, call after call, while sharing one
 fixed 16 MiB device array. This file is collected last on purpose.
 """
