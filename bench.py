@@ -462,8 +462,55 @@ def moe_layer_inputs(torch, kb, dev, tokens, seed=0):
     return w, (gu_w, gu_s, dn_w, dn_s), x, logits, weight_bytes
 
 
+def mxfp4_to_ggml(blocks, scales, rows: int, cols: int):
+    """Exact repack of checkpoint MXFP4 rows (codes [rows, cols/2], value 2j in
+    the low nibble of byte j; E8M0 [rows, cols/32], value = e2m1 * 2^(E-127))
+    into ggml block_mxfp4 rows (GGML_TYPE_MXFP4 = 39: per 32 values the E8M0
+    byte, then 16 bytes whose low nibbles hold values 0..15 and high nibbles
+    16..31; ggml's doubled code table with its halved scale gives the same
+    value). Returns uint8 [rows, cols/32*17]."""
+    import numpy as np
+
+    b = np.asarray(blocks, dtype=np.uint8).reshape(rows, cols // 32, 16)
+    codes = np.stack([b & 15, b >> 4], axis=-1).reshape(rows, cols // 32, 32)
+    out = np.empty((rows, cols // 32, 17), dtype=np.uint8)
+    out[..., 0] = np.asarray(scales, dtype=np.uint8).reshape(rows, cols // 32)
+    out[..., 1:] = codes[..., :16] | (codes[..., 16:] << 4)
+    return out.reshape(rows, -1)
+
+
+def moe_cpu_layer(ref, oracle, x, logits, gu_ggml, dn_ggml, *, hidden: int, inter: int, experts: int, top_k: int,
+                  threads: int, limit: float = 7.0, alpha: float = 1.702):
+    """The MoE layer on the reference's host path: routing with the reference's
+    MoeLayer::forward semantics (oracle restatement, qwen_layers.cpp:397-491),
+    each expert's gathered rows through kadan::text::CpuMatvec on MXFP4 rows
+    (activations quantised to Q8_0 as the reference does, 64-column units on
+    `threads` workers), the gpt-oss SwiGLU on interleaved gate/up, and the
+    weighted sum in selection order. x: float32 [T, H]."""
+    import numpy as np
+
+    chosen, weight = oracle.moe_route(logits, top_k)
+    tokens = x.shape[0]
+    per_slot = np.zeros((tokens, top_k, hidden), dtype=np.float32)
+    for e in range(experts):
+        toks, slots = np.nonzero(chosen == e)
+        if not len(toks):
+            continue
+        gu = ref.cpu_matvec(39, gu_ggml[e * 2 * inter:(e + 1) * 2 * inter], x[toks], hidden, 2 * inter, threads)
+        gate = np.minimum(gu[:, 0::2], limit).astype(np.float64)
+        up = np.clip(gu[:, 1::2], -limit, limit)
+        act = (gate / (1.0 + np.exp(np.minimum(-alpha * gate, 700.0))) * (up + 1.0)).astype(np.float32)
+        per_slot[toks, slots] = ref.cpu_matvec(39, dn_ggml[e * hidden:(e + 1) * hidden], act, inter, hidden, threads)
+    out = np.zeros((tokens, hidden), dtype=np.float32)
+    for k in range(top_k):
+        out += weight[:, k:k + 1].astype(np.float32) * per_slot[:, k]
+    return out
+
+
 def run_moe(args):
-    """--case moe: the config-3 MoE layer at --tokens T (tokens/s, TFLOP/s)."""
+    """--case moe: the config-3 MoE layer at --tokens T (tokens/s, TFLOP/s),
+    with the reference's host path (moe_cpu_layer on all host threads) timed
+    on a bounded sample of the same tokens as cpu_baseline."""
     import torch
 
     import kadan_b200 as kb
@@ -484,9 +531,36 @@ def run_moe(args):
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
     flops = 2.0 * T * K * (2 * I * H + H * I)
-    print(json.dumps({"case": "moe-config3", "tokens": T, "ms_per_layer": round(ms, 4),
-                      "tokens_per_s": round(T / (ms * 1e-3), 1), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
-                      "all_expert_weight_gbps": round(weight_bytes / (ms * 1e-3) / 1e9, 1)}), flush=True)
+    line = {"case": "moe-config3", "tokens": T, "ms_per_layer": round(ms, 4),
+            "tokens_per_s": round(T / (ms * 1e-3), 1), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+            "all_expert_weight_gbps": round(weight_bytes / (ms * 1e-3) / 1e9, 1)}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = moe_cpu_baseline(keep, x, logits, T)
+    print(json.dumps(line), flush=True)
+
+
+def moe_cpu_baseline(keep, x, logits, tokens: int, min_seconds: float = 5.0) -> dict:
+    """The config-3 layer on the reference's host path (moe_cpu_layer), all host
+    threads, over the first min(tokens, 64) tokens, repeated until at least
+    `min_seconds` of host work has been timed."""
+    from oracle.pyoracle import Oracle, Reference
+
+    E, H, I, K = 32, 2880, 2880, 4
+    sample = min(tokens, 64)
+    gu_w, gu_s, dn_w, dn_s = (t.cpu().numpy() for t in keep)
+    gu_g, dn_g = mxfp4_to_ggml(gu_w, gu_s, E * 2 * I, H), mxfp4_to_ggml(dn_w, dn_s, E * H, I)
+    xs = x[:sample].float().cpu().numpy()
+    ls = logits[:sample].cpu().numpy()
+    ref, oracle, threads = Reference(), Oracle(), os.cpu_count() or 1
+    moe_cpu_layer(ref, oracle, xs[:1], ls[:1], gu_g, dn_g, hidden=H, inter=I, experts=E, top_k=K, threads=threads)
+    reps, t0 = 0, time.perf_counter()
+    while reps == 0 or time.perf_counter() - t0 < min_seconds:
+        moe_cpu_layer(ref, oracle, xs, ls, gu_g, dn_g, hidden=H, inter=I, experts=E, top_k=K, threads=threads)
+        reps += 1
+    s = time.perf_counter() - t0
+    return {"value": round(reps * sample / s, 1), "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"{sample} tokens of the layer x {reps} passes ({s:.1f} s): oracle routing, CpuMatvec "
+                      "(ggml MXFP4, Q8_0 activations) experts from oracle/_ref, gpt-oss SwiGLU, selection-order combine"}
 
 
 def run_prefill(args):
