@@ -341,18 +341,54 @@ def cpu_baseline(layers, kb, budget_s: float = 15.0):
                 for n, o, i in g:
                     orc.gemv_f64(1, mats[n][: max(1, o // 64)], x[i], i, max(1, o // 64))
 
-    one_layer()
-    t0, n = time.perf_counter(), 0
-    while time.perf_counter() - t0 < budget_s:
-        one_layer()
-        n += 1
-    dt = (time.perf_counter() - t0) / n
+    dt, n = timed_repeats(one_layer, budget_s)
     per_layer = layer_weight_bytes() if kind == "reference" else sum(
         weight_bytes(max(1, o // 64), i) for g in GROUPS for _, o, i in g)
-    return {"value": round(per_layer / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": kind,
-            "sample": f"layer 0 of the stack (7 matrices, {per_layer} weight bytes) x {n} repetitions, "
-                      f"{round(dt * n, 1)} s; kadan::text::CpuMatvec 64-column units, activations quantized "
-                      f"to Q8_K once per input as the reference does"}
+    out = {"value": round(per_layer / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+           "sample": f"layer 0 of the stack (7 matrices, {per_layer} weight bytes) x {n} repetitions, "
+                     f"{round(dt * n, 1)} s; kadan::text::CpuMatvec 64-column units, activations quantized "
+                     f"to Q8_K once per input as the reference does"}
+    if kind == "reference":
+        out["single_core"] = single_core_baselines(ref, Oracle(), mats, x)
+    return out
+
+
+def timed_repeats(fn, budget_s: float):
+    """Seconds per call of `fn` (one untimed call first), repeated for at least `budget_s`."""
+    fn()
+    t0, n = time.perf_counter(), 0
+    while n == 0 or time.perf_counter() - t0 < budget_s:
+        fn()
+        n += 1
+    return (time.perf_counter() - t0) / n, n
+
+
+def single_core_baselines(ref, oracle, mats, x, budget_s: float = 3.0) -> dict:
+    """The other host figures of the decode path, each on one core, GB/s of
+    Q4_K weight bytes: the reference's CpuMatvec with one worker over layer 0
+    (its production host path), and the scalar restatement (decode each
+    block, fp64 dot: the oracle's gemv) over the first 512 columns of each
+    of layer 0's matrices."""
+    def cpu_matvec_one():
+        for g in GROUPS:
+            for n, o, i in g:
+                ref.cpu_matvec(12, mats[n], x[i], i, o, threads=1)
+
+    cols = 512
+
+    def scalar():
+        for g in GROUPS:
+            for n, o, i in g:
+                oracle.gemv_f64(1, mats[n][:cols], x[i], i, cols)
+
+    dt1, n1 = timed_repeats(cpu_matvec_one, budget_s)
+    dt2, n2 = timed_repeats(scalar, budget_s)
+    scalar_bytes = sum(weight_bytes(cols, i) for g in GROUPS for _, _, i in g)
+    return {"cpu_matvec_1_core_gbps": round(layer_weight_bytes() / dt1 / 1e9, 3),
+            "cpu_matvec_1_core_sample": f"layer 0 x {n1}",
+            "scalar_restatement_1_core_gbps": round(scalar_bytes / dt2 / 1e9, 3),
+            "scalar_restatement_1_core_sample": f"first {cols} columns of each layer-0 matrix x {n2} "
+                                                "(oracle Q4_K decode + fp64 dot)"}
 
 
 def run_reference(args, rank, world):
@@ -560,7 +596,23 @@ def moe_cpu_baseline(keep, x, logits, tokens: int, min_seconds: float = 5.0) -> 
     s = time.perf_counter() - t0
     return {"value": round(reps * sample / s, 1), "unit": "tokens/s", "cores": threads, "kind": "reference",
             "sample": f"{sample} tokens of the layer x {reps} passes ({s:.1f} s): oracle routing, CpuMatvec "
-                      "(ggml MXFP4, Q8_0 activations) experts from oracle/_ref, gpt-oss SwiGLU, selection-order combine"}
+                      "(ggml MXFP4, Q8_0 activations) experts from oracle/_ref, gpt-oss SwiGLU, selection-order combine",
+            "single_core": mxfp4_single_core(ref, gu_w, gu_s, gu_g, xs[0], H, I)}
+
+
+def mxfp4_single_core(ref, gu_w, gu_s, gu_g, x, hidden: int, inter: int, budget_s: float = 3.0) -> dict:
+    """One expert's fused gate/up matrix (2*inter x hidden MXFP4) times one
+    token on one core, GB/s of MXFP4 bytes: the reference's numerical path
+    quantization::matvec (checkpoint layout, fp64 accumulation) and its
+    production host path CpuMatvec on the repacked ggml rows."""
+    rows = 2 * inter
+    w, sc = gu_w[:rows], gu_s[:rows]
+    nbytes = w.nbytes + sc.nbytes
+    dt1, n1 = timed_repeats(lambda: ref.mxfp4_matvec(w, sc, rows, hidden, x), budget_s)
+    dt2, n2 = timed_repeats(lambda: ref.cpu_matvec(39, gu_g[:rows], x, hidden, rows, 1), budget_s)
+    return {"quantization_matvec_1_core_gbps": round(nbytes / dt1 / 1e9, 3),
+            "cpu_matvec_mxfp4_1_core_gbps": round(nbytes / dt2 / 1e9, 3),
+            "sample": f"expert 0 gate/up ({rows}x{hidden}, {nbytes} bytes), one token, x {n1} and x {n2}"}
 
 
 def run_prefill(args):
