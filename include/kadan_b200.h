@@ -209,8 +209,9 @@ typedef struct kb200_host_job {
 #define KB200_RESULT_FINITE 2
 
 /* DenseCompute::dense_gguf_batch (IW/src/cuda/h3_compute.cu:3963-4375):
- * synchronous. Unsupported jobs return KB200_UNSUPPORTED (result
- * UNSUPPORTED) before any read or write; identical input spans upload once;
+ * synchronous. A cancel byte already set fails the call with KB200_CANCELLED
+ * first; then an empty batch or any unsupported job returns KB200_UNSUPPORTED
+ * (result UNSUPPORTED) before any read or write; identical input spans upload once;
  * non-finite inputs fail with KB200_NONFINITE_INPUT, outputs overlapping any
  * input with KB200_ALIAS; then one input upload, one launch per encoding, one
  * download of outputs plus the weight status word, and KB200_NONFINITE_WEIGHT

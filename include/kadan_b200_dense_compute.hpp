@@ -66,6 +66,12 @@ public:
     Compute& operator=(const Compute&) = delete;
 
     ProjectionResult dense_gguf_batch(std::span<const GgufBatchJob> jobs, const std::atomic_bool& cancel) override {
+        // A cancelled call throws before anything else, an empty batch is
+        // unsupported (h3_compute.cu:3966-3968).
+        if (cancel.load())
+            throw std::runtime_error(kb200_status_name(KB200_CANCELLED));
+        if (jobs.empty())
+            return ProjectionResult::unsupported;
         std::lock_guard lock(mutex_);
         Sources sources;
         std::vector<kb200_weight_identity> ids(jobs.size());
@@ -314,24 +320,32 @@ private:
             }
         }
         std::vector<std::thread> threads;
-        for (std::size_t d = 0; d < devices_.size(); ++d) {
-            if (parts[d].jobs.empty())
-                continue;
-            threads.emplace_back([&, d] {
-                Part& part = parts[d];
-                const Device& dev = devices_[d];
-                const float* slice_bias = bias ? bias + part.slices[0].part.first : nullptr;
-                part.status = single ? kb200_dense_gguf_source(dev.ctx, dev.bank, part.jobs.data(), slice_bias,
-                                                               scratch_, 0, cancel_byte(cancel), &part.result)
-                                     : kb200_dense_gguf_source_batch(dev.ctx, dev.bank, part.jobs.data(),
-                                                                     part.jobs.size(), scratch_, cancel_byte(cancel),
-                                                                     &part.result);
-                if (part.status != KB200_OK)
-                    part.error = kb200_last_error();
-            });
+        std::exception_ptr spawn_error;
+        try {
+            for (std::size_t d = 0; d < devices_.size(); ++d) {
+                if (parts[d].jobs.empty())
+                    continue;
+                threads.emplace_back([&, d] {
+                    Part& part = parts[d];
+                    const Device& dev = devices_[d];
+                    const float* slice_bias = bias ? bias + part.slices[0].part.first : nullptr;
+                    part.status = single ? kb200_dense_gguf_source(dev.ctx, dev.bank, part.jobs.data(), slice_bias,
+                                                                   scratch_, 0, cancel_byte(cancel), &part.result)
+                                         : kb200_dense_gguf_source_batch(dev.ctx, dev.bank, part.jobs.data(),
+                                                                         part.jobs.size(), scratch_,
+                                                                         cancel_byte(cancel), &part.result);
+                    if (part.status != KB200_OK)
+                        part.error = kb200_last_error();
+                });
+            }
+        } catch (...) {
+            // A thread that could not start: the started ones finish first.
+            spawn_error = std::current_exception();
         }
         for (auto& t : threads)
             t.join();
+        if (spawn_error)
+            std::rethrow_exception(spawn_error);
         if (sources.error)
             std::rethrow_exception(sources.error);
         bool finite = true;

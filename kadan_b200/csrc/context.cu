@@ -206,10 +206,11 @@ int kb200_dense_gguf_batch(
 ) {
     if (result)
         *result = KB200_RESULT_UNSUPPORTED;
+    // Cancellation first, then an empty batch is unsupported (h3_compute.cu:3966-3968).
+    if (c && cancelled(cancel))
+        return fail(KB200_CANCELLED, "cancelled before start");
     if (!c || !jobs || !count)
         return fail(KB200_UNSUPPORTED, "empty batch");
-    if (cancelled(cancel))
-        return fail(KB200_CANCELLED, "cancelled before start");
     // Unsupported precedes every read and write (gguf_batch_supported).
     for (size_t j = 0; j < count; ++j) {
         const auto& job = jobs[j];
@@ -334,10 +335,11 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
                                   uint64_t scratch_limit, const volatile uint8_t* cancel, int* result) {
     if (result)
         *result = KB200_RESULT_UNSUPPORTED;
+    // Cancellation first, then an empty batch is unsupported (h3_compute.cu:3966-3968).
+    if (c && cancelled(cancel))
+        return fail(KB200_CANCELLED, "cancelled before start");
     if (!c || !jobs || !count)
         return fail(KB200_UNSUPPORTED, "empty batch");
-    if (cancelled(cancel))
-        return fail(KB200_CANCELLED, "cancelled before start");
     // Unsupported precedes every source read and output write (gguf_batch_supported).
     for (size_t j = 0; j < count; ++j)
         if (!source_job_supported(jobs[j]))

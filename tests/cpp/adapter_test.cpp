@@ -185,6 +185,12 @@ int kb200_dense_gguf_source_batch(kb200_context* ctx, kb200_bank*, const kb200_s
         }
         project(packed, job.in, job.out, job.encoding, job.input, job.rows, job.output);
     }
+    // The library reads the caller's flag between chunks too.
+    if (cancel && *cancel) {
+        d.saw_cancel = true;
+        last_error = "cancelled";
+        return KB200_CANCELLED;
+    }
     if (d.status != KB200_OK) {
         last_error = d.error;
         return d.status;
@@ -241,6 +247,7 @@ struct Matrix {
     std::mutex mutex;
     std::multiset<std::size_t> rows_read;
     bool throw_on_read = false;
+    std::atomic_bool* cancel_on_read = nullptr;
     DenseCompute::GgufWeightSource source;
 
     Matrix(std::uint32_t in_, std::uint32_t out_, int encoding_, unsigned seed)
@@ -269,6 +276,8 @@ struct Matrix {
         source = [this](std::size_t first, std::span<std::byte> dst) {
             if (throw_on_read)
                 throw std::out_of_range("source_row_missing");
+            if (cancel_on_read)
+                *cancel_on_read = true;
             const std::size_t rb = row_bytes(in, encoding);
             CHECK(dst.size() % rb == 0 && first + dst.size() / rb <= out);
             std::memcpy(dst.data(), bytes.data() + first * rb, dst.size());
@@ -457,9 +466,20 @@ void failures() {
         device_of(ids.back()).result = KB200_RESULT_UNVALIDATED;
         CHECK(compute.dense_gguf_batch(jobs, cancel) == ProjectionResult::unvalidated);
         device_of(ids.back()).result = KB200_RESULT_FINITE;
+        // Cancelled on entry: thrown before any device call (h3_compute.cu:3966),
+        // also for an empty batch; an empty batch is otherwise unsupported.
+        const int calls = device_of(0).calls;
         cancel = true;
         CHECK(thrown([&] { compute.dense_gguf_batch(jobs, cancel); }) == "h3_cuda_cancelled");
+        CHECK(thrown([&] { compute.dense_gguf_batch({}, cancel); }) == "h3_cuda_cancelled");
+        CHECK(device_of(0).calls == calls && !device_of(0).saw_cancel);
+        cancel = false;
+        CHECK(compute.dense_gguf_batch({}, cancel) == ProjectionResult::unsupported);
+        // Cancelled while the sources are read: the devices see the caller's flag.
+        a.cancel_on_read = &cancel;
+        CHECK(thrown([&] { compute.dense_gguf_batch(jobs, cancel); }) == "h3_cuda_cancelled");
         CHECK(device_of(0).saw_cancel);
+        a.cancel_on_read = nullptr;
         cancel = false;
         // A source's own exception comes back as itself, after every device finished.
         a.throw_on_read = true;
