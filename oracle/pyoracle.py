@@ -10,6 +10,7 @@ this module, and only to check or time against the CUDA path.
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from pathlib import Path
 
@@ -18,7 +19,8 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libkadan_ref.so"
-REFERENCE_TREE = Path("/root/reference")
+# The reference checkout the recipes build from (KADAN_REFERENCE overrides).
+REFERENCE_TREE = Path(os.environ.get("KADAN_REFERENCE", "/root/reference"))
 
 _u8p = ctypes.POINTER(ctypes.c_uint8)
 _f32p = ctypes.POINTER(ctypes.c_float)
@@ -30,9 +32,10 @@ def build(ref: bool = True) -> None:
     """make the oracle (and the reference build when its sources are present)."""
     subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
     if ref and REFERENCE_TREE.exists():
-        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref"], check=True)
+        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), f"REF={REFERENCE_TREE}", "ref"], check=True)
         # The reference's device GEMV (a benchmark baseline only): best effort.
-        r = subprocess.run(["make", "-s", "-C", str(HERE), "ref-gpu"], capture_output=True, text=True)
+        r = subprocess.run(["make", "-s", "-C", str(HERE), f"REF={REFERENCE_TREE}", "ref-gpu"], capture_output=True,
+                           text=True)
         if r.returncode:
             print("oracle: reference GPU baseline not built:", r.stderr[-500:])
 
