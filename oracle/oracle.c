@@ -63,7 +63,10 @@ size_t orc_block_values(int e) {
     case ORC_Q3_K:
     case ORC_Q4_K:
     case ORC_Q6_K:
-    case ORC_IQ4_XS: return 256;
+    case ORC_IQ4_XS:
+    case ORC_IQ3_XXS:
+    case ORC_IQ2_S:
+    case ORC_IQ3_S: return 256;
     default: return 0;
     }
 }
@@ -76,6 +79,9 @@ size_t orc_block_bytes(int e) {
     case ORC_Q6_K: return 210;
     case ORC_IQ4_NL: return 18;
     case ORC_IQ4_XS: return 136;
+    case ORC_IQ3_XXS: return 98;
+    case ORC_IQ2_S: return 82;
+    case ORC_IQ3_S: return 110;
     case ORC_BF16: return 2;
     default: return 0;
     }
@@ -97,6 +103,29 @@ static void q4k_scale_min(const uint8_t* s, unsigned g, unsigned* sc, unsigned* 
         *sc = (s[g + 4] & 15u) | ((unsigned)(s[g - 4] >> 6) << 4);
         *m = (unsigned)(s[g + 4] >> 4) | ((unsigned)(s[g] >> 6) << 4);
     }
+}
+
+/* Code grids of the three grid-coded formats: each entry packs four (IQ3_XXS,
+ * IQ3_S) or eight (IQ2_S) unsigned magnitudes, one per byte, low byte first. */
+static uint32_t grid_iq3xxs[256], grid_iq3s[512];
+static uint64_t grid_iq2s[1024];
+static int grids_set;
+
+void orc_set_iq_grids(const uint32_t* iq3xxs, const uint64_t* iq2s, const uint32_t* iq3s) {
+    memcpy(grid_iq3xxs, iq3xxs, sizeof grid_iq3xxs);
+    memcpy(grid_iq2s, iq2s, sizeof grid_iq2s);
+    memcpy(grid_iq3s, iq3s, sizeof grid_iq3s);
+    grids_set = 1;
+}
+
+static uint32_t le32(const uint8_t* p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+/* Sign of lane j of an 8-value run: bit j of `signs`. The product with -1 or
+ * +1 is kept as a product, as the reference writes it. */
+static float signed_by(float magnitude, unsigned signs, unsigned j) {
+    return magnitude * ((signs >> j) & 1u ? -1.0f : 1.0f);
 }
 
 /* One value of one block (gguf_quantization.hpp:631-762). */
@@ -158,6 +187,49 @@ float orc_decode(int e, const uint8_t* b, size_t element) {
         const unsigned packed = b[8 + g * 16 + w % 16];
         const float factor = half_at(b) * (float)scale;
         return factor * (float)iq4nl_book[w < 16 ? packed & 15u : packed >> 4];
+    }
+    case ORC_IQ3_XXS: {
+        /* 98 bytes: half d, 64 grid indices (two per 8-value run), then per
+         * 32 values a little-endian word: scale nibble in bits 28-31 and four
+         * 7-bit sign sets, whose eighth sign makes the set's parity even
+         * (gguf_quantization.hpp:674-694). */
+        if (!grids_set)
+            return NAN;
+        const unsigned g = el / 32, run = (el % 32) / 8, j = el % 8;
+        const uint32_t word = le32(b + 66 + 4 * g);
+        const float scale = (half_at(b) * (0.5f + (float)(word >> 28))) * 0.5f;
+        unsigned signs = (word >> (7 * run)) & 127u, ones = 0;
+        for (unsigned t = signs; t; t &= t - 1)
+            ++ones;
+        signs |= (ones & 1u) << 7;
+        const uint32_t entry = grid_iq3xxs[b[2 + 8 * g + 2 * run + j / 4]];
+        return signed_by(scale * (float)((entry >> (8 * (j % 4))) & 255u), signs, j);
+    }
+    case ORC_IQ2_S: {
+        /* 82 bytes: half d, 32 low index bytes (one per 8-value run), 32 sign
+         * bytes, 8 bytes of two high index bits per run, 8 scale bytes of two
+         * nibbles (runs 0-1, runs 2-3) (gguf_quantization.hpp:702-717). */
+        if (!grids_set)
+            return NAN;
+        const unsigned g = el / 32, run = (el % 32) / 8, j = el % 8;
+        const unsigned nibble = run < 2 ? b[74 + g] & 15u : (unsigned)b[74 + g] >> 4;
+        const float scale = (half_at(b) * (0.5f + (float)nibble)) * 0.25f;
+        const unsigned index = b[2 + 4 * g + run] | ((((unsigned)b[66 + g] >> (2 * run)) & 3u) << 8);
+        const unsigned magnitude = (unsigned)(grid_iq2s[index] >> (8 * j)) & 255u;
+        return signed_by(scale * (float)magnitude, b[34 + 4 * g + run], j);
+    }
+    case ORC_IQ3_S: {
+        /* 110 bytes: half d, 64 low index bytes (two per run), 8 bytes of one
+         * high index bit each, 32 sign bytes, 4 scale bytes of two nibbles
+         * (odd scale 1 + 2n per 32 values) (gguf_quantization.hpp:719-734). */
+        if (!grids_set)
+            return NAN;
+        const unsigned g = el / 32, run = (el % 32) / 8, j = el % 8, k = 2 * run + j / 4;
+        const unsigned nibble = g & 1u ? (unsigned)b[106 + g / 2] >> 4 : b[106 + g / 2] & 15u;
+        const float scale = half_at(b) * (float)(1 + 2 * (int)nibble);
+        const unsigned index = b[2 + 8 * g + k] | ((((unsigned)b[66 + g] >> k) & 1u) << 8);
+        const unsigned magnitude = (grid_iq3s[index] >> (8 * (j % 4))) & 255u;
+        return signed_by(scale * (float)magnitude, b[74 + 4 * g + run], j);
     }
     default:
         return NAN;

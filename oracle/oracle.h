@@ -20,8 +20,11 @@ enum orc_encoding {
     ORC_Q4_K = 1,
     ORC_Q8_0 = 2,
     ORC_Q6_K = 3,
+    ORC_IQ3_XXS = 4,
     ORC_IQ4_NL = 5,
     ORC_IQ4_XS = 6,
+    ORC_IQ2_S = 7,
+    ORC_IQ3_S = 8,
     ORC_BF16 = 9
 };
 
@@ -29,6 +32,10 @@ float orc_half(uint16_t bits);
 size_t orc_block_values(int encoding);
 size_t orc_block_bytes(int encoding);
 float orc_decode(int encoding, const uint8_t* block, size_t element);
+/* The IQ3_XXS, IQ2_S and IQ3_S code grids (256, 1024 and 512 entries; ggml's
+ * iq3xxs_grid, iq2s_grid and iq3s_grid, the reference's
+ * gguf_quantization.hpp:99-495), copied; until set, those encodings decode to NaN. */
+void orc_set_iq_grids(const uint32_t* iq3xxs, const uint64_t* iq2s, const uint32_t* iq3s);
 void orc_decode_stream(int encoding, const uint8_t* packed, size_t count, float* out);
 
 /* y[r*y_stride + c] = sum_k decode(W[c,k]) * x[r*in + k], double accumulation. */

@@ -68,7 +68,15 @@ class Oracle:
                                                               ctypes.c_float, ctypes.c_int, _f32p]
         L.orc_bf16_round.restype = ctypes.c_float
         L.orc_bf16_round.argtypes = [ctypes.c_float]
+        L.orc_set_iq_grids.argtypes = [ctypes.c_void_p] * 3
         self.L = L
+
+    def set_iq_grids(self, grids) -> None:
+        """Copy the (iq3xxs[256] u32, iq2s[1024] u64, iq3s[512] u32) grids in."""
+        a, b, c = (np.ascontiguousarray(g) for g in grids)
+        assert a.dtype == np.uint32 and a.size == 256 and b.dtype == np.uint64 and b.size == 1024
+        assert c.dtype == np.uint32 and c.size == 512
+        self.L.orc_set_iq_grids(a.ctypes.data, b.ctypes.data, c.ctypes.data)
 
     def half(self, bits: int) -> float:
         return self.L.orc_half(bits)
@@ -347,6 +355,16 @@ class Reference:
         out = np.empty(count, dtype=np.float32)
         self.L.ref_gguf_decode_stream(e, _p(packed, _u8p), count, _p(out, _f32p))
         return out
+
+    def iq_grids(self):
+        """The reference's IQ3_XXS, IQ2_S and IQ3_S code grids, copied out:
+        (uint32[256], uint64[1024], uint32[512])."""
+        ptrs = [ctypes.c_void_p() for _ in range(3)]
+        self.L.ref_iq_grids(*(ctypes.byref(p) for p in ptrs))
+        out = []
+        for p, n, t in zip(ptrs, (256, 1024, 512), (ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32)):
+            out.append(np.ctypeslib.as_array((t * n).from_address(p.value)).copy())
+        return tuple(out)
 
     def decode_runs(self, e: int, packed: np.ndarray, count: int) -> np.ndarray:
         packed = np.ascontiguousarray(packed, dtype=np.uint8)

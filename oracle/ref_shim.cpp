@@ -51,6 +51,14 @@ float ref_gguf_decode(int encoding, const unsigned char* block, size_t element) 
     return kadan::gguf::decode(kadan::gguf::Encoding(encoding), block, element);
 }
 
+// The reference's own code grids of IQ3_XXS, IQ2_S and IQ3_S
+// (gguf_quantization.hpp:501-504), as a caller passes them to kb200_set_iq_grids.
+void ref_iq_grids(const uint32_t** iq3xxs, const uint64_t** iq2s, const uint32_t** iq3s) {
+    *iq3xxs = kadan::gguf::detail::iq3xxs_grid_host;
+    *iq2s = kadan::gguf::detail::iq2s_grid_host;
+    *iq3s = kadan::gguf::detail::iq3s_grid_host;
+}
+
 size_t ref_gguf_block_values(int encoding) {
     return kadan::gguf::block_values(kadan::gguf::Encoding(encoding));
 }

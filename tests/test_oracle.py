@@ -17,7 +17,7 @@ import pytest
 
 from conftest import GOLDEN, rel_err
 
-Q3_K, Q4_K, Q8_0, Q6_K, IQ4_NL, IQ4_XS, BF16 = 0, 1, 2, 3, 5, 6, 9
+Q3_K, Q4_K, Q8_0, Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS, IQ2_S, IQ3_S, BF16 = 0, 1, 2, 3, 4, 5, 6, 7, 8, 9
 
 
 def bits(v):
@@ -77,10 +77,17 @@ def _golden_blocks():
     return json.loads((GOLDEN / "gguf_blocks.json").read_text())["encodings"]
 
 
-@pytest.mark.parametrize("name", ["q8_0", "q4_k", "q6_k", "q3_k", "iq4_nl", "iq4_xs", "bf16"])
-def test_reference_blocks_digest(oracle, name):
+GRID_CODED = {"iq3_xxs": IQ3_XXS, "iq2_s": IQ2_S, "iq3_s": IQ3_S}
+
+
+@pytest.mark.parametrize("name", ["q8_0", "q4_k", "q6_k", "q3_k", "iq4_nl", "iq4_xs", "bf16", *GRID_CODED])
+def test_reference_blocks_digest(oracle, name, request):
+    """The grid-coded formats decode through code grids that the caller
+    supplies; here the reference's own, as the worker would pass them."""
     from golden.make_golden import canonical_digest, reference_blocks
 
+    if name in GRID_CODED:
+        oracle.set_iq_grids(request.getfixturevalue("ref").iq_grids())
     spec = _golden_blocks()[name]
     blocks = reference_blocks(spec["encoding"], spec["trials"])
     assert hashlib.sha256(blocks.tobytes()).hexdigest() == spec["sha256_blocks"]
@@ -90,10 +97,11 @@ def test_reference_blocks_digest(oracle, name):
     assert int(np.isnan(got).sum()) == spec["nan_count"]
 
 
-@pytest.mark.parametrize("enc", [Q8_0, Q4_K, Q6_K, Q3_K, IQ4_NL, IQ4_XS])
+@pytest.mark.parametrize("enc", [Q8_0, Q4_K, Q6_K, Q3_K, IQ4_NL, IQ4_XS, IQ3_XXS, IQ2_S, IQ3_S])
 def test_oracle_equals_reference_decode_and_runs(oracle, ref, enc):
     from golden.make_golden import reference_blocks
 
+    oracle.set_iq_grids(ref.iq_grids())
     blocks = reference_blocks(enc, 256)
     n = blocks.shape[0] * oracle.block_values(enc)
     mine = oracle.decode(enc, blocks, n)
