@@ -73,8 +73,18 @@ KB200_API const char* kb200_status_name(int status);
 /* Text of the last failure on the calling thread. */
 KB200_API const char* kb200_last_error(void);
 KB200_API int kb200_version(void);
-/* 1 if `encoding` has a device decoder (gguf::supported, gguf_quantization.hpp:57-63). */
+/* 1 if `encoding` has a device decoder (gguf::supported, gguf_quantization.hpp:57-63):
+ * IQ3_XXS, IQ2_S and IQ3_S only once their code grids are registered. */
 KB200_API int kb200_encoding_supported(int encoding);
+/* Registers the code grids of IQ3_XXS, IQ2_S and IQ3_S (copied): 256, 1024 and
+ * 512 entries, ggml's iq3xxs_grid, iq2s_grid and iq3s_grid, which the worker
+ * holds as kadan::gguf::detail::iq3xxs_grid_host, iq2s_grid_host and
+ * iq3s_grid_host (IW/include/kadan/gguf_quantization.hpp:501-504). Until this
+ * call those encodings are unsupported. Registering the same grids again is a
+ * no-op; other values fail with KB200_INVALID. The first dequant or GEMV of
+ * one of these encodings on a device copies the grids to it synchronously
+ * (once per device), so make that first call outside any stream capture. */
+KB200_API int kb200_set_iq_grids(const uint32_t* iq3xxs_grid, const uint64_t* iq2s_grid, const uint32_t* iq3s_grid);
 KB200_API size_t kb200_block_values(int encoding);
 KB200_API size_t kb200_block_bytes(int encoding);
 

@@ -44,6 +44,9 @@ public:
         : fallback_(std::move(fallback)), scratch_(scratch_bytes) {
         if (devices.empty())
             throw std::invalid_argument("b200_devices");
+        // IQ3_XXS, IQ2_S and IQ3_S decode with the worker's own code grids.
+        check(kb200_set_iq_grids(gguf::detail::iq3xxs_grid_host, gguf::detail::iq2s_grid_host,
+                                 gguf::detail::iq3s_grid_host));
         for (const int d : devices) {
             Device dev{d};
             int s = kb200_context_create(d, &dev.ctx);

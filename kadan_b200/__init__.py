@@ -133,6 +133,7 @@ def _load() -> ctypes.CDLL:
     lib.kb200_block_bytes.restype = c_size
     lib.kb200_block_bytes.argtypes = [c_int]
     lib.kb200_gguf_dequant.argtypes = [c_int, vp, c_size, vp, vp, vp]
+    lib.kb200_set_iq_grids.argtypes = [vp, vp, vp]
     lib.kb200_gguf_gemv_batch.argtypes = [ctypes.POINTER(GemvJob), c_size, vp]
     lib.kb200_gemv_path.argtypes = [ctypes.POINTER(GemvJob)]
     lib.kb200_gguf_gemm_workspace_bytes.restype = c_size
@@ -196,6 +197,19 @@ def _stream_ptr(stream) -> Optional[int]:
 
 def _ptr(t) -> Optional[int]:
     return None if t is None else t.data_ptr()
+
+
+def set_iq_grids(iq3xxs, iq2s, iq3s) -> None:
+    """kb200_set_iq_grids: the IQ3_XXS, IQ2_S and IQ3_S code grids (host
+    arrays of uint32[256], uint64[1024], uint32[512]), after which those
+    encodings decode on the device."""
+    import numpy as np
+
+    a, b, c = (np.ascontiguousarray(g) for g in (iq3xxs, iq2s, iq3s))
+    if not (a.dtype == np.uint32 and a.size == 256 and b.dtype == np.uint64 and b.size == 1024
+            and c.dtype == np.uint32 and c.size == 512):
+        raise ValueError("IQ code grids: uint32[256], uint64[1024], uint32[512]")
+    check(lib.kb200_set_iq_grids(a.ctypes.data, b.ctypes.data, c.ctypes.data))
 
 
 def gguf_dequant(encoding: int, packed, count: int, out, status=None, stream=None) -> None:

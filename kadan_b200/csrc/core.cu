@@ -1,13 +1,30 @@
 // C-ABI housekeeping (status text, last error, watchdog word) and the exact
 // dequantisation kernel.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "gguf_formats.cuh"
 #include "kb200_device.cuh"
 #include "kb200_host.hpp"
 
 namespace kb200 {
+
+namespace {
+
+// Host copies of the caller's IQ code grids; published once, never changed.
+uint32_t iq3xxs_grid_host[256], iq3s_grid_host[512];
+unsigned long long iq2s_grid_host[1024];
+const IqGrids iq_grids_host{iq3xxs_grid_host, iq2s_grid_host, iq3s_grid_host};
+std::atomic<bool> iq_grids_set{false};
+std::mutex iq_grids_lock;
+
+}  // namespace
+
+const IqGrids* registered_iq_grids() {
+    return iq_grids_set.load(std::memory_order_acquire) ? &iq_grids_host : nullptr;
+}
 
 // Set (one bit per cause) by a kernel whose bounded wait ran out; read and
 // cleared by kb200_take_device_error(). A file-scope device variable.
@@ -91,7 +108,24 @@ int kb200_version(void) {
 }
 
 int kb200_encoding_supported(int encoding) {
-    return encoding == KB200_F32 || decodable(encoding) ? 1 : 0;
+    return encoding == KB200_F32 || decodable(encoding) || (grid_coded(encoding) && registered_iq_grids()) ? 1 : 0;
+}
+
+int kb200_set_iq_grids(const uint32_t* iq3xxs, const uint64_t* iq2s, const uint32_t* iq3s) {
+    if (!iq3xxs || !iq2s || !iq3s)
+        return fail(KB200_INVALID, "null IQ code grid");
+    std::lock_guard<std::mutex> guard(iq_grids_lock);
+    if (iq_grids_set.load(std::memory_order_relaxed)) {
+        const bool same = !std::memcmp(iq3xxs_grid_host, iq3xxs, sizeof(iq3xxs_grid_host))
+                          && !std::memcmp(iq2s_grid_host, iq2s, sizeof(iq2s_grid_host))
+                          && !std::memcmp(iq3s_grid_host, iq3s, sizeof(iq3s_grid_host));
+        return same ? KB200_OK : fail(KB200_INVALID, "IQ code grids are already registered with other values");
+    }
+    std::memcpy(iq3xxs_grid_host, iq3xxs, sizeof(iq3xxs_grid_host));
+    std::memcpy(iq2s_grid_host, iq2s, sizeof(iq2s_grid_host));
+    std::memcpy(iq3s_grid_host, iq3s, sizeof(iq3s_grid_host));
+    iq_grids_set.store(true, std::memory_order_release);
+    return KB200_OK;
 }
 
 size_t kb200_block_values(int encoding) {
@@ -120,7 +154,7 @@ int kb200_take_device_error(unsigned* value) {
 int kb200_gguf_dequant(
     int encoding, const void* packed, size_t count, float* out, unsigned* status, void* stream
 ) {
-    if (!decodable(encoding))
+    if (encoding == KB200_F32 || !kb200_encoding_supported(encoding))
         return fail(KB200_UNSUPPORTED, "encoding has no device decoder");
     if (count % size_t(block_values(encoding)))
         return fail(KB200_INVALID, "count is not whole blocks");
@@ -131,6 +165,8 @@ int kb200_gguf_dequant(
     const size_t packed_bytes = count / block_values(encoding) * block_bytes(encoding);
     if (overlap(out, count * sizeof(float), packed, packed_bytes))
         return fail(KB200_ALIAS, "output overlaps packed input");
+    if (const int s = ensure_iq_grids(encoding))
+        return s;
     const unsigned threads = 256;
     const size_t want = (count + threads - 1) / threads;
     const unsigned blocks = unsigned(want < 148u * 16u ? want : 148u * 16u);

@@ -610,6 +610,8 @@ bool staged_format(int e) {
 int check_job(const kb200_gemv_job& j) {
     if (!kb200_encoding_supported(j.encoding))
         return fail(KB200_UNSUPPORTED, "encoding has no device decoder");
+    if (const int s = ensure_iq_grids(j.encoding))
+        return s;
     const size_t values = block_values(j.encoding), bytes = block_bytes(j.encoding);
     // gguf_batch_supported (IW/include/kadan/gguf_batch_partition.hpp:12-31).
     if (!j.in || !j.columns || !j.rows || j.rows > KB200_BATCH_MAX_ROWS || j.in % 8 || j.in % values)

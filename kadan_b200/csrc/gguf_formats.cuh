@@ -8,13 +8,64 @@
 // read exactly as written; the arithmetic around them is this file's own.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda_fp16.h>
+#include <mutex>
 
 #include "gguf_geometry.hpp"
+#include "iq_decode.hpp"
 #include "kadan_b200.h"
+#include "kb200_host.hpp"
 
 namespace kb200 {
+
+// The caller's IQ code grids (kb200_set_iq_grids), or null before they are set.
+const IqGrids* registered_iq_grids();
+
+namespace {
+
+// This translation unit's device copies of the IQ code grids.
+__device__ uint32_t iq3xxs_grid_device[256];
+__device__ unsigned long long iq2s_grid_device[1024];
+__device__ uint32_t iq3s_grid_device[512];
+
+// Before the first launch that decodes a grid-coded encoding on the current
+// device: copies the registered grids into this translation unit's arrays
+// there (three synchronous copies, once per device). KB200_UNSUPPORTED while
+// no grids are registered.
+inline int ensure_iq_grids(int encoding) {
+    if (!grid_coded(encoding))
+        return KB200_OK;
+    const IqGrids* grids = registered_iq_grids();
+    if (!grids)
+        return fail(KB200_UNSUPPORTED, "IQ code grids are not registered (kb200_set_iq_grids)");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64)
+        return fail(KB200_UNSUPPORTED, "device index above 63");
+    static std::atomic<unsigned long long> uploaded{0};
+    const unsigned long long bit = 1ull << dev;
+    if (uploaded.load(std::memory_order_acquire) & bit)
+        return KB200_OK;
+    static std::mutex lock;
+    std::lock_guard<std::mutex> guard(lock);
+    if (uploaded.load(std::memory_order_relaxed) & bit)
+        return KB200_OK;
+    e = cudaMemcpyToSymbol(iq3xxs_grid_device, grids->iq3xxs, sizeof(iq3xxs_grid_device));
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbol(iq2s_grid_device, grids->iq2s, sizeof(iq2s_grid_device));
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbol(iq3s_grid_device, grids->iq3s, sizeof(iq3s_grid_device));
+    if (e != cudaSuccess)
+        return cuda_fail(e, "cudaMemcpyToSymbol (IQ code grids)");
+    uploaded.fetch_or(bit, std::memory_order_release);
+    return KB200_OK;
+}
+
+}  // namespace
 
 // binary16 -> binary32 by integer operations, exact for every pattern
 // including subnormals and NaN payloads.
@@ -103,6 +154,10 @@ __device__ __forceinline__ float decode_value(int e, const uint8_t* b, unsigned 
             __fmul_rn(half_at(b), float(scale)), float(iq4nl_book[w < 16 ? packed & 15u : packed >> 4])
         );
     }
+    case KB200_IQ3_XXS:
+    case KB200_IQ2_S:
+    case KB200_IQ3_S:
+        return iq::value(e, b, el, IqGrids{iq3xxs_grid_device, iq2s_grid_device, iq3s_grid_device});
     default:
         return __int_as_float(0x7fc00000);
     }

@@ -26,9 +26,9 @@ KB200_HD constexpr int block_bytes(int e) {
     case KB200_Q6_K: return 210;
     case KB200_IQ4_NL: return 18;
     case KB200_IQ4_XS: return 136;
-    case KB200_IQ3_XXS: return 98;  // geometry only: no device decoder here
-    case KB200_IQ2_S: return 82;    // geometry only
-    case KB200_IQ3_S: return 110;   // geometry only
+    case KB200_IQ3_XXS: return 98;  // decoded once the caller registers the code grids
+    case KB200_IQ2_S: return 82;
+    case KB200_IQ3_S: return 110;
     case KB200_BF16: return 2;
     case KB200_F32: return 4;
     default: return 0;
@@ -40,7 +40,9 @@ KB200_HD constexpr bool gguf_geometry(int e) {
     return e >= KB200_Q3_K && e <= KB200_BF16;
 }
 
-// Encodings with a device decoder here.
+// Encodings with a device decoder here that needs no caller data (the
+// grid-coded IQ3_XXS, IQ2_S and IQ3_S also decode once their grids are
+// registered: kb200_encoding_supported).
 KB200_HD constexpr bool decodable(int e) {
     return e == KB200_Q3_K || e == KB200_Q4_K || e == KB200_Q8_0 || e == KB200_Q6_K || e == KB200_IQ4_NL
            || e == KB200_IQ4_XS || e == KB200_BF16;

@@ -436,7 +436,10 @@ void unsupported_before_any_read() {
     CHECK(compute.dense_gguf_source(good.id, *good.gguf_encoding(), good.source, {}, xg, 64, 8,
                                     std::span(yg).first(7), cancel)
           == ProjectionResult::unsupported);
-    // Encodings without a decoder here.
+    // The grid-coded encodings were enabled with the worker's own grids; their
+    // blocks are 256 values, so a 64-column input is still unsupported.
+    CHECK(kb200_encoding_supported(KB200_IQ2_S) && kb200_encoding_supported(KB200_IQ3_XXS)
+          && kb200_encoding_supported(KB200_IQ3_S));
     CHECK(compute.dense_gguf_source(good.id, kadan::gguf::Encoding::iq2_s, good.source, {}, xg, 64, 8, yg, cancel)
           == ProjectionResult::unsupported);
     CHECK(good.rows_read.empty() && odd.rows_read.empty() && device_of(0).calls == 0);

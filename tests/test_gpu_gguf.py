@@ -26,6 +26,35 @@ def to_dev(a, cuda):
 
 @pytest.mark.parametrize("name", ["q8_0", "q4_k", "q6_k", "q3_k", "iq4_nl", "iq4_xs", "bf16"])
 def test_dequant_bit_exact_reference_blocks(kb, oracle, cuda, name):
+    check_dequant(kb, oracle, cuda, name)
+
+
+@pytest.fixture
+def iq_grids(kb, oracle, ref):
+    """The reference's IQ code grids, registered with the library (as the
+    worker's adapter registers its own) and with the oracle."""
+    grids = ref.iq_grids()
+    kb.set_iq_grids(*grids)
+    oracle.set_iq_grids(grids)
+    return grids
+
+
+@pytest.mark.parametrize("name", ["iq3_xxs", "iq2_s", "iq3_s"])
+def test_dequant_grid_coded_bit_exact(kb, oracle, cuda, iq_grids, name):
+    check_dequant(kb, oracle, cuda, name)
+
+
+@pytest.mark.parametrize("enc_name", ["iq3_xxs", "iq2_s", "iq3_s"])
+@pytest.mark.parametrize("rows", [1, 5])
+def test_gemv_grid_coded_parity(kb, oracle, cuda, iq_grids, enc_name, rows):
+    enc = getattr(kb, enc_name.upper())
+    y, want = gemv_case(kb, oracle, cuda, enc, 512, 23, rows)
+    assert rel_err(y, want) <= TOL
+
+
+def check_dequant(kb, oracle, cuda, name):
+    """The golden blocks of `name` decoded on the device: the reference's
+    digest, the oracle's bits (NaN payloads aside) and the status word."""
     import torch
 
     from golden.make_golden import canonical_digest, reference_blocks
