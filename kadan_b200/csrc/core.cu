@@ -58,6 +58,7 @@ int cuda_fail(cudaError_t code, const char* where) {
 }
 
 // Decode `count` values; each thread writes one value so stores stay coalesced.
+template <bool Grids>
 __global__ void dequant_kernel(
     int encoding, const uint8_t* packed, size_t count, float* out, unsigned* status
 ) {
@@ -65,7 +66,7 @@ __global__ void dequant_kernel(
     bool bad = false;
     for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
          i += size_t(gridDim.x) * blockDim.x) {
-        const float v = decode_value(encoding, packed + i / values * bytes, unsigned(i % values));
+        const float v = decode_value<Grids>(encoding, packed + i / values * bytes, unsigned(i % values));
         out[i] = v;
         bad |= !isfinite(v);
     }
@@ -170,9 +171,14 @@ int kb200_gguf_dequant(
     const unsigned threads = 256;
     const size_t want = (count + threads - 1) / threads;
     const unsigned blocks = unsigned(want < 148u * 16u ? want : 148u * 16u);
-    dequant_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-        encoding, static_cast<const uint8_t*>(packed), count, out, status
-    );
+    if (grid_coded(encoding))
+        dequant_kernel<true><<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+            encoding, static_cast<const uint8_t*>(packed), count, out, status
+        );
+    else
+        dequant_kernel<false><<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+            encoding, static_cast<const uint8_t*>(packed), count, out, status
+        );
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "dequant_kernel launch");
 }

@@ -484,7 +484,7 @@ __global__ void __launch_bounds__(kThreads) gemv_staged_kernel(const __grid_cons
 // KB200_BATCH_ROWS input rows per pass (the reference's matvec_rows shape).
 constexpr int kGenericWarps = 8;
 
-template <int Rows>
+template <int Rows, bool Grids>
 __global__ void __launch_bounds__(32 * kGenericWarps) gemv_generic_kernel(const __grid_constant__ GemvParams p) {
     const uint32_t tile = blockIdx.x;
     const DevJob& job = p.jobs[find_job(p, tile)];
@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(32 * kGenericWarps) gemv_generic_kernel(const 
             const int values = block_values(encoding), bytes = block_bytes(encoding);
 #pragma unroll
             for (int k = 0; k < 8; ++k)
-                w[k] = decode_value(encoding, row + size_t((i + k) / values) * bytes, (i + k) % values);
+                w[k] = decode_value<Grids>(encoding, row + size_t((i + k) / values) * bytes, (i + k) % values);
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k)
@@ -598,7 +598,10 @@ template <class F, int T> int launch_staged(const GemvParams& p, cudaStream_t st
 }
 
 template <int Rows> int launch_generic(const GemvParams& p, cudaStream_t stream) {
-    gemv_generic_kernel<Rows><<<p.total_tiles, 32 * kGenericWarps, 0, stream>>>(p);
+    if (grid_coded(p.encoding))
+        gemv_generic_kernel<Rows, true><<<p.total_tiles, 32 * kGenericWarps, 0, stream>>>(p);
+    else
+        gemv_generic_kernel<Rows, false><<<p.total_tiles, 32 * kGenericWarps, 0, stream>>>(p);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "gemv_generic_kernel launch");
 }

@@ -95,8 +95,13 @@ __device__ __forceinline__ int as_s8(uint32_t b) {
 __constant__ const int8_t iq4nl_book[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
                                             1,    13,   25,  38,  53,  69,  89,  113};
 
-// One value of one block.
+// One value of one block. Grids = true: the grid-coded IQ3_XXS, IQ2_S and
+// IQ3_S, in kernel instantiations of their own, so the kernels of the other
+// formats compile as if these did not exist.
+template <bool Grids = false>
 __device__ __forceinline__ float decode_value(int e, const uint8_t* b, unsigned el) {
+    if constexpr (Grids)
+        return iq::value(e, b, el, IqGrids{iq3xxs_grid_device, iq2s_grid_device, iq3s_grid_device});
     switch (e) {
     case KB200_BF16:
         return __uint_as_float((uint32_t(b[0]) | (uint32_t(b[1]) << 8)) << 16);
@@ -154,10 +159,6 @@ __device__ __forceinline__ float decode_value(int e, const uint8_t* b, unsigned 
             __fmul_rn(half_at(b), float(scale)), float(iq4nl_book[w < 16 ? packed & 15u : packed >> 4])
         );
     }
-    case KB200_IQ3_XXS:
-    case KB200_IQ2_S:
-    case KB200_IQ3_S:
-        return iq::value(e, b, el, IqGrids{iq3xxs_grid_device, iq2s_grid_device, iq3s_grid_device});
     default:
         return __int_as_float(0x7fc00000);
     }
