@@ -114,6 +114,24 @@ def test_registration_rules(kb):
         assert [kb.lib.kb200_block_bytes(e) for e in iq] == [98, 82, 110]
         assert [kb.lib.kb200_block_values(e) for e in iq] == [256] * 3
         kb.set_iq_grids(*grids)
+        # Registered, the support predicate agrees with the reference's
+        # gguf_batch_supported for these encodings as for the others.
+        if REF_LIB.exists():
+            import ctypes
+            from kadan_b200.weight_bank import SourceJobC, WeightIdentityC, _ROW_SOURCE
+            ref = Reference()
+            kb.lib.kb200_source_job_supported.argtypes = [ctypes.POINTER(SourceJobC)]
+            ident, src, checked = WeightIdentityC(), _ROW_SOURCE(lambda *a: 0), 0
+            for e in iq:
+                for in_ in (8, 256, 264, 512, 4096, 14336, (16 << 20) // 110 * 256, ((16 << 20) // 82 + 1) * 256):
+                    for out, rows in ((1, 1), (19, 3), (5, 4096), (5, 4097)):
+                        if in_ * rows > (1 << 24):
+                            continue
+                        job = SourceJobC(ctypes.pointer(ident), src, None, 0x1000, 0x2000, in_, out, rows, e, 1)
+                        got = bool(kb.lib.kb200_source_job_supported(ctypes.byref(job)))
+                        assert got == ref.gguf_batch_supported(in_, out, rows, e), (e, in_, out, rows)
+                        checked += got
+            assert checked > 0
         other = grids[1].copy()
         other[5] ^= 1
         try:

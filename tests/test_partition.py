@@ -72,7 +72,9 @@ def test_partition_covers_every_column_once_and_scatters(kb, caps):
 def test_source_job_support_matches_reference(kb, ref):
     """kb200_source_job_supported agrees with the reference's
     gguf_batch_supported on every job shape, except for the encodings that
-    have no device decoder here (IQ3_XXS, IQ2_S, IQ3_S), which it declines."""
+    have no device decoder until their code grids are registered (IQ3_XXS,
+    IQ2_S, IQ3_S), which it declines here (registered, they agree too:
+    tests/test_iq_grids.py)."""
     import ctypes
 
     from kadan_b200.weight_bank import SourceJobC, WeightIdentityC, _ROW_SOURCE
