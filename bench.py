@@ -2,20 +2,31 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (decode): the Llama-3-8B-shaped Q4_K linear stack,
-32 layers x {q, o: 4096x4096; k, v: 1024x4096; gate, up: 14336x4096;
-down: 4096x14336}, one input row (T=1). A step is one token through the whole
-stack: per layer four dependent launches ([q,k,v], [o], [gate,up], [down]),
-captured once in a CUDA graph. The weights (3.93 GB) are far larger than L2,
-so no flush is needed between steps.
+Headline workload (decode): the Llama-3-70B-shaped mixed
+Q6_K/Q4_K stack (hidden 8192, 64 q / 8 kv heads of 128, ffn 28672, 80
+layers; 46.46 GB of packed weights), T=1, tensor-parallel over the N ranks of
+one node, N=1 included. q/k/v (by heads) and gate/up (by output columns) are
+column shards; o and down are cut along K on super-block boundaries, and
+their partial sums are added over NVLink by the GEMV epilogue's peer stores
+plus a gather kernel (`--collective fused`, the default). A step is one
+token through the whole stack, captured once in a CUDA graph; the weights
+(46 GB, 5.8 GB per rank at N=8) are far larger than L2, so no flush is needed
+between steps. Total work is fixed as N grows (strong scaling): value = the
+stack's weight + activation bytes per step / device time per step (CUDA
+events, max over ranks).
 
-metric value = weight+activation bytes streamed per step / device time per
-step, summed over ranks (each rank runs its own replica of the stack: the path
-has no exchange step at this config, so scaling is weak).
+On the same line: `launches` (per dependency group, the time of one launch
+of every layer, each group replayed alone), `roofline` (the group with the
+largest share), `parity` (outputs of the timed graph against the CPU oracle),
+`e2e`, and at N=1 on rank 0 `config2` (the config-2 Llama-3-8B Q4_K decode
+stack), `moe` (the config-3 MXFP4 MoE layer at T=4096 and T=1), `h3_reference`
+(the reference worker's own device GEMV rebuilt for sm_100a, on the config-2
+stack) and `cpu_baseline`.
 
 `--impl reference` times the reference's own CPU path (kadan::text::CpuMatvec
-over ggml's AVX2 Q4_K dot, compiled from the reference sources into
-oracle/_ref) on a bounded sample of the same stack with all host threads.
+over ggml's AVX2 Q6_K / Q4_K dots, compiled from the reference sources into
+oracle/_ref) on one layer of the same stack per step, with all host threads.
+It loads nothing of this repository's CUDA library.
 """
 from __future__ import annotations
 
@@ -35,6 +46,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "decode GB/s (% HBM peak) & MXFP4 MoE tokens/s at 1/2/4/8 B200"
+# Config 2: Llama-3-8B Q4_K stack.
 HIDDEN, KV, FFN, LAYERS = 4096, 1024, 14336, 32
 # (name, out, in) per layer; dependency groups of one decode step.
 GROUPS = [[("q", HIDDEN, HIDDEN), ("k", KV, HIDDEN), ("v", KV, HIDDEN)],
@@ -42,22 +54,47 @@ GROUPS = [[("q", HIDDEN, HIDDEN), ("k", KV, HIDDEN), ("v", KV, HIDDEN)],
           [("gate", FFN, HIDDEN), ("up", FFN, HIDDEN)],
           [("down", HIDDEN, FFN)]]
 Q4K_BLOCK, Q4K_VALUES = 144, 256
+# Config 4: Llama-3-70B, Q6_K attention and down, Q4_K gate/up. Encodings are
+# kadan::gguf::Encoding values (Q4_K 1, Q6_K 3); GGML_TYPE ids 12 and 14.
+Q4K, Q6K = 1, 3
+GGML_TYPE = {Q4K: 12, Q6K: 14}
+BLOCK = {Q4K: (144, 256), Q6K: (210, 256)}
+C4_HIDDEN, C4_FFN, C4_LAYERS = 8192, 28672, 80
+C4_GROUPS = [[("q", Q6K, 8192, 8192), ("k", Q6K, 1024, 8192), ("v", Q6K, 1024, 8192)],
+             [("o", Q6K, 8192, 8192)],
+             [("gate", Q4K, 28672, 8192), ("up", Q4K, 28672, 8192)],
+             [("down", Q6K, 8192, 28672)]]
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) of one [gate, up] launch, from an ncu capture of
-# that launch (the profile summary of gemv_q4k_mma_kernel holds the command).
+FALLBACK_BF16_TFLOPS = 1590.0
+# DRAM bytes (read + write) of one [gate, up] launch of the config-2 stack,
+# from an ncu capture of that launch (the profile summary of
+# gemv_q4k_mma_kernel holds the command).
 GATE_UP_TRAFFIC = 66922496  # 66,164,224 read + 758,272 written
+# DRAM bytes per launch of the config-4 groups at N=1, keyed by group, from
+# ncu captures of a 2-layer stack (profiles/ summaries give the commands);
+# scaled to nothing: the launches are the same size at any layer count.
+C4_TRAFFIC: dict = {}
 
 
 def weight_bytes(out: int, in_: int) -> int:
     return out * in_ // Q4K_VALUES * Q4K_BLOCK
 
 
+def packed_bytes(enc: int, out: int, in_: int) -> int:
+    bb, bv = BLOCK[enc]
+    return out * (in_ // bv) * bb
+
+
 def layer_weight_bytes() -> int:
     return sum(weight_bytes(o, i) for g in GROUPS for _, o, i in g)
 
 
+def c4_layer_bytes() -> int:
+    return sum(packed_bytes(e, o, i) for g in C4_GROUPS for _, e, o, i in g)
+
+
 def step_bytes() -> tuple[int, int]:
-    """(weight bytes, activation bytes) streamed per step."""
+    """(weight bytes, activation bytes) streamed per config-2 step."""
     w = LAYERS * layer_weight_bytes()
     act = 0
     for g in GROUPS:
@@ -66,15 +103,35 @@ def step_bytes() -> tuple[int, int]:
     return w, LAYERS * act
 
 
-def peaks():
+def c4_step_bytes(layers: int, tokens: int) -> tuple[int, int]:
+    """(weight bytes, activation bytes) of one config-4 step (whole stack)."""
+    act = sum(tokens * 4 * (g[0][3] + sum(o for _, _, o, _ in g)) for g in C4_GROUPS)
+    return layers * c4_layer_bytes(), layers * act
+
+
+def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
+    out = {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS,
+           "bf16_tflops_sustained": FALLBACK_BF16_TFLOPS, "source": "fallback"}
     if p.exists():
         try:
             d = json.loads(p.read_text())
-            return float(d["hbm_gbs"]), "measured"
+            out = {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                   "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                   "source": "measured"}
         except Exception:
             pass
-    return FALLBACK_HBM_GBS, "fallback"
+    return out
+
+
+def rel_err(got, want) -> float:
+    """max|got - want| / max(max|want|, 1): the reference's own GEMV check
+    (IW/tests/gguf_text.cpp:247-250)."""
+    import numpy as np
+
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    return float(np.max(np.abs(got - want)) / max(float(np.max(np.abs(want))), 1.0))
 
 
 class ClockSampler:
@@ -96,6 +153,8 @@ class ClockSampler:
                  "-i", str(self.index)], stdout=self.file, stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
+        # nvidia-smi needs a moment before its first sample.
+        time.sleep(0.3)
         return self
 
     def __exit__(self, *exc):
@@ -125,7 +184,17 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3] not in ("", "[N/A]"))}
 
 
-# --------------------------------------------------------------------- ours
+def max_over_ranks(dist, value: float, device) -> float:
+    if not dist:
+        return value
+    import torch
+
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------ config 2 stack
 def build_stack(torch, kb, device, seed: int = 0):
     from kadan_b200 import synth
 
@@ -156,40 +225,138 @@ def step_jobs(kb, layers, acts, outs):
     return calls
 
 
-def run_ours(args, rank, world, local_rank):
+def graph_of(torch, stream, fn):
+    """fn() once outside capture (kernel attributes, per-stream buffers), then
+    captured into a CUDA graph on `stream`."""
+    with torch.cuda.stream(stream):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fn()
+    torch.cuda.synchronize()
+    return graph
+
+
+def time_graph(torch, stream, graph, reps: int, warm: int = 1) -> float:
+    """ms per replay of `graph` on `stream` (CUDA events on that stream)."""
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            graph.replay()
+        a.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def config2_object(args, torch, kb, device, pk) -> tuple[dict, tuple]:
+    """The config-2 decode stack (Llama-3-8B Q4_K, 32 layers, T=1), one CUDA
+    graph per token, and each dependency group's launches replayed alone."""
+    layers, acts, outs = build_stack(torch, kb, device)
+    calls = step_jobs(kb, layers, acts, outs)
+    stream = torch.cuda.Stream(device)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+
+    def launch(group=None):
+        for gi, arr, n in calls:
+            if group is None or gi == group:
+                kb.check(kb.lib.kb200_gguf_gemv_batch(arr, n, sptr))
+
+    graph = graph_of(torch, stream, launch)
+    time_graph(torch, stream, graph, max(3, args.warmup), warm=0)
+    steps = max(args.steps, 20)
+    ms = time_graph(torch, stream, graph, steps)
+    wbytes, abytes = step_bytes()
+    names = ["q,k,v", "o", "gate,up", "down"]
+    launches = []
+    for gi, g in enumerate(GROUPS):
+        gg = graph_of(torch, stream, lambda gi=gi: launch(gi))
+        us = time_graph(torch, stream, gg, max(3, steps // 4)) / LAYERS * 1e3
+        nbytes = sum(weight_bytes(o, i) for _, o, i in g)
+        launches.append({"launch": names[gi], "kernel": "gemv_q4k_mma_kernel<1>", "bytes": nbytes,
+                         "us": round(us, 2), "gbps": round(nbytes / us / 1e3, 1),
+                         "frac": round(nbytes / us / 1e3 / pk["hbm_gbs"], 4)})
+        del gg
+    value = (wbytes + abytes) / (ms * 1e-3) / 1e9
+    gu = launches[2]
+    out = {"workload": "BASELINE config 2 decode: Llama-3-8B Q4_K linear stack, 32 layers, T=1",
+           "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 5), "steps": steps,
+           "hbm_frac": round(value / pk["hbm_gbs"], 4), "weight_bytes_per_step": wbytes,
+           "launch": "one CUDA graph per step, 4 dependent launches per layer", "launches": launches,
+           "roofline": {"bound": "hbm", "kernel": "gemv_q4k_mma_kernel<1> ([gate, up] launch)",
+                        "achieved": gu["gbps"], "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gu["frac"],
+                        "traffic": GATE_UP_TRAFFIC, "algorithmic_bytes_per_launch": gu["bytes"]}}
+    graph = None
+    return out, (layers, acts, outs)
+
+
+# --------------------------------------------------------- headline: config 4
+def tp_parity(torch, kb, stack, groups, world: int, rank: int, dist, device, cols: int = 256) -> dict:
+    """Outputs the timed graph left behind (the last layer's) against the CPU
+    oracle (decode, then a float64 dot), on the first `cols` output columns:
+    gate (column shard: this rank's slice) and down (row shards: every rank's
+    oracle partial sum over its K slice, added over the ranks, against the
+    all-reduced device output). Tolerance 1e-3 (fp32 outputs)."""
+    import numpy as np
+
+    from kadan_b200 import tensor_parallel as tp
+    from oracle.pyoracle import Oracle
+
+    orc = Oracle()
+    proj = {p.name: p for g in groups for p in g}
+    first_of = {p.name: g[0].name for g in groups for p in g}
+    res = {}
+    for name in ("gate", "down"):
+        p = proj[name]
+        s = tp.shard(p, world, rank)
+        n = min(cols, s.out_count)
+        rb = kb.row_bytes(p.encoding, s.in_count)
+        w = np.ascontiguousarray(stack.weights[-1][name][:n].cpu().numpy()[:, :rb])
+        x = stack.local_inputs[first_of[name]]
+        want = torch.from_numpy(orc.gemv_f64(p.encoding, w, x.cpu().numpy(), s.in_count, n)).to(device)
+        if p.mode == "row" and dist:
+            dist.all_reduce(want)
+        got = stack.outputs[name][:, :n].double()
+        res[name] = rel_err(got.cpu().numpy(), want.cpu().numpy())
+    return {"ok": all(v <= 1e-3 for v in res.values()), "max_rel_err": res, "tolerance": 1e-3,
+            "columns_checked": cols,
+            "what": "last layer's gate (this rank's column shard) and down (all-reduced over the ranks) outputs "
+                    "of the graph-replayed stack vs the oracle (decode + float64 dot)"}
+
+
+def run_default(args, rank, world, local_rank):
+    import datetime
+
+    import numpy as np
     import torch
 
     import kadan_b200 as kb
+    from kadan_b200 import tensor_parallel as tp
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     dist = None
     if world > 1:
-        import datetime
-
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    pk = peaks()
+    tokens = args.tokens if args.tokens and args.tokens <= 32 else 1
+    layers = args.layers or C4_LAYERS
+    groups = tp.llama3_70b_projections()
+    assert [[(p.name, p.encoding, p.out, p.in_) for p in g] for g in groups] == C4_GROUPS_T
+    weights = tp.synth_shards(groups, layers, world, rank, device)
+    reducer = None
+    if dist and args.collective in ("fused", "peer"):
+        from kadan_b200.collectives import PeerAllReduce
 
-    layers, acts, outs = build_stack(torch, kb, device, seed=rank)
-    calls = step_jobs(kb, layers, acts, outs)
+        reducer = PeerAllReduce(tokens * C4_HIDDEN, fused=args.collective == "fused")
+    stack = tp.DecodeStack(groups, weights, tokens, world, rank, device, collective=reducer)
     stream = torch.cuda.Stream(device)
-    sptr = ctypes.c_void_p(stream.cuda_stream)
-    gate_up_bytes = 2 * weight_bytes(FFN, HIDDEN)
-
-    def launch_step():
-        for gi, arr, n in calls:
-            kb.check(kb.lib.kb200_gguf_gemv_batch(arr, n, sptr))
-
-    # First call per kernel sets attributes/occupancy outside capture.
-    with torch.cuda.stream(stream):
-        launch_step()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        launch_step()
-    torch.cuda.synchronize()
-
+    graph = graph_of(torch, stream, lambda: stack.launch(stream))
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             graph.replay()
@@ -197,86 +364,117 @@ def run_ours(args, rank, world, local_rank):
     if dist:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    gate_up = [(gi, arr, n) for gi, arr, n in calls if gi == 2]
-    gu_start, gu_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    gu_reps = max(1, args.steps // 20)
+    names = [",".join(p.name for p in g) for g in groups]
+    group_graphs = [graph_of(torch, stream, lambda gi=gi: stack.launch(stream, gi)) for gi in range(len(groups))]
+    if dist:
+        dist.barrier()
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
-        with torch.cuda.stream(stream):  # replays run on the capture stream
+        with torch.cuda.stream(stream):
             start.record(stream)
             for _ in range(args.steps):
                 graph.replay()
             end.record(stream)
-        # The dominant launch ([gate, up] of every layer, 66 MB each) timed on
-        # its own stream with events, back to back, same clocks window.
-        gu_start.record(stream)
-        for _ in range(gu_reps):
-            for _, arr, n in gate_up:
-                kb.check(kb.lib.kb200_gguf_gemv_batch(arr, n, sptr))
-        gu_end.record(stream)
         torch.cuda.synchronize()
-    gate_up_ms = [gu_start.elapsed_time(gu_end) / (gu_reps * len(gate_up))]
-    ms = start.elapsed_time(end) / args.steps
-    if dist:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    wbytes, abytes = step_bytes()
-    value = world * (wbytes + abytes) / (ms * 1e-3) / 1e9
-    peak, peak_kind = peaks()
-    achieved = gate_up_bytes / (statistics.mean(gate_up_ms) * 1e-3) / 1e9
+        # Each dependency group alone (one launch per layer, captured), in the
+        # same clocks window: per-launch device time of the kernels of a step.
+        group_ms = [time_graph(torch, stream, gg, max(3, args.steps // 4)) for gg in group_graphs]
+    ms = max_over_ranks(dist, start.elapsed_time(end) / args.steps, device)
+    group_ms = [max_over_ranks(dist, v, device) for v in group_ms]
+    clock = clocks.summary()
+    group_graphs = None
 
-    # End to end through the host-span C ABI: host inputs, one upload, the
-    # launches, one download and a sync per dependency group (128 per token).
-    import numpy as np
+    per_launch = 2 if dist and reducer else 1
+    launches = []
+    for gi, g in enumerate(groups):
+        nbytes = sum(tp.shard(p, world, rank).out_count * tp.shard_pitch(p, tp.shard(p, world, rank)) for p in g)
+        us = group_ms[gi] / layers * 1e3
+        row = any(p.mode == "row" for p in g) and dist is not None
+        kernel = "gemv_q6k_mma_kernel<1>" if g[0].encoding == kb.Q6_K else "gemv_q4k_mma_kernel<1>"
+        if row and reducer:
+            kernel += " + peer_allreduce_kernel (gather)" if reducer.fused else " + peer_allreduce_kernel"
+        launches.append({"launch": names[gi], "kernel": kernel, "bytes": nbytes, "us": round(us, 2),
+                         "gbps": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / pk["hbm_gbs"], 4),
+                         "share": round(group_ms[gi] / sum(group_ms), 4)})
+    top = max(range(len(groups)), key=lambda i: group_ms[i])
+    dom = launches[top]
+    parity = tp_parity(torch, kb, stack, groups, world, rank, dist, device)
 
-    ctx = kb.Context(local_rank)
-    host_in = {n: a.cpu().numpy().copy() for n, a in acts.items()}
-    host_out = {n: np.empty((1, o), dtype=np.float32) for g in GROUPS for n, o, _ in g}
-    inputs = ["x", "attn", "h", "g"]
-    host_calls = []
-    for mats in layers:
-        for gi, g in enumerate(GROUPS):
-            jobs = [kb.host_job(kb.Q4_K, mats[n].data_ptr(), host_in[inputs[gi]], host_out[n], in_=i, out=o,
-                                validated=True) for n, o, i in g]
-            host_calls.append((kb.HostJob * len(jobs))(*jobs))
-    result = ctypes.c_int(0)
+    # End to end with host buffers.
+    h2d = tokens * C4_HIDDEN * 4
+    d2h = tokens * C4_HIDDEN * 4
+    e2e_steps = max(3, min(args.steps, 10))
+    pin_in = torch.empty(tokens, C4_HIDDEN, pin_memory=True)
+    pin_out = torch.empty(tokens, C4_HIDDEN, pin_memory=True)
+    dev_in = stack.local_inputs["q"]  # column group: the whole input row
+    pin_in.copy_(dev_in.cpu())
+    dev_out = stack.outputs["down"]
 
-    def e2e_step():
-        for arr in host_calls:
-            kb.check(kb.lib.kb200_dense_gguf_batch(ctx.handle, arr, len(arr), None, ctypes.byref(result)))
+    def graph_e2e():
+        with torch.cuda.stream(stream):
+            dev_in.copy_(pin_in, non_blocking=True)
+            graph.replay()
+            pin_out.copy_(dev_out, non_blocking=True)
+        stream.synchronize()
 
-    e2e_step()
-    e2e_steps = max(3, min(args.steps // 20, 50))
-    torch.cuda.synchronize()
+    graph_e2e()
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        e2e_step()
-    e2e_s = (time.perf_counter() - t0) / e2e_steps
-    if dist:
-        t = torch.tensor([e2e_s], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    h2d = LAYERS * sum(g[0][2] * 4 for g in GROUPS)
-    d2h = LAYERS * sum(o * 4 for g in GROUPS for _, o, _ in g)
-    e2e = {"value": round(world * (wbytes + abytes) / e2e_s / 1e9, 2), "unit": "GB/s",
-           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-           "calls_per_step": len(host_calls), "ms_per_step": round(e2e_s * 1e3, 4),
-           "timing": "host wall clock around synchronous kb200_dense_gguf_batch calls"}
-    ctx.close()
+        graph_e2e()
+    graph_s = max_over_ranks(dist, (time.perf_counter() - t0) / e2e_steps, device)
+    wbytes, abytes = c4_step_bytes(layers, tokens)
+    graph_path = {"value": round((wbytes + abytes) / graph_s / 1e9, 2), "unit": "GB/s",
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(graph_s * 1e3, 4),
+                  "timing": "host wall clock per step: pinned upload of the step's input, the step's CUDA graph "
+                            "(the library's launches), download of the last projection's output, stream sync"}
+    if world == 1:
+        # The reference-facing call (DenseCompute::dense_gguf_batch): one
+        # synchronous kb200_dense_gguf_batch per dependency group with host
+        # spans (upload, launch, download, sync inside each call).
+        ctx = kb.Context(local_rank)
+        host_in = {g[0].name: stack.inputs[g[0].name].cpu().numpy().copy() for g in groups}
+        host_out = {p.name: np.empty((tokens, p.out), dtype=np.float32) for g in groups for p in g}
+        host_calls = []
+        for mats in stack.weights:
+            for g in groups:
+                jobs = [kb.host_job(p.encoding, mats[p.name].data_ptr(), host_in[g[0].name], host_out[p.name],
+                                    in_=p.in_, out=p.out, validated=True, row_bytes_=tp.shard_pitch(p, tp.shard(p, 1, 0)))
+                        for p in g]
+                host_calls.append((kb.HostJob * len(jobs))(*jobs))
+        result = ctypes.c_int(0)
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(layers, kb, budget_s=args.cpu_seconds)
+        def host_step():
+            for arr in host_calls:
+                kb.check(kb.lib.kb200_dense_gguf_batch(ctx.handle, arr, len(arr), None, ctypes.byref(result)))
 
-    clock = clocks.summary()
+        host_step()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            host_step()
+        host_s = (time.perf_counter() - t0) / e2e_steps
+        ctx.close()
+        e2e = {"value": round((wbytes + abytes) / host_s / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": layers * sum(tokens * g[0].in_ * 4 for g in groups),
+               "d2h_bytes_per_step": layers * sum(tokens * p.out * 4 for g in groups for p in g),
+               "calls_per_step": len(host_calls), "ms_per_step": round(host_s * 1e3, 4),
+               "timing": "host wall clock around synchronous kb200_dense_gguf_batch calls (host spans), one per "
+                         "dependency group", "graph_path": graph_path}
+    else:
+        e2e = dict(graph_path)
+
+    graph = None
     if dist:
-        graph = None
+        if reducer:
+            reducer.close()
+        dist.barrier()
         dist.destroy_process_group()
-    if rank != 0:
-        return
+    local_bytes = stack.weight_bytes()
+    del stack, weights
+    torch.cuda.empty_cache()
+    value = (wbytes + abytes) / (ms * 1e-3) / 1e9
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -286,68 +484,133 @@ def run_ours(args, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 5),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "q4_k weights, fp32 activations and accumulation",
-        "data": "synthetic (seeded Q4_K blocks and fp16-representable N(0,1) activations on the device)",
-        "config": {"workload": "BASELINE config 2 decode: Llama-3-8B Q4_K linear stack, 32 layers, T=1",
-                   "weight_bytes_per_step": wbytes, "activation_bytes_per_step": abytes,
-                   "l2": "inputs larger than L2 (3.93 GB of weights per step)",
-                   "launch": "one CUDA graph per step, 4 dependent launches per layer",
-                   "parallelism": f"replicas x{world}"},
-        "hbm_frac": round(value / world / peak, 4),
-        "gpu_launches": len(calls) * args.steps,
-        "gpu_launches_note": "kernel launches of the timed graph replays (one per encoding per group)",
-        "roofline": {"bound": "hbm", "kernel": "gemv_q4k_mma_kernel<1> ([gate, up] launch, balanced split)",
-                     "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                     "traffic": GATE_UP_TRAFFIC,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch "
-                                       "(one-pass capture, bench.py --steps 3 --warmup 3)",
-                     "algorithmic_bytes_per_launch": gate_up_bytes},
+        "dtype": "q6_k/q4_k weights; activations quantised per 256-value super-block and token to two int8 levels "
+                 "(x ~ s*(h + l/254)); exact int32 sub-block sums on the integer tensor pipe, fp32 scale "
+                 "combination and accumulation; fp32 outputs",
+        "data": "synthetic (seeded Q6_K/Q4_K shards drawn on each device, bf16-representable N(0,1) activations)",
+        "config": c4_config(layers, tokens, world),
+        "setup": {"weight_bytes_per_rank": local_bytes,
+                  "collective": ("none (one rank)" if world == 1 else
+                                 "GEMV epilogue stores to peers + gather kernel (fp32, NVLink)" if reducer and
+                                 reducer.fused else "peer-memory all-reduce kernel (fp32)" if reducer else
+                                 "NCCL all-reduce (fp32)") + (" after o and down" if world > 1 else ""),
+                  "launch": f"one CUDA graph per step, {len(groups) + (2 if dist and reducer else 0)} launches "
+                            "per layer"},
+        "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+        "gpu_launches": args.steps * layers * (len(groups) + (2 if dist and reducer else 0)),
+        "gpu_launches_note": "kernel launches of the timed graph replays (one GEMV launch per dependency group, "
+                             "plus one gather kernel per row-parallel group at N > 1)",
+        "launches": launches,
+        "roofline": {"bound": "hbm", "kernel": f"{dom['kernel']} ([{dom['launch']}] launch)",
+                     "achieved": dom["gbps"], "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": dom["frac"],
+                     "peak_source": f"{pk['source']} hbm_gbs",
+                     "traffic": C4_TRAFFIC.get(dom["launch"]) if world == 1 else None,
+                     "algorithmic_bytes_per_launch": dom["bytes"],
+                     "timing": "CUDA events around the group's launches of all layers replayed alone (a captured "
+                               "graph), same clocks window as the timed steps"},
+        "parity": parity,
+        "parity_ok": parity["ok"],
         "e2e": e2e,
         "clocks": clock,
     }
-    if cpu:
-        line["cpu_baseline"] = cpu
+    if rank == 0 and world == 1 and not args.no_extras:
+        extras(args, torch, kb, device, pk, line)
+    if rank != 0:
+        return
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline(layers, kb, budget_s: float = 15.0):
-    """The reference's CpuMatvec on the same bytes: one layer's seven matrices
-    copied to the host, repeated for about `budget_s` seconds on all cores."""
+C4_GROUPS_T = [[tuple(x) for x in g] for g in C4_GROUPS]
+
+
+def c4_config(layers: int, tokens: int, world: int) -> dict:
+    """The headline workload's config, identical on both arms."""
+    wbytes, abytes = c4_step_bytes(layers, tokens)
+    return {"workload": f"BASELINE config 4 decode: Llama-3-70B Q6_K/Q4_K linear stack, {layers} layers, T={tokens}",
+            "weight_bytes_per_step": wbytes, "activation_bytes_per_step": abytes, "parallelism": f"tp{world}",
+            "l2": "inputs larger than L2 (46.5 GB of weights per step; 5.8 GB per rank at N=8)"}
+
+
+def extras(args, torch, kb, device, pk, line):
+    """N=1, rank 0: config 2, the config-3 MoE layer, the reference's device
+    GEMV, and the CPU baselines. A failure here is reported, not raised."""
+    def guarded(name, fn):
+        try:
+            return fn()
+        except Exception as e:  # an extra must not cost the headline line
+            return {"error": f"{type(e).__name__}: {e}"}
+
+    c2 = guarded("config2", lambda: config2_object(args, torch, kb, device, pk))
+    if isinstance(c2, tuple):
+        line["config2"], stack2 = c2
+        line["h3_reference"] = guarded("h3", lambda: h3_reference_object(args, torch, kb, *stack2))
+        del stack2
+    else:
+        line["config2"] = c2
+    torch.cuda.empty_cache()
+    line["moe"] = guarded("moe", lambda: moe_object(args, torch, kb, device, pk))
+    torch.cuda.empty_cache()
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = guarded("cpu", lambda: cpu_baseline(budget_s=args.cpu_seconds))
+
+
+def c4_host_layer(synth):
+    """One config-4 layer's packed matrices and activations, host side
+    (the same generators as the tests; seeded)."""
+    mats = {}
+    for gi, g in enumerate(C4_GROUPS):
+        for i, (name, enc, out, in_) in enumerate(g):
+            gen = synth.q6_k if enc == Q6K else synth.q4_k
+            mats[name] = gen(out, in_, seed=gi * 4 + i)
+    x = {C4_HIDDEN: synth.activations(C4_HIDDEN, seed=1, dtype="bf16"),
+         C4_FFN: synth.activations(C4_FFN, seed=2, dtype="bf16")}
+    return mats, x
+
+
+def load_synth():
+    """kadan_b200/synth.py by file path: its host generators need numpy only,
+    and importing the package would load the CUDA library."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("kb200_synth_host", ROOT / "kadan_b200" / "synth.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def cpu_baseline(budget_s: float = 10.0) -> dict:
+    """The reference's CpuMatvec (oracle/_ref) on one config-4 layer (seven
+    matrices, 580.8 MB of Q6_K/Q4_K), all host cores, repeated for about
+    `budget_s` seconds; plus the same on one core and the scalar restatement."""
     from oracle.pyoracle import REF_LIB, Oracle, Reference
 
-    import numpy as np
-
     threads = os.cpu_count() or 1
-    mats = {n: t.cpu().numpy() for n, t in layers[0].items()}
-    x = {HIDDEN: np.random.default_rng(0).standard_normal(HIDDEN).astype(np.float16).astype(np.float32),
-         FFN: np.random.default_rng(1).standard_normal(FFN).astype(np.float16).astype(np.float32)}
+    mats, x = c4_host_layer(load_synth())
     if REF_LIB.exists():
         ref = Reference()
         kind = "reference"
 
         def one_layer():
-            for g in GROUPS:
-                for n, o, i in g:
-                    ref.cpu_matvec(12, mats[n], x[i], i, o, threads=threads)
+            for g in C4_GROUPS:
+                for n, e, o, i in g:
+                    ref.cpu_matvec(GGML_TYPE[e], mats[n], x[i], i, o, threads=threads)
+        nbytes = c4_layer_bytes()
     else:
         orc = Oracle()
         kind, threads = "port", 1
 
         def one_layer():
-            for g in GROUPS:
-                for n, o, i in g:
-                    orc.gemv_f64(1, mats[n][: max(1, o // 64)], x[i], i, max(1, o // 64))
-
+            for g in C4_GROUPS:
+                for n, e, o, i in g:
+                    orc.gemv_f64(e, mats[n][:64], x[i], i, 64)
+        nbytes = sum(packed_bytes(e, 64, i) for g in C4_GROUPS for _, e, _, i in g)
     dt, n = timed_repeats(one_layer, budget_s)
-    per_layer = layer_weight_bytes() if kind == "reference" else sum(
-        weight_bytes(max(1, o // 64), i) for g in GROUPS for _, o, i in g)
-    out = {"value": round(per_layer / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": kind,
-           "sample": f"layer 0 of the stack (7 matrices, {per_layer} weight bytes) x {n} repetitions, "
-                     f"{round(dt * n, 1)} s; kadan::text::CpuMatvec 64-column units, activations quantized "
-                     f"to Q8_K once per input as the reference does"}
+    out = {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+           "sample": f"one layer of the config-4 stack (7 matrices, {nbytes} weight bytes) x {n} repetitions, "
+                     f"{round(dt * n, 1)} s; kadan::text::CpuMatvec 64-column units, activations quantized to Q8_K "
+                     f"once per input as the reference does"}
     if kind == "reference":
         out["single_core"] = single_core_baselines(ref, Oracle(), mats, x)
     return out
@@ -365,66 +628,59 @@ def timed_repeats(fn, budget_s: float):
 
 def single_core_baselines(ref, oracle, mats, x, budget_s: float = 3.0) -> dict:
     """The other host figures of the decode path, each on one core, GB/s of
-    Q4_K weight bytes: the reference's CpuMatvec with one worker over layer 0
-    (its production host path), and the scalar restatement (decode each
-    block, fp64 dot: the oracle's gemv) over the first 512 columns of each
-    of layer 0's matrices."""
+    packed weight bytes: the reference's CpuMatvec with one worker over the
+    layer (its production host path), and the scalar restatement (decode each
+    block, fp64 dot: the oracle's gemv) over the first 256 columns of each
+    matrix."""
     def cpu_matvec_one():
-        for g in GROUPS:
-            for n, o, i in g:
-                ref.cpu_matvec(12, mats[n], x[i], i, o, threads=1)
+        for g in C4_GROUPS:
+            for n, e, o, i in g:
+                ref.cpu_matvec(GGML_TYPE[e], mats[n], x[i], i, o, threads=1)
 
-    cols = 512
+    cols = 256
 
     def scalar():
-        for g in GROUPS:
-            for n, o, i in g:
-                oracle.gemv_f64(1, mats[n][:cols], x[i], i, cols)
+        for g in C4_GROUPS:
+            for n, e, o, i in g:
+                oracle.gemv_f64(e, mats[n][:cols], x[i], i, cols)
 
     dt1, n1 = timed_repeats(cpu_matvec_one, budget_s)
     dt2, n2 = timed_repeats(scalar, budget_s)
-    scalar_bytes = sum(weight_bytes(cols, i) for g in GROUPS for _, _, i in g)
-    return {"cpu_matvec_1_core_gbps": round(layer_weight_bytes() / dt1 / 1e9, 3),
-            "cpu_matvec_1_core_sample": f"layer 0 x {n1}",
+    scalar_bytes = sum(packed_bytes(e, cols, i) for g in C4_GROUPS for _, e, _, i in g)
+    return {"cpu_matvec_1_core_gbps": round(c4_layer_bytes() / dt1 / 1e9, 3),
+            "cpu_matvec_1_core_sample": f"one layer x {n1}",
             "scalar_restatement_1_core_gbps": round(scalar_bytes / dt2 / 1e9, 3),
-            "scalar_restatement_1_core_sample": f"first {cols} columns of each layer-0 matrix x {n2} "
-                                                "(oracle Q4_K decode + fp64 dot)"}
+            "scalar_restatement_1_core_sample": f"first {cols} columns of each matrix x {n2} "
+                                                "(oracle decode + fp64 dot)"}
 
 
 def run_reference(args, rank, world):
-    """Reference arm: the reference's CPU path on the box's host cores."""
+    """Reference arm: the reference's CPU path on the box's host cores, one
+    config-4 layer per step (rank 0 only; other ranks exit at once)."""
     if rank != 0:
         return
-    import numpy as np
-
-    from kadan_b200 import synth
     from oracle.pyoracle import REF_LIB, Oracle, Reference
 
     threads = os.cpu_count() or 1
-    rng_x = {HIDDEN: synth.activations(HIDDEN, seed=1), FFN: synth.activations(FFN, seed=2)}
-    # Bounded sample: one layer's matrices (122.7 MB) drawn host-side per step.
-    mats = {}
-    for g in GROUPS:
-        for n, o, i in g:
-            mats[n] = synth.q4_k(o, i, seed=len(mats))
+    mats, x = c4_host_layer(load_synth())
     if REF_LIB.exists():
         ref = Reference()
         kind = "reference"
 
         def sample():
-            for g in GROUPS:
-                for n, o, i in g:
-                    ref.cpu_matvec(12, mats[n], rng_x[i], i, o, threads=threads)
-        sample_bytes = layer_weight_bytes()
+            for g in C4_GROUPS:
+                for n, e, o, i in g:
+                    ref.cpu_matvec(GGML_TYPE[e], mats[n], x[i], i, o, threads=threads)
+        sample_bytes = c4_layer_bytes()
     else:
         orc = Oracle()
         kind, threads = "port", 1
 
         def sample():
-            for g in GROUPS:
-                for n, o, i in g:
-                    orc.gemv_f64(1, mats[n][:64], rng_x[i], i, 64)
-        sample_bytes = sum(weight_bytes(64, i) for g in GROUPS for _, _, i in g)
+            for g in C4_GROUPS:
+                for n, e, o, i in g:
+                    orc.gemv_f64(e, mats[n][:64], x[i], i, 64)
+        sample_bytes = sum(packed_bytes(e, 64, i) for g in C4_GROUPS for _, e, _, i in g)
     for _ in range(args.warmup):
         sample()
     t0 = time.perf_counter()
@@ -432,16 +688,17 @@ def run_reference(args, rank, world):
         sample()
     dt = (time.perf_counter() - t0) / args.steps
     value = sample_bytes / dt / 1e9
-    wbytes, abytes = step_bytes()
+    layers = args.layers or C4_LAYERS
+    maps = Path("/proc/self/maps").read_text() if Path("/proc/self/maps").exists() else ""
+    assert "libkadan_b200" not in maps, "the reference arm must not load this repository's CUDA library"
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "q4_k weights, Q8_K-quantized activations (reference CPU dot)",
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "q6_k/q4_k weights, Q8_K-quantized activations (reference CPU dot)",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": "BASELINE config 2 decode: Llama-3-8B Q4_K linear stack, 32 layers, T=1",
-                   "sample": "one layer (7 matrices) per step", "full_step_weight_bytes": wbytes},
+        "config": c4_config(layers, 1, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
-                         "sample": "one layer of the stack per step"},
+                         "sample": f"one layer of the stack ({sample_bytes} weight bytes) per step"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -680,7 +937,7 @@ def run_tp(args, rank, world, local_rank):
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    tokens = args.tokens if args.tokens <= 32 else 1
+    tokens = args.tokens if 1 <= args.tokens <= 32 else 1
     layers = args.layers or 80
     groups = tp.llama3_70b_projections()
     weights = tp.synth_shards(groups, layers, world, rank, device)
@@ -990,33 +1247,27 @@ def run_source(args):
     print(json.dumps(line), flush=True)
 
 
-def run_h3_reference(args):
-    """--case h3-reference: the reference worker's own device GEMV
-    (IW/src/cuda/h3_compute.cu, built from the reference sources for sm_100a
-    into oracle/_ref/libh3_ref.so by the oracle recipe) over the config-2
-    decode stack: per dependency group, its job table copied and one launch per
-    encoding on the legacy stream, as dense_gguf_batch launches resident
-    chunks. Device time per step (CUDA events), the headline's bytes; also the
-    largest relative difference between its [gate, up] outputs of the last
-    layer and this library's."""
-    import torch
-
-    import kadan_b200 as kb
-
+def h3_reference_object(args, torch, kb, layers, acts, outs) -> dict:
+    """The reference worker's own device GEMV (IW/src/cuda/h3_compute.cu,
+    built from the reference sources for sm_100a into oracle/_ref/libh3_ref.so
+    by the oracle recipe) over the config-2 decode stack: per dependency
+    group, its job table copied and one launch per encoding on the legacy
+    stream, as dense_gguf_batch launches resident chunks. Device time per
+    step (CUDA events), the headline's bytes; also the largest relative
+    difference between its [gate, up] outputs of the last layer and this
+    library's."""
     path = ROOT / "oracle" / "_ref" / "libh3_ref.so"
     try:
         L = ctypes.CDLL(str(path))
     except OSError as e:
-        print(json.dumps({"case": "h3-reference", "unavailable": f"{path.name}: {e}"}), flush=True)
-        return
+        return {"unavailable": f"{path.name}: {e}"}
     vp, sz, u32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint
     L.h3ref_last_error.restype = ctypes.c_char_p
     L.h3ref_job_bytes.restype = sz
     L.h3ref_matvec_batch.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.POINTER(sz),
                                      ctypes.POINTER(u32), ctypes.POINTER(u32), ctypes.POINTER(u32),
                                      ctypes.POINTER(ctypes.c_int), sz, vp]
-    device = torch.device("cuda:0")
-    layers, acts, outs = build_stack(torch, kb, device)
+    device = acts["x"].device
     inputs = ["x", "attn", "h", "g"]
     calls = []
     for mats in layers:
@@ -1058,24 +1309,108 @@ def run_h3_reference(args):
     torch.cuda.synchronize()
     ms = start.elapsed_time(end) / steps
     wbytes, abytes = step_bytes()
-    print(json.dumps({"case": "h3-reference", "ms_per_step": round(ms, 3),
-                      "gbps": round((wbytes + abytes) / (ms * 1e-3) / 1e9, 1), "steps": steps,
-                      "max_rel_diff_vs_ours": diff,
-                      "what": "reference device GEMV (gguf_matvec_batch_kernel, job table copied per group, legacy "
-                              "stream) over the config-2 decode stack"}), flush=True)
+    return {"ms_per_step": round(ms, 3), "gbps": round((wbytes + abytes) / (ms * 1e-3) / 1e9, 1), "steps": steps,
+            "max_rel_diff_vs_ours": diff,
+            "what": "reference device GEMV (gguf_matvec_batch_kernel built for sm_100a, job table copied per group, "
+                    "legacy stream) over the config-2 decode stack"}
+
+
+def run_h3_reference(args):
+    """--case h3-reference: h3_reference_object on its own line."""
+    import torch
+
+    import kadan_b200 as kb
+
+    device = torch.device("cuda:0")
+    layers, acts, outs = build_stack(torch, kb, device)
+    print(json.dumps({"case": "h3-reference", **h3_reference_object(args, torch, kb, layers, acts, outs)}), flush=True)
+
+
+def moe_object(args, torch, kb, device, pk) -> dict:
+    """The config-3 MoE layer (gpt-oss-20b: H=2880, 32 experts, top-4, I=2880,
+    SwiGLU clamp 7) through kb200_moe_forward at T=4096 (tensor bound: TFLOP/s
+    against the measured sustained dense bf16 rate, the fp16 operands' rate)
+    and T=1 (HBM bound: the four selected experts' MXFP4 bytes per layer
+    against the measured copy bandwidth); outputs of sampled tokens against
+    the unrounded oracle (1e-3); the reference's host path as cpu_baseline."""
+    import numpy as np
+
+    from oracle.pyoracle import Oracle
+
+    E, H, I, K = 32, 2880, 2880, 4
+    orc = Oracle()
+    res = {"workload": "BASELINE config 3: gpt-oss-20b MoE layer, H=2880, E=32, top-4, I=2880, SwiGLU clamp 7"}
+    for T in (4096, 1):
+        w, keep, x, logits, wbytes = moe_layer_inputs(torch, kb, device, T)
+        out = torch.empty(T, H, device=device)
+        ws = torch.empty(kb.moe_workspace_bytes(w, T), dtype=torch.uint8, device=device)
+        status = torch.zeros(1, dtype=torch.int32, device=device)
+        stream = torch.cuda.current_stream()
+        for _ in range(max(3, args.warmup)):
+            kb.moe_forward(w, x, logits, out=out, workspace=ws, status=status)
+        torch.cuda.synchronize()
+        steps = max(20, args.steps)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(device.index or 0) as clocks:
+            a.record(stream)
+            for _ in range(steps):
+                kb.moe_forward(w, x, logits, out=out, workspace=ws, status=status)
+            b.record(stream)
+            torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        flops = 2.0 * T * K * (2 * I * H + H * I)
+        entry = {"tokens": T, "ms_per_layer": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1),
+                 "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "status": int(status.item()),
+                 "clocks": clocks.summary()}
+        if T >= 512:
+            tf = flops / (ms * 1e-3) / 1e12
+            entry["roofline"] = {"bound": "tensor", "kernel": "moe_gemm_kernel (tcgen05 kind::f16)",
+                                 "achieved": round(tf, 1), "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                                 "frac": round(tf / pk["bf16_tflops_sustained"], 4),
+                                 "peak_source": f"{pk['source']} bf16_tflops_sustained (whole layer timed)",
+                                 "frac_of_nominal_mxf8f6f4_4500": round(tf / 4500.0, 4)}
+        else:
+            touched = K * (wbytes // E)
+            gbps = touched / (ms * 1e-3) / 1e9
+            entry["roofline"] = {"bound": "hbm", "kernel": "whole layer (route + grouped MXFP4 GEMV + combine)",
+                                 "achieved": round(gbps, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                 "frac": round(gbps / pk["hbm_gbs"], 4), "algorithmic_bytes": touched,
+                                 "peak_source": f"{pk['source']} hbm_gbs"}
+        # Parity on sampled tokens against the unrounded oracle (fp32
+        # intermediate, as the reference's MoeLayer keeps it).
+        pick = np.unique(np.linspace(0, T - 1, min(T, 6)).astype(np.int64))
+        host = [t.cpu().numpy() for t in keep]
+        xs = x.float().cpu().numpy()[pick]
+        ls = logits.cpu().numpy()[pick]
+        want = orc.moe_forward(xs, ls, *host, hidden=H, inter=I, experts=E, top_k=K, round_act=0)
+        err = rel_err(out.cpu().numpy()[pick], want)
+        entry["parity"] = {"ok": err <= 1e-3, "max_rel_err": err, "tokens_checked": int(len(pick)),
+                           "what": "unrounded oracle (routing, exact MXFP4 decode, fp64 dots, fp32 SwiGLU)"}
+        res[f"T{T}"] = entry
+        if T == 4096 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = moe_cpu_baseline(keep, x, logits, T, min_seconds=min(args.cpu_seconds, 5.0))
+        del w, keep, x, logits, out, ws
+        torch.cuda.empty_cache()
+    big = res["T4096"]
+    res.update({"value": big["tokens_per_s"], "unit": "tokens/s", "roofline": big["roofline"],
+                "parity_ok": all(res[k]["parity"]["ok"] for k in ("T4096", "T1"))})
+    return res
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None, help="profiling case instead of the headline workload")
-    ap.add_argument("--tokens", type=int, default=4096, help="tokens for --case moe / prefill")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="tokens per step (default: 1 for the headline and tp70b, 4096 for --case moe / prefill)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=15.0,
-                    help="host seconds for the default case's CPU baseline (the MoE case uses at most 5)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="host seconds for the default case's CPU baseline (the MoE layer uses at most 5)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="headline only: no config2 / moe / h3_reference / cpu_baseline objects")
     ap.add_argument("--collective", choices=["fused", "peer", "nccl"], default="fused",
                     help="all-reduce of --case tp70b at N > 1: GEMV+exchange fused, peer kernel after the GEMV, NCCL")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="nccl",
@@ -1089,6 +1424,8 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.case in ("moe", "prefill") and not args.tokens:
+        args.tokens = 4096
     if args.case == "moe":
         run_moe(args)
     elif args.case == "prefill":
@@ -1108,7 +1445,7 @@ def main():
             args.steps = 20
         run_reference(args, rank, world)
     else:
-        run_ours(args, rank, world, local_rank)
+        run_default(args, rank, world, local_rank)
 
 
 if __name__ == "__main__":

@@ -35,16 +35,22 @@ thread_local char error_text[512];
 }
 
 unsigned* watchdog_word() {
-    static unsigned* cached[64] = {};
+    // One slot per device, filled on first use; threads that drive different
+    // devices may race to fill a slot, so slots are atomic (every racer
+    // stores the same address).
+    static std::atomic<unsigned*> cached[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return nullptr;
-    if (!cached[dev]) {
+    unsigned* word = cached[dev].load(std::memory_order_acquire);
+    if (!word) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, device_error) == cudaSuccess)
-            cached[dev] = static_cast<unsigned*>(p);
+        if (cudaGetSymbolAddress(&p, device_error) == cudaSuccess) {
+            word = static_cast<unsigned*>(p);
+            cached[dev].store(word, std::memory_order_release);
+        }
     }
-    return cached[dev];
+    return word;
 }
 
 int fail(int status, const char* what) {

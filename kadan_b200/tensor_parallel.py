@@ -180,14 +180,18 @@ class DecodeStack:
                 reduce = [self.outputs[p.name] for p in g if p.mode == "row"] if world > 1 else []
                 self.calls.append((arr, len(jobs), reduce))
 
-    def launch(self, stream) -> None:
+    def launch(self, stream, group_index: Optional[int] = None) -> None:
         """Enqueue one step on `stream` (must be torch's current stream, so
-        that the collectives order after the GEMVs)."""
+        that the collectives order after the GEMVs). group_index: only that
+        dependency group of every layer (a per-launch timing; every rank must
+        pass the same)."""
         import torch.distributed as dist
 
         sptr = ctypes.c_void_p(stream.cuda_stream)
         fused = getattr(self.collective, "fused", False)
-        for arr, n, reduce in self.calls:
+        for i, (arr, n, reduce) in enumerate(self.calls):
+            if group_index is not None and i % len(self.groups) != group_index:
+                continue
             if fused and reduce and n == 1:
                 self.collective.gemv_allreduce(arr[0], stream)
                 continue

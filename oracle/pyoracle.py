@@ -19,8 +19,9 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libkadan_ref.so"
-# The reference checkout the recipes build from (KADAN_REFERENCE overrides).
-REFERENCE_TREE = Path(os.environ.get("KADAN_REFERENCE", "/root/reference"))
+# The reference checkout the recipes build from: the `reference` directory
+# beside this repository, unless KADAN_REFERENCE names another.
+REFERENCE_TREE = Path(os.environ.get("KADAN_REFERENCE", HERE.parent.parent / "reference"))
 
 _u8p = ctypes.POINTER(ctypes.c_uint8)
 _f32p = ctypes.POINTER(ctypes.c_float)

@@ -1,9 +1,14 @@
 """GPU parity of the MXFP4 MoE layer against the pinned oracle.
 
-The device keeps the activation fed to the down projection in fp16, so the
-tight check (1e-3, fp32 accumulation) is against the oracle with the same
-fp16 rounding; the loose check (2e-2) is against the unrounded oracle.
-Tolerances use max|y - ref| / max(max|ref|, 1) (IW/tests/gguf_text.cpp:247-250).
+The device keeps the activation fed to the down projection in fp16. At the
+gpt-oss-20b layer shape the layer is held to 1e-3
+against the unrounded oracle, which keeps that activation in fp32 as the
+reference's MoeLayer::forward does (IW/src/models/text/qwen_layers.cpp:460-476):
+the fp16 rounding moves those outputs by ~6e-5 of their largest magnitude.
+At toy shapes (outputs below 1, where the tolerance's denominator is 1 and
+rounding is relatively larger) the unrounded check is 2e-2 and the tight one
+is against the oracle with the same fp16 rounding. Tolerances use
+max|y - ref| / max(max|ref|, 1) (IW/tests/gguf_text.cpp:247-250).
 """
 from __future__ import annotations
 
@@ -95,6 +100,33 @@ def test_moe_config3_shape_small_batch(kb, oracle, cuda):
     assert rel_err(out.cpu().numpy(), ref16) <= 1e-3
 
 
+@pytest.fixture(scope="module")
+def config3_layer(kb, cuda):
+    E, H, I, K = 32, 2880, 2880, 4
+    return layer(kb, cuda, E=E, H=H, I=I, K=K, seed=21)
+
+
+@pytest.mark.parametrize("T", [1, 64, 512, 4096])
+def test_moe_config3_vs_unrounded_oracle(kb, oracle, cuda, config3_layer, T):
+    """BASELINE config 3 (H=2880, 32 experts, top-4, I=2880) at each of its
+    token counts, against the unrounded oracle (fp32 SwiGLU output, float64
+    dots) at 1e-3 on sampled tokens: every token's output depends only on
+    its own row and logits, so a subset checks the full-size launch."""
+    import torch
+
+    E, H, I, K = 32, 2880, 2880, 4
+    w, dev, host = config3_layer
+    x, logits, xb, ld = inputs(cuda, T, H, E, seed=100 + T)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = kb.moe_forward(w, xb, ld, status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    pick = np.unique(np.linspace(0, T - 1, min(T, 8)).astype(np.int64))
+    want = oracle.moe_forward(x[pick], logits[pick], host["gu_w"], host["gu_s"], host["dn_w"], host["dn_s"], hidden=H,
+                              inter=I, experts=E, top_k=K, round_act=0)
+    assert rel_err(out.cpu().numpy()[pick], want) <= 1e-3
+
+
 def decode_mxfp4_torch(blocks, scales, rows, cols):
     """Exact MXFP4 decode on the GPU (test reference): e2m1(code) * 2^(E-127)."""
     import torch
@@ -108,8 +140,9 @@ def decode_mxfp4_torch(blocks, scales, rows, cols):
 
 
 def test_moe_config3_full_batch_vs_torch_fp32(kb, oracle, cuda):
-    """Config 3 at T=4096 tokens: against a torch fp32 evaluation of the same
-    layer from exactly decoded weights (oracle routing, fp16 activation)."""
+    """Config 3 at T=4096 tokens, every token: against a float64 torch
+    evaluation of the same layer from exactly decoded weights (oracle
+    routing, unrounded SwiGLU output)."""
     import torch
 
     E, H, I, K, T = 32, 2880, 2880, 4, 4096
@@ -129,7 +162,7 @@ def test_moe_config3_full_batch_vs_torch_fp32(kb, oracle, cuda):
         dn = decode_mxfp4_torch(dev["dn_w"].view(E, -1)[e], dev["dn_s"].view(E, -1)[e], H, I)
         h = xt[tok].double() @ gu.double().T
         g, u = h[:, 0::2].clamp(max=7.0), h[:, 1::2].clamp(-7.0, 7.0)
-        a = (g * torch.sigmoid(1.702 * g) * (u + 1)).float().half().double()
+        a = g * torch.sigmoid(1.702 * g) * (u + 1)
         y = a @ dn.double().T
         ref.index_add_(0, tok, wt[:, None] * y)
     torch.cuda.synchronize()

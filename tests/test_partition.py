@@ -99,7 +99,8 @@ def test_source_job_support_matches_reference(kb, ref):
                 want = ref.gguf_batch_supported(in_, out, rows, enc)
                 job = SourceJobC(ctypes.pointer(ident), src, None, 0x1000, 0x2000, in_, out, rows, enc, 1)
                 got = bool(kb.lib.kb200_source_job_supported(ctypes.byref(job)))
-                if enc in no_decoder:
+                if enc in no_decoder and not kb.lib.kb200_encoding_supported(enc):
+                    # Grid-coded encodings before their grids are registered.
                     assert not got
                 else:
                     assert got == want, (enc, in_, out, rows, want)
