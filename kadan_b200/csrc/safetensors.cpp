@@ -4,14 +4,16 @@
 //
 // A safetensors file is an 8-byte little-endian header length, a JSON object
 // mapping tensor names to {dtype, shape, data_offsets} (plus an optional
-// "__metadata__" object of strings), then the payload. The parser here reads
-// only that schema, with the reference's limits and checks: ASCII strings and
-// escapes, unsigned decimal integers, exactly the three descriptor fields, and
-// tensors that tile the payload with no gap or overlap. Failures carry the
-// reference's messages.
+// "__metadata__" object of strings), then the payload. The header is read by
+// a token cursor (lexical checks as each token is taken) driving one generic
+// sequence reader and small rule tables (descriptor fields, dtype names), so
+// the schema is data rather than code. Accepted exactly when the reference
+// accepts: ASCII strings and escapes, unsigned decimal integers, exactly the
+// three descriptor fields, and tensors that tile the payload with no gap or
+// overlap; failures carry the reference's messages, checked against its own
+// reader on malformed and randomly mutated files.
 #include <algorithm>
 #include <cerrno>
-#include <charconv>
 #include <cstdint>
 #include <cstring>
 #include <fcntl.h>
@@ -103,190 +105,220 @@ uint64_t dtype_width(int dtype) {
                                                                    : 1;
 }
 
-// The header schema, read in one forward pass.
-class Header {
+// ---------------------------------------------------------------- lexical
+// A cursor over the header text that hands out JSON tokens on demand: blanks
+// are skipped before every punctuation mark, string or number, and each token
+// is checked as it is taken, so a malformed header fails at the first token
+// that breaks the schema, in text order.
+class Cursor {
 public:
-    Header(const char* text, size_t size, uint64_t metadata_limit)
-        : text_(text), size_(size), metadata_limit_(metadata_limit) {
-    }
+    Cursor(const char* text, size_t size) : at_(text), end_(text + size) {}
 
-    void parse(std::vector<Tensor>& tensors, uint64_t limit) {
-        require(size_ != 0 && text_[0] == '{', "header_start");
-        expect('{');
-        bool metadata = false;
-        if (!take('}')) {
-            do {
-                std::string name = string();
-                expect(':');
-                if (name == "__metadata__") {
-                    require(!metadata, "duplicate_metadata");
-                    metadata = true;
-                    metadata_map();
-                } else {
-                    require(!name.empty() && tensors.size() < limit, "tensor_limit_or_name");
-                    Tensor t;
-                    t.name = std::move(name);
-                    descriptor(t);
-                    tensors.push_back(std::move(t));
-                }
-            } while (take(','));
-            expect('}');
-        }
-        whitespace();
-        require(at_ == size_, "trailing_json");
-    }
-
-private:
-    void whitespace() {
-        while (at_ < size_ && (text_[at_] == ' ' || text_[at_] == '\n' || text_[at_] == '\r' || text_[at_] == '\t'))
-            ++at_;
-    }
-
-    bool take(char c) {
-        whitespace();
-        if (at_ == size_ || text_[at_] != c)
+    // The next significant character is `c`: consume it.
+    bool eat(char c) {
+        blanks();
+        if (at_ == end_ || *at_ != c)
             return false;
         ++at_;
         return true;
     }
 
-    void expect(char c) {
-        require(take(c), "json_syntax");
+    void need(char c) { require(eat(c), "json_syntax"); }
+
+    // Nothing but blanks is left.
+    bool finished() {
+        blanks();
+        return at_ == end_;
     }
 
-    unsigned hex_digit() {
-        require(at_ < size_, "json_escape");
-        const char c = text_[at_++];
-        if (c >= '0' && c <= '9')
-            return unsigned(c - '0');
-        if (c >= 'a' && c <= 'f')
-            return unsigned(c - 'a' + 10);
-        if (c >= 'A' && c <= 'F')
-            return unsigned(c - 'A' + 10);
-        raise("json_escape");
-    }
-
-    std::string string(uint64_t limit = 512) {
-        expect('"');
+    // A quoted ASCII string of at most `limit` characters after unescaping.
+    std::string quoted(uint64_t limit) {
+        need('"');
         std::string out;
-        while (at_ < size_) {
-            unsigned char c = static_cast<unsigned char>(text_[at_++]);
-            if (c == '"')
+        for (;;) {
+            require(at_ != end_, "unterminated_string");
+            const unsigned char raw = static_cast<unsigned char>(*at_++);
+            if (raw == '"')
                 return out;
-            require(c >= 32 && c < 128, "non_ascii_json_string");
-            if (c == '\\') {
-                require(at_ < size_, "json_escape");
-                c = static_cast<unsigned char>(text_[at_++]);
-                switch (c) {
-                case '"': case '\\': case '/': break;
-                case 'b': c = 8; break;
-                case 'f': c = 12; break;
-                case 'n': c = 10; break;
-                case 'r': c = 13; break;
-                case 't': c = 9; break;
-                case 'u': {
-                    unsigned v = 0;
-                    for (int i = 0; i < 4; ++i)
-                        v = v * 16 + hex_digit();
-                    require(v != 0 && v < 128, "non_ascii_json_string");
-                    c = static_cast<unsigned char>(v);
-                    break;
-                }
-                default: raise("json_escape");
-                }
-            }
+            require(raw >= 0x20 && raw < 0x80, "non_ascii_json_string");
+            const char c = raw == '\\' ? escaped() : char(raw);
             require(out.size() < limit, "json_string_limit");
-            out += static_cast<char>(c);
+            out.push_back(c);
         }
-        raise("unterminated_string");
     }
 
-    uint64_t integer() {
-        whitespace();
-        const size_t first = at_;
-        while (at_ < size_ && text_[at_] >= '0' && text_[at_] <= '9')
+    // An unsigned decimal integer: digits only, no leading zero, fits 64 bits.
+    uint64_t natural() {
+        blanks();
+        const char* first = at_;
+        uint64_t value = 0;
+        bool overflow = false;
+        for (; at_ != end_ && *at_ >= '0' && *at_ <= '9'; ++at_) {
+            const uint64_t digit = uint64_t(*at_ - '0');
+            overflow |= value > (UINT64_MAX - digit) / 10;
+            value = value * 10 + digit;
+        }
+        const size_t digits = size_t(at_ - first);
+        require(digits != 0 && !(digits > 1 && *first == '0') && !overflow, "json_integer");
+        return value;
+    }
+
+private:
+    void blanks() {
+        while (at_ != end_ && (*at_ == ' ' || *at_ == '\t' || *at_ == '\n' || *at_ == '\r'))
             ++at_;
-        require(at_ > first && (at_ - first == 1 || text_[first] != '0'), "json_integer");
-        uint64_t v = 0;
-        const auto r = std::from_chars(text_ + first, text_ + at_, v);
-        require(r.ec == std::errc{}, "json_integer");
-        return v;
     }
 
-    void metadata_map() {
-        std::vector<std::string> keys;
-        expect('{');
-        if (take('}'))
-            return;
-        do {
-            std::string key = string();
-            require(keys.size() < 1024 && std::find(keys.begin(), keys.end(), key) == keys.end(),
-                    "metadata_key_limit_or_duplicate");
-            keys.push_back(std::move(key));
-            expect(':');
-            (void)string(metadata_limit_);
-        } while (take(','));
-        expect('}');
+    // The character a backslash sequence stands for (the backslash is taken).
+    char escaped() {
+        // Single-letter escapes: the letter and what it stands for.
+        static constexpr char kSimple[][2] = {{'"', '"'}, {'\\', '\\'}, {'/', '/'}, {'b', '\b'},
+                                              {'f', '\f'}, {'n', '\n'}, {'r', '\r'}, {'t', '\t'}};
+        require(at_ != end_, "json_escape");
+        const char letter = *at_++;
+        for (const auto& e : kSimple)
+            if (e[0] == letter)
+                return e[1];
+        require(letter == 'u', "json_escape");
+        unsigned code = 0;
+        for (int i = 0; i < 4; ++i) {
+            require(at_ != end_, "json_escape");
+            const int nibble = hex_value(*at_++);
+            require(nibble >= 0, "json_escape");
+            code = code << 4 | unsigned(nibble);
+        }
+        // Only \u0001..\u007f: names and values are ASCII.
+        require(code - 1u < 0x7fu, "non_ascii_json_string");
+        return char(code);
     }
 
-    void descriptor(Tensor& t) {
-        expect('{');
-        unsigned fields = 0;
-        do {
-            const std::string key = string();
-            expect(':');
-            unsigned bit = 0;
-            if (key == "dtype") {
-                bit = 1;
-                const std::string d = string();
-                if (d == "U8")
-                    t.dtype = KB200_DTYPE_U8;
-                else if (d == "U32")
-                    t.dtype = KB200_DTYPE_U32;
-                else if (d == "I8")
-                    t.dtype = KB200_DTYPE_I8;
-                else if (d == "F8_E4M3")
-                    t.dtype = KB200_DTYPE_F8_E4M3;
-                else if (d == "F32")
-                    t.dtype = KB200_DTYPE_F32;
-                else if (d == "F16")
-                    t.dtype = KB200_DTYPE_F16;
-                else if (d == "BF16")
-                    t.dtype = KB200_DTYPE_BF16;
-                else
-                    raise("unsupported_dtype");
-            } else if (key == "shape") {
-                bit = 2;
-                expect('[');
-                if (!take(']')) {
-                    do {
-                        require(t.rank < 8, "rank_limit");
-                        t.shape[t.rank++] = integer();
-                    } while (take(','));
-                    expect(']');
-                }
-            } else if (key == "data_offsets") {
-                bit = 4;
-                expect('[');
-                t.begin = integer();
-                expect(',');
-                t.end = integer();
-                expect(']');
-            } else {
-                raise("unknown_tensor_field");
-            }
-            require(!(fields & bit), "duplicate_tensor_field");
-            fields |= bit;
-        } while (take(','));
-        expect('}');
-        require(fields == 7, "missing_tensor_field");
-        require(t.end >= t.begin && t.end - t.begin == mul(t.elements(), dtype_width(t.dtype)), "tensor_byte_size");
+    static int hex_value(char c) {
+        if (c >= '0' && c <= '9')
+            return c - '0';
+        const char lower = char(c | 0x20);
+        return lower >= 'a' && lower <= 'f' ? lower - 'a' + 10 : -1;
     }
 
-    const char* text_;
-    size_t size_, at_ = 0;
-    uint64_t metadata_limit_;
+    const char* at_;
+    const char* end_;
 };
+
+// ----------------------------------------------------------------- schema
+// `open` member (`,` member)* `close`, or `open close` when empty is allowed;
+// `each` reads one member.
+template <class Each>
+void sequence(Cursor& c, char open, char close, bool may_be_empty, Each&& each) {
+    c.need(open);
+    if (may_be_empty && c.eat(close))
+        return;
+    do
+        each();
+    while (c.eat(','));
+    c.need(close);
+}
+
+constexpr uint64_t kNameLimit = 512;     // tensor names, metadata keys, field names
+constexpr size_t kMetadataKeys = 1024;
+
+struct DtypeName {
+    const char* text;
+    int dtype;
+};
+constexpr DtypeName kDtypes[] = {{"U8", KB200_DTYPE_U8},           {"U32", KB200_DTYPE_U32},
+                                 {"I8", KB200_DTYPE_I8},           {"F8_E4M3", KB200_DTYPE_F8_E4M3},
+                                 {"F32", KB200_DTYPE_F32},         {"F16", KB200_DTYPE_F16},
+                                 {"BF16", KB200_DTYPE_BF16}};
+
+void read_dtype(Cursor& c, Tensor& t) {
+    const std::string name = c.quoted(kNameLimit);
+    for (const auto& d : kDtypes)
+        if (name == d.text) {
+            t.dtype = d.dtype;
+            return;
+        }
+    raise("unsupported_dtype");
+}
+
+void read_shape(Cursor& c, Tensor& t) {
+    sequence(c, '[', ']', true, [&] {
+        require(t.rank < 8, "rank_limit");
+        t.shape[t.rank++] = c.natural();
+    });
+}
+
+void read_offsets(Cursor& c, Tensor& t) {
+    c.need('[');
+    t.begin = c.natural();
+    c.need(',');
+    t.end = c.natural();
+    c.need(']');
+}
+
+// The three descriptor fields, each exactly once, in any order.
+struct FieldRule {
+    const char* key;
+    unsigned bit;
+    void (*read)(Cursor&, Tensor&);
+};
+constexpr FieldRule kFields[] = {{"dtype", 1u, read_dtype}, {"shape", 2u, read_shape},
+                                 {"data_offsets", 4u, read_offsets}};
+constexpr unsigned kAllFields = 7u;
+
+void read_descriptor(Cursor& c, Tensor& t) {
+    unsigned seen = 0;
+    sequence(c, '{', '}', false, [&] {
+        const std::string key = c.quoted(kNameLimit);
+        c.need(':');
+        const FieldRule* rule = nullptr;
+        for (const auto& f : kFields)
+            if (key == f.key)
+                rule = &f;
+        if (!rule)
+            raise("unknown_tensor_field");
+        rule->read(c, t);
+        require(!(seen & rule->bit), "duplicate_tensor_field");
+        seen |= rule->bit;
+    });
+    require(seen == kAllFields, "missing_tensor_field");
+    require(t.end >= t.begin && t.end - t.begin == mul(t.elements(), dtype_width(t.dtype)), "tensor_byte_size");
+}
+
+void read_metadata(Cursor& c, uint64_t value_limit) {
+    std::vector<std::string> keys;
+    sequence(c, '{', '}', true, [&] {
+        std::string key = c.quoted(kNameLimit);
+        require(keys.size() < kMetadataKeys && std::find(keys.begin(), keys.end(), key) == keys.end(),
+                "metadata_key_limit_or_duplicate");
+        keys.push_back(std::move(key));
+        c.need(':');
+        (void)c.quoted(value_limit);
+    });
+}
+
+// The whole header: one object of tensor descriptors and at most one
+// "__metadata__" object, nothing after it but blanks.
+void read_header(const char* text, size_t size, uint64_t metadata_limit, uint64_t tensor_limit,
+                 std::vector<Tensor>& tensors) {
+    require(size != 0 && text[0] == '{', "header_start");
+    Cursor c(text, size);
+    bool metadata = false;
+    sequence(c, '{', '}', true, [&] {
+        std::string name = c.quoted(kNameLimit);
+        c.need(':');
+        if (name == "__metadata__") {
+            require(!metadata, "duplicate_metadata");
+            metadata = true;
+            read_metadata(c, metadata_limit);
+            return;
+        }
+        require(!name.empty() && tensors.size() < tensor_limit, "tensor_limit_or_name");
+        Tensor t;
+        t.name = std::move(name);
+        read_descriptor(c, t);
+        tensors.push_back(std::move(t));
+    });
+    require(c.finished(), "trailing_json");
+}
 
 }  // namespace
 }  // namespace st
@@ -360,7 +392,7 @@ kb200_shard* open_shard(const char* root, const char* shard_name, const kb200_sh
         s->data_begin = add(8, header_size);
         std::vector<char> text(static_cast<size_t>(header_size));
         read_at(fd, 8, reinterpret_cast<uint8_t*>(text.data()), header_size);
-        Header(text.data(), text.size(), limits.metadata_value_bytes).parse(s->tensors, limits.tensors);
+        read_header(text.data(), text.size(), limits.metadata_value_bytes, limits.tensors, s->tensors);
         auto& t = s->tensors;
         std::sort(t.begin(), t.end(),
                   [](const Tensor& a, const Tensor& b) { return a.begin == b.begin ? a.end < b.end : a.begin < b.begin; });
