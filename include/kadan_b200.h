@@ -143,13 +143,25 @@ KB200_API int kb200_gemv_path(const kb200_gemv_job* job);
  * decodes the packed chunk to an fp32 tile in scratch and runs an FP32
  * cublasSgemm (Compute::project, h3_compute.cu:1781-2480; decode :2201-2218,
  * SGEMM :2435-2468). Here: Y[t, n] = sum_k decode(W[n, k]) * X[t, k] for all
- * job.rows input rows in one pass over the weights, with fp16 operands (each
- * input row scaled by a power of two first, undone exactly on output) and
- * fp32 accumulation. Q4_K only (KB200_UNSUPPORTED otherwise); job.in a
- * multiple of 256, 16-byte aligned weights and row_bytes. `workspace`: device,
- * 256-byte aligned, at least kb200_gguf_gemm_workspace_bytes(rows, in).
- * Asynchronous on `stream`. */
+ * job.rows input rows in one pass over the weights, decoded in shared memory
+ * to fp16 operands (each input row scaled by a power of two first, undone
+ * exactly on output) with fp32 accumulation. Q4_K, Q6_K and Q8_0
+ * (KB200_UNSUPPORTED otherwise, or when kb200_gguf_gemm_supported is 0);
+ * `workspace`: device, 256-byte aligned, at least
+ * kb200_gguf_gemm_workspace_bytes(rows, in). Asynchronous on `stream`.
+ * job.status (optional) receives bit 0 (1) when a decoded weight is not finite
+ * and bit 1 (2) when a block's scales could put a weight beyond the fp16
+ * operand range (|w| > 65504): that job's outputs are then not valid and the
+ * GEMV path (kb200_gguf_gemv_batch) must compute it. The same condition sets
+ * the 32-bit word at workspace + kb200_gguf_gemm_range_offset(rows, in),
+ * cleared by every call. */
 KB200_API size_t kb200_gguf_gemm_workspace_bytes(uint32_t rows, uint32_t in);
+KB200_API size_t kb200_gguf_gemm_range_offset(uint32_t rows, uint32_t in);
+/* 1 when the GEMM takes the job's weights: one of its encodings, job.in a
+ * multiple of 256, 16-byte aligned weights, row_bytes a multiple of 16 (Q6_K
+ * rows of K values are 210 K / 256 bytes: a multiple of 16 when K is a
+ * multiple of 2048). */
+KB200_API int kb200_gguf_gemm_supported(const kb200_gemv_job* job);
 KB200_API int kb200_gguf_gemm(const kb200_gemv_job* job, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
@@ -190,6 +202,21 @@ KB200_API void* kb200_context_stream(kb200_context* ctx);
  * three workers and the caller, IW/include/kadan/packed_read_team.hpp:22-275).
  * Sources may then run concurrently on disjoint rows. */
 KB200_API int kb200_context_set_read_lanes(kb200_context* ctx, int lanes);
+
+/* Work the context's calls have issued so far (cumulative; for tests and
+ * telemetry). A projection of more than KB200_BATCH_ROWS input rows runs on
+ * the tensor-core GEMM when kb200_gguf_gemm_supported takes its weights (one
+ * GEMM launch per job or bank/staging chunk: the reference's switch from the
+ * batched GEMV to decode + GEMM, h3_compute.cu:1863-1865); everything else
+ * runs as GEMV batches. gemm_fallbacks counts GEMM jobs recomputed on the GEMV
+ * path because a block's scales could exceed the fp16 operand range. */
+typedef struct kb200_context_counters {
+    uint64_t calls;          /* kb200_dense_gguf_batch / _source_batch calls that reached the device */
+    uint64_t gemm_launches;  /* kb200_gguf_gemm launches */
+    uint64_t gemv_batches;   /* kb200_gguf_gemv_batch calls (one launch per encoding each) */
+    uint64_t gemm_fallbacks; /* GEMM jobs recomputed on the GEMV path */
+} kb200_context_counters;
+KB200_API int kb200_context_counters_get(kb200_context* ctx, kb200_context_counters* out);
 
 /* Caller-managed device-resident packed rows for kb200_dense_gguf_batch: a
  * synchronous upload of `bytes` host bytes into a 256-byte aligned device

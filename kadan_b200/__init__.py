@@ -87,6 +87,13 @@ class HostJob(ctypes.Structure):
     ]
 
 
+class ContextCounters(ctypes.Structure):
+    """kb200_context_counters: work a context's calls issued (cumulative)."""
+
+    _fields_ = [("calls", ctypes.c_uint64), ("gemm_launches", ctypes.c_uint64), ("gemv_batches", ctypes.c_uint64),
+                ("gemm_fallbacks", ctypes.c_uint64)]
+
+
 RESULT_UNSUPPORTED, RESULT_UNVALIDATED, RESULT_FINITE = 0, 1, 2
 MOE_SWIGLU_OAI, MOE_SILU = 0, 1
 
@@ -139,6 +146,10 @@ def _load() -> ctypes.CDLL:
     lib.kb200_gguf_gemm_workspace_bytes.restype = c_size
     lib.kb200_gguf_gemm_workspace_bytes.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
     lib.kb200_gguf_gemm.argtypes = [ctypes.POINTER(GemvJob), vp, c_size, vp]
+    lib.kb200_gguf_gemm_supported.argtypes = [ctypes.POINTER(GemvJob)]
+    lib.kb200_gguf_gemm_range_offset.restype = c_size
+    lib.kb200_gguf_gemm_range_offset.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
+    lib.kb200_context_counters_get.argtypes = [vp, ctypes.POINTER(ContextCounters)]
     lib.kb200_weight_boundary.restype = c_size
     lib.kb200_weight_boundary.argtypes = [c_size, ctypes.POINTER(ctypes.c_uint64), c_size, c_size]
     lib.kb200_gguf_batch_partition.argtypes = [c_size, c_size, c_int, ctypes.POINTER(ctypes.c_uint64), c_size,
@@ -235,8 +246,18 @@ def gemm_workspace_bytes(rows: int, in_: int) -> int:
     return int(lib.kb200_gguf_gemm_workspace_bytes(rows, in_))
 
 
+def gemm_supported(job: GemvJob) -> bool:
+    """kb200_gguf_gemm_supported: the prefill GEMM takes the job's weights."""
+    return bool(lib.kb200_gguf_gemm_supported(ctypes.byref(job)))
+
+
+def gemm_range_offset(rows: int, in_: int) -> int:
+    """Byte offset in the GEMM workspace of its fp16-range word."""
+    return int(lib.kb200_gguf_gemm_range_offset(rows, in_))
+
+
 def gguf_gemm(job: GemvJob, workspace, stream=None) -> None:
-    """Prefill GEMM of one Q4_K job (all of job.rows at once) on the tensor cores."""
+    """Prefill GEMM of one Q4_K, Q6_K or Q8_0 job (all of job.rows at once) on the tensor cores."""
     check(lib.kb200_gguf_gemm(ctypes.byref(job), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
                               _stream_ptr(stream)))
 
@@ -308,6 +329,12 @@ class Context:
     @property
     def stream_ptr(self) -> int:
         return int(lib.kb200_context_stream(self.handle))
+
+    def counters(self) -> dict:
+        """kb200_context_counters_get: calls, GEMM launches, GEMV batches, GEMM fallbacks so far."""
+        c = ContextCounters()
+        check(lib.kb200_context_counters_get(self.handle, ctypes.byref(c)))
+        return {name: int(getattr(c, name)) for name, _ in ContextCounters._fields_}
 
     def set_read_lanes(self, lanes: int) -> None:
         """Host threads (caller included) that read packed-row sources."""

@@ -5,8 +5,10 @@
 // download, one stream synchronisation per call. Over packed-row sources:
 // bank hits as one launch, misses streamed through two pinned staging halves
 // and admitted into the bank once they decoded finite.
+#include <algorithm>
 #include <climits>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -26,6 +28,7 @@ struct kb200_context {
     cudaEvent_t staged[2] = {nullptr, nullptr};  // source batch: staging half done
     int read_lanes = 4;                           // source reads: 3 workers + the caller
     kb200::ReadTeam* team = nullptr;              // created by the first source batch
+    kb200_context_counters counters = {};         // launches of every call, cumulative
 };
 
 namespace kb200 {
@@ -119,6 +122,72 @@ void stage_inputs(const Job* jobs, size_t count, const InputLayout& l, uint8_t* 
             std::memcpy(host + l.at[j] * sizeof(float), jobs[j].input, size_t(jobs[j].rows) * jobs[j].in * sizeof(float));
 }
 
+// The reference's switch between its two projection paths: packed jobs of
+// more than gguf_batch_rows input rows leave the batched GEMV for decode +
+// GEMM (`matvec = packed && rows <= 8`, h3_compute.cu:1863-1865). Here those
+// jobs run on the tensor-core GEMM when it takes their weights
+// (KB200_PREFILL_GEMM=0 keeps every job on the GEMV path).
+bool prefill_gemm_enabled() {
+    static const bool on = [] {
+        const char* s = std::getenv("KB200_PREFILL_GEMM");
+        return !s || std::atoi(s) != 0;
+    }();
+    return on;
+}
+
+bool to_gemm(const kb200_gemv_job& j) {
+    return j.rows > KB200_BATCH_ROWS && prefill_gemm_enabled() && gemm_eligible(j);
+}
+
+// Device scratch the GEMM jobs among `jobs` need (one at a time, in stream order).
+size_t gemm_scratch(const kb200_gemv_job* jobs, size_t count) {
+    size_t need = 0;
+    for (size_t j = 0; j < count; ++j)
+        if (to_gemm(jobs[j]))
+            need = std::max(need, kb200_gguf_gemm_workspace_bytes(jobs[j].rows, jobs[j].in));
+    return need;
+}
+
+// Enqueue device jobs on the context's stream: one GEMM per job to_gemm
+// selects (reporting to `gemm_status`: bit 0 a non-finite weight, bit 1 a
+// weight beyond the fp16 operand range), every other job in one GEMV batch.
+int launch_projections(kb200_context* c, const kb200_gemv_job* jobs, size_t count, void* scratch, size_t scratch_bytes,
+                       unsigned* gemm_status) {
+    std::vector<kb200_gemv_job> gemv;
+    gemv.reserve(count);
+    for (size_t j = 0; j < count; ++j) {
+        if (!to_gemm(jobs[j])) {
+            gemv.push_back(jobs[j]);
+            continue;
+        }
+        kb200_gemv_job g = jobs[j];
+        g.status = gemm_status;
+        if (const int s = kb200_gguf_gemm(&g, scratch, scratch_bytes, c->stream))
+            return s;
+        ++c->counters.gemm_launches;
+    }
+    if (!gemv.empty()) {
+        if (const int s = kb200_gguf_gemv_batch(gemv.data(), gemv.size(), c->stream))
+            return s;
+        ++c->counters.gemv_batches;
+    }
+    return KB200_OK;
+}
+
+// The GEMM jobs among `jobs` again, on the GEMV path (a block's scales put a
+// weight beyond the fp16 operands the GEMM uses).
+int rerun_gemm_jobs(kb200_context* c, const kb200_gemv_job* jobs, size_t count) {
+    std::vector<kb200_gemv_job> again;
+    for (size_t j = 0; j < count; ++j)
+        if (to_gemm(jobs[j]))
+            again.push_back(jobs[j]);
+    if (again.empty())
+        return KB200_OK;
+    c->counters.gemm_fallbacks += again.size();
+    ++c->counters.gemv_batches;
+    return kb200_gguf_gemv_batch(again.data(), again.size(), c->stream);
+}
+
 }  // namespace
 }  // namespace kb200
 
@@ -163,6 +232,13 @@ void kb200_context_destroy(kb200_context* c) {
 
 void* kb200_context_stream(kb200_context* c) {
     return c ? static_cast<void*>(c->stream) : nullptr;
+}
+
+int kb200_context_counters_get(kb200_context* c, kb200_context_counters* out) {
+    if (!c || !out)
+        return fail(KB200_INVALID, "null context or output");
+    *out = c->counters;
+    return KB200_OK;
 }
 
 int kb200_context_set_read_lanes(kb200_context* c, int lanes) {
@@ -233,57 +309,70 @@ int kb200_dense_gguf_batch(
         return s;
 
     DeviceScope scope(c->device);
-    // Device layout: [inputs][outputs][status]; host staging mirrors it.
+    ++c->counters.calls;
+    // Device jobs over the workspace's spans (addresses filled in once it exists).
+    std::vector<kb200_gemv_job> device_jobs(count);
+    for (size_t j = 0; j < count; ++j) {
+        const auto& job = jobs[j];
+        device_jobs[j] = kb200_gemv_job{job.weights, nullptr, nullptr, nullptr, job.row_bytes, job.out,
+                                        job.in,      job.out, job.rows, job.encoding};
+    }
+    // Device layout: [inputs][outputs][status: GEMV, GEMM][GEMM scratch];
+    // host staging mirrors all but the scratch.
     const size_t in_bytes = inputs.floats * sizeof(float), out_bytes = outputs * sizeof(float);
     const size_t status_at = up16(in_bytes + out_bytes);
-    const size_t total = status_at + 16;
-    if (const int s = ensure(c, total, total))
+    const size_t scratch_at = up256(status_at + 16), scratch = gemm_scratch(device_jobs.data(), count);
+    if (const int s = ensure(c, scratch_at + scratch, status_at + 16))
         return s;
     auto* dev = static_cast<uint8_t*>(c->workspace);
     auto* host = static_cast<uint8_t*>(c->pinned);
     stage_inputs(jobs, count, inputs, host);
-    std::memset(host + status_at, 0, sizeof(unsigned));
+    std::memset(host + status_at, 0, 2 * sizeof(unsigned));
     cudaError_t e = cudaMemcpyAsync(dev, host, in_bytes, cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess)
-        e = cudaMemcpyAsync(dev + status_at, host + status_at, sizeof(unsigned), cudaMemcpyHostToDevice, c->stream);
+        e = cudaMemcpyAsync(dev + status_at, host + status_at, 2 * sizeof(unsigned), cudaMemcpyHostToDevice,
+                            c->stream);
     if (e != cudaSuccess)
         return cuda_fail(e, "input upload");
     if (cancelled(cancel)) {
         cudaStreamSynchronize(c->stream);
         return fail(KB200_CANCELLED, "cancelled after upload");
     }
-    std::vector<kb200_gemv_job> device_jobs(count);
     auto* status = reinterpret_cast<unsigned*>(dev + status_at);
     for (size_t j = 0; j < count; ++j) {
-        const auto& job = jobs[j];
-        device_jobs[j] = kb200_gemv_job{
-            job.weights,
-            reinterpret_cast<const float*>(dev) + inputs.at[j],
-            reinterpret_cast<float*>(dev + in_bytes) + output_at[j],
-            job.validated ? nullptr : status,
-            job.row_bytes,
-            job.out,
-            job.in,
-            job.out,
-            job.rows,
-            job.encoding};
+        device_jobs[j].input = reinterpret_cast<const float*>(dev) + inputs.at[j];
+        device_jobs[j].output = reinterpret_cast<float*>(dev + in_bytes) + output_at[j];
+        device_jobs[j].status = jobs[j].validated ? nullptr : status;
     }
-    if (const int s = kb200_gguf_gemv_batch(device_jobs.data(), count, c->stream)) {
+    if (const int s = launch_projections(c, device_jobs.data(), count, dev + scratch_at, scratch, status + 1)) {
         cudaStreamSynchronize(c->stream);
         return s;
     }
-    e = cudaMemcpyAsync(host + in_bytes, dev + in_bytes, status_at + sizeof(unsigned) - in_bytes,
-                        cudaMemcpyDeviceToHost, c->stream);
+    const size_t download = status_at + 2 * sizeof(unsigned) - in_bytes;
+    e = cudaMemcpyAsync(host + in_bytes, dev + in_bytes, download, cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess)
         e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess)
         return cuda_fail(e, "output download");
     if (cancelled(cancel))
         return fail(KB200_CANCELLED, "cancelled after download");
-    unsigned invalid = 0;
+    unsigned invalid = 0, gemm = 0;
     std::memcpy(&invalid, host + status_at, sizeof(invalid));
-    if (invalid)
+    std::memcpy(&gemm, host + status_at + sizeof(unsigned), sizeof(gemm));
+    if (invalid || (gemm & 1u))
         return fail(KB200_NONFINITE_WEIGHT, "a decoded weight is not finite");
+    if (gemm & 2u) {
+        // A weight beyond the GEMM's fp16 operands: those jobs again on the GEMV path.
+        if (const int s = rerun_gemm_jobs(c, device_jobs.data(), count)) {
+            cudaStreamSynchronize(c->stream);
+            return s;
+        }
+        e = cudaMemcpyAsync(host + in_bytes, dev + in_bytes, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+        if (e == cudaSuccess)
+            e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess)
+            return cuda_fail(e, "output download");
+    }
     for (size_t j = 0; j < count; ++j)
         std::memcpy(jobs[j].output, host + in_bytes + output_at[j] * sizeof(float),
                     size_t(jobs[j].rows) * jobs[j].out * sizeof(float));
@@ -366,6 +455,7 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
         return fail(KB200_INVALID, "the weight bank holds another device's memory");
 
     DeviceScope scope(c->device);
+    ++c->counters.calls;
     // Bank lookups (h3_compute.cu:4063-4115): hits run from the bank, misses stream.
     std::vector<Chunk> hits, misses;
     for (size_t j = 0; j < count; ++j) {
@@ -400,13 +490,25 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
         k = g.end;
     }
 
-    // Device layout: [inputs][outputs][2 status words][staging half 0][half 1];
-    // the pinned host buffer mirrors it.
+    // GEMM scratch: every chunk of a job has the job's rows, in and row pitch,
+    // and both bank entries and staging offsets are 256-byte aligned.
+    size_t scratch = 0;
+    for (size_t j = 0; j < count; ++j) {
+        const auto& job = jobs[j];
+        const uint64_t row_bytes = job.in / kb200_block_values(job.encoding) * kb200_block_bytes(job.encoding);
+        const kb200_gemv_job probe{reinterpret_cast<const void*>(uintptr_t(256)), nullptr, nullptr, nullptr,
+                                   size_t(row_bytes), job.out, job.in, job.out, job.rows, job.encoding};
+        scratch = std::max(scratch, gemm_scratch(&probe, 1));
+    }
+    // Device layout: [inputs][outputs][status: half 0, half 1, bank hits]
+    // [staging half 0][half 1][GEMM scratch]; the pinned host buffer mirrors
+    // all but the scratch.
     const size_t in_bytes = up256(inputs.floats * sizeof(float)), out_bytes = up256(outputs * sizeof(float));
     const size_t status_at = in_bytes + out_bytes, staging_at = status_at + 256;
     const size_t total = staging_at + (groups.empty() ? 0 : 2 * kHalf);
-    if (const int s = ensure(c, total, total))
+    if (const int s = ensure(c, total + scratch, total))
         return s;
+    uint8_t* dev_scratch = static_cast<uint8_t*>(c->workspace) + total;
     for (cudaEvent_t& e : c->staged)
         if (!e)
             if (const cudaError_t err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming))
@@ -434,22 +536,31 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
     if (const cudaError_t e = cudaMemcpyAsync(dev, host, inputs.floats * sizeof(float), cudaMemcpyHostToDevice,
                                               c->stream))
         return abandon(cuda_fail(e, "input upload"));
+    std::vector<kb200_gemv_job> hit_jobs;
     if (!hits.empty()) {
         // Bank entries were checked finite when they were admitted.
-        std::vector<kb200_gemv_job> launch;
         for (const Chunk& ch : hits)
-            launch.push_back(device_job(ch, ch.resident, nullptr));
-        if (const int s = kb200_gguf_gemv_batch(launch.data(), launch.size(), c->stream))
+            hit_jobs.push_back(device_job(ch, ch.resident, nullptr));
+        if (const cudaError_t e = cudaMemsetAsync(dev_status + 2, 0, sizeof(unsigned), c->stream))
+            return abandon(cuda_fail(e, "status clear"));
+        if (const int s = launch_projections(c, hit_jobs.data(), hit_jobs.size(), dev_scratch, scratch, dev_status + 2))
             return abandon(s);
     }
+    std::vector<std::vector<kb200_gemv_job>> group_jobs(groups.size());
     // Group g uses half g % 2; before it is refilled, group g - 2 is finished:
     // its status read, and its chunks admitted while their bytes are still staged.
     auto finish = [&](size_t g) -> int {
         const size_t half = g % 2;
         if (const cudaError_t e = cudaEventSynchronize(c->staged[half]))
             return cuda_fail(e, "streamed group");
-        if (host_status[half])
+        if (host_status[half] & 1u)
             return fail(KB200_NONFINITE_WEIGHT, "a decoded weight is not finite");
+        // A weight beyond the GEMM's fp16 operands: the group's GEMM chunks
+        // again on the GEMV path while their bytes are staged (the half is
+        // refilled later on the same stream).
+        if (host_status[half] & 2u)
+            if (const int s = rerun_gemm_jobs(c, group_jobs[g].data(), group_jobs[g].size()))
+                return s;
         if (cancelled(cancel))
             return fail(KB200_CANCELLED, "cancelled after a streamed group");
         if (!bank)
@@ -482,7 +593,7 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
         if (cancelled(cancel))
             return abandon(fail(KB200_CANCELLED, "cancelled before a streamed group"));
         uint8_t* staged = host_stage + half * kHalf;
-        std::vector<kb200_gemv_job> launch;
+        std::vector<kb200_gemv_job>& launch = group_jobs[g];
         reads.clear();
         for (size_t k = groups[g].begin; k < groups[g].end; ++k) {
             const Chunk& m = misses[k];
@@ -499,7 +610,7 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
             e = cudaMemsetAsync(dev_status + half, 0, sizeof(unsigned), c->stream);
         if (e != cudaSuccess)
             return abandon(cuda_fail(e, "staging upload"));
-        if (const int s = kb200_gguf_gemv_batch(launch.data(), launch.size(), c->stream))
+        if (const int s = launch_projections(c, launch.data(), launch.size(), dev_scratch, scratch, dev_status + half))
             return abandon(s);
         e = cudaMemcpyAsync(const_cast<unsigned*>(host_status + half), dev_status + half, sizeof(unsigned),
                             cudaMemcpyDeviceToHost, c->stream);
@@ -511,7 +622,8 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
     for (size_t g = groups.size() >= 2 ? groups.size() - 2 : 0; g < groups.size(); ++g)
         if (const int s = finish(g))
             return abandon(s);
-    cudaError_t e = cudaMemcpyAsync(host + in_bytes, dev_out, outputs * sizeof(float), cudaMemcpyDeviceToHost,
+    // Outputs and, right after them, the status words (the bank hits' last).
+    cudaError_t e = cudaMemcpyAsync(host + in_bytes, dev_out, out_bytes + 3 * sizeof(unsigned), cudaMemcpyDeviceToHost,
                                     c->stream);
     if (e == cudaSuccess)
         e = cudaStreamSynchronize(c->stream);
@@ -519,6 +631,18 @@ int kb200_dense_gguf_source_batch(kb200_context* c, kb200_bank* bank, const kb20
         return abandon(cuda_fail(e, "output download"));
     if (cancelled(cancel))
         return fail(KB200_CANCELLED, "cancelled after download");
+    const unsigned hit_status = hits.empty() ? 0u : host_status[2];
+    if (hit_status & 1u)
+        return fail(KB200_NONFINITE_WEIGHT, "a decoded weight is not finite");
+    if (hit_status & 2u) {
+        if (const int s = rerun_gemm_jobs(c, hit_jobs.data(), hit_jobs.size()))
+            return abandon(s);
+        e = cudaMemcpyAsync(host + in_bytes, dev_out, outputs * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
+        if (e == cudaSuccess)
+            e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess)
+            return abandon(cuda_fail(e, "output download"));
+    }
     for (size_t j = 0; j < count; ++j)
         std::memcpy(jobs[j].output, host + in_bytes + output_at[j] * sizeof(float),
                     size_t(jobs[j].rows) * jobs[j].out * sizeof(float));

@@ -839,10 +839,12 @@ template <int NT> constexpr int q6_seg_budget() {
 }
 constexpr uint32_t kQ6MinUnitsPerCta = 2;
 
-// NT = 1 (4 rows per pass): 3 stages; NT = 2 (8 rows): 2 stages, so that the
-// twice larger activation segment still leaves room for two CTAs per SM.
-template <int NT> struct Q6Layout {
-    static constexpr int kStages = NT == 1 ? 3 : 2;
+// S stages of one chunk each. NT = 1 (4 rows per pass): 3 stages (two CTAs per
+// SM) or 2 stages (three CTAs per SM: more warps to hide the integer chains
+// of the 6-bit unpack, the same bytes in flight); NT = 2 (8 rows): 2 stages,
+// so that the twice larger activation segment still leaves room for two CTAs.
+template <int NT, int S> struct Q6Layout {
+    static constexpr int kStages = S;
     static constexpr int kSegBudget = q6_seg_budget<NT>();
     static constexpr int kStagesOff = 0;
     static constexpr int kSegOff = kStages * kQ6StageBytes;
@@ -851,8 +853,14 @@ template <int NT> struct Q6Layout {
     static constexpr int kBarOff = kRedOff + kRedBytes;
     static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
 };
-static_assert(2 * (Q6Layout<1>::kTotal + 128 + 1024) <= 228 * 1024, "two Q6_K CTAs per SM (NT = 1)");
-static_assert(2 * (Q6Layout<2>::kTotal + 128 + 1024) <= 228 * 1024, "two Q6_K CTAs per SM (NT = 2)");
+static_assert(2 * (Q6Layout<1, 3>::kTotal + 128 + 1024) <= 228 * 1024, "two Q6_K CTAs per SM (NT = 1)");
+static_assert(3 * (Q6Layout<1, 2>::kTotal + 128 + 1024) <= 228 * 1024, "three Q6_K CTAs per SM (NT = 1, 2 stages)");
+static_assert(2 * (Q6Layout<2, 2>::kTotal + 128 + 1024) <= 228 * 1024, "two Q6_K CTAs per SM (NT = 2)");
+
+// CTAs per SM the kernel is compiled for (register budget).
+template <int NT, int S> constexpr int q6_min_ctas() {
+    return NT == 1 && S == 2 ? 3 : 2;
+}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
     asm volatile(
@@ -951,9 +959,9 @@ __device__ __forceinline__ void q6k_block(const uint8_t* bg, const uint8_t* b8, 
 // its 8 blocks split over the 4 consumer warps (2 each), which add up in
 // shared memory at the end of a piece. Everything else (pieces, fixup,
 // programmatic dependent launch) is the Q4_K kernel's.
-template <int NT>
-__global__ void __launch_bounds__(kThreadsQ, 2) gemv_q6k_mma_kernel(const __grid_constant__ MmaParams p) {
-    using L = Q6Layout<NT>;
+template <int NT, int S>
+__global__ void __launch_bounds__(kThreadsQ, q6_min_ctas<NT, S>()) gemv_q6k_mma_kernel(const __grid_constant__ MmaParams p) {
+    using L = Q6Layout<NT, S>;
     constexpr int kStages = L::kStages;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
@@ -1184,6 +1192,7 @@ struct Tuning {
     uint32_t min_units = kMinUnitsPerCta;       // KB200_GEMV_MIN_UNITS=<units per CTA>
     uint32_t q6_min_units = kQ6MinUnitsPerCta;  // KB200_GEMV_Q6K_MIN_UNITS=<units per CTA>
     int ctas_per_sm = 0;                        // KB200_GEMV_CTAS_PER_SM=<n>: grid slots per SM (0: all that fit)
+    int q6_stages = 3;                          // KB200_GEMV_Q6K_STAGES=2|3: ring depth at 1-4 rows per pass
 };
 
 const Tuning& tuning() {
@@ -1197,6 +1206,8 @@ const Tuning& tuning() {
             v.min_units = uint32_t(std::max(1, std::atoi(s)));
         if (const char* s = std::getenv("KB200_GEMV_Q6K_MIN_UNITS"))
             v.q6_min_units = uint32_t(std::max(1, std::atoi(s)));
+        if (const char* s = std::getenv("KB200_GEMV_Q6K_STAGES"))
+            v.q6_stages = std::atoi(s) == 2 ? 2 : 3;
         if (const char* s = std::getenv("KB200_GEMV_L2_PREFETCH"))
             v.prefetch = uint32_t(std::max(0, std::min(64, std::atoi(s))));
         return v;
@@ -1204,19 +1215,19 @@ const Tuning& tuning() {
     return t;
 }
 
-template <int NT> int q6k_slots() {
+template <int NT, int S> int q6k_slots() {
     static int blocks_per_sm[64] = {};
     static std::mutex lock;
     int dev = 0;
     cudaGetDevice(&dev);
-    constexpr int smem = Q6Layout<NT>::kTotal + 128;
+    constexpr int smem = Q6Layout<NT, S>::kTotal + 128;
     std::lock_guard<std::mutex> guard(lock);
     if (!blocks_per_sm[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_mma_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_mma_kernel<NT, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_mma_kernel attribute");
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_mma_kernel<NT>, kThreadsQ, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_mma_kernel<NT, S>, kThreadsQ, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_mma_kernel occupancy");
         blocks_per_sm[dev] = n > 0 ? n : 1;
@@ -1285,7 +1296,8 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         max_rows = std::max(max_rows, int(std::min(j->rows, uint32_t(KB200_BATCH_ROWS))));
     const int nt = max_rows <= 4 ? 1 : 2;
     const uint32_t group_rows = uint32_t(4 * nt);
-    int slots = nt == 1 ? q6k_slots<1>() : q6k_slots<2>();
+    const bool two_stage = nt == 1 && tuning().q6_stages == 2;
+    int slots = nt == 2 ? q6k_slots<2, 2>() : two_stage ? q6k_slots<1, 2>() : q6k_slots<1, 3>();
     if (slots <= 0)
         return -slots;
     if (tuning().ctas_per_sm > 0)
@@ -1345,15 +1357,17 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
         cfg.blockDim = dim3(kThreadsQ);
-        cfg.dynamicSmemBytes = (nt == 1 ? Q6Layout<1>::kTotal : Q6Layout<2>::kTotal) + 128;
+        cfg.dynamicSmemBytes = (nt == 2 ? Q6Layout<2, 2>::kTotal : two_stage ? Q6Layout<1, 2>::kTotal
+                                                                             : Q6Layout<1, 3>::kTotal) + 128;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t e = nt == 1 ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1>, p)
-                                      : cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<2>, p);
+        const cudaError_t e = nt == 2     ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<2, 2>, p)
+                              : two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 2>, p)
+                                          : cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 3>, p);
         if (e != cudaSuccess)
             return cuda_fail(e, "gemv_q6k_mma_kernel launch");
     }

@@ -55,6 +55,9 @@ int sm_count();
 // launch gave up, its cut tiles' partial words may be left behind). Synchronous.
 void clear_gemv_fixups();
 
+// The prefill GEMM (kb200_gguf_gemm) takes the job's weights.
+bool gemm_eligible(const kb200_gemv_job& j);
+
 // The CUDA device whose memory a weight bank holds, or -1 for a bank over
 // caller-supplied operations.
 int bank_device(const kb200_bank* bank);

@@ -225,3 +225,22 @@ def test_new_entry_points_reject_bad_arguments_on_host(kb):
     assert kb.lib.kb200_status_name(kb.QUARANTINED) == b"weight_cleanup_unconfirmed"
     assert kb.lib.kb200_status_name(kb.NONFINITE_BIAS) == b"h3_cuda_nonfinite_bias"
     assert kb.lib.kb200_status_name(kb.NONFINITE_OUTPUT) == b"h3_cuda_nonfinite_output"
+
+
+def test_gemm_supported_predicate(kb):
+    """kb200_gguf_gemm_supported (host only): Q4_K, Q6_K and Q8_0 in whole
+    256-value steps with 16-byte aligned rows of a 16-byte multiple pitch."""
+    def job(enc, in_, row_bytes, ptr=0x10000):
+        return kb.GemvJob(ptr, 0x200000, 0x300000, None, row_bytes, 64, in_, 64, 16, enc)
+
+    assert kb.gemm_supported(job(kb.Q4_K, 4096, 2304))
+    assert kb.gemm_supported(job(kb.Q6_K, 8192, 6720))
+    assert kb.gemm_supported(job(kb.Q6_K, 4096, 3360))
+    assert kb.gemm_supported(job(kb.Q8_0, 4096, 4352))
+    assert not kb.gemm_supported(job(kb.Q6_K, 1024, 840))   # 840-byte rows: not a 16-byte pitch
+    assert kb.gemm_supported(job(kb.Q6_K, 1024, 848))       # the same rows padded
+    assert not kb.gemm_supported(job(kb.Q8_0, 4128, 4386))  # not whole 256-value steps
+    assert not kb.gemm_supported(job(kb.Q4_K, 4096, 2304, ptr=0x10008))  # unaligned weights
+    assert not kb.gemm_supported(job(kb.Q4_K, 4096, 2288))  # rows shorter than K
+    for enc in (kb.Q3_K, kb.IQ4_NL, kb.IQ4_XS, kb.BF16, kb.F32):
+        assert not kb.gemm_supported(job(enc, 4096, 8192))

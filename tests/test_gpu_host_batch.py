@@ -351,3 +351,84 @@ def test_single_source_projection_with_bias(kb, oracle, cuda):
     finally:
         bank.close()
         ctx.close()
+
+
+@pytest.mark.parametrize("enc,in_,out", [(1, 4096, 512), (3, 4096, 256), (2, 4096, 384)], ids=["q4_k", "q6_k", "q8_0"])
+def test_prefill_through_dense_gguf_source(kb, oracle, cuda, enc, in_, out):
+    """A T = 512 prefill through kb200_dense_gguf_source, the worker's own
+    prefill call (IW/src/models/text/gguf_weights.cpp:570-582), runs on the
+    tensor-core GEMM: one GEMM launch per chunk and no GEMV batch, when the
+    rows stream from their source and again when they are bank hits; the
+    outputs match the oracle (1e-3)."""
+    from kadan_b200.weight_bank import WeightBank, dense_gguf_source
+
+    jobs, refs = source_jobs(kb, oracle, [(enc, in_, out, 512)])
+    job = jobs[0]
+    ctx = kb.Context(0)
+    bank = WeightBank.cuda(0, 64 << 20)
+    try:
+        before = ctx.counters()
+        assert dense_gguf_source(ctx, bank, job) == kb.RESULT_FINITE
+        after = ctx.counters()
+        assert after["gemm_launches"] - before["gemm_launches"] == 1
+        assert after["gemv_batches"] == before["gemv_batches"]
+        assert rows_read(job).tolist() == [1] * out
+        assert rel_err(job.y, refs[0]) <= TOL
+        job.reads.clear()
+        job.y[:] = np.nan
+        assert dense_gguf_source(ctx, bank, job) == kb.RESULT_FINITE
+        hits = ctx.counters()
+        assert not job.reads
+        assert hits["gemm_launches"] - after["gemm_launches"] == 1 and hits["gemm_fallbacks"] == 0
+        assert rel_err(job.y, refs[0]) <= TOL
+    finally:
+        bank.close()
+        ctx.close()
+
+
+def test_dense_gguf_batch_switches_at_eight_rows(kb, oracle, cuda):
+    """The resident batch path keeps jobs of up to 8 rows on the GEMV (one
+    batch) and sends 9 rows and more to the GEMM, as the reference's
+    project switches (h3_compute.cu:1863-1865); both within tolerance."""
+    from kadan_b200 import synth
+
+    ctx = kb.Context(0)
+    in_, out = 2048, 320
+    w = synth.gguf(kb.Q6_K, out, in_, seed=3)
+    ptr = ctx.upload(w)
+    try:
+        for rows, gemm in ((8, 0), (9, 1), (200, 1)):
+            x = synth.activations(rows * in_, seed=rows).reshape(rows, in_)
+            y = np.full((rows, out), np.nan, dtype=np.float32)
+            before = ctx.counters()
+            assert ctx.dense_gguf_batch([kb.host_job(kb.Q6_K, ptr, x, y, in_=in_, out=out)]) == kb.RESULT_UNVALIDATED
+            after = ctx.counters()
+            assert after["gemm_launches"] - before["gemm_launches"] == gemm
+            assert after["gemv_batches"] - before["gemv_batches"] == 1 - gemm
+            assert rel_err(y, oracle.gemv_f64(kb.Q6_K, w, x, in_, out)) <= TOL
+    finally:
+        ctx.free(ptr)
+        ctx.close()
+
+
+def test_gemm_range_fallback_through_the_boundary(kb, oracle, cuda):
+    """A Q8_0 block whose weights exceed fp16 (d = 1000): the boundary's GEMM
+    reports it and the call recomputes that job on the GEMV path, so the
+    outputs still match the oracle; the counters record one fallback."""
+    from kadan_b200 import synth
+
+    ctx = kb.Context(0)
+    rows, in_, out = 64, 1024, 96
+    w = synth.q8_0(out, in_, seed=8)
+    w[11, 5 * 34:5 * 34 + 2] = [0xD0, 0x63]
+    ptr = ctx.upload(w)
+    try:
+        x = synth.activations(rows * in_, seed=9).reshape(rows, in_)
+        y = np.full((rows, out), np.nan, dtype=np.float32)
+        assert ctx.dense_gguf_batch([kb.host_job(kb.Q8_0, ptr, x, y, in_=in_, out=out)]) == kb.RESULT_UNVALIDATED
+        c = ctx.counters()
+        assert c["gemm_launches"] == 1 and c["gemm_fallbacks"] == 1
+        assert rel_err(y, oracle.gemv_f64(kb.Q8_0, w, x, in_, out)) <= TOL
+    finally:
+        ctx.free(ptr)
+        ctx.close()
