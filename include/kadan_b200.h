@@ -296,6 +296,28 @@ typedef struct kb200_moe_weights {
     float limit, alpha;
 } kb200_moe_weights;
 
+/* GGUF MXFP4 (ggml type 39, block_mxfp4: IW/third_party/ggml/src/ggml-common.h:
+ * 214-219): one E8M0 byte e and 16 code bytes per 32 values; value j < 16 is
+ * the low nibble of byte j, value j + 16 its high nibble; value =
+ * kvalues_fp4[c] * 2^(e - 128) (dequantize_row_mxfp4, ggml-quants.c:569-585).
+ * The reference decodes it on the host only (ggml-cpu); these put it on the
+ * device. Pointers are device memory; asynchronous on `stream`. */
+#define KB200_MXFP4_GGML_BLOCK_BYTES 17
+/* out[32 count] = the values of `count` consecutive blocks, bit for bit as
+ * ggml's dequantize_row_mxfp4 gives them. */
+KB200_API int kb200_mxfp4_ggml_dequant(const void* blocks, size_t count, float* out, void* stream);
+/* GGUF MXFP4 rows [experts][rows][cols/32 blocks] (a GGUF expert tensor such
+ * as ffn_gate_exps, or one matrix with experts = 1) into the MXFP4 expert
+ * layout of kb200_moe_weights: rows [first_row, first_row + rows) of each
+ * expert of codes [experts][dst_rows][cols/2] (16-byte aligned) and E8M0
+ * scales [experts][dst_rows][cols/32]. Same values (ggml's code 8, +0, is
+ * written as code 0; the expert layout's code 8 is -0); scale bytes are kept,
+ * so kb200_moe_forward's scale-range flag applies to them. Separate gate and
+ * up tensors go to first_row 0 and `inter` of a gate_up destination of
+ * dst_rows = 2 * inter, used with interleaved = 0. */
+KB200_API int kb200_mxfp4_from_ggml(const void* blocks, size_t experts, size_t rows, size_t cols, void* codes,
+                                    void* scales, size_t dst_rows, size_t first_row, void* stream);
+
 /* Device scratch that kb200_moe_forward needs for `tokens` input rows. */
 KB200_API size_t kb200_moe_workspace_bytes(const kb200_moe_weights* w, size_t tokens);
 
@@ -661,6 +683,16 @@ typedef struct kb200_gguf_tensor {
 } kb200_gguf_tensor;
 
 KB200_API int kb200_gguf_open(const char* root, const volatile uint8_t* cancel, kb200_gguf** out);
+/* kb200_gguf_open with options. KB200_GGUF_ACCEPT_MXFP4: also accept tensors
+ * of ggml type 39 (GGUF MXFP4, block_mxfp4: IW/third_party/ggml/src/
+ * ggml-common.h:214-219), which the reference's reader refuses
+ * ("gguf_tensor_type", gguf_checkpoint.cpp:229-230, gguf::encoding has no
+ * MXFP4); they report encoding KB200_GGUF_MXFP4, 32 values per 17-byte block,
+ * and read as packed rows like any other tensor. Without flags the reader
+ * accepts and refuses exactly what the reference's does. */
+#define KB200_GGUF_ACCEPT_MXFP4 1u
+#define KB200_GGUF_MXFP4 (-3)
+KB200_API int kb200_gguf_open_flags(const char* root, const volatile uint8_t* cancel, uint32_t flags, kb200_gguf** out);
 KB200_API void kb200_gguf_close(kb200_gguf* file);
 KB200_API size_t kb200_gguf_tensor_count(const kb200_gguf* file);
 /* Tensors in name order; *name stays valid until kb200_gguf_close. */

@@ -470,6 +470,25 @@ def rows_regroup(src, dst, segments, max_rows: int, stream=None) -> None:
                                  _stream_ptr(stream)))
 
 
+lib.kb200_mxfp4_ggml_dequant.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
+lib.kb200_mxfp4_from_ggml.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
+                                      ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p]
+MXFP4_GGML_BLOCK_BYTES = 17
+
+
+def mxfp4_ggml_dequant(blocks, count: int, out, stream=None) -> None:
+    """out[:32 count] (fp32) = ggml's decode of `count` GGUF MXFP4 blocks (device tensors)."""
+    check(lib.kb200_mxfp4_ggml_dequant(_ptr(blocks), count, _ptr(out), _stream_ptr(stream)))
+
+
+def mxfp4_from_ggml(blocks, experts: int, rows: int, cols: int, codes, scales, dst_rows: int, first_row: int = 0,
+                    stream=None) -> None:
+    """GGUF MXFP4 rows [experts][rows][cols/32 blocks] into rows [first_row, first_row + rows)
+    of the expert layout codes [experts][dst_rows][cols/2], scales [experts][dst_rows][cols/32]."""
+    check(lib.kb200_mxfp4_from_ggml(_ptr(blocks), experts, rows, cols, _ptr(codes), _ptr(scales), dst_rows, first_row,
+                                    _stream_ptr(stream)))
+
+
 lib.kb200_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
 STATIC_MOE_SCRATCH_BYTES = 16 << 20

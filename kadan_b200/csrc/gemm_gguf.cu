@@ -215,7 +215,8 @@ __device__ __forceinline__ void prepare(RowState<kQ4K>& st, const uint8_t* blk, 
     const float d = half_bits_to_float(head.x & 0xffffu), dmin = half_bits_to_float(head.x >> 16);
     if (valid) {
         finite = finite && isfinite(d) && isfinite(dmin);
-        range = range || fabsf(d) * (63.f * 15.f) + fabsf(dmin) * 63.f > kHalfMax;
+        // Scales that are not finite are reported as such, not as out of range.
+        range = range || (isfinite(d) && isfinite(dmin) && fabsf(d) * (63.f * 15.f) + fabsf(dmin) * 63.f > kHalfMax);
     }
     // 6-bit scales and mins of sub-blocks 0-3 / 4-7, one per byte.
     const uint32_t sc_lo = head.y & 0x3F3F3F3Fu;
@@ -280,7 +281,7 @@ __device__ __forceinline__ void prepare(RowState<kQ6K>& st, const uint8_t* row, 
     const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(row + st.o + 208));
     if (valid) {
         finite = finite && isfinite(d);
-        range = range || fabsf(d) * 4096.f > kHalfMax;  // |sc| <= 128, |q - 32| <= 32
+        range = range || (isfinite(d) && fabsf(d) * 4096.f > kHalfMax);  // |sc| <= 128, |q - 32| <= 32
     }
     const auto* sc = reinterpret_cast<const int8_t*>(row + st.o + 192);
 #pragma unroll
@@ -333,7 +334,7 @@ __device__ __forceinline__ void step8(const uint8_t* row, int j, int r, uint8_t*
     const float d = half_bits_to_float(dbits);
     if (valid) {
         finite = finite && isfinite(d);
-        range = range || fabsf(d) * 128.f > kHalfMax;
+        range = range || (isfinite(d) && fabsf(d) * 128.f > kHalfMax);
     }
     const uint32_t d2 = dbits | (dbits << 16);
     const int qs = at + 2, base = qs & ~15, o = qs & 15;

@@ -1101,6 +1101,377 @@ __global__ void __launch_bounds__(kThreadsQ, q6_min_ctas<NT, S>()) gemv_q6k_mma_
     }
 }
 
+// ------------------------------------------------------- Q6_K, 1-2 input rows
+// Decode-size Q6_K (T <= 2) with half the tensor-pipe work and a third of the
+// integer work of the kernel above. One mma.m16n8k32.u8.s8 covers two
+// sub-blocks of 16 values (an even one in k 0..15, the odd one after it) and
+// keeps them apart in the N dimension: column n = 4 tok + 2 par + hl holds
+// token tok's activations at level hl (h or l) in the k half of sub-block
+// parity par and zeros in the other half, so each lane's C values belong to
+// one sub-block (par = lane % 2) and take that sub-block's scale alone.
+//   A   : the unsigned 6-bit codes q (no -32 bias: two masks and a select per
+//         4 values)
+//   -32 : sum_s sc_s * 32 * X_s per row and token, X_s = sum of sub-block s's
+//         quantised activations, from one mma.m16n8k16.s8 per block with A =
+//         the row's 16 int8 scales as stored and B = X_s split as 64 X1 + X0
+//         (both int8; column 4 tok + 2 digit + hl)
+//   sums: lane pairs (par 0, 1) hold disjoint sub-blocks of one token and are
+//         added once at the end of a piece
+// Activation segment per (block, token): B words [pair p = 4 ip + qt][par]
+// [hl][t] (512 bytes; lane (g, t) of pair p reads word (g % 4) * 4 + t of its
+// token), X words [digit][hl][t] (64 bytes), the scale s (4 bytes).
+constexpr int kPairWordBytes = 512, kPairXBytes = 64, kPairTokenBlock = kPairWordBytes + kPairXBytes + 4;
+constexpr int kPairSegBudget = 32 * kPairTokenBlock;  // all of K = 8192 for one token
+
+__host__ __device__ constexpr int pair_segment_blocks(int rows) {
+    return kPairSegBudget / (rows * kPairTokenBlock) / kQ6Chunk * kQ6Chunk;
+}
+
+template <int S> struct PairLayout {
+    static constexpr int kStages = S;
+    static constexpr int kStagesOff = 0;
+    static constexpr int kSegOff = kStages * kQ6StageBytes;
+    static constexpr int kRedOff = kSegOff + kPairSegBudget;
+    static constexpr int kRedBytes = kConsumerThreads * 4 * 4;
+    static constexpr int kBarOff = kRedOff + kRedBytes;
+    static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
+};
+static_assert(2 * (PairLayout<3>::kTotal + 128 + 1024) <= 228 * 1024, "two Q6_K pair CTAs per SM");
+static_assert(3 * (PairLayout<2>::kTotal + 128 + 1024) <= 228 * 1024, "three Q6_K pair CTAs per SM (2 stages)");
+
+struct PairSegment {
+    int blocks, rows, off;
+    __device__ PairSegment(int r, int offset) : blocks(pair_segment_blocks(r)), rows(r), off(offset) {}
+    __device__ uint32_t* words(uint8_t* smem) const { return reinterpret_cast<uint32_t*>(smem + off); }
+    __device__ uint32_t* xwords(uint8_t* smem) const { return words(smem) + blocks * rows * (kPairWordBytes / 4); }
+    __device__ float* scales(uint8_t* smem) const {
+        return reinterpret_cast<float*>(xwords(smem) + blocks * rows * (kPairXBytes / 4));
+    }
+};
+
+// Quantise super-blocks [blk0, blk0 + nblk) of the segment's tokens into the
+// pair layout: one warp per (block, token); lane L owns values 8L..8L+7 (half
+// L % 2 of sub-block L / 2). Every load of a warp's items is in flight before
+// the first is used.
+__device__ void prep_pairs(uint8_t* smem, const PairSegment& seg, const float* x, size_t in, int blk0, int nblk) {
+    const int rows = seg.rows;
+    uint32_t* words = seg.words(smem);
+    uint8_t* xbytes = reinterpret_cast<uint8_t*>(seg.xwords(smem));
+    float* scales = seg.scales(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (in & 3) == 0;
+    const int items = nblk * rows;
+    const int s = lane >> 1, half = lane & 1;
+    const int ip = s >> 3, qt = (s >> 1) & 3, par = s & 1;
+    constexpr int kBatch = 4;
+    for (int base = warp; base < items; base += kWarps * kBatch) {
+        float v[kBatch][8];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const int item = min(base + q * kWarps, items - 1);
+            const int blk = item / rows, tok = item % rows;
+            const float* xr = x + size_t(tok) * in + size_t(blk0 + blk) * 256 + lane * 8;
+            if (vec) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(xr)), b = __ldg(reinterpret_cast<const float4*>(xr) + 1);
+                v[q][0] = a.x, v[q][1] = a.y, v[q][2] = a.z, v[q][3] = a.w;
+                v[q][4] = b.x, v[q][5] = b.y, v[q][6] = b.z, v[q][7] = b.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    v[q][i] = __ldg(xr + i);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const int item = base + q * kWarps;
+            if (item >= items)
+                break;
+            const int blk = item / rows, tok = item % rows;
+            float m = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                m = fmaxf(m, fabsf(v[q][i]));
+            m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+            // 1/s to within an ulp: the levels below absorb it (x ~ s (h + l / 254)
+            // with s = m / 127 exactly as stored).
+            const float inv = m > 0.f ? 127.f * __frcp_rn(m) : 0.f;
+            // x ~ s (h + l / 254): h = round(x / s), l = round(254 (x / s - h)).
+            const float2 inv2 = make_float2(inv, inv), magic = make_float2(kMagic, kMagic);
+            const float2 neg_magic = make_float2(-kMagic, -kMagic), k254 = make_float2(254.f, 254.f);
+            int h[8], l[8];
+            int xh = 0, xl = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                const float2 y = mul2(make_float2(v[q][i], v[q][i + 1]), inv2);
+                const float2 r1 = add2(y, magic);
+                const float2 d = sub2(y, add2(r1, neg_magic));
+                const float2 r2 = fma2(d, k254, magic);
+                h[i] = int(__float_as_uint(r1.x) << 10) >> 10, h[i + 1] = int(__float_as_uint(r1.y) << 10) >> 10;
+                l[i] = int(__float_as_uint(r2.x) << 10) >> 10, l[i + 1] = int(__float_as_uint(r2.y) << 10) >> 10;
+                xh += h[i] + h[i + 1];
+                xl += l[i] + l[i + 1];
+            }
+            // B words of this lane: pair p, parity par, t = 2 half + {0, 1}.
+            uint32_t* w = words + ((blk * 8 + 4 * ip + qt) * rows + tok) * 16 + par * 8 + 2 * half;
+            w[0] = pack4(h[0], h[1], h[2], h[3]);
+            w[1] = pack4(h[4], h[5], h[6], h[7]);
+            w[4] = pack4(l[0], l[1], l[2], l[3]);
+            w[5] = pack4(l[4], l[5], l[6], l[7]);
+            // Sub-block sums (both halves), split X = 64 X1 + X0, X0 in [-32, 31].
+            xh += __shfl_xor_sync(0xffffffffu, xh, 1);
+            xl += __shfl_xor_sync(0xffffffffu, xl, 1);
+            if (!half) {
+                uint8_t* xb = xbytes + (blk * rows + tok) * kPairXBytes + (s & 3);
+                const int h1 = (xh + 32) >> 6, l1 = (xl + 32) >> 6;
+                // [digit][hl][t = s / 4][byte s % 4]
+                xb[(0 * 2 + 0) * 16 + (s >> 2) * 4] = uint8_t(h1);
+                xb[(0 * 2 + 1) * 16 + (s >> 2) * 4] = uint8_t(l1);
+                xb[(1 * 2 + 0) * 16 + (s >> 2) * 4] = uint8_t(xh - 64 * h1);
+                xb[(1 * 2 + 1) * 16 + (s >> 2) * 4] = uint8_t(xl - 64 * l1);
+            }
+            if (lane == 0)
+                scales[blk * rows + tok] = m > 0.f ? m / 127.f : 0.f;
+        }
+    }
+}
+
+
+
+// Code word of 4 values: low nibbles (shift `ls`) and the high bit pairs
+// placed at bits 4-5 (qh moved by `hs`: left when positive).
+__device__ __forceinline__ uint32_t q6_code(uint32_t ql, uint32_t qh, int ls, int hs) {
+    const uint32_t hi = (hs >= 0 ? qh << hs : qh >> -hs) & 0x30303030u;
+    return ((ql >> ls) & 0x0F0F0F0Fu) | hi;
+}
+
+// prmt selector that sign-extends byte b of a word (prmt's default mode
+// replicates a byte's sign where the selector nibble's top bit is set; the
+// __byte_perm intrinsic ignores that bit).
+__host__ __device__ constexpr uint32_t sext_sel(uint32_t b) {
+    return ((b | 8u) << 12) | ((b | 8u) << 8) | ((b | 8u) << 4) | b;
+}
+
+__device__ __forceinline__ int sext_byte(uint32_t w, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+    return int(r);
+}
+
+// One block of rows g (bg) and g + 8 (b8): adds this lane's sub-blocks of
+// its token to acc. A lane supplies B column g (token g / 4, parity g / 2 % 2,
+// level g % 2): bw points at its word of pair 0 (pairs `pair_stride` words
+// apart), xw is its X word. It receives C columns 2t, 2t + 1: token t / 2,
+// parity t % 2 (the scales it applies), h and l; sc_tok is that token's
+// activation scale.
+template <bool kOdd>
+__device__ __forceinline__ void q6k_pair_block(const uint8_t* bg, const uint8_t* b8, const uint32_t* bw, int pair_stride,
+                                               uint32_t xw, int g, int t, float sc_tok, float& acc_g, float& acc_8,
+                                               bool& finite_g, bool& finite_8) {
+    const float dg = half_bits_to_float(*reinterpret_cast<const uint16_t*>(bg + 208));
+    const float d8 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b8 + 208));
+    finite_g = finite_g && isfinite(dg);
+    finite_8 = finite_8 && isfinite(d8);
+    const bool b_odd = (g >> 1) & 1;  // parity of the B column this lane supplies
+    const bool odd_col = t & 1;       // parity of the C columns this lane receives
+    // -32 correction: sum_s sc_s (64 X1_s + X0_s) for digit (t % 2) = X1 / X0.
+    int I[4];
+    {
+        int cx[4];
+        imma16(cx, ld_word<kOdd>(bg + 192 + 4 * t), ld_word<kOdd>(b8 + 192 + 4 * t), xw);
+        const int mult = odd_col ? -32 : -32 * 64;
+        I[0] = mult * cx[0], I[1] = mult * cx[1], I[2] = mult * cx[2], I[3] = mult * cx[3];
+    }
+    uint32_t scg[4], sc8[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        scg[w] = ld_word<kOdd>(bg + 192 + 4 * w);
+        sc8[w] = ld_word<kOdd>(b8 + 192 + 4 * w);
+    }
+    const uint32_t sel0 = sext_sel(odd_col ? 1u : 0u), sel1 = sext_sel(odd_col ? 3u : 2u);
+#pragma unroll
+    for (int ip = 0; ip < 2; ++ip) {
+        // ql words [a][h] (a = qt & 1) and qh words [h] of both rows.
+        uint32_t qlg[2][2], ql8[2][2], qhg[2], qh8[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+                qlg[a][h] = ld_word<kOdd>(bg + 64 * ip + 32 * a + 16 * h + 4 * t);
+                ql8[a][h] = ld_word<kOdd>(b8 + 64 * ip + 32 * a + 16 * h + 4 * t);
+            }
+            qhg[h] = ld_word<kOdd>(bg + 128 + 32 * ip + 16 * h + 4 * t);
+            qh8[h] = ld_word<kOdd>(b8 + 128 + 32 * ip + 16 * h + 4 * t);
+        }
+#pragma unroll
+        for (int qt = 0; qt < 4; ++qt) {
+            const int ls = 4 * (qt >> 1), hs = 4 - 2 * qt;
+            const int a = qt & 1;
+            const uint32_t a0 = q6_code(qlg[a][0], qhg[0], ls, hs), a1 = q6_code(ql8[a][0], qh8[0], ls, hs);
+            const uint32_t a2 = q6_code(qlg[a][1], qhg[1], ls, hs), a3 = q6_code(ql8[a][1], qh8[1], ls, hs);
+            const uint32_t w = bw[(4 * ip + qt) * pair_stride];
+            int c[4];
+            imma(c, a0, a1, a2, a3, b_odd ? 0u : w, b_odd ? w : 0u);
+            // Scale of sub-block 8 ip + 2 qt + par: word 2 ip + qt / 2, byte 2 (qt % 2) + par.
+            const uint32_t sel = (qt & 1) ? sel1 : sel0;
+            const int sg = sext_byte(scg[2 * ip + (qt >> 1)], sel);
+            const int s8 = sext_byte(sc8[2 * ip + (qt >> 1)], sel);
+            I[0] += sg * c[0], I[1] += sg * c[1];
+            I[2] += s8 * c[2], I[3] += s8 * c[3];
+        }
+    }
+    acc_g = fmaf(dg * sc_tok, fmaf(float(I[1]), 1.f / 254.f, float(I[0])), acc_g);
+    acc_8 = fmaf(d8 * sc_tok, fmaf(float(I[3]), 1.f / 254.f, float(I[2])), acc_8);
+}
+
+// Q6_K decode GEMV for one or two input rows per pass: the Q6_K kernel's
+// tiles, stages, pieces, fixup and programmatic dependent launch, with the
+// paired-sub-block inner loop above.
+template <int S>
+__global__ void __launch_bounds__(kThreadsQ, S == 2 ? 3 : 2) gemv_q6k_pair_kernel(const __grid_constant__ MmaParams p) {
+    using L = PairLayout<S>;
+    constexpr int kStages = L::kStages;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
+    auto* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+    auto* empty = full + kStages;
+    auto* abort_flag = reinterpret_cast<int*>(empty + kStages);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int KS = kWarps;
+    auto* red = reinterpret_cast<float*>(smem + L::kRedOff);
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+        grid_dependents_launch();
+    }
+    __syncthreads();
+
+    if (warp == kWarps) {
+        // ------------------------------ producer ------------------------------
+        if (lane != 0)
+            return;
+        uint32_t it = 0;
+        PieceIter pieces(p);
+        Piece pc;
+        while (pieces.next(p, pc)) {
+            const MmaJob& job = p.jobs[pc.job];
+            const int row0 = int((pc.tile / job.row_groups) * uint32_t(kQ6Rows));
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&job.map) : "memory");
+            for (uint32_t ch = pc.k0; ch < pc.k1; ++ch, ++it) {
+                const int slot = int(it % kStages);
+                if (it >= kStages && !mbar_wait(&empty[slot], ((it / kStages) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog))
+                    atomicExch(abort_flag, 1);
+                if (*reinterpret_cast<volatile int*>(abort_flag))
+                    goto drain;
+                mbar_expect_tx(&full[slot], uint32_t(kQ6StageBytes));
+                tma_load_2d(smem + L::kStagesOff + slot * kQ6StageBytes, &job.map, int(ch) * (kQ6Chunk * kQ6Block / 8),
+                            row0, &full[slot]);
+            }
+        }
+    drain:
+        for (uint32_t k = 0; k < kStages && k < it; ++k) {
+            const uint32_t last = it - 1 - k;
+            mbar_wait(&full[last % kStages], (last / kStages) & 1u, watchdog_drain, p.watchdog);
+        }
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
+    bool dependency_met = false;
+    auto await_dependency = [&] {
+        if (!dependency_met) {
+            grid_dependency_wait();
+            dependency_met = true;
+        }
+    };
+    const int g = lane >> 2, t = lane & 3, ks = warp;
+    uint32_t it = 0;
+    const float* seg_x = nullptr;
+    int seg_rows = -1, seg_blk0 = -1, seg_nblk = 0;
+    PieceIter pieces(p);
+    Piece pc;
+    while (pieces.next(p, pc)) {
+        const MmaJob& job = p.jobs[pc.job];
+        const uint32_t row0 = (pc.tile / job.row_groups) * uint32_t(kQ6Rows);
+        const uint32_t r0 = (pc.tile % job.row_groups) * job.group_rows;
+        const int rows = int(min(job.group_rows, job.rows - r0));
+        const int nblocks = int(job.in / 256);
+        const float* x = job.input + size_t(r0) * job.in;
+        const PairSegment seg(rows, L::kSegOff);
+        if (seg.blocks < kQ6Chunk)
+            atomicExch(abort_flag, 1);
+        const uint32_t* words = seg.words(smem);
+        const uint32_t* xwords = seg.xwords(smem);
+        const float* scales = seg.scales(smem);
+        // B side: the token of the column this lane supplies (g / 4) and its
+        // word in every group of 16; C side: the token of the columns it
+        // receives (t / 2). Both clamped to the rows present.
+        const int btok = min(g >> 2, rows - 1), ctok = min(t >> 1, rows - 1);
+        const int lane_word = (g & 3) * 4 + t;
+        const uint32_t my_row = row0 + g;
+        const bool valid_lo = my_row < job.columns, valid_hi = my_row + 8 < job.columns;
+        const bool check = job.status != nullptr;
+        bool finite_g = true, finite_8 = true;
+        float acc_g = 0.f, acc_8 = 0.f;
+
+        for (uint32_t ch = pc.k0; ch < pc.k1; ++ch, ++it) {
+            const int slot = int(it % kStages);
+            const int blk_first = int(ch) * kQ6Chunk;
+            const int nb = min(kQ6Chunk, nblocks - blk_first);
+            if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
+                && seg.blocks >= kQ6Chunk) {
+                const int start = nblocks <= seg.blocks ? 0 : blk_first;
+                const int count = min(seg.blocks, nblocks - start);
+                await_dependency();
+                named_sync(1, kConsumerThreads);
+                prep_pairs(smem, seg, x, job.in, start, count);
+                named_sync(1, kConsumerThreads);
+                seg_x = x, seg_rows = rows, seg_blk0 = start, seg_nblk = count;
+            }
+            const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
+            if (!aborted && !mbar_wait(&full[slot], (it / kStages) & 1u, watchdog_full_barrier, p.watchdog))
+                atomicExch(abort_flag, 1);
+            if (!aborted) {
+                const uint8_t* stage = smem + L::kStagesOff + slot * kQ6StageBytes;
+#pragma unroll
+                for (int bb = 0; bb < 2; ++bb) {
+                    const int b = 2 * ks + bb;  // block of the chunk; odd b sits 2 bytes off a word
+                    if (b >= nb)
+                        break;
+                    const int sblk = blk_first + b - seg_blk0;
+                    const uint8_t* bg = stage + g * (kQ6Chunk * kQ6Block) + b * kQ6Block;
+                    const uint8_t* b8 = bg + 8 * (kQ6Chunk * kQ6Block);
+                    const uint32_t* bw = words + (sblk * 8 * rows + btok) * 16 + lane_word;
+                    const uint32_t xw = xwords[(sblk * rows + btok) * 16 + lane_word];
+                    const float sc_tok = scales[sblk * rows + ctok];
+                    if (bb)
+                        q6k_pair_block<true>(bg, b8, bw, rows * 16, xw, g, t, sc_tok, acc_g, acc_8, finite_g, finite_8);
+                    else
+                        q6k_pair_block<false>(bg, b8, bw, rows * 16, xw, g, t, sc_tok, acc_g, acc_8, finite_g, finite_8);
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&empty[slot]);
+        }
+        if (check && !((finite_g || !valid_lo) && (finite_8 || !valid_hi)))
+            atomicOr(job.status, 1u);
+        // Lanes t = 2k, 2k + 1 hold token k's even and odd sub-blocks: add
+        // them, then give lane t the sums of token t (lanes 0 and 1 of each
+        // group of four) as the common piece ending expects.
+        acc_g += __shfl_xor_sync(0xffffffffu, acc_g, 1);
+        acc_8 += __shfl_xor_sync(0xffffffffu, acc_8, 1);
+        const int from = (lane & ~3) | ((2 * t) & 3);
+        float acc[1][2] = {{__shfl_sync(0xffffffffu, acc_g, from), __shfl_sync(0xffffffffu, acc_8, from)}};
+        finish_piece<1>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0, rows, red, abort_flag,
+                        await_dependency);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1193,6 +1564,7 @@ struct Tuning {
     uint32_t q6_min_units = kQ6MinUnitsPerCta;  // KB200_GEMV_Q6K_MIN_UNITS=<units per CTA>
     int ctas_per_sm = 0;                        // KB200_GEMV_CTAS_PER_SM=<n>: grid slots per SM (0: all that fit)
     int q6_stages = 3;                          // KB200_GEMV_Q6K_STAGES=2|3: ring depth at 1-4 rows per pass
+    bool q6_pair = true;                        // KB200_GEMV_Q6K_PAIR=0: 1-2 rows on the 4-row kernel
 };
 
 const Tuning& tuning() {
@@ -1206,6 +1578,8 @@ const Tuning& tuning() {
             v.min_units = uint32_t(std::max(1, std::atoi(s)));
         if (const char* s = std::getenv("KB200_GEMV_Q6K_MIN_UNITS"))
             v.q6_min_units = uint32_t(std::max(1, std::atoi(s)));
+        if (const char* s = std::getenv("KB200_GEMV_Q6K_PAIR"))
+            v.q6_pair = std::atoi(s) != 0;
         if (const char* s = std::getenv("KB200_GEMV_Q6K_STAGES"))
             v.q6_stages = std::atoi(s) == 2 ? 2 : 3;
         if (const char* s = std::getenv("KB200_GEMV_L2_PREFETCH"))
@@ -1230,6 +1604,26 @@ template <int NT, int S> int q6k_slots() {
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_mma_kernel<NT, S>, kThreadsQ, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_mma_kernel occupancy");
+        blocks_per_sm[dev] = n > 0 ? n : 1;
+    }
+    return sm_count() * blocks_per_sm[dev];
+}
+
+template <int S> int q6k_pair_slots() {
+    static int blocks_per_sm[64] = {};
+    static std::mutex lock;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    constexpr int smem = PairLayout<S>::kTotal + 128;
+    std::lock_guard<std::mutex> guard(lock);
+    if (!blocks_per_sm[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_pair_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess)
+            return -cuda_fail(e, "gemv_q6k_pair_kernel attribute");
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_pair_kernel<S>, kThreadsQ, smem);
+        if (e != cudaSuccess)
+            return -cuda_fail(e, "gemv_q6k_pair_kernel occupancy");
         blocks_per_sm[dev] = n > 0 ? n : 1;
     }
     return sm_count() * blocks_per_sm[dev];
@@ -1295,9 +1689,12 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     for (const auto* j : jobs)
         max_rows = std::max(max_rows, int(std::min(j->rows, uint32_t(KB200_BATCH_ROWS))));
     const int nt = max_rows <= 4 ? 1 : 2;
-    const uint32_t group_rows = uint32_t(4 * nt);
+    // 1-2 rows: the paired-sub-block kernel (2 rows per pass).
+    const bool pair = max_rows <= 2 && tuning().q6_pair;
+    const uint32_t group_rows = pair ? 2u : uint32_t(4 * nt);
     const bool two_stage = nt == 1 && tuning().q6_stages == 2;
-    int slots = nt == 2 ? q6k_slots<2, 2>() : two_stage ? q6k_slots<1, 2>() : q6k_slots<1, 3>();
+    int slots = pair ? (two_stage ? q6k_pair_slots<2>() : q6k_pair_slots<3>())
+              : nt == 2 ? q6k_slots<2, 2>() : two_stage ? q6k_slots<1, 2>() : q6k_slots<1, 3>();
     if (slots <= 0)
         return -slots;
     if (tuning().ctas_per_sm > 0)
@@ -1357,15 +1754,18 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
         cfg.blockDim = dim3(kThreadsQ);
-        cfg.dynamicSmemBytes = (nt == 2 ? Q6Layout<2, 2>::kTotal : two_stage ? Q6Layout<1, 2>::kTotal
-                                                                             : Q6Layout<1, 3>::kTotal) + 128;
+        cfg.dynamicSmemBytes = (pair ? (two_stage ? PairLayout<2>::kTotal : PairLayout<3>::kTotal)
+                                : nt == 2 ? Q6Layout<2, 2>::kTotal
+                                : two_stage ? Q6Layout<1, 2>::kTotal : Q6Layout<1, 3>::kTotal) + 128;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t e = nt == 2     ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<2, 2>, p)
+        const cudaError_t e = pair && two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2>, p)
+                              : pair        ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<3>, p)
+                              : nt == 2     ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<2, 2>, p)
                               : two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 2>, p)
                                           : cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 3>, p);
         if (e != cudaSuccess)

@@ -73,8 +73,15 @@ void stop(const volatile uint8_t* cancel) {
         raise("gguf_cancelled", KB200_CANCELLED);
 }
 
-// ggml type id -> kb200 encoding (F32 included); -2 for types the reader refuses.
-int encoding_of(uint32_t ggml_type) {
+// ggml type id -> kb200 encoding (F32 included); -2 for types the reader
+// refuses. GGUF MXFP4 (ggml type 39) is refused as the reference's reader
+// refuses it (gguf::encoding has no MXFP4, gguf_checkpoint.cpp:229-230) unless
+// the caller opened with KB200_GGUF_ACCEPT_MXFP4; it then reads as
+// KB200_GGUF_MXFP4 (32 values in 17 bytes, converted for the MoE layer by
+// kb200_mxfp4_from_ggml).
+int encoding_of(uint32_t ggml_type, uint32_t flags) {
+    if (ggml_type == 39)
+        return (flags & KB200_GGUF_ACCEPT_MXFP4) ? KB200_GGUF_MXFP4 : -2;
     switch (ggml_type) {
     case 0: return KB200_F32;
     case 8: return KB200_Q8_0;
@@ -277,7 +284,7 @@ struct Parsed {
 
 // One file's header: the reference's preflight (gguf_checkpoint.cpp:181-262)
 // and then ggml's own layout rules (gguf.cpp), in that order of precedence.
-Parsed parse_header(const File& f, const volatile uint8_t* cancel) {
+Parsed parse_header(const File& f, const volatile uint8_t* cancel, uint32_t flags) {
     HeaderReader r(f, cancel);
     Parsed p;
     require(r.u32() == 0x46554747u && r.u32() == 3, "gguf_version");
@@ -341,9 +348,11 @@ Parsed parse_header(const File& f, const volatile uint8_t* cancel) {
                 rows = mul(rows, e.shape[d]);
         }
         e.type = r.u32();
-        e.encoding = encoding_of(e.type);
+        e.encoding = encoding_of(e.type, flags);
         require(e.encoding != -2, "gguf_tensor_type");
-        const uint64_t values = uint64_t(block_values(e.encoding)), width = uint64_t(block_bytes(e.encoding));
+        const bool mx = e.encoding == KB200_GGUF_MXFP4;
+        const uint64_t values = mx ? 32 : uint64_t(block_values(e.encoding));
+        const uint64_t width = mx ? 17 : uint64_t(block_bytes(e.encoding));
         require(e.shape[0] % values == 0, "gguf_tensor_block_alignment");
         require(mul(e.shape[0], rows) <= uint64_t(INT64_MAX) && e.shape[0] <= SIZE_MAX / width, "gguf_tensor_shape");
         e.row_bytes = e.shape[0] / values * width;
@@ -441,7 +450,7 @@ void check_unchanged(const kb200_gguf* g) {
 }
 
 // GgufCheckpoint::GgufCheckpoint (gguf_checkpoint.cpp:441-540).
-kb200_gguf* open_root(const char* root, const volatile uint8_t* cancel) {
+kb200_gguf* open_root(const char* root, const volatile uint8_t* cancel, uint32_t flags) {
     require(root != nullptr, "gguf_missing_files");
     std::vector<std::string> names;
     {
@@ -479,7 +488,7 @@ kb200_gguf* open_root(const char* root, const volatile uint8_t* cancel) {
             require(single || (prefix == prefix0 && number == i + 1 && count == names.size()), "gguf_split_name");
             g->files.emplace_back(::openat(directory.fd, names[i].c_str(), O_RDONLY | O_NOFOLLOW | O_CLOEXEC), false);
             const File& file = g->files.back();
-            Parsed p = parse_header(file, cancel);
+            Parsed p = parse_header(file, cancel, flags);
             metadata_bytes = add(metadata_bytes, p.header_end);
             require(metadata_bytes <= kSplitMetadataLimit, "gguf_metadata_limit");
             file.unchanged();
@@ -570,10 +579,16 @@ using namespace kb200;
 extern "C" {
 
 int kb200_gguf_open(const char* root, const volatile uint8_t* cancel, kb200_gguf** out) {
+    return kb200_gguf_open_flags(root, cancel, 0, out);
+}
+
+int kb200_gguf_open_flags(const char* root, const volatile uint8_t* cancel, uint32_t flags, kb200_gguf** out) {
     if (!out)
         return fail(KB200_INVALID, "null output");
     *out = nullptr;
-    return guarded([&] { *out = open_root(root, cancel); });
+    if (flags & ~uint32_t(KB200_GGUF_ACCEPT_MXFP4))
+        return fail(KB200_INVALID, "unknown GGUF open flags");
+    return guarded([&] { *out = open_root(root, cancel, flags); });
 }
 
 void kb200_gguf_close(kb200_gguf* g) {

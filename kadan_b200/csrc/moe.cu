@@ -247,11 +247,17 @@ __global__ void moe_combine_kernel(
 }
 
 // ----------------------------------------------------------- grouped GEMM
-constexpr int BM = 128, BN = 128, BK = 64, kStagesG = 4;
+// Tiles of 128 sorted rows (M) x 256 weight rows (N): each 16 KB activation
+// tile feeds 256 output columns, half the L2 -> SM bytes per FLOP of 128-row
+// weight tiles (measured: with 128-row tiles the activation TMA tiles took ~2
+// us to arrive and the tensor pipe sat at 26 %). Activation and raw-code
+// stages (kStagesG) and dequantised B stages (kStagesB) are separate rings.
+constexpr int BM = 128, BN = 256, BK = 64, kStagesG = 4, kStagesB = 2;
 constexpr int kABytes = BM * BK * 2, kBBytes = BN * BK * 2, kRawBytes = BN * BK / 2;
 constexpr int kMaxK = 4096;
 constexpr int kScaleBytes = BN * (kMaxK / 32);
-constexpr int kThreadsG = 320;  // producer, MMA, 4 dequant warps, 4 epilogue warps
+constexpr int kDequantWarpsG = 8;                    // one B row per thread
+constexpr int kThreadsG = 32 * (2 + kDequantWarpsG + 4);  // producer, MMA, dequant, 4 epilogue warps
 
 struct GroupParams {
     CUtensorMap a_map;  // fp16 [rows, K], box {64, 128}, 128-byte swizzle
@@ -268,7 +274,7 @@ struct GroupParams {
 };
 
 struct GemmShared {
-    uint64_t tma_full[kStagesG], b_full[kStagesG], stage_empty[kStagesG];
+    uint64_t tma_full[kStagesG], stage_empty[kStagesG], b_full[kStagesB], b_empty[kStagesB];
     uint64_t sc_full[2], sc_empty[2], acc_full[2], acc_empty[2];
     uint32_t tmem_base;
     int abort;
@@ -276,7 +282,7 @@ struct GemmShared {
 
 constexpr int kSmemA = 0;
 constexpr int kSmemB = kSmemA + kStagesG * kABytes;
-constexpr int kSmemRaw = kSmemB + kStagesG * kBBytes;
+constexpr int kSmemRaw = kSmemB + kStagesB * kBBytes;
 constexpr int kSmemScale = kSmemRaw + kStagesG * kRawBytes;
 constexpr int kSmemShared = kSmemScale + 2 * kScaleBytes;
 constexpr int kSmemTotal = kSmemShared + int(sizeof(GemmShared)) + 1024;
@@ -370,12 +376,15 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
     if (tid == 0) {
         for (int s = 0; s < kStagesG; ++s) {
             mbar_init(&sh->tma_full[s], 1);
-            mbar_init(&sh->b_full[s], 128);
             mbar_init(&sh->stage_empty[s], 1);
+        }
+        for (int s = 0; s < kStagesB; ++s) {
+            mbar_init(&sh->b_full[s], 32 * kDequantWarpsG);
+            mbar_init(&sh->b_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&sh->sc_full[b], 1);
-            mbar_init(&sh->sc_empty[b], 128);
+            mbar_init(&sh->sc_empty[b], 32 * kDequantWarpsG);
             mbar_init(&sh->acc_full[b], 1);
             mbar_init(&sh->acc_empty[b], 4);
         }
@@ -383,7 +392,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
         fence_barrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(&sh->tmem_base, 256);
+        tmem_alloc(&sh->tmem_base, 2 * BN);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -425,13 +434,11 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                 const int kx = k_step(ks, t.nt, KS);
                 mbar_expect_tx(&sh->tma_full[s], uint32_t(kABytes + kRawBytes));
                 tma_load_2d(smem + kSmemA + s * kABytes, &p.a_map, kx * BK, t.m0, &sh->tma_full[s]);
+                // Two boxes of 128 code rows: gate and up halves (split), or
+                // the tile's lower and upper 128 rows.
                 uint8_t* raw = smem + kSmemRaw + s * kRawBytes;
-                if (p.split) {
-                    tma_load_2d(raw, &p.b_map, kx * (BK / 2), r_lo, &sh->tma_full[s]);
-                    tma_load_2d(raw + (BN / 2) * (BK / 2), &p.b_map, kx * (BK / 2), r_hi, &sh->tma_full[s]);
-                } else {
-                    tma_load_2d(raw, &p.b_map, kx * (BK / 2), r_lo, &sh->tma_full[s]);
-                }
+                tma_load_2d(raw, &p.b_map, kx * (BK / 2), r_lo, &sh->tma_full[s]);
+                tma_load_2d(raw + (BN / 2) * (BK / 2), &p.b_map, kx * (BK / 2), r_hi, &sh->tma_full[s]);
             }
         }
         // Drain: every copy this thread issued lands before the CTA can exit.
@@ -456,21 +463,21 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
             }
             tc_fence_after();
             for (int ks = 0; ks < KS; ++ks, ++it) {
-                const int s = int(it % kStagesG);
-                const uint32_t ph = (it / kStagesG) & 1u;
-                if (!mbar_wait(&sh->tma_full[s], ph, watchdog_full_barrier, p.watchdog)
-                    || !mbar_wait(&sh->b_full[s], ph, watchdog_full_barrier, p.watchdog)) {
+                const int s = int(it % kStagesG), sb = int(it % kStagesB);
+                if (!mbar_wait(&sh->tma_full[s], (it / kStagesG) & 1u, watchdog_full_barrier, p.watchdog)
+                    || !mbar_wait(&sh->b_full[sb], (it / kStagesB) & 1u, watchdog_full_barrier, p.watchdog)) {
                     *abort_flag = 1;
                     break;
                 }
                 tc_fence_after();
                 const uint64_t ad = sw128_desc(smem_addr(smem + kSmemA + s * kABytes));
-                const uint64_t bd = sw128_desc(smem_addr(smem + kSmemB + s * kBBytes));
+                const uint64_t bd = sw128_desc(smem_addr(smem + kSmemB + sb * kBBytes));
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk)
                     umma_f16(tmem + uint32_t(acc * BN), ad + uint64_t(2 * kk), bd + uint64_t(2 * kk), idesc,
                              (ks | kk) != 0);
                 umma_commit(&sh->stage_empty[s]);
+                umma_commit(&sh->b_empty[sb]);
                 issued = true;
             }
             umma_commit(&sh->acc_full[acc]);
@@ -480,7 +487,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
             const uint32_t last = it - 1;
             mbar_wait(&sh->stage_empty[last % kStagesG], (last / kStagesG) & 1u, watchdog_drain, p.watchdog);
         }
-    } else if (warp >= 2 && warp < 6) {
+    } else if (warp >= 2 && warp < 2 + kDequantWarpsG) {
         // ------------------------------------------------- dequant warps
         const int r = tid - 64;  // B-operand row of this thread
         uint32_t it = 0, lt = 0;
@@ -498,8 +505,11 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
             tile_rows(p, ti, r_lo, r_hi);
             const bool row_in_tensor = (r < BN / 2 ? r_lo + r : r_hi + (r - BN / 2)) < p.E * p.Nrows;
             for (int ks = 0; ks < KS; ++ks, ++it) {
-                const int s = int(it % kStagesG);
-                if (!mbar_wait(&sh->tma_full[s], (it / kStagesG) & 1u, watchdog_full_barrier, p.watchdog)) {
+                const int s = int(it % kStagesG), sbs = int(it % kStagesB);
+                if (!mbar_wait(&sh->tma_full[s], (it / kStagesG) & 1u, watchdog_full_barrier, p.watchdog)
+                    || (it >= kStagesB
+                        && !mbar_wait(&sh->b_empty[sbs], ((it / kStagesB) & 1u) ^ 1u, watchdog_empty_barrier,
+                                      p.watchdog))) {
                     *abort_flag = 1;
                     break;
                 }
@@ -511,7 +521,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                 const uint32_t s0 = e8m0_half2(srow[2 * kx], ok0), s1 = e8m0_half2(srow[2 * kx + 1], ok1);
                 scale_ok = scale_ok && (!row_in_tensor || (ok0 && ok1));
                 const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                uint8_t* brow = smem + kSmemB + s * kBBytes + r * 128;
+                uint8_t* brow = smem + kSmemB + sbs * kBBytes + r * 128;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
                     // 16-byte chunk c = values 8c..8c+7 = code bytes 4c..4c+3.
@@ -524,13 +534,13 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                     *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = h;
                 }
                 fence_proxy_async();
-                mbar_arrive(&sh->b_full[s]);
+                mbar_arrive(&sh->b_full[sbs]);
             }
             mbar_arrive(&sh->sc_empty[sb]);
         }
         if (!scale_ok && p.status)
             atomicOr(p.status, 2u);
-    } else if (warp >= 6) {
+    } else if (warp >= 2 + kDequantWarpsG) {
         // ------------------------------------------------- epilogue warps
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row = 32 * q + lane;
@@ -550,11 +560,11 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                 // Activation of (gate, up) pairs -> fp16 act[prow, j].
                 auto* act = static_cast<__half*>(p.out);
                 const int I = p.Nrows / 2;
-                for (int c = 0; c < 2; ++c) {
+                for (int c = 0; c < BN / 64; ++c) {
                     uint32_t g[32], u[32];
                     if (p.split) {
                         tmem_ld32(taddr + uint32_t(32 * c), g);
-                        tmem_ld32(taddr + uint32_t(64 + 32 * c), u);
+                        tmem_ld32(taddr + uint32_t(BN / 2 + 32 * c), u);
                     } else {
                         // Interleaved: column 2i gate, 2i+1 up.
                         uint32_t a[32], b[32];
@@ -629,7 +639,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     if (warp == 1)
-        tmem_dealloc(tmem, 256);
+        tmem_dealloc(tmem, 2 * BN);
 }
 
 // ----------------------------------------------------------- grouped GEMV
@@ -932,7 +942,7 @@ int launch_gemm(GroupParams& p, int max_tiles, cudaStream_t stream) {
         return -slots;
     p.watchdog = watchdog_word();
     const int grid = std::max(1, std::min(slots, max_tiles));
-    // A plain launch: GEMM CTAs launched early would hold SMs (176 KB of
+    // A plain launch: GEMM CTAs launched early would hold SMs (225 KB of
     // shared memory each) that the gather kernel before them still needs.
     moe_gemm_kernel<<<grid, kThreadsG, kSmemTotal, stream>>>(p);
     const cudaError_t e = cudaGetLastError();
@@ -1094,7 +1104,7 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
     if (!encode_2d(&g1.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xs, uint64_t(H), n, BK, BM,
                    CU_TENSOR_MAP_SWIZZLE_128B)
         || !encode_2d(&g1.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->gate_up_blocks, uint64_t(H / 2),
-                      uint64_t(E) * 2 * I, BK / 2, split ? BN / 2 : BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+                      uint64_t(E) * 2 * I, BK / 2, BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(KB200_INVALID, "tensor map encoding (gate/up)");
     g1.scales = w->gate_up_scales;
     g1.bias = w->gate_up_bias;
@@ -1104,7 +1114,9 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
     g1.K = H;
     g1.Nrows = 2 * I;
     g1.E = E;
-    g1.n_tiles = split ? I / (BN / 2) : 2 * I / BN;
+    // 128 (gate, up) pairs per tile; the last tile of an expert may be partial
+    // (its extra rows are read and their outputs dropped).
+    g1.n_tiles = (I + BN / 2 - 1) / (BN / 2);
     g1.split = split ? 1 : 0;
     g1.epilogue = 0;
     g1.out_cols = I;
@@ -1112,8 +1124,6 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
     g1.limit = w->limit;
     g1.alpha = w->alpha;
     g1.status = status;
-    if ((2 * I) % BN && !split)
-        return fail(KB200_UNSUPPORTED, "interleaved gate/up needs 2*inter to be a multiple of 128");
     if (const int s = launch_gemm(g1, mtiles_max * g1.n_tiles, stream))
         return s;
 
@@ -1123,7 +1133,7 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
     if (!encode_2d(&g2.a_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, act, uint64_t(I), n, BK, BM,
                    CU_TENSOR_MAP_SWIZZLE_128B)
         || !encode_2d(&g2.b_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->down_blocks, uint64_t(I / 2), uint64_t(E) * H,
-                      BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+                      BK / 2, BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(KB200_INVALID, "tensor map encoding (down)");
     g2.scales = w->down_scales;
     g2.bias = w->down_bias;

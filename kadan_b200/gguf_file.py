@@ -35,6 +35,9 @@ class GgufRowsC(ctypes.Structure):
 
 
 lib.kb200_gguf_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(c_u8), ctypes.POINTER(vp)]
+lib.kb200_gguf_open_flags.argtypes = [ctypes.c_char_p, ctypes.POINTER(c_u8), ctypes.c_uint32, ctypes.POINTER(vp)]
+ACCEPT_MXFP4 = 1  # KB200_GGUF_ACCEPT_MXFP4
+MXFP4 = -3        # KB200_GGUF_MXFP4: the encoding an accepted ggml type-39 tensor reports
 lib.kb200_gguf_close.argtypes = [vp]
 lib.kb200_gguf_close.restype = None
 lib.kb200_gguf_tensor_count.argtypes = [vp]
@@ -96,11 +99,13 @@ class GgufRows:
 
 
 class GgufCheckpoint:
-    def __init__(self, root, cancel: Optional[ctypes.c_ubyte] = None):
+    def __init__(self, root, cancel: Optional[ctypes.c_ubyte] = None, flags: int = 0):
+        """flags: ACCEPT_MXFP4 also opens files with GGUF MXFP4 tensors, which
+        the reference's reader (and this one by default) refuses."""
         h = vp()
         self._h = None
-        check(lib.kb200_gguf_open(str(root).encode(), None if cancel is None else ctypes.pointer(cancel),
-                                  ctypes.byref(h)))
+        check(lib.kb200_gguf_open_flags(str(root).encode(), None if cancel is None else ctypes.pointer(cancel), flags,
+                                        ctypes.byref(h)))
         self._h = h.value
 
     def close(self) -> None:

@@ -13,7 +13,7 @@ _FMT = {U8: "<B", I8: "<b", U16: "<H", I16: "<h", U32: "<I", I32: "<i", F32: "<f
         I64: "<q", F64: "<d"}
 # ggml type -> (values per block, bytes per block) for the types the reader accepts.
 GEOMETRY = {0: (1, 4), 8: (32, 34), 11: (256, 110), 12: (256, 144), 14: (256, 210), 18: (256, 98), 20: (32, 18),
-            21: (256, 110), 22: (256, 82), 23: (256, 136), 30: (1, 2)}
+            21: (256, 110), 22: (256, 82), 23: (256, 136), 30: (1, 2), 39: (32, 17)}
 
 
 def text(s) -> bytes:

@@ -342,3 +342,27 @@ def test_read_vector_matches_reference(gg, ref, tmp_path):
             assert message_of_call(lambda: ours.read_vector(name, count)) == want, (name, want)
     finally:
         ref.gguf_close(h)
+
+
+def test_mxfp4_tensors_opt_in(gg, ref, tmp_path):
+    """GGUF MXFP4 (ggml type 39): refused by default with the reference's own
+    message (its reader has no MXFP4 encoding); opened with ACCEPT_MXFP4, the
+    tensor reports 17-byte blocks of 32 values and reads back byte for byte."""
+    rng = np.random.default_rng(3)
+    gate = rng.integers(0, 256, size=4 * 6 * (64 // 32) * 17, dtype=np.uint8)
+    tensors = TENSORS + [("blk.0.ffn_gate_exps.weight", [64, 6, 4], 39, gate.tobytes())]
+    root, payloads = single(tmp_path, tensors=tensors)
+    want = ref.gguf_open(root)
+    assert want == "gguf_tensor_type"
+    assert our_error(gg, root) == want
+    ours = gg.GgufCheckpoint(root, flags=gg.ACCEPT_MXFP4)
+    try:
+        t = ours.tensor("blk.0.ffn_gate_exps.weight")
+        assert (t.shape, t.ggml_type, t.encoding, t.row_bytes, t.bytes) == ((64, 6, 4), 39, gg.MXFP4, 34, 4 * 6 * 34)
+        for expert in range(4):
+            got = ours.read_packed_rows(t.name, expert, 1, 5 * 34)
+            assert np.array_equal(got, gate[(expert * 6 + 1) * 34:(expert * 6 + 6) * 34])
+        # The other tensors are unchanged by the option.
+        assert [x.name for x in ours.tensors()] == sorted(payloads)
+    finally:
+        ours.close()

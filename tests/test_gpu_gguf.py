@@ -306,12 +306,14 @@ def test_q4k_streams_share_nothing(kb, cuda):
 
 
 @pytest.mark.parametrize("in_,out,rows", [(8192, 40, 1), (3584, 131, 1), (1024, 8192, 1), (256, 33, 3), (28672, 64, 2),
-                                          (8192, 1280, 4), (14336, 17, 5), (2048, 4096, 8), (4096, 29, 7)])
+                                          (8192, 1280, 4), (14336, 17, 5), (2048, 4096, 8), (4096, 29, 7),
+                                          (28672, 1024, 1), (2048, 333, 2), (8192, 2048, 2), (512, 7, 1)])
 def test_q6k_tensor_pipe_parity(kb, oracle, cuda, in_, out, rows):
     """Q6_K on the integer tensor pipe: rows padded to a 16-byte pitch (as the
     tensor-parallel shards are), chunks of 8 blocks with ragged last chunks,
-    up to 4 input rows per pass and row groups beyond, balanced and
-    whole-tile launches."""
+    the paired-sub-block kernel at 1-2 rows (activation windows shorter than
+    K at 28672), up to 4 input rows per pass and row groups beyond, balanced
+    and whole-tile launches."""
     import torch
 
     from kadan_b200 import synth
