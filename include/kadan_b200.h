@@ -339,6 +339,28 @@ KB200_API int kb200_moe_forward(
     void* stream
 );
 
+/* kb200_moe_forward over fp32 token rows x [tokens, hidden] (device), each
+ * value rounded once to the fp16 operand (status bit 2 when beyond its range). */
+KB200_API int kb200_moe_forward_f32(const kb200_moe_weights* w, const float* x, const float* logits, size_t tokens,
+                                    float* out, void* workspace, size_t workspace_bytes, unsigned* status,
+                                    void* stream);
+
+/* The MoE layer with host spans on a context, synchronous, in the
+ * conventions of DenseCompute::dense_gguf_batch (IW/include/kadan/
+ * dense_compute.hpp:215-221): x fp32 [tokens, hidden] and router logits fp32
+ * [tokens, experts] on the host, out fp32 [tokens, hidden] on the host; the
+ * weights stay device-resident (kb200_moe_weights). KB200_UNSUPPORTED (and
+ * *result KB200_RESULT_UNSUPPORTED) with nothing of `out` written when the
+ * call is outside the layer's contract or when the weights' scales or the
+ * activations fall outside what the fp16 operands hold exactly: the caller's
+ * host path then takes the layer (MoeLayer::forward, IW/src/models/text/
+ * qwen_layers.cpp:378-492). Non-finite inputs fail with
+ * KB200_NONFINITE_INPUT before any device work, a non-finite output with
+ * KB200_NONFINITE_OUTPUT; on success *result is KB200_RESULT_FINITE. */
+KB200_API int kb200_moe_forward_host(kb200_context* ctx, const kb200_moe_weights* w, const float* x,
+                                     const float* logits, size_t tokens, float* out, const volatile uint8_t* cancel,
+                                     int* result);
+
 /* kb200_moe_forward without a caller workspace and without any allocation.
  * No counterpart in the reference: it exists for callers that cannot
  * allocate device memory per call — workers whose device memory is fully

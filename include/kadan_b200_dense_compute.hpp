@@ -97,6 +97,37 @@ public:
         return run(full, nullptr, false, cancel, sources);
     }
 
+    // The MXFP4 mixture-of-experts layer. The reference's DenseCompute has no
+    // virtual for it (its MoeLayer::forward runs routing, gather and combine
+    // on the host around batched expert GEMVs, IW/src/models/text/
+    // qwen_layers.cpp:378-492), so this is a member of the adapter alone, in
+    // DenseCompute's conventions: synchronous host spans; unsupported, with
+    // nothing read from a source and nothing of `output` written, when the
+    // shapes do not fit or the device operands cannot hold the weights'
+    // scales or the activations exactly (the caller then runs its own
+    // layer); failures throw. `weights` are device pointers on device
+    // `device` (an index into the constructor's list); input [tokens, hidden]
+    // and logits [tokens, experts] are the layer's rows and router outputs.
+    ProjectionResult moe_mxfp4(const kb200_moe_weights& weights, std::span<const float> input,
+                               std::span<const float> logits, std::size_t tokens, std::span<float> output,
+                               const std::atomic_bool& cancel, std::size_t device = 0) {
+        if (cancel.load())
+            throw std::runtime_error(kb200_status_name(KB200_CANCELLED));
+        std::lock_guard lock(mutex_);
+        const std::size_t hidden = std::size_t(weights.hidden > 0 ? weights.hidden : 0);
+        const std::size_t experts = std::size_t(weights.experts > 0 ? weights.experts : 0);
+        if (!tokens || device >= devices_.size() || input.size() != tokens * hidden
+            || logits.size() != tokens * experts || output.size() != input.size())
+            return ProjectionResult::unsupported;
+        int result = KB200_RESULT_UNSUPPORTED;
+        const int status = kb200_moe_forward_host(devices_[device].ctx, &weights, input.data(), logits.data(), tokens,
+                                                  output.data(), cancel_byte(cancel), &result);
+        if (status == KB200_UNSUPPORTED)
+            return ProjectionResult::unsupported;
+        check(status);
+        return result == KB200_RESULT_FINITE ? ProjectionResult::finite : ProjectionResult::unvalidated;
+    }
+
     ProjectionResult dense_gguf_source(const WeightIdentity& id, gguf::Encoding encoding,
                                        const GgufWeightSource& source, std::span<const float> bias,
                                        std::span<const float> input, std::size_t in, std::size_t out,

@@ -489,6 +489,31 @@ def mxfp4_from_ggml(blocks, experts: int, rows: int, cols: int, codes, scales, d
                                     _stream_ptr(stream)))
 
 
+lib.kb200_moe_forward_f32.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
+lib.kb200_moe_forward_host.argtypes = [ctypes.c_void_p, ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(ctypes.c_ubyte),
+                                       ctypes.POINTER(ctypes.c_int)]
+
+
+def moe_forward_host(ctx: "Context", w: MoeWeights, x, logits, out=None, cancel=None) -> tuple:
+    """kb200_moe_forward_host: the layer on host fp32 arrays (numpy x [T, H],
+    logits [T, E]); returns (out, result). Raises Unsupported when the
+    caller's own path must take the layer."""
+    import numpy as np
+
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    tokens = x.shape[0]
+    if out is None:
+        out = np.empty((tokens, w.hidden), dtype=np.float32)
+    result = ctypes.c_int(0)
+    check(lib.kb200_moe_forward_host(ctx.handle, ctypes.byref(w), x.ctypes.data, logits.ctypes.data, tokens,
+                                     out.ctypes.data, None if cancel is None else ctypes.byref(cancel),
+                                     ctypes.byref(result)))
+    return out, int(result.value)
+
+
 lib.kb200_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
 STATIC_MOE_SCRATCH_BYTES = 16 << 20

@@ -686,3 +686,78 @@ int kb200_dense_gguf_source(kb200_context* c, kb200_bank* bank, const kb200_sour
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- MoE layer
+extern "C" {
+
+int kb200_moe_forward_host(kb200_context* c, const kb200_moe_weights* w, const float* x, const float* logits,
+                           size_t tokens, float* out, const volatile uint8_t* cancel, int* result) {
+    using namespace kb200;
+    if (result)
+        *result = KB200_RESULT_UNSUPPORTED;
+    if (c && cancelled(cancel))
+        return fail(KB200_CANCELLED, "cancelled before start");
+    // Unsupported first: nothing read from the caller and nothing written.
+    const size_t need = w ? kb200_moe_workspace_bytes(w, tokens) : 0;
+    if (!c || !w || !tokens || !x || !logits || !out || !need)
+        return fail(KB200_UNSUPPORTED, "MoE call outside the layer's contract");
+    const size_t H = size_t(w->hidden), E = size_t(w->experts);
+    const size_t x_bytes = tokens * H * sizeof(float), l_bytes = tokens * E * sizeof(float);
+    if (overlap(out, x_bytes, x, x_bytes) || overlap(out, x_bytes, logits, l_bytes))
+        return fail(KB200_ALIAS, "output overlaps an input");
+    for (size_t i = 0; i < tokens * H; ++i)
+        if (!std::isfinite(x[i]))
+            return fail(KB200_NONFINITE_INPUT, "non-finite input value");
+    for (size_t i = 0; i < tokens * E; ++i)
+        if (!std::isfinite(logits[i]))
+            return fail(KB200_NONFINITE_INPUT, "non-finite router logit");
+    DeviceScope scope(c->device);
+    ++c->counters.calls;
+    // Device: [x][logits][out][status][layer workspace]; host mirrors all but the workspace.
+    const size_t l_at = up256(x_bytes), o_at = l_at + up256(l_bytes), s_at = o_at + up256(x_bytes);
+    const size_t ws_at = s_at + 256;
+    if (const int s = ensure(c, ws_at + need, ws_at))
+        return s;
+    auto* dev = static_cast<uint8_t*>(c->workspace);
+    auto* host = static_cast<uint8_t*>(c->pinned);
+    std::memcpy(host, x, x_bytes);
+    std::memcpy(host + l_at, logits, l_bytes);
+    std::memset(host + s_at, 0, sizeof(unsigned));
+    cudaError_t e = cudaMemcpyAsync(dev, host, o_at, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(dev + s_at, host + s_at, sizeof(unsigned), cudaMemcpyHostToDevice, c->stream);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "MoE input upload");
+    auto* status = reinterpret_cast<unsigned*>(dev + s_at);
+    if (const int s = kb200_moe_forward_f32(w, reinterpret_cast<const float*>(dev),
+                                            reinterpret_cast<const float*>(dev + l_at), tokens,
+                                            reinterpret_cast<float*>(dev + o_at), dev + ws_at, need, status,
+                                            c->stream)) {
+        cudaStreamSynchronize(c->stream);
+        return s;
+    }
+    e = cudaMemcpyAsync(host + o_at, dev + o_at, s_at + sizeof(unsigned) - o_at, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess)
+        e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "MoE output download");
+    if (cancelled(cancel))
+        return fail(KB200_CANCELLED, "cancelled after download");
+    unsigned flags = 0;
+    std::memcpy(&flags, host + s_at, sizeof(flags));
+    // Scales or activations the fp16 operands cannot hold exactly: the
+    // caller's own path must take the layer (nothing of its output written).
+    if (flags & 6u)
+        return fail(KB200_UNSUPPORTED, flags & 2u ? "MXFP4 scale outside the exact fp16 range"
+                                                  : "activation outside the fp16 range");
+    const auto* y = reinterpret_cast<const float*>(host + o_at);
+    for (size_t i = 0; i < tokens * H; ++i)
+        if (!std::isfinite(y[i]))
+            return fail(KB200_NONFINITE_OUTPUT, "a layer output is not finite");
+    std::memcpy(out, y, x_bytes);
+    if (result)
+        *result = KB200_RESULT_FINITE;
+    return KB200_OK;
+}
+
+}  // extern "C"

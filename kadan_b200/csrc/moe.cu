@@ -199,9 +199,25 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(
 }
 
 // ----------------------------------------------------------------- gather
+// Eight values of a token row as fp32 pairs: bf16 rows (the layer's input)
+// or fp32 rows (the host-span call's).
+__device__ __forceinline__ void load8(const __nv_bfloat16* row, float2 (&f)[4]) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(row);
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        f[k] = __bfloat1622float2(b[k]);
+}
+
+__device__ __forceinline__ void load8(const float* row, float2 (&f)[4]) {
+    const float4 a = *reinterpret_cast<const float4*>(row), b = *reinterpret_cast<const float4*>(row + 4);
+    f[0] = make_float2(a.x, a.y), f[1] = make_float2(a.z, a.w), f[2] = make_float2(b.x, b.y), f[3] = make_float2(b.z, b.w);
+}
+
 // Xs[p, :] = fp16(x[perm[p] / K, :]) for p < n, 8 values per thread.
+template <class T>
 __global__ void moe_gather_kernel(
-    const __nv_bfloat16* x, const int* perm, int n, int K, int H, __half* xs, unsigned* status
+    const T* x, const int* perm, int n, int K, int H, __half* xs, unsigned* status
 ) {
     pdl_enter();
     const int per_row = H / 8;
@@ -210,13 +226,13 @@ __global__ void moe_gather_kernel(
     for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
         const int p = int(i / per_row), c = int(i % per_row);
         const int token = perm[p] / K;
-        const uint4 raw = *reinterpret_cast<const uint4*>(x + size_t(token) * H + c * 8);
-        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        float2 vals[4];
+        load8(x + size_t(token) * H + c * 8, vals);
         uint4 outv;
         __half2* o = reinterpret_cast<__half2*>(&outv);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const float2 f = __bfloat1622float2(b[k]);
+            const float2 f = vals[k];
             bad |= fabsf(f.x) > 65504.f || fabsf(f.y) > 65504.f;
             o[k] = __floats2half2_rn(f.x, f.y);
         }
@@ -1017,9 +1033,10 @@ __global__ void rows_regroup_kernel(const uint4* src, uint4* dst, size_t row_wor
         to[i] = from[i];
 }
 
-// Routing, stable sort by expert and the gather of the sorted fp16 rows.
-int dispatch_launch(const float* logits, const uint16_t* x_bf16, size_t tokens, int H, int E, int K,
-                    const Workspace& ws, unsigned* status, cudaStream_t stream) {
+// Routing, stable sort by expert and the gather of the sorted fp16 rows
+// from bf16 token rows (x_f32 false) or fp32 rows.
+int dispatch_launch(const float* logits, const void* x, size_t tokens, int H, int E, int K,
+                    const Workspace& ws, unsigned* status, cudaStream_t stream, bool x_f32 = false) {
     const size_t n = tokens * size_t(K);
     cudaError_t e = cudaMemsetAsync(ws.counts, 0, size_t(E) * 4, stream);
     if (e != cudaSuccess)
@@ -1032,9 +1049,12 @@ int dispatch_launch(const float* logits, const uint16_t* x_bf16, size_t tokens, 
     const size_t work = n * size_t(H / 8);
     const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
     if (e == cudaSuccess)
-        e = launch_pdl(moe_gather_kernel, dim3(blocks), dim3(256), 0, stream,
-                       reinterpret_cast<const __nv_bfloat16*>(x_bf16), static_cast<const int*>(ws.perm), int(n), K, H,
-                       ws.xs, status);
+        e = x_f32 ? launch_pdl(moe_gather_kernel<float>, dim3(blocks), dim3(256), 0, stream,
+                               static_cast<const float*>(x), static_cast<const int*>(ws.perm), int(n), K, H, ws.xs,
+                               status)
+                  : launch_pdl(moe_gather_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream,
+                               static_cast<const __nv_bfloat16*>(x), static_cast<const int*>(ws.perm), int(n), K, H,
+                               ws.xs, status);
     if (e != cudaSuccess || (e = cudaGetLastError()) != cudaSuccess)
         return cuda_fail(e, "MoE routing launches");
     return KB200_OK;
@@ -1186,15 +1206,21 @@ int kb200_moe_route(const float* logits, size_t tokens, int32_t experts, int32_t
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_route_kernel launch");
 }
 
-int kb200_moe_forward(const kb200_moe_weights* w, const uint16_t* x_bf16, const float* logits, size_t tokens, float* out,
-                      void* workspace, size_t workspace_bytes, unsigned* status, void* stream_ptr) {
+}  // extern "C"
+
+namespace kb200 {
+namespace {
+
+// The whole layer over token rows x (bf16, or fp32 when x_f32).
+int forward_layer(const kb200_moe_weights* w, const void* x, bool x_f32, const float* logits, size_t tokens, float* out,
+                  void* workspace, size_t workspace_bytes, unsigned* status, void* stream_ptr) {
     if (const int s = check_weights(w))
         return s;
     if (!tokens)
         return KB200_OK;
-    if (!x_bf16 || !logits || !out || !workspace)
+    if (!x || !logits || !out || !workspace)
         return fail(KB200_INVALID, "null pointer");
-    if (!aligned(x_bf16, 16) || !aligned(out, 16) || !aligned(workspace, 256))
+    if (!aligned(x, 16) || !aligned(out, 16) || !aligned(workspace, 256))
         return fail(KB200_INVALID, "MoE activations must be 16-byte aligned, workspace 256-byte aligned");
     const size_t n = tokens * size_t(w->top_k);
     if (n > size_t(INT32_MAX) / 4)
@@ -1205,11 +1231,26 @@ int kb200_moe_forward(const kb200_moe_weights* w, const uint16_t* x_bf16, const 
     if (!encoder())
         return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
     auto stream = static_cast<cudaStream_t>(stream_ptr);
-    if (const int s = dispatch_launch(logits, x_bf16, tokens, w->hidden, w->experts, w->top_k, ws, status, stream))
+    if (const int s = dispatch_launch(logits, x, tokens, w->hidden, w->experts, w->top_k, ws, status, stream, x_f32))
         return s;
     if (const int s = experts_launch(w, ws.xs, ws.offsets, ws.mtile, n, ws.act, ws.y, status, stream))
         return s;
     return combine_launch(ws.y, ws.weight, ws.pos, tokens, w->top_k, w->hidden, out, stream);
+}
+
+}  // namespace
+}  // namespace kb200
+
+extern "C" {
+
+int kb200_moe_forward(const kb200_moe_weights* w, const uint16_t* x_bf16, const float* logits, size_t tokens, float* out,
+                      void* workspace, size_t workspace_bytes, unsigned* status, void* stream) {
+    return forward_layer(w, x_bf16, false, logits, tokens, out, workspace, workspace_bytes, status, stream);
+}
+
+int kb200_moe_forward_f32(const kb200_moe_weights* w, const float* x, const float* logits, size_t tokens, float* out,
+                          void* workspace, size_t workspace_bytes, unsigned* status, void* stream) {
+    return forward_layer(w, x, true, logits, tokens, out, workspace, workspace_bytes, status, stream);
 }
 
 size_t kb200_moe_dispatch_workspace_bytes(size_t tokens, int32_t hidden, int32_t experts, int32_t top_k) {

@@ -212,6 +212,23 @@ int kb200_dense_gguf_source(kb200_context* ctx, kb200_bank* bank, const kb200_so
     return s;
 }
 
+// The MoE layer on a fake device: out = 2 * x when it answers OK.
+int kb200_moe_forward_host(kb200_context* ctx, const kb200_moe_weights* w, const float* x, const float*,
+                           std::size_t tokens, float* out, const volatile std::uint8_t* cancel, int* result) {
+    auto& d = device_of(reinterpret_cast<kb200_context_fake*>(ctx)->device);
+    ++d.calls;
+    d.saw_cancel = cancel != nullptr;
+    *result = KB200_RESULT_UNSUPPORTED;
+    if (d.status != KB200_OK) {
+        last_error = d.error;
+        return d.status;
+    }
+    for (std::size_t i = 0; i < tokens * std::size_t(w->hidden); ++i)
+        out[i] = 2.f * x[i];
+    *result = d.result;
+    return KB200_OK;
+}
+
 }  // extern "C"
 
 namespace {
@@ -504,7 +521,40 @@ void failures() {
 
 }  // namespace
 
+// The adapter's MoE member: shapes that do not fit are unsupported before
+// the device is asked, the device's unsupported stays unsupported with the
+// output untouched, its failures throw the reference's messages, and a
+// success returns the device's result on the chosen device.
+void moe_layer() {
+    reset({{0, 1ull << 30}, {1, 1ull << 30}});
+    kadan::b200::Compute compute(std::make_shared<Fallback>(), {0, 1}, 1ull << 30, 1ull << 20);
+    kb200_moe_weights w{};
+    w.hidden = 8, w.experts = 4, w.top_k = 2;
+    std::vector<float> x(3 * 8), logits(3 * 4), y(3 * 8, -1.f);
+    for (std::size_t i = 0; i < x.size(); ++i)
+        x[i] = float(i);
+    std::atomic_bool cancel{false};
+    CHECK(compute.moe_mxfp4(w, x, logits, 3, std::span(y).first(8), cancel) == ProjectionResult::unsupported);
+    CHECK(compute.moe_mxfp4(w, x, std::span(logits).first(4), 3, y, cancel) == ProjectionResult::unsupported);
+    CHECK(compute.moe_mxfp4(w, x, logits, 3, y, cancel, 2) == ProjectionResult::unsupported);
+    CHECK(device_of(0).calls == 0 && device_of(1).calls == 0);
+    CHECK(compute.moe_mxfp4(w, x, logits, 3, y, cancel, 1) == ProjectionResult::finite);
+    CHECK(device_of(1).calls == 1 && device_of(0).calls == 0 && y[5] == 10.f && device_of(1).saw_cancel);
+    device_of(0).status = KB200_UNSUPPORTED;
+    std::vector<float> untouched(y.size(), -1.f);
+    CHECK(compute.moe_mxfp4(w, x, logits, 3, untouched, cancel) == ProjectionResult::unsupported);
+    CHECK(untouched[5] == -1.f);
+    device_of(0).status = KB200_NONFINITE_INPUT;
+    CHECK(thrown([&] { compute.moe_mxfp4(w, x, logits, 3, y, cancel); }) == "h3_cuda_nonfinite_input");
+    device_of(0).status = KB200_CUDA;
+    device_of(0).error = "h3_cuda: launch failed (moe)";
+    CHECK(thrown([&] { compute.moe_mxfp4(w, x, logits, 3, y, cancel); }) == "h3_cuda: launch failed (moe)");
+    cancel = true;
+    CHECK(thrown([&] { compute.moe_mxfp4(w, x, logits, 3, y, cancel); }) == "h3_cuda_cancelled");
+}
+
 int main() {
+    moe_layer();
     batch_over_two_devices();
     source_with_bias_over_two_devices();
     unsupported_before_any_read();

@@ -230,3 +230,47 @@ def test_moe_layer_from_safetensors_shard(kb, oracle, cuda, tmp_path):
                                layer.down_scales, round_act=2, **args)
     assert rel_err(out.cpu().numpy(), ref16) <= 1e-3
     assert status.item() == 0
+
+
+def test_moe_host_span_call(kb, oracle, cuda, config3_layer):
+    """kb200_moe_forward_host: fp32 host rows through the layer (config 3, T =
+    64) within 1e-3 of the unrounded oracle on sampled tokens, result
+    certified finite; calls outside the contract or with scales the fp16
+    operands cannot hold are unsupported and leave the output untouched;
+    non-finite inputs are refused before any device work."""
+    import torch
+
+    from kadan_b200 import synth
+
+    E, H, I, K, T = 32, 2880, 2880, 4, 64
+    w, dev, host = config3_layer
+    x = synth.activations(T * H, seed=71, dtype="f32").reshape(T, H)
+    logits = synth.activations(T * E, seed=72, dtype="f32").reshape(T, E)
+    ctx = kb.Context(0)
+    try:
+        out, result = kb.moe_forward_host(ctx, w, x, logits)
+        assert result == kb.RESULT_FINITE
+        pick = np.array([0, 9, 31, 63])
+        want = oracle.moe_forward(x[pick], logits[pick], host["gu_w"], host["gu_s"], host["dn_w"], host["dn_s"],
+                                  hidden=H, inter=I, experts=E, top_k=K, round_act=0)
+        assert rel_err(out[pick], want) <= 1e-3
+        # A scale byte outside 104..140: the caller's path must take the layer.
+        bad_s = dev["gu_s"].clone()
+        bad_s.view(-1)[5] = 200
+        wb = kb.moe_weights(dev["gu_w"], bad_s, dev["dn_w"], dev["dn_s"], hidden=H, inter=I, experts=E, top_k=K)
+        sentinel = np.full((T, H), np.nan, dtype=np.float32)
+        routed_to_0 = bool((oracle.moe_route(logits, K)[0] == 0).any())
+        if routed_to_0:
+            with pytest.raises(kb.Unsupported):
+                kb.moe_forward_host(ctx, wb, x, logits, out=sentinel)
+            assert np.isnan(sentinel).all()
+        with pytest.raises(kb.Unsupported):
+            kb.moe_forward_host(ctx, w, x[:0], logits[:0])
+        nan_x = x.copy()
+        nan_x[3, 7] = np.nan
+        with pytest.raises(kb.KadanError) as err:
+            kb.moe_forward_host(ctx, w, nan_x, logits)
+        assert err.value.status == kb.NONFINITE_INPUT
+        torch.cuda.synchronize()
+    finally:
+        ctx.close()
