@@ -390,7 +390,8 @@ def run_default(args, rank, world, local_rank):
         nbytes = sum(tp.shard(p, world, rank).out_count * tp.shard_pitch(p, tp.shard(p, world, rank)) for p in g)
         us = group_ms[gi] / layers * 1e3
         row = any(p.mode == "row" for p in g) and dist is not None
-        kernel = "gemv_q6k_mma_kernel<1>" if g[0].encoding == kb.Q6_K else "gemv_q4k_mma_kernel<1>"
+        kernel = ("gemv_q6k_pair_kernel<3>" if tokens <= 2 else "gemv_q6k_mma_kernel<1,3>") if g[0].encoding == kb.Q6_K \
+            else "gemv_q4k_mma_kernel<1>"
         if row and reducer:
             kernel += " + peer_allreduce_kernel (gather)" if reducer.fused else " + peer_allreduce_kernel"
         launches.append({"launch": names[gi], "kernel": kernel, "bytes": nbytes, "us": round(us, 2),
