@@ -70,10 +70,10 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # from an ncu capture of that launch (the profile summary of
 # gemv_q4k_mma_kernel holds the command).
 GATE_UP_TRAFFIC = 66922496  # 66,164,224 read + 758,272 written
-# DRAM bytes per launch of the config-4 groups at N=1, keyed by group, from
-# ncu captures of a 2-layer stack (profiles/ summaries give the commands);
-# scaled to nothing: the launches are the same size at any layer count.
-C4_TRAFFIC: dict = {}
+# DRAM bytes (read + write) per launch of config-4 groups at N=1, keyed by
+# group, from ncu captures of a 2-layer stack (a launch has the same size at
+# any layer count; the profile summaries give the commands).
+C4_TRAFFIC: dict = {"down": 194824960 + 4199424}  # gemv_q6k_pair_kernel<3>
 
 
 def weight_bytes(out: int, in_: int) -> int:
