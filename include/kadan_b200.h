@@ -821,6 +821,74 @@ KB200_API int kb200_shard_load_mxfp4_expert_rows(const kb200_shard* shard, const
                                                  void* weights, uint64_t weights_capacity, void* scales,
                                                  uint64_t scales_capacity, uint64_t* columns);
 
+/* ---------------------------------------------------------------------------
+ * Per-kernel telemetry (the reference's CudaPhaseScope / cuda_trace::kernel,
+ * IW/include/kadan/cuda_phase_metrics.hpp:9-87, IW/src/cuda/cuda_telemetry.cuh:
+ * 101-160). A phase collects, for every launch the library issues on a
+ * thread while the phase is that thread's current one: the call count and
+ * host seconds of the launch call per kernel id, and the device seconds
+ * between CUDA events recorded around the launch on its stream. Events are
+ * read without waiting (at later launches, at kb200_phase_snapshot and when
+ * the thread leaves the phase); a pair still running when the thread leaves
+ * the phase counts as dropped, one that cannot be recorded or read as
+ * unavailable, and launches into a stream under graph capture are counted
+ * without events. Telemetry never fails a launch. Ids are a fixed protocol
+ * order: new kernels are added before KB200_KERNEL_COUNT. */
+typedef enum kb200_kernel {
+    KB200_KERNEL_GGUF_DEQUANT = 0,      /* dequant_kernel (gguf_decode_kernel) */
+    KB200_KERNEL_GEMV_STAGED = 1,       /* gemv_staged_kernel (Q8_0 and the staged formats) */
+    KB200_KERNEL_GEMV_GENERIC = 2,      /* gemv_generic_kernel (every encoding) */
+    KB200_KERNEL_GEMV_Q4K_MMA = 3,      /* gemv_q4k_mma_kernel */
+    KB200_KERNEL_GEMV_Q6K_MMA = 4,      /* gemv_q6k_mma_kernel (3-8 input rows) */
+    KB200_KERNEL_GEMV_Q6K_PAIR = 5,     /* gemv_q6k_pair_kernel (1-2 input rows) */
+    KB200_KERNEL_GEMM_PREFILL_ROWS = 6, /* prefill_rows_kernel (GEMM activation rows) */
+    KB200_KERNEL_GEMM_GGUF = 7,         /* gemm_gguf_kernel (tcgen05 prefill GEMM) */
+    KB200_KERNEL_MOE_ROUTE = 8,
+    KB200_KERNEL_MOE_SORT = 9,
+    KB200_KERNEL_MOE_GATHER = 10,
+    KB200_KERNEL_MOE_MTILE = 11,
+    KB200_KERNEL_MOE_GEMM = 12,         /* grouped tcgen05 GEMM (gate/up or down) */
+    KB200_KERNEL_MOE_GEMV = 13,         /* grouped GEMV (decode-sized batches) */
+    KB200_KERNEL_MOE_COMBINE = 14,
+    KB200_KERNEL_ROWS_REGROUP = 15,
+    KB200_KERNEL_MXFP4_GGML_DEQUANT = 16,
+    KB200_KERNEL_MXFP4_FROM_GGML = 17,
+    KB200_KERNEL_PEER_ALLREDUCE = 18,   /* peer all-reduce / row-parallel gather */
+    KB200_KERNEL_EP_EXCHANGE = 19,      /* expert-parallel peer exchange */
+    KB200_KERNEL_COUNT = 20
+} kb200_kernel;
+
+typedef struct kb200_kernel_metrics {
+    uint64_t calls;       /* launches issued */
+    double host_seconds;  /* time inside the launch calls */
+    uint64_t measured;    /* launches with a device interval read back */
+    double gpu_seconds;   /* sum of those intervals */
+} kb200_kernel_metrics;
+
+typedef struct kb200_phase_metrics {
+    kb200_kernel_metrics kernels[KB200_KERNEL_COUNT];
+    uint64_t dropped;           /* event pairs not finished when collected for the last time, or over capacity */
+    uint64_t unavailable;       /* event pairs that could not be created, recorded or read */
+    uint64_t shared_batch_size; /* as given to kb200_phase_create */
+    int32_t observed;           /* nonzero once anything was counted */
+} kb200_phase_metrics;
+
+typedef struct kb200_phase kb200_phase;
+
+KB200_API int kb200_phase_create(uint64_t shared_batch_size, kb200_phase** out);
+/* Makes `phase` (or none, NULL) the calling thread's current phase; the
+ * previous one is returned in *previous when that is not NULL (it stays
+ * referenced by the thread until then: pass it to kb200_phase_release). Event
+ * pairs of the previous phase are collected first. */
+KB200_API int kb200_phase_enter(kb200_phase* phase, kb200_phase** previous);
+/* The phase's counters; collects the calling thread's finished event pairs
+ * first (without waiting). */
+KB200_API int kb200_phase_snapshot(kb200_phase* phase, kb200_phase_metrics* out);
+/* Drops one reference (the creator's, or one returned by kb200_phase_enter). */
+KB200_API void kb200_phase_release(kb200_phase* phase);
+/* Stable name of a kernel id ("moe_gemm_kernel", ...); NULL when out of range. */
+KB200_API const char* kb200_kernel_name(int kernel);
+
 #ifdef __cplusplus
 }
 #endif

@@ -94,6 +94,23 @@ class ContextCounters(ctypes.Structure):
                 ("gemm_fallbacks", ctypes.c_uint64)]
 
 
+KERNEL_COUNT = 20
+
+
+class KernelMetrics(ctypes.Structure):
+    """kb200_kernel_metrics: one kernel id's launches in a phase."""
+
+    _fields_ = [("calls", ctypes.c_uint64), ("host_seconds", ctypes.c_double), ("measured", ctypes.c_uint64),
+                ("gpu_seconds", ctypes.c_double)]
+
+
+class PhaseMetrics(ctypes.Structure):
+    """kb200_phase_metrics."""
+
+    _fields_ = [("kernels", KernelMetrics * KERNEL_COUNT), ("dropped", ctypes.c_uint64),
+                ("unavailable", ctypes.c_uint64), ("shared_batch_size", ctypes.c_uint64), ("observed", ctypes.c_int32)]
+
+
 RESULT_UNSUPPORTED, RESULT_UNVALIDATED, RESULT_FINITE = 0, 1, 2
 MOE_SWIGLU_OAI, MOE_SILU = 0, 1
 
@@ -150,6 +167,13 @@ def _load() -> ctypes.CDLL:
     lib.kb200_gguf_gemm_range_offset.restype = c_size
     lib.kb200_gguf_gemm_range_offset.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
     lib.kb200_context_counters_get.argtypes = [vp, ctypes.POINTER(ContextCounters)]
+    lib.kb200_phase_create.argtypes = [ctypes.c_uint64, ctypes.POINTER(vp)]
+    lib.kb200_phase_enter.argtypes = [vp, ctypes.POINTER(vp)]
+    lib.kb200_phase_snapshot.argtypes = [vp, ctypes.POINTER(PhaseMetrics)]
+    lib.kb200_phase_release.restype = None
+    lib.kb200_phase_release.argtypes = [vp]
+    lib.kb200_kernel_name.restype = ctypes.c_char_p
+    lib.kb200_kernel_name.argtypes = [c_int]
     lib.kb200_weight_boundary.restype = c_size
     lib.kb200_weight_boundary.argtypes = [c_size, ctypes.POINTER(ctypes.c_uint64), c_size, c_size]
     lib.kb200_gguf_batch_partition.argtypes = [c_size, c_size, c_int, ctypes.POINTER(ctypes.c_uint64), c_size,
@@ -494,6 +518,61 @@ lib.kb200_moe_forward_f32.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_void_
 lib.kb200_moe_forward_host.argtypes = [ctypes.c_void_p, ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(ctypes.c_ubyte),
                                        ctypes.POINTER(ctypes.c_int)]
+
+
+def kernel_name(kernel: int):
+    """Stable name of a telemetry kernel id, or None."""
+    name = lib.kb200_kernel_name(kernel)
+    return name.decode() if name is not None else None
+
+
+class Phase:
+    """A telemetry phase (kb200_phase): while entered (a `with` block) every
+    launch the library issues on this thread is counted and timed."""
+
+    def __init__(self, shared_batch_size: int = 1):
+        h = ctypes.c_void_p()
+        check(lib.kb200_phase_create(shared_batch_size, ctypes.byref(h)))
+        self.handle = h
+        self._previous = []
+
+    def __enter__(self):
+        prev = ctypes.c_void_p()
+        check(lib.kb200_phase_enter(self.handle, ctypes.byref(prev)))
+        self._previous.append(prev)
+        return self
+
+    def __exit__(self, *exc):
+        prev = self._previous.pop()
+        check(lib.kb200_phase_enter(prev, None))
+        if prev:
+            lib.kb200_phase_release(prev)
+        return False
+
+    def snapshot(self) -> dict:
+        """Counters by kernel name (only ids with calls), plus dropped,
+        unavailable, shared_batch_size and observed."""
+        m = PhaseMetrics()
+        check(lib.kb200_phase_snapshot(self.handle, ctypes.byref(m)))
+        kernels = {}
+        for i in range(KERNEL_COUNT):
+            k = m.kernels[i]
+            if k.calls or k.measured:
+                kernels[kernel_name(i)] = {"calls": int(k.calls), "host_seconds": float(k.host_seconds),
+                                           "measured": int(k.measured), "gpu_seconds": float(k.gpu_seconds)}
+        return {"kernels": kernels, "dropped": int(m.dropped), "unavailable": int(m.unavailable),
+                "shared_batch_size": int(m.shared_batch_size), "observed": bool(m.observed)}
+
+    def close(self) -> None:
+        if self.handle:
+            lib.kb200_phase_release(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def moe_forward_host(ctx: "Context", w: MoeWeights, x, logits, out=None, cancel=None) -> tuple:

@@ -177,6 +177,7 @@ int kb200_gguf_dequant(
     const unsigned threads = 256;
     const size_t want = (count + threads - 1) / threads;
     const unsigned blocks = unsigned(want < 148u * 16u ? want : 148u * 16u);
+    TraceScope trace(KB200_KERNEL_GGUF_DEQUANT, static_cast<cudaStream_t>(stream));
     if (grid_coded(encoding))
         dequant_kernel<true><<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
             encoding, static_cast<const uint8_t*>(packed), count, out, status

@@ -327,6 +327,7 @@ int ep_launch(bool dispatch, EpParams& p, void* const* peers, double timeout_s, 
     // flags CTA 0 collects): a cooperative launch guarantees they are all
     // resident, or fails.
     void* args[] = {&p};
+    TraceScope trace(KB200_KERNEL_EP_EXCHANGE, static_cast<cudaStream_t>(stream));
     const cudaError_t e = cudaLaunchCooperativeKernel(
         dispatch ? reinterpret_cast<const void*>(ep_dispatch_kernel) : reinterpret_cast<const void*>(ep_return_kernel),
         dim3(kEpCtas), dim3(kEpThreads), args, 0, static_cast<cudaStream_t>(stream));

@@ -689,6 +689,7 @@ size_t exp_bytes(uint32_t rows) {
 }
 
 template <int F, int BN> void launch_gemm(const GemmParams& p, int grid, cudaStream_t stream) {
+    TraceScope trace(KB200_KERNEL_GEMM_GGUF, stream);
     gemm_gguf_kernel<F, BN><<<grid, kThreads, smem_total<F, BN>(), stream>>>(p);
 }
 
@@ -760,8 +761,12 @@ int kb200_gguf_gemm(const kb200_gemv_job* job, void* workspace, size_t workspace
     auto* xh = reinterpret_cast<__half*>(base);
     auto* row_exp = reinterpret_cast<int*>(base + xh_bytes(j.rows, j.in));
     auto* range = reinterpret_cast<unsigned*>(base + xh_bytes(j.rows, j.in) + exp_bytes(j.rows));
-    prefill_rows_kernel<<<j.rows, 256, 0, stream>>>(j.input, j.in, xh, row_exp, range);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    {
+        TraceScope trace(KB200_KERNEL_GEMM_PREFILL_ROWS, stream);
+        prefill_rows_kernel<<<j.rows, 256, 0, stream>>>(j.input, j.in, xh, row_exp, range);
+        e = cudaGetLastError();
+    }
     if (e != cudaSuccess)
         return cuda_fail(e, "prefill_rows_kernel launch");
 

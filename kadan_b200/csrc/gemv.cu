@@ -592,12 +592,14 @@ template <class F, int T> int launch_staged(const GemvParams& p, cudaStream_t st
     }
     const uint32_t slots = uint32_t(sm_count() * info[dev].blocks_per_sm);
     const uint32_t grid = std::min(p.total_tiles, slots);
+    TraceScope trace(KB200_KERNEL_GEMV_STAGED, stream);
     gemv_staged_kernel<F, T><<<grid, kThreads, smem, stream>>>(p);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "gemv_staged_kernel launch");
 }
 
 template <int Rows> int launch_generic(const GemvParams& p, cudaStream_t stream) {
+    TraceScope trace(KB200_KERNEL_GEMV_GENERIC, stream);
     if (grid_coded(p.encoding))
         gemv_generic_kernel<Rows, true><<<p.total_tiles, 32 * kGenericWarps, 0, stream>>>(p);
     else

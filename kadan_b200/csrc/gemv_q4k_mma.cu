@@ -476,30 +476,31 @@ __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, 
 // tile), add the later pieces' sums in CTA order (tail piece), or write the
 // outputs (whole tile or tail piece). acc[nt][0/1]: rows my_row, my_row + 8
 // for token nt*4 + t.
-template <int NT, class Await>
+template <int NT, class Await, int CT = kConsumerThreads>
 __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc, const MmaJob& job, float (&acc)[NT][2],
                                              int KS, int ks, int tid, uint32_t my_row, bool valid_lo, bool valid_hi,
                                              uint32_t r0, int rows, float* red, int* abort_flag, Await& await_dependency) {
+    static_assert(2 * NT * CT <= kSlotFloats, "a fixup slot holds every consumer thread's partial sums");
     const int warp = tid >> 5, lane = tid & 31, t = lane & 3;
     if (KS > 1) {
         // Sum the K splits of each row group: warp (rg, 0) collects.
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            red[(nt * 2 + 0) * kConsumerThreads + tid] = acc[nt][0];
-            red[(nt * 2 + 1) * kConsumerThreads + tid] = acc[nt][1];
+            red[(nt * 2 + 0) * CT + tid] = acc[nt][0];
+            red[(nt * 2 + 1) * CT + tid] = acc[nt][1];
         }
-        named_sync(1, kConsumerThreads);
+        named_sync(1, CT);
         if (ks == 0) {
             for (int k = 1; k < KS; ++k) {
                 const int other = (warp + k) * 32 + lane;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    acc[nt][0] += red[(nt * 2 + 0) * kConsumerThreads + other];
-                    acc[nt][1] += red[(nt * 2 + 1) * kConsumerThreads + other];
+                    acc[nt][0] += red[(nt * 2 + 0) * CT + other];
+                    acc[nt][1] += red[(nt * 2 + 1) * CT + other];
                 }
             }
         }
-        named_sync(1, kConsumerThreads);
+        named_sync(1, CT);
     }
     await_dependency();
     bool write = ks == 0;
@@ -511,8 +512,8 @@ __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc
         unsigned long long* mine = p.partials + size_t(blockIdx.x) * kSlotFloats;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            store_relaxed(mine + (nt * 2 + 0) * kConsumerThreads + tid, tagged(acc[nt][0]));
-            store_relaxed(mine + (nt * 2 + 1) * kConsumerThreads + tid, tagged(acc[nt][1]));
+            store_relaxed(mine + (nt * 2 + 0) * CT + tid, tagged(acc[nt][0]));
+            store_relaxed(mine + (nt * 2 + 1) * CT + tid, tagged(acc[nt][1]));
         }
         write = false;
     } else if (!pc.whole) {
@@ -529,8 +530,8 @@ __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc
                 const unsigned long long* part = p.partials + size_t(c) * kSlotFloats;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    w[q][nt][0] = load_relaxed(part + (nt * 2 + 0) * kConsumerThreads + tid);
-                    w[q][nt][1] = load_relaxed(part + (nt * 2 + 1) * kConsumerThreads + tid);
+                    w[q][nt][0] = load_relaxed(part + (nt * 2 + 0) * CT + tid);
+                    w[q][nt][1] = load_relaxed(part + (nt * 2 + 1) * CT + tid);
                 }
             }
 #pragma unroll
@@ -542,7 +543,7 @@ __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc
                 for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
                     for (int hl = 0; hl < 2; ++hl) {
-                        unsigned long long* at = part + (nt * 2 + hl) * kConsumerThreads + tid;
+                        unsigned long long* at = part + (nt * 2 + hl) * CT + tid;
                         unsigned long long v = w[q][nt][hl];
                         for (uint32_t poll = 0; (v >> 32) != 1ull; ++poll) {
                             if (poll == wait_polls) {
@@ -1127,12 +1128,13 @@ __host__ __device__ constexpr int pair_segment_blocks(int rows) {
     return kPairSegBudget / (rows * kPairTokenBlock) / kQ6Chunk * kQ6Chunk;
 }
 
-template <int S> struct PairLayout {
+// S stages, W consumer warps (each takes kQ6Chunk / W blocks of a stage).
+template <int S, int W = kWarps> struct PairLayout {
     static constexpr int kStages = S;
     static constexpr int kStagesOff = 0;
     static constexpr int kSegOff = kStages * kQ6StageBytes;
     static constexpr int kRedOff = kSegOff + kPairSegBudget;
-    static constexpr int kRedBytes = kConsumerThreads * 4 * 4;
+    static constexpr int kRedBytes = 32 * W * 4 * 4;
     static constexpr int kBarOff = kRedOff + kRedBytes;
     static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
 };
@@ -1153,6 +1155,7 @@ struct PairSegment {
 // pair layout: one warp per (block, token); lane L owns values 8L..8L+7 (half
 // L % 2 of sub-block L / 2). Every load of a warp's items is in flight before
 // the first is used.
+template <int W>
 __device__ void prep_pairs(uint8_t* smem, const PairSegment& seg, const float* x, size_t in, int blk0, int nblk) {
     const int rows = seg.rows;
     uint32_t* words = seg.words(smem);
@@ -1164,11 +1167,11 @@ __device__ void prep_pairs(uint8_t* smem, const PairSegment& seg, const float* x
     const int s = lane >> 1, half = lane & 1;
     const int ip = s >> 3, qt = (s >> 1) & 3, par = s & 1;
     constexpr int kBatch = 4;
-    for (int base = warp; base < items; base += kWarps * kBatch) {
+    for (int base = warp; base < items; base += W * kBatch) {
         float v[kBatch][8];
 #pragma unroll
         for (int q = 0; q < kBatch; ++q) {
-            const int item = min(base + q * kWarps, items - 1);
+            const int item = min(base + q * W, items - 1);
             const int blk = item / rows, tok = item % rows;
             const float* xr = x + size_t(tok) * in + size_t(blk0 + blk) * 256 + lane * 8;
             if (vec) {
@@ -1183,7 +1186,7 @@ __device__ void prep_pairs(uint8_t* smem, const PairSegment& seg, const float* x
         }
 #pragma unroll
         for (int q = 0; q < kBatch; ++q) {
-            const int item = base + q * kWarps;
+            const int item = base + q * W;
             if (item >= items)
                 break;
             const int blk = item / rows, tok = item % rows;
@@ -1326,23 +1329,25 @@ __device__ __forceinline__ void q6k_pair_block(const uint8_t* bg, const uint8_t*
 // Q6_K decode GEMV for one or two input rows per pass: the Q6_K kernel's
 // tiles, stages, pieces, fixup and programmatic dependent launch, with the
 // paired-sub-block inner loop above.
-template <int S>
-__global__ void __launch_bounds__(kThreadsQ, S == 2 ? 3 : 2) gemv_q6k_pair_kernel(const __grid_constant__ MmaParams p) {
-    using L = PairLayout<S>;
+template <int S, int W>
+__global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_kernel(const __grid_constant__ MmaParams p) {
+    using L = PairLayout<S, W>;
     constexpr int kStages = L::kStages;
+    constexpr int CT = 32 * W;               // consumer threads
+    constexpr int kPerWarp = kQ6Chunk / W;   // blocks of a stage per consumer warp
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
     auto* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
     auto* empty = full + kStages;
     auto* abort_flag = reinterpret_cast<int*>(empty + kStages);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr int KS = kWarps;
+    constexpr int KS = W;
     auto* red = reinterpret_cast<float*>(smem + L::kRedOff);
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kWarps);
+            mbar_init(&empty[s], W);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -1350,7 +1355,7 @@ __global__ void __launch_bounds__(kThreadsQ, S == 2 ? 3 : 2) gemv_q6k_pair_kerne
     }
     __syncthreads();
 
-    if (warp == kWarps) {
+    if (warp == W) {
         // ------------------------------ producer ------------------------------
         if (lane != 0)
             return;
@@ -1427,9 +1432,9 @@ __global__ void __launch_bounds__(kThreadsQ, S == 2 ? 3 : 2) gemv_q6k_pair_kerne
                 const int start = nblocks <= seg.blocks ? 0 : blk_first;
                 const int count = min(seg.blocks, nblocks - start);
                 await_dependency();
-                named_sync(1, kConsumerThreads);
-                prep_pairs(smem, seg, x, job.in, start, count);
-                named_sync(1, kConsumerThreads);
+                named_sync(1, CT);
+                prep_pairs<W>(smem, seg, x, job.in, start, count);
+                named_sync(1, CT);
                 seg_x = x, seg_rows = rows, seg_blk0 = start, seg_nblk = count;
             }
             const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
@@ -1438,8 +1443,8 @@ __global__ void __launch_bounds__(kThreadsQ, S == 2 ? 3 : 2) gemv_q6k_pair_kerne
             if (!aborted) {
                 const uint8_t* stage = smem + L::kStagesOff + slot * kQ6StageBytes;
 #pragma unroll
-                for (int bb = 0; bb < 2; ++bb) {
-                    const int b = 2 * ks + bb;  // block of the chunk; odd b sits 2 bytes off a word
+                for (int bb = 0; bb < kPerWarp; ++bb) {
+                    const int b = kPerWarp * ks + bb;  // block of the chunk; odd b sits 2 bytes off a word
                     if (b >= nb)
                         break;
                     const int sblk = blk_first + b - seg_blk0;
@@ -1448,7 +1453,7 @@ __global__ void __launch_bounds__(kThreadsQ, S == 2 ? 3 : 2) gemv_q6k_pair_kerne
                     const uint32_t* bw = words + (sblk * 8 * rows + btok) * 16 + lane_word;
                     const uint32_t xw = xwords[(sblk * rows + btok) * 16 + lane_word];
                     const float sc_tok = scales[sblk * rows + ctok];
-                    if (bb)
+                    if (b & 1)
                         q6k_pair_block<true>(bg, b8, bw, rows * 16, xw, g, t, sc_tok, acc_g, acc_8, finite_g, finite_8);
                     else
                         q6k_pair_block<false>(bg, b8, bw, rows * 16, xw, g, t, sc_tok, acc_g, acc_8, finite_g, finite_8);
@@ -1467,8 +1472,8 @@ __global__ void __launch_bounds__(kThreadsQ, S == 2 ? 3 : 2) gemv_q6k_pair_kerne
         acc_8 += __shfl_xor_sync(0xffffffffu, acc_8, 1);
         const int from = (lane & ~3) | ((2 * t) & 3);
         float acc[1][2] = {{__shfl_sync(0xffffffffu, acc_g, from), __shfl_sync(0xffffffffu, acc_8, from)}};
-        finish_piece<1>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0, rows, red, abort_flag,
-                        await_dependency);
+        finish_piece<1, decltype(await_dependency), CT>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0,
+                                                        rows, red, abort_flag, await_dependency);
     }
 }
 
@@ -1609,19 +1614,19 @@ template <int NT, int S> int q6k_slots() {
     return sm_count() * blocks_per_sm[dev];
 }
 
-template <int S> int q6k_pair_slots() {
+template <int S, int W> int q6k_pair_slots() {
     static int blocks_per_sm[64] = {};
     static std::mutex lock;
     int dev = 0;
     cudaGetDevice(&dev);
-    constexpr int smem = PairLayout<S>::kTotal + 128;
+    constexpr int smem = PairLayout<S, W>::kTotal + 128;
     std::lock_guard<std::mutex> guard(lock);
     if (!blocks_per_sm[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_pair_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_pair_kernel<S, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_pair_kernel attribute");
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_pair_kernel<S>, kThreadsQ, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_pair_kernel<S, W>, 32 * W + 32, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_pair_kernel occupancy");
         blocks_per_sm[dev] = n > 0 ? n : 1;
@@ -1640,6 +1645,7 @@ template <int NT> int launch_q4k(const MmaParams& p, uint32_t grid, cudaStream_t
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    TraceScope trace(KB200_KERNEL_GEMV_Q4K_MMA, stream);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_q4k_mma_kernel<NT>, p);
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "gemv_q4k_mma_kernel launch");
 }
@@ -1693,7 +1699,7 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     const bool pair = max_rows <= 2 && tuning().q6_pair;
     const uint32_t group_rows = pair ? 2u : uint32_t(4 * nt);
     const bool two_stage = nt == 1 && tuning().q6_stages == 2;
-    int slots = pair ? (two_stage ? q6k_pair_slots<2>() : q6k_pair_slots<3>())
+    int slots = pair ? (two_stage ? q6k_pair_slots<2, 4>() : q6k_pair_slots<3, 4>())
               : nt == 2 ? q6k_slots<2, 2>() : two_stage ? q6k_slots<1, 2>() : q6k_slots<1, 3>();
     if (slots <= 0)
         return -slots;
@@ -1763,8 +1769,9 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t e = pair && two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2>, p)
-                              : pair        ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<3>, p)
+        TraceScope trace(pair ? KB200_KERNEL_GEMV_Q6K_PAIR : KB200_KERNEL_GEMV_Q6K_MMA, stream);
+        const cudaError_t e = pair && two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 4>, p)
+                              : pair        ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<3, 4>, p)
                               : nt == 2     ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<2, 2>, p)
                               : two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 2>, p)
                                           : cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 3>, p);

@@ -58,6 +58,25 @@ void clear_gemv_fixups();
 // The prefill GEMM (kb200_gguf_gemm) takes the job's weights.
 bool gemm_eligible(const kb200_gemv_job& j);
 
+// Counts and times one kernel launch for the calling thread's current phase
+// (kb200_phase_enter): construct it right before the launch and let it go out
+// of scope right after. Without a current phase it does nothing.
+class TraceScope {
+public:
+    TraceScope(kb200_kernel id, cudaStream_t stream);
+    ~TraceScope();
+    TraceScope(const TraceScope&) = delete;
+    TraceScope& operator=(const TraceScope&) = delete;
+
+private:
+    bool active_ = false, timed_ = false;
+    int kernel_ = 0;
+    cudaStream_t stream_ = nullptr;
+    void* start_ = nullptr;  // CUevent
+    void* end_ = nullptr;    // CUevent
+    double t0_ = 0.0;
+};
+
 // The CUDA device whose memory a weight bank holds, or -1 for a bank over
 // caller-supplied operations.
 int bank_device(const kb200_bank* bank);

@@ -55,8 +55,9 @@ __device__ __forceinline__ void pdl_enter() {
 }
 
 template <class... Params, class... Args>
-cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                       Args&&... args) {
+cudaError_t launch_pdl(kb200_kernel id, void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+    TraceScope trace(id, stream);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -268,10 +269,12 @@ __global__ void moe_combine_kernel(
 // weight tiles (measured: with 128-row tiles the activation TMA tiles took ~2
 // us to arrive and the tensor pipe sat at 26 %). Activation and raw-code
 // stages (kStagesG) and dequantised B stages (kStagesB) are separate rings.
-constexpr int BM = 128, BN = 256, BK = 64, kStagesG = 4, kStagesB = 2;
+// The dequant threads read their rows' block scales straight from global
+// memory (L2 hits after the first m-tile of an expert), one K step ahead, so
+// shared memory holds four dequantised B stages.
+constexpr int BM = 128, BN = 256, BK = 64, kStagesG = 4, kStagesB = 4;
 constexpr int kABytes = BM * BK * 2, kBBytes = BN * BK * 2, kRawBytes = BN * BK / 2;
 constexpr int kMaxK = 4096;
-constexpr int kScaleBytes = BN * (kMaxK / 32);
 constexpr int kDequantWarpsG = 8;                    // one B row per thread
 constexpr int kThreadsG = 32 * (2 + kDequantWarpsG + 4);  // producer, MMA, dequant, 4 epilogue warps
 
@@ -291,7 +294,7 @@ struct GroupParams {
 
 struct GemmShared {
     uint64_t tma_full[kStagesG], stage_empty[kStagesG], b_full[kStagesB], b_empty[kStagesB];
-    uint64_t sc_full[2], sc_empty[2], acc_full[2], acc_empty[2];
+    uint64_t acc_full[2], acc_empty[2];
     uint32_t tmem_base;
     int abort;
 };
@@ -299,8 +302,7 @@ struct GemmShared {
 constexpr int kSmemA = 0;
 constexpr int kSmemB = kSmemA + kStagesG * kABytes;
 constexpr int kSmemRaw = kSmemB + kStagesB * kBBytes;
-constexpr int kSmemScale = kSmemRaw + kStagesG * kRawBytes;
-constexpr int kSmemShared = kSmemScale + 2 * kScaleBytes;
+constexpr int kSmemShared = kSmemRaw + kStagesG * kRawBytes;
 constexpr int kSmemTotal = kSmemShared + int(sizeof(GemmShared)) + 1024;
 static_assert(kSmemTotal <= 232448, "shared memory per CTA");
 
@@ -399,8 +401,6 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
             mbar_init(&sh->b_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&sh->sc_full[b], 1);
-            mbar_init(&sh->sc_empty[b], 32 * kDequantWarpsG);
             mbar_init(&sh->acc_full[b], 1);
             mbar_init(&sh->acc_empty[b], 4);
         }
@@ -419,27 +419,11 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------ producer (TMA)
-        uint32_t it = 0, lt = 0;
-        uint32_t issued_sc = 0;
-        for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x, ++lt) {
+        uint32_t it = 0;
+        for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x) {
             const TileInfo t = tile_info(p, tile);
             int r_lo, r_hi;
             tile_rows(p, t, r_lo, r_hi);
-            const int sb = int(lt & 1u);
-            if (lt >= 2 && !mbar_wait(&sh->sc_empty[sb], ((lt >> 1) & 1u) ^ 1u, watchdog_empty_barrier, p.watchdog)) {
-                *abort_flag = 1;
-                break;
-            }
-            // Scale rows of the tile: two runs of 64 rows, clamped to the tensor.
-            const int limit_rows = p.E * p.Nrows;
-            const int n_lo = max(0, min(BN / 2, limit_rows - r_lo)), n_hi = max(0, min(BN / 2, limit_rows - r_hi));
-            mbar_expect_tx(&sh->sc_full[sb], uint32_t((n_lo + n_hi) * sc_row));
-            uint8_t* sdst = smem + kSmemScale + sb * kScaleBytes;
-            if (n_lo)
-                bulk_g2s(sdst, p.scales + size_t(r_lo) * sc_row, uint32_t(n_lo * sc_row), &sh->sc_full[sb]);
-            if (n_hi)
-                bulk_g2s(sdst + (BN / 2) * sc_row, p.scales + size_t(r_hi) * sc_row, uint32_t(n_hi * sc_row), &sh->sc_full[sb]);
-            ++issued_sc;
             for (int ks = 0; ks < KS; ++ks, ++it) {
                 const int s = int(it % kStagesG);
                 if (it >= kStagesG
@@ -461,10 +445,6 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
         for (uint32_t k = 0; k < kStagesG && k < it; ++k) {
             const uint32_t last = it - 1 - k;
             mbar_wait(&sh->tma_full[last % kStagesG], (last / kStagesG) & 1u, watchdog_drain, p.watchdog);
-        }
-        for (uint32_t k = 0; k < 2 && k < issued_sc; ++k) {
-            const uint32_t last = issued_sc - 1 - k;
-            mbar_wait(&sh->sc_full[last & 1u], (last >> 1) & 1u, watchdog_drain, p.watchdog);
         }
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------- MMA issuer
@@ -506,21 +486,26 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
     } else if (warp >= 2 && warp < 2 + kDequantWarpsG) {
         // ------------------------------------------------- dequant warps
         const int r = tid - 64;  // B-operand row of this thread
-        uint32_t it = 0, lt = 0;
+        uint32_t it = 0;
         bool scale_ok = true;
-        for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x, ++lt) {
-            const int sb = int(lt & 1u);
-            if (!mbar_wait(&sh->sc_full[sb], (lt >> 1) & 1u, watchdog_full_barrier, p.watchdog)) {
-                *abort_flag = 1;
-                break;
-            }
-            const uint8_t* srow = smem + kSmemScale + sb * kScaleBytes + r * sc_row;
-            // Rows past the weight tensor were zero-filled and have no scale bytes.
+        for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x) {
+            // Rows past the weight tensor were zero-filled and have no scale
+            // bytes: they take scale byte 0 (a zero factor).
             int r_lo, r_hi;
             const TileInfo ti = tile_info(p, tile);
             tile_rows(p, ti, r_lo, r_hi);
-            const bool row_in_tensor = (r < BN / 2 ? r_lo + r : r_hi + (r - BN / 2)) < p.E * p.Nrows;
+            const int wrow = r < BN / 2 ? r_lo + r : r_hi + (r - BN / 2);
+            const bool row_in_tensor = wrow < p.E * p.Nrows;
+            const uint8_t* srow = p.scales + size_t(row_in_tensor ? wrow : 0) * sc_row;
+            // The two block scales of K step kx, loaded one step ahead.
+            auto scales_of = [&](int kx) -> uint32_t {
+                return row_in_tensor ? uint32_t(__ldg(srow + 2 * kx)) | uint32_t(__ldg(srow + 2 * kx + 1)) << 8 : 0u;
+            };
+            uint32_t next_sc = scales_of(k_step(0, ti.nt, KS));
             for (int ks = 0; ks < KS; ++ks, ++it) {
+                const uint32_t sc_pair = next_sc;
+                if (ks + 1 < KS)
+                    next_sc = scales_of(k_step(ks + 1, ti.nt, KS));
                 const int s = int(it % kStagesG), sbs = int(it % kStagesB);
                 if (!mbar_wait(&sh->tma_full[s], (it / kStagesG) & 1u, watchdog_full_barrier, p.watchdog)
                     || (it >= kStagesB
@@ -533,8 +518,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                 const uint4 c0 = *reinterpret_cast<const uint4*>(raw);
                 const uint4 c1 = *reinterpret_cast<const uint4*>(raw + 16);
                 bool ok0, ok1;
-                const int kx = k_step(ks, ti.nt, KS);
-                const uint32_t s0 = e8m0_half2(srow[2 * kx], ok0), s1 = e8m0_half2(srow[2 * kx + 1], ok1);
+                const uint32_t s0 = e8m0_half2(sc_pair & 0xFFu, ok0), s1 = e8m0_half2(sc_pair >> 8, ok1);
                 scale_ok = scale_ok && (!row_in_tensor || (ok0 && ok1));
                 const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
                 uint8_t* brow = smem + kSmemB + sbs * kBBytes + r * 128;
@@ -552,7 +536,6 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                 fence_proxy_async();
                 mbar_arrive(&sh->b_full[sbs]);
             }
-            mbar_arrive(&sh->sc_empty[sb]);
         }
         if (!scale_ok && p.status)
             atomicOr(p.status, 2u);
@@ -595,7 +578,8 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                     tmem_wait_ld();
                     const int j0 = t.nt * (BN / 2) + 32 * c;
                     if (valid && j0 < I) {
-                        __align__(16) __half vals[32];
+                        // Pairs of fp16 outputs in registers (constant indices only).
+                        uint32_t hv[16];
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             const int j = j0 + i;
@@ -605,17 +589,20 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                                 gv += p.bias[size_t(t.e) * p.Nrows + gr];
                                 uv += p.bias[size_t(t.e) * p.Nrows + ur];
                             }
-                            vals[i] = __float2half_rn(act_fn(gv, uv, p.act_kind, p.limit, p.alpha));
+                            const uint32_t h = __half_as_ushort(__float2half_rn(act_fn(gv, uv, p.act_kind, p.limit, p.alpha)));
+                            hv[i / 2] = (i & 1) ? hv[i / 2] | (h << 16) : h;
                         }
                         __half* dst = act + size_t(prow) * p.out_cols + j0;
                         const int n = min(32, I - j0);
                         if (n == 32) {
 #pragma unroll
                             for (int v = 0; v < 4; ++v)
-                                reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(vals)[v];
+                                reinterpret_cast<uint4*>(dst)[v] = make_uint4(hv[4 * v], hv[4 * v + 1], hv[4 * v + 2], hv[4 * v + 3]);
                         } else {
-                            for (int i = 0; i < n; ++i)
-                                dst[i] = vals[i];
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (i < n)
+                                    dst[i] = __ushort_as_half(uint16_t(hv[i / 2] >> (16 * (i & 1))));
                         }
                     }
                 }
@@ -629,7 +616,7 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                     if (valid && n0 < p.Nrows) {
                         float* dst = y + size_t(prow) * p.out_cols + n0;
                         const int n = min(32, p.Nrows - n0);
-                        __align__(16) float f[32];
+                        float f[32];
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             f[i] = __uint_as_float(v[i])
@@ -637,10 +624,12 @@ __global__ void __launch_bounds__(kThreadsG, 1) moe_gemm_kernel(const __grid_con
                         if (n == 32) {
 #pragma unroll
                             for (int k = 0; k < 8; ++k)
-                                reinterpret_cast<float4*>(dst)[k] = reinterpret_cast<const float4*>(f)[k];
+                                reinterpret_cast<float4*>(dst)[k] = make_float4(f[4 * k], f[4 * k + 1], f[4 * k + 2], f[4 * k + 3]);
                         } else {
-                            for (int i = 0; i < n; ++i)
-                                dst[i] = f[i];
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (i < n)
+                                    dst[i] = f[i];
                         }
                     }
                 }
@@ -960,6 +949,7 @@ int launch_gemm(GroupParams& p, int max_tiles, cudaStream_t stream) {
     const int grid = std::max(1, std::min(slots, max_tiles));
     // A plain launch: GEMM CTAs launched early would hold SMs (225 KB of
     // shared memory each) that the gather kernel before them still needs.
+    TraceScope trace(KB200_KERNEL_MOE_GEMM, stream);
     moe_gemm_kernel<<<grid, kThreadsG, kSmemTotal, stream>>>(p);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_gemm_kernel launch");
@@ -1041,18 +1031,18 @@ int dispatch_launch(const float* logits, const void* x, size_t tokens, int H, in
     cudaError_t e = cudaMemsetAsync(ws.counts, 0, size_t(E) * 4, stream);
     if (e != cudaSuccess)
         return cuda_fail(e, "counts memset");
-    e = launch_pdl(moe_route_kernel, dim3(unsigned((tokens * 32 + 255) / 256)), dim3(256), 0, stream, logits,
+    e = launch_pdl(KB200_KERNEL_MOE_ROUTE, moe_route_kernel, dim3(unsigned((tokens * 32 + 255) / 256)), dim3(256), 0, stream, logits,
                    int(tokens), E, K, ws.chosen, ws.weight, ws.counts);
     if (e == cudaSuccess)
-        e = launch_pdl(moe_sort_kernel, dim3(1), dim3(1024), 0, stream, static_cast<const int*>(ws.chosen), int(n), E,
+        e = launch_pdl(KB200_KERNEL_MOE_SORT, moe_sort_kernel, dim3(1), dim3(1024), 0, stream, static_cast<const int*>(ws.chosen), int(n), E,
                        static_cast<const int*>(ws.counts), ws.offsets, ws.perm, ws.pos, ws.mtile);
     const size_t work = n * size_t(H / 8);
     const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
     if (e == cudaSuccess)
-        e = x_f32 ? launch_pdl(moe_gather_kernel<float>, dim3(blocks), dim3(256), 0, stream,
+        e = x_f32 ? launch_pdl(KB200_KERNEL_MOE_GATHER, moe_gather_kernel<float>, dim3(blocks), dim3(256), 0, stream,
                                static_cast<const float*>(x), static_cast<const int*>(ws.perm), int(n), K, H, ws.xs,
                                status)
-                  : launch_pdl(moe_gather_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream,
+                  : launch_pdl(KB200_KERNEL_MOE_GATHER, moe_gather_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, stream,
                                static_cast<const __nv_bfloat16*>(x), static_cast<const int*>(ws.perm), int(n), K, H,
                                ws.xs, status);
     if (e != cudaSuccess || (e = cudaGetLastError()) != cudaSuccess)
@@ -1097,7 +1087,7 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
         v.limit = w->limit;
         v.alpha = w->alpha;
         v.status = status;
-        e = launch_pdl(moe_gemv_kernel, dim3(std::min(E * v.chunks, grid_cap)), dim3(32 * kGemvWarps), 0, stream, v);
+        e = launch_pdl(KB200_KERNEL_MOE_GEMV, moe_gemv_kernel, dim3(std::min(E * v.chunks, grid_cap)), dim3(32 * kGemvWarps), 0, stream, v);
         if (e != cudaSuccess)
             return cuda_fail(e, "moe_gemv_kernel launch");
         v.blocks = w->down_blocks;
@@ -1111,7 +1101,7 @@ int experts_launch(const kb200_moe_weights* w, const __half* xs, const int* offs
         v.epilogue = 1;
         v.split = 0;
         v.out_cols = H;
-        e = launch_pdl(moe_gemv_kernel, dim3(std::min(E * v.chunks, grid_cap)), dim3(32 * kGemvWarps), 0, stream, v);
+        e = launch_pdl(KB200_KERNEL_MOE_GEMV, moe_gemv_kernel, dim3(std::min(E * v.chunks, grid_cap)), dim3(32 * kGemvWarps), 0, stream, v);
         if (e != cudaSuccess)
             return cuda_fail(e, "moe_gemv_kernel launch");
         return KB200_OK;
@@ -1175,7 +1165,7 @@ int combine_launch(const float* y, const float* weight, const int* pos, size_t t
                    cudaStream_t stream) {
     const size_t work = tokens * size_t(H / 4);
     const int blocks = int(std::min<size_t>((work + 255) / 256, size_t(sm_count()) * 16));
-    const cudaError_t e = launch_pdl(moe_combine_kernel, dim3(blocks), dim3(256), 0, stream, y, weight, pos,
+    const cudaError_t e = launch_pdl(KB200_KERNEL_MOE_COMBINE, moe_combine_kernel, dim3(blocks), dim3(256), 0, stream, y, weight, pos,
                                      int(tokens), K, H, out);
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_combine_kernel launch");
 }
@@ -1200,6 +1190,7 @@ int kb200_moe_route(const float* logits, size_t tokens, int32_t experts, int32_t
     if (!logits || !chosen || !weight)
         return fail(KB200_INVALID, "null pointer");
     const int threads = 256, blocks = int((tokens * 32 + threads - 1) / threads);
+    TraceScope trace(KB200_KERNEL_MOE_ROUTE, static_cast<cudaStream_t>(stream));
     moe_route_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(logits, int(tokens), experts, top_k,
                                                                               chosen, weight, nullptr);
     const cudaError_t e = cudaGetLastError();
@@ -1309,8 +1300,12 @@ int kb200_moe_experts(const kb200_moe_weights* w, const uint16_t* rows_f16, cons
     if (ws.bytes > workspace_bytes)
         return fail(KB200_NO_MEMORY, "expert workspace too small (see kb200_moe_experts_workspace_bytes)");
     auto stream = static_cast<cudaStream_t>(stream_ptr);
-    moe_mtile_kernel<<<1, 32, 0, stream>>>(offsets, w->experts, ws.mtile);
-    const cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    {
+        TraceScope trace(KB200_KERNEL_MOE_MTILE, stream);
+        moe_mtile_kernel<<<1, 32, 0, stream>>>(offsets, w->experts, ws.mtile);
+        e = cudaGetLastError();
+    }
     if (e != cudaSuccess)
         return cuda_fail(e, "moe_mtile_kernel launch");
     return experts_launch(w, reinterpret_cast<const __half*>(rows_f16), offsets, ws.mtile, rows, ws.act, y, status,
@@ -1342,6 +1337,7 @@ int kb200_rows_regroup(const void* src, void* dst, size_t row_bytes, const int64
         return fail(KB200_UNSUPPORTED, "at most 65535 segments");
     const size_t words = std::max<size_t>(1, max_rows) * (row_bytes / 16);
     const dim3 grid(unsigned(std::min<size_t>((words + 255) / 256, 64)), unsigned(count));
+    TraceScope trace(KB200_KERNEL_ROWS_REGROUP, static_cast<cudaStream_t>(stream));
     rows_regroup_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint4*>(src), static_cast<uint4*>(dst), row_bytes / 16,
         reinterpret_cast<const long long*>(segments));

@@ -98,6 +98,7 @@ int kb200_mxfp4_ggml_dequant(const void* blocks, size_t count, float* out, void*
         return fail(KB200_INVALID, "null blocks or output");
     if (overlap(out, count * 32 * sizeof(float), blocks, count * kMxBlock))
         return fail(KB200_ALIAS, "output overlaps the blocks");
+    TraceScope trace(KB200_KERNEL_MXFP4_GGML_DEQUANT, static_cast<cudaStream_t>(stream));
     mxfp4_ggml_dequant_kernel<<<grid_for(count, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint8_t*>(blocks), count, out);
     const cudaError_t e = cudaGetLastError();
@@ -121,6 +122,7 @@ int kb200_mxfp4_from_ggml(const void* blocks, size_t experts, size_t rows, size_
     if (overlap(codes, code_bytes, blocks, total * kMxBlock) || overlap(scales, scale_bytes, blocks, total * kMxBlock)
         || overlap(codes, code_bytes, scales, scale_bytes))
         return fail(KB200_ALIAS, "source and destinations overlap");
+    TraceScope trace(KB200_KERNEL_MXFP4_FROM_GGML, static_cast<cudaStream_t>(stream));
     mxfp4_from_ggml_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint8_t*>(blocks), experts, rows, nblk, static_cast<uint8_t*>(codes),
         static_cast<uint8_t*>(scales), dst_rows, first_row);

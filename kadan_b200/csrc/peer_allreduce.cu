@@ -256,6 +256,7 @@ int launch_peer_allreduce(float* data, size_t count, const PeerOut& g, double ti
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    TraceScope trace(KB200_KERNEL_PEER_ALLREDUCE, stream);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, peer_allreduce_kernel, p);
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "peer_allreduce_kernel launch");
 }
