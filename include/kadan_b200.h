@@ -822,6 +822,77 @@ KB200_API int kb200_shard_load_mxfp4_expert_rows(const kb200_shard* shard, const
                                                  uint64_t scales_capacity, uint64_t* columns);
 
 /* ---------------------------------------------------------------------------
+ * Layer math around the path on the device (device pointers, stream order).
+ * The reference runs it on the host: rms_norm / l2_norm / rope / attend /
+ * delta_rule (IW/src/models/text/gguf_weights.cpp:639-818) from
+ * AttentionLayer::forward and DeltaNetLayer::forward (qwen_layers.cpp:74-330),
+ * unless its DenseCompute takes attend_cached / delta_step
+ * (IW/include/kadan/dense_compute.hpp:275-330). */
+
+/* rms_norm (gguf_weights.cpp:639-666): each row of `width` values times
+ * 1 / sqrt(float(sum of squares in double / width) + eps), then times weight
+ * (NULL: the unweighted form). out may equal x. Bit 0 of *status (when not
+ * NULL) is set if an output is not finite (gguf_text_norm_nonfinite). */
+KB200_API int kb200_rms_norm(const float* x, const float* weight, size_t rows, size_t width, float eps, float* out,
+                             unsigned* status, void* stream);
+/* l2_norm (gguf_weights.cpp:667-674): x / sqrt(sum x^2 + eps) per row. */
+KB200_API int kb200_l2_norm(const float* x, size_t rows, size_t width, float eps, float* out, void* stream);
+/* rope (gguf_weights.cpp:676-700) in place over `rows` rows of row_width
+ * values, each a run of heads of `width` values; row r is at position + r
+ * (AttentionLayer::forward, qwen_layers.cpp:242-256). Pairs (i, i + rotary/2)
+ * of each head turn by (position + r) * base^(-2i/rotary). */
+KB200_API int kb200_rope(float* x, size_t rows, size_t row_width, size_t width, size_t rotary, size_t position,
+                         float base, void* stream);
+
+/* Cached attention (attend_cached, dense_compute.hpp:275-300; the host's
+ * attend, gguf_weights.cpp:700-777): q [rows][heads][dim]; keys and values
+ * [positions][kv_heads][dim] (16-byte aligned) with at least position + rows
+ * positions; row r is at position + r and attends every position up to its
+ * own, or with `selected` the positions selected[offsets[r] ..
+ * offsets[r + 1]) (offsets has rows + 1 entries; at most position + rows per
+ * row, none after the row's own position). out [rows][heads][dim]. The
+ * softmax is over scale * q.k. Supported: head dim 64, 128 or 256, at most 16
+ * query heads per KV head and heads/kv_heads * dim <= 2048
+ * (kb200_attend_supported); otherwise KB200_UNSUPPORTED before any work. */
+KB200_API int kb200_attend_supported(size_t heads, size_t kv_heads, size_t dim);
+KB200_API size_t kb200_attend_workspace_bytes(size_t rows, size_t position, size_t heads, size_t dim);
+KB200_API int kb200_attend_cached(const float* q, const float* keys, const float* values, size_t rows,
+                                  size_t position, size_t heads, size_t kv_heads, size_t dim, float scale,
+                                  const uint32_t* selected, const uint32_t* offsets, float* out, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* One gated delta-net step over `rows` rows in order (delta_step,
+ * dense_compute.hpp:302-330; the host's DeltaNetLayer::forward,
+ * qwen_layers.cpp:131-180): causal depthwise convolution with SiLU over qkv
+ * (channels = (2 key_heads + value_heads) dim: q, k, v), L2-normalised q and
+ * k heads, then per value head the decayed delta rule (delta_rule,
+ * gguf_weights.cpp:778-818) with decay exp(softplus(alpha + dt) a) and
+ * sigmoid(beta), RMSNorm by `norm` and the sigmoid (sigmoid_gate) or SiLU
+ * gate of z. history [(kernel - 1)][channels] (oldest first) and state
+ * [value_heads][dim][dim] are read and updated. */
+typedef struct kb200_delta_args {
+    const float* qkv;    /* [rows][channels] */
+    const float* z;      /* [rows][value_heads * dim] */
+    const float* alpha;  /* [rows][value_heads] */
+    const float* beta;   /* [rows][value_heads] */
+    const float* conv;   /* [channels][kernel] */
+    const float* dt;     /* [value_heads] */
+    const float* a;      /* [value_heads] */
+    const float* norm;   /* [dim] */
+    float* history;      /* [(kernel - 1)][channels], updated */
+    float* state;        /* [value_heads][dim][dim], updated */
+    float* output;       /* [rows][value_heads * dim] */
+    uint32_t rows, key_heads, value_heads, dim, kernel;
+    float eps;
+    int32_t sigmoid_gate;
+} kb200_delta_args;
+/* dim a multiple of 32 up to 256, value_heads a multiple of key_heads,
+ * kernel 1..64. */
+KB200_API int kb200_delta_supported(uint32_t key_heads, uint32_t value_heads, uint32_t dim, uint32_t kernel);
+KB200_API size_t kb200_delta_workspace_bytes(const kb200_delta_args* args);
+KB200_API int kb200_delta_step(const kb200_delta_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Per-kernel telemetry (the reference's CudaPhaseScope / cuda_trace::kernel,
  * IW/include/kadan/cuda_phase_metrics.hpp:9-87, IW/src/cuda/cuda_telemetry.cuh:
  * 101-160). A phase collects, for every launch the library issues on a
@@ -855,7 +926,14 @@ typedef enum kb200_kernel {
     KB200_KERNEL_MXFP4_FROM_GGML = 17,
     KB200_KERNEL_PEER_ALLREDUCE = 18,   /* peer all-reduce / row-parallel gather */
     KB200_KERNEL_EP_EXCHANGE = 19,      /* expert-parallel peer exchange */
-    KB200_KERNEL_COUNT = 20
+    KB200_KERNEL_RMS_NORM = 20,         /* rms_norm_kernel (RMSNorm and L2 norm) */
+    KB200_KERNEL_ROPE = 21,
+    KB200_KERNEL_ATTEND = 22,           /* attend_kernel (cached attention, per segment) */
+    KB200_KERNEL_ATTEND_COMBINE = 23,
+    KB200_KERNEL_DELTA_CONV = 24,
+    KB200_KERNEL_DELTA_L2 = 25,
+    KB200_KERNEL_DELTA_HEADS = 26,
+    KB200_KERNEL_COUNT = 27
 } kb200_kernel;
 
 typedef struct kb200_kernel_metrics {

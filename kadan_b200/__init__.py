@@ -94,7 +94,7 @@ class ContextCounters(ctypes.Structure):
                 ("gemm_fallbacks", ctypes.c_uint64)]
 
 
-KERNEL_COUNT = 20
+KERNEL_COUNT = 27
 
 
 class KernelMetrics(ctypes.Structure):
@@ -109,6 +109,15 @@ class PhaseMetrics(ctypes.Structure):
 
     _fields_ = [("kernels", KernelMetrics * KERNEL_COUNT), ("dropped", ctypes.c_uint64),
                 ("unavailable", ctypes.c_uint64), ("shared_batch_size", ctypes.c_uint64), ("observed", ctypes.c_int32)]
+
+
+class DeltaArgs(ctypes.Structure):
+    """kb200_delta_args (device pointers)."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n in ("qkv", "z", "alpha", "beta", "conv", "dt", "a", "norm", "history",
+                                               "state", "output")] + \
+               [(n, ctypes.c_uint32) for n in ("rows", "key_heads", "value_heads", "dim", "kernel")] + \
+               [("eps", ctypes.c_float), ("sigmoid_gate", ctypes.c_int32)]
 
 
 RESULT_UNSUPPORTED, RESULT_UNVALIDATED, RESULT_FINITE = 0, 1, 2
@@ -167,6 +176,18 @@ def _load() -> ctypes.CDLL:
     lib.kb200_gguf_gemm_range_offset.restype = c_size
     lib.kb200_gguf_gemm_range_offset.argtypes = [ctypes.c_uint32, ctypes.c_uint32]
     lib.kb200_context_counters_get.argtypes = [vp, ctypes.POINTER(ContextCounters)]
+    lib.kb200_rms_norm.argtypes = [vp, vp, c_size, c_size, ctypes.c_float, vp, vp, vp]
+    lib.kb200_l2_norm.argtypes = [vp, c_size, c_size, ctypes.c_float, vp, vp]
+    lib.kb200_rope.argtypes = [vp, c_size, c_size, c_size, c_size, c_size, ctypes.c_float, vp]
+    lib.kb200_attend_supported.argtypes = [c_size, c_size, c_size]
+    lib.kb200_attend_workspace_bytes.restype = c_size
+    lib.kb200_attend_workspace_bytes.argtypes = [c_size, c_size, c_size, c_size]
+    lib.kb200_attend_cached.argtypes = [vp, vp, vp, c_size, c_size, c_size, c_size, c_size, ctypes.c_float, vp, vp,
+                                        vp, vp, c_size, vp]
+    lib.kb200_delta_supported.argtypes = [ctypes.c_uint32] * 4
+    lib.kb200_delta_workspace_bytes.restype = c_size
+    lib.kb200_delta_workspace_bytes.argtypes = [ctypes.POINTER(DeltaArgs)]
+    lib.kb200_delta_step.argtypes = [ctypes.POINTER(DeltaArgs), vp, c_size, vp]
     lib.kb200_phase_create.argtypes = [ctypes.c_uint64, ctypes.POINTER(vp)]
     lib.kb200_phase_enter.argtypes = [vp, ctypes.POINTER(vp)]
     lib.kb200_phase_snapshot.argtypes = [vp, ctypes.POINTER(PhaseMetrics)]
@@ -518,6 +539,57 @@ lib.kb200_moe_forward_f32.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_void_
 lib.kb200_moe_forward_host.argtypes = [ctypes.c_void_p, ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(ctypes.c_ubyte),
                                        ctypes.POINTER(ctypes.c_int)]
+
+
+def rms_norm(x, weight, *, width: int, eps: float, out=None, status=None, stream=None):
+    """kb200_rms_norm over rows of `width` (weight None: unweighted); out may be x."""
+    import torch
+
+    out = torch.empty_like(x) if out is None else out
+    check(lib.kb200_rms_norm(x.data_ptr(), _ptr(weight), x.numel() // width, width, eps, out.data_ptr(),
+                             _ptr(status), _stream_ptr(stream)))
+    return out
+
+
+def l2_norm(x, *, width: int, eps: float, out=None, stream=None):
+    import torch
+
+    out = torch.empty_like(x) if out is None else out
+    check(lib.kb200_l2_norm(x.data_ptr(), x.numel() // width, width, eps, out.data_ptr(), _stream_ptr(stream)))
+    return out
+
+
+def rope(x, *, rows: int, width: int, rotary: int, position: int, base: float, stream=None):
+    """kb200_rope in place on x ([rows][heads * width])."""
+    check(lib.kb200_rope(x.data_ptr(), rows, x.numel() // rows, width, rotary, position, base, _stream_ptr(stream)))
+    return x
+
+
+def attend_cached(q, keys, values, *, rows: int, position: int, heads: int, kv_heads: int, dim: int, scale: float,
+                  selected=None, offsets=None, out=None, stream=None):
+    """kb200_attend_cached on device tensors; returns out [rows, heads, dim]."""
+    import torch
+
+    out = torch.empty(rows, heads, dim, device=q.device) if out is None else out
+    ws = torch.empty(max(1, lib.kb200_attend_workspace_bytes(rows, position, heads, dim)), dtype=torch.uint8,
+                     device=q.device)
+    check(lib.kb200_attend_cached(q.data_ptr(), keys.data_ptr(), values.data_ptr(), rows, position, heads, kv_heads,
+                                  dim, scale, _ptr(selected), _ptr(offsets), out.data_ptr(), ws.data_ptr(),
+                                  ws.numel(), _stream_ptr(stream)))
+    return out
+
+
+def delta_step(*, qkv, z, alpha, beta, conv, dt, a, norm, history, state, output, rows: int, key_heads: int,
+               value_heads: int, dim: int, kernel: int, eps: float, sigmoid_gate: bool, stream=None) -> None:
+    """kb200_delta_step on device tensors (history and state updated in place)."""
+    import torch
+
+    args = DeltaArgs(qkv.data_ptr(), z.data_ptr(), alpha.data_ptr(), beta.data_ptr(), conv.data_ptr(), dt.data_ptr(),
+                     a.data_ptr(), norm.data_ptr(), _ptr(history), state.data_ptr(), output.data_ptr(), rows,
+                     key_heads, value_heads, dim, kernel, eps, int(bool(sigmoid_gate)))
+    ws = torch.empty(max(1, lib.kb200_delta_workspace_bytes(ctypes.byref(args))), dtype=torch.uint8,
+                     device=qkv.device)
+    check(lib.kb200_delta_step(ctypes.byref(args), ws.data_ptr(), ws.numel(), _stream_ptr(stream)))
 
 
 def kernel_name(kernel: int):

@@ -109,6 +109,21 @@ int orc_moe_forward(
 
 float orc_bf16_round(float v);
 
+/* Layer math around the path (layer.c): the reference worker's host RMSNorm,
+ * L2 norm, RoPE, cached attention and gated delta-net step. */
+int orc_rms_norm(float* x, const float* weight, size_t rows, size_t width, float eps);
+void orc_l2_norm(float* x, size_t rows, size_t width, float eps);
+void orc_rope(float* x, size_t rows, size_t row_width, size_t width, size_t rotary, size_t position, float base);
+int orc_attend_cached(const float* q, const float* keys, const float* values, size_t rows, size_t position,
+                      size_t heads, size_t kv_heads, size_t dim, float scale, const uint32_t* selected,
+                      const uint32_t* offsets, float* out);
+void orc_delta_rule(float* state, const float* q, const float* k, const float* v, const float* decay, size_t decays,
+                    float beta, size_t dim, float* out);
+int orc_delta_step(const float* qkv, const float* z, const float* alpha, const float* beta, const float* conv,
+                   const float* dt, const float* a, const float* norm, size_t rows, size_t key_heads,
+                   size_t value_heads, size_t dim, size_t kernel, float eps, int sigmoid_gate, float* history,
+                   float* state, float* out);
+
 #ifdef __cplusplus
 }
 #endif

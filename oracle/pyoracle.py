@@ -70,6 +70,17 @@ class Oracle:
         L.orc_bf16_round.restype = ctypes.c_float
         L.orc_bf16_round.argtypes = [ctypes.c_float]
         L.orc_set_iq_grids.argtypes = [ctypes.c_void_p] * 3
+        sz, f32 = ctypes.c_size_t, ctypes.c_float
+        L.orc_rms_norm.argtypes = [_f32p, _f32p, sz, sz, f32]
+        L.orc_l2_norm.restype = None
+        L.orc_l2_norm.argtypes = [_f32p, sz, sz, f32]
+        L.orc_rope.restype = None
+        L.orc_rope.argtypes = [_f32p, sz, sz, sz, sz, sz, f32]
+        _u32p = ctypes.POINTER(ctypes.c_uint32)
+        L.orc_attend_cached.argtypes = [_f32p, _f32p, _f32p, sz, sz, sz, sz, sz, f32, _u32p, _u32p, _f32p]
+        L.orc_delta_rule.restype = None
+        L.orc_delta_rule.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, sz, f32, sz, _f32p]
+        L.orc_delta_step.argtypes = [_f32p] * 8 + [sz] * 5 + [f32, ctypes.c_int, _f32p, _f32p, _f32p]
         self.L = L
 
     def set_iq_grids(self, grids) -> None:
@@ -146,6 +157,64 @@ class Oracle:
             activation, interleaved, limit, alpha, round_act, _p(out, _f32p))
         if rc:
             raise ValueError(f"orc_moe_forward failed: {rc}")
+        return out
+
+    # ----------------------------------------------------------- layer math
+    @staticmethod
+    def _f(a) -> np.ndarray:
+        return np.ascontiguousarray(a, dtype=np.float32)
+
+    def rms_norm(self, x, weight=None, *, width: int, eps: float) -> np.ndarray:
+        y = self._f(x).copy()
+        w = None if weight is None else self._f(weight)
+        rc = self.L.orc_rms_norm(_p(y, _f32p), None if w is None else _p(w, _f32p), y.size // width, width, eps)
+        if rc:
+            raise ValueError("gguf_text_norm_nonfinite")
+        return y
+
+    def l2_norm(self, x, *, width: int, eps: float) -> np.ndarray:
+        y = self._f(x).copy()
+        self.L.orc_l2_norm(_p(y, _f32p), y.size // width, width, eps)
+        return y
+
+    def rope(self, x, *, rows: int, width: int, rotary: int, position: int, base: float) -> np.ndarray:
+        y = self._f(x).copy()
+        self.L.orc_rope(_p(y, _f32p), rows, y.size // rows, width, rotary, position, base)
+        return y
+
+    def attend_cached(self, q, keys, values, *, rows, position, heads, kv_heads, dim, scale, selected=None,
+                      offsets=None) -> np.ndarray:
+        q, k, v = self._f(q), self._f(keys), self._f(values)
+        out = np.empty(rows * heads * dim, dtype=np.float32)
+        u32 = ctypes.POINTER(ctypes.c_uint32)
+        sel = None if selected is None else np.ascontiguousarray(selected, dtype=np.uint32)
+        off = None if offsets is None else np.ascontiguousarray(offsets, dtype=np.uint32)
+        rc = self.L.orc_attend_cached(_p(q, _f32p), _p(k, _f32p), _p(v, _f32p), rows, position, heads, kv_heads,
+                                      dim, scale, None if sel is None else _p(sel, u32),
+                                      None if off is None else _p(off, u32), _p(out, _f32p))
+        if rc:
+            raise ValueError("gguf_text_attention_shape")
+        return out.reshape(rows, heads, dim)
+
+    def delta_rule(self, state, q, k, v, decay, beta: float) -> np.ndarray:
+        """One delta_rule step; `state` (float32, dim*dim) is updated in place."""
+        dim = len(q)
+        out = np.empty(dim, dtype=np.float32)
+        d = self._f(decay)
+        qs, ks, vs = self._f(q), self._f(k), self._f(v)
+        self.L.orc_delta_rule(_p(state, _f32p), _p(qs, _f32p), _p(ks, _f32p), _p(vs, _f32p), _p(d, _f32p), d.size,
+                              beta, dim, _p(out, _f32p))
+        return out
+
+    def delta_step(self, qkv, z, alpha, beta, conv, dt, a, norm, *, rows, key_heads, value_heads, dim, kernel, eps,
+                   sigmoid_gate, history, state) -> np.ndarray:
+        """`history` and `state` (float32 arrays) are updated in place."""
+        ins = [self._f(t) for t in (qkv, z, alpha, beta, conv, dt, a, norm)]
+        out = np.empty(rows * value_heads * dim, dtype=np.float32)
+        rc = self.L.orc_delta_step(*[_p(t, _f32p) for t in ins], rows, key_heads, value_heads, dim, kernel, eps,
+                                   int(bool(sigmoid_gate)), _p(history, _f32p), _p(state, _f32p), _p(out, _f32p))
+        if rc:
+            raise ValueError("gguf_text_delta_shape")
         return out
 
 

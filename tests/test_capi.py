@@ -244,3 +244,34 @@ def test_gemm_supported_predicate(kb):
     assert not kb.gemm_supported(job(kb.Q4_K, 4096, 2288))  # rows shorter than K
     for enc in (kb.Q3_K, kb.IQ4_NL, kb.IQ4_XS, kb.BF16, kb.F32):
         assert not kb.gemm_supported(job(enc, 4096, 8192))
+
+
+def test_layer_math_host_checks(kb):
+    """Shape rules of the layer-math entries are checked before any launch."""
+    L = kb.lib
+    fake = ctypes.c_void_p(0x10000000)
+    # gguf_text_rope_shape: odd rotary, rotary above the head width, ragged rows.
+    assert L.kb200_rope(fake, 1, 128, 128, 127, 0, 10000.0, None) == kb.INVALID
+    assert L.kb200_rope(fake, 1, 128, 64, 128, 0, 10000.0, None) == kb.INVALID
+    assert L.kb200_rope(fake, 1, 100, 64, 64, 0, 10000.0, None) == kb.INVALID
+    # Attention: head dims 64/128/256, at most 16 query heads per KV head.
+    assert L.kb200_attend_supported(64, 8, 128) == 1
+    assert L.kb200_attend_supported(64, 8, 96) == 0
+    assert L.kb200_attend_supported(64, 2, 128) == 0
+    assert L.kb200_attend_supported(16, 1, 256) == 0
+    assert L.kb200_attend_supported(6, 4, 128) == 0
+    assert L.kb200_attend_cached(fake, fake, fake, 1, 0, 64, 2, 128, 1.0, None, None, fake, fake, 1 << 20,
+                                 None) == kb.UNSUPPORTED
+    need = L.kb200_attend_workspace_bytes(2, 300, 8, 64)
+    assert need == 2 * 8 * 2 * 66 * 4
+    assert L.kb200_attend_cached(fake, fake, fake, 2, 300, 8, 2, 64, 1.0, None, None, ctypes.c_void_p(0x20000000),
+                                 fake, need - 1, None) == kb.NO_MEMORY
+    # Delta net: dim a multiple of 32 up to 256, value heads a multiple of key heads.
+    assert L.kb200_delta_supported(16, 32, 128, 4) == 1
+    assert L.kb200_delta_supported(16, 24, 128, 4) == 0
+    assert L.kb200_delta_supported(2, 4, 96 + 8, 4) == 0
+    assert L.kb200_delta_supported(2, 4, 512, 4) == 0
+    args = kb.DeltaArgs(rows=1, key_heads=3, value_heads=4, dim=128, kernel=4)
+    assert L.kb200_delta_step(ctypes.byref(args), fake, 1 << 20, None) == kb.UNSUPPORTED
+    args = kb.DeltaArgs(rows=2, key_heads=2, value_heads=4, dim=64, kernel=4)
+    assert L.kb200_delta_workspace_bytes(ctypes.byref(args)) == ((2 + 3) * (2 * 2 + 4) * 64 * 4 + 255) // 256 * 256

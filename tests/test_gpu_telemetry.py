@@ -63,13 +63,13 @@ def test_graph_capture_counts_without_timing(kb, cuda):
     job = kb.gemv_job(kb.Q4_K, w, x, y, in_=in_, columns=out, rows=1)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
-        kb.gguf_gemv_batch([job], stream=s.cuda_stream)  # first use outside capture sets the stream up
+        kb.gguf_gemv_batch([job], stream=s)  # first use outside capture sets the stream up
         s.synchronize()
         g = torch.cuda.CUDAGraph()
         with kb.Phase() as ph:
-            kb.gguf_gemv_batch([job], stream=s.cuda_stream)  # eager: counted and timed
+            kb.gguf_gemv_batch([job], stream=s)  # eager: counted and timed
             with torch.cuda.graph(g, stream=s):
-                kb.gguf_gemv_batch([job], stream=s.cuda_stream)  # captured: counted only
+                kb.gguf_gemv_batch([job], stream=s)  # captured: counted only
             g.replay()
             s.synchronize()
             snap = ph.snapshot()
