@@ -892,6 +892,58 @@ KB200_API int kb200_delta_supported(uint32_t key_heads, uint32_t value_heads, ui
 KB200_API size_t kb200_delta_workspace_bytes(const kb200_delta_args* args);
 KB200_API int kb200_delta_step(const kb200_delta_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Host-span forms on a context (synchronous; calls on one context must not
+ * overlap). The context keeps per-layer device state, keyed by the caller's
+ * `layer` id, until kb200_context_release_layers (the reference's
+ * release_scratch) or kb200_context_destroy.
+ *
+ * attend_cached (dense_compute.hpp:275-300): keys / values hold at least
+ * position + rows positions of [kv_heads][dim]. The context mirrors the
+ * layer's KV cache: positions mirrored by earlier calls below `position` are
+ * reused, positions from min(mirrored, position) to position + rows are
+ * uploaded. selected / offsets (host, may be NULL) as for kb200_attend_cached;
+ * a selected position after its row's own fails with KB200_INVALID.
+ * KB200_UNSUPPORTED (nothing read or written) when kb200_attend_supported
+ * rejects the shape: the caller's own attention then runs. */
+KB200_API int kb200_attend_cached_host(kb200_context* ctx, uint64_t layer, const float* q, const float* keys,
+                                       const float* values, size_t rows, size_t position, size_t heads,
+                                       size_t kv_heads, size_t dim, float scale, const uint32_t* selected,
+                                       const uint32_t* offsets, float* output, const volatile uint8_t* cancel);
+
+/* delta_step (dense_compute.hpp:302-330, its DeltaStep fields): host spans of
+ * the step's inputs; the layer's recurrent state and convolution history stay
+ * on the device. `fresh` starts them at zero, or at initial_state
+ * ([value_heads][dim][dim]) / initial_history ([(kernel - 1)][channels]) when
+ * those are not NULL. A fresh step with an unsupported shape returns
+ * KB200_UNSUPPORTED before any output write; a later step of a layer without
+ * device state fails with KB200_INVALID ("recurrent_state_lost"). */
+typedef struct kb200_delta_host {
+    uint64_t layer;
+    int32_t fresh;
+    const float* qkv;    /* [rows][channels] */
+    const float* z;      /* [rows][value_heads * dim] */
+    const float* alpha;  /* [rows][value_heads] */
+    const float* beta;   /* [rows][value_heads] */
+    const float* conv;   /* [channels][kernel] */
+    const float* dt;     /* [value_heads] */
+    const float* a;      /* [value_heads] */
+    const float* norm;   /* [dim] */
+    uint32_t rows, key_heads, value_heads, dim, kernel;
+    float eps;
+    int32_t sigmoid_gate;
+    float* output;                /* [rows][value_heads * dim] */
+    const float* initial_state;   /* NULL or [value_heads][dim][dim] */
+    const float* initial_history; /* NULL or [(kernel - 1)][channels] */
+} kb200_delta_host;
+KB200_API int kb200_delta_step_host(kb200_context* ctx, const kb200_delta_host* step,
+                                    const volatile uint8_t* cancel);
+/* copy_recurrent_state (dense_compute.hpp:323-326): the layer's device state
+ * and history into host arrays of exactly state_floats / history_floats. */
+KB200_API int kb200_recurrent_state_get(kb200_context* ctx, uint64_t layer, float* state, size_t state_floats,
+                                        float* history, size_t history_floats);
+/* Frees every layer's KV mirror and recurrent state (release_scratch). */
+KB200_API int kb200_context_release_layers(kb200_context* ctx);
+
 /* ---------------------------------------------------------------------------
  * Per-kernel telemetry (the reference's CudaPhaseScope / cuda_trace::kernel,
  * IW/include/kadan/cuda_phase_metrics.hpp:9-87, IW/src/cuda/cuda_telemetry.cuh:

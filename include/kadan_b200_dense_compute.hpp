@@ -4,9 +4,11 @@
 // kadan/dense_compute.hpp, services/hikari/inference_worker/include/kadan/
 // dense_compute.hpp:60-342) and is not part of libkadan_b200.so. It overrides
 // the quantized-weight hot path — dense_gguf_batch and dense_gguf_source —
-// and forwards every other virtual to the compute it wraps (the worker's own
-// CUDA compute), so it can take that object's place; release_weights and
-// weight_placement also cover the B200 weight bank. Status codes map onto the
+// and the layer math around it — attend_cached, delta_step and
+// copy_recurrent_state, over per-layer state that release_scratch(false)
+// frees — and forwards every other virtual to the compute it wraps (the
+// worker's own CUDA compute), so it can take that object's place;
+// release_weights and weight_placement also cover the B200 weight bank. Status codes map onto the
 // reference's conventions: KB200_UNSUPPORTED -> ProjectionResult::unsupported
 // (nothing read or written), KB200_OK -> the call's result, any other status
 // -> std::runtime_error: the reference's own message where the status stands
@@ -20,6 +22,7 @@
 #include <exception>
 #include <memory>
 #include <mutex>
+#include <set>
 #include <span>
 #include <stdexcept>
 #include <string>
@@ -189,10 +192,111 @@ public:
         fallback_->release_devices();
     }
 
-    // -- everything else is the wrapped compute's.
+    // Request boundary: without `keep` the per-layer KV mirrors and recurrent
+    // states this adapter holds are released with the wrapped compute's.
     Footprint release_scratch(bool keep) override {
+        if (!keep) {
+            std::lock_guard lock(mutex_);
+            for (const auto& d : devices_)
+                check(kb200_context_release_layers(d.ctx));
+            delta_layers_.clear();
+        }
         return fallback_->release_scratch(keep);
     }
+
+    // Cached attention on the first device (kb200_attend_cached_host); shapes
+    // it does not take go to the wrapped compute before anything is read.
+    bool attend_cached(std::uint64_t layer, std::span<const float> q, std::span<const float> keys,
+                       std::span<const float> values, std::size_t rows, std::size_t position, std::size_t heads,
+                       std::size_t kv_heads, std::size_t dim, float scale, std::span<float> output,
+                       const std::atomic_bool& cancel, std::span<const std::uint32_t> selected,
+                       std::span<const std::uint32_t> offsets) override {
+        const std::size_t kv = (position + rows) * kv_heads * dim;
+        const bool shaped = rows && q.size() == rows * heads * dim && output.size() == q.size() && keys.size() >= kv
+                            && values.size() >= kv && (selected.empty() || offsets.size() == rows + 1)
+                            && kb200_attend_supported(heads, kv_heads, dim);
+        if (!shaped)
+            return fallback_->attend_cached(layer, q, keys, values, rows, position, heads, kv_heads, dim, scale,
+                                            output, cancel, selected, offsets);
+        if (cancel.load())
+            throw std::runtime_error(kb200_status_name(KB200_CANCELLED));
+        std::lock_guard lock(mutex_);
+        const int status = kb200_attend_cached_host(devices_.front().ctx, layer, q.data(), keys.data(), values.data(),
+                                                    rows, position, heads, kv_heads, dim, scale,
+                                                    selected.empty() ? nullptr : selected.data(),
+                                                    selected.empty() ? nullptr : offsets.data(), output.data(),
+                                                    cancel_byte(cancel));
+        if (status == KB200_UNSUPPORTED)
+            return false;
+        check(status);
+        return true;
+    }
+
+    // Delta-net steps on the first device (kb200_delta_step_host) for the
+    // layers whose fresh step it took; other layers stay with the wrapped
+    // compute, so a layer's state never moves between the two.
+    bool delta_step(const DeltaStep& step, const std::atomic_bool& cancel) override {
+        const std::size_t channels = (2 * step.key_heads + step.value_heads) * step.dim;
+        const std::size_t inner = step.value_heads * step.dim, rows = step.rows;
+        std::unique_lock lock(mutex_);
+        const bool ours = delta_layers_.count(step.layer) != 0;
+        if (!step.fresh && !ours) {
+            lock.unlock();
+            return fallback_->delta_step(step, cancel);
+        }
+        const bool shaped = rows && step.qkv.size() == rows * channels && step.z.size() == rows * inner
+                            && step.alpha.size() == rows * step.value_heads
+                            && step.beta.size() == rows * step.value_heads
+                            && step.conv.size() == channels * step.kernel && step.dt.size() == step.value_heads
+                            && step.a.size() == step.value_heads && step.norm.size() == step.dim
+                            && step.output.size() == rows * inner
+                            && (step.initial_state.empty()
+                                || step.initial_state.size() == step.value_heads * step.dim * step.dim)
+                            && (step.initial_history.empty()
+                                || step.initial_history.size() == (step.kernel - 1) * channels)
+                            && kb200_delta_supported(std::uint32_t(step.key_heads), std::uint32_t(step.value_heads),
+                                                     std::uint32_t(step.dim), std::uint32_t(step.kernel));
+        if (step.fresh && !shaped) {
+            delta_layers_.erase(step.layer);
+            lock.unlock();
+            return fallback_->delta_step(step, cancel);
+        }
+        if (!shaped)
+            throw std::runtime_error("gguf_text_recurrent_device_lost");
+        if (cancel.load())
+            throw std::runtime_error(kb200_status_name(KB200_CANCELLED));
+        const kb200_delta_host host{step.layer, step.fresh ? 1 : 0, step.qkv.data(), step.z.data(),
+                                    step.alpha.data(), step.beta.data(), step.conv.data(), step.dt.data(),
+                                    step.a.data(), step.norm.data(), std::uint32_t(rows),
+                                    std::uint32_t(step.key_heads), std::uint32_t(step.value_heads),
+                                    std::uint32_t(step.dim), std::uint32_t(step.kernel), step.eps,
+                                    step.sigmoid_gate ? 1 : 0, step.output.data(),
+                                    step.initial_state.empty() ? nullptr : step.initial_state.data(),
+                                    step.initial_history.empty() ? nullptr : step.initial_history.data()};
+        const int status = kb200_delta_step_host(devices_.front().ctx, &host, cancel_byte(cancel));
+        if (status == KB200_UNSUPPORTED && step.fresh) {
+            delta_layers_.erase(step.layer);
+            lock.unlock();
+            return fallback_->delta_step(step, cancel);
+        }
+        check(status);
+        delta_layers_.insert(step.layer);
+        return true;
+    }
+
+    void copy_recurrent_state(std::uint64_t layer, std::span<float> state, std::span<float> history) override {
+        {
+            std::lock_guard lock(mutex_);
+            if (delta_layers_.count(layer)) {
+                check(kb200_recurrent_state_get(devices_.front().ctx, layer, state.data(), state.size(),
+                                                history.data(), history.size()));
+                return;
+            }
+        }
+        fallback_->copy_recurrent_state(layer, state, history);
+    }
+
+    // -- everything else is the wrapped compute's.
     Footprint retained_weights() const override {
         return fallback_->retained_weights();
     }
@@ -247,20 +351,6 @@ public:
                 const std::atomic_bool& cancel) override {
         return fallback_->attend(q, k, v, queries, keys, heads, kv_heads, dim, causal_queries, window, offset, y,
                                  cancel);
-    }
-    bool attend_cached(std::uint64_t layer, std::span<const float> q, std::span<const float> keys,
-                       std::span<const float> values, std::size_t rows, std::size_t position, std::size_t heads,
-                       std::size_t kv_heads, std::size_t dim, float scale, std::span<float> output,
-                       const std::atomic_bool& cancel, std::span<const std::uint32_t> selected,
-                       std::span<const std::uint32_t> offsets) override {
-        return fallback_->attend_cached(layer, q, keys, values, rows, position, heads, kv_heads, dim, scale, output,
-                                        cancel, selected, offsets);
-    }
-    void copy_recurrent_state(std::uint64_t layer, std::span<float> state, std::span<float> history) override {
-        fallback_->copy_recurrent_state(layer, state, history);
-    }
-    bool delta_step(const DeltaStep& step, const std::atomic_bool& cancel) override {
-        return fallback_->delta_step(step, cancel);
     }
 
 private:
@@ -459,6 +549,7 @@ private:
     std::shared_ptr<DenseCompute> fallback_;
     std::uint64_t scratch_;
     std::vector<Device> devices_;
+    std::set<std::uint64_t> delta_layers_;  // layers whose recurrent state this adapter holds
     mutable std::mutex mutex_;  // the reference serialises DenseCompute calls (h3_compute.cu:1639)
 };
 

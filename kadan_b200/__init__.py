@@ -668,3 +668,76 @@ def moe_forward_host(ctx: "Context", w: MoeWeights, x, logits, out=None, cancel=
 lib.kb200_moe_forward_noalloc.argtypes = [ctypes.POINTER(MoeWeights), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
 STATIC_MOE_SCRATCH_BYTES = 16 << 20
+
+
+class DeltaHost(ctypes.Structure):
+    """kb200_delta_host (host pointers)."""
+
+    _fields_ = [("layer", ctypes.c_uint64), ("fresh", ctypes.c_int32)] + \
+               [(n, ctypes.c_void_p) for n in ("qkv", "z", "alpha", "beta", "conv", "dt", "a", "norm")] + \
+               [(n, ctypes.c_uint32) for n in ("rows", "key_heads", "value_heads", "dim", "kernel")] + \
+               [("eps", ctypes.c_float), ("sigmoid_gate", ctypes.c_int32), ("output", ctypes.c_void_p),
+                ("initial_state", ctypes.c_void_p), ("initial_history", ctypes.c_void_p)]
+
+
+_vp = ctypes.c_void_p
+lib.kb200_attend_cached_host.argtypes = [_vp, ctypes.c_uint64, _vp, _vp, _vp] + [ctypes.c_size_t] * 5 + \
+    [ctypes.c_float, _vp, _vp, _vp, _vp]
+lib.kb200_delta_step_host.argtypes = [_vp, ctypes.POINTER(DeltaHost), _vp]
+lib.kb200_recurrent_state_get.argtypes = [_vp, ctypes.c_uint64, _vp, ctypes.c_size_t, _vp, ctypes.c_size_t]
+lib.kb200_context_release_layers.argtypes = [_vp]
+
+
+def _f32(a):
+    import numpy as np
+
+    return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+def attend_cached_host(ctx: "Context", layer: int, q, keys, values, *, rows: int, position: int, heads: int,
+                       kv_heads: int, dim: int, scale: float, selected=None, offsets=None, cancel=None):
+    """kb200_attend_cached_host on host arrays; returns out [rows, heads, dim]."""
+    import numpy as np
+
+    q, keys, values = _f32(q), _f32(keys), _f32(values)
+    out = np.empty((rows, heads, dim), dtype=np.float32)
+    sel = None if selected is None else np.ascontiguousarray(selected, dtype=np.uint32)
+    off = None if offsets is None else np.ascontiguousarray(offsets, dtype=np.uint32)
+    check(lib.kb200_attend_cached_host(ctx.handle, layer, q.ctypes.data, keys.ctypes.data, values.ctypes.data, rows,
+                                       position, heads, kv_heads, dim, scale,
+                                       None if sel is None else sel.ctypes.data,
+                                       None if off is None else off.ctypes.data, out.ctypes.data,
+                                       None if cancel is None else ctypes.byref(cancel)))
+    return out
+
+
+def delta_step_host(ctx: "Context", layer: int, *, fresh: bool, qkv, z, alpha, beta, conv, dt, a, norm, rows: int,
+                    key_heads: int, value_heads: int, dim: int, kernel: int, eps: float, sigmoid_gate: bool,
+                    initial_state=None, initial_history=None, cancel=None):
+    """kb200_delta_step_host on host arrays; returns the output [rows, value_heads * dim]."""
+    import numpy as np
+
+    keep = [_f32(t) for t in (qkv, z, alpha, beta, conv, dt, a, norm)]
+    init = [_f32(initial_state), _f32(initial_history)]
+    out = np.empty((rows, value_heads * dim), dtype=np.float32)
+    st = DeltaHost(layer, int(bool(fresh)), *[t.ctypes.data for t in keep], rows, key_heads, value_heads, dim,
+                   kernel, eps, int(bool(sigmoid_gate)), out.ctypes.data,
+                   *[None if t is None else t.ctypes.data for t in init])
+    check(lib.kb200_delta_step_host(ctx.handle, ctypes.byref(st), None if cancel is None else ctypes.byref(cancel)))
+    return out
+
+
+def recurrent_state_get(ctx: "Context", layer: int, state_floats: int, history_floats: int):
+    """kb200_recurrent_state_get: (state, history) of the layer as host arrays."""
+    import numpy as np
+
+    state = np.empty(state_floats, dtype=np.float32)
+    history = np.empty(max(history_floats, 1), dtype=np.float32)
+    check(lib.kb200_recurrent_state_get(ctx.handle, layer, state.ctypes.data, state_floats, history.ctypes.data,
+                                        history_floats))
+    return state, history[:history_floats]
+
+
+def release_layers(ctx: "Context") -> None:
+    """kb200_context_release_layers."""
+    check(lib.kb200_context_release_layers(ctx.handle))

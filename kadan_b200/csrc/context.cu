@@ -14,27 +14,14 @@
 #include <new>
 #include <vector>
 
+#include "context.hpp"
 #include "gguf_formats.cuh"
 #include "kb200_host.hpp"
 #include "read_team.hpp"
 
-struct kb200_context {
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    void* workspace = nullptr;
-    size_t workspace_bytes = 0;
-    void* pinned = nullptr;
-    size_t pinned_bytes = 0;
-    cudaEvent_t staged[2] = {nullptr, nullptr};  // source batch: staging half done
-    int read_lanes = 4;                           // source reads: 3 workers + the caller
-    kb200::ReadTeam* team = nullptr;              // created by the first source batch
-    kb200_context_counters counters = {};         // launches of every call, cumulative
-};
-
 namespace kb200 {
-namespace {
 
-int ensure(kb200_context* c, size_t device_bytes, size_t host_bytes) {
+int context_ensure(kb200_context* c, size_t device_bytes, size_t host_bytes) {
     if (device_bytes > c->workspace_bytes) {
         if (c->workspace)
             cudaFree(c->workspace);
@@ -58,8 +45,10 @@ int ensure(kb200_context* c, size_t device_bytes, size_t host_bytes) {
     return KB200_OK;
 }
 
-bool cancelled(const volatile uint8_t* cancel) {
-    return cancel && *cancel;
+namespace {
+
+int ensure(kb200_context* c, size_t device_bytes, size_t host_bytes) {
+    return context_ensure(c, device_bytes, host_bytes);
 }
 
 size_t up16(size_t v) {
@@ -226,6 +215,7 @@ void kb200_context_destroy(kb200_context* c) {
         if (e)
             cudaEventDestroy(e);
     delete c->team;
+    release_layers(c->layers);
     cudaStreamDestroy(c->stream);
     delete c;
 }

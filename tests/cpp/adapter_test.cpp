@@ -8,6 +8,7 @@
 // reference's exception messages, a source's exception rethrown, the
 // finite/unvalidated result over devices, and the residency virtuals over
 // the wrapped compute plus the banks. Prints "ok".
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -43,6 +44,8 @@ struct FakeDevice {
     const float* bias = nullptr;
     bool saw_cancel = false;
     std::uint64_t released = 0;
+    int layer_calls = 0, layers_released = 0;
+    std::vector<int> fresh;  // fresh flag of every delta step it ran
 };
 
 std::mutex fake_mutex;
@@ -229,6 +232,47 @@ int kb200_moe_forward_host(kb200_context* ctx, const kb200_moe_weights* w, const
     return KB200_OK;
 }
 
+// Attention on a fake device: out = q when it answers OK.
+int kb200_attend_cached_host(kb200_context* ctx, std::uint64_t, const float* q, const float*, const float*,
+                             std::size_t rows, std::size_t, std::size_t heads, std::size_t, std::size_t dim, float,
+                             const std::uint32_t*, const std::uint32_t*, float* out,
+                             const volatile std::uint8_t*) {
+    auto& d = device_of(reinterpret_cast<kb200_context_fake*>(ctx)->device);
+    ++d.layer_calls;
+    if (d.status != KB200_OK) {
+        last_error = d.error;
+        return d.status;
+    }
+    std::copy(q, q + rows * heads * dim, out);
+    return KB200_OK;
+}
+
+// A delta-net step on a fake device: every output 1.
+int kb200_delta_step_host(kb200_context* ctx, const kb200_delta_host* st, const volatile std::uint8_t*) {
+    auto& d = device_of(reinterpret_cast<kb200_context_fake*>(ctx)->device);
+    ++d.layer_calls;
+    d.fresh.push_back(st->fresh);
+    if (d.status != KB200_OK) {
+        last_error = d.error;
+        return d.status;
+    }
+    std::fill(st->output, st->output + std::size_t(st->rows) * st->value_heads * st->dim, 1.f);
+    return KB200_OK;
+}
+
+int kb200_recurrent_state_get(kb200_context* ctx, std::uint64_t, float* state, std::size_t n, float* history,
+                              std::size_t m) {
+    ++device_of(reinterpret_cast<kb200_context_fake*>(ctx)->device).layer_calls;
+    std::fill(state, state + n, 5.f);
+    std::fill(history, history + m, 6.f);
+    return KB200_OK;
+}
+
+int kb200_context_release_layers(kb200_context* ctx) {
+    ++device_of(reinterpret_cast<kb200_context_fake*>(ctx)->device).layers_released;
+    return KB200_OK;
+}
+
 }  // extern "C"
 
 namespace {
@@ -252,6 +296,22 @@ struct Fallback final : DenseCompute {
     }
     void release_devices() override {
         ++release_devices_calls;
+    }
+    int layer_calls = 0;
+    bool attend_cached(std::uint64_t, std::span<const float>, std::span<const float>, std::span<const float>,
+                       std::size_t, std::size_t, std::size_t, std::size_t, std::size_t, float, std::span<float>,
+                       const std::atomic_bool&, std::span<const std::uint32_t>,
+                       std::span<const std::uint32_t>) override {
+        ++layer_calls;
+        return false;
+    }
+    bool delta_step(const DeltaStep&, const std::atomic_bool&) override {
+        ++layer_calls;
+        return true;
+    }
+    void copy_recurrent_state(std::uint64_t, std::span<float> state, std::span<float>) override {
+        ++layer_calls;
+        std::fill(state.begin(), state.end(), 7.f);
     }
 };
 
@@ -553,7 +613,58 @@ void moe_layer() {
     CHECK(thrown([&] { compute.moe_mxfp4(w, x, logits, 3, y, cancel); }) == "h3_cuda_cancelled");
 }
 
+// Attention and delta-net: shapes the library does not take, and layers
+// whose fresh step it did not take, stay with the wrapped compute; the
+// library's layers keep every later step and the snapshot; release_scratch
+// without keep drops them.
+void layer_math() {
+    reset({{0, 1ull << 30}});
+    auto fallback = std::make_shared<Fallback>();
+    kadan::b200::Compute compute(fallback, {0}, 1ull << 30, 1ull << 20);
+    std::atomic_bool cancel{false};
+    std::vector<float> q(2 * 8 * 128, 0.5f), kv(6 * 2 * 128), out(q.size());
+    CHECK(compute.attend_cached(1, q, kv, kv, 2, 1, 8, 2, 128, 1.f, out, cancel, {}, {}));
+    CHECK(device_of(0).layer_calls == 1 && out[7] == 0.5f && fallback->layer_calls == 0);
+    std::vector<float> q96(8 * 96), kv96(2 * 96), out96(q96.size());
+    CHECK(!compute.attend_cached(1, q96, kv96, kv96, 1, 0, 8, 2, 96, 1.f, out96, cancel, {}, {}));
+    CHECK(fallback->layer_calls == 1 && device_of(0).layer_calls == 1);
+    device_of(0).status = KB200_CUDA;
+    device_of(0).error = "h3_cuda: launch failed (attention)";
+    CHECK(thrown([&] { compute.attend_cached(1, q, kv, kv, 2, 1, 8, 2, 128, 1.f, out, cancel, {}, {}); })
+          == "h3_cuda: launch failed (attention)");
+    device_of(0).status = KB200_OK;
+
+    const std::size_t kh = 2, vh = 4, dim = 64, kernel = 4, rows = 1, channels = (2 * kh + vh) * dim;
+    std::vector<float> qkv(rows * channels), z(rows * vh * dim), ab(rows * vh), conv(channels * kernel), dt(vh),
+        a(vh), norm(dim), y(rows * vh * dim);
+    auto step = [&](std::uint64_t layer, bool fresh, std::size_t d) {
+        return DenseCompute::DeltaStep{layer, fresh, qkv, z, ab, ab, conv, dt, a, std::span(norm).first(d), rows, kh,
+                                       vh, d, kernel, 1e-6f, true, y};
+    };
+    const int before = device_of(0).layer_calls;
+    // Layer 5: its fresh step does not fit (norm of 32 for dim 64), so the
+    // wrapped compute keeps it, later steps included.
+    CHECK(compute.delta_step(step(5, true, 32), cancel) && fallback->layer_calls == 2);
+    CHECK(compute.delta_step(step(5, false, dim), cancel) && fallback->layer_calls == 3);
+    // Layer 6: the library's from its fresh step on.
+    CHECK(compute.delta_step(step(6, true, dim), cancel) && y[3] == 1.f);
+    CHECK(compute.delta_step(step(6, false, dim), cancel));
+    CHECK(device_of(0).layer_calls == before + 2 && device_of(0).fresh == std::vector<int>({1, 0}));
+    std::vector<float> st(vh * dim * dim), hist((kernel - 1) * channels);
+    compute.copy_recurrent_state(6, st, hist);
+    CHECK(st[0] == 5.f && hist[0] == 6.f);
+    compute.copy_recurrent_state(5, st, hist);
+    CHECK(st[0] == 7.f && fallback->layer_calls == 4);
+    compute.release_scratch(true);
+    CHECK(device_of(0).layers_released == 0);
+    compute.release_scratch(false);
+    CHECK(device_of(0).layers_released == 1);
+    // After the release layer 6 is no longer the library's.
+    CHECK(compute.delta_step(step(6, false, dim), cancel) && fallback->layer_calls == 5);
+}
+
 int main() {
+    layer_math();
     moe_layer();
     batch_over_two_devices();
     source_with_bias_over_two_devices();

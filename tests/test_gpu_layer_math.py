@@ -141,3 +141,81 @@ def test_delta_step_sequence(kb, oracle, cuda, key_heads, value_heads, dim, kern
         assert rel_err(state_d.cpu().numpy(), state) <= 1e-4
         if kernel > 1:
             assert np.array_equal(hist_d.cpu().numpy(), history)
+
+
+def test_attend_cached_host_mirrors_the_cache(kb, oracle, cuda):
+    """attend_cached from host spans over the context's per-layer KV mirror:
+    a 6-row prefill, then decode rows; positions mirrored earlier are reused
+    (a change the caller makes to them below `position` is not seen), the
+    call's own positions are uploaded again; two layers do not mix."""
+    rng = np.random.default_rng(21)
+    heads, kv_heads, dim, total = 16, 4, 128, 12
+    k = rng.standard_normal((total, kv_heads * dim)).astype(np.float32)
+    v = rng.standard_normal((total, kv_heads * dim)).astype(np.float32)
+    ctx = kb.Context(0)
+    scale = 0.088
+    mirror_k, mirror_v = k.copy(), v.copy()
+    for rows, position in ((6, 0), (1, 6), (2, 7), (1, 9)):
+        q = rng.standard_normal(rows * heads * dim).astype(np.float32)
+        if position:
+            # Rewrite a position the context already mirrors: it keeps its copy.
+            k[0] += 1.0
+        got = kb.attend_cached_host(ctx, 7, q, k, v, rows=rows, position=position, heads=heads, kv_heads=kv_heads,
+                                    dim=dim, scale=scale)
+        mirror_k[position:position + rows] = k[position:position + rows]
+        mirror_v[position:position + rows] = v[position:position + rows]
+        want = oracle.attend_cached(q, mirror_k, mirror_v, rows=rows, position=position, heads=heads,
+                                    kv_heads=kv_heads, dim=dim, scale=scale)
+        assert rel_err(got, want) <= 1e-4
+    # Another layer id starts its own mirror from the caller's current cache.
+    q = rng.standard_normal(heads * dim).astype(np.float32)
+    got = kb.attend_cached_host(ctx, 8, q, k, v, rows=1, position=9, heads=heads, kv_heads=kv_heads, dim=dim,
+                                scale=scale)
+    want = oracle.attend_cached(q, k, v, rows=1, position=9, heads=heads, kv_heads=kv_heads, dim=dim, scale=scale)
+    assert rel_err(got, want) <= 1e-4
+    with pytest.raises(kb.Unsupported):
+        kb.attend_cached_host(ctx, 9, q, k, v, rows=1, position=9, heads=heads, kv_heads=kv_heads, dim=96,
+                              scale=scale)
+    kb.release_layers(ctx)
+    ctx.close()
+
+
+def test_delta_step_host_carries_state(kb, oracle, cuda):
+    """delta_step from host spans: a fresh step, two later steps on the state
+    the device carries, a snapshot equal to the oracle's state, a restore from
+    that snapshot, and the lost-state rule after release."""
+    rng = np.random.default_rng(5)
+    key_heads, value_heads, dim, kernel = 4, 8, 128, 4
+    channels = (2 * key_heads + value_heads) * dim
+    conv = (rng.standard_normal(channels * kernel) * 0.5).astype(np.float32)
+    dt = rng.standard_normal(value_heads).astype(np.float32)
+    a = -np.abs(rng.standard_normal(value_heads)).astype(np.float32)
+    norm = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    history = np.zeros((kernel - 1) * channels, np.float32)
+    state = np.zeros(value_heads * dim * dim, np.float32)
+    ctx = kb.Context(0)
+    shape = dict(key_heads=key_heads, value_heads=value_heads, dim=dim, kernel=kernel, eps=1e-6, sigmoid_gate=True)
+
+    def inputs(rows):
+        return dict(qkv=rng.standard_normal(rows * channels), z=rng.standard_normal(rows * value_heads * dim),
+                    alpha=rng.standard_normal(rows * value_heads), beta=rng.standard_normal(rows * value_heads))
+
+    for i, rows in enumerate((3, 1, 1)):
+        x = {n: t.astype(np.float32) for n, t in inputs(rows).items()}
+        got = kb.delta_step_host(ctx, 3, fresh=i == 0, conv=conv, dt=dt, a=a, norm=norm, rows=rows, **x, **shape)
+        want = oracle.delta_step(x["qkv"], x["z"], x["alpha"], x["beta"], conv, dt, a, norm, rows=rows,
+                                 history=history, state=state, **shape)
+        assert rel_err(got.reshape(-1), want) <= 1e-4
+    snap_state, snap_hist = kb.recurrent_state_get(ctx, 3, state.size, history.size)
+    assert rel_err(snap_state, state) <= 1e-4
+    assert np.array_equal(snap_hist, history)
+    # Restore the snapshot into a fresh layer and take the same next step on both.
+    x = {n: t.astype(np.float32) for n, t in inputs(1).items()}
+    a1 = kb.delta_step_host(ctx, 3, fresh=False, conv=conv, dt=dt, a=a, norm=norm, rows=1, **x, **shape)
+    a2 = kb.delta_step_host(ctx, 4, fresh=True, conv=conv, dt=dt, a=a, norm=norm, rows=1, initial_state=snap_state,
+                            initial_history=snap_hist, **x, **shape)
+    assert np.array_equal(a1, a2)
+    kb.release_layers(ctx)
+    with pytest.raises(kb.KadanError, match="recurrent_state_lost"):
+        kb.delta_step_host(ctx, 3, fresh=False, conv=conv, dt=dt, a=a, norm=norm, rows=1, **x, **shape)
+    ctx.close()
