@@ -553,8 +553,92 @@ def extras(args, torch, kb, device, pk, line):
     torch.cuda.empty_cache()
     line["moe"] = guarded("moe", lambda: moe_object(args, torch, kb, device, pk))
     torch.cuda.empty_cache()
+    line["layer_math"] = guarded("layer_math", lambda: layer_math_object(args, torch, kb, device, pk))
+    torch.cuda.empty_cache()
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = guarded("cpu", lambda: cpu_baseline(budget_s=args.cpu_seconds))
+
+
+def layer_math_object(args, torch, kb, device, pk) -> dict:
+    """The layer math around the path on the device: Llama-3-70B decode
+    attention (64 query / 8 KV heads of 128, one query row) over a 4k and a
+    32k-position fp32 KV cache (HBM bound: the K and V bytes per call against
+    the measured copy bandwidth; the 32k cache, 256 MB, exceeds L2), parity of
+    the 4k case against the oracle; and one gated delta-net step (16 key / 32
+    value heads of 128, kernel 4, one row) with its state read and written."""
+    import numpy as np
+
+    from oracle.pyoracle import Oracle
+
+    res = {}
+    heads, kv_heads, dim = 64, 8, 128
+    gen = torch.Generator(device=device).manual_seed(0)
+    for ctx in (4096, 32768):
+        q = torch.randn(heads * dim, device=device, generator=gen)
+        k = torch.randn(ctx * kv_heads * dim, device=device, generator=gen)
+        v = torch.randn(ctx * kv_heads * dim, device=device, generator=gen)
+        out = torch.empty(1, heads, dim, device=device)
+        ws = torch.empty(kb.lib.kb200_attend_workspace_bytes(1, ctx - 1, heads, dim), dtype=torch.uint8,
+                         device=device)
+        stream = torch.cuda.current_stream()
+
+        def call():
+            kb.check(kb.lib.kb200_attend_cached(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, ctx - 1, heads,
+                                                kv_heads, dim, 1.0 / dim ** 0.5, None, None, out.data_ptr(),
+                                                ws.data_ptr(), ws.numel(), stream.cuda_stream))
+
+        for _ in range(5):
+            call()
+        torch.cuda.synchronize()
+        reps = 50
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            call()
+        b.record(stream)
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) / reps * 1e3
+        kv_bytes = 2 * ctx * kv_heads * dim * 4
+        gbps = kv_bytes / (us * 1e-6) / 1e9
+        entry = {"us_per_call": round(us, 2), "kv_bytes": kv_bytes,
+                 "roofline": {"bound": "hbm", "kernel": "attend_kernel + attend_combine_kernel",
+                              "achieved": round(gbps, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                              "frac": round(gbps / pk["hbm_gbs"], 4), "peak_source": f"{pk['source']} hbm_gbs"}}
+        if ctx == 4096:
+            want = Oracle().attend_cached(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), rows=1,
+                                          position=ctx - 1, heads=heads, kv_heads=kv_heads, dim=dim,
+                                          scale=1.0 / dim ** 0.5)
+            err = rel_err(out.cpu().numpy(), want)
+            entry["parity"] = {"ok": err <= 1e-4, "max_rel_err": err, "tolerance": 1e-4}
+        res[f"attention_ctx{ctx}"] = entry
+        del q, k, v, ws
+    kh, vh, dd, kern = 16, 32, 128, 4
+    channels = (2 * kh + vh) * dd
+    t = {n: torch.randn(sz, device=device, generator=gen) for n, sz in
+         (("qkv", channels), ("z", vh * dd), ("alpha", vh), ("beta", vh), ("conv", channels * kern), ("dt", vh),
+          ("norm", dd))}
+    t["a"] = -torch.rand(vh, device=device, generator=gen)
+    hist = torch.zeros((kern - 1) * channels, device=device)
+    state = torch.zeros(vh * dd * dd, device=device)
+    y = torch.empty(vh * dd, device=device)
+
+    def step():
+        kb.delta_step(history=hist, state=state, output=y, rows=1, key_heads=kh, value_heads=vh, dim=dd,
+                      kernel=kern, eps=1e-6, sigmoid_gate=True, **t)
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(50):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    res["delta_step"] = {"us_per_step": round(a.elapsed_time(b) / 50 * 1e3, 2), "rows": 1, "key_heads": kh,
+                         "value_heads": vh, "dim": dd, "kernel": kern, "state_bytes": vh * dd * dd * 4,
+                         "note": "includes the step workspace allocation of the Python binding"}
+    return res
 
 
 def c4_host_layer(synth):
