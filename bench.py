@@ -456,11 +456,22 @@ def run_default(args, rank, world, local_rank):
         for _ in range(e2e_steps):
             host_step()
         host_s = (time.perf_counter() - t0) / e2e_steps
+        # The Python side of those calls alone: the same number of ctypes
+        # calls of kb200_dense_gguf_batch with an empty batch (it returns
+        # KB200_UNSUPPORTED at once, before touching anything).
+        empty = (kb.HostJob * 1)()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            for _arr in host_calls:
+                kb.lib.kb200_dense_gguf_batch(ctx.handle, empty, 0, None, ctypes.byref(result))
+        ctypes_s = (time.perf_counter() - t0) / e2e_steps
         ctx.close()
         e2e = {"value": round((wbytes + abytes) / host_s / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": layers * sum(tokens * g[0].in_ * 4 for g in groups),
                "d2h_bytes_per_step": layers * sum(tokens * p.out * 4 for g in groups for p in g),
                "calls_per_step": len(host_calls), "ms_per_step": round(host_s * 1e3, 4),
+               "python_call_ms_per_step": round(ctypes_s * 1e3, 4),
+               "library_ms_per_step": round((host_s - ctypes_s) * 1e3, 4),
                "timing": "host wall clock around synchronous kb200_dense_gguf_batch calls (host spans), one per "
                          "dependency group", "graph_path": graph_path}
     else:

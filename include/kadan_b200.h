@@ -432,6 +432,20 @@ KB200_API int kb200_moe_combine(
     float* out, void* stream
 );
 
+/* The reference MoE's sigmoid-gated shared expert (MoeLayer::forward,
+ * IW/src/models/text/qwen_layers.cpp:383-396, :477-490): a dense FFN beside
+ * the routed experts whose gate/up/down projections are ordinary GGUF
+ * matrices (kb200_gguf_gemv_batch / kb200_gguf_gemm or the host-span batch).
+ * kb200_silu_mul: out[j] = silu(gate[j]) * up[j] (the activation between its
+ * gate/up and down projections, :390-395), n values; out may equal gate.
+ * kb200_moe_add_shared: per token t, out[t][d] += down[t][d] *
+ * sigmoid(sum_c shared_gate[c] * x[t][c]) (:477-490); x [tokens][hidden]
+ * fp32, shared_gate [hidden], down and out [tokens][hidden]. Applied to
+ * kb200_moe_forward's output this gives the reference layer's output. */
+KB200_API int kb200_silu_mul(const float* gate, const float* up, size_t n, float* out, void* stream);
+KB200_API int kb200_moe_add_shared(const float* x, const float* shared_gate, const float* down, size_t tokens,
+                                   size_t hidden, float* out, void* stream);
+
 /* Row permutation by segments: dst rows [d, d+n) = src rows [s, s+n) for
  * each {s, d, n} of `segments` (device int64 [count][3]); row_bytes a
  * multiple of 16; max_rows the longest segment (sizes the grid). Used to
@@ -985,7 +999,9 @@ typedef enum kb200_kernel {
     KB200_KERNEL_DELTA_CONV = 24,
     KB200_KERNEL_DELTA_L2 = 25,
     KB200_KERNEL_DELTA_HEADS = 26,
-    KB200_KERNEL_COUNT = 27
+    KB200_KERNEL_SILU_MUL = 27,
+    KB200_KERNEL_MOE_SHARED = 28,       /* moe_shared_kernel (shared expert's gated add) */
+    KB200_KERNEL_COUNT = 29
 } kb200_kernel;
 
 typedef struct kb200_kernel_metrics {

@@ -94,7 +94,7 @@ class ContextCounters(ctypes.Structure):
                 ("gemm_fallbacks", ctypes.c_uint64)]
 
 
-KERNEL_COUNT = 27
+KERNEL_COUNT = 29
 
 
 class KernelMetrics(ctypes.Structure):
@@ -741,3 +741,23 @@ def recurrent_state_get(ctx: "Context", layer: int, state_floats: int, history_f
 def release_layers(ctx: "Context") -> None:
     """kb200_context_release_layers."""
     check(lib.kb200_context_release_layers(ctx.handle))
+
+
+lib.kb200_silu_mul.argtypes = [_vp, _vp, ctypes.c_size_t, _vp, _vp]
+lib.kb200_moe_add_shared.argtypes = [_vp, _vp, _vp, ctypes.c_size_t, ctypes.c_size_t, _vp, _vp]
+
+
+def silu_mul(gate, up, out=None, stream=None):
+    """kb200_silu_mul on device tensors: silu(gate) * up."""
+    import torch
+
+    out = torch.empty_like(gate) if out is None else out
+    check(lib.kb200_silu_mul(gate.data_ptr(), up.data_ptr(), gate.numel(), out.data_ptr(), _stream_ptr(stream)))
+    return out
+
+
+def moe_add_shared(x, shared_gate, down, out, stream=None) -> None:
+    """kb200_moe_add_shared: out += down * sigmoid(shared_gate . x) per token (device tensors, in place)."""
+    hidden = shared_gate.numel()
+    check(lib.kb200_moe_add_shared(x.data_ptr(), shared_gate.data_ptr(), down.data_ptr(), x.numel() // hidden, hidden,
+                                   out.data_ptr(), _stream_ptr(stream)))

@@ -12,13 +12,15 @@
 // repeated float multiplication, softmax over max-subtracted scores.
 //
 // B200 layout of the two heavy kernels:
-//   attention  one CTA per (query row, KV head, segment of 256 keys) serves
+//   attention  one CTA per (query row, KV head, segment of 128 keys) serves
 //              all query heads of the KV head's group, so every key and value
 //              row is read from HBM once per group instead of once per head.
-//              Each warp scores 32 keys at a time with one key per lane
+//              Each warp stages 32 key rows in shared memory (one coalesced
+//              row per load, all 32 in flight), scores them one key per lane
 //              (exponentials one per lane, not one per key), then adds the
-//              32 value rows with lanes owning dim / 32 contiguous dims
-//              (coalesced rows). Segments are combined by a second kernel.
+//              32 value rows, several in flight, with lanes owning dim / 32
+//              contiguous dims (coalesced rows). Segments are combined by a
+//              second kernel.
 //   delta net  one CTA per value head with the head's dim x dim state in
 //              shared memory for the whole step (read and written once per
 //              step, not once per row); thread j owns state column j.
@@ -96,7 +98,7 @@ __global__ void rope_kernel(float* x, size_t rows, size_t row_width, size_t widt
 
 // -------------------------------------------------------------- attention
 constexpr int kAttnWarps = 4;
-constexpr int kAttnSegment = 256;  // keys per CTA
+constexpr int kAttnSegment = 32 * kAttnWarps;  // keys per CTA: one 32-key chunk per warp
 constexpr int kAttnMaxGE = 64;     // group heads x dims per lane held in registers
 constexpr int kAttnMaxG = 16;      // query heads per KV head
 
@@ -106,8 +108,9 @@ struct AttnParams {
     const float* values;  // same
     const uint32_t* selected;
     const uint32_t* offsets;
-    float* partial;       // [rows][heads][segments][dim + 2]
+    float* partial;       // sums [rows][heads][segments][dim], then (max, total) [rows][heads][segments][2]
     uint32_t position, heads, kv_heads, dim, segments;
+    uint32_t seg_len;     // keys per segment, a multiple of 32 * kAttnWarps
     float scale;
 };
 
@@ -125,19 +128,28 @@ __device__ __forceinline__ void load_dims(const float* p, float (&v)[8], int E) 
 }
 
 // E = dim / 32 (2, 4 or 8): dims [E lane, E lane + E) of a row belong to
-// lane `lane` when value rows are added. G = query heads per KV head.
-template <int E>
+// lane `lane` when value rows are added. G = query heads per KV head, at most
+// GM (a power of two fixed at compile time, so the per-head state stays in
+// registers). Shared
+// memory: the group's queries [G][dim], then per warp half of its 32 key rows
+// at a time, [32][dim/2 + 4] (the pad keeps lane t's reads of row t
+// conflict-free), reused at the end as merge space.
+template <int E, int GM>
 __global__ void __launch_bounds__(32 * kAttnWarps) attend_kernel(const __grid_constant__ AttnParams p) {
-    constexpr int GM = kAttnMaxGE / E < kAttnMaxG ? kAttnMaxGE / E : kAttnMaxG;  // most group heads
-    extern __shared__ float qs[];       // [G][dim] queries, then [warps][2 + G][...] merge space
+    constexpr int D = 32 * E, H = D / 2, KP = H + 4;  // head dim, staged half, key row pitch
+    constexpr int VU = E >= 8 ? 4 : 8;                // value rows in flight
+    extern __shared__ __align__(16) float smem_f[];
     const int row = blockIdx.x, kv = blockIdx.y, seg = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int dim = int(p.dim), G = int(p.heads / p.kv_heads);
+    const int G = int(p.heads / p.kv_heads);
+    float* qs = smem_f;
+    float* ks = smem_f + G * D + warp * 32 * KP;
     const uint32_t* chosen = p.selected ? p.selected + p.offsets[row] : nullptr;
     const int visible = int(p.selected ? p.offsets[row + 1] - p.offsets[row] : p.position + uint32_t(row) + 1u);
-    const int begin = seg * kAttnSegment, end = min(visible, begin + kAttnSegment);
-    for (int i = threadIdx.x; i < G * dim; i += blockDim.x)
-        qs[i] = p.q[(size_t(row) * p.heads + size_t(kv) * G) * dim + i];
+    const int begin = seg * int(p.seg_len), end = min(visible, begin + int(p.seg_len));
+    const size_t stride = size_t(p.kv_heads) * D;  // floats between cache positions
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x)
+        qs[i] = p.q[(size_t(row) * p.heads + size_t(kv) * G) * D + i];
     __syncthreads();
 
     float m[GM], l[GM], acc[GM][E];
@@ -149,28 +161,48 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attend_kernel(const __grid_co
             acc[g][e] = 0.f;
     }
     for (int c0 = begin + 32 * warp; c0 < end; c0 += 32 * kAttnWarps) {
-        // Scores: lane t takes key c0 + t.
-        const int t = c0 + lane;
-        const bool live = t < end;
-        const size_t at = (size_t(live ? (chosen ? chosen[t] : uint32_t(t)) : 0u) * p.kv_heads + kv) * dim;
+        const int n = min(32, end - c0);
+        // Scores: lane t takes key c0 + t, over the two halves of the dims.
+        const bool live = lane < n;
         float s[GM];
 #pragma unroll
         for (int g = 0; g < GM; ++g)
             s[g] = 0.f;
-        const float* key = p.keys + at;
-        for (int d = 0; d < dim; d += 4) {
-            const float4 k4 = *reinterpret_cast<const float4*>(key + d);
+        const float* mine = ks + lane * KP;
 #pragma unroll
-            for (int g = 0; g < GM; ++g)
-                if (g < G) {
-                    const float4 q4 = *reinterpret_cast<const float4*>(qs + g * dim + d);
+        for (int half = 0; half < 2; ++half) {
+            // Half of each key row into shared memory: lanes cover the half
+            // row in 16-byte pieces, 32 / (H / 4) rows per warp load, every
+            // load in flight before the first store.
+            constexpr int PIECES = H / 4, RPL = 32 / PIECES;
+            const int piece = lane % PIECES, sub = lane / PIECES;
+#pragma unroll 8
+            for (int r0 = 0; r0 < 32; r0 += RPL) {
+                const int r = r0 + sub;
+                if (r < n) {
+                    const float* key = p.keys + size_t(chosen ? chosen[c0 + r] : uint32_t(c0 + r)) * stride
+                                       + size_t(kv) * D + half * H;
+                    *reinterpret_cast<float4*>(ks + r * KP + 4 * piece) = *reinterpret_cast<const float4*>(key + 4 * piece);
+                }
+            }
+            __syncwarp();
+#pragma unroll 4
+            for (int d = 0; d < H; d += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(mine + d);
+#pragma unroll
+                for (int g = 0; g < GM; ++g) {
+                    if (g >= G)
+                        break;
+                    const float4 q4 = *reinterpret_cast<const float4*>(qs + g * D + half * H + d);
                     s[g] = fmaf(q4.x, k4.x, s[g]);
                     s[g] = fmaf(q4.y, k4.y, s[g]);
                     s[g] = fmaf(q4.z, k4.z, s[g]);
                     s[g] = fmaf(q4.w, k4.w, s[g]);
                 }
+            }
+            __syncwarp();
         }
-        // Online softmax per head over the chunk, then the 32 value rows.
+        // Online softmax per head over the chunk.
         float pr[GM];
 #pragma unroll
         for (int g = 0; g < GM; ++g) {
@@ -192,28 +224,37 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attend_kernel(const __grid_co
             for (int e = 0; e < E; ++e)
                 acc[g][e] *= corr;
         }
-        const int n = min(32, end - c0);
-        for (int j = 0; j < n; ++j) {
-            const int tj = c0 + j;
-            const size_t vat = (size_t(chosen ? chosen[tj] : uint32_t(tj)) * p.kv_heads + kv) * dim + size_t(E) * lane;
-            float v[8];
-            load_dims(p.values + vat, v, E);
+        // The chunk's value rows, VU rows in flight at a time; lane owns dims
+        // [E lane, E lane + E) of each (coalesced rows).
+        for (int j0 = 0; j0 < n; j0 += VU) {
+            float v[VU][8];
 #pragma unroll
-            for (int g = 0; g < GM; ++g) {
-                if (g >= G)
+            for (int u = 0; u < VU; ++u) {
+                const int tj = c0 + min(j0 + u, n - 1);
+                const float* vr = p.values + size_t(chosen ? chosen[tj] : uint32_t(tj)) * stride + size_t(kv) * D;
+                load_dims(vr + size_t(E) * lane, v[u], E);
+            }
+#pragma unroll
+            for (int u = 0; u < VU; ++u) {
+                if (j0 + u >= n)
                     break;
-                const float w = __shfl_sync(0xffffffffu, pr[g], j);
 #pragma unroll
-                for (int e = 0; e < E; ++e)
-                    acc[g][e] = fmaf(w, v[e], acc[g][e]);
+                for (int g = 0; g < GM; ++g) {
+                    if (g >= G)
+                        break;
+                    const float w = __shfl_sync(0xffffffffu, pr[g], j0 + u);
+#pragma unroll
+                    for (int e = 0; e < E; ++e)
+                        acc[g][e] = fmaf(w, v[u][e], acc[g][e]);
+                }
             }
         }
     }
-    // Merge the warps: each writes (m, l) and its dims, warp 0 combines.
+    // Merge the warps: each writes (m, l) and its dims, then the CTA combines.
     __syncthreads();
-    float* ms = qs;                               // [warps][G]
-    float* ls = ms + kAttnWarps * G;              // [warps][G]
-    float* as = ls + kAttnWarps * G;              // [warps][G][dim]
+    float* ms = smem_f;                     // [warps][G]
+    float* ls = ms + kAttnWarps * G;        // [warps][G]
+    float* as = ls + kAttnWarps * G;        // [warps][G][dim]
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
         if (g >= G)
@@ -222,11 +263,12 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attend_kernel(const __grid_co
             ms[warp * G + g] = m[g], ls[warp * G + g] = l[g];
 #pragma unroll
         for (int e = 0; e < E; ++e)
-            as[(warp * G + g) * dim + E * lane + e] = acc[g][e];
+            as[(warp * G + g) * D + E * lane + e] = acc[g][e];
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < G * (dim + 2); i += blockDim.x) {
-        const int g = i / (dim + 2), d = i % (dim + 2);
+    const size_t entries = size_t(gridDim.x) * p.heads * p.segments;
+    for (int i = threadIdx.x; i < G * (D + 2); i += blockDim.x) {
+        const int g = i / (D + 2), d = i % (D + 2);
         float M = -INFINITY;
         for (int w = 0; w < kAttnWarps; ++w)
             if (ls[w * G + g] > 0.f)
@@ -235,33 +277,80 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attend_kernel(const __grid_co
         for (int w = 0; w < kAttnWarps; ++w)
             if (ls[w * G + g] > 0.f) {
                 const float f = expf(ms[w * G + g] - M);
-                sum += (d == 0 ? 0.f : d == 1 ? ls[w * G + g] : as[(w * G + g) * dim + d - 2]) * f;
+                sum += (d == 0 ? 0.f : d == 1 ? ls[w * G + g] : as[(w * G + g) * D + d - 2]) * f;
             }
-        const size_t head = size_t(kv) * G + g;
-        p.partial[((size_t(row) * p.heads + head) * p.segments + seg) * (dim + 2) + d] = d == 0 ? M : sum;
+        const size_t entry = (size_t(row) * p.heads + size_t(kv) * G + g) * p.segments + seg;
+        if (d >= 2)
+            p.partial[entry * D + d - 2] = sum;
+        else
+            p.partial[entries * D + entry * 2 + d] = d == 0 ? M : sum;
     }
 }
 
 // out[row][head][d] = sum_seg acc * e^(m - M) / sum_seg l * e^(m - M), over
-// segments that saw a key.
-__global__ void attend_combine_kernel(const float* partial, float* out, uint32_t heads, uint32_t dim,
-                                      uint32_t segments) {
+// segments that saw a key. One CTA of 256 threads per (row, head): the
+// segment weights e^(m - M) / total in parallel into shared memory, then
+// threads = (dim / 4 float4 columns) x (groups of segments), a group's sums
+// added through shared memory.
+__global__ void __launch_bounds__(256) attend_combine_kernel(const float* partial, float* out, uint32_t heads,
+                                                             uint32_t dim, uint32_t segments) {
+    extern __shared__ __align__(16) float cw[];  // [segments] weights, then [groups][dim] sums
+    __shared__ float red[8];
     const size_t rh = size_t(blockIdx.x) * heads + blockIdx.y;
-    const float* in = partial + rh * segments * (dim + 2);
+    const size_t entries = size_t(gridDim.x) * heads * segments;
+    const float* ml = partial + entries * dim + rh * segments * 2;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float M = -INFINITY;
-    for (uint32_t z = 0; z < segments; ++z)
-        if (in[z * (dim + 2) + 1] > 0.f)
-            M = fmaxf(M, in[z * (dim + 2)]);
+    for (uint32_t z = tid; z < segments; z += blockDim.x)
+        if (ml[2 * z + 1] > 0.f)
+            M = fmaxf(M, ml[2 * z]);
+    for (int o = 16; o; o >>= 1)
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0)
+        red[warp] = M;
+    __syncthreads();
+    M = red[0];
+    for (int w = 1; w < int(blockDim.x >> 5); ++w)
+        M = fmaxf(M, red[w]);
+    __syncthreads();
     float total = 0.f;
-    for (uint32_t z = 0; z < segments; ++z)
-        if (in[z * (dim + 2) + 1] > 0.f)
-            total += in[z * (dim + 2) + 1] * expf(in[z * (dim + 2)] - M);
-    for (uint32_t d = threadIdx.x; d < dim; d += blockDim.x) {
-        float sum = 0.f;
-        for (uint32_t z = 0; z < segments; ++z)
-            if (in[z * (dim + 2) + 1] > 0.f)
-                sum += in[z * (dim + 2) + 2 + d] * expf(in[z * (dim + 2)] - M);
-        out[rh * dim + d] = sum / total;
+    for (uint32_t z = tid; z < segments; z += blockDim.x) {
+        const float l = ml[2 * z + 1];
+        const float f = l > 0.f ? expf(ml[2 * z] - M) : 0.f;
+        cw[z] = f;
+        total += l * f;
+    }
+    for (int o = 16; o; o >>= 1)
+        total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (lane == 0)
+        red[warp] = total;
+    __syncthreads();
+    total = 0.f;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w)
+        total += red[w];
+    const int cols = int(dim / 4), groups = int(blockDim.x) / cols;
+    const int col = tid % cols, grp = tid / cols;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (grp < groups) {
+        const float* acc = partial + rh * segments * dim + 4 * col;
+#pragma unroll 4
+        for (uint32_t z = grp; z < segments; z += groups) {
+            const float w = cw[z];
+            const float4 a = *reinterpret_cast<const float4*>(acc + size_t(z) * dim);
+            sum.x = fmaf(w, a.x, sum.x), sum.y = fmaf(w, a.y, sum.y);
+            sum.z = fmaf(w, a.z, sum.z), sum.w = fmaf(w, a.w, sum.w);
+        }
+    }
+    float* gs = cw + ((segments + 3) & ~3u);
+    __syncthreads();
+    if (grp < groups)
+        *reinterpret_cast<float4*>(gs + grp * dim + 4 * col) = sum;
+    __syncthreads();
+    for (uint32_t d = tid; d < dim; d += blockDim.x) {
+        float v = 0.f;
+        for (int g = 0; g < groups; ++g)
+            v += gs[g * dim + d];
+        out[rh * dim + d] = v / total;
     }
 }
 
@@ -387,15 +476,72 @@ int launch_status(const char* what) {
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, what);
 }
 
-template <int E> int launch_attend(const AttnParams& p, size_t rows, cudaStream_t stream) {
+// Shared memory of attend_kernel<E, GM> for G heads per KV head: queries and
+// the warps' half key rows, or the merge space, whichever is larger.
+constexpr size_t attend_smem(int E, int G) {
+    return sizeof(float) * std::max(size_t(G) * 32 * E + size_t(kAttnWarps) * 32 * (16 * E + 4),
+                                     size_t(kAttnWarps) * G * (32 * E + 2));
+}
+
+void attend_split(size_t rows, size_t position, size_t kv_heads, size_t target, uint32_t& segments,
+                  uint32_t& seg_len);
+
+// Launch with about two waves of CTAs over the SMs (the variant's occupancy,
+// queried once per device), each segment a whole number of 128-key chunks.
+template <int E, int GM> int launch_attend(AttnParams& p, size_t rows, size_t position, cudaStream_t stream) {
+    static int blocks_per_sm[64] = {};
+    static std::mutex lock;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64)
+        return fail(KB200_UNSUPPORTED, "device index above 63");
+    const size_t smem_max = attend_smem(E, GM);
+    {
+        std::lock_guard<std::mutex> guard(lock);
+        if (!blocks_per_sm[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(attend_kernel<E, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 int(smem_max));
+            int n = 0;
+            if (e == cudaSuccess)
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attend_kernel<E, GM>, 32 * kAttnWarps, smem_max);
+            if (e != cudaSuccess)
+                return cuda_fail(e, "attend_kernel set-up");
+            blocks_per_sm[dev] = n > 0 ? n : 1;
+        }
+    }
     const int G = int(p.heads / p.kv_heads);
-    const size_t smem = size_t(4) * G * (p.dim + 2) * sizeof(float);  // merge space covers the queries
-    attend_kernel<E><<<dim3(unsigned(rows), p.kv_heads, p.segments), 32 * kAttnWarps, smem, stream>>>(p);
+    attend_split(rows, position, p.kv_heads, size_t(sm_count()) * blocks_per_sm[dev] * 2, p.segments, p.seg_len);
+    attend_kernel<E, GM><<<dim3(unsigned(rows), p.kv_heads, p.segments), 32 * kAttnWarps, attend_smem(E, G), stream>>>(p);
     return launch_status("attend_kernel launch");
+}
+
+template <int E> int launch_attend_e(AttnParams& p, size_t rows, size_t position, cudaStream_t stream) {
+    const uint32_t G = p.heads / p.kv_heads;
+    if (G <= 1)
+        return launch_attend<E, 1>(p, rows, position, stream);
+    if (G <= 2)
+        return launch_attend<E, 2>(p, rows, position, stream);
+    if (G <= 4)
+        return launch_attend<E, 4>(p, rows, position, stream);
+    if (G <= 8 || E >= 8)
+        return launch_attend<E, 8>(p, rows, position, stream);
+    return launch_attend<E, (E >= 8 ? 8 : 16)>(p, rows, position, stream);
 }
 
 size_t attend_segments(size_t rows, size_t position) {
     return (position + rows + kAttnSegment - 1) / kAttnSegment;
+}
+
+// Segments of a launch: about `target` CTAs in all, each segment a whole
+// number of 128-key chunks; at most attend_segments (the workspace bound).
+void attend_split(size_t rows, size_t position, size_t kv_heads, size_t target, uint32_t& segments,
+                  uint32_t& seg_len) {
+    const size_t keys = position + rows, most = attend_segments(rows, position);
+    const size_t want = std::max<size_t>(1, target / std::max<size_t>(1, rows * kv_heads));
+    const size_t n = std::min(most, want);
+    const size_t chunks = (keys + kAttnSegment - 1) / kAttnSegment;
+    seg_len = uint32_t((chunks + n - 1) / n * kAttnSegment);
+    segments = uint32_t((keys + seg_len - 1) / seg_len);
 }
 
 bool delta_shape_ok(uint32_t key_heads, uint32_t value_heads, uint32_t dim, uint32_t kernel) {
@@ -497,17 +643,19 @@ int kb200_attend_cached(const float* q, const float* keys, const float* values, 
     p.q = q, p.keys = keys, p.values = values, p.selected = selected, p.offsets = offsets;
     p.partial = static_cast<float*>(workspace);
     p.position = uint32_t(position), p.heads = uint32_t(heads), p.kv_heads = uint32_t(kv_heads);
-    p.dim = uint32_t(dim), p.segments = uint32_t(attend_segments(rows, position)), p.scale = scale;
+    p.dim = uint32_t(dim), p.scale = scale;
     {
         TraceScope trace(KB200_KERNEL_ATTEND, s);
-        const int st = dim == 64 ? launch_attend<2>(p, rows, s) : dim == 128 ? launch_attend<4>(p, rows, s)
-                                                                             : launch_attend<8>(p, rows, s);
+        const int st = dim == 64    ? launch_attend_e<2>(p, rows, position, s)
+                       : dim == 128 ? launch_attend_e<4>(p, rows, position, s)
+                                    : launch_attend_e<8>(p, rows, position, s);
         if (st)
             return st;
     }
     TraceScope trace(KB200_KERNEL_ATTEND_COMBINE, s);
-    attend_combine_kernel<<<dim3(unsigned(rows), unsigned(heads)), 128, 0, s>>>(p.partial, out, p.heads, p.dim,
-                                                                               p.segments);
+    const size_t combine_smem = (size_t((p.segments + 3) & ~3u) + 1024) * sizeof(float);
+    attend_combine_kernel<<<dim3(unsigned(rows), unsigned(heads)), 256, combine_smem, s>>>(p.partial, out, p.heads,
+                                                                                          p.dim, p.segments);
     return launch_status("attend_combine_kernel launch");
 }
 

@@ -263,6 +263,36 @@ __global__ void moe_combine_kernel(
     }
 }
 
+// ----------------------------------------------------------- shared expert
+__global__ void silu_mul_kernel(const float* gate, const float* up, size_t n, float* out) {
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+        const float g = gate[i];
+        out[i] = g / (1.f + expf(-g)) * up[i];
+    }
+}
+
+// One CTA per token: the gate dot product, its sigmoid, then the gated add.
+__global__ void __launch_bounds__(256) moe_shared_kernel(const float* x, const float* shared_gate, const float* down,
+                                                         int hidden, float* out) {
+    __shared__ float part[8];
+    const size_t t = blockIdx.x;
+    const float* xt = x + t * hidden;
+    float dot = 0.f;
+    for (int c = threadIdx.x; c < hidden; c += blockDim.x)
+        dot = fmaf(shared_gate[c], xt[c], dot);
+    for (int o = 16; o; o >>= 1)
+        dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if ((threadIdx.x & 31) == 0)
+        part[threadIdx.x >> 5] = dot;
+    __syncthreads();
+    float g = 0.f;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w)
+        g += part[w];
+    g = 1.f / (1.f + expf(-g));
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x)
+        out[t * hidden + d] += down[t * hidden + d] * g;
+}
+
 // ----------------------------------------------------------- grouped GEMM
 // Tiles of 128 sorted rows (M) x 256 weight rows (N): each 16 KB activation
 // tile feeds 256 output columns, half the L2 -> SM bytes per FLOP of 128-row
@@ -1310,6 +1340,38 @@ int kb200_moe_experts(const kb200_moe_weights* w, const uint16_t* rows_f16, cons
         return cuda_fail(e, "moe_mtile_kernel launch");
     return experts_launch(w, reinterpret_cast<const __half*>(rows_f16), offsets, ws.mtile, rows, ws.act, y, status,
                           stream);
+}
+
+int kb200_silu_mul(const float* gate, const float* up, size_t n, float* out, void* stream) {
+    if (!n)
+        return KB200_OK;
+    if (!gate || !up || !out)
+        return fail(KB200_INVALID, "null pointer");
+    if ((out != gate && overlap(out, n * 4, gate, n * 4)) || (out != up && overlap(out, n * 4, up, n * 4)))
+        return fail(KB200_ALIAS, "output partly overlaps an input");
+    const unsigned grid = unsigned(std::min<size_t>((n + 255) / 256, size_t(sm_count()) * 8));
+    TraceScope trace(KB200_KERNEL_SILU_MUL, static_cast<cudaStream_t>(stream));
+    silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(gate, up, n, out);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "silu_mul_kernel launch");
+}
+
+int kb200_moe_add_shared(const float* x, const float* shared_gate, const float* down, size_t tokens, size_t hidden,
+                         float* out, void* stream) {
+    if (!tokens)
+        return KB200_OK;
+    if (!x || !shared_gate || !down || !out || !hidden)
+        return fail(KB200_INVALID, "null pointer or zero width");
+    if (hidden > (1u << 30) || tokens > 0x7FFFFFFFu)
+        return fail(KB200_UNSUPPORTED, "shape");
+    const size_t bytes = tokens * hidden * 4;
+    if (overlap(out, bytes, x, bytes) || overlap(out, bytes, down, bytes) || overlap(out, bytes, shared_gate, hidden * 4))
+        return fail(KB200_ALIAS, "output overlaps an input");
+    TraceScope trace(KB200_KERNEL_MOE_SHARED, static_cast<cudaStream_t>(stream));
+    moe_shared_kernel<<<unsigned(tokens), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, shared_gate, down,
+                                                                                       int(hidden), out);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_shared_kernel launch");
 }
 
 int kb200_moe_combine(const float* y, const float* weight, const int32_t* pos, size_t tokens, int32_t top_k,

@@ -226,3 +226,25 @@ int orc_delta_step(const float* qkv, const float* z, const float* alpha, const f
     free(mixed);
     return 0;
 }
+
+/* The reference MoE's shared expert (MoeLayer::forward, qwen_layers.cpp:
+ * 390-395 and 477-490): the activation silu(gate) * up between its gate/up
+ * and down projections, and the gated add of its down projection to the
+ * routed experts' sum, gate = sigmoid(shared_gate . x) with the dot product
+ * accumulated in float in column order. */
+void orc_silu_mul(const float* gate, const float* up, size_t n, float* out) {
+    for (size_t j = 0; j < n; ++j)
+        out[j] = f_silu(gate[j]) * up[j];
+}
+
+void orc_moe_add_shared(const float* x, const float* shared_gate, const float* down, size_t tokens, size_t hidden,
+                        float* out) {
+    for (size_t t = 0; t < tokens; ++t) {
+        float gate = 0;
+        for (size_t c = 0; c < hidden; ++c)
+            gate += shared_gate[c] * x[t * hidden + c];
+        gate = f_sigmoid(gate);
+        for (size_t d = 0; d < hidden; ++d)
+            out[t * hidden + d] = out[t * hidden + d] + down[t * hidden + d] * gate;
+    }
+}

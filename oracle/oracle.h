@@ -117,6 +117,9 @@ void orc_rope(float* x, size_t rows, size_t row_width, size_t width, size_t rota
 int orc_attend_cached(const float* q, const float* keys, const float* values, size_t rows, size_t position,
                       size_t heads, size_t kv_heads, size_t dim, float scale, const uint32_t* selected,
                       const uint32_t* offsets, float* out);
+void orc_silu_mul(const float* gate, const float* up, size_t n, float* out);
+void orc_moe_add_shared(const float* x, const float* shared_gate, const float* down, size_t tokens, size_t hidden,
+                        float* out);
 void orc_delta_rule(float* state, const float* q, const float* k, const float* v, const float* decay, size_t decays,
                     float beta, size_t dim, float* out);
 int orc_delta_step(const float* qkv, const float* z, const float* alpha, const float* beta, const float* conv,

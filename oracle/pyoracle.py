@@ -78,6 +78,10 @@ class Oracle:
         L.orc_rope.argtypes = [_f32p, sz, sz, sz, sz, sz, f32]
         _u32p = ctypes.POINTER(ctypes.c_uint32)
         L.orc_attend_cached.argtypes = [_f32p, _f32p, _f32p, sz, sz, sz, sz, sz, f32, _u32p, _u32p, _f32p]
+        L.orc_silu_mul.restype = None
+        L.orc_silu_mul.argtypes = [_f32p, _f32p, sz, _f32p]
+        L.orc_moe_add_shared.restype = None
+        L.orc_moe_add_shared.argtypes = [_f32p, _f32p, _f32p, sz, sz, _f32p]
         L.orc_delta_rule.restype = None
         L.orc_delta_rule.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, sz, f32, sz, _f32p]
         L.orc_delta_step.argtypes = [_f32p] * 8 + [sz] * 5 + [f32, ctypes.c_int, _f32p, _f32p, _f32p]
@@ -195,6 +199,19 @@ class Oracle:
         if rc:
             raise ValueError("gguf_text_attention_shape")
         return out.reshape(rows, heads, dim)
+
+    def silu_mul(self, gate, up) -> np.ndarray:
+        g, u = self._f(gate), self._f(up)
+        out = np.empty_like(g)
+        self.L.orc_silu_mul(_p(g, _f32p), _p(u, _f32p), g.size, _p(out, _f32p))
+        return out
+
+    def moe_add_shared(self, x, shared_gate, down, out, *, hidden: int) -> np.ndarray:
+        """out + down * sigmoid(shared_gate . x) per token (a new array)."""
+        xs, g, d = self._f(x), self._f(shared_gate), self._f(down)
+        y = self._f(out).copy()
+        self.L.orc_moe_add_shared(_p(xs, _f32p), _p(g, _f32p), _p(d, _f32p), xs.size // hidden, hidden, _p(y, _f32p))
+        return y
 
     def delta_rule(self, state, q, k, v, decay, beta: float) -> np.ndarray:
         """One delta_rule step; `state` (float32, dim*dim) is updated in place."""

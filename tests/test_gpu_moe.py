@@ -274,3 +274,42 @@ def test_moe_host_span_call(kb, oracle, cuda, config3_layer):
         torch.cuda.synchronize()
     finally:
         ctx.close()
+
+
+def test_shared_expert_composition(kb, oracle, cuda):
+    """The reference MoE layer with its sigmoid-gated shared expert
+    (qwen_layers.cpp:383-396, :477-490): the shared FFN's Q8_0 gate/up
+    projections on the GEMV, silu(gate) * up on the device, its down
+    projection, the routed layer, then the gated add; against the oracle
+    composed the same way (double dots for the projections, the unrounded
+    routed layer). Outputs are fp32: 1e-3."""
+    import torch
+
+    from kadan_b200 import synth
+
+    E, H, I, K, T, SF = 8, 256, 128, 2, 24, 512
+    w, dev, host = layer(kb, cuda, E=E, H=H, I=I, K=K, seed=11, activation=1, interleaved=False)
+    x, logits, xb, ld = inputs(cuda, T, H, E, seed=12)
+    g_w = synth.gguf(kb.Q8_0, SF, H, seed=13)
+    u_w = synth.gguf(kb.Q8_0, SF, H, seed=14)
+    d_w = synth.gguf(kb.Q8_0, H, SF, seed=15)
+    sg = (np.random.default_rng(16).standard_normal(H) * 0.05).astype(np.float32)
+    xf = torch.from_numpy(x).to(cuda)
+    gd = kb.gguf_gemv(kb.Q8_0, torch.from_numpy(g_w).to(cuda), xf, in_=H, columns=SF)
+    ud = kb.gguf_gemv(kb.Q8_0, torch.from_numpy(u_w).to(cuda), xf, in_=H, columns=SF)
+    sd = kb.silu_mul(gd, ud)
+    dd = kb.gguf_gemv(kb.Q8_0, torch.from_numpy(d_w).to(cuda), sd, in_=SF, columns=H)
+    y = kb.moe_forward(w, xb, ld)
+    kb.moe_add_shared(xf, torch.from_numpy(sg).to(cuda), dd, y)
+    torch.cuda.synchronize()
+
+    g = oracle.gemv_f64(kb.Q8_0, g_w, x, H, SF)
+    u = oracle.gemv_f64(kb.Q8_0, u_w, x, H, SF)
+    s = oracle.silu_mul(g, u).reshape(T, SF)
+    d = oracle.gemv_f64(kb.Q8_0, d_w, s, SF, H)
+    routed = oracle.moe_forward(x, logits, host["gu_w"], host["gu_s"], host["dn_w"], host["dn_s"], hidden=H, inter=I,
+                                experts=E, top_k=K, activation=1, interleaved=0, round_act=0)
+    want = oracle.moe_add_shared(x, sg, d, routed, hidden=H)
+    assert rel_err(y.cpu().numpy(), want) <= 1e-3
+    # silu_mul alone is elementwise float arithmetic.
+    assert rel_err(sd.cpu().numpy(), oracle.silu_mul(gd.cpu().numpy(), ud.cpu().numpy())) <= 1e-6
