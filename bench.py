@@ -456,6 +456,15 @@ def run_default(args, rank, world, local_rank):
         for _ in range(e2e_steps):
             host_step()
         host_s = (time.perf_counter() - t0) / e2e_steps
+        # The library's own view of one step (telemetry phase): launches per
+        # kernel, host seconds inside the launch calls, device seconds.
+        with kb.Phase() as phase:
+            host_step()
+            torch.cuda.synchronize()
+            tel = phase.snapshot()
+        phase.close()
+        telemetry = {k: {"calls": v["calls"], "launch_host_ms": round(v["host_seconds"] * 1e3, 3),
+                         "gpu_ms": round(v["gpu_seconds"] * 1e3, 3)} for k, v in tel["kernels"].items()}
         # The Python side of those calls alone: the same number of ctypes
         # calls of kb200_dense_gguf_batch with an empty batch (it returns
         # KB200_UNSUPPORTED at once, before touching anything).
@@ -472,6 +481,7 @@ def run_default(args, rank, world, local_rank):
                "calls_per_step": len(host_calls), "ms_per_step": round(host_s * 1e3, 4),
                "python_call_ms_per_step": round(ctypes_s * 1e3, 4),
                "library_ms_per_step": round((host_s - ctypes_s) * 1e3, 4),
+               "telemetry_one_step": telemetry,
                "timing": "host wall clock around synchronous kb200_dense_gguf_batch calls (host spans), one per "
                          "dependency group", "graph_path": graph_path}
     else:

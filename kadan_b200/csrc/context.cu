@@ -307,21 +307,20 @@ int kb200_dense_gguf_batch(
         device_jobs[j] = kb200_gemv_job{job.weights, nullptr, nullptr, nullptr, job.row_bytes, job.out,
                                         job.in,      job.out, job.rows, job.encoding};
     }
-    // Device layout: [inputs][outputs][status: GEMV, GEMM][GEMM scratch];
-    // host staging mirrors all but the scratch.
+    // Device layout: [inputs][status: GEMV, GEMM][outputs][GEMM scratch], so
+    // one upload carries the inputs and the cleared status words and one
+    // download the status words and the outputs; host staging mirrors all
+    // but the scratch.
     const size_t in_bytes = inputs.floats * sizeof(float), out_bytes = outputs * sizeof(float);
-    const size_t status_at = up16(in_bytes + out_bytes);
-    const size_t scratch_at = up256(status_at + 16), scratch = gemm_scratch(device_jobs.data(), count);
-    if (const int s = ensure(c, scratch_at + scratch, status_at + 16))
+    const size_t status_at = up16(in_bytes), out_at = status_at + 16;
+    const size_t scratch_at = up256(out_at + out_bytes), scratch = gemm_scratch(device_jobs.data(), count);
+    if (const int s = ensure(c, scratch_at + scratch, out_at + out_bytes))
         return s;
     auto* dev = static_cast<uint8_t*>(c->workspace);
     auto* host = static_cast<uint8_t*>(c->pinned);
     stage_inputs(jobs, count, inputs, host);
     std::memset(host + status_at, 0, 2 * sizeof(unsigned));
-    cudaError_t e = cudaMemcpyAsync(dev, host, in_bytes, cudaMemcpyHostToDevice, c->stream);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(dev + status_at, host + status_at, 2 * sizeof(unsigned), cudaMemcpyHostToDevice,
-                            c->stream);
+    cudaError_t e = cudaMemcpyAsync(dev, host, status_at + 2 * sizeof(unsigned), cudaMemcpyHostToDevice, c->stream);
     if (e != cudaSuccess)
         return cuda_fail(e, "input upload");
     if (cancelled(cancel)) {
@@ -331,15 +330,15 @@ int kb200_dense_gguf_batch(
     auto* status = reinterpret_cast<unsigned*>(dev + status_at);
     for (size_t j = 0; j < count; ++j) {
         device_jobs[j].input = reinterpret_cast<const float*>(dev) + inputs.at[j];
-        device_jobs[j].output = reinterpret_cast<float*>(dev + in_bytes) + output_at[j];
+        device_jobs[j].output = reinterpret_cast<float*>(dev + out_at) + output_at[j];
         device_jobs[j].status = jobs[j].validated ? nullptr : status;
     }
     if (const int s = launch_projections(c, device_jobs.data(), count, dev + scratch_at, scratch, status + 1)) {
         cudaStreamSynchronize(c->stream);
         return s;
     }
-    const size_t download = status_at + 2 * sizeof(unsigned) - in_bytes;
-    e = cudaMemcpyAsync(host + in_bytes, dev + in_bytes, download, cudaMemcpyDeviceToHost, c->stream);
+    e = cudaMemcpyAsync(host + status_at, dev + status_at, out_at + out_bytes - status_at, cudaMemcpyDeviceToHost,
+                        c->stream);
     if (e == cudaSuccess)
         e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess)
@@ -357,14 +356,14 @@ int kb200_dense_gguf_batch(
             cudaStreamSynchronize(c->stream);
             return s;
         }
-        e = cudaMemcpyAsync(host + in_bytes, dev + in_bytes, out_bytes, cudaMemcpyDeviceToHost, c->stream);
+        e = cudaMemcpyAsync(host + out_at, dev + out_at, out_bytes, cudaMemcpyDeviceToHost, c->stream);
         if (e == cudaSuccess)
             e = cudaStreamSynchronize(c->stream);
         if (e != cudaSuccess)
             return cuda_fail(e, "output download");
     }
     for (size_t j = 0; j < count; ++j)
-        std::memcpy(jobs[j].output, host + in_bytes + output_at[j] * sizeof(float),
+        std::memcpy(jobs[j].output, host + out_at + output_at[j] * sizeof(float),
                     size_t(jobs[j].rows) * jobs[j].out * sizeof(float));
     if (result)
         *result = KB200_RESULT_UNVALIDATED;

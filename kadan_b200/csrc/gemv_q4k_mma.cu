@@ -699,9 +699,13 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
                 // The window covers all of K when the segment buffer holds
                 // it (one quantisation per input however the work is cut),
                 // else this stage and what follows, as far as it reaches.
+                // The CTA's last piece needs only its own blocks (small
+                // launches: a piece of a few units would otherwise quantise
+                // all of K).
                 const int nbk = int(job.nblocks);
-                const int start = nbk <= seg.blocks ? 0 : blk_first;
-                const int count = min(seg.blocks, nbk - start);
+                const bool last = pieces.cur >= pieces.end;
+                const int start = last || nbk > seg.blocks ? blk_first : 0;
+                const int count = min(seg.blocks, (last ? int(pc.k1) : nbk) - start);
                 await_dependency();
                 // Every warp is done with the previous segment before it is replaced.
                 named_sync(1, kConsumerThreads);
@@ -1056,8 +1060,10 @@ __global__ void __launch_bounds__(kThreadsQ, q6_min_ctas<NT, S>()) gemv_q6k_mma_
             const int nb = min(kQ6Chunk, nblocks - blk_first);
             if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
                 && seg.blocks >= kQ6Chunk) {
-                const int start = nblocks <= seg.blocks ? 0 : blk_first;
-                const int count = min(seg.blocks, nblocks - start);
+                // The CTA's last piece needs only its own chunks.
+                const bool last = pieces.cur >= pieces.end;
+                const int start = last || nblocks > seg.blocks ? blk_first : 0;
+                const int count = min(seg.blocks, (last ? min(nblocks, int(pc.k1) * kQ6Chunk) : nblocks) - start);
                 await_dependency();
                 named_sync(1, kConsumerThreads);
                 prep_segment<true>(smem, seg, x, job.in, start, count);
@@ -1429,8 +1435,10 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
             const int nb = min(kQ6Chunk, nblocks - blk_first);
             if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
                 && seg.blocks >= kQ6Chunk) {
-                const int start = nblocks <= seg.blocks ? 0 : blk_first;
-                const int count = min(seg.blocks, nblocks - start);
+                // The CTA's last piece needs only its own chunks.
+                const bool last = pieces.cur >= pieces.end;
+                const int start = last || nblocks > seg.blocks ? blk_first : 0;
+                const int count = min(seg.blocks, (last ? min(nblocks, int(pc.k1) * kQ6Chunk) : nblocks) - start);
                 await_dependency();
                 named_sync(1, CT);
                 prep_pairs<W>(smem, seg, x, job.in, start, count);
