@@ -1128,10 +1128,15 @@ __global__ void __launch_bounds__(kThreadsQ, q6_min_ctas<NT, S>()) gemv_q6k_mma_
 // [hl][t] (512 bytes; lane (g, t) of pair p reads word (g % 4) * 4 + t of its
 // token), X words [digit][hl][t] (64 bytes), the scale s (4 bytes).
 constexpr int kPairWordBytes = 512, kPairXBytes = 64, kPairTokenBlock = kPairWordBytes + kPairXBytes + 4;
-constexpr int kPairSegBudget = 32 * kPairTokenBlock;  // all of K = 8192 for one token
+// Segment of S stages: 48 blocks of one token with 3 stages (two CTAs per SM
+// still fit: a long-K launch such as K = 28672 re-quantises its window a
+// third less often), all of K = 8192 with 2 stages (three CTAs per SM).
+template <int S> constexpr int pair_seg_budget() {
+    return (S == 3 ? 48 : 32) * kPairTokenBlock;
+}
 
-__host__ __device__ constexpr int pair_segment_blocks(int rows) {
-    return kPairSegBudget / (rows * kPairTokenBlock) / kQ6Chunk * kQ6Chunk;
+__host__ __device__ constexpr int pair_segment_blocks(int rows, int budget) {
+    return budget / (rows * kPairTokenBlock) / kQ6Chunk * kQ6Chunk;
 }
 
 // S stages, W consumer warps (each takes kQ6Chunk / W blocks of a stage).
@@ -1139,7 +1144,8 @@ template <int S, int W = kWarps> struct PairLayout {
     static constexpr int kStages = S;
     static constexpr int kStagesOff = 0;
     static constexpr int kSegOff = kStages * kQ6StageBytes;
-    static constexpr int kRedOff = kSegOff + kPairSegBudget;
+    static constexpr int kSegBudget = pair_seg_budget<S>();
+    static constexpr int kRedOff = kSegOff + kSegBudget;
     static constexpr int kRedBytes = 32 * W * 4 * 4;
     static constexpr int kBarOff = kRedOff + kRedBytes;
     static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
@@ -1149,7 +1155,8 @@ static_assert(3 * (PairLayout<2>::kTotal + 128 + 1024) <= 228 * 1024, "three Q6_
 
 struct PairSegment {
     int blocks, rows, off;
-    __device__ PairSegment(int r, int offset) : blocks(pair_segment_blocks(r)), rows(r), off(offset) {}
+    __device__ PairSegment(int r, int offset, int budget)
+        : blocks(pair_segment_blocks(r, budget)), rows(r), off(offset) {}
     __device__ uint32_t* words(uint8_t* smem) const { return reinterpret_cast<uint32_t*>(smem + off); }
     __device__ uint32_t* xwords(uint8_t* smem) const { return words(smem) + blocks * rows * (kPairWordBytes / 4); }
     __device__ float* scales(uint8_t* smem) const {
@@ -1412,7 +1419,7 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
         const int rows = int(min(job.group_rows, job.rows - r0));
         const int nblocks = int(job.in / 256);
         const float* x = job.input + size_t(r0) * job.in;
-        const PairSegment seg(rows, L::kSegOff);
+        const PairSegment seg(rows, L::kSegOff, L::kSegBudget);
         if (seg.blocks < kQ6Chunk)
             atomicExch(abort_flag, 1);
         const uint32_t* words = seg.words(smem);
