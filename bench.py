@@ -73,7 +73,7 @@ GATE_UP_TRAFFIC = 66922496  # 66,164,224 read + 758,272 written
 # DRAM bytes (read + write) per launch of config-4 groups at N=1, keyed by
 # group, from ncu captures of a 2-layer stack (a launch has the same size at
 # any layer count; the profile summaries give the commands).
-C4_TRAFFIC: dict = {"down": 194824960 + 4199424}  # gemv_q6k_pair_kernel<3>
+C4_TRAFFIC: dict = {"down": 194813184 + 7026944}  # gemv_q6k_pair_kernel<3, 4>
 
 
 def weight_bytes(out: int, in_: int) -> int:
@@ -906,6 +906,24 @@ def moe_cpu_layer(ref, oracle, x, logits, gu_ggml, dn_ggml, *, hidden: int, inte
     return out
 
 
+def run_attention(args):
+    """--case attention: the layer math around the path (decode attention at
+    4k and 32k cached positions, one delta-net step), as in the default
+    line's `layer_math`, as its own JSON line."""
+    import torch
+
+    import kadan_b200 as kb
+
+    dev = torch.device("cuda:0")
+    res = layer_math_object(args, torch, kb, dev, peaks())
+    a32 = res["attention_ctx32768"]
+    print(json.dumps({"metric": "decode attention GB/s (64 query / 8 KV heads of 128, 32k fp32 positions)",
+                      "value": a32["roofline"]["achieved"], "unit": "GB/s", "n_gpus": 1, "steps": 50,
+                      "warmup": 5, "higher_is_better": True, "data": "synthetic", "dtype": "f32",
+                      "config": {"workload": "Llama-3-70B decode attention, one query row"}, "layer_math": res}),
+          flush=True)
+
+
 def run_moe(args):
     """--case moe: the config-3 MoE layer at --tokens T (tokens/s, TFLOP/s),
     with the reference's host path (moe_cpu_layer on all host threads) timed
@@ -1544,6 +1562,8 @@ def main():
         run_source(args)
     elif args.case == "h3-reference":
         run_h3_reference(args)
+    elif args.case == "attention":
+        run_attention(args)
     elif args.case:
         run_case(args)
     elif args.impl == "reference":
