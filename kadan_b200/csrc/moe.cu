@@ -72,15 +72,11 @@ cudaError_t launch_pdl(kb200_kernel id, void (*kernel)(Params...), dim3 grid, di
 }
 
 // ---------------------------------------------------------------- routing
-// One warp per token; experts strided over lanes (<= 8 per lane).
-__global__ void moe_route_kernel(
-    const float* logits, int tokens, int E, int K, int* chosen, float* weight, int* counts
-) {
-    pdl_enter();
-    const int warp = int((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-    if (warp >= tokens)
-        return;
-    const float* l = logits + size_t(warp) * E;
+// Routing of one token by one warp; experts strided over lanes (<= 8 per
+// lane). Lane 0 writes the K choices and weights (and counts them when
+// `counts` is not null).
+__device__ __forceinline__ void route_token(const float* l, int E, int K, int* chosen, float* weight, int* counts) {
+    const int lane = threadIdx.x & 31;
     float v[8];
     float mx = -INFINITY;
 #pragma unroll
@@ -133,11 +129,22 @@ __global__ void moe_route_kernel(
     sum = fmaxf(sum, 6.103515625e-5f);
     if (lane == 0)
         for (int s = 0; s < K; ++s) {
-            chosen[size_t(warp) * K + s] = idx[s];
-            weight[size_t(warp) * K + s] = picked[s] / sum;
+            chosen[s] = idx[s];
+            weight[s] = picked[s] / sum;
             if (counts)
                 atomicAdd(&counts[idx[s]], 1);
         }
+}
+
+// One warp per token.
+__global__ void moe_route_kernel(
+    const float* logits, int tokens, int E, int K, int* chosen, float* weight, int* counts
+) {
+    pdl_enter();
+    const int warp = int((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (warp >= tokens)
+        return;
+    route_token(logits + size_t(warp) * E, E, K, chosen + size_t(warp) * K, weight + size_t(warp) * K, counts);
 }
 
 // ------------------------------------------------------------------- sort
@@ -726,12 +733,70 @@ __device__ __forceinline__ int gemv_row(const GemvParams& p, int c, int i) {
     return 16 * c + i;
 }
 
+// One 16-row x 8-token MMA item over all of K: this warp's K steps (128
+// columns each; steps warp, warp + 4, ...), each step's operands loaded a
+// step ahead of its MMAs. code0/code1 and sc0/sc1: the lane's rows g and
+// g + 8 (codes, E8M0 bytes); xr: the lane's token row (fp16, global or
+// shared memory). acc: the mma C fragment (rows g, g + 8 x tokens 2t, 2t+1).
+__device__ __forceinline__ void gemv_item(const uint8_t* code0, const uint8_t* code1, const uint8_t* sc0,
+                                          const uint8_t* sc1, const __half* xr, int K, int warp, float (&acc)[4],
+                                          bool& scale_ok) {
+    const int t = threadIdx.x & 3, iters = (K + 127) / 128;
+    struct Step {
+        uint4 w0, w1, x0, x1, x2, x3;
+        uint32_t s0, s1;  // E8M0 scale bytes (decoded at MMA time, so no load is waited on early)
+        bool live;
+    };
+    auto load = [&](int it, Step& st) {
+        const int k0 = 128 * it + 32 * t;  // first column of this lane's block
+        // Past K (K % 128 == 64 leaves lanes t = 2, 3 without a block in the
+        // last step): zeros, since every lane takes part in the MMAs.
+        const bool live = it < iters && k0 < K;
+        const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+        st.w0 = live ? __ldg(reinterpret_cast<const uint4*>(code0 + k0 / 2)) : zero;
+        st.w1 = live ? __ldg(reinterpret_cast<const uint4*>(code1 + k0 / 2)) : zero;
+        st.live = live;
+        st.s0 = live ? uint32_t(sc0[k0 / 32]) : 127u;
+        st.s1 = live ? uint32_t(sc1[k0 / 32]) : 127u;
+        const uint4* xq = reinterpret_cast<const uint4*>(xr + (live ? k0 : 0));
+        st.x0 = live ? xq[0] : zero, st.x1 = live ? xq[1] : zero;
+        st.x2 = live ? xq[2] : zero, st.x3 = live ? xq[3] : zero;
+    };
+    auto mma = [&](const Step& st) {
+        bool ok0, ok1;
+        const uint32_t s0 = e8m0_half2(st.s0, ok0), s1 = e8m0_half2(st.s1, ok1);
+        scale_ok = scale_ok && ((ok0 && ok1) || !st.live);
+        const uint32_t cw0[4] = {st.w0.x, st.w0.y, st.w0.z, st.w0.w}, cw1[4] = {st.w1.x, st.w1.y, st.w1.z, st.w1.w};
+        const uint32_t xw[16] = {st.x0.x, st.x0.y, st.x0.z, st.x0.w, st.x1.x, st.x1.y, st.x1.z, st.x1.w,
+                                 st.x2.x, st.x2.y, st.x2.z, st.x2.w, st.x3.x, st.x3.y, st.x3.z, st.x3.w};
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            // Code bytes 2m, 2m+1 of the block: values 4m..4m+3.
+            const uint32_t wa = cw0[m >> 1] >> (16 * (m & 1)), wb = cw1[m >> 1] >> (16 * (m & 1));
+            const uint32_t a0 = hmul2_bits(e2m1x2_to_half2(wa & 0xFFu), s0);
+            const uint32_t a2 = hmul2_bits(e2m1x2_to_half2((wa >> 8) & 0xFFu), s0);
+            const uint32_t a1 = hmul2_bits(e2m1x2_to_half2(wb & 0xFFu), s1);
+            const uint32_t a3 = hmul2_bits(e2m1x2_to_half2((wb >> 8) & 0xFFu), s1);
+            hmma16816(acc, a0, a1, a2, a3, xw[2 * m], xw[2 * m + 1]);
+        }
+    };
+    Step cur, nxt;
+    load(warp, cur);
+    for (int it = warp; it < iters; it += 2 * kGemvWarps) {
+        load(it + kGemvWarps, nxt);
+        mma(cur);
+        load(it + 2 * kGemvWarps, cur);
+        if (it + kGemvWarps < iters)
+            mma(nxt);
+    }
+}
+
 __global__ void __launch_bounds__(32 * kGemvWarps) moe_gemv_kernel(const __grid_constant__ GemvParams p) {
     __shared__ float4 part[kGemvWarps][32];  // each lane's four accumulators, per warp
     __shared__ int off[kMaxExperts + 1];     // expert row offsets: the skip test costs no global load
     pdl_enter();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int blocks_per_row = p.K / 32, iters = (p.K + 127) / 128;
+    const int blocks_per_row = p.K / 32;
     for (int i = threadIdx.x; i <= p.E; i += blockDim.x)
         off[i] = p.offsets[i];
     __syncthreads();
@@ -748,58 +813,8 @@ __global__ void __launch_bounds__(32 * kGemvWarps) moe_gemv_kernel(const __grid_
         const uint8_t* sc1 = p.scales + (size_t(e) * p.Nrows + r1) * blocks_per_row;
         for (int q = 0; q < count; q += 8) {
             const int tok = min(q + g, count - 1);  // B column g: token q+g (clamped; unused columns ignored)
-            const __half* xr = p.x + size_t(p0 + tok) * p.K;
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            // One step's operands (this lane's block of rows r0/r1 and the
-            // token's 32 activations); steps it = warp, warp + 4, ... of this
-            // warp, each loaded a step ahead of its MMAs.
-            struct Step {
-                uint4 w0, w1, x0, x1, x2, x3;
-                uint32_t s0, s1;  // E8M0 scale bytes (decoded at MMA time, so no load is waited on early)
-                bool live;
-            };
-            auto load = [&](int it, Step& st) {
-                const int k0 = 128 * it + 32 * t;  // first column of this lane's block
-                // Past K (K % 128 == 64 leaves lanes t = 2, 3 without a block
-                // in the last step): zeros, since every lane takes part in the MMAs.
-                const bool live = it < iters && k0 < p.K;
-                const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-                st.w0 = live ? __ldg(reinterpret_cast<const uint4*>(code0 + k0 / 2)) : zero;
-                st.w1 = live ? __ldg(reinterpret_cast<const uint4*>(code1 + k0 / 2)) : zero;
-                st.live = live;
-                st.s0 = live ? uint32_t(sc0[k0 / 32]) : 127u;
-                st.s1 = live ? uint32_t(sc1[k0 / 32]) : 127u;
-                const uint4* xq = reinterpret_cast<const uint4*>(xr + (live ? k0 : 0));
-                st.x0 = live ? __ldg(xq) : zero, st.x1 = live ? __ldg(xq + 1) : zero;
-                st.x2 = live ? __ldg(xq + 2) : zero, st.x3 = live ? __ldg(xq + 3) : zero;
-            };
-            auto mma = [&](const Step& st) {
-                bool ok0, ok1;
-                const uint32_t s0 = e8m0_half2(st.s0, ok0), s1 = e8m0_half2(st.s1, ok1);
-                scale_ok = scale_ok && ((ok0 && ok1) || !st.live);
-                const uint32_t cw0[4] = {st.w0.x, st.w0.y, st.w0.z, st.w0.w}, cw1[4] = {st.w1.x, st.w1.y, st.w1.z, st.w1.w};
-                const uint32_t xw[16] = {st.x0.x, st.x0.y, st.x0.z, st.x0.w, st.x1.x, st.x1.y, st.x1.z, st.x1.w,
-                                         st.x2.x, st.x2.y, st.x2.z, st.x2.w, st.x3.x, st.x3.y, st.x3.z, st.x3.w};
-#pragma unroll
-                for (int m = 0; m < 8; ++m) {
-                    // Code bytes 2m, 2m+1 of the block: values 4m..4m+3.
-                    const uint32_t wa = cw0[m >> 1] >> (16 * (m & 1)), wb = cw1[m >> 1] >> (16 * (m & 1));
-                    const uint32_t a0 = hmul2_bits(e2m1x2_to_half2(wa & 0xFFu), s0);
-                    const uint32_t a2 = hmul2_bits(e2m1x2_to_half2((wa >> 8) & 0xFFu), s0);
-                    const uint32_t a1 = hmul2_bits(e2m1x2_to_half2(wb & 0xFFu), s1);
-                    const uint32_t a3 = hmul2_bits(e2m1x2_to_half2((wb >> 8) & 0xFFu), s1);
-                    hmma16816(acc, a0, a1, a2, a3, xw[2 * m], xw[2 * m + 1]);
-                }
-            };
-            Step cur, nxt;
-            load(warp, cur);
-            for (int it = warp; it < iters; it += 2 * kGemvWarps) {
-                load(it + kGemvWarps, nxt);
-                mma(cur);
-                load(it + 2 * kGemvWarps, cur);
-                if (it + kGemvWarps < iters)
-                    mma(nxt);
-            }
+            gemv_item(code0, code1, sc0, sc1, p.x + size_t(p0 + tok) * p.K, p.K, warp, acc, scale_ok);
             // Sum the warps' K ranges (fixed order), then warp 0 finishes.
             part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
             __syncthreads();
@@ -835,6 +850,215 @@ __global__ void __launch_bounds__(32 * kGemvWarps) moe_gemv_kernel(const __grid_
     }
     if (!scale_ok && p.status)
         atomicOr(p.status, 2u);
+}
+
+// --------------------------------------------------------- fused decode
+// The whole layer for a few tokens (T <= kDecodeTokens) in one cooperative
+// launch. Every CTA routes all T tokens itself (the same warp code as
+// moe_route_kernel, so the same choices) and converts their rows to fp16 in
+// shared memory; phase 1 deals (routed expert, 8 gate/up outputs) items over
+// the CTAs with the activation written as fp16 rows in slot order; a grid
+// barrier; phase 2 deals (routed expert, 16 down rows) items, fp32 rows in
+// slot order; a grid barrier; phase 3 adds each token's k rows in selection
+// order, as moe_combine_kernel does. Items use the same per-item loop as
+// moe_gemv_kernel, so the outputs are the staged path's. The barrier words
+// are zero at launch and the waits bounded: a grid that cannot meet reports
+// to the watchdog and leaves the outputs.
+constexpr int kDecodeTokens = 8;
+constexpr int kDecodeSlots = kDecodeTokens * kMaxTopK;
+
+struct DecodeParams {
+    const uint8_t *gu_blocks, *gu_scales, *dn_blocks, *dn_scales;
+    const float *gu_bias, *dn_bias;
+    const void* x;  // [T][H] bf16 (x_f32 0) or fp32
+    const float* logits;  // [T][E]
+    __half* act;          // [T * K][I] workspace
+    float* y;             // [T * K][H] workspace
+    float* out;           // [T][H]
+    unsigned* barrier;    // two words, zero at launch
+    unsigned* status;
+    unsigned* watchdog;
+    int T, H, I, E, K, split, act_kind, x_f32;
+    float limit, alpha;
+};
+
+struct DecodeShared {
+    int chosen[kDecodeSlots];
+    float weight[kDecodeSlots];
+    int pos[kDecodeSlots];               // act row of (token, selection)
+    int slot_expert[kDecodeSlots];       // routed experts, ascending
+    int slot_base[kDecodeSlots + 1];     // first act row of each
+    int slot_token[kDecodeSlots];        // token of each act row
+    int slots;
+    float4 part[kGemvWarps][32];
+};
+
+// All CTAs of the (co-resident) grid arrive; false when the wait ran out.
+__device__ bool decode_barrier(unsigned* word, unsigned* watchdog, int* failed) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(word, 1u);
+        uint32_t polls = 0;
+        while (*reinterpret_cast<volatile unsigned*>(word) < gridDim.x) {
+            if (++polls == wait_polls) {
+                atomicOr(watchdog, watchdog_full_barrier);
+                *failed = 1;
+                break;
+            }
+            __nanosleep(64);
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    return !*failed;
+}
+
+__global__ void __launch_bounds__(32 * kGemvWarps) moe_decode_kernel(const __grid_constant__ DecodeParams p) {
+    __shared__ DecodeShared sh;
+    extern __shared__ __align__(16) __half xh[];  // [T][H]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int T = p.T, H = p.H, I = p.I, K = p.K;
+    // Routing of every token (warp per token) and the fp16 rows.
+    for (int tok = warp; tok < T; tok += kGemvWarps)
+        route_token(p.logits + size_t(tok) * p.E, p.E, K, sh.chosen + tok * K, sh.weight + tok * K, nullptr);
+    bool bad = false;
+    for (int i = threadIdx.x; i < T * H / 8; i += blockDim.x) {
+        float2 v[4];
+        if (p.x_f32)
+            load8(static_cast<const float*>(p.x) + size_t(i) * 8, v);
+        else
+            load8(static_cast<const __nv_bfloat16*>(p.x) + size_t(i) * 8, v);
+        uint4 o;
+        __half2* h = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            bad |= fabsf(v[k].x) > 65504.f || fabsf(v[k].y) > 65504.f;
+            h[k] = __floats2half2_rn(v[k].x, v[k].y);
+        }
+        *reinterpret_cast<uint4*>(xh + size_t(i) * 8) = o;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // Routed experts in ascending order, their tokens in token order (the
+        // stable counting sort's order), and each (token, selection)'s row.
+        int n = 0, row = 0;
+        for (int e = 0; e < p.E; ++e) {
+            int cnt = 0;
+            for (int tok = 0; tok < T; ++tok)
+                for (int s = 0; s < K; ++s)
+                    if (sh.chosen[tok * K + s] == e) {
+                        sh.slot_token[row + cnt] = tok;
+                        sh.pos[tok * K + s] = row + cnt;
+                        ++cnt;
+                    }
+            if (cnt) {
+                sh.slot_expert[n] = e;
+                sh.slot_base[n] = row;
+                ++n;
+                row += cnt;
+            }
+        }
+        sh.slot_base[n] = row;
+        sh.slots = n;
+        if (bad && blockIdx.x == 0 && p.status)
+            atomicOr(p.status, 4u);
+    }
+    __syncthreads();
+    const int slots = sh.slots;
+    bool scale_ok = true;
+
+    // Phase 1: gate/up items (slot, 8 outputs).
+    const int chunks1 = I / 8;
+    for (int item = blockIdx.x; item < slots * chunks1; item += gridDim.x) {
+        const int s = item / chunks1, c = item % chunks1, e = sh.slot_expert[s];
+        const int b0 = sh.slot_base[s], count = sh.slot_base[s + 1] - b0;
+        const int j0 = 8 * c + g;
+        const int r0 = p.split ? j0 : 2 * j0, r1 = p.split ? I + j0 : 2 * j0 + 1;  // gate, up rows
+        const size_t N1 = size_t(2) * I;
+        const uint8_t* code0 = p.gu_blocks + (size_t(e) * N1 + r0) * (H / 2);
+        const uint8_t* code1 = p.gu_blocks + (size_t(e) * N1 + r1) * (H / 2);
+        const uint8_t* sc0 = p.gu_scales + (size_t(e) * N1 + r0) * (H / 32);
+        const uint8_t* sc1 = p.gu_scales + (size_t(e) * N1 + r1) * (H / 32);
+        const int tok = sh.slot_token[b0 + min(g, count - 1)];
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        gemv_item(code0, code1, sc0, sc1, xh + size_t(tok) * H, H, warp, acc, scale_ok);
+        sh.part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        __syncthreads();
+        if (warp == 0) {
+            float4 sum = sh.part[0][lane];
+            for (int w = 1; w < kGemvWarps; ++w) {
+                const float4 o = sh.part[w][lane];
+                sum.x += o.x, sum.y += o.y, sum.z += o.z, sum.w += o.w;
+            }
+            const float bg = p.gu_bias ? p.gu_bias[size_t(e) * N1 + r0] : 0.f;
+            const float bu = p.gu_bias ? p.gu_bias[size_t(e) * N1 + r1] : 0.f;
+            const float v0[2] = {sum.x + bg, sum.y + bg}, v1[2] = {sum.z + bu, sum.w + bu};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int tl = 2 * t + h;
+                if (tl < count)
+                    p.act[size_t(b0 + tl) * I + j0] = __float2half_rn(act_fn(v0[h], v1[h], p.act_kind, p.limit, p.alpha));
+            }
+        }
+        __syncthreads();
+    }
+
+    // Every activation row is written before any is read.
+    __shared__ int failed;
+    if (threadIdx.x == 0)
+        failed = 0;
+    if (!decode_barrier(p.barrier, p.watchdog, &failed))
+        return;
+
+    // Phase 2: down items (routed expert, 16 rows), fp32 rows in slot order.
+    const int chunks2 = H / 16;
+    for (int item = blockIdx.x; item < slots * chunks2; item += gridDim.x) {
+        const int s = item / chunks2, c = item % chunks2;
+        const int e = sh.slot_expert[s], b0 = sh.slot_base[s], count = sh.slot_base[s + 1] - b0;
+        const int r0 = 16 * c + g, r1 = r0 + 8;
+        const uint8_t* code0 = p.dn_blocks + (size_t(e) * H + r0) * (I / 2);
+        const uint8_t* code1 = p.dn_blocks + (size_t(e) * H + r1) * (I / 2);
+        const uint8_t* sc0 = p.dn_scales + (size_t(e) * H + r0) * (I / 32);
+        const uint8_t* sc1 = p.dn_scales + (size_t(e) * H + r1) * (I / 32);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        gemv_item(code0, code1, sc0, sc1, p.act + size_t(b0 + min(g, count - 1)) * I, I, warp, acc, scale_ok);
+        sh.part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        __syncthreads();
+        if (warp == 0) {
+            float4 sum = sh.part[0][lane];
+            for (int w = 1; w < kGemvWarps; ++w) {
+                const float4 o = sh.part[w][lane];
+                sum.x += o.x, sum.y += o.y, sum.z += o.z, sum.w += o.w;
+            }
+            const float b_0 = p.dn_bias ? p.dn_bias[size_t(e) * H + r0] : 0.f;
+            const float b_1 = p.dn_bias ? p.dn_bias[size_t(e) * H + r1] : 0.f;
+            const float v0[2] = {sum.x + b_0, sum.y + b_0}, v1[2] = {sum.z + b_1, sum.w + b_1};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int tl = 2 * t + h;
+                if (tl < count) {
+                    p.y[size_t(b0 + tl) * H + r0] = v0[h];
+                    p.y[size_t(b0 + tl) * H + r1] = v1[h];
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (!scale_ok && p.status)
+        atomicOr(p.status, 2u);
+    if (!decode_barrier(p.barrier + 1, p.watchdog, &failed))
+        return;
+
+    // Phase 3: each token's k rows in selection order.
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < size_t(T) * H;
+         i += size_t(gridDim.x) * blockDim.x) {
+        const int tok = int(i / H), d = int(i % H);
+        float acc = 0.f;
+        for (int k = 0; k < K; ++k)
+            acc = fmaf(sh.weight[tok * K + k], p.y[size_t(sh.pos[tok * K + k]) * H + d], acc);
+        p.out[i] = acc;
+    }
 }
 
 // ------------------------------------------------------------- host side
@@ -1233,6 +1457,75 @@ namespace kb200 {
 namespace {
 
 // The whole layer over token rows x (bf16, or fp32 when x_f32).
+// The fused decode kernel takes the layer for at most kDecodeAuto tokens
+// (measured on B200 at the gpt-oss-20b shape: T=1 47 us against 54 us
+// staged, T=8 219 us against 175 us), rows that fit its shared memory, unless
+// KB200_MOE_DECODE=0 or a staged path named by KB200_MOE_PATH says otherwise;
+// KB200_MOE_DECODE=1 takes it up to kDecodeTokens (both read at every call).
+constexpr int kDecodeAuto = 2;
+
+bool decode_eligible(const kb200_moe_weights* w, size_t tokens) {
+    size_t most = size_t(kDecodeAuto);
+    if (const char* v = std::getenv("KB200_MOE_DECODE")) {
+        if (std::strcmp(v, "0") == 0)
+            return false;
+        if (std::strcmp(v, "1") == 0)
+            most = size_t(kDecodeTokens);
+    }
+    if (std::getenv("KB200_MOE_PATH"))
+        return false;
+    return tokens <= most && w->top_k <= kMaxTopK && w->hidden <= kMaxK && w->hidden % 16 == 0 && w->inter % 8 == 0;
+}
+
+int decode_launch(const kb200_moe_weights* w, const void* x, bool x_f32, const float* logits, size_t tokens, float* out,
+                  const Workspace& ws, unsigned* status, cudaStream_t stream) {
+    // Co-resident CTAs per SM for each token count (the rows' shared memory
+    // grows with it), queried once per device.
+    static int blocks_per_sm[64][kDecodeTokens + 1] = {};
+    static std::mutex lock;
+    constexpr size_t kMaxDyn = size_t(kDecodeTokens) * kMaxK * sizeof(__half);
+    const size_t dyn = tokens * size_t(w->hidden) * sizeof(__half);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64)
+        return fail(KB200_UNSUPPORTED, "device index above 63");
+    {
+        std::lock_guard<std::mutex> guard(lock);
+        int& slot = blocks_per_sm[dev][tokens];
+        if (!slot) {
+            cudaError_t e = cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 int(kMaxDyn));
+            int n = 0;
+            if (e == cudaSuccess)
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, moe_decode_kernel, 32 * kGemvWarps,
+                                                                  tokens * size_t(kMaxK) * sizeof(__half));
+            if (e != cudaSuccess)
+                return cuda_fail(e, "moe_decode_kernel set-up");
+            slot = n > 0 ? n : 1;
+        }
+    }
+    DecodeParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.gu_blocks = w->gate_up_blocks, p.gu_scales = w->gate_up_scales, p.gu_bias = w->gate_up_bias;
+    p.dn_blocks = w->down_blocks, p.dn_scales = w->down_scales, p.dn_bias = w->down_bias;
+    p.x = x, p.logits = logits, p.act = ws.act, p.y = ws.y, p.out = out;
+    p.barrier = reinterpret_cast<unsigned*>(ws.counts);
+    p.status = status, p.watchdog = watchdog_word();
+    p.T = int(tokens), p.H = w->hidden, p.I = w->inter, p.E = w->experts, p.K = w->top_k;
+    p.split = w->interleaved ? 0 : 1, p.act_kind = w->activation, p.x_f32 = x_f32 ? 1 : 0;
+    p.limit = w->limit, p.alpha = w->alpha;
+    cudaError_t e = cudaMemsetAsync(p.barrier, 0, 2 * sizeof(unsigned), stream);
+    if (e != cudaSuccess)
+        return cuda_fail(e, "decode barrier reset");
+    // Co-resident CTAs only (the grid barrier waits for all of them).
+    const int grid = sm_count() * std::min(blocks_per_sm[dev][tokens], 8);
+    void* args[] = {&p};
+    TraceScope trace(KB200_KERNEL_MOE_DECODE, stream);
+    e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(moe_decode_kernel), dim3(grid),
+                                    dim3(32 * kGemvWarps), args, dyn, stream);
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "moe_decode_kernel launch");
+}
+
 int forward_layer(const kb200_moe_weights* w, const void* x, bool x_f32, const float* logits, size_t tokens, float* out,
                   void* workspace, size_t workspace_bytes, unsigned* status, void* stream_ptr) {
     if (const int s = check_weights(w))
@@ -1252,6 +1545,8 @@ int forward_layer(const kb200_moe_weights* w, const void* x, bool x_f32, const f
     if (!encoder())
         return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
     auto stream = static_cast<cudaStream_t>(stream_ptr);
+    if (decode_eligible(w, tokens))
+        return decode_launch(w, x, x_f32, logits, tokens, out, ws, status, stream);
     if (const int s = dispatch_launch(logits, x, tokens, w->hidden, w->experts, w->top_k, ws, status, stream, x_f32))
         return s;
     if (const int s = experts_launch(w, ws.xs, ws.offsets, ws.mtile, n, ws.act, ws.y, status, stream))

@@ -313,3 +313,37 @@ def test_shared_expert_composition(kb, oracle, cuda):
     assert rel_err(y.cpu().numpy(), want) <= 1e-3
     # silu_mul alone is elementwise float arithmetic.
     assert rel_err(sd.cpu().numpy(), oracle.silu_mul(gd.cpu().numpy(), ud.cpu().numpy())) <= 1e-6
+
+
+@pytest.mark.parametrize("T,E,H,I,K,interleaved,activation,bias", [
+    (1, 8, 256, 128, 2, True, 0, False), (5, 8, 256, 128, 2, False, 0, True), (8, 8, 256, 128, 2, True, 1, True),
+    (1, 32, 2880, 2880, 4, True, 0, False), (8, 32, 2880, 2880, 4, True, 0, False), (3, 64, 512, 256, 8, False, 1, False)])
+def test_moe_decode_kernel_matches_staged_path(kb, oracle, cuda, monkeypatch, T, E, H, I, K, interleaved, activation,
+                                               bias):
+    """The fused decode kernel (one cooperative launch: routing in every CTA,
+    gate/up, a grid barrier, down, a grid barrier, the combine; taken by
+    default up to 2 tokens and, with KB200_MOE_DECODE=1, up to 8) runs the
+    staged path's per-item arithmetic in the same order, so its outputs equal
+    the staged path's (route, sort, gather, grouped GEMVs, combine) to the
+    last bit, and both stay within the oracle's tolerance."""
+    import torch
+
+    w, dev, host = layer(kb, cuda, E=E, H=H, I=I, K=K, seed=T + E + K, interleaved=interleaved,
+                         activation=activation, bias=bias)
+    x, logits, xb, ld = inputs(cuda, T, H, E, seed=T + 11)
+    outs = {}
+    for name, flag in (("fused", "1"), ("staged", "0")):
+        monkeypatch.setenv("KB200_MOE_DECODE", flag)
+        status = torch.zeros(1, dtype=torch.int32, device=cuda)
+        with kb.Phase() as ph:
+            outs[name] = kb.moe_forward(w, xb, ld, status=status)
+            torch.cuda.synchronize()
+            ks = ph.snapshot()["kernels"]
+        ph.close()
+        assert status.item() == 0
+        assert ("moe_decode_kernel" in ks) == (name == "fused"), ks.keys()
+    assert torch.equal(outs["fused"], outs["staged"])
+    args = dict(hidden=H, inter=I, experts=E, top_k=K, gu_bias=host["gu_b"], dn_bias=host["dn_b"],
+                activation=activation, interleaved=int(interleaved))
+    ref16 = oracle.moe_forward(x, logits, host["gu_w"], host["gu_s"], host["dn_w"], host["dn_s"], round_act=2, **args)
+    assert rel_err(outs["fused"].cpu().numpy(), ref16) <= 1e-3
