@@ -238,6 +238,18 @@ def graph_of(torch, stream, fn):
     return graph
 
 
+def launches_of(kb, torch, stream, fn) -> dict:
+    """The library's kernel launches of one eager call of fn() on `stream`,
+    by kernel name (telemetry phase: every launch is counted)."""
+    with kb.Phase() as phase:
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize()
+        snap = phase.snapshot()
+    phase.close()
+    return {k: v["calls"] for k, v in snap["kernels"].items()}
+
+
 def time_graph(torch, stream, graph, reps: int, warm: int = 1) -> float:
     """ms per replay of `graph` on `stream` (CUDA events on that stream)."""
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -366,6 +378,8 @@ def run_default(args, rank, world, local_rank):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     names = [",".join(p.name for p in g) for g in groups]
     group_graphs = [graph_of(torch, stream, lambda gi=gi: stack.launch(stream, gi)) for gi in range(len(groups))]
+    group_kernels = [launches_of(kb, torch, stream, lambda gi=gi: stack.launch(stream, gi)) for gi in range(len(groups))]
+    launches_per_step = sum(sum(k.values()) for k in group_kernels)
     if dist:
         dist.barrier()
     with ClockSampler(local_rank) as clocks:
@@ -384,17 +398,16 @@ def run_default(args, rank, world, local_rank):
     clock = clocks.summary()
     group_graphs = None
 
-    per_launch = 2 if dist and reducer else 1
     launches = []
     for gi, g in enumerate(groups):
         nbytes = sum(tp.shard(p, world, rank).out_count * tp.shard_pitch(p, tp.shard(p, world, rank)) for p in g)
         us = group_ms[gi] / layers * 1e3
-        row = any(p.mode == "row" for p in g) and dist is not None
-        kernel = ("gemv_q6k_pair_kernel<3>" if tokens <= 2 else "gemv_q6k_mma_kernel<1,3>") if g[0].encoding == kb.Q6_K \
+        main = ("gemv_q6k_pair_kernel<3>" if tokens <= 2 else "gemv_q6k_mma_kernel<1,3>") if g[0].encoding == kb.Q6_K \
             else "gemv_q4k_mma_kernel<1>"
-        if row and reducer:
-            kernel += " + peer_allreduce_kernel (gather)" if reducer.fused else " + peer_allreduce_kernel"
+        kernel = " + ".join(main if k.startswith(main.split("<")[0]) else k
+                            for k in sorted(group_kernels[gi], key=lambda k: k.startswith("gemv")))
         launches.append({"launch": names[gi], "kernel": kernel, "bytes": nbytes, "us": round(us, 2),
+                         "kernel_launches_per_layer": {k: v // layers for k, v in group_kernels[gi].items()},
                          "gbps": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / pk["hbm_gbs"], 4),
                          "share": round(group_ms[gi] / sum(group_ms), 4)})
     top = max(range(len(groups)), key=lambda i: group_ms[i])
@@ -518,12 +531,12 @@ def run_default(args, rank, world, local_rank):
                                  "GEMV epilogue stores to peers + gather kernel (fp32, NVLink)" if reducer and
                                  reducer.fused else "peer-memory all-reduce kernel (fp32)" if reducer else
                                  "NCCL all-reduce (fp32)") + (" after o and down" if world > 1 else ""),
-                  "launch": f"one CUDA graph per step, {len(groups) + (2 if dist and reducer else 0)} launches "
-                            "per layer"},
+                  "launch": f"one CUDA graph per step, {launches_per_step // layers} launches per layer"},
         "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
-        "gpu_launches": args.steps * layers * (len(groups) + (2 if dist and reducer else 0)),
-        "gpu_launches_note": "kernel launches of the timed graph replays (one GEMV launch per dependency group, "
-                             "plus one gather kernel per row-parallel group at N > 1)",
+        "gpu_launches": args.steps * launches_per_step,
+        "gpu_launches_note": "the library's kernel launches of the timed graph replays: per step, the launches "
+                             "telemetry counts for one eager call of the captured work (GEMV, Q6_K activation "
+                             "quantisation, and the gather kernel of a row-parallel group at N > 1)",
         "launches": launches,
         "roofline": {"bound": "hbm", "kernel": f"{dom['kernel']} ([{dom['launch']}] launch)",
                      "achieved": dom["gbps"], "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": dom["frac"],

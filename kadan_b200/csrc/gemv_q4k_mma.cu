@@ -82,6 +82,7 @@ struct alignas(64) MmaJob {
     const float* input;
     float* output;
     unsigned* status;
+    const uint8_t* staged;  // Q6_K pair kernel: quantised activations, chunk after chunk (or null)
     uint32_t stride, in, columns, rows;
     uint32_t first_tile, first_unit;  // prefix of tiles / of tiles x nblocks
     uint32_t row_groups, group_rows, nblocks;
@@ -1139,12 +1140,23 @@ __host__ __device__ constexpr int pair_segment_blocks(int rows, int budget) {
     return budget / (rows * kPairTokenBlock) / kQ6Chunk * kQ6Chunk;
 }
 
+// Chunk of kQ6Chunk blocks in the pair layout (the staged path's unit): B
+// words, X words and scales of `rows` tokens, 580 bytes per (block, token).
+__host__ __device__ constexpr int pair_chunk_bytes(int rows) {
+    return kQ6Chunk * rows * kPairTokenBlock;
+}
+
 // S stages, W consumer warps (each takes kQ6Chunk / W blocks of a stage).
-template <int S, int W = kWarps> struct PairLayout {
+// kStaged: a stage also holds its chunk's quantised activations (up to two
+// tokens, copied from the launch's staging buffer), and there is no
+// per-CTA activation window.
+template <int S, int W = kWarps, bool kStaged = false> struct PairLayout {
     static constexpr int kStages = S;
+    // A stage starts on a 128-byte boundary (the TMA tile destination).
+    static constexpr int kStageBytes = (kQ6StageBytes + (kStaged ? pair_chunk_bytes(2) : 0) + 127) / 128 * 128;
     static constexpr int kStagesOff = 0;
-    static constexpr int kSegOff = kStages * kQ6StageBytes;
-    static constexpr int kSegBudget = pair_seg_budget<S>();
+    static constexpr int kSegOff = kStages * kStageBytes;
+    static constexpr int kSegBudget = kStaged ? 0 : pair_seg_budget<S>();
     static constexpr int kRedOff = kSegOff + kSegBudget;
     static constexpr int kRedBytes = 32 * W * 4 * 4;
     static constexpr int kBarOff = kRedOff + kRedBytes;
@@ -1152,6 +1164,11 @@ template <int S, int W = kWarps> struct PairLayout {
 };
 static_assert(2 * (PairLayout<3>::kTotal + 128 + 1024) <= 228 * 1024, "two Q6_K pair CTAs per SM");
 static_assert(3 * (PairLayout<2>::kTotal + 128 + 1024) <= 228 * 1024, "three Q6_K pair CTAs per SM (2 stages)");
+static_assert(2 * (PairLayout<3, kWarps, true>::kTotal + 128 + 1024) <= 228 * 1024, "two staged pair CTAs per SM");
+static_assert(3 * (PairLayout<2, kWarps, true>::kTotal + 128 + 1024) <= 228 * 1024, "three staged pair CTAs per SM");
+static_assert(kQ6StageBytes % 128 == 0 && PairLayout<3, kWarps, true>::kStageBytes % 128 == 0,
+              "tensor copies land on 128-byte boundaries");
+static_assert(pair_chunk_bytes(1) % 16 == 0, "bulk copy sizes and source offsets are multiples of 16 bytes");
 
 struct PairSegment {
     int blocks, rows, off;
@@ -1163,6 +1180,73 @@ struct PairSegment {
         return reinterpret_cast<float*>(xwords(smem) + blocks * rows * (kPairXBytes / 4));
     }
 };
+
+// Quantises one (block, token) item: lane L holds values 8L..8L+7 of the
+// block in v and writes its B words, X bytes and (lane 0) the scale into a
+// pair-layout area of `blocks` blocks x `rows` tokens at words / xbytes /
+// scales (shared or global memory).
+__device__ __forceinline__ void pair_quant_store(const float (&v)[8], uint32_t* words, uint8_t* xbytes, float* scales,
+                                                 int rows, int blk, int tok, int lane) {
+    const int s = lane >> 1, half = lane & 1;
+    const int ip = s >> 3, qt = (s >> 1) & 3, par = s & 1;
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        m = fmaxf(m, fabsf(v[i]));
+    m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+    // 1/s to within an ulp: the levels below absorb it (x ~ s (h + l / 254)
+    // with s = m / 127 exactly as stored).
+    const float inv = m > 0.f ? 127.f * __frcp_rn(m) : 0.f;
+    // x ~ s (h + l / 254): h = round(x / s), l = round(254 (x / s - h)).
+    const float2 inv2 = make_float2(inv, inv), magic = make_float2(kMagic, kMagic);
+    const float2 neg_magic = make_float2(-kMagic, -kMagic), k254 = make_float2(254.f, 254.f);
+    int h[8], l[8];
+    int xh = 0, xl = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        const float2 y = mul2(make_float2(v[i], v[i + 1]), inv2);
+        const float2 r1 = add2(y, magic);
+        const float2 d = sub2(y, add2(r1, neg_magic));
+        const float2 r2 = fma2(d, k254, magic);
+        h[i] = int(__float_as_uint(r1.x) << 10) >> 10, h[i + 1] = int(__float_as_uint(r1.y) << 10) >> 10;
+        l[i] = int(__float_as_uint(r2.x) << 10) >> 10, l[i + 1] = int(__float_as_uint(r2.y) << 10) >> 10;
+        xh += h[i] + h[i + 1];
+        xl += l[i] + l[i + 1];
+    }
+    // B words of this lane: pair p, parity par, t = 2 half + {0, 1}.
+    uint32_t* w = words + ((blk * 8 + 4 * ip + qt) * rows + tok) * 16 + par * 8 + 2 * half;
+    w[0] = pack4(h[0], h[1], h[2], h[3]);
+    w[1] = pack4(h[4], h[5], h[6], h[7]);
+    w[4] = pack4(l[0], l[1], l[2], l[3]);
+    w[5] = pack4(l[4], l[5], l[6], l[7]);
+    // Sub-block sums (both halves), split X = 64 X1 + X0, X0 in [-32, 31].
+    xh += __shfl_xor_sync(0xffffffffu, xh, 1);
+    xl += __shfl_xor_sync(0xffffffffu, xl, 1);
+    if (!half) {
+        uint8_t* xb = xbytes + (blk * rows + tok) * kPairXBytes + (s & 3);
+        const int h1 = (xh + 32) >> 6, l1 = (xl + 32) >> 6;
+        // [digit][hl][t = s / 4][byte s % 4]
+        xb[(0 * 2 + 0) * 16 + (s >> 2) * 4] = uint8_t(h1);
+        xb[(0 * 2 + 1) * 16 + (s >> 2) * 4] = uint8_t(l1);
+        xb[(1 * 2 + 0) * 16 + (s >> 2) * 4] = uint8_t(xh - 64 * h1);
+        xb[(1 * 2 + 1) * 16 + (s >> 2) * 4] = uint8_t(xl - 64 * l1);
+    }
+    if (lane == 0)
+        scales[blk * rows + tok] = m > 0.f ? m / 127.f : 0.f;
+}
+
+// Values 8 lane .. 8 lane + 7 of 256 at xr (16-byte vectors when `vec`).
+__device__ __forceinline__ void load_lane8(float (&v)[8], const float* xr, bool vec) {
+    if (vec) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(xr)), b = __ldg(reinterpret_cast<const float4*>(xr) + 1);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+        v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            v[i] = __ldg(xr + i);
+    }
+}
 
 // Quantise super-blocks [blk0, blk0 + nblk) of the segment's tokens into the
 // pair layout: one warp per (block, token); lane L owns values 8L..8L+7 (half
@@ -1177,8 +1261,6 @@ __device__ void prep_pairs(uint8_t* smem, const PairSegment& seg, const float* x
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (in & 3) == 0;
     const int items = nblk * rows;
-    const int s = lane >> 1, half = lane & 1;
-    const int ip = s >> 3, qt = (s >> 1) & 3, par = s & 1;
     constexpr int kBatch = 4;
     for (int base = warp; base < items; base += W * kBatch) {
         float v[kBatch][8];
@@ -1186,72 +1268,61 @@ __device__ void prep_pairs(uint8_t* smem, const PairSegment& seg, const float* x
         for (int q = 0; q < kBatch; ++q) {
             const int item = min(base + q * W, items - 1);
             const int blk = item / rows, tok = item % rows;
-            const float* xr = x + size_t(tok) * in + size_t(blk0 + blk) * 256 + lane * 8;
-            if (vec) {
-                const float4 a = __ldg(reinterpret_cast<const float4*>(xr)), b = __ldg(reinterpret_cast<const float4*>(xr) + 1);
-                v[q][0] = a.x, v[q][1] = a.y, v[q][2] = a.z, v[q][3] = a.w;
-                v[q][4] = b.x, v[q][5] = b.y, v[q][6] = b.z, v[q][7] = b.w;
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    v[q][i] = __ldg(xr + i);
-            }
+            load_lane8(v[q], x + size_t(tok) * in + size_t(blk0 + blk) * 256 + lane * 8, vec);
         }
 #pragma unroll
         for (int q = 0; q < kBatch; ++q) {
             const int item = base + q * W;
             if (item >= items)
                 break;
-            const int blk = item / rows, tok = item % rows;
-            float m = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                m = fmaxf(m, fabsf(v[q][i]));
-            m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
-            // 1/s to within an ulp: the levels below absorb it (x ~ s (h + l / 254)
-            // with s = m / 127 exactly as stored).
-            const float inv = m > 0.f ? 127.f * __frcp_rn(m) : 0.f;
-            // x ~ s (h + l / 254): h = round(x / s), l = round(254 (x / s - h)).
-            const float2 inv2 = make_float2(inv, inv), magic = make_float2(kMagic, kMagic);
-            const float2 neg_magic = make_float2(-kMagic, -kMagic), k254 = make_float2(254.f, 254.f);
-            int h[8], l[8];
-            int xh = 0, xl = 0;
-#pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                const float2 y = mul2(make_float2(v[q][i], v[q][i + 1]), inv2);
-                const float2 r1 = add2(y, magic);
-                const float2 d = sub2(y, add2(r1, neg_magic));
-                const float2 r2 = fma2(d, k254, magic);
-                h[i] = int(__float_as_uint(r1.x) << 10) >> 10, h[i + 1] = int(__float_as_uint(r1.y) << 10) >> 10;
-                l[i] = int(__float_as_uint(r2.x) << 10) >> 10, l[i + 1] = int(__float_as_uint(r2.y) << 10) >> 10;
-                xh += h[i] + h[i + 1];
-                xl += l[i] + l[i + 1];
-            }
-            // B words of this lane: pair p, parity par, t = 2 half + {0, 1}.
-            uint32_t* w = words + ((blk * 8 + 4 * ip + qt) * rows + tok) * 16 + par * 8 + 2 * half;
-            w[0] = pack4(h[0], h[1], h[2], h[3]);
-            w[1] = pack4(h[4], h[5], h[6], h[7]);
-            w[4] = pack4(l[0], l[1], l[2], l[3]);
-            w[5] = pack4(l[4], l[5], l[6], l[7]);
-            // Sub-block sums (both halves), split X = 64 X1 + X0, X0 in [-32, 31].
-            xh += __shfl_xor_sync(0xffffffffu, xh, 1);
-            xl += __shfl_xor_sync(0xffffffffu, xl, 1);
-            if (!half) {
-                uint8_t* xb = xbytes + (blk * rows + tok) * kPairXBytes + (s & 3);
-                const int h1 = (xh + 32) >> 6, l1 = (xl + 32) >> 6;
-                // [digit][hl][t = s / 4][byte s % 4]
-                xb[(0 * 2 + 0) * 16 + (s >> 2) * 4] = uint8_t(h1);
-                xb[(0 * 2 + 1) * 16 + (s >> 2) * 4] = uint8_t(l1);
-                xb[(1 * 2 + 0) * 16 + (s >> 2) * 4] = uint8_t(xh - 64 * h1);
-                xb[(1 * 2 + 1) * 16 + (s >> 2) * 4] = uint8_t(xl - 64 * l1);
-            }
-            if (lane == 0)
-                scales[blk * rows + tok] = m > 0.f ? m / 127.f : 0.f;
+            pair_quant_store(v[q], words, xbytes, scales, rows, item / rows, item % rows, lane);
         }
     }
 }
 
+// Inputs of one pair-layout quantisation launch: each region is one distinct
+// input (x, in, rows) of a GEMV launch, written chunk after chunk at dst.
+struct PairQuantRegion {
+    const float* x;
+    uint8_t* dst;
+    uint32_t in, rows, first_item;  // items: blocks x rows, prefix over regions
+};
+struct PairQuantParams {
+    PairQuantRegion regions[kMaxJobsQ];
+    uint32_t count, items;
+};
 
+// Quantises every (block, token) of the launch's inputs once into the
+// staging buffer the GEMV's producer copies from, one warp per item. Waits
+// for the previous kernel of the stream (which may write the inputs) and
+// lets the GEMV that follows start streaming weights at once.
+__global__ void __launch_bounds__(128) pair_quant_kernel(const __grid_constant__ PairQuantParams p) {
+    if (threadIdx.x == 0)
+        grid_dependents_launch();
+    grid_dependency_wait();
+    const int lane = threadIdx.x & 31;
+    const uint32_t warps = gridDim.x * (blockDim.x >> 5);
+    for (uint32_t item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < p.items; item += warps) {
+        uint32_t r = 0;
+        while (r + 1 < p.count && item >= p.regions[r + 1].first_item)
+            ++r;
+        const PairQuantRegion& g = p.regions[r];
+        const int rows = int(g.rows);
+        const uint32_t local = item - g.first_item;
+        const int blk = int(local / g.rows), tok = int(local % g.rows);
+        const int chunk = blk / kQ6Chunk, b = blk % kQ6Chunk;
+        uint8_t* base = g.dst + size_t(chunk) * pair_chunk_bytes(rows);
+        uint32_t* words = reinterpret_cast<uint32_t*>(base);
+        uint8_t* xbytes = base + kQ6Chunk * rows * kPairWordBytes;
+        float* scales = reinterpret_cast<float*>(xbytes + kQ6Chunk * rows * kPairXBytes);
+        const bool vec = (reinterpret_cast<uintptr_t>(g.x) & 15u) == 0 && (g.in & 3) == 0;
+        float v[8];
+        load_lane8(v, g.x + size_t(tok) * g.in + size_t(blk) * 256 + lane * 8, vec);
+        pair_quant_store(v, words, xbytes, scales, rows, b, tok, lane);
+    }
+    // The GEMV reads the buffer with bulk async copies.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 
 // Code word of 4 values: low nibbles (shift `ls`) and the high bit pairs
 // placed at bits 4-5 (qh moved by `hs`: left when positive).
@@ -1342,9 +1413,18 @@ __device__ __forceinline__ void q6k_pair_block(const uint8_t* bg, const uint8_t*
 // Q6_K decode GEMV for one or two input rows per pass: the Q6_K kernel's
 // tiles, stages, pieces, fixup and programmatic dependent launch, with the
 // paired-sub-block inner loop above.
-template <int S, int W>
+//
+// kStaged: the activations come quantised from the launch's staging buffer
+// (pair_quant_kernel, launched just before): the producer copies chunk ch's
+// slice with the chunk's weights into the same stage, so consumers never
+// quantise and never wait at a window refill. The producer issues the first
+// S weight loads before it waits for the quantisation kernel, then the
+// activation copies of those stages, then both parts of every later stage.
+// Otherwise each CTA quantises a window of activations into shared memory
+// whenever its chunks leave the current one.
+template <int S, int W, bool kStaged>
 __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_kernel(const __grid_constant__ MmaParams p) {
-    using L = PairLayout<S, W>;
+    using L = PairLayout<S, W, kStaged>;
     constexpr int kStages = L::kStages;
     constexpr int CT = 32 * W;               // consumer threads
     constexpr int kPerWarp = kQ6Chunk / W;   // blocks of a stage per consumer warp
@@ -1373,11 +1453,26 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
         if (lane != 0)
             return;
         uint32_t it = 0;
+        // Staged: activation copies of the first stages, held back until the
+        // quantisation kernel has finished.
+        bool staged_ready = false;
+        const uint8_t* held_src[kStages];
+        uint32_t held_bytes[kStages];
+        uint32_t held = 0;
+        auto release_held = [&] {
+            grid_dependency_wait();
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            staged_ready = true;
+            for (uint32_t k = 0; k < held; ++k)
+                bulk_g2s(smem + L::kStagesOff + k * L::kStageBytes + kQ6StageBytes, held_src[k], held_bytes[k], &full[k]);
+            held = 0;
+        };
         PieceIter pieces(p);
         Piece pc;
         while (pieces.next(p, pc)) {
             const MmaJob& job = p.jobs[pc.job];
             const int row0 = int((pc.tile / job.row_groups) * uint32_t(kQ6Rows));
+            const uint32_t act_bytes = kStaged ? uint32_t(pair_chunk_bytes(int(job.rows))) : 0u;
             asm volatile("prefetch.tensormap [%0];" ::"l"(&job.map) : "memory");
             for (uint32_t ch = pc.k0; ch < pc.k1; ++ch, ++it) {
                 const int slot = int(it % kStages);
@@ -1385,11 +1480,24 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
                     atomicExch(abort_flag, 1);
                 if (*reinterpret_cast<volatile int*>(abort_flag))
                     goto drain;
-                mbar_expect_tx(&full[slot], uint32_t(kQ6StageBytes));
-                tma_load_2d(smem + L::kStagesOff + slot * kQ6StageBytes, &job.map, int(ch) * (kQ6Chunk * kQ6Block / 8),
-                            row0, &full[slot]);
+                uint8_t* stage = smem + L::kStagesOff + slot * L::kStageBytes;
+                mbar_expect_tx(&full[slot], uint32_t(kQ6StageBytes) + act_bytes);
+                tma_load_2d(stage, &job.map, int(ch) * (kQ6Chunk * kQ6Block / 8), row0, &full[slot]);
+                if constexpr (kStaged) {
+                    const uint8_t* src = job.staged + size_t(ch) * act_bytes;
+                    if (staged_ready) {
+                        bulk_g2s(stage + kQ6StageBytes, src, act_bytes, &full[slot]);
+                    } else {
+                        held_src[held] = src, held_bytes[held] = act_bytes;
+                        if (++held == uint32_t(kStages))
+                            release_held();
+                    }
+                }
             }
         }
+        if constexpr (kStaged)
+            if (!staged_ready)
+                release_held();
     drain:
         for (uint32_t k = 0; k < kStages && k < it; ++k) {
             const uint32_t last = it - 1 - k;
@@ -1419,12 +1527,9 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
         const int rows = int(min(job.group_rows, job.rows - r0));
         const int nblocks = int(job.in / 256);
         const float* x = job.input + size_t(r0) * job.in;
-        const PairSegment seg(rows, L::kSegOff, L::kSegBudget);
-        if (seg.blocks < kQ6Chunk)
+        const PairSegment seg(rows, kStaged ? 0 : L::kSegOff, kStaged ? pair_chunk_bytes(rows) : L::kSegBudget);
+        if (!kStaged && seg.blocks < kQ6Chunk)
             atomicExch(abort_flag, 1);
-        const uint32_t* words = seg.words(smem);
-        const uint32_t* xwords = seg.xwords(smem);
-        const float* scales = seg.scales(smem);
         // B side: the token of the column this lane supplies (g / 4) and its
         // word in every group of 16; C side: the token of the columns it
         // receives (t / 2). Both clamped to the rows present.
@@ -1440,29 +1545,40 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
             const int slot = int(it % kStages);
             const int blk_first = int(ch) * kQ6Chunk;
             const int nb = min(kQ6Chunk, nblocks - blk_first);
-            if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
-                && seg.blocks >= kQ6Chunk) {
-                // The CTA's last piece needs only its own chunks.
-                const bool last = pieces.cur >= pieces.end;
-                const int start = last || nblocks > seg.blocks ? blk_first : 0;
-                const int count = min(seg.blocks, (last ? min(nblocks, int(pc.k1) * kQ6Chunk) : nblocks) - start);
-                await_dependency();
-                named_sync(1, CT);
-                prep_pairs<W>(smem, seg, x, job.in, start, count);
-                named_sync(1, CT);
-                seg_x = x, seg_rows = rows, seg_blk0 = start, seg_nblk = count;
+            uint8_t* stage = smem + L::kStagesOff + slot * L::kStageBytes;
+            // Activations of this chunk: the stage's own slice (staged) or the
+            // CTA's window, refilled when the chunk leaves it.
+            uint8_t* act_base = stage + kQ6StageBytes;
+            int act_blk0 = blk_first;
+            if constexpr (!kStaged) {
+                act_base = smem;
+                if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
+                    && seg.blocks >= kQ6Chunk) {
+                    // The CTA's last piece needs only its own chunks.
+                    const bool last = pieces.cur >= pieces.end;
+                    const int start = last || nblocks > seg.blocks ? blk_first : 0;
+                    const int count = min(seg.blocks, (last ? min(nblocks, int(pc.k1) * kQ6Chunk) : nblocks) - start);
+                    await_dependency();
+                    named_sync(1, CT);
+                    prep_pairs<W>(smem, seg, x, job.in, start, count);
+                    named_sync(1, CT);
+                    seg_x = x, seg_rows = rows, seg_blk0 = start, seg_nblk = count;
+                }
+                act_blk0 = seg_blk0;
             }
+            const uint32_t* words = seg.words(act_base);
+            const uint32_t* xwords = seg.xwords(act_base);
+            const float* scales = seg.scales(act_base);
             const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
             if (!aborted && !mbar_wait(&full[slot], (it / kStages) & 1u, watchdog_full_barrier, p.watchdog))
                 atomicExch(abort_flag, 1);
             if (!aborted) {
-                const uint8_t* stage = smem + L::kStagesOff + slot * kQ6StageBytes;
 #pragma unroll
                 for (int bb = 0; bb < kPerWarp; ++bb) {
                     const int b = kPerWarp * ks + bb;  // block of the chunk; odd b sits 2 bytes off a word
                     if (b >= nb)
                         break;
-                    const int sblk = blk_first + b - seg_blk0;
+                    const int sblk = blk_first + b - act_blk0;
                     const uint8_t* bg = stage + g * (kQ6Chunk * kQ6Block) + b * kQ6Block;
                     const uint8_t* b8 = bg + 8 * (kQ6Chunk * kQ6Block);
                     const uint32_t* bw = words + (sblk * 8 * rows + btok) * 16 + lane_word;
@@ -1577,6 +1693,43 @@ const Fixup* fixup_for(cudaStream_t stream) {
     return &f;
 }
 
+// Staging buffer of the pair kernel's quantised activations for one (device,
+// stream). The quantisation kernel writes it after its grid-dependency wait
+// (the previous kernel of the stream is done) and the GEMV after it reads it
+// after its own, so the launches of one stream share it. Allocated by the
+// first call outside graph capture and never moved or freed: captured graphs
+// hold its address. A launch whose inputs do not fit falls back to per-CTA
+// quantisation.
+constexpr size_t kStagingBytes = size_t(8) << 20;
+
+struct StagingTable {
+    std::mutex lock;
+    std::map<std::pair<int, cudaStream_t>, uint8_t*> table;
+};
+
+uint8_t* staging_for(cudaStream_t stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return nullptr;
+    static StagingTable t;
+    std::lock_guard<std::mutex> guard(t.lock);
+    uint8_t*& buf = t.table[{dev, stream}];
+    if (buf)
+        return buf;
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess || capture != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    void* p = nullptr;
+    if (cudaMalloc(&p, kStagingBytes) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    buf = static_cast<uint8_t*>(p);
+    return buf;
+}
+
 struct Tuning {
     bool balanced = true;  // KB200_GEMV_BALANCED=0: whole tiles round-robin
     uint32_t prefetch = 0; // KB200_GEMV_L2_PREFETCH=<stages>
@@ -1585,6 +1738,7 @@ struct Tuning {
     int ctas_per_sm = 0;                        // KB200_GEMV_CTAS_PER_SM=<n>: grid slots per SM (0: all that fit)
     int q6_stages = 3;                          // KB200_GEMV_Q6K_STAGES=2|3: ring depth at 1-4 rows per pass
     bool q6_pair = true;                        // KB200_GEMV_Q6K_PAIR=0: 1-2 rows on the 4-row kernel
+    bool q6_staged = true;                      // KB200_GEMV_Q6K_STAGED=0: pair kernel quantises per CTA
 };
 
 const Tuning& tuning() {
@@ -1600,6 +1754,8 @@ const Tuning& tuning() {
             v.q6_min_units = uint32_t(std::max(1, std::atoi(s)));
         if (const char* s = std::getenv("KB200_GEMV_Q6K_PAIR"))
             v.q6_pair = std::atoi(s) != 0;
+        if (const char* s = std::getenv("KB200_GEMV_Q6K_STAGED"))
+            v.q6_staged = std::atoi(s) != 0;
         if (const char* s = std::getenv("KB200_GEMV_Q6K_STAGES"))
             v.q6_stages = std::atoi(s) == 2 ? 2 : 3;
         if (const char* s = std::getenv("KB200_GEMV_L2_PREFETCH"))
@@ -1629,19 +1785,20 @@ template <int NT, int S> int q6k_slots() {
     return sm_count() * blocks_per_sm[dev];
 }
 
-template <int S, int W> int q6k_pair_slots() {
+template <int S, int W, bool kStaged> int q6k_pair_slots() {
     static int blocks_per_sm[64] = {};
     static std::mutex lock;
     int dev = 0;
     cudaGetDevice(&dev);
-    constexpr int smem = PairLayout<S, W>::kTotal + 128;
+    constexpr int smem = PairLayout<S, W, kStaged>::kTotal + 128;
     std::lock_guard<std::mutex> guard(lock);
     if (!blocks_per_sm[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_pair_kernel<S, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_pair_kernel<S, W, kStaged>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_pair_kernel attribute");
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_pair_kernel<S, W>, 32 * W + 32, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_pair_kernel<S, W, kStaged>, 32 * W + 32, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_pair_kernel occupancy");
         blocks_per_sm[dev] = n > 0 ? n : 1;
@@ -1698,9 +1855,62 @@ bool mma_eligible(const kb200_gemv_job& j) {
     return false;
 }
 
+// Fills q with one region per distinct input of the launch's jobs (pointer,
+// length and rows), points each job at its region of the staging buffer and
+// returns true, or returns false (and stages nothing) when the regions do not
+// fit the buffer.
+bool stage_inputs(MmaParams& p, uint8_t* staging, PairQuantParams& q) {
+    std::memset(&q, 0, sizeof(q));
+    size_t used = 0;
+    for (uint32_t m = 0; m < p.count; ++m) {
+        MmaJob& d = p.jobs[m];
+        uint32_t r = 0;
+        while (r < q.count && !(q.regions[r].x == d.input && q.regions[r].in == d.in && q.regions[r].rows == d.rows))
+            ++r;
+        if (r == q.count) {
+            const size_t bytes = size_t(d.nblocks) * size_t(pair_chunk_bytes(int(d.rows)));
+            if (used + bytes > kStagingBytes) {
+                for (uint32_t k = 0; k < p.count; ++k)
+                    p.jobs[k].staged = nullptr;
+                return false;
+            }
+            PairQuantRegion& g = q.regions[q.count++];
+            g.x = d.input;
+            g.dst = staging + used;
+            g.in = d.in;
+            g.rows = d.rows;
+            g.first_item = q.items;
+            q.items += d.in / 256 * d.rows;
+            used += bytes;
+        }
+        d.staged = q.regions[r].dst;
+    }
+    if (q.items == 0)
+        for (uint32_t k = 0; k < p.count; ++k)
+            p.jobs[k].staged = nullptr;
+    return q.items > 0;
+}
+
+int launch_pair_quant(const PairQuantParams& q, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(std::min((q.items + 3) / 4, uint32_t(sm_count()) * 8u));  // warp per item, grid-stride
+    cfg.blockDim = dim3(128);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    TraceScope trace(KB200_KERNEL_PAIR_QUANT, stream);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, pair_quant_kernel, q);
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "pair_quant_kernel launch");
+}
+
 // Q6_K: 16-row tiles, units of (tile, chunk of 8 blocks), up to 8 input rows
 // per pass (more rows become row groups), balanced split when whole tiles
-// would leave a tenth of the CTA slots idle.
+// would leave a tenth of the CTA slots idle. 1-2 rows run on the pair
+// kernel, with the activations quantised once per launch into the stream's
+// staging buffer when it has one and they fit.
 int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer) {
     auto encode = encode_fn();
     if (!encode)
@@ -1714,13 +1924,12 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     const bool pair = max_rows <= 2 && tuning().q6_pair;
     const uint32_t group_rows = pair ? 2u : uint32_t(4 * nt);
     const bool two_stage = nt == 1 && tuning().q6_stages == 2;
-    int slots = pair ? (two_stage ? q6k_pair_slots<2, 4>() : q6k_pair_slots<3, 4>())
-              : nt == 2 ? q6k_slots<2, 2>() : two_stage ? q6k_slots<1, 2>() : q6k_slots<1, 3>();
-    if (slots <= 0)
-        return -slots;
-    if (tuning().ctas_per_sm > 0)
-        slots = std::min(slots, sm_count() * tuning().ctas_per_sm);
+    uint8_t* staging = pair && tuning().q6_staged ? staging_for(stream) : nullptr;
     const Fixup* fixup = tuning().balanced ? fixup_for(stream) : nullptr;
+    // Both pair kernels are set up on the first call (which may be the only
+    // one outside graph capture), whichever this launch takes.
+    const int pair_slots = !pair ? 0 : two_stage ? q6k_pair_slots<2, 4, false>() : q6k_pair_slots<3, 4, false>();
+    const int pair_slots_staged = !pair ? 0 : two_stage ? q6k_pair_slots<2, 4, true>() : q6k_pair_slots<3, 4, true>();
     for (size_t first = 0; first < jobs.size(); first += kMaxJobsQ) {
         const size_t n = std::min(jobs.size() - first, size_t(kMaxJobsQ));
         MmaParams p;
@@ -1762,6 +1971,14 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         }
         p.count = uint32_t(n);
         p.total_tiles = tiles;
+        PairQuantParams q;
+        const bool staged = staging && stage_inputs(p, staging, q);
+        int slots = !pair ? (nt == 2 ? q6k_slots<2, 2>() : two_stage ? q6k_slots<1, 2>() : q6k_slots<1, 3>())
+                    : staged ? pair_slots_staged : pair_slots;
+        if (slots <= 0)
+            return -slots;
+        if (tuning().ctas_per_sm > 0)
+            slots = std::min(slots, sm_count() * tuning().ctas_per_sm);
         const uint64_t waves = (tiles + uint64_t(slots) - 1) / uint64_t(slots);
         const bool ragged = uint64_t(tiles) * 10 < waves * uint64_t(slots) * 9;
         const bool balanced = fixup && fixup->ctas >= uint32_t(slots) && ragged
@@ -1772,12 +1989,18 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             p.total_units = units;
             p.partials = fixup->partials;
         }
+        if (staged)
+            if (const int st = launch_pair_quant(q, stream))
+                return st;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
         cfg.blockDim = dim3(kThreadsQ);
-        cfg.dynamicSmemBytes = (pair ? (two_stage ? PairLayout<2>::kTotal : PairLayout<3>::kTotal)
-                                : nt == 2 ? Q6Layout<2, 2>::kTotal
-                                : two_stage ? Q6Layout<1, 2>::kTotal : Q6Layout<1, 3>::kTotal) + 128;
+        cfg.dynamicSmemBytes = (!pair       ? (nt == 2      ? Q6Layout<2, 2>::kTotal
+                                               : two_stage ? Q6Layout<1, 2>::kTotal
+                                                           : Q6Layout<1, 3>::kTotal)
+                                : staged    ? (two_stage ? PairLayout<2, 4, true>::kTotal : PairLayout<3, 4, true>::kTotal)
+                                            : (two_stage ? PairLayout<2, 4>::kTotal : PairLayout<3, 4>::kTotal))
+                               + 128;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1785,11 +2008,17 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         TraceScope trace(pair ? KB200_KERNEL_GEMV_Q6K_PAIR : KB200_KERNEL_GEMV_Q6K_MMA, stream);
-        const cudaError_t e = pair && two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 4>, p)
-                              : pair        ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<3, 4>, p)
-                              : nt == 2     ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<2, 2>, p)
-                              : two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 2>, p)
-                                          : cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 3>, p);
+        cudaError_t e;
+        if (pair && staged)
+            e = two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 4, true>, p)
+                          : cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<3, 4, true>, p);
+        else if (pair)
+            e = two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 4, false>, p)
+                          : cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<3, 4, false>, p);
+        else
+            e = nt == 2     ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<2, 2>, p)
+                : two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 2>, p)
+                            : cudaLaunchKernelEx(&cfg, gemv_q6k_mma_kernel<1, 3>, p);
         if (e != cudaSuccess)
             return cuda_fail(e, "gemv_q6k_mma_kernel launch");
     }

@@ -335,6 +335,114 @@ def test_q6k_tensor_pipe_parity(kb, oracle, cuda, in_, out, rows):
     assert kb.take_device_error() == 0
 
 
+# Q6_K batches at 1-2 input rows (the pair kernel): q/k/v-like jobs sharing
+# one input, a long-K job, mixed 1- and 2-row jobs with a ragged last chunk.
+_PAIR_BATCHES = r"""
+import numpy as np, torch
+import kadan_b200 as kb
+from kadan_b200 import synth
+from kadan_b200.tensor_parallel import pad_rows
+
+BATCHES = (((8192, 1024, 1, 0), (8192, 256, 1, 0), (8192, 256, 1, 0), (28672, 512, 1, 1)),
+           ((8192, 2048, 2, 2), (2304, 96, 1, 3)),
+           ((256, 33, 2, 4),))
+
+
+def pair_batches(dev, stream=None, capture=None):
+    outs = []
+    for batch in BATCHES:
+        keep, jobs, ys, xs = [], [], [], {}
+        for i, (in_, out, rows, xi) in enumerate(batch):
+            w = synth.q6_k(out, in_, seed=10 * xi + i)
+            pitch = (w.shape[1] + 15) // 16 * 16
+            wd = torch.from_numpy(pad_rows(w, pitch)).to(dev)
+            if xi not in xs:
+                x = synth.activations(rows * in_, seed=100 + xi, dtype="bf16").reshape(rows, in_)
+                xs[xi] = torch.from_numpy(x).to(dev)
+            y = torch.full((rows, out), float("nan"), device=dev)
+            keep.append(wd)
+            ys.append(y)
+            jobs.append(kb.gemv_job(kb.Q6_K, wd, xs[xi], y, in_=in_, columns=out, rows=rows, row_bytes_=pitch))
+        if capture is None:
+            kb.gguf_gemv_batch(jobs, stream=stream)
+        else:
+            capture(lambda: kb.gguf_gemv_batch(jobs, stream=stream))
+        torch.cuda.synchronize()
+        outs += [y.cpu().numpy() for y in ys]
+    return outs
+"""
+
+
+def _pair_namespace():
+    ns = {}
+    exec(_PAIR_BATCHES, ns)
+    return ns
+
+
+def test_q6k_staged_activations_match_per_cta_quantisation(kb, oracle, cuda, tmp_path):
+    """Activations quantised once per launch (pair_quant_kernel, copied into
+    each stage) give the bit-identical outputs of the per-CTA activation
+    windows (KB200_GEMV_Q6K_STAGED=0, another process), and both are within
+    the tolerance of the oracle."""
+    import os
+    import subprocess
+    import sys
+
+    from conftest import ROOT
+
+    ns = _pair_namespace()
+    with kb.Phase() as ph:
+        got = ns["pair_batches"](cuda)
+        calls = {k: v["calls"] for k, v in ph.snapshot()["kernels"].items()}
+    ph.close()
+    assert calls == {"pair_quant_kernel": 3, "gemv_q6k_pair_kernel": 3}
+    out = tmp_path / "unstaged.npz"
+    code = _PAIR_BATCHES + f"\nnp.savez({str(out)!r}, *pair_batches(torch.device('cuda:0')))\n"
+    env = {**os.environ, "KB200_GEMV_Q6K_STAGED": "0", "KADAN_B200_NO_BUILD": "1", "PYTHONPATH": str(ROOT)}
+    subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, check=True, timeout=600)
+    with np.load(out) as z:
+        want = [z[f"arr_{i}"] for i in range(len(z.files))]
+    assert len(want) == len(got) == 7
+    for a, b in zip(got, want):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    from kadan_b200 import synth
+
+    flat = [(i, job) for b in ns["BATCHES"] for i, job in enumerate(b)]
+    for (i, (in_, cols, rows, xi)), y in zip(flat, got):
+        w = synth.q6_k(cols, in_, seed=10 * xi + i)
+        x = synth.activations(rows * in_, seed=100 + xi, dtype="bf16").reshape(rows, in_)
+        assert rel_err(y, oracle.gemv_f64(kb.Q6_K, w, x, in_, cols)) <= TOL
+
+
+def test_q6k_pair_first_use_inside_capture(kb, oracle, cuda):
+    """A stream whose first Q6_K launch is captured into a CUDA graph has no
+    staging buffer (nor fixup buffer) yet: the captured launch quantises per
+    CTA, and its replay matches the eager results of another stream within
+    the oracle's tolerance."""
+    import torch
+
+    ns = _pair_namespace()
+    want = ns["pair_batches"](cuda)
+    stream = torch.cuda.Stream(cuda)
+    graphs = []
+
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        graphs.append(g)
+        g.replay()
+
+    with kb.Phase() as ph:
+        got = ns["pair_batches"](cuda, stream=stream, capture=capture)
+        calls = {k: v["calls"] for k, v in ph.snapshot()["kernels"].items()}
+    ph.close()
+    assert calls == {"gemv_q6k_pair_kernel": 3}
+    for a, b in zip(got, want):
+        assert rel_err(a, b) <= TOL
+    del graphs
+
+
 def test_q6k_tensor_pipe_nonfinite_scale_sets_status(kb, cuda):
     import torch
 

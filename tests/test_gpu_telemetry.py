@@ -39,6 +39,7 @@ def test_gemv_and_moe_launches_are_counted_and_timed(kb, cuda):
     ks = snap["kernels"]
     assert ks["gemv_q4k_mma_kernel"]["calls"] == 3
     assert ks["gemv_q6k_pair_kernel"]["calls"] == 3
+    assert ks["pair_quant_kernel"]["calls"] == 3  # the Q6_K launch's activations, quantised once
     for name in ("moe_route_kernel", "moe_sort_kernel", "moe_gather_kernel", "moe_combine_kernel"):
         assert ks[name]["calls"] == 1, name
     assert ks["moe_gemm_kernel"]["calls"] == 2  # gate/up, then down
