@@ -1003,7 +1003,8 @@ typedef enum kb200_kernel {
     KB200_KERNEL_MOE_SHARED = 28,       /* moe_shared_kernel (shared expert's gated add) */
     KB200_KERNEL_MOE_DECODE = 29,       /* moe_decode_kernel (the whole layer for at most 8 tokens) */
     KB200_KERNEL_PAIR_QUANT = 30,       /* pair_quant_kernel (a Q6_K decode launch's activations, once) */
-    KB200_KERNEL_COUNT = 31
+    KB200_KERNEL_Q4K_QUANT = 31,        /* q4k_quant_kernel (a Q4_K decode launch's activations, once) */
+    KB200_KERNEL_COUNT = 32
 } kb200_kernel;
 
 typedef struct kb200_kernel_metrics {

@@ -94,7 +94,7 @@ class ContextCounters(ctypes.Structure):
                 ("gemm_fallbacks", ctypes.c_uint64)]
 
 
-KERNEL_COUNT = 31
+KERNEL_COUNT = 32
 
 
 class KernelMetrics(ctypes.Structure):

@@ -164,14 +164,28 @@ constexpr int kMinBytes = 32;
 constexpr int kTokenBlockTotal = kTokenBlockBytes + kMinBytes + 4;
 constexpr int kSegBudget = 16 * 1024;
 
-struct Layout {
+// One (block, token set) record of the staged Q4_K activations: the rows'
+// operands, minimum-term operands and scales, padded to 16 bytes.
+__host__ __device__ constexpr int q4k_record_bytes(int rows) {
+    return (rows * kTokenBlockTotal + 15) / 16 * 16;
+}
+
+// kStaged: a stage (64 rows x 2 super-blocks) also holds the activation
+// records of its super-blocks for up to 4 tokens, copied from the launch's
+// staging buffer, and there is no activation segment.
+template <bool kStaged = false> struct LayoutQ4 {
+    // A stage starts on a 128-byte boundary (the TMA tile destinations).
+    static constexpr int kStride = kStaged ? (kStageBytes + 2 * q4k_record_bytes(4) + 127) / 128 * 128 : kStageBytes;
     static constexpr int kStagesOff = 0;
-    static constexpr int kSegOff = kStages * kStageBytes;
-    static constexpr int kRedOff = kSegOff + kSegBudget;       // split-K partials
+    static constexpr int kSegOff = kStages * kStride;
+    static constexpr int kRedOff = kSegOff + (kStaged ? 0 : kSegBudget);  // split-K partials
     static constexpr int kRedBytes = kConsumerThreads * 4 * 4;  // [nt<=2][2][thread]
     static constexpr int kBarOff = kRedOff + kRedBytes;  // full[], empty[], abort flag
     static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
 };
+using Layout = LayoutQ4<false>;
+static_assert(kStageBytes % 128 == 0 && LayoutQ4<true>::kStride % 128 == 0, "tensor copies land on 128-byte boundaries");
+static_assert(3 * (LayoutQ4<true>::kTotal + 128 + 1024) <= 228 * 1024, "three staged Q4_K CTAs per SM");
 
 // Segment of `rows` tokens: the most whole stages (multiples of `bps`
 // super-blocks) that fit kSegBudget; operands first, then minimum-term
@@ -362,6 +376,84 @@ __device__ __forceinline__ void grid_dependents_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Values 8 lane .. 8 lane + 7 of 256 at xr (16-byte vectors when `vec`).
+__device__ __forceinline__ void load_lane8(float (&v)[8], const float* xr, bool vec) {
+    if (vec) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(xr)), b = __ldg(reinterpret_cast<const float4*>(xr) + 1);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+        v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            v[i] = __ldg(xr + i);
+    }
+}
+
+// The two int8 levels of 8 values with absmax m: pairs of values at a time,
+// y = v/s, r1 = y + M (M = 1.5 * 2^23, so r1's low bits are round(y) as an
+// integer), d = y - round(y) in [-1/2, 1/2] (exact), r2 = d * 254 + M (low
+// bits round(254 d), within [-127, 127]). The int8 codes are the low bytes
+// of h (r1) and l (r2).
+__device__ __forceinline__ void quantise_levels(const float (&v)[8], float m, uint32_t (&h)[8], uint32_t (&l)[8]) {
+    const float inv = m > 0.f ? 127.f / m : 0.f;
+    const float2 inv2 = make_float2(inv, inv), magic = make_float2(kMagic, kMagic);
+    const float2 neg_magic = make_float2(-kMagic, -kMagic), k254 = make_float2(254.f, 254.f);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        const float2 y = mul2(make_float2(v[i], v[i + 1]), inv2);
+        const float2 r1 = add2(y, magic);
+        const float2 d = sub2(y, add2(r1, neg_magic));
+        const float2 r2 = fma2(d, k254, magic);
+        h[i] = __float_as_uint(r1.x), h[i + 1] = __float_as_uint(r1.y);
+        l[i] = __float_as_uint(r2.x), l[i + 1] = __float_as_uint(r2.y);
+    }
+}
+
+// One (block, token) item of the Q4_K activation operands: lane L holds
+// values 8L..8L+7 (v), m is the block's absmax, sum the sum of the lane's
+// sub-block G = L/4 and next that of G ^ 1. Writes the lane's B words of the
+// 512-byte record frag, (lanes 8t') the minimum-term operands of the 32-byte
+// record minb and (lane 0) the scale.
+__device__ __forceinline__ void q4k_store_item(const float (&v)[8], float m, float sum, float next, uint32_t* frag,
+                                               uint32_t* minb, float* scale, int lane) {
+    const int G = lane >> 2, t = lane & 3;
+    uint32_t h[8], l[8];
+    quantise_levels(v, m, h, l);
+    const int idx = (((G >> 1) * 4 + t) * 2) * 4 + (G & 1) * 2;  // part h; part l is +4
+    frag[idx] = pack4(int(h[0]), int(h[1]), int(h[2]), int(h[3]));
+    frag[idx + 1] = pack4(int(h[4]), int(h[5]), int(h[6]), int(h[7]));
+    frag[idx + 4] = pack4(int(l[0]), int(l[1]), int(l[2]), int(l[3]));
+    frag[idx + 5] = pack4(int(l[4]), int(l[5]), int(l[6]), int(l[7]));
+    // Minimum term B' for lane (g, t') = sums of sub-blocks 2t', 2t'+1
+    // (scaled by 1/256) split into fp16 hi and lo: written by lanes 8t'.
+    if ((lane & 7) == 0) {
+        const float s0 = sum * (1.f / 256.f), s1 = next * (1.f / 256.f);
+        const __half2 hi = __floats2half2_rn(s0, s1);
+        const float2 hf = __half22float2(hi);
+        const __half2 lo = __floats2half2_rn(s0 - hf.x, s1 - hf.y);
+        minb[lane >> 3] = pack_half2(hi);
+        minb[4 + (lane >> 3)] = pack_half2(lo);
+    }
+    if (lane == 0)
+        *scale = m > 0.f ? m / 127.f : 0.f;
+}
+
+// Absmax, own sub-block sum and the neighbouring sub-block's sum of a
+// warp's 256 values (lane L: values 8L..8L+7).
+__device__ __forceinline__ void q4k_block_stats(const float (&v)[8], float& m, float& sum, float& next) {
+    m = 0.f, sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        m = fmaxf(m, fabsf(v[i]));
+        sum += v[i];
+    }
+    // Non-negative floats order as their bit patterns.
+    m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    next = __shfl_xor_sync(0xffffffffu, sum, 4);  // sum of sub-block G ^ 1
+}
+
 // Quantise the activations of super-blocks [blk0, blk0 + nblk) for the
 // segment's tokens. One warp per (block, token): lane L owns values
 // 8L..8L+7, which are the B registers b0 (k = 4t..4t+3 <-> values 8t..8t+3)
@@ -377,7 +469,6 @@ __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, 
     uint32_t* minb = seg.minb(smem);
     float* scales = seg.scales(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = lane >> 2, t = lane & 3;
     const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (in & 3) == 0;
     const int items = nblk * rows;
     // kBatch items per warp at a time, without branches between them: all
@@ -391,83 +482,35 @@ __device__ void prep_segment(uint8_t* smem, const Segment& seg, const float* x, 
         for (int q = 0; q < kBatch; ++q) {
             const int item = min(base + q * kWarps, items - 1);  // past the end: reload the last, store nothing
             const int blk = item / rows, tok = item % rows;
-            const float* xr = x + size_t(tok) * in + size_t(blk0 + blk) * 256 + lane * 8;
-            if (vec) {
-                const float4 a = __ldg(reinterpret_cast<const float4*>(xr)), b = __ldg(reinterpret_cast<const float4*>(xr) + 1);
-                v[q][0] = a.x, v[q][1] = a.y, v[q][2] = a.z, v[q][3] = a.w;
-                v[q][4] = b.x, v[q][5] = b.y, v[q][6] = b.z, v[q][7] = b.w;
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    v[q][i] = __ldg(xr + i);
-            }
+            load_lane8(v[q], x + size_t(tok) * in + size_t(blk0 + blk) * 256 + lane * 8, vec);
         }
         float m[kBatch], sum[kBatch], next[kBatch];
 #pragma unroll
-        for (int q = 0; q < kBatch; ++q) {
-            m[q] = 0.f, sum[q] = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                m[q] = fmaxf(m[q], fabsf(v[q][i]));
-                sum[q] += v[q][i];
-            }
-            // Non-negative floats order as their bit patterns.
-            m[q] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m[q])));
-            sum[q] += __shfl_xor_sync(0xffffffffu, sum[q], 1);
-            sum[q] += __shfl_xor_sync(0xffffffffu, sum[q], 2);
-            next[q] = __shfl_xor_sync(0xffffffffu, sum[q], 4);  // sum of sub-block G ^ 1
-        }
+        for (int q = 0; q < kBatch; ++q)
+            q4k_block_stats(v[q], m[q], sum[q], next[q]);
 #pragma unroll
         for (int q = 0; q < kBatch; ++q) {
             const int item = base + q * kWarps;
             if (item >= items)
                 break;
             const int blk = item / rows, tok = item % rows;
-            const float inv = m[q] > 0.f ? 127.f / m[q] : 0.f;
-            // Pairs of values at a time: y = v/s, r1 = y + M (M = 1.5 * 2^23,
-            // so r1's low bits are round(y) as an integer), d = y - round(y)
-            // in [-1/2, 1/2] (exact), r2 = d * 254 + M (low bits round(254 d),
-            // within [-127, 127]). The int8 codes are the low bytes of r1, r2.
-            const float2 inv2 = make_float2(inv, inv), magic = make_float2(kMagic, kMagic);
-            const float2 neg_magic = make_float2(-kMagic, -kMagic), k254 = make_float2(254.f, 254.f);
-            uint32_t h[8], l[8];
-#pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                const float2 y = mul2(make_float2(v[q][i], v[q][i + 1]), inv2);
-                const float2 r1 = add2(y, magic);
-                const float2 d = sub2(y, add2(r1, neg_magic));
-                const float2 r2 = fma2(d, k254, magic);
-                h[i] = __float_as_uint(r1.x), h[i + 1] = __float_as_uint(r1.y);
-                l[i] = __float_as_uint(r2.x), l[i + 1] = __float_as_uint(r2.y);
-            }
             const int slot = blk * rows + tok;
-            uint32_t* dst;
-            int idx;
             if constexpr (kQ6) {
+                uint32_t h[8], l[8];
+                quantise_levels(v[q], m[q], h, l);
                 // Lane L: values 8L..8L+7 = words 2(L&1), 2(L&1)+1 of sub-block L/2.
-                dst = frag + blk * rows * (kTokenBlockBytes / 4);
-                idx = (((lane >> 1) * rows + tok) * 2) * 4 + 2 * (lane & 1);
+                uint32_t* dst = frag + blk * rows * (kTokenBlockBytes / 4);
+                const int idx = (((lane >> 1) * rows + tok) * 2) * 4 + 2 * (lane & 1);
+                dst[idx] = pack4(int(h[0]), int(h[1]), int(h[2]), int(h[3]));
+                dst[idx + 1] = pack4(int(h[4]), int(h[5]), int(h[6]), int(h[7]));
+                dst[idx + 4] = pack4(int(l[0]), int(l[1]), int(l[2]), int(l[3]));
+                dst[idx + 5] = pack4(int(l[4]), int(l[5]), int(l[6]), int(l[7]));
+                if (lane == 0)
+                    scales[slot] = m[q] > 0.f ? m[q] / 127.f : 0.f;
             } else {
-                dst = frag + slot * (kTokenBlockBytes / 4);
-                idx = (((G >> 1) * 4 + t) * 2) * 4 + (G & 1) * 2;  // part h; part l is +4
+                q4k_store_item(v[q], m[q], sum[q], next[q], frag + slot * (kTokenBlockBytes / 4),
+                               minb + slot * (kMinBytes / 4), scales + slot, lane);
             }
-            dst[idx] = pack4(int(h[0]), int(h[1]), int(h[2]), int(h[3]));
-            dst[idx + 1] = pack4(int(h[4]), int(h[5]), int(h[6]), int(h[7]));
-            dst[idx + 4] = pack4(int(l[0]), int(l[1]), int(l[2]), int(l[3]));
-            dst[idx + 5] = pack4(int(l[4]), int(l[5]), int(l[6]), int(l[7]));
-            // Minimum term B' for lane (g, t') = sums of sub-blocks 2t', 2t'+1
-            // (scaled by 1/256) split into fp16 hi and lo: written by lanes 8t'.
-            if (!kQ6 && (lane & 7) == 0) {
-                const float s0 = sum[q] * (1.f / 256.f), s1 = next[q] * (1.f / 256.f);
-                const __half2 hi = __floats2half2_rn(s0, s1);
-                const float2 hf = __half22float2(hi);
-                const __half2 lo = __floats2half2_rn(s0 - hf.x, s1 - hf.y);
-                uint32_t* mb = minb + slot * (kMinBytes / 4);
-                mb[lane >> 3] = pack_half2(hi);
-                mb[4 + (lane >> 3)] = pack_half2(lo);
-            }
-            if (lane == 0)
-                scales[slot] = m[q] > 0.f ? m[q] / 127.f : 0.f;
         }
     }
 }
@@ -588,9 +631,14 @@ __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc
     }
 }
 
-template <int NT>
+// kStaged (64-row tiles, at most 4 input rows): the activations come
+// quantised from the launch's staging buffer (q4k_quant_kernel, launched just
+// before), one record per super-block copied with the stage's weights; the
+// producer issues the first stages' weight loads before it waits for the
+// quantisation kernel. Otherwise the consumers quantise activation segments.
+template <int NT, bool kStaged = false>
 __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid_constant__ MmaParams p) {
-    using L = Layout;
+    using L = LayoutQ4<kStaged>;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // TMA destinations (no swizzle) want 128-byte alignment.
     uint8_t* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
@@ -618,6 +666,20 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
         if (lane != 0)
             return;
         uint32_t it = 0;
+        // Staged: activation copies of the first stages, held back until the
+        // quantisation kernel has finished.
+        bool staged_ready = false;
+        const uint8_t* held_src[kStages];
+        uint32_t held_bytes[kStages];
+        uint32_t held = 0;
+        auto release_held = [&] {
+            grid_dependency_wait();
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            staged_ready = true;
+            for (uint32_t k = 0; k < held; ++k)
+                bulk_g2s(smem + L::kStagesOff + k * L::kStride + kStageBytes, held_src[k], held_bytes[k], &full[k]);
+            held = 0;
+        };
         PieceIter pieces(p);
         Prefetcher ahead(p);
         for (uint32_t i = 0; i < p.prefetch; ++i)
@@ -626,6 +688,7 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
         while (pieces.next(p, pc)) {
             const MmaJob& job = p.jobs[pc.job];
             const int row0 = int((pc.tile / job.row_groups) * uint32_t(R));
+            const uint32_t record = kStaged ? uint32_t(q4k_record_bytes(int(job.rows))) : 0u;
             asm volatile("prefetch.tensormap [%0];" ::"l"(&job.map) : "memory");
             for (uint32_t b0 = pc.k0; b0 < pc.k1; b0 += BPS, ++it) {
                 const int slot = int(it % kStages);
@@ -634,14 +697,27 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
                 if (*reinterpret_cast<volatile int*>(abort_flag))
                     goto drain;
                 const int nb = int(min(uint32_t(BPS), pc.k1 - b0));
-                mbar_expect_tx(&full[slot], uint32_t(nb * R * kBlockBytes));
+                uint8_t* stage = smem + L::kStagesOff + slot * L::kStride;
+                mbar_expect_tx(&full[slot], uint32_t(nb * R * kBlockBytes) + uint32_t(nb) * record);
                 for (int b = 0; b < nb; ++b)
-                    tma_load_3d(smem + L::kStagesOff + slot * kStageBytes + b * R * kBlockBytes, &job.map, 0,
-                                int(b0 + b), row0, &full[slot]);
+                    tma_load_3d(stage + b * R * kBlockBytes, &job.map, 0, int(b0 + b), row0, &full[slot]);
+                if constexpr (kStaged) {
+                    const uint8_t* src = job.staged + size_t(b0) * record;
+                    if (staged_ready) {
+                        bulk_g2s(stage + kStageBytes, src, uint32_t(nb) * record, &full[slot]);
+                    } else {
+                        held_src[held] = src, held_bytes[held] = uint32_t(nb) * record;
+                        if (++held == uint32_t(kStages))
+                            release_held();
+                    }
+                }
                 if (p.prefetch)
                     ahead.step(p, R, BPS);
             }
         }
+        if constexpr (kStaged)
+            if (!staged_ready)
+                release_held();
     drain:
         for (uint32_t k = 0; k < kStages && k < it; ++k) {
             const uint32_t last = it - 1 - k;
@@ -677,11 +753,9 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
         const int rows = int(min(job.group_rows, job.rows - r0));
         const float* x = job.input + size_t(r0) * job.in;
         const Segment seg(rows, BPS);
-        if (seg.blocks < BPS)  // a stage's activations would overflow the segment buffer
+        if (!kStaged && seg.blocks < BPS)  // a stage's activations would overflow the segment buffer
             atomicExch(abort_flag, 1);
-        const uint8_t* frag = seg.frag(smem);
-        const uint32_t* minb = seg.minb(smem);
-        const float* scales = seg.scales(smem);
+        const int record = q4k_record_bytes(rows);
         const uint32_t my_row = row0 + 16 * rg + g;  // and my_row + 8
         const bool valid_lo = my_row < job.columns, valid_hi = my_row + 8 < job.columns;
         const bool check = job.status != nullptr;
@@ -695,7 +769,8 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
             const int slot = int(it % kStages);
             const int nb = int(min(uint32_t(BPS), pc.k1 - b0));
             const int blk_first = int(b0);
-            if ((x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
+            if (!kStaged
+                && (x != seg_x || rows != seg_rows || blk_first < seg_blk0 || blk_first + nb > seg_blk0 + seg_nblk)
                 && seg.blocks >= BPS) {
                 // The window covers all of K when the segment buffer holds
                 // it (one quantisation per input however the work is cut),
@@ -718,13 +793,21 @@ __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid
             if (!aborted && !mbar_wait(&full[slot], (it / kStages) & 1u, watchdog_full_barrier, p.watchdog))
                 atomicExch(abort_flag, 1);
             if (!aborted) {
-                const uint8_t* stage = smem + L::kStagesOff + slot * kStageBytes;
+                const uint8_t* stage = smem + L::kStagesOff + slot * L::kStride;
 #pragma unroll
                 for (int bb = 0; bb < 2; ++bb) {
                     const int b = 2 * ks + bb;  // this warp's super-blocks of the stage
                     if (b >= nb)
                         break;
-                    const int sblk = blk_first + b - seg_blk0;  // block index within the segment
+                    // Activation operands of (block, token): the stage's record of
+                    // block b (staged) or the segment's arrays.
+                    const int sblk = kStaged ? 0 : blk_first + b - seg_blk0;  // block index within the segment
+                    const uint8_t* rec = stage + kStageBytes + b * record;
+                    const uint8_t* frag = kStaged ? rec : seg.frag(smem);
+                    const uint32_t* minb = kStaged ? reinterpret_cast<const uint32_t*>(rec + rows * kTokenBlockBytes)
+                                                   : seg.minb(smem);
+                    const float* scales = kStaged ? reinterpret_cast<const float*>(rec + rows * (kTokenBlockBytes + kMinBytes))
+                                                  : seg.scales(smem);
                     const uint8_t* rgp = stage + b * R * kBlockBytes + (16 * rg + g) * kBlockBytes;
                     const uint8_t* r8p = rgp + 8 * kBlockBytes;
                     const uint4 hg = *reinterpret_cast<const uint4*>(rgp);
@@ -1235,19 +1318,6 @@ __device__ __forceinline__ void pair_quant_store(const float (&v)[8], uint32_t* 
         scales[blk * rows + tok] = m > 0.f ? m / 127.f : 0.f;
 }
 
-// Values 8 lane .. 8 lane + 7 of 256 at xr (16-byte vectors when `vec`).
-__device__ __forceinline__ void load_lane8(float (&v)[8], const float* xr, bool vec) {
-    if (vec) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(xr)), b = __ldg(reinterpret_cast<const float4*>(xr) + 1);
-        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
-        v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-            v[i] = __ldg(xr + i);
-    }
-}
-
 // Quantise super-blocks [blk0, blk0 + nblk) of the segment's tokens into the
 // pair layout: one warp per (block, token); lane L owns values 8L..8L+7 (half
 // L % 2 of sub-block L / 2). Every load of a warp's items is in flight before
@@ -1280,33 +1350,70 @@ __device__ void prep_pairs(uint8_t* smem, const PairSegment& seg, const float* x
     }
 }
 
-// Inputs of one pair-layout quantisation launch: each region is one distinct
-// input (x, in, rows) of a GEMV launch, written chunk after chunk at dst.
-struct PairQuantRegion {
+// Inputs of one activation quantisation launch: each region is one distinct
+// input (x, in, rows) of a GEMV launch, written at dst in the layout its
+// GEMV kernel copies into its stages.
+struct StageQuantRegion {
     const float* x;
     uint8_t* dst;
     uint32_t in, rows, first_item;  // items: blocks x rows, prefix over regions
 };
-struct PairQuantParams {
-    PairQuantRegion regions[kMaxJobsQ];
+struct StageQuantParams {
+    StageQuantRegion regions[kMaxJobsQ];
     uint32_t count, items;
 };
+
+// The region holding `item` (regions in first_item order).
+__device__ __forceinline__ const StageQuantRegion& quant_region(const StageQuantParams& p, uint32_t item) {
+    uint32_t r = 0;
+    while (r + 1 < p.count && item >= p.regions[r + 1].first_item)
+        ++r;
+    return p.regions[r];
+}
+
+// Q4_K: every (block, token) of the launch's inputs quantised once into one
+// record per block and input (q4k_record_bytes), one warp per item. Waits for
+// the previous kernel of the stream (which may write the inputs); lets the
+// GEMV that follows launch only once its items are done: launched earlier,
+// that GEMV's CTAs take the SMs piecemeal while the previous kernel drains
+// (measured: a step of the config-4 stack 10 % slower).
+__global__ void __launch_bounds__(128) q4k_quant_kernel(const __grid_constant__ StageQuantParams p) {
+    grid_dependency_wait();
+    const int lane = threadIdx.x & 31;
+    const uint32_t warps = gridDim.x * (blockDim.x >> 5);
+    for (uint32_t item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < p.items; item += warps) {
+        const StageQuantRegion& g = quant_region(p, item);
+        const int rows = int(g.rows);
+        const uint32_t local = item - g.first_item;
+        const int blk = int(local / g.rows), tok = int(local % g.rows);
+        uint8_t* rec = g.dst + size_t(blk) * q4k_record_bytes(rows);
+        const bool vec = (reinterpret_cast<uintptr_t>(g.x) & 15u) == 0 && (g.in & 3) == 0;
+        float v[8], m, sum, next;
+        load_lane8(v, g.x + size_t(tok) * g.in + size_t(blk) * 256 + lane * 8, vec);
+        q4k_block_stats(v, m, sum, next);
+        q4k_store_item(v, m, sum, next, reinterpret_cast<uint32_t*>(rec + tok * kTokenBlockBytes),
+                       reinterpret_cast<uint32_t*>(rec + rows * kTokenBlockBytes + tok * kMinBytes),
+                       reinterpret_cast<float*>(rec + rows * (kTokenBlockBytes + kMinBytes)) + tok, lane);
+    }
+    // The GEMV reads the buffer with bulk async copies.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0)
+        grid_dependents_launch();
+}
 
 // Quantises every (block, token) of the launch's inputs once into the
 // staging buffer the GEMV's producer copies from, one warp per item. Waits
 // for the previous kernel of the stream (which may write the inputs) and
 // lets the GEMV that follows start streaming weights at once.
-__global__ void __launch_bounds__(128) pair_quant_kernel(const __grid_constant__ PairQuantParams p) {
+__global__ void __launch_bounds__(128) pair_quant_kernel(const __grid_constant__ StageQuantParams p) {
     if (threadIdx.x == 0)
         grid_dependents_launch();
     grid_dependency_wait();
     const int lane = threadIdx.x & 31;
     const uint32_t warps = gridDim.x * (blockDim.x >> 5);
     for (uint32_t item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < p.items; item += warps) {
-        uint32_t r = 0;
-        while (r + 1 < p.count && item >= p.regions[r + 1].first_item)
-            ++r;
-        const PairQuantRegion& g = p.regions[r];
+        const StageQuantRegion& g = quant_region(p, item);
         const int rows = int(g.rows);
         const uint32_t local = item - g.first_item;
         const int blk = int(local / g.rows), tok = int(local % g.rows);
@@ -1624,19 +1731,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // CTA slots of the kernel on the current device (SMs x resident CTAs), or a
 // negative kb200_status.
-template <int NT> int kernel_slots() {
+template <int NT, bool kStaged = false> int kernel_slots() {
     static int blocks_per_sm[64] = {};
     static std::mutex lock;
     int dev = 0;
     cudaGetDevice(&dev);
-    constexpr int smem = Layout::kTotal + 128;  // + alignment slack
+    constexpr int smem = LayoutQ4<kStaged>::kTotal + 128;  // + alignment slack
     std::lock_guard<std::mutex> guard(lock);
     if (!blocks_per_sm[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_q4k_mma_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_q4k_mma_kernel<NT, kStaged>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q4k_mma_kernel attribute");
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q4k_mma_kernel<NT>, kThreadsQ, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q4k_mma_kernel<NT, kStaged>, kThreadsQ, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q4k_mma_kernel occupancy");
         blocks_per_sm[dev] = n > 0 ? n : 1;
@@ -1739,6 +1847,7 @@ struct Tuning {
     int q6_stages = 3;                          // KB200_GEMV_Q6K_STAGES=2|3: ring depth at 1-4 rows per pass
     bool q6_pair = true;                        // KB200_GEMV_Q6K_PAIR=0: 1-2 rows on the 4-row kernel
     bool q6_staged = true;                      // KB200_GEMV_Q6K_STAGED=0: pair kernel quantises per CTA
+    bool q4_staged = true;                      // KB200_GEMV_Q4K_STAGED=0: Q4_K kernel quantises per CTA
 };
 
 const Tuning& tuning() {
@@ -1756,6 +1865,8 @@ const Tuning& tuning() {
             v.q6_pair = std::atoi(s) != 0;
         if (const char* s = std::getenv("KB200_GEMV_Q6K_STAGED"))
             v.q6_staged = std::atoi(s) != 0;
+        if (const char* s = std::getenv("KB200_GEMV_Q4K_STAGED"))
+            v.q4_staged = std::atoi(s) != 0;
         if (const char* s = std::getenv("KB200_GEMV_Q6K_STAGES"))
             v.q6_stages = std::atoi(s) == 2 ? 2 : 3;
         if (const char* s = std::getenv("KB200_GEMV_L2_PREFETCH"))
@@ -1806,11 +1917,11 @@ template <int S, int W, bool kStaged> int q6k_pair_slots() {
     return sm_count() * blocks_per_sm[dev];
 }
 
-template <int NT> int launch_q4k(const MmaParams& p, uint32_t grid, cudaStream_t stream) {
+template <int NT, bool kStaged = false> int launch_q4k(const MmaParams& p, uint32_t grid, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreadsQ);
-    cfg.dynamicSmemBytes = Layout::kTotal + 128;
+    cfg.dynamicSmemBytes = LayoutQ4<kStaged>::kTotal + 128;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1818,7 +1929,7 @@ template <int NT> int launch_q4k(const MmaParams& p, uint32_t grid, cudaStream_t
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     TraceScope trace(KB200_KERNEL_GEMV_Q4K_MMA, stream);
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_q4k_mma_kernel<NT>, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_q4k_mma_kernel<NT, kStaged>, p);
     return e == cudaSuccess ? KB200_OK : cuda_fail(e, "gemv_q4k_mma_kernel launch");
 }
 
@@ -1858,8 +1969,9 @@ bool mma_eligible(const kb200_gemv_job& j) {
 // Fills q with one region per distinct input of the launch's jobs (pointer,
 // length and rows), points each job at its region of the staging buffer and
 // returns true, or returns false (and stages nothing) when the regions do not
-// fit the buffer.
-bool stage_inputs(MmaParams& p, uint8_t* staging, PairQuantParams& q) {
+// fit the buffer. Layout: Q4_K records per block (q4k) or Q6_K pair-layout
+// chunks of 8 blocks.
+bool stage_inputs(MmaParams& p, uint8_t* staging, StageQuantParams& q, bool q4k) {
     std::memset(&q, 0, sizeof(q));
     size_t used = 0;
     for (uint32_t m = 0; m < p.count; ++m) {
@@ -1868,13 +1980,15 @@ bool stage_inputs(MmaParams& p, uint8_t* staging, PairQuantParams& q) {
         while (r < q.count && !(q.regions[r].x == d.input && q.regions[r].in == d.in && q.regions[r].rows == d.rows))
             ++r;
         if (r == q.count) {
-            const size_t bytes = size_t(d.nblocks) * size_t(pair_chunk_bytes(int(d.rows)));
+            const size_t blocks = d.in / 256;
+            const size_t bytes = q4k ? blocks * size_t(q4k_record_bytes(int(d.rows)))
+                                     : (blocks + kQ6Chunk - 1) / kQ6Chunk * size_t(pair_chunk_bytes(int(d.rows)));
             if (used + bytes > kStagingBytes) {
                 for (uint32_t k = 0; k < p.count; ++k)
                     p.jobs[k].staged = nullptr;
                 return false;
             }
-            PairQuantRegion& g = q.regions[q.count++];
+            StageQuantRegion& g = q.regions[q.count++];
             g.x = d.input;
             g.dst = staging + used;
             g.in = d.in;
@@ -1891,7 +2005,7 @@ bool stage_inputs(MmaParams& p, uint8_t* staging, PairQuantParams& q) {
     return q.items > 0;
 }
 
-int launch_pair_quant(const PairQuantParams& q, cudaStream_t stream) {
+int launch_stage_quant(const StageQuantParams& q, cudaStream_t stream, bool q4k) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(std::min((q.items + 3) / 4, uint32_t(sm_count()) * 8u));  // warp per item, grid-stride
     cfg.blockDim = dim3(128);
@@ -1901,9 +2015,9 @@ int launch_pair_quant(const PairQuantParams& q, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    TraceScope trace(KB200_KERNEL_PAIR_QUANT, stream);
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, pair_quant_kernel, q);
-    return e == cudaSuccess ? KB200_OK : cuda_fail(e, "pair_quant_kernel launch");
+    TraceScope trace(q4k ? KB200_KERNEL_Q4K_QUANT : KB200_KERNEL_PAIR_QUANT, stream);
+    const cudaError_t e = q4k ? cudaLaunchKernelEx(&cfg, q4k_quant_kernel, q) : cudaLaunchKernelEx(&cfg, pair_quant_kernel, q);
+    return e == cudaSuccess ? KB200_OK : cuda_fail(e, q4k ? "q4k_quant_kernel launch" : "pair_quant_kernel launch");
 }
 
 // Q6_K: 16-row tiles, units of (tile, chunk of 8 blocks), up to 8 input rows
@@ -1971,8 +2085,8 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         }
         p.count = uint32_t(n);
         p.total_tiles = tiles;
-        PairQuantParams q;
-        const bool staged = staging && stage_inputs(p, staging, q);
+        StageQuantParams q;
+        const bool staged = staging && stage_inputs(p, staging, q, false);
         int slots = !pair ? (nt == 2 ? q6k_slots<2, 2>() : two_stage ? q6k_slots<1, 2>() : q6k_slots<1, 3>())
                     : staged ? pair_slots_staged : pair_slots;
         if (slots <= 0)
@@ -1990,7 +2104,7 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             p.partials = fixup->partials;
         }
         if (staged)
-            if (const int st = launch_pair_quant(q, stream))
+            if (const int st = launch_stage_quant(q, stream, false))
                 return st;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
@@ -2038,6 +2152,17 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     int slots = nt == 1 ? kernel_slots<1>() : kernel_slots<2>();
     if (slots <= 0)
         return -slots;
+    // Activations quantised once per launch (64-row tiles, at most 4 rows)
+    // when the staged kernel fits as many CTAs per SM (both are set up on
+    // the first call, which may be the only one outside graph capture).
+    uint8_t* staging = nullptr;
+    if (nt == 1 && tuning().q4_staged) {
+        const int staged_slots = kernel_slots<1, true>();
+        if (staged_slots <= 0)
+            return -staged_slots;
+        if (staged_slots == slots)
+            staging = staging_for(stream);
+    }
     if (tuning().ctas_per_sm > 0)
         slots = std::min(slots, sm_count() * tuning().ctas_per_sm);
     const Fixup* fixup = tuning().balanced ? fixup_for(stream) : nullptr;
@@ -2135,7 +2260,13 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             p.total_units = units;
             p.partials = fixup->partials;
         }
-        const int s = nt == 1 ? launch_q4k<1>(p, grid, stream) : launch_q4k<2>(p, grid, stream);
+        StageQuantParams q;
+        const bool staged = staging && R == 64 && stage_inputs(p, staging, q, true);
+        if (staged)
+            if (const int st = launch_stage_quant(q, stream, true))
+                return st;
+        const int s = nt == 2 ? launch_q4k<2>(p, grid, stream)
+                      : staged ? launch_q4k<1, true>(p, grid, stream) : launch_q4k<1>(p, grid, stream);
         if (s)
             return s;
     }

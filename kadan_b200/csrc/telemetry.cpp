@@ -168,7 +168,7 @@ const char* const kNames[KB200_KERNEL_COUNT] = {
     "mxfp4_ggml_dequant_kernel", "mxfp4_from_ggml_kernel", "peer_allreduce_kernel",  "ep_exchange_kernel",
     "rms_norm_kernel",        "rope_kernel",            "attend_kernel",             "attend_combine_kernel",
     "delta_conv_kernel",      "delta_l2_kernel",        "delta_heads_kernel",        "silu_mul_kernel",
-    "moe_shared_kernel",      "moe_decode_kernel",      "pair_quant_kernel",
+    "moe_shared_kernel",      "moe_decode_kernel",      "pair_quant_kernel",         "q4k_quant_kernel",
 };
 
 }  // namespace

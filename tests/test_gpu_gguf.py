@@ -335,25 +335,35 @@ def test_q6k_tensor_pipe_parity(kb, oracle, cuda, in_, out, rows):
     assert kb.take_device_error() == 0
 
 
-# Q6_K batches at 1-2 input rows (the pair kernel): q/k/v-like jobs sharing
-# one input, a long-K job, mixed 1- and 2-row jobs with a ragged last chunk.
-_PAIR_BATCHES = r"""
+# Batches whose activations are quantised once per launch: Q6_K at 1-2
+# input rows (the pair kernel; q/k/v-like jobs sharing one input, a long-K
+# job, mixed 1- and 2-row jobs with a ragged last chunk) and Q4_K at up to 4
+# rows on 64-row tiles (balanced splits; shared inputs, 3- and 4-row jobs,
+# K of 9 super-blocks).
+_STAGED_BATCHES = r"""
 import numpy as np, torch
 import kadan_b200 as kb
 from kadan_b200 import synth
 from kadan_b200.tensor_parallel import pad_rows
 
-BATCHES = (((8192, 1024, 1, 0), (8192, 256, 1, 0), (8192, 256, 1, 0), (28672, 512, 1, 1)),
-           ((8192, 2048, 2, 2), (2304, 96, 1, 3)),
-           ((256, 33, 2, 4),))
+BATCHES = {
+    "q6_k": (((8192, 1024, 1, 0), (8192, 256, 1, 0), (8192, 256, 1, 0), (28672, 512, 1, 1)),
+             ((8192, 2048, 2, 2), (2304, 96, 1, 3)),
+             ((256, 33, 2, 4),)),
+    "q4_k": (((8192, 8192, 1, 0), (8192, 4096, 1, 0)),
+             ((4096, 14336, 3, 1), (4096, 2048, 4, 2)),
+             ((2304, 28672, 2, 3),)),
+}
 
 
-def pair_batches(dev, stream=None, capture=None):
+def run_batches(name, dev, stream=None, capture=None):
+    enc = getattr(kb, name.upper())
+    make = synth.q6_k if name == "q6_k" else synth.q4_k
     outs = []
-    for batch in BATCHES:
+    for batch in BATCHES[name]:
         keep, jobs, ys, xs = [], [], [], {}
         for i, (in_, out, rows, xi) in enumerate(batch):
-            w = synth.q6_k(out, in_, seed=10 * xi + i)
+            w = make(out, in_, seed=10 * xi + i)
             pitch = (w.shape[1] + 15) // 16 * 16
             wd = torch.from_numpy(pad_rows(w, pitch)).to(dev)
             if xi not in xs:
@@ -362,7 +372,7 @@ def pair_batches(dev, stream=None, capture=None):
             y = torch.full((rows, out), float("nan"), device=dev)
             keep.append(wd)
             ys.append(y)
-            jobs.append(kb.gemv_job(kb.Q6_K, wd, xs[xi], y, in_=in_, columns=out, rows=rows, row_bytes_=pitch))
+            jobs.append(kb.gemv_job(enc, wd, xs[xi], y, in_=in_, columns=out, rows=rows, row_bytes_=pitch))
         if capture is None:
             kb.gguf_gemv_batch(jobs, stream=stream)
         else:
@@ -371,58 +381,65 @@ def pair_batches(dev, stream=None, capture=None):
         outs += [y.cpu().numpy() for y in ys]
     return outs
 """
+_STAGED = {"q6_k": ("KB200_GEMV_Q6K_STAGED", "pair_quant_kernel", "gemv_q6k_pair_kernel"),
+           "q4_k": ("KB200_GEMV_Q4K_STAGED", "q4k_quant_kernel", "gemv_q4k_mma_kernel")}
 
 
-def _pair_namespace():
+def _staged_namespace():
     ns = {}
-    exec(_PAIR_BATCHES, ns)
+    exec(_STAGED_BATCHES, ns)
     return ns
 
 
-def test_q6k_staged_activations_match_per_cta_quantisation(kb, oracle, cuda, tmp_path):
-    """Activations quantised once per launch (pair_quant_kernel, copied into
-    each stage) give the bit-identical outputs of the per-CTA activation
-    windows (KB200_GEMV_Q6K_STAGED=0, another process), and both are within
-    the tolerance of the oracle."""
+@pytest.mark.parametrize("name", ["q6_k", "q4_k"])
+def test_staged_activations_match_per_cta_quantisation(kb, oracle, cuda, tmp_path, name):
+    """Activations quantised once per launch (a quantisation kernel, its
+    records copied into each weight stage) give the bit-identical outputs of
+    the per-CTA activation segments (the staging switch off, another
+    process), and both are within the tolerance of the oracle."""
     import os
     import subprocess
     import sys
 
     from conftest import ROOT
+    from kadan_b200 import synth
 
-    ns = _pair_namespace()
+    env_name, quant, gemv = _STAGED[name]
+    ns = _staged_namespace()
     with kb.Phase() as ph:
-        got = ns["pair_batches"](cuda)
+        got = ns["run_batches"](name, cuda)
         calls = {k: v["calls"] for k, v in ph.snapshot()["kernels"].items()}
     ph.close()
-    assert calls == {"pair_quant_kernel": 3, "gemv_q6k_pair_kernel": 3}
+    assert calls == {quant: 3, gemv: 3}
     out = tmp_path / "unstaged.npz"
-    code = _PAIR_BATCHES + f"\nnp.savez({str(out)!r}, *pair_batches(torch.device('cuda:0')))\n"
-    env = {**os.environ, "KB200_GEMV_Q6K_STAGED": "0", "KADAN_B200_NO_BUILD": "1", "PYTHONPATH": str(ROOT)}
+    code = _STAGED_BATCHES + f"\nnp.savez({str(out)!r}, *run_batches({name!r}, torch.device('cuda:0')))\n"
+    env = {**os.environ, env_name: "0", "KADAN_B200_NO_BUILD": "1", "PYTHONPATH": str(ROOT)}
     subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, check=True, timeout=600)
     with np.load(out) as z:
         want = [z[f"arr_{i}"] for i in range(len(z.files))]
-    assert len(want) == len(got) == 7
+    flat = [(i, job) for b in ns["BATCHES"][name] for i, job in enumerate(b)]
+    assert len(want) == len(got) == len(flat)
     for a, b in zip(got, want):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
-    from kadan_b200 import synth
-
-    flat = [(i, job) for b in ns["BATCHES"] for i, job in enumerate(b)]
+    make = synth.q6_k if name == "q6_k" else synth.q4_k
+    enc = getattr(kb, name.upper())
     for (i, (in_, cols, rows, xi)), y in zip(flat, got):
-        w = synth.q6_k(cols, in_, seed=10 * xi + i)
+        w = make(cols, in_, seed=10 * xi + i)
         x = synth.activations(rows * in_, seed=100 + xi, dtype="bf16").reshape(rows, in_)
-        assert rel_err(y, oracle.gemv_f64(kb.Q6_K, w, x, in_, cols)) <= TOL
+        assert rel_err(y, oracle.gemv_f64(enc, w, x, in_, cols)) <= TOL
 
 
-def test_q6k_pair_first_use_inside_capture(kb, oracle, cuda):
-    """A stream whose first Q6_K launch is captured into a CUDA graph has no
-    staging buffer (nor fixup buffer) yet: the captured launch quantises per
-    CTA, and its replay matches the eager results of another stream within
-    the oracle's tolerance."""
+@pytest.mark.parametrize("name", ["q6_k", "q4_k"])
+def test_first_use_inside_capture_quantises_per_cta(kb, cuda, name):
+    """A stream whose first launch is captured into a CUDA graph has no
+    staging buffer (nor fixup buffer) yet: the captured launches quantise per
+    CTA (no quantisation kernel is captured), and their replay matches the
+    eager results of another stream within the oracle's tolerance."""
     import torch
 
-    ns = _pair_namespace()
-    want = ns["pair_batches"](cuda)
+    _, quant, gemv = _STAGED[name]
+    ns = _staged_namespace()
+    want = ns["run_batches"](name, cuda)
     stream = torch.cuda.Stream(cuda)
     graphs = []
 
@@ -434,10 +451,10 @@ def test_q6k_pair_first_use_inside_capture(kb, oracle, cuda):
         g.replay()
 
     with kb.Phase() as ph:
-        got = ns["pair_batches"](cuda, stream=stream, capture=capture)
+        got = ns["run_batches"](name, cuda, stream=stream, capture=capture)
         calls = {k: v["calls"] for k, v in ph.snapshot()["kernels"].items()}
     ph.close()
-    assert calls == {"gemv_q6k_pair_kernel": 3}
+    assert calls == {gemv: 3}
     for a, b in zip(got, want):
         assert rel_err(a, b) <= TOL
     del graphs
