@@ -284,11 +284,15 @@ def config2_object(args, torch, kb, device, pk) -> tuple[dict, tuple]:
     wbytes, abytes = step_bytes()
     names = ["q,k,v", "o", "gate,up", "down"]
     launches = []
+    per_layer = 0
     for gi, g in enumerate(GROUPS):
         gg = graph_of(torch, stream, lambda gi=gi: launch(gi))
         us = time_graph(torch, stream, gg, max(3, steps // 4)) / LAYERS * 1e3
         nbytes = sum(weight_bytes(o, i) for _, o, i in g)
-        launches.append({"launch": names[gi], "kernel": "gemv_q4k_mma_kernel<1>", "bytes": nbytes,
+        kernels = launches_of(kb, torch, stream, lambda gi=gi: launch(gi))
+        per_layer += sum(kernels.values()) // LAYERS
+        launches.append({"launch": names[gi], "kernel": " + ".join(sorted(kernels, key=lambda k: (k.startswith("gemv"), k))),
+                         "bytes": nbytes,
                          "us": round(us, 2), "gbps": round(nbytes / us / 1e3, 1),
                          "frac": round(nbytes / us / 1e3 / pk["hbm_gbs"], 4)})
         del gg
@@ -297,8 +301,8 @@ def config2_object(args, torch, kb, device, pk) -> tuple[dict, tuple]:
     out = {"workload": "BASELINE config 2 decode: Llama-3-8B Q4_K linear stack, 32 layers, T=1",
            "value": round(value, 2), "unit": "GB/s", "ms_per_step": round(ms, 5), "steps": steps,
            "hbm_frac": round(value / pk["hbm_gbs"], 4), "weight_bytes_per_step": wbytes,
-           "launch": "one CUDA graph per step, 4 dependent launches per layer", "launches": launches,
-           "roofline": {"bound": "hbm", "kernel": "gemv_q4k_mma_kernel<1> ([gate, up] launch)",
+           "launch": f"one CUDA graph per step, {per_layer} dependent launches per layer", "launches": launches,
+           "roofline": {"bound": "hbm", "kernel": f"{gu['kernel']} ([gate, up] launch)",
                         "achieved": gu["gbps"], "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gu["frac"],
                         "traffic": GATE_UP_TRAFFIC, "algorithmic_bytes_per_launch": gu["bytes"]}}
     graph = None
@@ -402,10 +406,7 @@ def run_default(args, rank, world, local_rank):
     for gi, g in enumerate(groups):
         nbytes = sum(tp.shard(p, world, rank).out_count * tp.shard_pitch(p, tp.shard(p, world, rank)) for p in g)
         us = group_ms[gi] / layers * 1e3
-        main = ("gemv_q6k_pair_kernel<3>" if tokens <= 2 else "gemv_q6k_mma_kernel<1,3>") if g[0].encoding == kb.Q6_K \
-            else "gemv_q4k_mma_kernel<1>"
-        kernel = " + ".join(main if k.startswith(main.split("<")[0]) else k
-                            for k in sorted(group_kernels[gi], key=lambda k: k.startswith("gemv")))
+        kernel = " + ".join(sorted(group_kernels[gi], key=lambda k: (k.startswith("gemv"), k)))
         launches.append({"launch": names[gi], "kernel": kernel, "bytes": nbytes, "us": round(us, 2),
                          "kernel_launches_per_layer": {k: v // layers for k, v in group_kernels[gi].items()},
                          "gbps": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / pk["hbm_gbs"], 4),

@@ -1233,10 +1233,10 @@ __host__ __device__ constexpr int pair_chunk_bytes(int rows) {
 // kStaged: a stage also holds its chunk's quantised activations (up to two
 // tokens, copied from the launch's staging buffer), and there is no
 // per-CTA activation window.
-template <int S, int W = kWarps, bool kStaged = false> struct PairLayout {
+template <int S, int W = kWarps, bool kStaged = false, int TP = 1> struct PairLayout {
     static constexpr int kStages = S;
     // A stage starts on a 128-byte boundary (the TMA tile destination).
-    static constexpr int kStageBytes = (kQ6StageBytes + (kStaged ? pair_chunk_bytes(2) : 0) + 127) / 128 * 128;
+    static constexpr int kStageBytes = (kQ6StageBytes + (kStaged ? pair_chunk_bytes(2 * TP) : 0) + 127) / 128 * 128;
     static constexpr int kStagesOff = 0;
     static constexpr int kSegOff = kStages * kStageBytes;
     static constexpr int kSegBudget = kStaged ? 0 : pair_seg_budget<S>();
@@ -1249,6 +1249,8 @@ static_assert(2 * (PairLayout<3>::kTotal + 128 + 1024) <= 228 * 1024, "two Q6_K 
 static_assert(3 * (PairLayout<2>::kTotal + 128 + 1024) <= 228 * 1024, "three Q6_K pair CTAs per SM (2 stages)");
 static_assert(2 * (PairLayout<3, kWarps, true>::kTotal + 128 + 1024) <= 228 * 1024, "two staged pair CTAs per SM");
 static_assert(3 * (PairLayout<2, kWarps, true>::kTotal + 128 + 1024) <= 228 * 1024, "three staged pair CTAs per SM");
+static_assert(2 * (PairLayout<2, kWarps, true, 2>::kTotal + 128 + 1024) <= 228 * 1024, "two staged 4-row pair CTAs per SM");
+static_assert(PairLayout<2, kWarps, true, 2>::kStageBytes % 128 == 0, "tensor copies land on 128-byte boundaries");
 static_assert(kQ6StageBytes % 128 == 0 && PairLayout<3, kWarps, true>::kStageBytes % 128 == 0,
               "tensor copies land on 128-byte boundaries");
 static_assert(pair_chunk_bytes(1) % 16 == 0, "bulk copy sizes and source offsets are multiples of 16 bytes");
@@ -1357,6 +1359,7 @@ struct StageQuantRegion {
     const float* x;
     uint8_t* dst;
     uint32_t in, rows, first_item;  // items: blocks x rows, prefix over regions
+    uint32_t group_rows;            // pair layout: rows per row group (groups follow one another)
 };
 struct StageQuantParams {
     StageQuantRegion regions[kMaxJobsQ];
@@ -1414,17 +1417,20 @@ __global__ void __launch_bounds__(128) pair_quant_kernel(const __grid_constant__
     const uint32_t warps = gridDim.x * (blockDim.x >> 5);
     for (uint32_t item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < p.items; item += warps) {
         const StageQuantRegion& g = quant_region(p, item);
-        const int rows = int(g.rows);
         const uint32_t local = item - g.first_item;
-        const int blk = int(local / g.rows), tok = int(local % g.rows);
+        const int blk = int(local / g.rows), row = int(local % g.rows);
         const int chunk = blk / kQ6Chunk, b = blk % kQ6Chunk;
-        uint8_t* base = g.dst + size_t(chunk) * pair_chunk_bytes(rows);
+        // Row group of this row, its rows and the row's token within it.
+        const int gr = int(g.group_rows), rg = row / gr, tok = row % gr;
+        const int rows = min(gr, int(g.rows) - rg * gr);
+        const int chunks = int((g.in / 256 + kQ6Chunk - 1) / kQ6Chunk);
+        uint8_t* base = g.dst + size_t(rg) * chunks * pair_chunk_bytes(gr) + size_t(chunk) * pair_chunk_bytes(rows);
         uint32_t* words = reinterpret_cast<uint32_t*>(base);
         uint8_t* xbytes = base + kQ6Chunk * rows * kPairWordBytes;
         float* scales = reinterpret_cast<float*>(xbytes + kQ6Chunk * rows * kPairXBytes);
         const bool vec = (reinterpret_cast<uintptr_t>(g.x) & 15u) == 0 && (g.in & 3) == 0;
         float v[8];
-        load_lane8(v, g.x + size_t(tok) * g.in + size_t(blk) * 256 + lane * 8, vec);
+        load_lane8(v, g.x + size_t(row) * g.in + size_t(blk) * 256 + lane * 8, vec);
         pair_quant_store(v, words, xbytes, scales, rows, b, tok, lane);
     }
     // The GEMV reads the buffer with bulk async copies.
@@ -1452,15 +1458,20 @@ __device__ __forceinline__ int sext_byte(uint32_t w, uint32_t sel) {
 }
 
 // One block of rows g (bg) and g + 8 (b8): adds this lane's sub-blocks of
-// its token to acc. A lane supplies B column g (token g / 4, parity g / 2 % 2,
-// level g % 2): bw points at its word of pair 0 (pairs `pair_stride` words
-// apart), xw is its X word. It receives C columns 2t, 2t + 1: token t / 2,
-// parity t % 2 (the scales it applies), h and l; sc_tok is that token's
-// activation scale.
-template <bool kOdd>
+// its tokens to acc, for TP pairs of tokens (2 TP input rows per pass). A lane
+// supplies B column g of every token pair (token 2 tp + g / 4, parity g / 2 %
+// 2, level g % 2): bw points at its word of pair 0 for token pair 0 (pairs
+// `pair_stride` words apart, token pairs 32 words apart), xw[tp] are its X
+// words. It receives C columns 2t, 2t + 1: token 2 tp + t / 2, parity t % 2
+// (the scales it applies), h and l; sc_tok[tp] is that token's activation
+// scale. boff[tp]: word offset of token pair tp's B word from bw (tokens
+// past the last present one are clamped to it). The weight operands are
+// unpacked once for all token pairs.
+template <bool kOdd, int TP>
 __device__ __forceinline__ void q6k_pair_block(const uint8_t* bg, const uint8_t* b8, const uint32_t* bw, int pair_stride,
-                                               uint32_t xw, int g, int t, float sc_tok, float& acc_g, float& acc_8,
-                                               bool& finite_g, bool& finite_8) {
+                                               const int (&boff)[TP], const uint32_t (&xw)[TP], int g, int t,
+                                               const float (&sc_tok)[TP],
+                                               float (&acc_g)[TP], float (&acc_8)[TP], bool& finite_g, bool& finite_8) {
     const float dg = half_bits_to_float(*reinterpret_cast<const uint16_t*>(bg + 208));
     const float d8 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b8 + 208));
     finite_g = finite_g && isfinite(dg);
@@ -1468,12 +1479,16 @@ __device__ __forceinline__ void q6k_pair_block(const uint8_t* bg, const uint8_t*
     const bool b_odd = (g >> 1) & 1;  // parity of the B column this lane supplies
     const bool odd_col = t & 1;       // parity of the C columns this lane receives
     // -32 correction: sum_s sc_s (64 X1_s + X0_s) for digit (t % 2) = X1 / X0.
-    int I[4];
+    int I[TP][4];
     {
-        int cx[4];
-        imma16(cx, ld_word<kOdd>(bg + 192 + 4 * t), ld_word<kOdd>(b8 + 192 + 4 * t), xw);
+        const uint32_t sa = ld_word<kOdd>(bg + 192 + 4 * t), sb = ld_word<kOdd>(b8 + 192 + 4 * t);
         const int mult = odd_col ? -32 : -32 * 64;
-        I[0] = mult * cx[0], I[1] = mult * cx[1], I[2] = mult * cx[2], I[3] = mult * cx[3];
+#pragma unroll
+        for (int tp = 0; tp < TP; ++tp) {
+            int cx[4];
+            imma16(cx, sa, sb, xw[tp]);
+            I[tp][0] = mult * cx[0], I[tp][1] = mult * cx[1], I[tp][2] = mult * cx[2], I[tp][3] = mult * cx[3];
+        }
     }
     uint32_t scg[4], sc8[4];
 #pragma unroll
@@ -1502,19 +1517,25 @@ __device__ __forceinline__ void q6k_pair_block(const uint8_t* bg, const uint8_t*
             const int a = qt & 1;
             const uint32_t a0 = q6_code(qlg[a][0], qhg[0], ls, hs), a1 = q6_code(ql8[a][0], qh8[0], ls, hs);
             const uint32_t a2 = q6_code(qlg[a][1], qhg[1], ls, hs), a3 = q6_code(ql8[a][1], qh8[1], ls, hs);
-            const uint32_t w = bw[(4 * ip + qt) * pair_stride];
-            int c[4];
-            imma(c, a0, a1, a2, a3, b_odd ? 0u : w, b_odd ? w : 0u);
             // Scale of sub-block 8 ip + 2 qt + par: word 2 ip + qt / 2, byte 2 (qt % 2) + par.
             const uint32_t sel = (qt & 1) ? sel1 : sel0;
             const int sg = sext_byte(scg[2 * ip + (qt >> 1)], sel);
             const int s8 = sext_byte(sc8[2 * ip + (qt >> 1)], sel);
-            I[0] += sg * c[0], I[1] += sg * c[1];
-            I[2] += s8 * c[2], I[3] += s8 * c[3];
+#pragma unroll
+            for (int tp = 0; tp < TP; ++tp) {
+                const uint32_t w = bw[(4 * ip + qt) * pair_stride + boff[tp]];
+                int c[4];
+                imma(c, a0, a1, a2, a3, b_odd ? 0u : w, b_odd ? w : 0u);
+                I[tp][0] += sg * c[0], I[tp][1] += sg * c[1];
+                I[tp][2] += s8 * c[2], I[tp][3] += s8 * c[3];
+            }
         }
     }
-    acc_g = fmaf(dg * sc_tok, fmaf(float(I[1]), 1.f / 254.f, float(I[0])), acc_g);
-    acc_8 = fmaf(d8 * sc_tok, fmaf(float(I[3]), 1.f / 254.f, float(I[2])), acc_8);
+#pragma unroll
+    for (int tp = 0; tp < TP; ++tp) {
+        acc_g[tp] = fmaf(dg * sc_tok[tp], fmaf(float(I[tp][1]), 1.f / 254.f, float(I[tp][0])), acc_g[tp]);
+        acc_8[tp] = fmaf(d8 * sc_tok[tp], fmaf(float(I[tp][3]), 1.f / 254.f, float(I[tp][2])), acc_8[tp]);
+    }
 }
 
 // Q6_K decode GEMV for one or two input rows per pass: the Q6_K kernel's
@@ -1529,9 +1550,16 @@ __device__ __forceinline__ void q6k_pair_block(const uint8_t* bg, const uint8_t*
 // activation copies of those stages, then both parts of every later stage.
 // Otherwise each CTA quantises a window of activations into shared memory
 // whenever its chunks leave the current one.
-template <int S, int W, bool kStaged>
-__global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_kernel(const __grid_constant__ MmaParams p) {
-    using L = PairLayout<S, W, kStaged>;
+//
+// TP token pairs per pass (staged only for TP = 2): 2 TP input rows share
+// each unpacked weight fragment; more rows are row groups, whose staged
+// activations follow one another (group stride: the job's chunks x a full
+// group's chunk bytes).
+template <int S, int W, bool kStaged, int TP = 1>
+__global__ void __launch_bounds__(32 * W + 32, S == 2 && TP == 1 ? 3 : 2)
+    gemv_q6k_pair_kernel(const __grid_constant__ MmaParams p) {
+    static_assert(TP == 1 || kStaged, "4-row passes take staged activations");
+    using L = PairLayout<S, W, kStaged, TP>;
     constexpr int kStages = L::kStages;
     constexpr int CT = 32 * W;               // consumer threads
     constexpr int kPerWarp = kQ6Chunk / W;   // blocks of a stage per consumer warp
@@ -1579,7 +1607,10 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
         while (pieces.next(p, pc)) {
             const MmaJob& job = p.jobs[pc.job];
             const int row0 = int((pc.tile / job.row_groups) * uint32_t(kQ6Rows));
-            const uint32_t act_bytes = kStaged ? uint32_t(pair_chunk_bytes(int(job.rows))) : 0u;
+            // Staged activations of this tile's row group.
+            const uint32_t rg = pc.tile % job.row_groups;
+            const uint32_t act_bytes = kStaged ? uint32_t(pair_chunk_bytes(int(min(job.group_rows, job.rows - rg * job.group_rows)))) : 0u;
+            const uint8_t* act_src = kStaged ? job.staged + size_t(rg) * job.nblocks * pair_chunk_bytes(int(job.group_rows)) : nullptr;
             asm volatile("prefetch.tensormap [%0];" ::"l"(&job.map) : "memory");
             for (uint32_t ch = pc.k0; ch < pc.k1; ++ch, ++it) {
                 const int slot = int(it % kStages);
@@ -1591,7 +1622,7 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
                 mbar_expect_tx(&full[slot], uint32_t(kQ6StageBytes) + act_bytes);
                 tma_load_2d(stage, &job.map, int(ch) * (kQ6Chunk * kQ6Block / 8), row0, &full[slot]);
                 if constexpr (kStaged) {
-                    const uint8_t* src = job.staged + size_t(ch) * act_bytes;
+                    const uint8_t* src = act_src + size_t(ch) * act_bytes;
                     if (staged_ready) {
                         bulk_g2s(stage + kQ6StageBytes, src, act_bytes, &full[slot]);
                     } else {
@@ -1637,16 +1668,24 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
         const PairSegment seg(rows, kStaged ? 0 : L::kSegOff, kStaged ? pair_chunk_bytes(rows) : L::kSegBudget);
         if (!kStaged && seg.blocks < kQ6Chunk)
             atomicExch(abort_flag, 1);
-        // B side: the token of the column this lane supplies (g / 4) and its
-        // word in every group of 16; C side: the token of the columns it
-        // receives (t / 2). Both clamped to the rows present.
-        const int btok = min(g >> 2, rows - 1), ctok = min(t >> 1, rows - 1);
+        // B side: the token of the column this lane supplies (2 tp + g / 4)
+        // and its word in every group of 16; C side: the token of the
+        // columns it receives (2 tp + t / 2). Both clamped to the rows present.
+        int btok[TP], ctok[TP], boff[TP];
+#pragma unroll
+        for (int tp = 0; tp < TP; ++tp) {
+            btok[tp] = min(2 * tp + (g >> 2), rows - 1), ctok[tp] = min(2 * tp + (t >> 1), rows - 1);
+            boff[tp] = (btok[tp] - btok[0]) * 16;
+        }
         const int lane_word = (g & 3) * 4 + t;
         const uint32_t my_row = row0 + g;
         const bool valid_lo = my_row < job.columns, valid_hi = my_row + 8 < job.columns;
         const bool check = job.status != nullptr;
         bool finite_g = true, finite_8 = true;
-        float acc_g = 0.f, acc_8 = 0.f;
+        float acc_g[TP], acc_8[TP];
+#pragma unroll
+        for (int tp = 0; tp < TP; ++tp)
+            acc_g[tp] = acc_8[tp] = 0.f;
 
         for (uint32_t ch = pc.k0; ch < pc.k1; ++ch, ++it) {
             const int slot = int(it % kStages);
@@ -1688,13 +1727,20 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
                     const int sblk = blk_first + b - act_blk0;
                     const uint8_t* bg = stage + g * (kQ6Chunk * kQ6Block) + b * kQ6Block;
                     const uint8_t* b8 = bg + 8 * (kQ6Chunk * kQ6Block);
-                    const uint32_t* bw = words + (sblk * 8 * rows + btok) * 16 + lane_word;
-                    const uint32_t xw = xwords[(sblk * rows + btok) * 16 + lane_word];
-                    const float sc_tok = scales[sblk * rows + ctok];
+                    const uint32_t* bw = words + (sblk * 8 * rows + btok[0]) * 16 + lane_word;
+                    uint32_t xw[TP];
+                    float sc_tok[TP];
+#pragma unroll
+                    for (int tp = 0; tp < TP; ++tp) {
+                        xw[tp] = xwords[(sblk * rows + btok[tp]) * 16 + lane_word];
+                        sc_tok[tp] = scales[sblk * rows + ctok[tp]];
+                    }
                     if (b & 1)
-                        q6k_pair_block<true>(bg, b8, bw, rows * 16, xw, g, t, sc_tok, acc_g, acc_8, finite_g, finite_8);
+                        q6k_pair_block<true, TP>(bg, b8, bw, rows * 16, boff, xw, g, t, sc_tok, acc_g, acc_8, finite_g,
+                                                 finite_8);
                     else
-                        q6k_pair_block<false>(bg, b8, bw, rows * 16, xw, g, t, sc_tok, acc_g, acc_8, finite_g, finite_8);
+                        q6k_pair_block<false, TP>(bg, b8, bw, rows * 16, boff, xw, g, t, sc_tok, acc_g, acc_8, finite_g,
+                                                  finite_8);
                 }
             }
             __syncwarp();
@@ -1703,13 +1749,20 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 ? 3 : 2) gemv_q6k_pair_ker
         }
         if (check && !((finite_g || !valid_lo) && (finite_8 || !valid_hi)))
             atomicOr(job.status, 1u);
-        // Lanes t = 2k, 2k + 1 hold token k's even and odd sub-blocks: add
-        // them, then give lane t the sums of token t (lanes 0 and 1 of each
-        // group of four) as the common piece ending expects.
-        acc_g += __shfl_xor_sync(0xffffffffu, acc_g, 1);
-        acc_8 += __shfl_xor_sync(0xffffffffu, acc_8, 1);
+        // Lanes t = 2k, 2k + 1 hold token 2 tp + k's even and odd
+        // sub-blocks: add them, then give lane t the sums of token t (token
+        // pair t / 2, lane 2 (t % 2) of each group of four) as the common
+        // piece ending expects.
         const int from = (lane & ~3) | ((2 * t) & 3);
-        float acc[1][2] = {{__shfl_sync(0xffffffffu, acc_g, from), __shfl_sync(0xffffffffu, acc_8, from)}};
+        float acc[1][2];
+#pragma unroll
+        for (int tp = 0; tp < TP; ++tp) {
+            acc_g[tp] += __shfl_xor_sync(0xffffffffu, acc_g[tp], 1);
+            acc_8[tp] += __shfl_xor_sync(0xffffffffu, acc_8[tp], 1);
+            const float vg = __shfl_sync(0xffffffffu, acc_g[tp], from), v8 = __shfl_sync(0xffffffffu, acc_8[tp], from);
+            if (tp == 0 || (t >> 1) == tp)
+                acc[0][0] = vg, acc[0][1] = v8;
+        }
         finish_piece<1, decltype(await_dependency), CT>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0,
                                                         rows, red, abort_flag, await_dependency);
     }
@@ -1844,7 +1897,7 @@ struct Tuning {
     uint32_t min_units = kMinUnitsPerCta;       // KB200_GEMV_MIN_UNITS=<units per CTA>
     uint32_t q6_min_units = kQ6MinUnitsPerCta;  // KB200_GEMV_Q6K_MIN_UNITS=<units per CTA>
     int ctas_per_sm = 0;                        // KB200_GEMV_CTAS_PER_SM=<n>: grid slots per SM (0: all that fit)
-    int q6_stages = 3;                          // KB200_GEMV_Q6K_STAGES=2|3: ring depth at 1-4 rows per pass
+    int q6_stages = 0;                          // KB200_GEMV_Q6K_STAGES=2|3: ring depth at 1-4 rows per pass (0: auto)
     bool q6_pair = true;                        // KB200_GEMV_Q6K_PAIR=0: 1-2 rows on the 4-row kernel
     bool q6_staged = true;                      // KB200_GEMV_Q6K_STAGED=0: pair kernel quantises per CTA
     bool q4_staged = true;                      // KB200_GEMV_Q4K_STAGED=0: Q4_K kernel quantises per CTA
@@ -1896,20 +1949,21 @@ template <int NT, int S> int q6k_slots() {
     return sm_count() * blocks_per_sm[dev];
 }
 
-template <int S, int W, bool kStaged> int q6k_pair_slots() {
+template <int S, int W, bool kStaged, int TP = 1> int q6k_pair_slots() {
     static int blocks_per_sm[64] = {};
     static std::mutex lock;
     int dev = 0;
     cudaGetDevice(&dev);
-    constexpr int smem = PairLayout<S, W, kStaged>::kTotal + 128;
+    constexpr int smem = PairLayout<S, W, kStaged, TP>::kTotal + 128;
     std::lock_guard<std::mutex> guard(lock);
     if (!blocks_per_sm[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_pair_kernel<S, W, kStaged>,
+        cudaError_t e = cudaFuncSetAttribute(gemv_q6k_pair_kernel<S, W, kStaged, TP>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_pair_kernel attribute");
         int n = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_pair_kernel<S, W, kStaged>, 32 * W + 32, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_q6k_pair_kernel<S, W, kStaged, TP>, 32 * W + 32,
+                                                          smem);
         if (e != cudaSuccess)
             return -cuda_fail(e, "gemv_q6k_pair_kernel occupancy");
         blocks_per_sm[dev] = n > 0 ? n : 1;
@@ -1977,12 +2031,14 @@ bool stage_inputs(MmaParams& p, uint8_t* staging, StageQuantParams& q, bool q4k)
     for (uint32_t m = 0; m < p.count; ++m) {
         MmaJob& d = p.jobs[m];
         uint32_t r = 0;
-        while (r < q.count && !(q.regions[r].x == d.input && q.regions[r].in == d.in && q.regions[r].rows == d.rows))
+        while (r < q.count && !(q.regions[r].x == d.input && q.regions[r].in == d.in && q.regions[r].rows == d.rows
+                                && q.regions[r].group_rows == d.group_rows))
             ++r;
         if (r == q.count) {
             const size_t blocks = d.in / 256;
             const size_t bytes = q4k ? blocks * size_t(q4k_record_bytes(int(d.rows)))
-                                     : (blocks + kQ6Chunk - 1) / kQ6Chunk * size_t(pair_chunk_bytes(int(d.rows)));
+                                     : size_t(d.row_groups) * ((blocks + kQ6Chunk - 1) / kQ6Chunk)
+                                           * size_t(pair_chunk_bytes(int(d.group_rows)));
             if (used + bytes > kStagingBytes) {
                 for (uint32_t k = 0; k < p.count; ++k)
                     p.jobs[k].staged = nullptr;
@@ -1993,6 +2049,7 @@ bool stage_inputs(MmaParams& p, uint8_t* staging, StageQuantParams& q, bool q4k)
             g.dst = staging + used;
             g.in = d.in;
             g.rows = d.rows;
+            g.group_rows = d.group_rows;
             g.first_item = q.items;
             q.items += d.in / 256 * d.rows;
             used += bytes;
@@ -2034,18 +2091,44 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     for (const auto* j : jobs)
         max_rows = std::max(max_rows, int(std::min(j->rows, uint32_t(KB200_BATCH_ROWS))));
     const int nt = max_rows <= 4 ? 1 : 2;
-    // 1-2 rows: the paired-sub-block kernel (2 rows per pass).
+    // 1-2 rows: the paired-sub-block kernel (2 rows per pass). 3-8 rows: the
+    // same kernel with two token pairs per pass (row groups of 4) when the
+    // activations can be staged, else the 4/8-row kernel.
     const bool pair = max_rows <= 2 && tuning().q6_pair;
-    const uint32_t group_rows = pair ? 2u : uint32_t(4 * nt);
-    const bool two_stage = nt == 1 && tuning().q6_stages == 2;
-    uint8_t* staging = pair && tuning().q6_staged ? staging_for(stream) : nullptr;
+    // Ring depth: 2 stages (three CTAs per SM) for the pair kernel when no job
+    // is longer than 64 super-blocks (more warps for short, launch-bound K),
+    // else 3 (two CTAs per SM, deeper ring for long K); forced by the tuning.
+    uint32_t max_in = 0;
+    for (const auto* j : jobs)
+        max_in = std::max(max_in, j->in);
+    const bool two_stage = nt == 1
+                           && (tuning().q6_stages == 2 || (tuning().q6_stages == 0 && pair && max_in <= 16384));
+    uint8_t* staging = max_rows <= 8 && tuning().q6_pair && tuning().q6_staged ? staging_for(stream) : nullptr;
     const Fixup* fixup = tuning().balanced ? fixup_for(stream) : nullptr;
     // Both pair kernels are set up on the first call (which may be the only
     // one outside graph capture), whichever this launch takes.
     const int pair_slots = !pair ? 0 : two_stage ? q6k_pair_slots<2, 4, false>() : q6k_pair_slots<3, 4, false>();
     const int pair_slots_staged = !pair ? 0 : two_stage ? q6k_pair_slots<2, 4, true>() : q6k_pair_slots<3, 4, true>();
+    const int quad_slots = !pair && staging ? q6k_pair_slots<2, 4, true, 2>() : 0;
+    if (pair_slots < 0 || pair_slots_staged < 0 || quad_slots < 0)
+        return -std::min(pair_slots, std::min(pair_slots_staged, quad_slots));
     for (size_t first = 0; first < jobs.size(); first += kMaxJobsQ) {
         const size_t n = std::min(jobs.size() - first, size_t(kMaxJobsQ));
+        // 4-row passes when this batch's distinct inputs fit the staging buffer.
+        bool quad = false;
+        if (!pair && staging) {
+            size_t bytes = 0;
+            for (size_t m = 0; m < n; ++m) {
+                const auto& j = *jobs[first + m];
+                bool seen = false;
+                for (size_t k = 0; k < m && !seen; ++k)
+                    seen = jobs[first + k]->input == j.input && jobs[first + k]->in == j.in && jobs[first + k]->rows == j.rows;
+                if (!seen)
+                    bytes += size_t((j.rows + 3) / 4) * ((j.in / 256 + kQ6Chunk - 1) / kQ6Chunk) * size_t(pair_chunk_bytes(4));
+            }
+            quad = bytes <= kStagingBytes;
+        }
+        const uint32_t group_rows = pair ? 2u : quad ? 4u : uint32_t(4 * nt);
         MmaParams p;
         std::memset(&p, 0, sizeof(p));
         p.watchdog = watchdog_word();
@@ -2086,8 +2169,11 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         p.count = uint32_t(n);
         p.total_tiles = tiles;
         StageQuantParams q;
-        const bool staged = staging && stage_inputs(p, staging, q, false);
-        int slots = !pair ? (nt == 2 ? q6k_slots<2, 2>() : two_stage ? q6k_slots<1, 2>() : q6k_slots<1, 3>())
+        const bool staged = staging && (pair || quad) && stage_inputs(p, staging, q, false);
+        if (quad && !staged)  // only a batch without any super-block gets here
+            return fail(KB200_INVALID, "Q6_K jobs without input values");
+        int slots = quad     ? quad_slots
+                    : !pair  ? (nt == 2 ? q6k_slots<2, 2>() : two_stage ? q6k_slots<1, 2>() : q6k_slots<1, 3>())
                     : staged ? pair_slots_staged : pair_slots;
         if (slots <= 0)
             return -slots;
@@ -2109,7 +2195,8 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
         cfg.blockDim = dim3(kThreadsQ);
-        cfg.dynamicSmemBytes = (!pair       ? (nt == 2      ? Q6Layout<2, 2>::kTotal
+        cfg.dynamicSmemBytes = (quad        ? PairLayout<2, 4, true, 2>::kTotal
+                                : !pair     ? (nt == 2      ? Q6Layout<2, 2>::kTotal
                                                : two_stage ? Q6Layout<1, 2>::kTotal
                                                            : Q6Layout<1, 3>::kTotal)
                                 : staged    ? (two_stage ? PairLayout<2, 4, true>::kTotal : PairLayout<3, 4, true>::kTotal)
@@ -2121,9 +2208,11 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        TraceScope trace(pair ? KB200_KERNEL_GEMV_Q6K_PAIR : KB200_KERNEL_GEMV_Q6K_MMA, stream);
+        TraceScope trace(pair || quad ? KB200_KERNEL_GEMV_Q6K_PAIR : KB200_KERNEL_GEMV_Q6K_MMA, stream);
         cudaError_t e;
-        if (pair && staged)
+        if (quad)
+            e = cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 4, true, 2>, p);
+        else if (pair && staged)
             e = two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 4, true>, p)
                           : cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<3, 4, true>, p);
         else if (pair)

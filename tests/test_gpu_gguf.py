@@ -429,6 +429,41 @@ def test_staged_activations_match_per_cta_quantisation(kb, oracle, cuda, tmp_pat
         assert rel_err(y, oracle.gemv_f64(enc, w, x, in_, cols)) <= TOL
 
 
+@pytest.mark.parametrize("rows", [3, 4, 6, 8])
+def test_q6k_multi_row_pairs_of_tokens(kb, oracle, cuda, rows):
+    """Q6_K at 3-8 input rows: the pair kernel with two token pairs per pass
+    (row groups of 4 past 4 rows), activations staged once per launch; a
+    batch of jobs sharing one input, one with a ragged last chunk, one with a
+    long K; within the oracle's tolerance."""
+    import torch
+
+    from kadan_b200 import synth
+    from kadan_b200.tensor_parallel import pad_rows
+
+    shapes = [(8192, 1024), (8192, 256), (2304, 200), (28672, 160)]
+    x = {in_: synth.activations(rows * in_, seed=rows + in_, dtype="bf16").reshape(rows, in_) for in_, _ in shapes}
+    xd = {in_: to_dev(v, cuda) for in_, v in x.items()}
+    keep, jobs, ys, ws = [], [], [], []
+    for i, (in_, out) in enumerate(shapes):
+        w = synth.q6_k(out, in_, seed=7 * i + rows)
+        pitch = (w.shape[1] + 15) // 16 * 16
+        wd = to_dev(pad_rows(w, pitch), cuda)
+        y = torch.full((rows, out), float("nan"), device=cuda)
+        keep.append(wd)
+        ws.append(w)
+        ys.append(y)
+        jobs.append(kb.gemv_job(kb.Q6_K, wd, xd[in_], y, in_=in_, columns=out, rows=rows, row_bytes_=pitch))
+    with kb.Phase() as ph:
+        kb.gguf_gemv_batch(jobs)
+        torch.cuda.synchronize()
+        calls = {k: v["calls"] for k, v in ph.snapshot()["kernels"].items()}
+    ph.close()
+    assert calls == {"pair_quant_kernel": 1, "gemv_q6k_pair_kernel": 1}
+    for (in_, out), w, y in zip(shapes, ws, ys):
+        assert rel_err(y.cpu().numpy(), oracle.gemv_f64(kb.Q6_K, w, x[in_], in_, out)) <= TOL
+    assert kb.take_device_error() == 0
+
+
 @pytest.mark.parametrize("name", ["q6_k", "q4_k"])
 def test_first_use_inside_capture_quantises_per_cta(kb, cuda, name):
     """A stream whose first launch is captured into a CUDA graph has no
