@@ -171,11 +171,14 @@ __host__ __device__ constexpr int q4k_record_bytes(int rows) {
 }
 
 // kStaged: a stage (64 rows x 2 super-blocks) also holds the activation
-// records of its super-blocks for up to 4 tokens, copied from the launch's
-// staging buffer, and there is no activation segment.
-template <bool kStaged = false> struct LayoutQ4 {
+// records of its super-blocks for up to 4 NT tokens, copied from the launch's
+// staging buffer, and there is no activation segment. Staged 8-row passes
+// keep two stages, so that three CTAs still fit an SM.
+template <bool kStaged = false, int NT = 1> struct LayoutQ4 {
+    static constexpr int kStages = kStaged && NT == 2 ? 2 : ::kb200::kStages;
     // A stage starts on a 128-byte boundary (the TMA tile destinations).
-    static constexpr int kStride = kStaged ? (kStageBytes + 2 * q4k_record_bytes(4) + 127) / 128 * 128 : kStageBytes;
+    static constexpr int kStride =
+        kStaged ? (kStageBytes + 2 * q4k_record_bytes(4 * NT) + 127) / 128 * 128 : kStageBytes;
     static constexpr int kStagesOff = 0;
     static constexpr int kSegOff = kStages * kStride;
     static constexpr int kRedOff = kSegOff + (kStaged ? 0 : kSegBudget);  // split-K partials
@@ -184,8 +187,10 @@ template <bool kStaged = false> struct LayoutQ4 {
     static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
 };
 using Layout = LayoutQ4<false>;
-static_assert(kStageBytes % 128 == 0 && LayoutQ4<true>::kStride % 128 == 0, "tensor copies land on 128-byte boundaries");
+static_assert(kStageBytes % 128 == 0 && LayoutQ4<true>::kStride % 128 == 0 && LayoutQ4<true, 2>::kStride % 128 == 0,
+              "tensor copies land on 128-byte boundaries");
 static_assert(3 * (LayoutQ4<true>::kTotal + 128 + 1024) <= 228 * 1024, "three staged Q4_K CTAs per SM");
+static_assert(3 * (LayoutQ4<true, 2>::kTotal + 128 + 1024) <= 228 * 1024, "three staged 8-row Q4_K CTAs per SM");
 
 // Segment of `rows` tokens: the most whole stages (multiples of `bps`
 // super-blocks) that fit kSegBudget; operands first, then minimum-term
@@ -631,14 +636,15 @@ __device__ __forceinline__ void finish_piece(const MmaParams& p, const Piece& pc
     }
 }
 
-// kStaged (64-row tiles, at most 4 input rows): the activations come
+// kStaged (64-row tiles, one row group of at most 8 input rows): the activations come
 // quantised from the launch's staging buffer (q4k_quant_kernel, launched just
 // before), one record per super-block copied with the stage's weights; the
 // producer issues the first stages' weight loads before it waits for the
 // quantisation kernel. Otherwise the consumers quantise activation segments.
 template <int NT, bool kStaged = false>
 __global__ void __launch_bounds__(kThreadsQ, 3) gemv_q4k_mma_kernel(const __grid_constant__ MmaParams p) {
-    using L = LayoutQ4<kStaged>;
+    using L = LayoutQ4<kStaged, NT>;
+    constexpr int kStages = L::kStages;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // TMA destinations (no swizzle) want 128-byte alignment.
     uint8_t* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
@@ -1789,7 +1795,7 @@ template <int NT, bool kStaged = false> int kernel_slots() {
     static std::mutex lock;
     int dev = 0;
     cudaGetDevice(&dev);
-    constexpr int smem = LayoutQ4<kStaged>::kTotal + 128;  // + alignment slack
+    constexpr int smem = LayoutQ4<kStaged, NT>::kTotal + 128;  // + alignment slack
     std::lock_guard<std::mutex> guard(lock);
     if (!blocks_per_sm[dev]) {
         cudaError_t e = cudaFuncSetAttribute(gemv_q4k_mma_kernel<NT, kStaged>,
@@ -1975,7 +1981,7 @@ template <int NT, bool kStaged = false> int launch_q4k(const MmaParams& p, uint3
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreadsQ);
-    cfg.dynamicSmemBytes = LayoutQ4<kStaged>::kTotal + 128;
+    cfg.dynamicSmemBytes = LayoutQ4<kStaged, NT>::kTotal + 128;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -2241,12 +2247,12 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     int slots = nt == 1 ? kernel_slots<1>() : kernel_slots<2>();
     if (slots <= 0)
         return -slots;
-    // Activations quantised once per launch (64-row tiles, at most 4 rows)
+    // Activations quantised once per launch (64-row tiles, one row group)
     // when the staged kernel fits as many CTAs per SM (both are set up on
     // the first call, which may be the only one outside graph capture).
     uint8_t* staging = nullptr;
-    if (nt == 1 && tuning().q4_staged) {
-        const int staged_slots = kernel_slots<1, true>();
+    if (tuning().q4_staged) {
+        const int staged_slots = nt == 1 ? kernel_slots<1, true>() : kernel_slots<2, true>();
         if (staged_slots <= 0)
             return -staged_slots;
         if (staged_slots == slots)
@@ -2350,11 +2356,14 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
             p.partials = fixup->partials;
         }
         StageQuantParams q;
-        const bool staged = staging && R == 64 && stage_inputs(p, staging, q, true);
+        bool one_group = true;
+        for (uint32_t m = 0; m < p.count; ++m)
+            one_group = one_group && p.jobs[m].row_groups == 1;
+        const bool staged = staging && R == 64 && one_group && stage_inputs(p, staging, q, true);
         if (staged)
             if (const int st = launch_stage_quant(q, stream, true))
                 return st;
-        const int s = nt == 2 ? launch_q4k<2>(p, grid, stream)
+        const int s = nt == 2 ? (staged ? launch_q4k<2, true>(p, grid, stream) : launch_q4k<2>(p, grid, stream))
                       : staged ? launch_q4k<1, true>(p, grid, stream) : launch_q4k<1>(p, grid, stream);
         if (s)
             return s;

@@ -337,9 +337,9 @@ def test_q6k_tensor_pipe_parity(kb, oracle, cuda, in_, out, rows):
 
 # Batches whose activations are quantised once per launch: Q6_K at 1-2
 # input rows (the pair kernel; q/k/v-like jobs sharing one input, a long-K
-# job, mixed 1- and 2-row jobs with a ragged last chunk) and Q4_K at up to 4
-# rows on 64-row tiles (balanced splits; shared inputs, 3- and 4-row jobs,
-# K of 9 super-blocks).
+# job, mixed 1- and 2-row jobs with a ragged last chunk) and Q4_K at up to 8
+# rows on 64-row tiles (balanced splits; shared inputs, 3-, 4-, 6- and 8-row
+# jobs, K of 9 super-blocks).
 _STAGED_BATCHES = r"""
 import numpy as np, torch
 import kadan_b200 as kb
@@ -352,7 +352,8 @@ BATCHES = {
              ((256, 33, 2, 4),)),
     "q4_k": (((8192, 8192, 1, 0), (8192, 4096, 1, 0)),
              ((4096, 14336, 3, 1), (4096, 2048, 4, 2)),
-             ((2304, 28672, 2, 3),)),
+             ((2304, 28672, 2, 3),),
+             ((8192, 8192, 8, 5), (8192, 4096, 6, 6))),
 }
 
 
@@ -410,7 +411,7 @@ def test_staged_activations_match_per_cta_quantisation(kb, oracle, cuda, tmp_pat
         got = ns["run_batches"](name, cuda)
         calls = {k: v["calls"] for k, v in ph.snapshot()["kernels"].items()}
     ph.close()
-    assert calls == {quant: 3, gemv: 3}
+    assert calls == {quant: len(ns["BATCHES"][name]), gemv: len(ns["BATCHES"][name])}
     out = tmp_path / "unstaged.npz"
     code = _STAGED_BATCHES + f"\nnp.savez({str(out)!r}, *run_batches({name!r}, torch.device('cuda:0')))\n"
     env = {**os.environ, env_name: "0", "KADAN_B200_NO_BUILD": "1", "PYTHONPATH": str(ROOT)}
@@ -489,7 +490,7 @@ def test_first_use_inside_capture_quantises_per_cta(kb, cuda, name):
         got = ns["run_batches"](name, cuda, stream=stream, capture=capture)
         calls = {k: v["calls"] for k, v in ph.snapshot()["kernels"].items()}
     ph.close()
-    assert calls == {gemv: 3}
+    assert calls == {gemv: len(ns["BATCHES"][name])}
     for a, b in zip(got, want):
         assert rel_err(a, b) <= TOL
     del graphs
