@@ -73,7 +73,8 @@ GATE_UP_TRAFFIC = 66922496  # 66,164,224 read + 758,272 written
 # DRAM bytes (read + write) per launch of config-4 groups at N=1, keyed by
 # group, from ncu captures of a 2-layer stack (a launch has the same size at
 # any layer count; the profile summaries give the commands).
-C4_TRAFFIC: dict = {"down": 194813184 + 7026944}  # gemv_q6k_pair_kernel<3, 4>
+C4_TRAFFIC: dict = {"down": 194910464 + 4431872,  # gemv_q6k_pair_kernel<3, 4, staged>
+                    "gate,up": 270300928 + 4588800}  # gemv_q4k_mma_kernel<1, staged>
 
 
 def weight_bytes(out: int, in_: int) -> int:

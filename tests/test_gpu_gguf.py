@@ -338,8 +338,9 @@ def test_q6k_tensor_pipe_parity(kb, oracle, cuda, in_, out, rows):
 # Batches whose activations are quantised once per launch: Q6_K at 1-2
 # input rows (the pair kernel; q/k/v-like jobs sharing one input, a long-K
 # job, mixed 1- and 2-row jobs with a ragged last chunk) and Q4_K at up to 8
-# rows on 64-row tiles (balanced splits; shared inputs, 3-, 4-, 6- and 8-row
-# jobs, K of 9 super-blocks).
+# rows on 64-row tiles where each CTA's share of K is longer than its own
+# activation segment (balanced splits; shared inputs, 3-, 4-, 6- and 8-row
+# jobs, K of 19 super-blocks).
 _STAGED_BATCHES = r"""
 import numpy as np, torch
 import kadan_b200 as kb
@@ -350,9 +351,9 @@ BATCHES = {
     "q6_k": (((8192, 1024, 1, 0), (8192, 256, 1, 0), (8192, 256, 1, 0), (28672, 512, 1, 1)),
              ((8192, 2048, 2, 2), (2304, 96, 1, 3)),
              ((256, 33, 2, 4),)),
-    "q4_k": (((8192, 8192, 1, 0), (8192, 4096, 1, 0)),
+    "q4_k": (((24576, 8192, 1, 0), (24576, 4096, 1, 0)),
              ((4096, 14336, 3, 1), (4096, 2048, 4, 2)),
-             ((2304, 28672, 2, 3),),
+             ((4864, 28672, 2, 3),),
              ((8192, 8192, 8, 5), (8192, 4096, 6, 6))),
 }
 
