@@ -1811,6 +1811,15 @@ template <int NT, bool kStaged = false> int kernel_slots() {
     return sm_count() * blocks_per_sm[dev];
 }
 
+// Key of a stream's per-stream buffers: the handle itself, except for
+// cudaStreamPerThread, one handle that names a different stream in every
+// host thread (keyed by a thread-local address, which no stream handle
+// equals).
+cudaStream_t stream_key(cudaStream_t stream) {
+    static thread_local char per_thread;
+    return stream == cudaStreamPerThread ? reinterpret_cast<cudaStream_t>(&per_thread) : stream;
+}
+
 // Fixup buffer of the balanced split for one (device, stream). Launches on one
 // stream run in order, and a launch touches the buffer only after its
 // grid-dependency wait, so every launch of the stream can share it.
@@ -1837,7 +1846,7 @@ const Fixup* fixup_for(cudaStream_t stream) {
         return nullptr;
     FixupTable& t = fixups();
     std::lock_guard<std::mutex> guard(t.lock);
-    Fixup& f = t.table[{dev, stream}];
+    Fixup& f = t.table[{dev, stream_key(stream)}];
     if (f.ctas)
         return &f;
     cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
@@ -1880,7 +1889,7 @@ uint8_t* staging_for(cudaStream_t stream) {
         return nullptr;
     static StagingTable t;
     std::lock_guard<std::mutex> guard(t.lock);
-    uint8_t*& buf = t.table[{dev, stream}];
+    uint8_t*& buf = t.table[{dev, stream_key(stream)}];
     if (buf)
         return buf;
     cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
