@@ -32,6 +32,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <map>
 #include <mutex>
 
 #include "kb200_device.cuh"
@@ -733,6 +734,29 @@ __device__ __forceinline__ int gemv_row(const GemvParams& p, int c, int i) {
     return 16 * c + i;
 }
 
+// The MMAs of one 128-column step: the lane's 32-value blocks of rows g (w0,
+// E8M0 byte s0b) and g + 8 (w1, s1b) and its 32 fp16 activations (x0..x3).
+// live: the lane holds a block of K (else zeros, which every lane feeds).
+__device__ __forceinline__ void gemv_step(uint4 w0, uint4 w1, uint32_t s0b, uint32_t s1b, uint4 x0, uint4 x1,
+                                          uint4 x2, uint4 x3, bool live, float (&acc)[4], bool& scale_ok) {
+    bool ok0, ok1;
+    const uint32_t s0 = e8m0_half2(s0b, ok0), s1 = e8m0_half2(s1b, ok1);
+    scale_ok = scale_ok && ((ok0 && ok1) || !live);
+    const uint32_t cw0[4] = {w0.x, w0.y, w0.z, w0.w}, cw1[4] = {w1.x, w1.y, w1.z, w1.w};
+    const uint32_t xw[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
+                             x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        // Code bytes 2m, 2m+1 of the block: values 4m..4m+3.
+        const uint32_t wa = cw0[m >> 1] >> (16 * (m & 1)), wb = cw1[m >> 1] >> (16 * (m & 1));
+        const uint32_t a0 = hmul2_bits(e2m1x2_to_half2(wa & 0xFFu), s0);
+        const uint32_t a2 = hmul2_bits(e2m1x2_to_half2((wa >> 8) & 0xFFu), s0);
+        const uint32_t a1 = hmul2_bits(e2m1x2_to_half2(wb & 0xFFu), s1);
+        const uint32_t a3 = hmul2_bits(e2m1x2_to_half2((wb >> 8) & 0xFFu), s1);
+        hmma16816(acc, a0, a1, a2, a3, xw[2 * m], xw[2 * m + 1]);
+    }
+}
+
 // One 16-row x 8-token MMA item over all of K: this warp's K steps (128
 // columns each; steps warp, warp + 4, ...), each step's operands loaded a
 // step ahead of its MMAs. code0/code1 and sc0/sc1: the lane's rows g and
@@ -763,22 +787,7 @@ __device__ __forceinline__ void gemv_item(const uint8_t* code0, const uint8_t* c
         st.x2 = live ? xq[2] : zero, st.x3 = live ? xq[3] : zero;
     };
     auto mma = [&](const Step& st) {
-        bool ok0, ok1;
-        const uint32_t s0 = e8m0_half2(st.s0, ok0), s1 = e8m0_half2(st.s1, ok1);
-        scale_ok = scale_ok && ((ok0 && ok1) || !st.live);
-        const uint32_t cw0[4] = {st.w0.x, st.w0.y, st.w0.z, st.w0.w}, cw1[4] = {st.w1.x, st.w1.y, st.w1.z, st.w1.w};
-        const uint32_t xw[16] = {st.x0.x, st.x0.y, st.x0.z, st.x0.w, st.x1.x, st.x1.y, st.x1.z, st.x1.w,
-                                 st.x2.x, st.x2.y, st.x2.z, st.x2.w, st.x3.x, st.x3.y, st.x3.z, st.x3.w};
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-            // Code bytes 2m, 2m+1 of the block: values 4m..4m+3.
-            const uint32_t wa = cw0[m >> 1] >> (16 * (m & 1)), wb = cw1[m >> 1] >> (16 * (m & 1));
-            const uint32_t a0 = hmul2_bits(e2m1x2_to_half2(wa & 0xFFu), s0);
-            const uint32_t a2 = hmul2_bits(e2m1x2_to_half2((wa >> 8) & 0xFFu), s0);
-            const uint32_t a1 = hmul2_bits(e2m1x2_to_half2(wb & 0xFFu), s1);
-            const uint32_t a3 = hmul2_bits(e2m1x2_to_half2((wb >> 8) & 0xFFu), s1);
-            hmma16816(acc, a0, a1, a2, a3, xw[2 * m], xw[2 * m + 1]);
-        }
+        gemv_step(st.w0, st.w1, st.s0, st.s1, st.x0, st.x1, st.x2, st.x3, st.live, acc, scale_ok);
     };
     Step cur, nxt;
     load(warp, cur);
@@ -790,6 +799,42 @@ __device__ __forceinline__ void gemv_item(const uint8_t* code0, const uint8_t* c
             mma(nxt);
     }
 }
+
+// gemv_item with every weight and scale load of the warp's steps issued
+// before its first MMA (K <= kSteps * kGemvWarps * 128), so an item costs one
+// memory round trip instead of one per two steps; the activations (shared
+// memory) are read at each step. The same MMAs in the same order, hence the
+// same sums.
+template <int kSteps>
+__device__ __forceinline__ void gemv_item_all(const uint8_t* code0, const uint8_t* code1, const uint8_t* sc0,
+                                              const uint8_t* sc1, const __half* xr, int K, int warp, float (&acc)[4],
+                                              bool& scale_ok) {
+    const int t = threadIdx.x & 3, iters = (K + 127) / 128;
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    uint4 w0[kSteps], w1[kSteps];
+    uint32_t s0[kSteps], s1[kSteps];
+#pragma unroll
+    for (int j = 0; j < kSteps; ++j) {
+        const int it = warp + kGemvWarps * j, k0 = 128 * it + 32 * t;
+        const bool live = it < iters && k0 < K;
+        w0[j] = live ? __ldg(reinterpret_cast<const uint4*>(code0 + k0 / 2)) : zero;
+        w1[j] = live ? __ldg(reinterpret_cast<const uint4*>(code1 + k0 / 2)) : zero;
+        s0[j] = live ? uint32_t(sc0[k0 / 32]) : 127u;
+        s1[j] = live ? uint32_t(sc1[k0 / 32]) : 127u;
+    }
+#pragma unroll
+    for (int j = 0; j < kSteps; ++j) {
+        const int it = warp + kGemvWarps * j, k0 = 128 * it + 32 * t;
+        if (it >= iters)
+            break;
+        const bool live = k0 < K;
+        const uint4* xq = reinterpret_cast<const uint4*>(xr + (live ? k0 : 0));
+        gemv_step(w0[j], w1[j], s0[j], s1[j], live ? xq[0] : zero, live ? xq[1] : zero, live ? xq[2] : zero,
+                  live ? xq[3] : zero, live, acc, scale_ok);
+    }
+}
+constexpr int kAllSteps = 6;                               // gemv_item_all in the decode kernel
+constexpr int kAllK = kAllSteps * kGemvWarps * 128;        // K up to 3072 (gpt-oss: 2880)
 
 __global__ void __launch_bounds__(32 * kGemvWarps) moe_gemv_kernel(const __grid_constant__ GemvParams p) {
     __shared__ float4 part[kGemvWarps][32];  // each lane's four accumulators, per warp
@@ -879,6 +924,7 @@ struct DecodeParams {
     unsigned* status;
     unsigned* watchdog;
     int T, H, I, E, K, split, act_kind, x_f32;
+    int act_smem;         // 1: phase 2 reads the activation rows from a shared-memory copy
     float limit, alpha;
 };
 
@@ -938,10 +984,44 @@ __global__ void __launch_bounds__(32 * kGemvWarps) moe_decode_kernel(const __gri
         }
         *reinterpret_cast<uint4*>(xh + size_t(i) * 8) = o;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
+    // Any input value beyond fp16 range, from whichever thread converted it.
+    bad = __syncthreads_or(bad) != 0;
+    if (T * K <= 32) {
         // Routed experts in ascending order, their tokens in token order (the
-        // stable counting sort's order), and each (token, selection)'s row.
+        // stable counting sort's order), and each (token, selection)'s row:
+        // entry l = tok * K + s goes to row rank(e_l, l), one lane per entry.
+        if (warp == 0) {
+            const int n = T * K;
+            const int e = lane < n ? sh.chosen[lane] : 0x7fffffff;
+            bool first = lane < n;
+            int rank = 0;
+            for (int m = 0; m < n; ++m) {
+                const int em = __shfl_sync(0xffffffffu, e, m);
+                rank += em < e || (em == e && m < lane);
+                first = first && !(em == e && m < lane);
+            }
+            const unsigned firsts = __ballot_sync(0xffffffffu, first);
+            int slot = 0;
+            for (int m = 0; m < n; ++m) {
+                const int em = __shfl_sync(0xffffffffu, e, m);
+                slot += ((firsts >> m) & 1u) && em < e;
+            }
+            if (lane < n) {
+                sh.pos[lane] = rank;
+                sh.slot_token[rank] = lane / K;
+                if (first)
+                    sh.slot_expert[slot] = e, sh.slot_base[slot] = rank;
+            }
+            if (lane == 0) {
+                const int slots = __popc(firsts);
+                sh.slot_base[slots] = n;
+                sh.slots = slots;
+                if (bad && blockIdx.x == 0 && p.status)
+                    atomicOr(p.status, 4u);
+            }
+        }
+    } else if (threadIdx.x == 0) {
+        // The same order, one thread.
         int n = 0, row = 0;
         for (int e = 0; e < p.E; ++e) {
             int cnt = 0;
@@ -982,7 +1062,10 @@ __global__ void __launch_bounds__(32 * kGemvWarps) moe_decode_kernel(const __gri
         const uint8_t* sc1 = p.gu_scales + (size_t(e) * N1 + r1) * (H / 32);
         const int tok = sh.slot_token[b0 + min(g, count - 1)];
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        gemv_item(code0, code1, sc0, sc1, xh + size_t(tok) * H, H, warp, acc, scale_ok);
+        if (H <= kAllK)
+            gemv_item_all<kAllSteps>(code0, code1, sc0, sc1, xh + size_t(tok) * H, H, warp, acc, scale_ok);
+        else
+            gemv_item(code0, code1, sc0, sc1, xh + size_t(tok) * H, H, warp, acc, scale_ok);
         sh.part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         __syncthreads();
         if (warp == 0) {
@@ -1011,6 +1094,19 @@ __global__ void __launch_bounds__(32 * kGemvWarps) moe_decode_kernel(const __gri
     if (!decode_barrier(p.barrier, p.watchdog, &failed))
         return;
 
+    // The activation rows into shared memory (the phase-1 rows' buffer) when
+    // they fit: phase 2 then reads them without a round trip to L2.
+    __half* act_rows = p.act;
+    if (p.act_smem) {
+        const int rows = sh.slot_base[slots];
+        const uint4* src = reinterpret_cast<const uint4*>(p.act);
+        uint4* dst = reinterpret_cast<uint4*>(xh);
+        for (int i = threadIdx.x; i < rows * I / 8; i += blockDim.x)
+            dst[i] = src[i];
+        __syncthreads();
+        act_rows = xh;
+    }
+
     // Phase 2: down items (routed expert, 16 rows), fp32 rows in slot order.
     const int chunks2 = H / 16;
     for (int item = blockIdx.x; item < slots * chunks2; item += gridDim.x) {
@@ -1022,7 +1118,11 @@ __global__ void __launch_bounds__(32 * kGemvWarps) moe_decode_kernel(const __gri
         const uint8_t* sc0 = p.dn_scales + (size_t(e) * H + r0) * (I / 32);
         const uint8_t* sc1 = p.dn_scales + (size_t(e) * H + r1) * (I / 32);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        gemv_item(code0, code1, sc0, sc1, p.act + size_t(b0 + min(g, count - 1)) * I, I, warp, acc, scale_ok);
+        const __half* xr = act_rows + size_t(b0 + min(g, count - 1)) * I;
+        if (p.act_smem && I <= kAllK)
+            gemv_item_all<kAllSteps>(code0, code1, sc0, sc1, xr, I, warp, acc, scale_ok);
+        else
+            gemv_item(code0, code1, sc0, sc1, xr, I, warp, acc, scale_ok);
         sh.part[warp][lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         __syncthreads();
         if (warp == 0) {
@@ -1479,30 +1579,33 @@ bool decode_eligible(const kb200_moe_weights* w, size_t tokens) {
 
 int decode_launch(const kb200_moe_weights* w, const void* x, bool x_f32, const float* logits, size_t tokens, float* out,
                   const Workspace& ws, unsigned* status, cudaStream_t stream) {
-    // Co-resident CTAs per SM for each token count (the rows' shared memory
-    // grows with it), queried once per device.
-    static int blocks_per_sm[64][kDecodeTokens + 1] = {};
-    static std::mutex lock;
+    // Dynamic shared memory: the tokens' fp16 rows (phase 1), reused for the
+    // activation rows of phase 2 when those fit kDecodeActSmem.
     constexpr size_t kMaxDyn = size_t(kDecodeTokens) * kMaxK * sizeof(__half);
-    const size_t dyn = tokens * size_t(w->hidden) * sizeof(__half);
+    constexpr size_t kDecodeActSmem = 48 * 1024;
+    const size_t act_bytes = tokens * size_t(w->top_k) * size_t(w->inter) * sizeof(__half);
+    const bool act_smem = act_bytes <= kDecodeActSmem;
+    const size_t dyn = std::max(tokens * size_t(w->hidden) * sizeof(__half), act_smem ? act_bytes : size_t(0));
+    // Co-resident CTAs per SM for each (device, shared memory size), queried once.
+    static std::map<std::pair<int, size_t>, int> blocks_per_sm;
+    static std::mutex lock;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64)
-        return fail(KB200_UNSUPPORTED, "device index above 63");
+    int resident = 0;
     {
         std::lock_guard<std::mutex> guard(lock);
-        int& slot = blocks_per_sm[dev][tokens];
+        int& slot = blocks_per_sm[{dev, dyn}];
         if (!slot) {
             cudaError_t e = cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  int(kMaxDyn));
             int n = 0;
             if (e == cudaSuccess)
-                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, moe_decode_kernel, 32 * kGemvWarps,
-                                                                  tokens * size_t(kMaxK) * sizeof(__half));
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, moe_decode_kernel, 32 * kGemvWarps, dyn);
             if (e != cudaSuccess)
                 return cuda_fail(e, "moe_decode_kernel set-up");
             slot = n > 0 ? n : 1;
         }
+        resident = slot;
     }
     DecodeParams p;
     std::memset(&p, 0, sizeof(p));
@@ -1514,11 +1617,12 @@ int decode_launch(const kb200_moe_weights* w, const void* x, bool x_f32, const f
     p.T = int(tokens), p.H = w->hidden, p.I = w->inter, p.E = w->experts, p.K = w->top_k;
     p.split = w->interleaved ? 0 : 1, p.act_kind = w->activation, p.x_f32 = x_f32 ? 1 : 0;
     p.limit = w->limit, p.alpha = w->alpha;
+    p.act_smem = act_smem ? 1 : 0;
     cudaError_t e = cudaMemsetAsync(p.barrier, 0, 2 * sizeof(unsigned), stream);
     if (e != cudaSuccess)
         return cuda_fail(e, "decode barrier reset");
     // Co-resident CTAs only (the grid barrier waits for all of them).
-    const int grid = sm_count() * std::min(blocks_per_sm[dev][tokens], 8);
+    const int grid = sm_count() * std::min(resident, 8);
     void* args[] = {&p};
     TraceScope trace(KB200_KERNEL_MOE_DECODE, stream);
     e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(moe_decode_kernel), dim3(grid),
