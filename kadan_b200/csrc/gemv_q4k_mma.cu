@@ -88,8 +88,9 @@ struct alignas(64) MmaJob {
     uint32_t row_groups, group_rows, nblocks;
 };
 
-// Partial sums of one piece: acc[NT <= 2][2] of each consumer thread.
-constexpr int kSlotFloats = 2 * 2 * kConsumerThreads;
+// Partial sums of one piece: acc[NT <= 2][2] of each consumer thread, for
+// up to 256 consumer threads (the 8-row Q6_K pair kernel's eight warps).
+constexpr int kSlotFloats = 2 * 2 * 256;
 // Fewest 64-row x 1 super-block units per CTA for which the balanced split
 // pays for its fixup (a round trip to L2 at the end of each cut tile).
 constexpr int kMinUnitsPerCta = 6;
@@ -1256,7 +1257,9 @@ static_assert(3 * (PairLayout<2>::kTotal + 128 + 1024) <= 228 * 1024, "three Q6_
 static_assert(2 * (PairLayout<3, kWarps, true>::kTotal + 128 + 1024) <= 228 * 1024, "two staged pair CTAs per SM");
 static_assert(3 * (PairLayout<2, kWarps, true>::kTotal + 128 + 1024) <= 228 * 1024, "three staged pair CTAs per SM");
 static_assert(2 * (PairLayout<2, kWarps, true, 2>::kTotal + 128 + 1024) <= 228 * 1024, "two staged 4-row pair CTAs per SM");
-static_assert(PairLayout<2, kWarps, true, 2>::kStageBytes % 128 == 0, "tensor copies land on 128-byte boundaries");
+static_assert(PairLayout<2, kWarps, true, 2>::kStageBytes % 128 == 0 && PairLayout<2, 8, true, 4>::kStageBytes % 128 == 0,
+              "tensor copies land on 128-byte boundaries");
+static_assert(PairLayout<2, 8, true, 4>::kTotal + 128 + 1024 <= 228 * 1024, "one staged 8-row pair CTA per SM");
 static_assert(kQ6StageBytes % 128 == 0 && PairLayout<3, kWarps, true>::kStageBytes % 128 == 0,
               "tensor copies land on 128-byte boundaries");
 static_assert(pair_chunk_bytes(1) % 16 == 0, "bulk copy sizes and source offsets are multiples of 16 bytes");
@@ -1562,9 +1565,10 @@ __device__ __forceinline__ void q6k_pair_block(const uint8_t* bg, const uint8_t*
 // activations follow one another (group stride: the job's chunks x a full
 // group's chunk bytes).
 template <int S, int W, bool kStaged, int TP = 1>
-__global__ void __launch_bounds__(32 * W + 32, S == 2 && TP == 1 ? 3 : 2)
+__global__ void __launch_bounds__(32 * W + 32, TP == 1 ? (S == 2 ? 3 : 2) : TP == 2 ? 2 : 1)
     gemv_q6k_pair_kernel(const __grid_constant__ MmaParams p) {
-    static_assert(TP == 1 || kStaged, "4-row passes take staged activations");
+    static_assert(TP == 1 || kStaged, "4- and 8-row passes take staged activations");
+    constexpr int NF = TP >= 4 ? 2 : 1;  // groups of 4 tokens in the piece ending
     using L = PairLayout<S, W, kStaged, TP>;
     constexpr int kStages = L::kStages;
     constexpr int CT = 32 * W;               // consumer threads
@@ -1756,21 +1760,23 @@ __global__ void __launch_bounds__(32 * W + 32, S == 2 && TP == 1 ? 3 : 2)
         if (check && !((finite_g || !valid_lo) && (finite_8 || !valid_hi)))
             atomicOr(job.status, 1u);
         // Lanes t = 2k, 2k + 1 hold token 2 tp + k's even and odd
-        // sub-blocks: add them, then give lane t the sums of token t (token
-        // pair t / 2, lane 2 (t % 2) of each group of four) as the common
-        // piece ending expects.
+        // sub-blocks: add them, then give lane t the sums of tokens t and
+        // 4 + t (token pairs t / 2 and 2 + t / 2, lane 2 (t % 2) of each group
+        // of four) as the common piece ending expects.
         const int from = (lane & ~3) | ((2 * t) & 3);
-        float acc[1][2];
+        float acc[NF][2];
 #pragma unroll
         for (int tp = 0; tp < TP; ++tp) {
             acc_g[tp] += __shfl_xor_sync(0xffffffffu, acc_g[tp], 1);
             acc_8[tp] += __shfl_xor_sync(0xffffffffu, acc_8[tp], 1);
             const float vg = __shfl_sync(0xffffffffu, acc_g[tp], from), v8 = __shfl_sync(0xffffffffu, acc_8[tp], from);
-            if (tp == 0 || (t >> 1) == tp)
-                acc[0][0] = vg, acc[0][1] = v8;
+#pragma unroll
+            for (int nf = 0; nf < NF; ++nf)
+                if (tp == (TP == 1 ? 0 : 2 * nf + (t >> 1)))
+                    acc[nf][0] = vg, acc[nf][1] = v8;
         }
-        finish_piece<1, decltype(await_dependency), CT>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0,
-                                                        rows, red, abort_flag, await_dependency);
+        finish_piece<NF, decltype(await_dependency), CT>(p, pc, job, acc, KS, ks, tid, my_row, valid_lo, valid_hi, r0,
+                                                         rows, red, abort_flag, await_dependency);
     }
 }
 
@@ -2106,9 +2112,10 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     for (const auto* j : jobs)
         max_rows = std::max(max_rows, int(std::min(j->rows, uint32_t(KB200_BATCH_ROWS))));
     const int nt = max_rows <= 4 ? 1 : 2;
-    // 1-2 rows: the paired-sub-block kernel (2 rows per pass). 3-8 rows: the
-    // same kernel with two token pairs per pass (row groups of 4) when the
-    // activations can be staged, else the 4/8-row kernel.
+    // 1-2 rows: the paired-sub-block kernel (2 rows per pass). 3-4 rows: the
+    // same kernel with two token pairs per pass, 5-8 rows with four (one CTA
+    // of eight consumer warps per SM), when the activations can be staged;
+    // else the 4/8-row kernel.
     const bool pair = max_rows <= 2 && tuning().q6_pair;
     // Ring depth: 2 stages (three CTAs per SM) for the pair kernel when no job
     // is longer than 64 super-blocks (more warps for short, launch-bound K),
@@ -2124,12 +2131,14 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     // one outside graph capture), whichever this launch takes.
     const int pair_slots = !pair ? 0 : two_stage ? q6k_pair_slots<2, 4, false>() : q6k_pair_slots<3, 4, false>();
     const int pair_slots_staged = !pair ? 0 : two_stage ? q6k_pair_slots<2, 4, true>() : q6k_pair_slots<3, 4, true>();
-    const int quad_slots = !pair && staging ? q6k_pair_slots<2, 4, true, 2>() : 0;
+    const bool eight = max_rows > 4;  // 5-8 rows: four token pairs per pass
+    const int quad_slots = !pair && staging ? (eight ? q6k_pair_slots<2, 8, true, 4>() : q6k_pair_slots<2, 4, true, 2>()) : 0;
     if (pair_slots < 0 || pair_slots_staged < 0 || quad_slots < 0)
         return -std::min(pair_slots, std::min(pair_slots_staged, quad_slots));
+    const int quad_rows = eight ? 8 : 4;
     for (size_t first = 0; first < jobs.size(); first += kMaxJobsQ) {
         const size_t n = std::min(jobs.size() - first, size_t(kMaxJobsQ));
-        // 4-row passes when this batch's distinct inputs fit the staging buffer.
+        // 4- or 8-row passes when this batch's distinct inputs fit the staging buffer.
         bool quad = false;
         if (!pair && staging) {
             size_t bytes = 0;
@@ -2139,11 +2148,12 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
                 for (size_t k = 0; k < m && !seen; ++k)
                     seen = jobs[first + k]->input == j.input && jobs[first + k]->in == j.in && jobs[first + k]->rows == j.rows;
                 if (!seen)
-                    bytes += size_t((j.rows + 3) / 4) * ((j.in / 256 + kQ6Chunk - 1) / kQ6Chunk) * size_t(pair_chunk_bytes(4));
+                    bytes += size_t((j.rows + quad_rows - 1) / quad_rows) * ((j.in / 256 + kQ6Chunk - 1) / kQ6Chunk)
+                             * size_t(pair_chunk_bytes(quad_rows));
             }
             quad = bytes <= kStagingBytes;
         }
-        const uint32_t group_rows = pair ? 2u : quad ? 4u : uint32_t(4 * nt);
+        const uint32_t group_rows = pair ? 2u : quad ? uint32_t(quad_rows) : uint32_t(4 * nt);
         MmaParams p;
         std::memset(&p, 0, sizeof(p));
         p.watchdog = watchdog_word();
@@ -2209,8 +2219,9 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
                 return st;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
-        cfg.blockDim = dim3(kThreadsQ);
-        cfg.dynamicSmemBytes = (quad        ? PairLayout<2, 4, true, 2>::kTotal
+        cfg.blockDim = dim3(quad && eight ? 32 * 8 + 32 : kThreadsQ);
+        cfg.dynamicSmemBytes = (quad && eight ? PairLayout<2, 8, true, 4>::kTotal
+                                : quad      ? PairLayout<2, 4, true, 2>::kTotal
                                 : !pair     ? (nt == 2      ? Q6Layout<2, 2>::kTotal
                                                : two_stage ? Q6Layout<1, 2>::kTotal
                                                            : Q6Layout<1, 3>::kTotal)
@@ -2226,7 +2237,8 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         TraceScope trace(pair || quad ? KB200_KERNEL_GEMV_Q6K_PAIR : KB200_KERNEL_GEMV_Q6K_MMA, stream);
         cudaError_t e;
         if (quad)
-            e = cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 4, true, 2>, p);
+            e = eight ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 8, true, 4>, p)
+                      : cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 4, true, 2>, p);
         else if (pair && staged)
             e = two_stage ? cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<2, 4, true>, p)
                           : cudaLaunchKernelEx(&cfg, gemv_q6k_pair_kernel<3, 4, true>, p);

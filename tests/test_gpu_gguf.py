@@ -434,7 +434,8 @@ def test_staged_activations_match_per_cta_quantisation(kb, oracle, cuda, tmp_pat
 @pytest.mark.parametrize("rows", [3, 4, 6, 8])
 def test_q6k_multi_row_pairs_of_tokens(kb, oracle, cuda, rows):
     """Q6_K at 3-8 input rows: the pair kernel with two token pairs per pass
-    (row groups of 4 past 4 rows), activations staged once per launch; a
+    (3-4 rows) or four (5-8 rows, eight consumer warps), activations staged
+    once per launch; a
     batch of jobs sharing one input, one with a ragged last chunk, one with a
     long K; within the oracle's tolerance."""
     import torch
