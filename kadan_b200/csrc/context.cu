@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "context.hpp"
+#include "gemv_mma.hpp"
 #include "gguf_formats.cuh"
 #include "kb200_host.hpp"
 #include "read_team.hpp"
@@ -156,7 +157,7 @@ int launch_projections(kb200_context* c, const kb200_gemv_job* jobs, size_t coun
         ++c->counters.gemm_launches;
     }
     if (!gemv.empty()) {
-        if (const int s = kb200_gguf_gemv_batch(gemv.data(), gemv.size(), c->stream))
+        if (const int s = gemv_batch(gemv.data(), gemv.size(), c->stream, true))
             return s;
         ++c->counters.gemv_batches;
     }
@@ -174,7 +175,7 @@ int rerun_gemm_jobs(kb200_context* c, const kb200_gemv_job* jobs, size_t count) 
         return KB200_OK;
     c->counters.gemm_fallbacks += again.size();
     ++c->counters.gemv_batches;
-    return kb200_gguf_gemv_batch(again.data(), again.size(), c->stream);
+    return gemv_batch(again.data(), again.size(), c->stream, true);
 }
 
 }  // namespace

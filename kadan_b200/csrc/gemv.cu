@@ -646,17 +646,9 @@ int path_of(const kb200_gemv_job& j) {
 }  // namespace
 }  // namespace kb200
 
-using namespace kb200;
+namespace kb200 {
 
-extern "C" {
-
-int kb200_gemv_path(const kb200_gemv_job* job) {
-    if (!job || check_job(*job) != KB200_OK)
-        return -1;
-    return path_of(*job);
-}
-
-int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream_ptr) {
+int gemv_batch(const kb200_gemv_job* jobs, size_t count, cudaStream_t stream, bool synchronous) {
     if (!count)
         return KB200_OK;
     if (!jobs)
@@ -673,7 +665,6 @@ int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream
             if (overlap(a.output, out_bytes, b.input, size_t(b.rows) * b.in * sizeof(float)))
                 return fail(KB200_ALIAS, "output overlaps another job's input");
         }
-    auto stream = static_cast<cudaStream_t>(stream_ptr);
     // One launch per (path, encoding, rows-per-pass), like plan_matvec's
     // per-format launches (IW/src/cuda/h3_compute.cu:325-345).
     struct Key {
@@ -695,7 +686,7 @@ int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream
     }
     for (const auto& [key, members] : groups) {
         if (key.path == 2) {
-            if (const int s = launch_mma(members, stream))
+            if (const int s = launch_mma(members, stream, nullptr, synchronous))
                 return s;
             continue;
         }
@@ -745,6 +736,22 @@ int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream
         }
     }
     return KB200_OK;
+}
+
+}  // namespace kb200
+
+using namespace kb200;
+
+extern "C" {
+
+int kb200_gemv_path(const kb200_gemv_job* job) {
+    if (!job || check_job(*job) != KB200_OK)
+        return -1;
+    return path_of(*job);
+}
+
+int kb200_gguf_gemv_batch(const kb200_gemv_job* jobs, size_t count, void* stream_ptr) {
+    return gemv_batch(jobs, count, static_cast<cudaStream_t>(stream_ptr), false);
 }
 
 // A row-parallel projection and the sum of its partial outputs over the

@@ -29,7 +29,14 @@ bool mma_eligible(const kb200_gemv_job& job);
 // per pass (8) become row groups. With `peer`, the
 // single job's outputs (rows x columns, contiguous) also go, as words tagged
 // with the group's next call number, to slot [rank] of every peer's buffer.
-int launch_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer = nullptr);
+// synchronous: the caller waits for this launch alone (a host-span call), so
+// nothing ahead on the stream hides a quantisation kernel in front of a GEMV;
+// activations are then staged only where CTAs would quantise many times.
+int launch_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer = nullptr,
+               bool synchronous = false);
+
+// kb200_gguf_gemv_batch with the synchronous hint of launch_mma.
+int gemv_batch(const kb200_gemv_job* jobs, size_t count, cudaStream_t stream, bool synchronous);
 
 // The peer all-reduce kernel; push = false when the values were already
 // pushed (by a GEMV launched with a PeerOut) and only the gather-sum is left.

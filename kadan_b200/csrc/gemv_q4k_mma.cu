@@ -2103,7 +2103,8 @@ int launch_stage_quant(const StageQuantParams& q, cudaStream_t stream, bool q4k)
 // would leave a tenth of the CTA slots idle. 1-2 rows run on the pair
 // kernel, with the activations quantised once per launch into the stream's
 // staging buffer when it has one and they fit.
-int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer) {
+int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer,
+                   bool synchronous) {
     auto encode = encode_fn();
     if (!encode)
         return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -2193,8 +2194,21 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         }
         p.count = uint32_t(n);
         p.total_tiles = tiles;
+        // In a synchronous call nothing ahead on the stream hides the
+        // quantisation kernel: 1-2 rows are staged there only where each CTA
+        // would otherwise quantise more than two activation windows (the
+        // host-span q,k,v and o launches of a 70B layer quantise per CTA;
+        // [down] is staged). 3-8 rows are always staged (their other kernel
+        // is far slower).
+        bool worth = true;
+        if (pair && synchronous) {
+            const int win_rows = std::min(max_rows, 2);
+            const int window = pair_segment_blocks(win_rows, two_stage ? pair_seg_budget<2>() : pair_seg_budget<3>());
+            const uint64_t cta_units = (uint64_t(units) + uint64_t(pair_slots_staged) - 1) / uint64_t(pair_slots_staged);
+            worth = cta_units * kQ6Chunk > 2u * uint64_t(window);
+        }
         StageQuantParams q;
-        const bool staged = staging && (pair || quad) && stage_inputs(p, staging, q, false);
+        const bool staged = staging && (pair || quad) && worth && stage_inputs(p, staging, q, false);
         if (quad && !staged)  // only a batch without any super-block gets here
             return fail(KB200_INVALID, "Q6_K jobs without input values");
         int slots = quad     ? quad_slots
@@ -2255,7 +2269,8 @@ int launch_q6k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     return KB200_OK;
 }
 
-int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer) {
+int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer,
+                   bool synchronous) {
     auto encode = encode_fn();
     if (!encode)
         return fail(KB200_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -2387,7 +2402,8 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
         for (uint32_t m = 0; m < p.count; ++m)
             one_group = one_group && p.jobs[m].row_groups == 1;
         const uint64_t units_per_cta = (uint64_t(units) + grid - 1) / grid;
-        const bool requantises = units_per_cta > uint64_t(segment_blocks(tokens, kStageUnits / int(R)));
+        // Synchronous calls: only where a CTA would quantise more than twice.
+        const bool requantises = units_per_cta > uint64_t(segment_blocks(tokens, kStageUnits / int(R))) * (synchronous ? 2u : 1u);
         const bool staged = staging && R == 64 && one_group && requantises && stage_inputs(p, staging, q, true);
         if (staged)
             if (const int st = launch_stage_quant(q, stream, true))
@@ -2400,13 +2416,14 @@ int launch_q4k_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t 
     return KB200_OK;
 }
 
-int launch_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer) {
+int launch_mma(const std::vector<const kb200_gemv_job*>& jobs, cudaStream_t stream, const PeerOut* peer,
+               bool synchronous) {
     if (jobs.empty())
         return KB200_OK;
     if (peer && peer->world > 1 && (jobs.size() != 1 || jobs.front()->stride != jobs.front()->columns))
         return fail(KB200_INVALID, "a peer exchange takes one job with contiguous output rows");
-    return jobs.front()->encoding == KB200_Q6_K ? launch_q6k_mma(jobs, stream, peer)
-                                                : launch_q4k_mma(jobs, stream, peer);
+    return jobs.front()->encoding == KB200_Q6_K ? launch_q6k_mma(jobs, stream, peer, synchronous)
+                                                : launch_q4k_mma(jobs, stream, peer, synchronous);
 }
 
 }  // namespace kb200
